@@ -1,0 +1,73 @@
+"""Seeded synthetic inputs with the shapes of the benchmark configurations.
+
+No dataset or checkpoint is used.  Every tensor is generated in fp32 on the
+CPU from ``torch.Generator("cpu").manual_seed(seed)`` and only then cast, so a
+device run and a CPU check see identical bits.
+
+* ``prefill_inputs``: Q/K/V ~ N(0, 1) in the attention layer's
+  ``[bsz, heads, L, head_dim]`` layout.  In each KV head, 1% of the key
+  positions are planted heavy hitters: ``K += 4 * normalize(mean of the
+  group's query heads over the last ``window`` queries)``.
+* ``DriftingDecode``: per step a query that drifts,
+  ``q_t = 0.9 * q_{t-1} + 0.1 * N(0, 1)``, plus fresh N(0, 1) keys/values.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Tuple
+
+import torch
+
+
+@dataclass
+class LayerGeometry:
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+
+    @property
+    def groups(self) -> int:
+        return self.num_heads // self.num_kv_heads
+
+
+LLAMA_8B = LayerGeometry(32, 8, 128)
+QWEN_7B = LayerGeometry(28, 4, 128)
+
+
+def prefill_inputs(geo: LayerGeometry, seq_len: int, *, bsz: int = 1, seed: int = 0,
+                   window: int = 32, planted_frac: float = 0.01, planted_scale: float = 4.0,
+                   dtype: torch.dtype = torch.float32) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    g = torch.Generator("cpu").manual_seed(seed)
+    H, KV, D, G = geo.num_heads, geo.num_kv_heads, geo.head_dim, geo.groups
+    q = torch.randn(bsz, H, seq_len, D, generator=g)
+    k = torch.randn(bsz, KV, seq_len, D, generator=g)
+    v = torch.randn(bsz, KV, seq_len, D, generator=g)
+    n_plant = max(1, int(round(planted_frac * seq_len)))
+    w = min(window, seq_len)
+    for b in range(bsz):
+        for h in range(KV):
+            mean_q = q[b, h * G:(h + 1) * G, seq_len - w:, :].mean(dim=(0, 1))
+            direction = mean_q / mean_q.norm().clamp_min(1e-12)
+            pos = torch.randperm(seq_len, generator=g)[:n_plant]
+            k[b, h, pos, :] += planted_scale * direction
+    return q.to(dtype), k.to(dtype), v.to(dtype)
+
+
+class DriftingDecode:
+    """Per-step decode inputs: ``q_t = 0.9 q_{t-1} + 0.1 noise``; fresh k, v."""
+
+    def __init__(self, geo: LayerGeometry, *, bsz: int = 1, seed: int = 1,
+                 q0: torch.Tensor = None, dtype: torch.dtype = torch.float32):
+        self.geo, self.bsz, self.dtype = geo, bsz, dtype
+        self.g = torch.Generator("cpu").manual_seed(seed)
+        H, D = geo.num_heads, geo.head_dim
+        self.q = (q0.float().clone() if q0 is not None
+                  else torch.randn(bsz, H, 1, D, generator=self.g))
+
+    def step(self) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        H, KV, D = self.geo.num_heads, self.geo.num_kv_heads, self.geo.head_dim
+        noise = torch.randn(self.bsz, H, 1, D, generator=self.g)
+        self.q = 0.9 * self.q + 0.1 * noise
+        k = torch.randn(self.bsz, KV, 1, D, generator=self.g)
+        v = torch.randn(self.bsz, KV, 1, D, generator=self.g)
+        return self.q.to(self.dtype), k.to(self.dtype), v.to(self.dtype)
