@@ -1,0 +1,89 @@
+"""ctypes binding of the C ABI declared in include/heterocache_b200.h.
+
+The shared library is built in-tree (``heterocache_b200/libhcb200.so``) by
+``heterocache_b200.build``.  There is no fallback: importing an op without the
+library raises, so a missing build can never silently route work elsewhere.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import c_double, c_float, c_int, c_int64, c_longlong, c_size_t, c_void_p
+
+LIB_NAME = "libhcb200.so"
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
+
+# Every entry point the header declares, with its ctypes signature.
+SIGNATURES = {
+    "hc_abi_version": (c_int, []),
+    "hc_status_string": (ctypes.c_char_p, [c_int]),
+    "hc_last_cuda_error": (ctypes.c_char_p, []),
+    "hc_prefill_keep": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                c_void_p, c_void_p]),
+    "hc_prefill_select_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "hc_prefill_select": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                  c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                                  c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_pivot_init_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "hc_pivot_init": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                              c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64,
+                              c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_decode_append": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                 c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                 c_void_p]),
+    "hc_flash_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "hc_flash_decode": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p,
+                                c_void_p, c_int, c_void_p, c_int, c_void_p, c_float, c_void_p, c_longlong,
+                                c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_drift_check_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "hc_drift_check": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_double,
+                               c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p,
+                               c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_retrieve": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
+                            c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                            c_int, c_void_p, c_int, c_void_p, c_void_p]),
+}
+
+_LIB = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Load the CUDA library (once) or raise if it has not been built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"heterocache_b200: the sm_100a library {LIB_PATH} is not built; run "
+                "`python -c 'import heterocache_b200.build as b; b.build()'` first")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        if handle.hc_abi_version() != 1:
+            raise RuntimeError("heterocache_b200: library ABI version mismatch")
+        _LIB = handle
+    return _LIB
+
+
+class HCError(RuntimeError):
+    """A status code returned by the C ABI."""
+
+    def __init__(self, op: str, code: int):
+        l = lib()
+        msg = l.hc_status_string(code).decode()
+        cuda = l.hc_last_cuda_error().decode()
+        super().__init__(f"{op}: {msg} (status {code})" + (f" [{cuda}]" if code == 5 and cuda else ""))
+        self.code = code
+
+
+def check(op: str, code: int) -> None:
+    if code != 0:
+        raise HCError(op, code)

@@ -1,0 +1,449 @@
+"""Drop-in ``HeteroCache`` for the B200 path.
+
+Same constructor input, method names and public tensors as the reference
+cache (heterocache/cache_utils.py:610-1196): ``update``, ``init_coefficient``,
+``prefill_select``, ``decode_select``, ``get_seq_length``; ``key_pools``,
+``value_pools``, ``block_tables``, ``heads_len``, ``prefill_topk_set``.
+Every data-path step runs in the sm_100a library through the C ABI; Python
+keeps only bookkeeping.
+
+Differences in mechanism (not in results):
+
+* The reference reads the device every layer and step (``.item()`` at
+  cache_utils.py:801, :985, :1114 and ``.tolist()`` at :1077).  Here the
+  per-row lengths and mapped-page counts are mirrored on the host (they evolve
+  deterministically), so the free-list check and its ``RuntimeError("Layer N
+  OOM.")`` happen before the launch with no device read, and the drift
+  decision stays on the device (the retrieval kernel reads the trigger).
+* ``prefill_topk_set[layer]`` holds the reference set of each pivot as
+  int32 positions in ascending order (the reference keeps the top-k indices
+  in score order; only the set is ever used, cache_utils.py:1063-1075).
+* With ``real_offload=True`` the full tier lives in pinned host memory and the
+  retrieval kernel reads it directly over the host link on a side stream,
+  ordered before the next attention of that layer by an event.  The
+  reference stages through one shared pinned buffer and copies per satellite
+  (cache_utils.py:941-948, :1095-1123), which lets the next satellite's
+  host-side gather overwrite a buffer an earlier copy may still be reading;
+  here there is no staging buffer.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+try:  # the reference subclasses transformers' DynamicCache
+    from transformers.cache_utils import DynamicCache as _CacheBase
+except Exception:  # pragma: no cover - transformers is optional for the kernels
+    _CacheBase = object
+
+from . import ops
+from .ops import PAGE, Workspace
+
+
+def get_compress_len(compression_ratio, full_heads, ori_len, num_kv_heads):
+    """Base per-head budget (heterocache/cache_utils.py:15-16)."""
+    return int((compression_ratio * num_kv_heads - full_heads) * ori_len / (num_kv_heads - full_heads))
+
+
+class HeteroCacheConfig:
+    """Same fields and defaults as heterocache/cache_utils.py:41-68.
+
+    ``window_size`` (default 1, the HeteroCache behaviour) extends the prefill
+    scoring to an observation window of the last W queries with SnapKV's
+    in-window causal mask and window sum (heterocache/kv_cluster.py:168-178).
+    """
+
+    def __init__(self, data: Optional[Dict], compression_ratio: Optional[float] = 0.5,
+                 stable_threshold: Optional[float] = 0.5, real_offload: Optional[bool] = True,
+                 max_gen_len: Optional[int] = 128, decode_step: Optional[int] = 4,
+                 pooling: Optional[str] = "avgpool", kernel_size: Optional[int] = 5,
+                 num_attn_heads: Optional[int] = 32, num_kv_heads: Optional[int] = 8,
+                 num_layers: Optional[int] = 32, window_size: int = 1):
+        self.data = data
+        self.stable_threshold = stable_threshold
+        self.compression_ratio = compression_ratio
+        self.real_offload = real_offload
+        self.max_gen_len = max_gen_len
+        self.decode_step = decode_step
+        self.pooling = pooling
+        self.kernel_size = kernel_size
+        self.quant_method = None
+        self.num_attn_heads = num_attn_heads
+        self.num_kv_heads = num_kv_heads
+        self.num_layers = num_layers
+        self.window_size = window_size
+
+
+class _LayerJobs:
+    """Device descriptors of one layer's drift-check jobs and satellites."""
+
+    def __init__(self, relations: Dict[str, List[int]], alloc: List[float], base: int, L: int, device):
+        jobs, slots, max_len = [], [], []
+        m_job, m_head, m_len = [], [], []
+        for idx, (leader, members) in enumerate(relations.items()):
+            if not members:
+                continue
+            lengths = [min(int(base * alloc[m]), L) for m in members]
+            j = len(jobs)
+            jobs.append(int(leader))
+            slots.append(idx)
+            max_len.append(max(lengths))
+            for m, n in zip(members, lengths):
+                if n == 0:
+                    continue
+                m_job.append(j)
+                m_head.append(int(m))
+                m_len.append(n)
+        self.n_jobs = len(jobs)
+        self.max_len_cap = max(max_len) if max_len else 0
+        self.max_member_len = max(m_len) if m_len else 0
+        i32 = dict(dtype=torch.int32, device=device)
+        self.pivot_heads = torch.tensor(jobs, **i32)
+        self.ref_slots = torch.tensor(slots, **i32)
+        self.max_len = torch.tensor(max_len, **i32)
+        self.member_job = torch.tensor(m_job, **i32)
+        self.member_head = torch.tensor(m_head, **i32)
+        self.member_len = torch.tensor(m_len, **i32)
+        self.trigger = torch.zeros(max(self.n_jobs, 1), **i32)
+        self.retrieve_positions = torch.zeros(max(self.n_jobs, 1), max(self.max_len_cap, 1), **i32)
+        self.coeffs = None
+        self.median = None
+
+
+class HeteroCache(_CacheBase):
+    def __init__(self, cache_config):
+        if _CacheBase is not object:
+            super().__init__()
+        self.config = cache_config
+        self.num_attn_heads = cache_config.num_attn_heads
+        self.num_kv_heads = cache_config.num_kv_heads
+        self.num_layers = cache_config.num_layers
+        self.gqa = self.num_kv_heads != self.num_attn_heads
+        self.num_key_value_groups = self.num_attn_heads // self.num_kv_heads
+        self.total_kv_heads = self.num_kv_heads * self.num_layers
+        self.page_size = PAGE
+        self.compression_ratio = cache_config.compression_ratio
+        self.window_size = getattr(cache_config, "window_size", 1)
+        n = self.num_layers
+        self.key_pools: List[Optional[torch.Tensor]] = [None] * n
+        self.value_pools: List[Optional[torch.Tensor]] = [None] * n
+        self.block_tables: List[Optional[torch.Tensor]] = [None] * n
+        self.free_blocks: List[Optional[torch.Tensor]] = [None] * n
+        self.free_block_pointers: List[int] = [0] * n
+        self.prefill_boundary_blocks: List[int] = [0] * n
+        self.layer_head_capacities: List = [0] * n
+        self.heads_len: List[Optional[torch.Tensor]] = [None] * n
+        self.head_indices = None
+        self.data = cache_config.data
+        counts = self.data["meta"]["counts"]
+        self.full_heads = counts["volatile"] + counts["pivot"]
+        self.key_cache_cpu: List = []
+        self.value_cache_cpu: List = []
+        self.prefill_topk_set: List = []
+        self.query_states_buffer = [[] for _ in range(n)]
+        self.bsz = None
+        self.head_dim = None
+        self.prefill_len = None
+        self._seen_tokens = 0
+        self.decode_step = cache_config.decode_step
+        self.stable_threshold = cache_config.stable_threshold
+        self.real_offload = bool(cache_config.real_offload)
+        self.device = "cpu" if cache_config.real_offload else "cuda"
+        self.pooling = cache_config.pooling
+        self.kernel_size = cache_config.kernel_size
+        # device-side state
+        self._dev = None
+        self._err = None
+        self._ws_score: Optional[Workspace] = None
+        self._ws_fd: Optional[Workspace] = None
+        self._free_ptr: List[Optional[torch.Tensor]] = [None] * n
+        self._ref_bitmap: List[Optional[torch.Tensor]] = [None] * n
+        self._qbuf: List[Optional[torch.Tensor]] = [None] * n
+        self._qcount = [0] * n
+        self._jobs: List[Optional[_LayerJobs]] = [None] * n
+        self._retrieve_done: List[Optional[torch.cuda.Event]] = [None] * n
+        self._side_stream: Optional[torch.cuda.Stream] = None
+        # host mirrors of deterministic bookkeeping
+        self._hlen: List[Optional[np.ndarray]] = [None] * n
+        self._mapped: List[Optional[np.ndarray]] = [None] * n
+        self.record_checks = False
+        self.check_log: List[Dict] = []
+
+    def __bool__(self):
+        return True
+
+    def __len__(self):
+        return self.num_layers
+
+    def get_seq_length(self, layer_idx: Optional[int] = 0) -> int:
+        if self._seen_tokens is None:
+            return 0
+        return self._seen_tokens
+
+    # ------------------------------------------------------------------
+    def _ensure_device(self, device: torch.device) -> None:
+        if self._dev is None:
+            self._dev = device
+            self._err = torch.zeros(1, dtype=torch.int32, device=device)
+            self._ws_score = Workspace(device)
+            self._ws_fd = Workspace(device)
+            self.head_indices = torch.arange(self.num_kv_heads, device=device)
+
+    def check_errors(self) -> None:
+        """Raise if a device-side check fired since the last call (syncs)."""
+        if self._err is None:
+            return
+        code = int(self._err.item())
+        if code:
+            self._err.zero_()
+            if self._ws_score is not None:
+                self._ws_score.reset()
+            names = {3: "free list exhausted (OOM)", 4: "page-table entry or index out of range",
+                     7: "device-side wait timed out"}
+            msgs = [v for b, v in names.items() if code & (1 << b)]
+            raise RuntimeError("HeteroCache device error: " + ", ".join(msgs or [f"flags {code:#x}"]))
+
+    def _init_layer_storage(self, layer_idx, device, dtype):
+        """heterocache/cache_utils.py:693-766 (same sizes, ids and order)."""
+        L = self.prefill_len
+        gen = self.config.max_gen_len
+        alloc = self.data["allocation_matrix"][layer_idx]
+        keep = self.data["need_to_keep_counts"][layer_idx]
+        caps, total, pre_total = [], 0, 0
+        for h in range(self.num_kv_heads):
+            if h in keep:
+                cap = L
+            else:
+                cap = max(min(int(self.base_compress_len * alloc[h]), L), 0)
+            nblk = (cap + PAGE - 1) // PAGE
+            caps.append(nblk * PAGE)
+            pre_total += nblk
+            total += (cap + gen + PAGE - 1) // PAGE
+        max_blocks = (L + gen + PAGE - 1) // PAGE + 1
+        rows = self.bsz * self.num_kv_heads
+        bt = np.full((rows, max_blocks), -1, dtype=np.int32)
+        mapped = np.zeros(rows, dtype=np.int64)
+        ptr = 0
+        for r in range(rows):
+            nb = caps[r % self.num_kv_heads] // PAGE
+            if nb > 0:
+                bt[r, :nb] = np.arange(ptr, ptr + nb, dtype=np.int32)
+                ptr += nb
+            mapped[r] = nb
+        if ptr > total:
+            raise RuntimeError(f"Layer {layer_idx}: Allocation logic error! Used more than allocated.")
+        self.key_pools[layer_idx] = torch.zeros(total, PAGE, 1, self.head_dim, device=device, dtype=dtype)
+        self.value_pools[layer_idx] = torch.zeros(total, PAGE, 1, self.head_dim, device=device, dtype=dtype)
+        self.block_tables[layer_idx] = torch.from_numpy(bt).to(device)
+        self.free_blocks[layer_idx] = torch.arange(ptr, total, dtype=torch.int32, device=device)
+        self.free_block_pointers[layer_idx] = 0
+        self._free_ptr[layer_idx] = torch.zeros(1, dtype=torch.int32, device=device)
+        self.heads_len[layer_idx] = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.prefill_boundary_blocks[layer_idx] = pre_total
+        self.layer_head_capacities[layer_idx] = caps
+        self._hlen[layer_idx] = np.zeros(rows, dtype=np.int64)
+        self._mapped[layer_idx] = mapped
+
+    def _side(self) -> torch.cuda.Stream:
+        if self._side_stream is None:
+            self._side_stream = torch.cuda.Stream(device=self._dev)
+        return self._side_stream
+
+    def _wait_retrieval(self, layer_idx: int) -> None:
+        ev = self._retrieve_done[layer_idx]
+        if ev is not None:
+            torch.cuda.current_stream(self._dev).wait_event(ev)
+            self._retrieve_done[layer_idx] = None
+
+    # ------------------------------------------------------------------
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        """heterocache/cache_utils.py:884-1005."""
+        if layer_idx == 0:
+            self._seen_tokens += key_states.shape[-2]
+        self._ensure_device(key_states.device)
+        if self.bsz is None:
+            self.bsz = key_states.shape[0]
+            self.head_dim = key_states.shape[-1]
+        if not hasattr(self, "base_compress_len"):
+            self.prefill_len = key_states.shape[-2]
+            self.base_compress_len = get_compress_len(self.compression_ratio, self.full_heads, self.prefill_len,
+                                                      self.total_kv_heads)
+        if self.key_pools[layer_idx] is None:
+            self._init_layer_storage(layer_idx, key_states.device, key_states.dtype)
+        seq_len = key_states.shape[-2]
+        if seq_len > 1:
+            self.prefill_len = seq_len
+            keep = self.data["need_to_keep_counts"][layer_idx]
+            upd = self.data["need_to_update_counts"][layer_idx]
+            if keep:
+                keep_t = torch.tensor(keep, dtype=torch.int32, device=key_states.device)
+                ops.prefill_keep(key_states, value_states, keep_t, self.key_pools[layer_idx],
+                                 self.value_pools[layer_idx], self.block_tables[layer_idx],
+                                 self.heads_len[layer_idx], self._err)
+                for b in range(self.bsz):
+                    for h in keep:
+                        self._hlen[layer_idx][b * self.num_kv_heads + h] = seq_len
+            if not upd:
+                self.key_cache_cpu.append(None)
+                self.value_cache_cpu.append(None)
+            elif self.real_offload:
+                side = self._side()
+                side.wait_stream(torch.cuda.current_stream(key_states.device))
+                with torch.cuda.stream(side):
+                    kc = torch.empty(key_states.shape, dtype=key_states.dtype, pin_memory=True)
+                    vc = torch.empty(value_states.shape, dtype=value_states.dtype, pin_memory=True)
+                    kc.copy_(key_states.detach(), non_blocking=True)
+                    vc.copy_(value_states.detach(), non_blocking=True)
+                key_states.record_stream(side)
+                value_states.record_stream(side)
+                self.key_cache_cpu.append(kc)
+                self.value_cache_cpu.append(vc)
+            else:
+                self.key_cache_cpu.append(key_states.detach())
+                self.value_cache_cpu.append(value_states.detach())
+            return key_states, value_states
+
+        # decode append: the free-list check mirrors cache_utils.py:981-990
+        hl = self._hlen[layer_idx]
+        logical = hl // PAGE
+        if np.any(logical >= self.block_tables[layer_idx].shape[1]):
+            raise IndexError(f"Layer {layer_idx}: block table has no column for the next decode token")
+        need = int(np.count_nonzero(logical >= self._mapped[layer_idx]))
+        if need > 0:
+            ptr = self.free_block_pointers[layer_idx]
+            if ptr + need > self.free_blocks[layer_idx].size(0):
+                raise RuntimeError(f"Layer {layer_idx} OOM.")
+            self.free_block_pointers[layer_idx] += need
+            self._mapped[layer_idx] += (logical >= self._mapped[layer_idx])
+        self._wait_retrieval(layer_idx)
+        ops.decode_append(key_states, value_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
+                          self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
+                          self._free_ptr[layer_idx], self._err)
+        hl += 1
+        return key_states, value_states
+
+    def init_coefficient(self, query_states, key_states, layer_idx):
+        """Pivot reference sets (heterocache/cache_utils.py:1149-1190)."""
+        pivots = self.data["need_to_select_counts"][layer_idx]
+        if len(pivots) == 0:
+            self.prefill_topk_set.append([])
+            return
+        if list(pivots) != list(range(pivots[0], pivots[0] + len(pivots))):
+            raise ValueError("pivot heads must be contiguous after the role permutation")
+        bsz = key_states.shape[0]
+        L = key_states.shape[-2]
+        K = self.base_compress_len
+        dev = key_states.device
+        ref = torch.empty(bsz, len(pivots), K, dtype=torch.int32, device=dev)
+        words = (L + 31) // 32
+        bitmap = torch.zeros(bsz, len(pivots), words, dtype=torch.int32, device=dev)
+        ops.pivot_init(query_states, key_states, first_pivot=pivots[0], n_pivots=len(pivots),
+                       groups=self.num_key_value_groups, pooling=self.pooling, kernel_size=self.kernel_size,
+                       topk=K, ref_positions=ref, ref_bitmap=bitmap, workspace=self._ws_score, err=self._err)
+        self._ref_bitmap[layer_idx] = bitmap
+        self.prefill_topk_set.append(ref)
+
+    def prefill_select(self, query_states, key_states, value_states, layer_idx):
+        """Compressed heads (heterocache/cache_utils.py:782-882)."""
+        bsz = query_states.shape[0]
+        nc = self.data["need_to_compress_counts"][layer_idx]
+        if nc == 0:
+            return
+        ratios = torch.tensor(self.data["allocation_matrix"][layer_idx][:nc], dtype=torch.float32)
+        caps = (self.base_compress_len * ratios).int()
+        L = key_states.shape[-2]
+        keep_lens = torch.clamp(caps, max=L)
+        max_k = int(keep_lens.max())
+        if max_k == 0:
+            self.heads_len[layer_idx][:nc] = 0
+            self._hlen[layer_idx][:nc] = 0
+            return
+        keep_dev = keep_lens.to(device=key_states.device, dtype=torch.int32)
+        ops.prefill_select(query_states, key_states, value_states, keep_dev, max_k, n_heads=nc,
+                           groups=self.num_key_value_groups, window=self.window_size, pooling=self.pooling,
+                           kernel_size=self.kernel_size, k_pool=self.key_pools[layer_idx],
+                           v_pool=self.value_pools[layer_idx], block_table=self.block_tables[layer_idx],
+                           heads_len=self.heads_len[layer_idx], workspace=self._ws_score, err=self._err)
+        kl = keep_lens.numpy().astype(np.int64)
+        for b in range(bsz):
+            self._hlen[layer_idx][b * self.num_kv_heads:b * self.num_kv_heads + nc] = kl
+
+    # ------------------------------------------------------------------
+    def decode_select(self, query_states, layer_idx):
+        """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
+        S = self.decode_step
+        if self._qbuf[layer_idx] is None:
+            bsz, H, _, D = query_states.shape
+            if bsz != 1 and self.data["leader_member_relations"][layer_idx]:
+                raise NotImplementedError("decode_select supports batch size 1 (as the reference, "
+                                          "cache_utils.py:1093)")
+            self._qbuf[layer_idx] = torch.empty(S, H, D, dtype=query_states.dtype, device=query_states.device)
+        self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
+        self._qcount[layer_idx] += 1
+        if self._qcount[layer_idx] < S:
+            return
+        self._qcount[layer_idx] = 0
+        relations = self.data["leader_member_relations"][layer_idx]
+        if len(relations) == 0:
+            return
+        jobs = self._jobs[layer_idx]
+        if jobs is None:
+            jobs = _LayerJobs(relations, self.data["allocation_matrix"][layer_idx], self.base_compress_len,
+                              self.prefill_len, query_states.device)
+            if self.record_checks:
+                jobs.coeffs = torch.zeros(max(jobs.n_jobs, 1), S, dtype=torch.float32, device=query_states.device)
+                jobs.median = torch.zeros(max(jobs.n_jobs, 1), dtype=torch.float64, device=query_states.device)
+            self._jobs[layer_idx] = jobs
+        if jobs.n_jobs == 0:
+            return
+        self._wait_retrieval(layer_idx)
+        ops.drift_check(self._qbuf[layer_idx], self.key_pools[layer_idx], self.block_tables[layer_idx],
+                        num_kv_heads=self.num_kv_heads, groups=self.num_key_value_groups, steps=S,
+                        seq_len=self.prefill_len, pooling=self.pooling, kernel_size=self.kernel_size,
+                        topk=self.base_compress_len, threshold=self.stable_threshold,
+                        pivot_heads=jobs.pivot_heads, ref_slots=jobs.ref_slots, max_len=jobs.max_len,
+                        max_len_cap=max(jobs.max_len_cap, 1), ref_bitmap=self._ref_bitmap[layer_idx],
+                        ref_positions=self.prefill_topk_set[layer_idx], trigger=jobs.trigger,
+                        retrieve_positions=jobs.retrieve_positions, workspace=self._ws_score, err=self._err,
+                        coeffs=jobs.coeffs, median=jobs.median)
+        if self.record_checks:
+            self.check_log.append({"layer": layer_idx, "trigger": jobs.trigger.clone(),
+                                   "coeffs": jobs.coeffs.clone(), "median": jobs.median.clone(),
+                                   "retrieved": jobs.retrieve_positions.clone(),
+                                   "pivots": jobs.pivot_heads.tolist()})
+        if jobs.member_job.numel() == 0:
+            return
+        full_k = self.key_cache_cpu[layer_idx]
+        full_v = self.value_cache_cpu[layer_idx]
+        if self.real_offload:
+            main = torch.cuda.current_stream(self._dev)
+            side = self._side()
+            side.wait_stream(main)
+            ops.retrieve(member_job=jobs.member_job, member_head=jobs.member_head, member_len=jobs.member_len,
+                         max_member_len=jobs.max_member_len, trigger=jobs.trigger,
+                         retrieve_positions=jobs.retrieve_positions, full_k=full_k, full_v=full_v,
+                         k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
+                         block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
+                         err=self._err, stream=side)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            self._retrieve_done[layer_idx] = ev
+        else:
+            ops.retrieve(member_job=jobs.member_job, member_head=jobs.member_head, member_len=jobs.member_len,
+                         max_member_len=jobs.max_member_len, trigger=jobs.trigger,
+                         retrieve_positions=jobs.retrieve_positions, full_k=full_k, full_v=full_v,
+                         k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
+                         block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
+                         err=self._err)
+
+    # ------------------------------------------------------------------
+    def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):
+        """Decode attention over this layer's pages: q [bsz, H, 1, D] -> [bsz, H, D]."""
+        self._wait_retrieval(layer_idx)
+        total = int(self._hlen[layer_idx].sum())
+        return ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
+                                self.block_tables[layer_idx], self.heads_len[layer_idx],
+                                num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
+                                err=self._err, total_tokens_hint=total)

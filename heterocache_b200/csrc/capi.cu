@@ -1,0 +1,321 @@
+// extern "C" boundary: argument validation, parameter packing, dispatch.
+#include <cmath>
+#include <cstring>
+
+#include <cstdio>
+
+#include "hc_params.cuh"
+
+namespace {
+
+thread_local char g_last_err[256] = {0};
+
+int note_cuda(int rc) {
+  if (rc == HC_ERR_CUDA) {
+    cudaError_t e = cudaGetLastError();
+    std::snprintf(g_last_err, sizeof(g_last_err), "%s", cudaGetErrorString(e));
+  }
+  return rc;
+}
+
+bool valid_dtype(int dtype) { return dtype == HC_F32 || dtype == HC_BF16 || dtype == HC_F16; }
+int elem_bytes(int dtype) { return dtype == HC_F32 ? 4 : 2; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// Row strides must keep every 128-element row 16-byte aligned.
+bool stride_ok(int dtype, int64_t s) { return (s * elem_bytes(dtype)) % 16 == 0; }
+
+float div_sqrt_d(int head_dim) { return (float)std::sqrt((double)head_dim); }
+
+}  // namespace
+
+extern "C" {
+
+int hc_abi_version(void) { return HC_ABI_VERSION; }
+
+const char* hc_status_string(int status) {
+  switch (status) {
+    case HC_OK: return "ok";
+    case HC_ERR_INVALID: return "invalid argument";
+    case HC_ERR_DTYPE: return "unsupported dtype";
+    case HC_ERR_OOM: return "decode free list exhausted";
+    case HC_ERR_RANGE: return "page-table entry or index out of range";
+    case HC_ERR_CUDA: return "CUDA error";
+    case HC_ERR_WORKSPACE: return "workspace missing or too small";
+    case HC_ERR_TIMEOUT: return "device-side wait timed out";
+    case HC_ERR_UNSUPPORTED: return "unsupported configuration";
+    default: return "unknown status";
+  }
+}
+
+const char* hc_last_cuda_error(void) { return g_last_err; }
+
+int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_dim, const int32_t* keep_heads,
+                    int n_keep, const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, void* k_pool,
+                    void* v_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks, int32_t* heads_len,
+                    int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || seq_len <= 0 || n_keep < 0) return HC_ERR_INVALID;
+  if (n_keep == 0) return HC_OK;
+  if (!aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh) || !stride_ok(dtype, st)) return HC_ERR_INVALID;
+  return note_cuda(hc::prefill_keep_dispatch(dtype, bsz, num_kv_heads, seq_len, keep_heads, n_keep, k, v, sb, sh, st,
+                                             k_pool, v_pool, n_pool_blocks, block_table, max_blocks, heads_len,
+                                             err_flag,
+                                             (cudaStream_t)stream));
+}
+
+size_t hc_prefill_select_workspace_size(int dtype, int bsz, int n_heads, int seq_len, int groups, int window) {
+  if (bsz <= 0 || n_heads <= 0 || seq_len <= 0) return 0;
+  return hc::score_workspace_size(dtype, bsz * n_heads, seq_len, groups * window, 1);
+}
+
+int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_len, int head_dim, int n_heads,
+                      int window, int pooling, int kernel_size, const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                      const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, const int32_t* keep_lens,
+                      int max_keep, void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table,
+                      int max_blocks, int32_t* heads_len, int32_t* out_indices, void* out_scores, void* workspace,
+                      size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || groups <= 0 || seq_len <= 0) return HC_ERR_INVALID;
+  if (n_heads < 0 || n_heads > num_kv_heads) return HC_ERR_INVALID;
+  if (n_heads == 0) return HC_OK;
+  if (window < 1 || window > seq_len) return HC_ERR_INVALID;
+  if (pooling != HC_AVGPOOL && pooling != HC_MAXPOOL) return HC_ERR_INVALID;
+  if (kernel_size < 1 || (kernel_size & 1) == 0 || kernel_size / 2 > 16) return HC_ERR_INVALID;
+  if (groups * window > 256) return HC_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool))
+    return HC_ERR_INVALID;
+  if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh) || !stride_ok(dtype, qst) || !stride_ok(dtype, sb) ||
+      !stride_ok(dtype, sh) || !stride_ok(dtype, st))
+    return HC_ERR_INVALID;
+  hc::ScoreParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mode = hc::MODE_PREFILL;
+  p.L = seq_len;
+  p.G = groups;
+  p.W = window;
+  p.S = 1;
+  p.Rq = groups * window;
+  p.pooling = pooling;
+  p.ksize = kernel_size;
+  p.halo = kernel_size / 2;
+  p.sqrt_d = div_sqrt_d(head_dim);
+  p.n_jobs = bsz * n_heads;
+  p.KV = num_kv_heads;
+  p.nh = n_heads;
+  p.nsel = 1;
+  p.keep_lens = keep_lens;
+  p.q = q;
+  p.qsb = qsb;
+  p.qsh = qsh;
+  p.qst = qst;
+  p.q_tok0 = seq_len - window;
+  p.k = k;
+  p.v = v;
+  p.ksb = sb;
+  p.ksh = sh;
+  p.kst = st;
+  p.bt = block_table;
+  p.max_blocks = max_blocks;
+  p.n_blocks = n_pool_blocks;
+  p.k_pool_out = k_pool;
+  p.v_pool_out = v_pool;
+  p.heads_len = heads_len;
+  p.out_indices = out_indices;
+  p.max_keep = max_keep;
+  p.out_scores = out_scores;
+  p.err = err_flag;
+  return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+size_t hc_pivot_init_workspace_size(int dtype, int bsz, int n_pivots, int seq_len, int groups) {
+  if (bsz <= 0 || n_pivots <= 0 || seq_len <= 0) return 0;
+  return hc::score_workspace_size(dtype, bsz * n_pivots, seq_len, groups, 1);
+}
+
+int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len, int head_dim, int first_pivot,
+                  int n_pivots, int pooling, int kernel_size, int topk, const void* q, int64_t qsb, int64_t qsh,
+                  int64_t qst, const void* k, int64_t sb, int64_t sh, int64_t st, int32_t* ref_positions,
+                  uint32_t* ref_bitmap, void* out_scores, void* workspace, size_t workspace_bytes, int32_t* err_flag,
+                  void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || groups <= 0 || seq_len <= 0) return HC_ERR_INVALID;
+  if (n_pivots == 0) return HC_OK;
+  if (n_pivots < 0 || first_pivot < 0 || first_pivot + n_pivots > num_kv_heads) return HC_ERR_INVALID;
+  if (topk < 0 || topk > seq_len) return HC_ERR_INVALID;
+  if (pooling != HC_AVGPOOL && pooling != HC_MAXPOOL) return HC_ERR_INVALID;
+  if (kernel_size < 1 || (kernel_size & 1) == 0 || kernel_size / 2 > 16) return HC_ERR_INVALID;
+  if (groups > 256) return HC_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh) || !stride_ok(dtype, qst) || !stride_ok(dtype, sb) ||
+      !stride_ok(dtype, sh) || !stride_ok(dtype, st))
+    return HC_ERR_INVALID;
+  hc::ScoreParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mode = hc::MODE_PIVOT;
+  p.L = seq_len;
+  p.G = groups;
+  p.W = 1;
+  p.S = 1;
+  p.Rq = groups;
+  p.pooling = pooling;
+  p.ksize = kernel_size;
+  p.halo = kernel_size / 2;
+  p.sqrt_d = div_sqrt_d(head_dim);
+  p.n_jobs = bsz * n_pivots;
+  p.KV = num_kv_heads;
+  p.nh = n_pivots;
+  p.first_head = first_pivot;
+  p.nsel = 1;
+  p.topk = topk;
+  p.q = q;
+  p.qsb = qsb;
+  p.qsh = qsh;
+  p.qst = qst;
+  p.q_tok0 = seq_len - 1;
+  p.k = k;
+  p.ksb = sb;
+  p.ksh = sh;
+  p.kst = st;
+  p.ref_positions = ref_positions;
+  p.ref_bitmap = ref_bitmap;
+  p.bitmap_words = (seq_len + 31) / 32;
+  p.out_scores = out_scores;
+  p.err = err_flag;
+  return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+int hc_decode_append(int dtype, int bsz, int num_kv_heads, int head_dim, const void* k, const void* v, int64_t sb,
+                     int64_t sh, void* k_pool, void* v_pool, int n_pool_blocks, int32_t* block_table, int max_blocks,
+                     int32_t* heads_len, const int32_t* free_blocks, int n_free, int32_t* free_ptr,
+                     int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || max_blocks <= 0 || n_free < 0)
+    return HC_ERR_INVALID;
+  if (!aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh)) return HC_ERR_INVALID;
+  return note_cuda(hc::decode_append_dispatch(dtype, bsz * num_kv_heads, num_kv_heads, k, v, sb, sh, k_pool, v_pool,
+                                              n_pool_blocks, block_table, max_blocks, heads_len, free_blocks, n_free, free_ptr,
+                                              err_flag, (cudaStream_t)stream));
+}
+
+size_t hc_flash_decode_workspace_size(int bsz, int num_kv_heads, int groups, int head_dim) {
+  (void)head_dim;
+  if (bsz <= 0 || num_kv_heads <= 0 || groups <= 0) return 0;
+  return hc::flash_decode_ws_bytes(bsz * num_kv_heads, groups);
+}
+
+int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q, int64_t qsb,
+                    int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
+                    const int32_t* block_table, int max_blocks, const int32_t* heads_len, float scale, void* out, long long total_tokens_hint, void* workspace,
+                    size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  (void)total_tokens_hint;
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || groups <= 0 || max_blocks <= 0)
+    return HC_ERR_INVALID;
+  if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh)) return HC_ERR_INVALID;
+  hc::FDParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.qsb = qsb;
+  p.qsh = qsh;
+  p.kp = k_pool;
+  p.vp = v_pool;
+  p.bt = block_table;
+  p.max_blocks = max_blocks;
+  p.n_blocks = n_pool_blocks;
+  p.heads_len = heads_len;
+  p.R = bsz * num_kv_heads;
+  p.KV = num_kv_heads;
+  p.G = groups;
+  const float sc = scale > 0.f ? scale : (float)(1.0 / std::sqrt((double)head_dim));
+  p.scale_log2 = sc * 1.4426950408889634f;
+  p.out = out;
+  p.err = err_flag;
+  return note_cuda(hc::flash_decode_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+size_t hc_drift_check_workspace_size(int dtype, int n_jobs, int steps, int seq_len, int groups) {
+  if (n_jobs <= 0 || steps <= 0 || seq_len <= 0) return 0;
+  return hc::score_workspace_size(dtype, n_jobs, seq_len, steps * groups, steps);
+}
+
+int hc_drift_check(int dtype, int num_kv_heads, int groups, int head_dim, int steps, int seq_len, int pooling,
+                   int kernel_size, int topk, double threshold, const void* qbuf, int64_t qss, int64_t qsh,
+                   const void* k_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks, int n_jobs,
+                   const int32_t* pivot_heads, const int32_t* ref_slots, const int32_t* max_len, int max_len_cap,
+                   uint32_t* ref_bitmap, int32_t* ref_positions, int32_t* trigger, float* coeffs, double* median,
+                   int32_t* retrieve_positions, void* out_scores, void* workspace, size_t workspace_bytes,
+                   int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || num_kv_heads <= 0 || groups <= 0 || seq_len <= 0) return HC_ERR_INVALID;
+  if (n_jobs == 0) return HC_OK;
+  if (n_jobs < 0 || steps < 1 || steps > 7) return steps > 7 ? HC_ERR_UNSUPPORTED : HC_ERR_INVALID;
+  if (topk < 0 || topk > seq_len || max_len_cap < 0) return HC_ERR_INVALID;
+  if (pooling != HC_AVGPOOL && pooling != HC_MAXPOOL) return HC_ERR_INVALID;
+  if (kernel_size < 1 || (kernel_size & 1) == 0 || kernel_size / 2 > 16) return HC_ERR_INVALID;
+  if (steps * groups > 256) return HC_ERR_UNSUPPORTED;
+  if (!aligned16(qbuf) || !aligned16(k_pool)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, qss) || !stride_ok(dtype, qsh)) return HC_ERR_INVALID;
+  if ((seq_len + HC_PAGE_SIZE - 1) / HC_PAGE_SIZE > max_blocks) return HC_ERR_INVALID;
+  hc::ScoreParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mode = hc::MODE_DRIFT;
+  p.L = seq_len;
+  p.G = groups;
+  p.W = 1;
+  p.S = steps;
+  p.Rq = steps * groups;
+  p.pooling = pooling;
+  p.ksize = kernel_size;
+  p.halo = kernel_size / 2;
+  p.sqrt_d = div_sqrt_d(head_dim);
+  p.n_jobs = n_jobs;
+  p.KV = num_kv_heads;
+  p.nh = n_jobs;
+  p.nsel = steps + 1;
+  p.job_heads = pivot_heads;
+  p.topk = topk;
+  p.max_len = max_len;
+  p.q = qbuf;
+  p.qsb = 0;
+  p.qsh = qsh;
+  p.qst = qss;
+  p.q_tok0 = 0;
+  p.k_pool = k_pool;
+  p.bt = block_table;
+  p.max_blocks = max_blocks;
+  p.n_blocks = n_pool_blocks;
+  p.ref_slots = ref_slots;
+  p.ref_bitmap = ref_bitmap;
+  p.ref_positions = ref_positions;
+  p.bitmap_words = (seq_len + 31) / 32;
+  p.trigger = trigger;
+  p.coeffs = coeffs;
+  p.median = median;
+  p.retrieve_positions = retrieve_positions;
+  p.max_len_cap = max_len_cap;
+  p.threshold = threshold;
+  p.out_scores = out_scores;
+  p.err = err_flag;
+  return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+int hc_retrieve(int dtype, int num_kv_heads, int head_dim, int n_members, const int32_t* member_job,
+                const int32_t* member_head, const int32_t* member_len, int max_member_len, const int32_t* trigger,
+                const int32_t* retrieve_positions, int retrieve_stride, const void* full_k, const void* full_v,
+                int64_t fsh, int64_t fst, void* k_pool, void* v_pool, int n_pool_blocks,
+                const int32_t* block_table, int max_blocks, int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || num_kv_heads <= 0 || n_members < 0 || max_blocks <= 0) return HC_ERR_INVALID;
+  if (n_members == 0) return HC_OK;
+  if (!aligned16(full_k) || !aligned16(full_v) || !aligned16(k_pool) || !aligned16(v_pool)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, fsh) || !stride_ok(dtype, fst)) return HC_ERR_INVALID;
+  return note_cuda(hc::retrieve_dispatch(dtype, n_members, member_job, member_head, member_len, max_member_len,
+                                         trigger, retrieve_positions, retrieve_stride, full_k, full_v, fsh, fst,
+                                         k_pool, v_pool, n_pool_blocks, block_table, max_blocks, err_flag,
+                                         (cudaStream_t)stream));
+}
+
+}  // extern "C"

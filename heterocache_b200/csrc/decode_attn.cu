@@ -1,0 +1,365 @@
+// Split-K paged flash-decode over ragged per-(batch, KV head) lengths.
+//
+// Replaces flash_attn_with_kvcache(q[bsz*KV, 1, G, D], k_pool, v_pool,
+// cache_seqlens=heads_len, block_table, causal=False) as called by the
+// patched attention (heterocache/llama_model.py:370-397,
+// heterocache/qwen_model.py:181-206).
+//
+// Work split: every row's length is padded to a multiple of 16 and the rows
+// are laid end to end; the grid (a fixed number of CTAs per SM) cuts that
+// flattened token space into equal spans, so every CTA streams the same
+// number of KV bytes whatever the per-head budgets are.  A CTA's span covers
+// one or more row pieces; per piece the 4 warps take 16-token groups (a group
+// never crosses a 256-token page), keep an online softmax per query head,
+// and are merged in shared memory into one partial (m, l, o[G][D]) stored at
+// slot (cta + row).  A second kernel merges each row's partials.
+//
+// Per 16-token group a warp issues 8 x 16-byte key loads and 16 x 8-byte
+// value loads per lane (coalesced 256-byte rows), computes q.K^T for the G
+// query heads with two m16n8k16 MMAs per 16 dims (queries on M, padded to 16;
+// tokens on N), and accumulates P.V on the CUDA cores with each lane owning 4
+// of the 128 output dims.
+#include "hc_params.cuh"
+
+namespace hc {
+
+
+
+// Padded prefix of row lengths into s_start[0..R]; returns total.
+__device__ __forceinline__ int row_prefix(const FDParams& p, int* s_start, int* s_warp) {
+  int carry = 0;
+  for (int c0 = 0; c0 < p.R; c0 += blockDim.x) {
+    int r = c0 + threadIdx.x;
+    int len = r < p.R ? p.heads_len[r] : 0;
+    len = len < 0 ? 0 : len;
+    int l16 = (len + 15) & ~15;
+    int tot;
+    int ex = block_exclusive_scan(l16, s_warp, tot);
+    if (r < p.R) s_start[r] = carry + ex;
+    carry += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) s_start[p.R] = carry;
+  __syncthreads();
+  return carry;
+}
+
+__device__ __forceinline__ int span_of(int total, int nctas) {
+  int s = (total + nctas - 1) / nctas;
+  return (s + 15) & ~15;
+}
+
+template <typename T>
+struct WarpState {
+  float m, l;           // for query head gid (identical across the 4 lanes of a gid)
+  float o[kGMax][4];    // dims 4*lane .. 4*lane+3 for every query head
+};
+
+// 16-bit dtypes: tensor-core q.K^T.
+template <typename T>
+__device__ __forceinline__ void fd_group_mma(const FDParams& p, WarpState<T>& st, const uint32_t (&qa)[8][2],
+                                             const T* kbase, const T* vbase, int valid, float* sp, float* sc) {
+  const int lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
+  uint4 kf[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int s = 0; s < 4; ++s) kf[nt][s] = ld_stream128(kbase + (8 * nt + gid) * kD + 32 * s + 8 * tig);
+  uint2 vf[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) vf[i] = ld_stream64(vbase + i * kD + 4 * lane);
+
+  float acc[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll
+  for (int s = 0; s < 4; ++s)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      mma16816<T>(acc[nt], qa[2 * s][0], 0u, qa[2 * s][1], 0u, kf[nt][s].x, kf[nt][s].y);
+      mma16816<T>(acc[nt], qa[2 * s + 1][0], 0u, qa[2 * s + 1][1], 0u, kf[nt][s].z, kf[nt][s].w);
+    }
+  float sv[4];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 8 * nt + 2 * tig + e;
+      float x = t < valid ? acc[nt][e] * p.scale_log2 : -INFINITY;
+      sv[nt * 2 + e] = x;
+      mx = fmaxf(mx, x);
+    }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float mnew = fmaxf(st.m, mx);
+  const float corr = (mnew == -INFINITY) ? 1.f : exp2f(st.m - mnew);
+  float rs = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float pv = (sv[i] == -INFINITY) ? 0.f : exp2f(sv[i] - mnew);
+    sv[i] = pv;
+    rs += pv;
+  }
+  rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+  rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+  st.l = st.l * corr + rs;
+  st.m = mnew;
+  if (gid < p.G) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      sp[gid * 16 + 8 * nt + 2 * tig] = sv[nt * 2];
+      sp[gid * 16 + 8 * nt + 2 * tig + 1] = sv[nt * 2 + 1];
+    }
+    if (tig == 0) sc[gid] = corr;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int g = 0; g < kGMax; ++g) {
+    if (g < p.G) {
+      const float c = sc[g];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.o[g][j] *= c;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 v01 = unpack2<T>(vf[i].x);
+    const float2 v23 = unpack2<T>(vf[i].y);
+#pragma unroll
+    for (int g = 0; g < kGMax; ++g) {
+      if (g < p.G) {
+        const float pv = sp[g * 16 + i];
+        st.o[g][0] = fmaf(pv, v01.x, st.o[g][0]);
+        st.o[g][1] = fmaf(pv, v01.y, st.o[g][1]);
+        st.o[g][2] = fmaf(pv, v23.x, st.o[g][2]);
+        st.o[g][3] = fmaf(pv, v23.y, st.o[g][3]);
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// fp32: lanes over dims, warp all-reduce per (query head, token).
+__device__ __forceinline__ void fd_group_f32(const FDParams& p, WarpState<float>& st, const float (&qf)[kGMax][4],
+                                             const float* kbase, const float* vbase, int valid, float (&mrow)[kGMax],
+                                             float (&lrow)[kGMax]) {
+  const int lane = threadIdx.x & 31;
+  for (int i = 0; i < 16; ++i) {
+    if (i >= valid) break;
+    const float4 k4 = *reinterpret_cast<const float4*>(kbase + i * kD + 4 * lane);
+    const float4 v4 = *reinterpret_cast<const float4*>(vbase + i * kD + 4 * lane);
+#pragma unroll
+    for (int g = 0; g < kGMax; ++g) {
+      if (g >= p.G) continue;
+      float s = qf[g][0] * k4.x + qf[g][1] * k4.y + qf[g][2] * k4.z + qf[g][3] * k4.w;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      s *= p.scale_log2;
+      const float mnew = fmaxf(mrow[g], s);
+      const float corr = exp2f(mrow[g] - mnew);
+      const float pv = exp2f(s - mnew);
+      lrow[g] = lrow[g] * corr + pv;
+      mrow[g] = mnew;
+      st.o[g][0] = st.o[g][0] * corr + pv * v4.x;
+      st.o[g][1] = st.o[g][1] * corr + pv * v4.y;
+      st.o[g][2] = st.o[g][2] * corr + pv * v4.z;
+      st.o[g][3] = st.o[g][3] * corr + pv * v4.w;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int* s_start = reinterpret_cast<int*>(smem_raw);
+  __shared__ int s_warp[32];
+  __shared__ float s_p[kFWarps][kGMax * 16];
+  __shared__ float s_c[kFWarps][kGMax];
+  __shared__ float s_m[kFWarps][kGMax], s_l[kFWarps][kGMax];
+  __shared__ float s_o[kFWarps][kGMax][kD];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int total = row_prefix(p, s_start, s_warp);
+  const int span = span_of(total, gridDim.x);
+  const int beg = blockIdx.x * span;
+  if (beg >= total) return;
+  const int end = min(total, beg + span);
+  // first row with s_start[r+1] > beg
+  int lo = 0, hi = p.R - 1;
+  while (lo < hi) {
+    int mid = (lo + hi) >> 1;
+    if (s_start[mid + 1] > beg) hi = mid; else lo = mid + 1;
+  }
+  for (int r = lo; r < p.R && s_start[r] < end; ++r) {
+    const int rs = s_start[r], re = s_start[r + 1];
+    if (re <= beg || re == rs) continue;
+    const int a = max(rs, beg) - rs, bnd = min(re, end) - rs;
+    const int len = p.heads_len[r];
+    const int b = r / p.KV, h = r % p.KV;
+    const T* qrow0 = reinterpret_cast<const T*>(p.q) + b * p.qsb + (int64_t)(h * p.G) * p.qsh;
+
+    WarpState<T> st;
+    st.m = -INFINITY;
+    st.l = 0.f;
+#pragma unroll
+    for (int g = 0; g < kGMax; ++g) st.o[g][0] = st.o[g][1] = st.o[g][2] = st.o[g][3] = 0.f;
+
+    if constexpr (std::is_same<T, float>::value) {
+      float qf[kGMax][4];
+      float mrow[kGMax], lrow[kGMax];
+#pragma unroll
+      for (int g = 0; g < kGMax; ++g) {
+        mrow[g] = -INFINITY;
+        lrow[g] = 0.f;
+        if (g < p.G) {
+          float4 q4 = *reinterpret_cast<const float4*>(qrow0 + g * p.qsh + 4 * lane);
+          qf[g][0] = q4.x; qf[g][1] = q4.y; qf[g][2] = q4.z; qf[g][3] = q4.w;
+        } else {
+          qf[g][0] = qf[g][1] = qf[g][2] = qf[g][3] = 0.f;
+        }
+      }
+      for (int t16 = a + warp * 16; t16 < bnd; t16 += kFWarps * 16) {
+        const int page = t16 >> 8;
+        int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
+        if (blk < 0 || blk >= p.n_blocks) { set_err(p.err, HC_ERR_RANGE); continue; }
+        const int64_t off = ((int64_t)blk * kPage + (t16 & (kPage - 1))) * kD;
+        fd_group_f32(p, st, qf, reinterpret_cast<const float*>(p.kp) + off,
+                     reinterpret_cast<const float*>(p.vp) + off, min(16, len - t16), mrow, lrow);
+      }
+      if (lane == 0) {
+        for (int g = 0; g < kGMax; ++g) { s_m[warp][g] = mrow[g]; s_l[warp][g] = lrow[g]; }
+      }
+    } else {
+      uint32_t qa[8][2];
+      const T* qg = qrow0 + (gid < p.G ? gid : 0) * p.qsh;
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          uint2 w = gid < p.G ? ldg64(qg + 32 * s + 8 * tig + 4 * u) : make_uint2(0u, 0u);
+          qa[2 * s + u][0] = w.x;
+          qa[2 * s + u][1] = w.y;
+        }
+      for (int t16 = a + warp * 16; t16 < bnd; t16 += kFWarps * 16) {
+        const int page = t16 >> 8;
+        int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
+        if (blk < 0 || blk >= p.n_blocks) { set_err(p.err, HC_ERR_RANGE); continue; }
+        const int64_t off = ((int64_t)blk * kPage + (t16 & (kPage - 1))) * kD;
+        fd_group_mma<T>(p, st, qa, reinterpret_cast<const T*>(p.kp) + off, reinterpret_cast<const T*>(p.vp) + off,
+                        min(16, len - t16), s_p[warp], s_c[warp]);
+      }
+      if (tig == 0 && gid < kGMax) {
+        s_m[warp][gid] = st.m;
+        s_l[warp][gid] = st.l;
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kGMax; ++g)
+      if (g < p.G)
+        *reinterpret_cast<float4*>(&s_o[warp][g][4 * lane]) = make_float4(st.o[g][0], st.o[g][1], st.o[g][2], st.o[g][3]);
+    __syncthreads();
+    // merge the 4 warps: thread d owns output dim d
+    const int d = threadIdx.x;
+    const int slot = blockIdx.x + r;
+    for (int g = 0; g < p.G; ++g) {
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kFWarps; ++w) M = fmaxf(M, s_m[w][g]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kFWarps; ++w) {
+        const float f = (s_m[w][g] == -INFINITY) ? 0.f : exp2f(s_m[w][g] - M);
+        L += f * s_l[w][g];
+        O += f * s_o[w][g][d];
+      }
+      p.part_o[((size_t)slot * p.G + g) * kD + d] = O;
+      if (d == 0) p.part_ml[(size_t)slot * p.G + g] = make_float2(M, L);
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFThreads) flash_combine_kernel(FDParams p, int nctas) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  int* s_start = reinterpret_cast<int*>(smem_raw);
+  __shared__ int s_warp[32];
+  const int total = row_prefix(p, s_start, s_warp);
+  const int span = span_of(total, nctas);
+  const int r = blockIdx.x;
+  const int d = threadIdx.x;
+  T* out = reinterpret_cast<T*>(p.out) + (size_t)r * p.G * kD;
+  const int rs = s_start[r], re = s_start[r + 1];
+  if (re == rs || span == 0) {
+    for (int g = 0; g < p.G; ++g) out[g * kD + d] = Elem<T>::from_f(0.f);
+    return;
+  }
+  const int c0 = rs / span, c1 = (re - 1) / span;
+  for (int g = 0; g < p.G; ++g) {
+    float M = -INFINITY;
+    for (int c = c0; c <= c1; ++c) M = fmaxf(M, p.part_ml[(size_t)(c + r) * p.G + g].x);
+    float L = 0.f, O = 0.f;
+    for (int c = c0; c <= c1; ++c) {
+      const float2 ml = p.part_ml[(size_t)(c + r) * p.G + g];
+      const float f = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+      L += f * ml.y;
+      O += f * p.part_o[((size_t)(c + r) * p.G + g) * kD + d];
+    }
+    out[g * kD + d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
+  }
+}
+
+static int fd_grid(int dtype) {
+  static int cached[3] = {0, 0, 0};
+  if (cached[dtype]) return cached[dtype];
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int occ = 0;
+  size_t dsm = (kMaxRowsFD + 1) * sizeof(int);
+  switch (dtype) {
+    case HC_F32: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, flash_decode_kernel<float>, kFThreads, dsm); break;
+    case HC_BF16: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, flash_decode_kernel<__nv_bfloat16>, kFThreads, dsm); break;
+    default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, flash_decode_kernel<__half>, kFThreads, dsm); break;
+  }
+  if (occ <= 0) occ = 1;
+  cached[dtype] = sms * occ;
+  return cached[dtype];
+}
+
+size_t flash_decode_ws_bytes(int R, int G) {
+  const size_t slots = (size_t)148 * 32 + R;
+  return slots * G * kD * sizeof(float) + slots * G * sizeof(float2) + 256;
+}
+
+template <typename T>
+static int fd_launch(FDParams& p, int grid, size_t dsm, cudaStream_t st) {
+  flash_decode_kernel<T><<<grid, kFThreads, dsm, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
+  flash_combine_kernel<T><<<p.R, kFThreads, dsm, st>>>(p, grid);
+  if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
+  return HC_OK;
+}
+
+int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (p.R <= 0 || p.R > kMaxRowsFD) return HC_ERR_UNSUPPORTED;
+  if (p.G <= 0 || p.G > kGMax) return HC_ERR_UNSUPPORTED;
+  const int grid = fd_grid(dtype);
+  const size_t slots = (size_t)grid + p.R;
+  const size_t need = slots * p.G * kD * sizeof(float) + slots * p.G * sizeof(float2);
+  if (!ws || ws_bytes < need) return HC_ERR_WORKSPACE;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
+  const size_t dsm = (size_t)(p.R + 1) * sizeof(int);
+  switch (dtype) {
+    case HC_F32: return fd_launch<float>(p, grid, dsm, st);
+    case HC_BF16: return fd_launch<__nv_bfloat16>(p, grid, dsm, st);
+    case HC_F16: return fd_launch<__half>(p, grid, dsm, st);
+    default: return HC_ERR_DTYPE;
+  }
+}
+
+}  // namespace hc

@@ -1,0 +1,225 @@
+// Shared device helpers for the sm_100a compressed-KV attention path.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "heterocache_b200.h"
+
+namespace hc {
+
+constexpr int kPage = HC_PAGE_SIZE;
+constexpr int kD = HC_HEAD_DIM;
+
+// ---------------------------------------------------------------------------
+// Element traits.  `rnd` rounds an fp32 value to the element type and back
+// (round to nearest even), which is how the reference's tensors in the model
+// dtype hold every intermediate.  `key` maps a value that is exactly
+// representable in the element type to an unsigned integer whose order is the
+// value's order (the radix-select key); kKeyBits is its width.
+template <typename T> struct Elem;
+
+template <> struct Elem<float> {
+  static constexpr int kKeyBits = 32;
+  __device__ __forceinline__ static float to_f(float x) { return x; }
+  __device__ __forceinline__ static float from_f(float x) { return x; }
+  __device__ __forceinline__ static float rnd(float x) { return x; }
+  __device__ __forceinline__ static uint32_t key(float x) {
+    uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  }
+  __device__ __forceinline__ static float unkey(uint32_t k) {
+    uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(b);
+  }
+};
+
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int kKeyBits = 16;
+  __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+  __device__ __forceinline__ static float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+  __device__ __forceinline__ static uint32_t key(float x) {
+    uint32_t b = __float_as_uint(x) >> 16;  // exact: x is a bf16 value
+    return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+  }
+  __device__ __forceinline__ static float unkey(uint32_t k) {
+    uint32_t b = (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu);
+    return __uint_as_float(b << 16);
+  }
+};
+
+template <> struct Elem<__half> {
+  static constexpr int kKeyBits = 16;
+  __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
+  __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
+  __device__ __forceinline__ static float rnd(float x) { return __half2float(__float2half_rn(x)); }
+  __device__ __forceinline__ static uint32_t key(float x) {
+    uint32_t b = (uint32_t)__half_as_ushort(__float2half_rn(x));  // exact: x is an f16 value
+    return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+  }
+  __device__ __forceinline__ static float unkey(uint32_t k) {
+    uint32_t b = (k & 0x8000u) ? (k & 0x7fffu) : (~k & 0xffffu);
+    return __half2float(__ushort_as_half((unsigned short)b));
+  }
+};
+
+// Unpack two 16-bit elements of a 32-bit word to fp32.
+template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t w);
+template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  return __half22float2(h);
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level tensor-core product D += A(16x16) * B(16x8), fp32 accumulate.
+template <typename T> __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                                uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1);
+template <> __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                                     uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <> __device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                              uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg128(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ uint2 ldg64(const void* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+
+// Streaming load that does not allocate in L1 (data read once).
+__device__ __forceinline__ uint4 ld_stream128(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint2 ld_stream64(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void set_err(int32_t* err, int code) {
+  if (err) atomicOr(err, 1 << code);
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// Grid barrier for cooperative launches (all CTAs co-resident).  Monotonic
+// arrival counter: barrier number e completes when count >= e * nblocks.
+// Every wait is bounded (kBarrierTimeoutNs); on timeout the CTA sets `abort`
+// and HC_ERR_TIMEOUT and every CTA leaves the kernel at its next barrier.
+// The state resets itself: after the final barrier each CTA increments
+// `depart`, and the last to depart zeroes the counters.
+struct GridBarrier {
+  unsigned int count;
+  unsigned int depart;
+  unsigned int abort;
+  unsigned int pad;
+};
+
+constexpr uint64_t kBarrierTimeoutNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Returns false if the grid aborted (caller must return).
+__device__ __forceinline__ bool grid_sync(GridBarrier* gb, unsigned int nblocks, unsigned int& epoch,
+                                          int32_t* err) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    epoch += 1;
+    const unsigned int target = epoch * nblocks;
+    __threadfence();
+    atomicAdd(&gb->count, 1u);
+    int ok = 1;
+    uint64_t t0 = 0;
+    unsigned int spins = 0;
+    while (true) {
+      if (ld_acquire_u32(&gb->count) >= target) break;
+      if (ld_acquire_u32(&gb->abort)) { ok = 0; break; }
+      if ((++spins & 63u) == 0) {
+        uint64_t now = globaltimer_ns();
+        if (t0 == 0) t0 = now;
+        else if (now - t0 > kBarrierTimeoutNs) {
+          atomicExch(&gb->abort, 1u);
+          set_err(err, HC_ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+      __nanosleep(40);
+    }
+    __threadfence();
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+// Call once per CTA after its last grid_sync (only if no abort happened).
+__device__ __forceinline__ void grid_depart(GridBarrier* gb, unsigned int nblocks) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned int d = atomicAdd(&gb->depart, 1u);
+    if (d == nblocks - 1) {
+      gb->count = 0;
+      gb->depart = 0;
+      __threadfence();
+    }
+  }
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int& total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int w = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) s_warp[lane] = w;  // inclusive warp totals
+  }
+  __syncthreads();
+  total = s_warp[nw - 1];
+  int base = wid > 0 ? s_warp[wid - 1] : 0;
+  int excl = base + x - v;
+  __syncthreads();
+  return excl;
+}
+
+}  // namespace hc

@@ -1,0 +1,106 @@
+// Launch parameter blocks and host dispatch entry points shared by the
+// kernels and the C ABI layer.
+#pragma once
+
+#include <type_traits>
+
+#include "hc_common.cuh"
+
+namespace hc {
+
+// ---- fused scoring / selection (score_select.cu)
+constexpr int kSThreads = 256;
+constexpr int kSWarps = kSThreads / 32;
+constexpr int kMargin = 16;
+constexpr int kMaxSel = 8;
+constexpr int kMaxRq = 256;
+constexpr int kMaxRows = 7;
+
+enum { MODE_PREFILL = 0, MODE_PIVOT = 1, MODE_DRIFT = 2 };
+
+struct ScoreParams {
+  int mode, L, G, W, S, Rq, pooling, ksize, halo;
+  float sqrt_d;
+  int n_jobs, cpj, T, TB, KV, nh, first_head, nsel;
+  const int32_t* job_heads;
+  const int32_t* keep_lens;
+  int topk;
+  const int32_t* max_len;
+  const void* q;
+  int64_t qsb, qsh, qst;
+  int q_tok0;
+  const void* k;
+  const void* v;
+  int64_t ksb, ksh, kst;
+  const void* k_pool;
+  const int32_t* bt;
+  int max_blocks;
+  int n_blocks;
+  void* k_pool_out;
+  void* v_pool_out;
+  int32_t* heads_len;
+  int32_t* out_indices;
+  int max_keep;
+  void* out_scores;
+  const int32_t* ref_slots;
+  uint32_t* ref_bitmap;
+  int32_t* ref_positions;
+  int bitmap_words;
+  int32_t* trigger;
+  float* coeffs;
+  double* median;
+  int32_t* retrieve_positions;
+  int max_len_cap;
+  double threshold;
+  GridBarrier* gb;
+  float2* part;
+  unsigned int* hist;
+  int2* cnt;
+  unsigned int* overlap;
+  void* glogits;
+  int logits_in_smem;
+  int32_t* err;
+};
+
+size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S);
+int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// ---- paged flash-decode (decode_attn.cu)
+constexpr int kFThreads = 128;
+constexpr int kFWarps = 4;
+constexpr int kGMax = 8;
+constexpr int kMaxRowsFD = 4096;
+
+struct FDParams {
+  const void* q;
+  int64_t qsb, qsh;
+  const void* kp;
+  const void* vp;
+  const int32_t* bt;
+  int max_blocks;
+  int n_blocks;
+  const int32_t* heads_len;
+  int R, KV, G;
+  float scale_log2;
+  float* part_o;
+  float2* part_ml;
+  void* out;
+  int32_t* err;
+};
+
+size_t flash_decode_ws_bytes(int R, int G);
+int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// ---- page copies (kv_copy.cu)
+int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k,
+                          const void* v, int64_t sb, int64_t sh, int64_t st, void* kp, void* vp, int nblocks,
+                          const int32_t* bt, int mb, int32_t* hl, int32_t* err, cudaStream_t s);
+int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, void* kp,
+                           void* vp, int nblocks, int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf,
+                           int32_t* fp, int32_t* err, cudaStream_t s);
+int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,
+                      const int32_t* trig, const int32_t* pos, int pos_stride, const void* fk, const void* fv,
+                      int64_t fsh, int64_t fst, void* kp, void* vp, int nblocks, const int32_t* bt, int mb,
+                      int32_t* err, cudaStream_t s);
+
+}  // namespace hc

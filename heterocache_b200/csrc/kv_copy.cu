@@ -1,0 +1,232 @@
+// Page writes of the HeteroCache path that are plain data movement:
+//   prefill keep-head copy   (heterocache/cache_utils.py:914-937)
+//   decode append            (heterocache/cache_utils.py:970-1005)
+//   satellite retrieval      (heterocache/cache_utils.py:1084-1147)
+// All three move whole 128-element rows with 16-byte vector accesses.
+#include "hc_params.cuh"
+
+namespace hc {
+
+// ---------------------------------------------------------------------------
+// Prefill: copy keep heads' [L, D] rows into their pages; heads_len = L.
+template <typename T>
+__global__ void __launch_bounds__(256) prefill_keep_kernel(const T* __restrict__ k, const T* __restrict__ v,
+                                                           int64_t sb, int64_t sh, int64_t st, int L, int KV,
+                                                           const int32_t* __restrict__ keep_heads, T* k_pool,
+                                                           T* v_pool, int n_blocks, const int32_t* __restrict__ bt,
+                                                           int max_blocks, int32_t* heads_len, int32_t* err) {
+  constexpr int CH = kD * sizeof(T) / 16;  // 16-byte chunks per row
+  constexpr int RPP = 256 / CH;            // rows per pass
+  const int b = blockIdx.z, i = blockIdx.y;
+  const int h = keep_heads[i];
+  const int row = b * KV + h;
+  const int c = threadIdx.x % CH;
+  const int t0 = blockIdx.x * 64;
+  for (int t = t0 + threadIdx.x / CH; t < min(L, t0 + 64); t += RPP) {
+    const int page = t >> 8;
+    const int blk = page < max_blocks ? bt[(int64_t)row * max_blocks + page] : -1;
+    if (blk < 0 || blk >= n_blocks) {
+      if (c == 0) set_err(err, HC_ERR_RANGE);
+      continue;
+    }
+    const int64_t src = b * sb + (int64_t)h * sh + (int64_t)t * st;
+    const int64_t dst = ((int64_t)blk * kPage + (t & (kPage - 1))) * kD;
+    reinterpret_cast<uint4*>(k_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(k + src) + c);
+    reinterpret_cast<uint4*>(v_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(v + src) + c);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) heads_len[row] = L;
+}
+
+// ---------------------------------------------------------------------------
+// Decode append.  One CTA; rows that need a page take one from the free list
+// in row order (the reference assigns free_blocks[ptr:ptr+n] to the rows of
+// the boolean mask in order).
+template <typename T>
+__global__ void __launch_bounds__(256) decode_append_kernel(const T* __restrict__ k, const T* __restrict__ v,
+                                                            int64_t sb, int64_t sh, int R, int KV, T* k_pool,
+                                                            T* v_pool, int n_blocks, int32_t* bt, int max_blocks,
+                                                            int32_t* heads_len, const int32_t* __restrict__ free_blocks,
+                                                            int n_free, int32_t* free_ptr, int32_t* err) {
+  __shared__ int s_warp[32];
+  __shared__ int s_total, s_fail;
+  const int base_ptr = *free_ptr;
+  int carry = 0;
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  // pass 1: count needed pages and detect range errors
+  for (int c0 = 0; c0 < R; c0 += blockDim.x) {
+    const int r = c0 + threadIdx.x;
+    int need = 0;
+    if (r < R) {
+      const int len = heads_len[r];
+      const int blk = len >> 8;
+      if (len < 0 || blk >= max_blocks) {
+        atomicExch(&s_fail, HC_ERR_RANGE);
+      } else {
+        const int phys = bt[(int64_t)r * max_blocks + blk];
+        need = phys == -1;
+        if (phys < -1 || phys >= n_blocks) atomicExch(&s_fail, HC_ERR_RANGE);
+      }
+    }
+    int tot;
+    block_exclusive_scan(need, s_warp, tot);
+    carry += tot;
+  }
+  if (threadIdx.x == 0) {
+    s_total = carry;
+    if (!s_fail && (base_ptr < 0 || base_ptr + carry > n_free)) s_fail = HC_ERR_OOM;
+  }
+  __syncthreads();
+  if (s_fail) {
+    if (threadIdx.x == 0) set_err(err, s_fail);
+    return;
+  }
+  // pass 2: allocate in row order and write the rows
+  carry = 0;
+  for (int c0 = 0; c0 < R; c0 += blockDim.x) {
+    const int r = c0 + threadIdx.x;
+    int need = 0, len = 0, blk = 0, phys = 0;
+    if (r < R) {
+      len = heads_len[r];
+      blk = len >> 8;
+      phys = bt[(int64_t)r * max_blocks + blk];
+      need = phys == -1;
+    }
+    int tot;
+    const int ex = block_exclusive_scan(need, s_warp, tot);
+    bool ok = r < R;
+    if (ok && need) {
+      phys = free_blocks[base_ptr + carry + ex];
+      if (phys < 0 || phys >= n_blocks) {  // corrupt free list: leave the row untouched
+        set_err(err, HC_ERR_RANGE);
+        ok = false;
+      } else {
+        bt[(int64_t)r * max_blocks + blk] = phys;
+      }
+    }
+    if (ok) {
+      const int b = r / KV, h = r % KV;
+      const uint4* ks = reinterpret_cast<const uint4*>(k + b * sb + (int64_t)h * sh);
+      const uint4* vs = reinterpret_cast<const uint4*>(v + b * sb + (int64_t)h * sh);
+      const int64_t dst = ((int64_t)phys * kPage + (len & (kPage - 1))) * kD;
+      uint4* kd = reinterpret_cast<uint4*>(k_pool + dst);
+      uint4* vd = reinterpret_cast<uint4*>(v_pool + dst);
+      constexpr int CH = kD * sizeof(T) / 16;
+#pragma unroll 4
+      for (int c = 0; c < CH; ++c) {
+        kd[c] = ks[c];
+        vd[c] = vs[c];
+      }
+      heads_len[r] = len + 1;
+    }
+    carry += tot;
+  }
+  if (threadIdx.x == 0) *free_ptr = base_ptr + s_total;
+}
+
+// ---------------------------------------------------------------------------
+// Retrieval gather: full tier (device or pinned host memory) -> satellite pages.
+template <typename T>
+__global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict__ member_job,
+                                                       const int32_t* __restrict__ member_head,
+                                                       const int32_t* __restrict__ member_len,
+                                                       const int32_t* __restrict__ trigger,
+                                                       const int32_t* __restrict__ positions, int pos_stride,
+                                                       const T* full_k, const T* full_v, int64_t fsh, int64_t fst,
+                                                       T* k_pool, T* v_pool, int n_blocks,
+                                                       const int32_t* __restrict__ bt, int max_blocks, int32_t* err) {
+  constexpr int CH = kD * sizeof(T) / 16;
+  constexpr int RPP = 256 / CH;
+  const int m = blockIdx.y;
+  const int job = member_job[m];
+  if (!trigger[job]) return;
+  const int n = member_len[m];
+  const int h = member_head[m];
+  const int start = bt[(int64_t)h * max_blocks];
+  if (start < 0) return;
+  if ((int64_t)start * kPage + n > (int64_t)n_blocks * kPage) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) set_err(err, HC_ERR_RANGE);
+    return;
+  }
+  const int c = threadIdx.x % CH;
+  const int i0 = blockIdx.x * 64;
+  for (int i = i0 + threadIdx.x / CH; i < min(n, i0 + 64); i += RPP) {
+    const int pos = positions[(size_t)job * pos_stride + i];
+    if (pos < 0) {
+      if (c == 0) set_err(err, HC_ERR_RANGE);
+      continue;
+    }
+    const int64_t src = (int64_t)h * fsh + (int64_t)pos * fst;
+    const int64_t dst = ((int64_t)start * kPage + i) * kD;
+    reinterpret_cast<uint4*>(k_pool + dst)[c] = reinterpret_cast<const uint4*>(full_k + src)[c];
+    reinterpret_cast<uint4*>(v_pool + dst)[c] = reinterpret_cast<const uint4*>(full_v + src)[c];
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <typename T>
+static int prefill_keep_t(int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k, const void* v,
+                          int64_t sb, int64_t sh, int64_t st, void* kp, void* vp, int nb, const int32_t* bt, int mb,
+                          int32_t* hl, int32_t* err, cudaStream_t s) {
+  dim3 grid((L + 63) / 64, n_keep, bsz);
+  prefill_keep_kernel<T><<<grid, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, st, L, KV, keep, (T*)kp, (T*)vp,
+                                              nb, bt, mb, hl, err);
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k,
+                          const void* v, int64_t sb, int64_t sh, int64_t st, void* kp, void* vp, int nb,
+                          const int32_t* bt, int mb, int32_t* hl, int32_t* err, cudaStream_t s) {
+  switch (dtype) {
+    case HC_F32: return prefill_keep_t<float>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, kp, vp, nb, bt, mb, hl, err, s);
+    case HC_BF16: return prefill_keep_t<__nv_bfloat16>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, kp, vp, nb, bt, mb, hl, err, s);
+    case HC_F16: return prefill_keep_t<__half>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, kp, vp, nb, bt, mb, hl, err, s);
+    default: return HC_ERR_DTYPE;
+  }
+}
+
+template <typename T>
+static int append_t(int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, void* kp, void* vp, int nb,
+                    int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf, int32_t* fp, int32_t* err,
+                    cudaStream_t s) {
+  decode_append_kernel<T><<<1, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, R, KV, (T*)kp, (T*)vp, nb, bt, mb, hl,
+                                            fb, nf, fp, err);
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, void* kp,
+                           void* vp, int nb, int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf,
+                           int32_t* fp, int32_t* err, cudaStream_t s) {
+  switch (dtype) {
+    case HC_F32: return append_t<float>(R, KV, k, v, sb, sh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    case HC_BF16: return append_t<__nv_bfloat16>(R, KV, k, v, sb, sh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    case HC_F16: return append_t<__half>(R, KV, k, v, sb, sh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    default: return HC_ERR_DTYPE;
+  }
+}
+
+template <typename T>
+static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,
+                      const int32_t* trig, const int32_t* pos, int pos_stride, const void* fk, const void* fv,
+                      int64_t fsh, int64_t fst, void* kp, void* vp, int nb, const int32_t* bt, int mb, int32_t* err,
+                      cudaStream_t s) {
+  if (n_members == 0 || max_len <= 0) return HC_OK;
+  dim3 grid((max_len + 63) / 64, n_members);
+  retrieve_kernel<T><<<grid, 256, 0, s>>>(mj, mh, ml, trig, pos, pos_stride, (const T*)fk, (const T*)fv, fsh, fst,
+                                          (T*)kp, (T*)vp, nb, bt, mb, err);
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,
+                      const int32_t* trig, const int32_t* pos, int pos_stride, const void* fk, const void* fv,
+                      int64_t fsh, int64_t fst, void* kp, void* vp, int nb, const int32_t* bt, int mb, int32_t* err,
+                      cudaStream_t s) {
+  switch (dtype) {
+    case HC_F32: return retrieve_t<float>(n_members, mj, mh, ml, max_len, trig, pos, pos_stride, fk, fv, fsh, fst, kp, vp, nb, bt, mb, err, s);
+    case HC_BF16: return retrieve_t<__nv_bfloat16>(n_members, mj, mh, ml, max_len, trig, pos, pos_stride, fk, fv, fsh, fst, kp, vp, nb, bt, mb, err, s);
+    case HC_F16: return retrieve_t<__half>(n_members, mj, mh, ml, max_len, trig, pos, pos_stride, fk, fv, fsh, fst, kp, vp, nb, bt, mb, err, s);
+    default: return HC_ERR_DTYPE;
+  }
+}
+
+}  // namespace hc

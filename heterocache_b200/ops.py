@@ -1,0 +1,196 @@
+"""Tensor-level wrappers over the C ABI (one per entry point).
+
+Each wrapper validates devices, dtypes and layouts, then passes raw pointers,
+element strides and the current CUDA stream to the library.  Shapes follow
+the reference's tensors: q ``[bsz, H, L, D]``, k/v ``[bsz, KV, L, D]``, pools
+``[n_blocks, 256, 1, D]``, block tables ``[bsz*KV, max_blocks]`` int32.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ._lib import check, lib
+
+DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+POOLING = {"avgpool": 0, "maxpool": 1}
+HEAD_DIM = 128
+PAGE = 256
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"heterocache_b200: unsupported dtype {t.dtype}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("heterocache_b200: tensors must live on a CUDA device")
+
+
+def _rows(t: torch.Tensor, name: str) -> None:
+    if t.shape[-1] != HEAD_DIM or t.stride(-1) != 1:
+        raise ValueError(f"heterocache_b200: {name} must have a contiguous last dim of {HEAD_DIM}")
+
+
+def _i32(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.int32 or not t.is_contiguous():
+        raise ValueError(f"heterocache_b200: {name} must be a contiguous int32 tensor")
+
+
+class Workspace:
+    """Grow-only, zero-initialised scratch buffer owned by the caller."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.buf = torch.zeros(0, dtype=torch.uint8, device=self.device)
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf.numel() < nbytes:
+            self.buf = torch.zeros(int(nbytes) + (1 << 20), dtype=torch.uint8, device=self.device)
+        return self.buf
+
+    def reset(self) -> None:
+        self.buf.zero_()
+
+
+def prefill_keep(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err):
+    _cuda(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err)
+    _rows(k, "k"), _rows(v, "v")
+    _i32(keep_heads, "keep_heads"), _i32(block_table, "block_table"), _i32(heads_len, "heads_len")
+    if k.stride() != v.stride():
+        raise ValueError("heterocache_b200: k and v must share strides")
+    bsz, KV, L, D = k.shape
+    rc = lib().hc_prefill_keep(dtype_code(k), bsz, KV, L, D, _ptr(keep_heads), keep_heads.numel(),
+                               _ptr(k), _ptr(v), k.stride(0), k.stride(1), k.stride(2),
+                               _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table), block_table.shape[1],
+                               _ptr(heads_len), _ptr(err), _stream(k))
+    check("hc_prefill_keep", rc)
+
+
+def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, pooling, kernel_size,
+                   k_pool, v_pool, block_table, heads_len, workspace: Workspace, err,
+                   out_indices=None, out_scores=None):
+    _cuda(q, k, v, keep_lens, k_pool, v_pool, block_table, heads_len, err)
+    _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
+    _i32(keep_lens, "keep_lens"), _i32(block_table, "block_table"), _i32(heads_len, "heads_len")
+    if k.stride() != v.stride():
+        raise ValueError("heterocache_b200: k and v must share strides")
+    bsz, KV, L, D = k.shape
+    dt = dtype_code(k)
+    nbytes = lib().hc_prefill_select_workspace_size(dt, bsz, n_heads, L, groups, window)
+    ws = workspace.get(nbytes)
+    rc = lib().hc_prefill_select(dt, bsz, KV, groups, L, D, n_heads, window, POOLING[pooling], kernel_size,
+                                 _ptr(q), q.stride(0), q.stride(1), q.stride(2),
+                                 _ptr(k), _ptr(v), k.stride(0), k.stride(1), k.stride(2),
+                                 _ptr(keep_lens), int(max_keep), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
+                                 _ptr(block_table), block_table.shape[1], _ptr(heads_len),
+                                 _ptr(out_indices), _ptr(out_scores), _ptr(ws), ws.numel(), _ptr(err), _stream(k))
+    check("hc_prefill_select", rc)
+
+
+def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, topk, ref_positions, ref_bitmap,
+               workspace: Workspace, err, out_scores=None):
+    _cuda(q, k, ref_positions, ref_bitmap, err)
+    _rows(q, "q"), _rows(k, "k")
+    bsz, KV, L, D = k.shape
+    dt = dtype_code(k)
+    nbytes = lib().hc_pivot_init_workspace_size(dt, bsz, n_pivots, L, groups)
+    ws = workspace.get(nbytes)
+    rc = lib().hc_pivot_init(dt, bsz, KV, groups, L, D, first_pivot, n_pivots, POOLING[pooling], kernel_size,
+                             int(topk), _ptr(q), q.stride(0), q.stride(1), q.stride(2),
+                             _ptr(k), k.stride(0), k.stride(1), k.stride(2),
+                             _ptr(ref_positions), _ptr(ref_bitmap), _ptr(out_scores), _ptr(ws), ws.numel(),
+                             _ptr(err), _stream(k))
+    check("hc_pivot_init", rc)
+
+
+def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err):
+    _cuda(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err)
+    _rows(k, "k"), _rows(v, "v")
+    if k.stride() != v.stride():
+        raise ValueError("heterocache_b200: k and v must share strides")
+    bsz, KV, one, D = k.shape
+    if one != 1:
+        raise ValueError("heterocache_b200: decode append takes one token per row")
+    rc = lib().hc_decode_append(dtype_code(k), bsz, KV, D, _ptr(k), _ptr(v), k.stride(0), k.stride(1),
+                                _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
+                                block_table.shape[1], _ptr(heads_len), _ptr(free_blocks), free_blocks.numel(),
+                                _ptr(free_ptr),
+                                _ptr(err), _stream(k))
+    check("hc_decode_append", rc)
+
+
+def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out=None, scale: float = 0.0,
+                 workspace: Workspace, err, total_tokens_hint: int = 0):
+    """q: [bsz, H, 1, D] -> out [bsz, H, D] (same dtype)."""
+    _cuda(q, k_pool, v_pool, block_table, heads_len, err)
+    _rows(q, "q")
+    bsz, H, one, D = q.shape
+    if one != 1:
+        raise ValueError("heterocache_b200: decode attention takes one query position")
+    groups = H // num_kv_heads
+    if out is None:
+        out = torch.empty(bsz, H, D, dtype=q.dtype, device=q.device)
+    nbytes = lib().hc_flash_decode_workspace_size(bsz, num_kv_heads, groups, D)
+    ws = workspace.get(nbytes)
+    rc = lib().hc_flash_decode(dtype_code(q), bsz, num_kv_heads, groups, D, _ptr(q), q.stride(0), q.stride(1),
+                               _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
+                               block_table.shape[1], _ptr(heads_len), float(scale), _ptr(out),
+                               int(total_tokens_hint),
+                               _ptr(ws), ws.numel(), _ptr(err), _stream(q))
+    check("hc_flash_decode", rc)
+    return out
+
+
+def drift_check(qbuf, k_pool, block_table, *, num_kv_heads, groups, steps, seq_len, pooling, kernel_size, topk,
+                threshold, pivot_heads, ref_slots, max_len, max_len_cap, ref_bitmap, ref_positions, trigger,
+                retrieve_positions, workspace: Workspace, err, coeffs=None, median=None, out_scores=None):
+    """qbuf: [S, H, D] (strided)."""
+    _cuda(qbuf, k_pool, block_table, pivot_heads, ref_slots, max_len, ref_bitmap, ref_positions, trigger,
+          retrieve_positions, err)
+    _rows(qbuf, "qbuf")
+    dt = dtype_code(qbuf)
+    n_jobs = pivot_heads.numel()
+    nbytes = lib().hc_drift_check_workspace_size(dt, n_jobs, steps, seq_len, groups)
+    ws = workspace.get(nbytes)
+    rc = lib().hc_drift_check(dt, num_kv_heads, groups, qbuf.shape[-1], steps, seq_len, POOLING[pooling],
+                              kernel_size, int(topk), float(threshold), _ptr(qbuf), qbuf.stride(0),
+                              qbuf.stride(1), _ptr(k_pool), k_pool.shape[0], _ptr(block_table),
+                              block_table.shape[1], n_jobs,
+                              _ptr(pivot_heads), _ptr(ref_slots), _ptr(max_len), int(max_len_cap),
+                              _ptr(ref_bitmap), _ptr(ref_positions), _ptr(trigger), _ptr(coeffs), _ptr(median),
+                              _ptr(retrieve_positions), _ptr(out_scores), _ptr(ws), ws.numel(), _ptr(err),
+                              _stream(qbuf))
+    check("hc_drift_check", rc)
+
+
+def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, retrieve_positions, full_k, full_v,
+             k_pool, v_pool, block_table, num_kv_heads, err, stream: Optional[torch.cuda.Stream] = None):
+    """full_k/full_v: [1, KV, L, D] on the device or in pinned host memory."""
+    _cuda(member_job, member_head, member_len, trigger, retrieve_positions, k_pool, v_pool, block_table, err)
+    _rows(full_k, "full_k"), _rows(full_v, "full_v")
+    if not full_k.is_cuda and not full_k.is_pinned():
+        raise ValueError("heterocache_b200: a host-memory full tier must be pinned")
+    if full_k.stride() != full_v.stride():
+        raise ValueError("heterocache_b200: full_k and full_v must share strides")
+    st = (stream or torch.cuda.current_stream(k_pool.device)).cuda_stream
+    rc = lib().hc_retrieve(dtype_code(k_pool), num_kv_heads, k_pool.shape[-1], member_job.numel(),
+                           _ptr(member_job), _ptr(member_head), _ptr(member_len), int(max_member_len),
+                           _ptr(trigger), _ptr(retrieve_positions), retrieve_positions.shape[-1],
+                           _ptr(full_k), _ptr(full_v), full_k.stride(1), full_k.stride(2),
+                           _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table), block_table.shape[1],
+                           _ptr(err), st)
+    check("hc_retrieve", rc)

@@ -1,0 +1,202 @@
+/*
+ * heterocache_b200.h -- C ABI of the B200 (sm_100a) compressed-KV attention path.
+ *
+ * One entry point per operation of HeteroCache's cache object and patched
+ * attention (ponytaill/HeteroCache, heterocache/cache_utils.py and
+ * heterocache/llama_model.py).  Every argument is a plain pointer, size,
+ * stride or scalar; no framework type crosses this boundary.
+ *
+ * Conventions
+ *   - All tensor pointers are device pointers (or, where stated, host memory
+ *     the GPU can address: pinned host memory under unified addressing).
+ *   - Strides are in ELEMENTS; the innermost (head_dim) stride is always 1.
+ *   - A "row" of the page table is one (batch, kv-head) pair: row = b*KV + h.
+ *   - Pages hold HC_PAGE_SIZE tokens; a pool is [n_blocks, 256, 1, head_dim],
+ *     i.e. token (page p, slot s) lives at element ((p*256)+s)*head_dim.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default).
+ *   - Return value: HC_OK or an hc_status code.  Launch errors return
+ *     HC_ERR_CUDA; conditions detected on the device (free list exhausted,
+ *     page-table entry out of range, a bounded wait that gave up) are OR-ed
+ *     into the caller's int32 `err_flag` on the device and read back by the
+ *     caller after the stream has progressed.
+ *   - Every op that needs scratch takes a caller-owned workspace; query its
+ *     size with the matching *_workspace_size function.  Workspaces must be
+ *     zero-filled once when first allocated (the grid barrier they hold
+ *     resets itself after each launch).
+ *   - Only head_dim == 128 is supported (Llama-3.x and Qwen2.x).
+ *   - n_pool_blocks is the pool's first dimension; every page id read from a
+ *     block table is checked against it on the device (out of range ->
+ *     HC_ERR_RANGE in err_flag, the access is skipped).
+ */
+#ifndef HETEROCACHE_B200_H
+#define HETEROCACHE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HC_PAGE_SIZE 256
+#define HC_HEAD_DIM 128
+#define HC_ABI_VERSION 1
+
+typedef enum hc_status {
+  HC_OK = 0,
+  HC_ERR_INVALID = 1,     /* bad shape, size or argument */
+  HC_ERR_DTYPE = 2,       /* unsupported element type */
+  HC_ERR_OOM = 3,         /* decode free list exhausted ("Layer N OOM.") */
+  HC_ERR_RANGE = 4,       /* page-table entry or index out of range */
+  HC_ERR_CUDA = 5,        /* CUDA runtime error at launch */
+  HC_ERR_WORKSPACE = 6,   /* workspace missing or too small */
+  HC_ERR_TIMEOUT = 7,     /* a bounded device-side wait gave up */
+  HC_ERR_UNSUPPORTED = 8  /* valid request outside what this build implements */
+} hc_status;
+
+typedef enum hc_dtype { HC_F32 = 0, HC_BF16 = 1, HC_F16 = 2 } hc_dtype;
+typedef enum hc_pooling { HC_AVGPOOL = 0, HC_MAXPOOL = 1 } hc_pooling;
+
+/* Library identity and diagnostics. */
+int hc_abi_version(void);
+const char* hc_status_string(int status);
+/* Last CUDA error string seen by this library on the calling thread. */
+const char* hc_last_cuda_error(void);
+
+/* ---------------------------------------------------------------------------
+ * Prefill: keep-head copy.  Replaces the prefill branch of HeteroCache.update
+ * (heterocache/cache_utils.py:900-937): the volatile and pivot heads are
+ * copied whole into their pages and heads_len[row] = L.
+ *   k, v: [bsz, KV, L, D] strided (sb, sh, st).  keep_heads: device int32[n_keep].
+ */
+int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_dim,
+                    const int32_t* keep_heads, int n_keep,
+                    const void* k, const void* v, int64_t sb, int64_t sh, int64_t st,
+                    void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table,
+                    int max_blocks, int32_t* heads_len, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Prefill: compressed-head selection.  Replaces HeteroCache.prefill_select
+ * (heterocache/cache_utils.py:782-882) and, for window > 1, the observation
+ * window scoring of SnapKVCluster.update_kv (heterocache/kv_cluster.py:160-178).
+ * Heads 0..n_heads-1 (anchor + satellite, which the role order puts first)
+ * are scored from the last `window` queries of their G query heads; head h
+ * keeps its top keep_lens[h] positions, written in ascending position order
+ * from flat pool slot block_table[row, 0]*256 on (the prefill pages of a row
+ * are contiguous, as the reference lays them out and writes them,
+ * cache_utils.py:735-747 and :862-877); heads_len[row] = keep_lens[h].
+ *   q: [bsz, H, L, D] strided (qsb, qsh, qst), k/v: [bsz, KV, L, D] strided.
+ *   keep_lens: device int32[n_heads].
+ *   out_indices (optional, may be NULL): int32 [bsz, n_heads, max_keep],
+ *     kept positions ascending, -1 padded.
+ *   out_scores (optional, may be NULL): [bsz, n_heads, L] pooled scores in
+ *     the model dtype (the values the selection ranks).
+ */
+size_t hc_prefill_select_workspace_size(int dtype, int bsz, int n_heads, int seq_len, int groups, int window);
+int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_len, int head_dim,
+                      int n_heads, int window, int pooling, int kernel_size,
+                      const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                      const void* k, const void* v, int64_t sb, int64_t sh, int64_t st,
+                      const int32_t* keep_lens, int max_keep,
+                      void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table,
+                      int max_blocks, int32_t* heads_len, int32_t* out_indices, void* out_scores,
+                      void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Prefill: pivot reference sets.  Replaces HeteroCache.init_coefficient
+ * (heterocache/cache_utils.py:1149-1190): pivot heads first_pivot ..
+ * first_pivot+n_pivots-1 (contiguous after the role permutation) are scored
+ * from the last query and their top-`topk` positions become the reference
+ * set, stored both as ascending positions ref_positions [bsz, n_pivots, topk]
+ * and as a bitmap ref_bitmap [bsz, n_pivots, ceil(L/32)] (uint32 words).
+ */
+size_t hc_pivot_init_workspace_size(int dtype, int bsz, int n_pivots, int seq_len, int groups);
+int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len, int head_dim,
+                  int first_pivot, int n_pivots, int pooling, int kernel_size, int topk,
+                  const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                  const void* k, int64_t sb, int64_t sh, int64_t st,
+                  int32_t* ref_positions, uint32_t* ref_bitmap, void* out_scores,
+                  void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode: append one token per row.  Replaces the decode branch of
+ * HeteroCache.update (heterocache/cache_utils.py:970-1005).  Rows whose next
+ * slot falls in an unmapped page (-1) take pages from free_blocks in row
+ * order starting at *free_ptr (device int32); if the free list would
+ * overflow nothing is written and HC_ERR_OOM is OR-ed into err_flag.
+ *   k, v: [bsz, KV, 1, D] strided (sb, sh).
+ */
+int hc_decode_append(int dtype, int bsz, int num_kv_heads, int head_dim,
+                     const void* k, const void* v, int64_t sb, int64_t sh,
+                     void* k_pool, void* v_pool, int n_pool_blocks, int32_t* block_table, int max_blocks,
+                     int32_t* heads_len, const int32_t* free_blocks, int n_free, int32_t* free_ptr,
+                     int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode attention.  Replaces the flash_attn_with_kvcache call of the patched
+ * attention (heterocache/llama_model.py:370-397, qwen_model.py:181-206):
+ * non-causal attention of each row's G query heads over its first
+ * heads_len[row] tokens, through the page table.  Split-K over a balanced
+ * partition of all rows' tokens, then a per-row combine.
+ *   q: [bsz, H, 1, D] strided (qsb, qsh); out: [bsz, H, D] contiguous
+ *   (== [bsz, 1, H*D]).  scale <= 0 selects 1/sqrt(D).
+ *   total_tokens_hint: sum of heads_len if the caller knows it (sizes the
+ *   grid), else 0.
+ */
+size_t hc_flash_decode_workspace_size(int bsz, int num_kv_heads, int groups, int head_dim);
+int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_dim,
+                    const void* q, int64_t qsb, int64_t qsh,
+                    const void* k_pool, const void* v_pool, int n_pool_blocks, const int32_t* block_table,
+                    int max_blocks, const int32_t* heads_len, float scale, void* out, long long total_tokens_hint,
+                    void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode: pivot drift check.  Replaces the scoring and overlap part of
+ * HeteroCache.decode_select (heterocache/cache_utils.py:1007-1082) for
+ * batch size 1.  For each job j (a pivot with at least one satellite):
+ *   - score the S buffered queries of the pivot's G query heads against the
+ *     pivot's first seq_len keys (read through its page-table row);
+ *   - per step, top-`topk` positions and their overlap with the reference
+ *     bitmap; coefficient = overlap/topk (fp32); median over the S steps;
+ *   - trigger[j] = median < threshold.  On trigger the reference set slot
+ *     becomes the last step's top-`topk` set (bitmap and ascending positions).
+ *   - always: retrieve_positions[j, 0..max_len[j]) = the last step's
+ *     top-max_len[j] positions in ascending order.
+ *   qbuf: [S, H, D] strided (qss, qsh).  pivot_heads, ref_slots, max_len:
+ *   device int32[n_jobs].  coeffs: float[n_jobs, S] (optional), median:
+ *   double[n_jobs] (optional).
+ */
+size_t hc_drift_check_workspace_size(int dtype, int n_jobs, int steps, int seq_len, int groups);
+int hc_drift_check(int dtype, int num_kv_heads, int groups, int head_dim, int steps, int seq_len,
+                   int pooling, int kernel_size, int topk, double threshold,
+                   const void* qbuf, int64_t qss, int64_t qsh,
+                   const void* k_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks,
+                   int n_jobs, const int32_t* pivot_heads, const int32_t* ref_slots,
+                   const int32_t* max_len, int max_len_cap,
+                   uint32_t* ref_bitmap, int32_t* ref_positions,
+                   int32_t* trigger, float* coeffs, double* median,
+                   int32_t* retrieve_positions, void* out_scores,
+                   void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode: satellite retrieval.  Replaces the retrieval part of
+ * HeteroCache.decode_select (heterocache/cache_utils.py:1084-1147) for batch
+ * size 1.  For member m (job member_job[m], KV head member_head[m],
+ * member_len[m] tokens): if trigger[job] is set, copy rows
+ * retrieve_positions[job, i] (i < member_len[m]) of that head from the full
+ * tier into the pool at flat slot block_table[row, 0]*256 + i.
+ * The full tier (full_k/full_v, [1, KV, L, D] strided) may be device memory
+ * or pinned host memory (read directly over the host link).
+ */
+int hc_retrieve(int dtype, int num_kv_heads, int head_dim, int n_members,
+                const int32_t* member_job, const int32_t* member_head, const int32_t* member_len,
+                int max_member_len, const int32_t* trigger, const int32_t* retrieve_positions,
+                int retrieve_stride,
+                const void* full_k, const void* full_v, int64_t fsh, int64_t fst,
+                void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks,
+                int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HETEROCACHE_B200_H */

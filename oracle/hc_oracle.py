@@ -94,6 +94,34 @@ def snapkv_indices(q: torch.Tensor, k: torch.Tensor, *, window: int, kernel_size
     return pooled.topk(capacity - W, dim=-1).indices
 
 
+def paged_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,
+                    heads_len: torch.Tensor, num_kv_heads: int, scale: Optional[float] = None) -> torch.Tensor:
+    """Restatement of flash_attn_with_kvcache(q[bsz*KV,1,G,D], k_pool, v_pool,
+    cache_seqlens=heads_len, block_table, causal=False) as the patched attention
+    calls it (heterocache/llama_model.py:370-397): per (batch row, KV head) row,
+    fp32 softmax(q K^T * scale) V over the row's first heads_len tokens.
+    q [bsz, H, 1, D] -> fp32 [bsz, H, D]."""
+    bsz, H, _, D = q.shape
+    KV = num_kv_heads
+    G = H // KV
+    scale = D ** -0.5 if scale is None else scale
+    out = torch.zeros(bsz, KV, G, D, dtype=torch.float32)
+    kp = k_pool.float().reshape(-1, D)
+    vp = v_pool.float().reshape(-1, D)
+    for b in range(bsz):
+        for h in range(KV):
+            row = b * KV + h
+            n = int(heads_len[row])
+            if n == 0:
+                continue
+            t = torch.arange(n)
+            phys = block_table[row, (t // PAGE)].long() * PAGE + t % PAGE
+            qq = q[b, h * G:(h + 1) * G, 0, :].float()
+            p = torch.softmax((qq @ kp[phys].T) * scale, dim=-1)
+            out[b, h] = p @ vp[phys]
+    return out.view(bsz, H, D)
+
+
 class OracleCache:
     """Restatement of ``HeteroCache`` (heterocache/cache_utils.py:610-1190) on CPU.
 

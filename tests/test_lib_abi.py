@@ -1,0 +1,65 @@
+"""The C-ABI library loads without a GPU and exports every declared symbol."""
+import os
+import re
+import subprocess
+
+import pytest
+
+from heterocache_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "heterocache_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(hc_\w+)\s*\(", src, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def built():
+    import __graft_entry__
+    __graft_entry__.build()
+    return _lib.library_path()
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("hc_prefill_keep", "hc_prefill_select", "hc_pivot_init", "hc_decode_append", "hc_flash_decode",
+              "hc_drift_check", "hc_retrieve"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(built):
+    out = subprocess.run(["nm", "-D", "--defined-only", built], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r" T (hc_\w+)", out))
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+
+
+def test_ctypes_signatures_cover_the_header(built):
+    assert sorted(_lib.SIGNATURES) == declared_functions()
+    lib = _lib.lib()
+    assert lib.hc_abi_version() == 1
+    assert lib.hc_status_string(3) == b"decode free list exhausted"
+
+
+def test_argument_validation_needs_no_gpu(built):
+    """Bad arguments are rejected on the host before any CUDA call."""
+    lib = _lib.lib()
+    # unsupported dtype / head_dim / window / kernel size
+    assert lib.hc_flash_decode(9, 1, 8, 4, 128, None, 0, 0, None, None, 1, None, 1, None, 0.0, None, 0,
+                               None, 0, None, None) == 2
+    assert lib.hc_flash_decode(1, 1, 8, 4, 64, None, 0, 0, None, None, 1, None, 1, None, 0.0, None, 0,
+                               None, 0, None, None) == 1
+    assert lib.hc_prefill_select(1, 1, 8, 4, 100, 128, 5, 200, 0, 5, None, 0, 0, 0, None, None, 0, 0, 0,
+                                 None, 0, None, None, 1, None, 1, None, None, None, None, 0, None, None) == 1
+    assert lib.hc_drift_check(1, 8, 4, 128, 9, 1000, 0, 5, 10, 0.5, None, 0, 0, None, 1, None, 4, 1, None,
+                              None, None, 1, None, None, None, None, None, None, None, None, 0, None, None) == 8
+    # nothing to do is not an error
+    assert lib.hc_retrieve(1, 8, 128, 0, None, None, None, 0, None, None, 0, None, None, 0, 0, None, None, 1,
+                           None, 1, None, None) == 0
+    # workspace sizes are pure host arithmetic
+    assert lib.hc_prefill_select_workspace_size(1, 1, 5, 32768, 4, 1) > 0
+    assert lib.hc_flash_decode_workspace_size(1, 8, 4, 128) > 0
