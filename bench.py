@@ -1,0 +1,445 @@
+"""Benchmark of the compressed-KV attention path (decode) on B200.
+
+Workload (one GPU): the attention path of Llama-3.1-8B at 128K context --
+32 layers x (32 query / 8 KV heads, head_dim 128), bf16, batch 1, a 131072-
+token prefill compressed by HeteroCache (ratio 0.5, seeded head roles: per
+layer one pivot + 3 satellites, 2 anchors, 2 volatiles), then decode steps
+of one token through all 32 layers: page append -> split-K paged
+flash-decode -> decode_select (pivot drift check + satellite retrieval every
+5 steps, stable_threshold 0.5).  The non-attention parts of the model
+(projections, MLP, norms) are not part of this path and are not run.
+
+A step is one decode token through the 32 layers.  value = decode tokens/s
+(all ranks); us_per_layer = step time / 32.  Inputs are resident in HBM; the
+KV pools (~268 MB per layer) exceed L2, so successive layers evict each
+other (no flush needed).  e2e repeats the run through the drop-in cache API
+with each step's q/k/v copied from pinned host memory and the attention
+output read back.
+
+--impl reference times the oracle restatement of the reference's own path
+(PyTorch on the host CPU) on the same workload, one sampled layer per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode µs/layer & tokens/s at 128K ctx; HBM GB/s vs roofline, 1/2/4/8 B200"
+LAYERS, H, KV, D = 32, 32, 8, 128
+STEPS_PER_CHECK = 5
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ctx", type=int, default=131072)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def config_dict(args, n):
+    return {"workload": f"llama-3.1-8b compressed-KV attention path, {args.layers} layers, decode at "
+                        f"{args.ctx} ctx after HeteroCache prefill (ratio 0.5, steps 5, threshold 0.5, "
+                        "seeded roles), bsz 1 per GPU",
+            "context": args.ctx, "layers": args.layers, "batch_per_gpu": 1, "heads": [H, KV, D],
+            "parallelism": f"sequence-sharded x{n} (independent sequences, no data-path collective)",
+            "l2": "KV pools (~268 MB/layer) exceed the 126 MB L2; no flush needed"}
+
+
+# ---------------------------------------------------------------------------
+def build_roles(layers, seed=2026):
+    from heterocache_b200.roles import derive_runtime_data, synthetic_roles
+    return derive_runtime_data(synthetic_roles(layers, KV, seed), layers, KV)
+
+
+def make_cache(data, layers, real_offload=False):
+    from heterocache_b200.cache import HeteroCache, HeteroCacheConfig
+    cfg = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.5, real_offload=real_offload,
+                            max_gen_len=1024, decode_step=STEPS_PER_CHECK, pooling="avgpool", kernel_size=5,
+                            num_attn_heads=H, num_kv_heads=KV, num_layers=layers)
+    return HeteroCache(cfg)
+
+
+def prefill(cache, args, dev, seed):
+    """Prefill every layer on the device; returns per-layer prefill kernel ms."""
+    from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
+    g = torch.Generator(device=dev).manual_seed(seed)
+    L = args.ctx
+    q = torch.randn(1, H, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    times = []
+    for layer in range(args.layers):
+        k, v = prefill_kv_device(LLAMA_8B, L, q[:, :, -32:, :], seed=seed * 1000 + layer, device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        cache.update(k, v, layer)
+        cache.init_coefficient(q, k, layer)
+        cache.prefill_select(q, k, v, layer)
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+        del k, v
+    q_last = q[:, :, -1:, :].clone()
+    del q
+    torch.cuda.empty_cache()
+    return times, q_last
+
+
+def decode_inputs(n_steps, layers, q0, dev, seed):
+    """Drifting queries (0.9 prev + 0.1 noise) and fresh k/v per step and layer."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    qs = torch.empty(n_steps, layers, 1, H, 1, D, device=dev, dtype=torch.bfloat16)
+    cur = q0.float().expand(layers, 1, H, 1, D).clone()
+    for s in range(n_steps):
+        cur = 0.9 * cur + 0.1 * torch.randn(cur.shape, generator=g, device=dev)
+        qs[s] = cur.to(torch.bfloat16)
+    ks = torch.randn(n_steps, layers, 1, KV, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    vs = torch.randn(n_steps, layers, 1, KV, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    return qs, ks, vs
+
+
+def decode_step(cache, qs, ks, vs, s, layers, outs):
+    for layer in range(layers):
+        q = qs[s, layer]
+        cache.update(ks[s, layer], vs[s, layer], layer)
+        cache.attention(q, layer, out=outs[layer])
+        cache.decode_select(q, layer)
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region."""
+
+    def __init__(self, index):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = [r.split(",") for r in open(self.f.name).read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 8 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) > 8 for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def flash_decode_bytes(cache, layers):
+    """Algorithmic bytes of one flash-decode launch per layer (K and V rows read,
+    q read, output written)."""
+    per = []
+    for layer in range(layers):
+        toks = int(cache._hlen[layer].sum())
+        per.append(toks * D * 2 * 2 + 2 * H * D * 2)
+    return per
+
+
+def time_kernels(cache, qs, ks, vs, layers, start_step, n_steps, outs):
+    """CUDA-event durations of the flash-decode launches (decode + combine) and
+    drift checks inside a decode run (same stream as the launches)."""
+    from heterocache_b200 import ops
+    fd, drift = [], []
+    fd_bytes = []
+    for s in range(start_step, start_step + n_steps):
+        for layer in range(layers):
+            q = qs[s % qs.shape[0], layer]
+            cache.update(ks[s % ks.shape[0], layer], vs[s % vs.shape[0], layer], layer)
+            b = int(cache._hlen[layer].sum()) * D * 2 * 2 + 2 * H * D * 2
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            cache.attention(q, layer, out=outs[layer])
+            e1.record()
+            fd.append((e0, e1))
+            fd_bytes.append(b)
+            check = (cache._qcount[layer] + 1) == cache.decode_step
+            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e2.record()
+            cache.decode_select(q, layer)
+            e3.record()
+            if check:
+                drift.append((e2, e3))
+    torch.cuda.synchronize()
+    fd_ms = [a.elapsed_time(b) for a, b in fd]
+    dr_ms = [a.elapsed_time(b) for a, b in drift]
+    return fd_ms, fd_bytes, dr_ms
+
+
+def cpu_baseline(cache, layer, n_steps, qs, ks, vs):
+    """Time the oracle (reference restatement, PyTorch on the host CPU) on one
+    layer's decode: update -> paged attention -> decode_select."""
+    from oracle.hc_oracle import OracleCache
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = cache.config
+    orc = OracleCache(cfg)
+    orc.bsz, orc.head_dim = 1, D
+    orc.prefill_len = cache.prefill_len
+    orc.base_compress_len = cache.base_compress_len
+    n = cfg.num_layers
+    orc.key_pools = [None] * n
+    orc.value_pools = [None] * n
+    orc.block_tables = [None] * n
+    orc.heads_len = [None] * n
+    orc.free_blocks = [None] * n
+    orc.full_k, orc.full_v = [None] * n, [None] * n
+    orc.key_pools[layer] = cache.key_pools[layer].cpu()
+    orc.value_pools[layer] = cache.value_pools[layer].cpu()
+    orc.block_tables[layer] = cache.block_tables[layer].cpu()
+    orc.heads_len[layer] = cache.heads_len[layer].cpu()
+    orc.free_blocks[layer] = cache.free_blocks[layer].cpu()
+    orc.free_ptr = [0] * n
+    orc.free_ptr[layer] = cache.free_block_pointers[layer]
+    if cache.key_cache_cpu[layer] is not None:
+        orc.full_k[layer] = cache.key_cache_cpu[layer].cpu()
+        orc.full_v[layer] = cache.value_cache_cpu[layer].cpu()
+    orc.prefill_topk_set = [None] * n
+    if isinstance(cache.prefill_topk_set[layer], torch.Tensor):
+        orc.prefill_topk_set[layer] = cache.prefill_topk_set[layer].cpu().long()
+    orc.qbuf = [[] for _ in range(n)]
+    times = []
+    for s in range(n_steps):
+        q, k, v = qs[s, layer].cpu(), ks[s, layer].cpu(), vs[s, layer].cpu()
+        t0 = time.perf_counter()
+        orc.update(k, v, layer)
+        orc.paged_attention(q, layer)
+        orc.decode_select(q, layer)
+        times.append(time.perf_counter() - t0)
+    return times, torch.get_num_threads()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per flash-decode launch from the committed ncu summary, scaled
+    to this run's tokens (profiles/flash_decode_128k.md, if present)."""
+    path = os.path.join(ROOT, "profiles", "flash_decode_128k.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("traffic_bytes_per_token:"):
+            return float(line.split(":")[1])
+    return None
+
+
+# ---------------------------------------------------------------------------
+def run_reference(args, rank, world):
+    """The reference arm: the oracle port on the host CPU, one sampled layer per step."""
+    if rank != 0:
+        return
+    from oracle.hc_oracle import OracleCache
+    from heterocache_b200.synthetic import LLAMA_8B, DriftingDecode, prefill_inputs
+    torch.set_num_threads(os.cpu_count() or 1)
+    data = build_roles(args.layers)
+    from types import SimpleNamespace
+    cfg = SimpleNamespace(data=data, compression_ratio=0.5, stable_threshold=0.5, real_offload=False,
+                          max_gen_len=1024, decode_step=STEPS_PER_CHECK, pooling="avgpool", kernel_size=5,
+                          num_attn_heads=H, num_kv_heads=KV, num_layers=args.layers)
+    orc = OracleCache(cfg)
+    sample_layers = [0, 1]
+    qs = {}
+    t_pre = time.perf_counter()
+    for layer in sample_layers:
+        q, k, v = prefill_inputs(LLAMA_8B, args.ctx, seed=7 + layer, dtype=torch.bfloat16)
+        orc.update(k, v, layer)
+        orc.init_coefficient(q, k, layer)
+        orc.prefill_select(q, k, v, layer)
+        qs[layer] = DriftingDecode(LLAMA_8B, seed=11 + layer, q0=q[:, :, -1:, :], dtype=torch.bfloat16)
+        del q
+    t_pre = time.perf_counter() - t_pre
+    per_layer = []
+    total = args.warmup + args.steps
+    for s in range(total):
+        layer = sample_layers[s % len(sample_layers)]
+        q, k, v = qs[layer].step()
+        t0 = time.perf_counter()
+        orc.update(k, v, layer)
+        orc.paged_attention(q, layer)
+        orc.decode_select(q, layer)
+        dt = time.perf_counter() - t0
+        if s >= args.warmup:
+            per_layer.append(dt)
+    us_layer = float(np.mean(per_layer)) * 1e6
+    tok_s = 1e6 / (us_layer * args.layers)
+    line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer * args.layers / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) with planted heavy hitters; drifting decode queries)",
+            "config": config_dict(args, world), "us_per_layer": us_layer,
+            "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"oracle decode (append + paged attention + decode_select) of one layer per "
+                                       f"step, layers {sample_layers} alternating, {args.steps} timed steps; "
+                                       f"tokens/s = 1 / (mean layer time x {args.layers})"},
+            "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "prefill_s_sampled_layers": t_pre}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank):
+    from heterocache_b200 import ops
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    data = build_roles(args.layers)
+    cache = make_cache(data, args.layers)
+    prefill_ms, q_last = prefill(cache, args, dev, seed=1234 + rank)
+    cache.check_errors()
+    total_steps = args.warmup + args.steps
+    n_in = total_steps + 2 * STEPS_PER_CHECK
+    qs, ks, vs = decode_inputs(n_in, args.layers, q_last, dev, seed=99 + rank)
+    outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
+    for s in range(args.warmup):
+        decode_step(cache, qs, ks, vs, s, args.layers, outs)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = Clocks(local_rank) if rank == 0 else None
+    launches0 = ops.LAUNCHES[0]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for s in range(args.warmup, total_steps):
+        decode_step(cache, qs, ks, vs, s, args.layers, outs)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ops.LAUNCHES[0] - launches0
+    clk = clocks.stop() if clocks else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    cache.check_errors()
+    ms_step = ms / args.steps
+    value = world * 1000.0 / ms_step
+    # kernel timing pass: flash-decode and drift checks with events around each launch
+    n_kt = 2 * STEPS_PER_CHECK
+    fd_ms, fd_bytes, dr_ms = time_kernels(cache, qs, ks, vs, args.layers, total_steps, n_kt, outs)
+    cache.check_errors()
+    peak, peak_kind = peaks()
+    fd_avg_ms = float(np.mean(fd_ms))
+    fd_avg_bytes = float(np.mean(fd_bytes))
+    achieved = fd_avg_bytes / (fd_avg_ms * 1e-3) / 1e9
+    tpt = profiled_traffic()
+    tokens_per_launch = (fd_avg_bytes - 2 * H * D * 2) / (D * 2 * 2)
+    roof = {"kernel": "flash_decode (split-K decode + combine)", "bound": "hbm", "achieved": achieved,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+            "traffic": (tpt * tokens_per_launch if tpt else None),
+            "algorithmic_bytes_per_launch": fd_avg_bytes, "avg_launch_us": fd_avg_ms * 1e3,
+            "drift_check_avg_us": float(np.mean(dr_ms)) * 1e3 if dr_ms else None}
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, cache, qs, ks, vs, dev, world)
+    cpu = None
+    if rank == 0 and not args.no_cpu:
+        times, cores = cpu_baseline(cache, 0, 2 * STEPS_PER_CHECK, qs, ks, vs)
+        us_layer = float(np.mean(times)) * 1e6
+        cpu = {"value": 1e6 / (us_layer * args.layers), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"oracle decode of layer 0 for {len(times)} steps (one drift check + retrieval "
+                         f"included), tokens/s = 1 / (mean layer time x {args.layers})",
+               "us_per_layer": us_layer}
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1) K/V with planted heavy hitters; drifting decode queries)",
+                "config": config_dict(args, world), "us_per_layer": ms_step * 1000.0 / args.layers,
+                "prefill_ms_per_layer": float(np.mean(prefill_ms)), "roofline": roof, "cpu_baseline": cpu,
+                "e2e": e2e, "gpu_launches": launches, "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, cache, qs, ks, vs, dev, world):
+    """Same decode loop through the cache API with host buffers: per step, q/k/v
+    for every layer copied from pinned host memory, attention read back."""
+    n = args.steps
+    hq = qs[:n].cpu().pin_memory()
+    hk = ks[:n].cpu().pin_memory()
+    hv = vs[:n].cpu().pin_memory()
+    hout = torch.empty(n, args.layers, 1, H, D, dtype=torch.bfloat16).pin_memory()
+    dq = torch.empty_like(qs[0])
+    dk = torch.empty_like(ks[0])
+    dv = torch.empty_like(vs[0])
+    outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(n):
+        dq.copy_(hq[s], non_blocking=True)
+        dk.copy_(hk[s], non_blocking=True)
+        dv.copy_(hv[s], non_blocking=True)
+        for layer in range(args.layers):
+            cache.update(dk[layer], dv[layer], layer)
+            cache.attention(dq[layer], layer, out=outs[layer])
+            cache.decode_select(dq[layer], layer)
+            hout[s, layer].copy_(outs[layer], non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    per = ms / n
+    h2d = (qs[0].numel() + ks[0].numel() + vs[0].numel()) * 2
+    d2h = args.layers * H * D * 2
+    return {"value": world * 1000.0 / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": per}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -168,8 +168,10 @@ class HeteroCache(_CacheBase):
         # host mirrors of deterministic bookkeeping
         self._hlen: List[Optional[np.ndarray]] = [None] * n
         self._mapped: List[Optional[np.ndarray]] = [None] * n
-        self.record_checks = False
+        # opt-in diagnostics for parity tests: pooled scores and selections
+        self.record_checks = bool(getattr(cache_config, "record_checks", False))
         self.check_log: List[Dict] = []
+        self.recorded: Dict = {}
 
     def __bool__(self):
         return True
@@ -339,9 +341,14 @@ class HeteroCache(_CacheBase):
         ref = torch.empty(bsz, len(pivots), K, dtype=torch.int32, device=dev)
         words = (L + 31) // 32
         bitmap = torch.zeros(bsz, len(pivots), words, dtype=torch.int32, device=dev)
+        scores = (torch.empty(bsz, len(pivots), L, dtype=key_states.dtype, device=dev)
+                  if self.record_checks else None)
         ops.pivot_init(query_states, key_states, first_pivot=pivots[0], n_pivots=len(pivots),
                        groups=self.num_key_value_groups, pooling=self.pooling, kernel_size=self.kernel_size,
-                       topk=K, ref_positions=ref, ref_bitmap=bitmap, workspace=self._ws_score, err=self._err)
+                       topk=K, ref_positions=ref, ref_bitmap=bitmap, workspace=self._ws_score, err=self._err,
+                       out_scores=scores)
+        if scores is not None:
+            self.recorded[("pivot_scores", layer_idx)] = scores
         self._ref_bitmap[layer_idx] = bitmap
         self.prefill_topk_set.append(ref)
 
@@ -360,12 +367,21 @@ class HeteroCache(_CacheBase):
             self.heads_len[layer_idx][:nc] = 0
             self._hlen[layer_idx][:nc] = 0
             return
-        keep_dev = keep_lens.to(device=key_states.device, dtype=torch.int32)
+        dev = key_states.device
+        keep_dev = keep_lens.to(device=dev, dtype=torch.int32)
+        scores = idx = None
+        if self.record_checks:
+            scores = torch.empty(bsz, nc, L, dtype=key_states.dtype, device=dev)
+            idx = torch.empty(bsz, nc, max_k, dtype=torch.int32, device=dev)
+            self.recorded[("prefill_scores", layer_idx)] = scores
+            self.recorded[("prefill_indices", layer_idx)] = idx
+            self.recorded[("keep_lens", layer_idx)] = keep_lens.clone()
         ops.prefill_select(query_states, key_states, value_states, keep_dev, max_k, n_heads=nc,
                            groups=self.num_key_value_groups, window=self.window_size, pooling=self.pooling,
                            kernel_size=self.kernel_size, k_pool=self.key_pools[layer_idx],
                            v_pool=self.value_pools[layer_idx], block_table=self.block_tables[layer_idx],
-                           heads_len=self.heads_len[layer_idx], workspace=self._ws_score, err=self._err)
+                           heads_len=self.heads_len[layer_idx], workspace=self._ws_score, err=self._err,
+                           out_indices=idx, out_scores=scores)
         kl = keep_lens.numpy().astype(np.int64)
         for b in range(bsz):
             self._hlen[layer_idx][b * self.num_kv_heads:b * self.num_kv_heads + nc] = kl
@@ -399,6 +415,8 @@ class HeteroCache(_CacheBase):
         if jobs.n_jobs == 0:
             return
         self._wait_retrieval(layer_idx)
+        scores = (torch.empty(jobs.n_jobs, S, self.prefill_len, dtype=query_states.dtype,
+                              device=query_states.device) if self.record_checks else None)
         ops.drift_check(self._qbuf[layer_idx], self.key_pools[layer_idx], self.block_tables[layer_idx],
                         num_kv_heads=self.num_kv_heads, groups=self.num_key_value_groups, steps=S,
                         seq_len=self.prefill_len, pooling=self.pooling, kernel_size=self.kernel_size,
@@ -407,12 +425,14 @@ class HeteroCache(_CacheBase):
                         max_len_cap=max(jobs.max_len_cap, 1), ref_bitmap=self._ref_bitmap[layer_idx],
                         ref_positions=self.prefill_topk_set[layer_idx], trigger=jobs.trigger,
                         retrieve_positions=jobs.retrieve_positions, workspace=self._ws_score, err=self._err,
-                        coeffs=jobs.coeffs, median=jobs.median)
+                        coeffs=jobs.coeffs, median=jobs.median, out_scores=scores)
         if self.record_checks:
             self.check_log.append({"layer": layer_idx, "trigger": jobs.trigger.clone(),
                                    "coeffs": jobs.coeffs.clone(), "median": jobs.median.clone(),
                                    "retrieved": jobs.retrieve_positions.clone(),
-                                   "pivots": jobs.pivot_heads.tolist()})
+                                   "pivots": jobs.pivot_heads.tolist(), "slots": jobs.ref_slots.tolist(),
+                                   "max_len": jobs.max_len.tolist(), "scores": scores,
+                                   "ref_after": self.prefill_topk_set[layer_idx].clone()})
         if jobs.member_job.numel() == 0:
             return
         full_k = self.key_cache_cpu[layer_idx]

@@ -18,6 +18,9 @@ POOLING = {"avgpool": 0, "maxpool": 1}
 HEAD_DIM = 128
 PAGE = 256
 
+# Kernel launches issued through this module (flash-decode is two kernels).
+LAUNCHES = [0]
+
 
 def dtype_code(t: torch.Tensor) -> int:
     try:
@@ -78,6 +81,7 @@ def prefill_keep(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err):
                                _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table), block_table.shape[1],
                                _ptr(heads_len), _ptr(err), _stream(k))
     check("hc_prefill_keep", rc)
+    LAUNCHES[0] += 1
 
 
 def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, pooling, kernel_size,
@@ -99,6 +103,7 @@ def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, poo
                                  _ptr(block_table), block_table.shape[1], _ptr(heads_len),
                                  _ptr(out_indices), _ptr(out_scores), _ptr(ws), ws.numel(), _ptr(err), _stream(k))
     check("hc_prefill_select", rc)
+    LAUNCHES[0] += 1
 
 
 def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, topk, ref_positions, ref_bitmap,
@@ -115,6 +120,7 @@ def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, top
                              _ptr(ref_positions), _ptr(ref_bitmap), _ptr(out_scores), _ptr(ws), ws.numel(),
                              _ptr(err), _stream(k))
     check("hc_pivot_init", rc)
+    LAUNCHES[0] += 1
 
 
 def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err):
@@ -131,6 +137,7 @@ def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, fre
                                 _ptr(free_ptr),
                                 _ptr(err), _stream(k))
     check("hc_decode_append", rc)
+    LAUNCHES[0] += 1
 
 
 def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out=None, scale: float = 0.0,
@@ -152,6 +159,7 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
                                int(total_tokens_hint),
                                _ptr(ws), ws.numel(), _ptr(err), _stream(q))
     check("hc_flash_decode", rc)
+    LAUNCHES[0] += 2
     return out
 
 
@@ -175,6 +183,7 @@ def drift_check(qbuf, k_pool, block_table, *, num_kv_heads, groups, steps, seq_l
                               _ptr(retrieve_positions), _ptr(out_scores), _ptr(ws), ws.numel(), _ptr(err),
                               _stream(qbuf))
     check("hc_drift_check", rc)
+    LAUNCHES[0] += 1
 
 
 def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, retrieve_positions, full_k, full_v,
@@ -194,3 +203,4 @@ def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, re
                            _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table), block_table.shape[1],
                            _ptr(err), st)
     check("hc_retrieve", rc)
+    LAUNCHES[0] += 1

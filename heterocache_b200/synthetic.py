@@ -53,6 +53,28 @@ def prefill_inputs(geo: LayerGeometry, seq_len: int, *, bsz: int = 1, seed: int 
     return q.to(dtype), k.to(dtype), v.to(dtype)
 
 
+def prefill_kv_device(geo: LayerGeometry, seq_len: int, q_last: torch.Tensor, *, seed: int, device,
+                      dtype: torch.dtype = torch.bfloat16, planted_frac: float = 0.01,
+                      planted_scale: float = 4.0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Benchmark-size K/V generated on the device (same recipe as
+    ``prefill_inputs``: N(0,1) plus planted heavy hitters along the group's
+    mean query direction over the window ``q_last`` [bsz, H, W, D])."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    bsz = q_last.shape[0]
+    KV, D, G = geo.num_kv_heads, geo.head_dim, geo.groups
+    k = torch.randn(bsz, KV, seq_len, D, generator=g, device=device, dtype=torch.float32)
+    v = torch.randn(bsz, KV, seq_len, D, generator=g, device=device, dtype=torch.float32)
+    n_plant = max(1, int(round(planted_frac * seq_len)))
+    mean_q = q_last.float().view(bsz, KV, G, -1, D).mean(dim=(2, 3))  # [bsz, KV, D]
+    direction = mean_q / mean_q.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+    pos = torch.randint(0, seq_len, (bsz, KV, n_plant), generator=g, device=device)
+    add = torch.zeros_like(k)
+    add.scatter_(2, pos.unsqueeze(-1).expand(-1, -1, -1, D), (planted_scale * direction).unsqueeze(2)
+                 .expand(-1, -1, n_plant, -1).contiguous())
+    k += add
+    return k.to(dtype), v.to(dtype)
+
+
 class DriftingDecode:
     """Per-step decode inputs: ``q_t = 0.9 q_{t-1} + 0.1 noise``; fresh k, v."""
 

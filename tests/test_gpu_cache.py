@@ -1,0 +1,165 @@
+"""End-to-end parity of the drop-in cache: GPU ``HeteroCache`` in lockstep with
+the CPU oracle on the golden scenarios.
+
+Per step: lengths and page tables bit-exact; prefill selections, pivot sets,
+drift triggers and retrieval lists under the selection rule of
+``tests/parity.py``; decode attention within 2e-2 (bf16) / 1e-5 (fp32) of the
+oracle's attention over the same pages.
+"""
+import numpy as np
+import pytest
+import torch
+
+from heterocache_b200.cache import HeteroCache, HeteroCacheConfig
+from heterocache_b200.synthetic import DriftingDecode
+from oracle.hc_oracle import OracleCache, paged_attention
+from parity import compare_selection
+from scenarios import SCENARIOS, make_config, scenario_inputs
+
+pytestmark = pytest.mark.gpu
+
+ATOL = {"float32": 1e-5, "bfloat16": 2e-2, "float16": 2e-2}
+FLIP_FRAC = 0.01
+MEDIAN_MARGIN = 0.01  # triggers must agree unless the oracle's median is this close to the threshold
+
+
+def _gpu_cache(sc, real_offload=False):
+    ns = make_config(sc)
+    kw = dict(vars(ns))
+    kw["real_offload"] = real_offload
+    cfg = HeteroCacheConfig(**kw)
+    cfg.record_checks = True
+    return HeteroCache(cfg), OracleCache(ns)
+
+
+def _check_prefill(gpu, orc, sc, layer_inputs, dtype):
+    D = 128
+    for layer, (q, k, v) in enumerate(layer_inputs):
+        assert torch.equal(gpu.heads_len[layer].cpu(), orc.heads_len[layer]), layer
+        assert torch.equal(gpu.block_tables[layer].cpu(), orc.block_tables[layer]), layer
+        nc = gpu.data["need_to_compress_counts"][layer]
+        bsz, KV = q.shape[0], gpu.num_kv_heads
+        kp = gpu.key_pools[layer].cpu().view(-1, D)
+        vp = gpu.value_pools[layer].cpu().view(-1, D)
+        if nc and ("prefill_scores", layer) in gpu.recorded:
+            dsc = gpu.recorded[("prefill_scores", layer)].float().cpu()
+            idx = gpu.recorded[("prefill_indices", layer)].cpu()
+            keep = gpu.recorded[("keep_lens", layer)].tolist()
+            for b in range(bsz):
+                for h in range(nc):
+                    sel = idx[b, h, :keep[h]].tolist()
+                    res = compare_selection(orc.prefill_scores[layer][b, h].float().numpy(), dsc[b, h].numpy(),
+                                            sel, keep[h], dtype)
+                    assert res["ok"] and res["flips"] <= FLIP_FRAC * q.shape[2], (layer, b, h, res)
+                    start = int(gpu.block_tables[layer][b * KV + h, 0]) * 256
+                    assert torch.equal(kp[start:start + keep[h]], k[b, h, sel])
+                    assert torch.equal(vp[start:start + keep[h]], v[b, h, sel])
+        for h in gpu.data["need_to_keep_counts"][layer]:
+            for b in range(bsz):
+                start = int(gpu.block_tables[layer][b * KV + h, 0]) * 256
+                L = k.shape[2]
+                assert torch.equal(kp[start:start + L], k[b, h])
+                assert torch.equal(vp[start:start + L], v[b, h])
+        pivots = gpu.data["need_to_select_counts"][layer]
+        if pivots:
+            dsc = gpu.recorded[("pivot_scores", layer)].float().cpu()
+            ref = gpu.prefill_topk_set[layer].cpu()
+            for b in range(bsz):
+                for i in range(len(pivots)):
+                    res = compare_selection(orc.pivot_scores[layer][b, i].float().numpy(), dsc[b, i].numpy(),
+                                            ref[b, i].tolist(), gpu.base_compress_len, dtype)
+                    assert res["ok"], (layer, b, i, res)
+
+
+def _run(name, real_offload=False):
+    sc = SCENARIOS[name]
+    gpu, orc = _gpu_cache(sc, real_offload)
+    geo, tdt, layer_inputs = scenario_inputs(sc)
+    dtype = sc["dtype"]
+    dev = torch.device("cuda", 0)
+    for layer, (q, k, v) in enumerate(layer_inputs):
+        qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+        gpu.update(kd, vd, layer)
+        gpu.init_coefficient(qd, kd, layer)
+        gpu.prefill_select(qd, kd, vd, layer)
+        orc.update(k, v, layer)
+        orc.init_coefficient(q, k, layer)
+        orc.prefill_select(q, k, v, layer)
+    torch.cuda.synchronize()
+    gpu.check_errors()
+    assert gpu.base_compress_len == orc.base_compress_len
+    _check_prefill(gpu, orc, sc, layer_inputs, dtype)
+    if sc["n_decode"] == 0:
+        return
+    gens = [DriftingDecode(geo, bsz=1, seed=sc["seed"] * 1000 + l, q0=layer_inputs[l][0][:, :, -1:, :], dtype=tdt)
+            for l in range(len(layer_inputs))]
+    n_checks = 0
+    for step in range(sc["n_decode"]):
+        for layer in range(len(layer_inputs)):
+            q, k, v = gens[layer].step()
+            err_g = err_o = None
+            try:
+                orc.update(k, v, layer)
+            except RuntimeError as e:
+                err_o = str(e)
+            try:
+                gpu.update(k.to(dev), v.to(dev), layer)
+            except RuntimeError as e:
+                err_g = str(e)
+            assert err_g == err_o, (step, err_g, err_o)
+            if err_o is not None:
+                assert sc.get("record_every") and "OOM" in err_o
+                return
+            out = gpu.attention(q.to(dev), layer)
+            torch.cuda.synchronize()
+            ref = paged_attention(q, gpu.key_pools[layer].cpu(), gpu.value_pools[layer].cpu(),
+                                  gpu.block_tables[layer].cpu(), gpu.heads_len[layer].cpu(), gpu.num_kv_heads)
+            diff = (out.float().cpu() - ref).abs().max().item()
+            assert diff <= ATOL[dtype], (step, layer, diff)
+            before = len(gpu.check_log)
+            gpu.decode_select(q.to(dev), layer)
+            n_before = len(orc.checks)
+            orc.decode_select(q, layer)
+            torch.cuda.synchronize()
+            gpu.check_errors()
+            assert torch.equal(gpu.heads_len[layer].cpu(), orc.heads_len[layer])
+            assert torch.equal(gpu.block_tables[layer].cpu(), orc.block_tables[layer])
+            new = orc.checks[n_before:]
+            if len(gpu.check_log) > before:
+                log = gpu.check_log[-1]
+                assert len(new) == len(log["pivots"])
+                for j, rec in enumerate(new):
+                    n_checks += 1
+                    trig = bool(log["trigger"][j].item())
+                    if trig != rec["trigger"]:
+                        assert abs(rec["median"] - sc["thr"]) <= MEDIAN_MARGIN, (step, rec["median"])
+                        continue
+                    coeff = log["coeffs"][j].cpu().tolist()
+                    assert np.allclose(coeff, rec["coeffs"], atol=0.02), (coeff, rec["coeffs"])
+                    dsc = log["scores"][j].float().cpu()
+                    S = dsc.shape[0]
+                    if trig:
+                        ml = log["max_len"][j]
+                        sel = log["retrieved"][j, :ml].cpu().tolist()
+                        res = compare_selection(rec["scores"][0, -1].float().numpy(), dsc[S - 1].numpy(), sel, ml,
+                                                dtype)
+                        assert res["ok"], (step, res)
+                        slot = log["slots"][j]
+                        res = compare_selection(rec["scores"][0, -1].float().numpy(), dsc[S - 1].numpy(),
+                                                log["ref_after"][0, slot].cpu().tolist(), gpu.base_compress_len,
+                                                dtype)
+                        assert res["ok"], (step, res)
+            else:
+                assert not new
+    if any(gpu.data["leader_member_relations"][l] for l in range(len(layer_inputs))):
+        assert n_checks > 0
+
+
+@pytest.mark.parametrize("name", [n for n in SCENARIOS])
+def test_cache_lockstep_with_oracle(cuda_device, name):
+    _run(name)
+
+
+def test_cache_host_tier(cuda_device):
+    """Full tier in pinned host memory, retrieval on a side stream."""
+    _run("llama_bf16_avg5", real_offload=True)
