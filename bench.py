@@ -44,8 +44,8 @@ STEPS_PER_CHECK = 5
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=40)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ctx", type=int, default=131072)
     ap.add_argument("--layers", type=int, default=LAYERS)
@@ -163,34 +163,45 @@ def flash_decode_bytes(cache, layers):
     return per
 
 
-def time_kernels(cache, qs, ks, vs, layers, start_step, n_steps, outs):
-    """CUDA-event durations of the flash-decode launches (decode + combine) and
-    drift checks inside a decode run (same stream as the launches)."""
-    from heterocache_b200 import ops
-    fd, drift = [], []
-    fd_bytes = []
-    for s in range(start_step, start_step + n_steps):
-        for layer in range(layers):
-            q = qs[s % qs.shape[0], layer]
-            cache.update(ks[s % ks.shape[0], layer], vs[s % vs.shape[0], layer], layer)
-            b = int(cache._hlen[layer].sum()) * D * 2 * 2 + 2 * H * D * 2
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            cache.attention(q, layer, out=outs[layer])
-            e1.record()
-            fd.append((e0, e1))
-            fd_bytes.append(b)
-            check = (cache._qcount[layer] + 1) == cache.decode_step
-            e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e2.record()
-            cache.decode_select(q, layer)
-            e3.record()
-            if check:
-                drift.append((e2, e3))
-    torch.cuda.synchronize()
-    fd_ms = [a.elapsed_time(b) for a, b in fd]
-    dr_ms = [a.elapsed_time(b) for a, b in drift]
-    return fd_ms, fd_bytes, dr_ms
+def time_kernels(cache, layers, reps=5):
+    """Per-launch durations from CUDA events around graph replays that contain
+    only one kind of launch for every layer: the flash-decode (decode +
+    combine kernels) and the drift check.  Same stream, same data as the run."""
+    dev = cache._dev
+    outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(layers)]
+    q = torch.randn(layers, 1, H, 1, D, device=dev).to(torch.bfloat16)
+
+    def attn():
+        for l in range(layers):
+            cache.attention(q[l], l, out=outs[l])
+
+    def drift():
+        for l in range(layers):
+            jobs = cache._jobs[l]
+            if jobs is not None and jobs.n_jobs:
+                cache._drift_and_retrieve(l, jobs, q[l])
+
+    res = {}
+    for name, fn in (("flash_decode", attn), ("drift_check", drift)):
+        fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = e0.elapsed_time(e1) / (reps * layers)
+        del g
+    bytes_per = [int(cache._hlen[l].sum()) * D * 2 * 2 + 2 * H * D * 2 for l in range(layers)]
+    drift_bytes = [cache.prefill_len * D * 2 * (cache._jobs[l].n_jobs if cache._jobs[l] is not None else 0)
+                   for l in range(layers)]
+    return res, float(np.mean(bytes_per)), float(np.mean(drift_bytes))
 
 
 def cpu_baseline(cache, layer, n_steps, qs, ks, vs):
@@ -317,24 +328,34 @@ def run_ours(args, rank, world, local_rank):
     prefill_ms, q_last = prefill(cache, args, dev, seed=1234 + rank)
     cache.check_errors()
     total_steps = args.warmup + args.steps
-    n_in = total_steps + 2 * STEPS_PER_CHECK
+    n_in = STEPS_PER_CHECK + total_steps + 2 * STEPS_PER_CHECK
     qs, ks, vs = decode_inputs(n_in, args.layers, q_last, dev, seed=99 + rank)
     outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
-    for s in range(args.warmup):
+    # eager warm-up: sizes the workspaces and warms the launch caches
+    for s in range(STEPS_PER_CHECK):
         decode_step(cache, qs, ks, vs, s, args.layers, outs)
+    torch.cuda.synchronize()
+    from heterocache_b200.graph import DecodeStepGraph
+    graph = DecodeStepGraph(cache, list(range(args.layers)))
+    clocks = Clocks(local_rank) if rank == 0 else None
+    time.sleep(0.5)  # let the sampler start before the timed region
+    for s in range(STEPS_PER_CHECK, STEPS_PER_CHECK + args.warmup):
+        graph.q.copy_(qs[s]), graph.k.copy_(ks[s]), graph.v.copy_(vs[s])
+        graph.step()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    clocks = Clocks(local_rank) if rank == 0 else None
-    launches0 = ops.LAUNCHES[0]
+    launches_per_step = graph_launches(cache, args.layers)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
-    for s in range(args.warmup, total_steps):
-        decode_step(cache, qs, ks, vs, s, args.layers, outs)
+    first = STEPS_PER_CHECK + args.warmup
+    for s in range(first, first + args.steps):
+        graph.q.copy_(qs[s]), graph.k.copy_(ks[s]), graph.v.copy_(vs[s])
+        graph.step()
     e1.record()
     torch.cuda.synchronize()
-    launches = ops.LAUNCHES[0] - launches0
+    launches = sum(launches_per_step[(s % STEPS_PER_CHECK)] for s in range(first, first + args.steps))
     clk = clocks.stop() if clocks else None
     ms = e0.elapsed_time(e1)
     if world > 1:
@@ -345,13 +366,10 @@ def run_ours(args, rank, world, local_rank):
     cache.check_errors()
     ms_step = ms / args.steps
     value = world * 1000.0 / ms_step
-    # kernel timing pass: flash-decode and drift checks with events around each launch
-    n_kt = 2 * STEPS_PER_CHECK
-    fd_ms, fd_bytes, dr_ms = time_kernels(cache, qs, ks, vs, args.layers, total_steps, n_kt, outs)
+    kt, fd_avg_bytes, drift_bytes = time_kernels(cache, args.layers)
     cache.check_errors()
     peak, peak_kind = peaks()
-    fd_avg_ms = float(np.mean(fd_ms))
-    fd_avg_bytes = float(np.mean(fd_bytes))
+    fd_avg_ms = kt["flash_decode"]
     achieved = fd_avg_bytes / (fd_avg_ms * 1e-3) / 1e9
     tpt = profiled_traffic()
     tokens_per_launch = (fd_avg_bytes - 2 * H * D * 2) / (D * 2 * 2)
@@ -359,10 +377,12 @@ def run_ours(args, rank, world, local_rank):
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
             "traffic": (tpt * tokens_per_launch if tpt else None),
             "algorithmic_bytes_per_launch": fd_avg_bytes, "avg_launch_us": fd_avg_ms * 1e3,
-            "drift_check_avg_us": float(np.mean(dr_ms)) * 1e3 if dr_ms else None}
+            "drift_check": {"avg_launch_us": kt["drift_check"] * 1e3,
+                            "algorithmic_bytes_per_launch": drift_bytes,
+                            "achieved_gbs": drift_bytes / (kt["drift_check"] * 1e-3) / 1e9}}
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, cache, qs, ks, vs, dev, world)
+        e2e = run_e2e(args, graph, qs, ks, vs, dev, world)
     cpu = None
     if rank == 0 and not args.no_cpu:
         times, cores = cpu_baseline(cache, 0, 2 * STEPS_PER_CHECK, qs, ks, vs)
@@ -382,32 +402,26 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, cache, qs, ks, vs, dev, world):
-    """Same decode loop through the cache API with host buffers: per step, q/k/v
-    for every layer copied from pinned host memory, attention read back."""
+def run_e2e(args, graph, qs, ks, vs, dev, world):
+    """The same decode loop through the public graph API with host buffers: per
+    step, q/k/v of every layer copied from pinned host memory into the graph's
+    inputs and the attention outputs of every layer read back."""
     n = args.steps
     hq = qs[:n].cpu().pin_memory()
     hk = ks[:n].cpu().pin_memory()
     hv = vs[:n].cpu().pin_memory()
-    hout = torch.empty(n, args.layers, 1, H, D, dtype=torch.bfloat16).pin_memory()
-    dq = torch.empty_like(qs[0])
-    dk = torch.empty_like(ks[0])
-    dv = torch.empty_like(vs[0])
-    outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
+    hout = torch.empty((n,) + tuple(graph.out.shape), dtype=graph.out.dtype).pin_memory()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(n):
-        dq.copy_(hq[s], non_blocking=True)
-        dk.copy_(hk[s], non_blocking=True)
-        dv.copy_(hv[s], non_blocking=True)
-        for layer in range(args.layers):
-            cache.update(dk[layer], dv[layer], layer)
-            cache.attention(dq[layer], layer, out=outs[layer])
-            cache.decode_select(dq[layer], layer)
-            hout[s, layer].copy_(outs[layer], non_blocking=True)
+        graph.q.copy_(hq[s], non_blocking=True)
+        graph.k.copy_(hk[s], non_blocking=True)
+        graph.v.copy_(hv[s], non_blocking=True)
+        out = graph.step()
+        hout[s].copy_(out, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
@@ -416,10 +430,23 @@ def run_e2e(args, cache, qs, ks, vs, dev, world):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
     per = ms / n
-    h2d = (qs[0].numel() + ks[0].numel() + vs[0].numel()) * 2
-    d2h = args.layers * H * D * 2
+    h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * hq.element_size()
+    d2h = hout[0].numel() * hout.element_size()
     return {"value": world * 1000.0 / per, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": per}
+
+
+def graph_launches(cache, layers):
+    """Our kernels per decode step, by phase of the drift cycle: append (1) and
+    flash-decode (2) per layer, plus drift check (1) and retrieval (1) per
+    layer with pivot jobs on the last phase."""
+    base = 3 * layers
+    extra = 0
+    for l in range(layers):
+        jobs = cache._jobs[l]
+        if jobs is not None and jobs.n_jobs:
+            extra += 1 + (1 if jobs.member_job.numel() else 0)
+    return [base] * (STEPS_PER_CHECK - 1) + [base + extra]
 
 
 def main():

@@ -307,24 +307,30 @@ class HeteroCache(_CacheBase):
                 self.value_cache_cpu.append(value_states.detach())
             return key_states, value_states
 
-        # decode append: the free-list check mirrors cache_utils.py:981-990
+        self._append_bookkeeping(layer_idx)
+        self._wait_retrieval(layer_idx)
+        ops.decode_append(key_states, value_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
+                          self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
+                          self._free_ptr[layer_idx], self._err)
+        return key_states, value_states
+
+    def _append_bookkeeping(self, layer_idx: int) -> None:
+        """Host side of a decode append: the free-list check of
+        cache_utils.py:981-990 on the mirrored lengths (raises before any
+        launch), then the mirrors advance as the device state will."""
         hl = self._hlen[layer_idx]
         logical = hl // PAGE
         if np.any(logical >= self.block_tables[layer_idx].shape[1]):
             raise IndexError(f"Layer {layer_idx}: block table has no column for the next decode token")
-        need = int(np.count_nonzero(logical >= self._mapped[layer_idx]))
+        grow = logical >= self._mapped[layer_idx]
+        need = int(np.count_nonzero(grow))
         if need > 0:
             ptr = self.free_block_pointers[layer_idx]
             if ptr + need > self.free_blocks[layer_idx].size(0):
                 raise RuntimeError(f"Layer {layer_idx} OOM.")
             self.free_block_pointers[layer_idx] += need
-            self._mapped[layer_idx] += (logical >= self._mapped[layer_idx])
-        self._wait_retrieval(layer_idx)
-        ops.decode_append(key_states, value_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
-                          self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
-                          self._free_ptr[layer_idx], self._err)
+            self._mapped[layer_idx] += grow
         hl += 1
-        return key_states, value_states
 
     def init_coefficient(self, query_states, key_states, layer_idx):
         """Pivot reference sets (heterocache/cache_utils.py:1149-1190)."""
@@ -387,8 +393,7 @@ class HeteroCache(_CacheBase):
             self._hlen[layer_idx][b * self.num_kv_heads:b * self.num_kv_heads + nc] = kl
 
     # ------------------------------------------------------------------
-    def decode_select(self, query_states, layer_idx):
-        """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
+    def _ensure_decode_state(self, layer_idx, query_states) -> None:
         S = self.decode_step
         if self._qbuf[layer_idx] is None:
             bsz, H, _, D = query_states.shape
@@ -396,24 +401,47 @@ class HeteroCache(_CacheBase):
                 raise NotImplementedError("decode_select supports batch size 1 (as the reference, "
                                           "cache_utils.py:1093)")
             self._qbuf[layer_idx] = torch.empty(S, H, D, dtype=query_states.dtype, device=query_states.device)
-        self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
-        self._qcount[layer_idx] += 1
-        if self._qcount[layer_idx] < S:
-            return
-        self._qcount[layer_idx] = 0
         relations = self.data["leader_member_relations"][layer_idx]
-        if len(relations) == 0:
-            return
-        jobs = self._jobs[layer_idx]
-        if jobs is None:
+        if self._jobs[layer_idx] is None and relations:
             jobs = _LayerJobs(relations, self.data["allocation_matrix"][layer_idx], self.base_compress_len,
                               self.prefill_len, query_states.device)
             if self.record_checks:
                 jobs.coeffs = torch.zeros(max(jobs.n_jobs, 1), S, dtype=torch.float32, device=query_states.device)
                 jobs.median = torch.zeros(max(jobs.n_jobs, 1), dtype=torch.float64, device=query_states.device)
             self._jobs[layer_idx] = jobs
-        if jobs.n_jobs == 0:
+
+    def prepare_decode(self, layers, query_example) -> None:
+        """Allocate every layer's decode-time buffers now (before graph capture)."""
+        for l in layers:
+            self._ensure_decode_state(l, query_example)
+
+    def _host_state(self):
+        return {"hlen": [None if h is None else h.copy() for h in self._hlen],
+                "mapped": [None if m is None else m.copy() for m in self._mapped],
+                "free_ptr": list(self.free_block_pointers), "qcount": list(self._qcount),
+                "retrieve_done": list(self._retrieve_done), "seen": self._seen_tokens}
+
+    def _restore_host_state(self, s) -> None:
+        self._hlen, self._mapped = s["hlen"], s["mapped"]
+        self.free_block_pointers, self._qcount = s["free_ptr"], s["qcount"]
+        self._retrieve_done, self._seen_tokens = s["retrieve_done"], s["seen"]
+
+    def decode_select(self, query_states, layer_idx):
+        """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
+        S = self.decode_step
+        self._ensure_decode_state(layer_idx, query_states)
+        self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
+        self._qcount[layer_idx] += 1
+        if self._qcount[layer_idx] < S:
             return
+        self._qcount[layer_idx] = 0
+        jobs = self._jobs[layer_idx]
+        if jobs is None or jobs.n_jobs == 0:
+            return
+        self._drift_and_retrieve(layer_idx, jobs, query_states)
+
+    def _drift_and_retrieve(self, layer_idx, jobs, query_states):
+        S = self.decode_step
         self._wait_retrieval(layer_idx)
         scores = (torch.empty(jobs.n_jobs, S, self.prefill_len, dtype=query_states.dtype,
                               device=query_states.device) if self.record_checks else None)

@@ -727,15 +727,43 @@ static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws
   p.T = pl.T;
   p.TB = pl.TB;
   auto kern = score_select_kernel<T>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
-    return HC_ERR_CUDA;
-  int occ = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSThreads, pl.smem) != cudaSuccess)
-    return HC_ERR_CUDA;
+  // Attribute and occupancy queries are made once per shared-memory size and
+  // cached, so a launch issues no non-stream CUDA call (graph capture safe
+  // after the first launch of a given shape).
+  static bool attr_set = false;
+  static int cache_smem[16], cache_occ[16], n_cache = 0;
+  if (!attr_set) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 4096) != cudaSuccess)
+      return HC_ERR_CUDA;
+    attr_set = true;
+  }
+  int occ = -1;
+  for (int i = 0; i < n_cache; ++i)
+    if (cache_smem[i] == (int)pl.smem) occ = cache_occ[i];
+  if (occ < 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSThreads, pl.smem) != cudaSuccess)
+      return HC_ERR_CUDA;
+    if (n_cache < 16) {
+      cache_smem[n_cache] = (int)pl.smem;
+      cache_occ[n_cache] = occ;
+      ++n_cache;
+    }
+  }
   if ((long long)occ * num_sms() < pl.grid) return HC_ERR_UNSUPPORTED;
-  void* args[] = {&p};
-  if (cudaLaunchCooperativeKernel((void*)kern, dim3(pl.grid), dim3(kSThreads), args, pl.smem, st) != cudaSuccess)
-    return HC_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kSThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return HC_ERR_CUDA;
   return HC_OK;
 }
 
