@@ -124,17 +124,25 @@ __device__ __forceinline__ void fd_group_mma(const FDParams& p, WarpState<T>& st
     }
   }
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float2 v01 = unpack2<T>(vf[i].x);
-    const float2 v23 = unpack2<T>(vf[i].y);
+  for (int i4 = 0; i4 < 16; i4 += 4) {
+    float2 va[4], vb[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      va[j] = unpack2<T>(vf[i4 + j].x);
+      vb[j] = unpack2<T>(vf[i4 + j].y);
+    }
 #pragma unroll
     for (int g = 0; g < kGMax; ++g) {
       if (g < p.G) {
-        const float pv = sp[g * 16 + i];
-        st.o[g][0] = fmaf(pv, v01.x, st.o[g][0]);
-        st.o[g][1] = fmaf(pv, v01.y, st.o[g][1]);
-        st.o[g][2] = fmaf(pv, v23.x, st.o[g][2]);
-        st.o[g][3] = fmaf(pv, v23.y, st.o[g][3]);
+        const float4 pv = *reinterpret_cast<const float4*>(&sp[g * 16 + i4]);
+        const float pj[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          st.o[g][0] = fmaf(pj[j], va[j].x, st.o[g][0]);
+          st.o[g][1] = fmaf(pj[j], va[j].y, st.o[g][1]);
+          st.o[g][2] = fmaf(pj[j], vb[j].x, st.o[g][2]);
+          st.o[g][3] = fmaf(pj[j], vb[j].y, st.o[g][3]);
+        }
       }
     }
   }
@@ -175,7 +183,7 @@ __global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s_start = reinterpret_cast<int*>(smem_raw);
   __shared__ int s_warp[32];
-  __shared__ float s_p[kFWarps][kGMax * 16];
+  __shared__ __align__(16) float s_p[kFWarps][kGMax * 16];
   __shared__ float s_c[kFWarps][kGMax];
   __shared__ float s_m[kFWarps][kGMax], s_l[kFWarps][kGMax];
   __shared__ float s_o[kFWarps][kGMax][kD];
@@ -282,33 +290,77 @@ __global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
   }
 }
 
+// Merge of one (row, query head): block-parallel over the row's partials.
+// Phase A: lanes over partials -> max, weights exp2(m_c - M) (kept in shared
+// memory) and the weighted normaliser.  Phase B: each warp takes every 8th
+// partial with lanes over 4-dim slices (512-byte coalesced rows), then the
+// 8 warp sums are added in shared memory.
+constexpr int kCThreads = 256;
+
 template <typename T>
-__global__ void __launch_bounds__(kFThreads) flash_combine_kernel(FDParams p, int nctas) {
+__global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, int nctas) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s_start = reinterpret_cast<int*>(smem_raw);
+  float* s_w = reinterpret_cast<float*>(smem_raw + (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15));
   __shared__ int s_warp[32];
+  __shared__ float s_red[kCThreads / 32];
+  __shared__ float4 s_acc[kCThreads / 32][kD / 4];
   const int total = row_prefix(p, s_start, s_warp);
   const int span = span_of(total, nctas);
-  const int r = blockIdx.x;
-  const int d = threadIdx.x;
-  T* out = reinterpret_cast<T*>(p.out) + (size_t)r * p.G * kD;
+  const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD;
   const int rs = s_start[r], re = s_start[r + 1];
   if (re == rs || span == 0) {
-    for (int g = 0; g < p.G; ++g) out[g * kD + d] = Elem<T>::from_f(0.f);
+    if (threadIdx.x < kD) out[threadIdx.x] = Elem<T>::from_f(0.f);
     return;
   }
-  const int c0 = rs / span, c1 = (re - 1) / span;
-  for (int g = 0; g < p.G; ++g) {
-    float M = -INFINITY;
-    for (int c = c0; c <= c1; ++c) M = fmaxf(M, p.part_ml[(size_t)(c + r) * p.G + g].x);
-    float L = 0.f, O = 0.f;
-    for (int c = c0; c <= c1; ++c) {
-      const float2 ml = p.part_ml[(size_t)(c + r) * p.G + g];
-      const float f = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-      L += f * ml.y;
-      O += f * p.part_o[((size_t)(c + r) * p.G + g) * kD + d];
-    }
-    out[g * kD + d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
+  const int c0 = rs / span, n = (re - 1) / span - c0 + 1;
+  const size_t slot0 = (size_t)(c0 + r);
+  // phase A
+  float M = -INFINITY;
+  for (int c = threadIdx.x; c < n; c += kCThreads) M = fmaxf(M, p.part_ml[(slot0 + c) * p.G + g].x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = s_red[0];
+#pragma unroll
+  for (int w = 1; w < kCThreads / 32; ++w) M = fmaxf(M, s_red[w]);
+  __syncthreads();
+  float L = 0.f;
+  for (int c = threadIdx.x; c < n; c += kCThreads) {
+    const float2 ml = p.part_ml[(slot0 + c) * p.G + g];
+    const float f = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+    s_w[c] = f;
+    L += f * ml.y;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  if (lane == 0) s_red[warp] = L;
+  __syncthreads();
+  L = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCThreads / 32; ++w) L += s_red[w];
+  // phase B
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int c = warp; c < n; c += kCThreads / 32) {
+    const float f = s_w[c];
+    const float4 o = *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + 4 * lane);
+    acc.x = fmaf(f, o.x, acc.x);
+    acc.y = fmaf(f, o.y, acc.y);
+    acc.z = fmaf(f, o.z, acc.z);
+    acc.w = fmaf(f, o.w, acc.w);
+  }
+  s_acc[warp][lane] = acc;
+  __syncthreads();
+  if (threadIdx.x < kD) {
+    const int d = threadIdx.x;
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCThreads / 32; ++w) O += reinterpret_cast<const float*>(&s_acc[w][d / 4])[d % 4];
+    out[d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
   }
 }
 
@@ -339,7 +391,8 @@ template <typename T>
 static int fd_launch(FDParams& p, int grid, size_t dsm, cudaStream_t st) {
   flash_decode_kernel<T><<<grid, kFThreads, dsm, st>>>(p);
   if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
-  flash_combine_kernel<T><<<p.R, kFThreads, dsm, st>>>(p, grid);
+  const size_t csm = ((dsm + 15) & ~(size_t)15) + (size_t)grid * sizeof(float);
+  flash_combine_kernel<T><<<p.R * p.G, kCThreads, csm, st>>>(p, grid);
   if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
   return HC_OK;
 }

@@ -348,17 +348,27 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
   if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
 
   // ---- phase 2: global softmax statistics, probabilities, pooling, keys
-  for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
+  {
+    // one warp per query row, lanes over the job's CTAs
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float2* pj = p.part + (size_t)ji.job * p.cpj * p.Rq;
-    float M = -INFINITY;
-    for (int c = 0; c < p.cpj; ++c) M = fmaxf(M, pj[c * p.Rq + qi].x);
-    float S = 0.f;
-    for (int c = 0; c < p.cpj; ++c) {
-      float2 v = pj[c * p.Rq + qi];
-      if (v.x != -INFINITY) S += v.y * expf(v.x - M);
+    for (int qi = warp; qi < p.Rq; qi += kSWarps) {
+      float M = -INFINITY;
+      for (int c = lane; c < p.cpj; c += 32) M = fmaxf(M, pj[c * p.Rq + qi].x);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      float S = 0.f;
+      for (int c = lane; c < p.cpj; c += 32) {
+        const float2 v = pj[c * p.Rq + qi];
+        if (v.x != -INFINITY) S += v.y * expf(v.x - M);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+      if (lane == 0) {
+        s_rowM[qi] = M;
+        s_rowInv[qi] = S;
+      }
     }
-    s_rowM[qi] = M;
-    s_rowInv[qi] = S;
   }
   __syncthreads();
   {
@@ -452,13 +462,15 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
       if (c) atomicAdd(&gh[(size_t)(i / 256) * ROUNDS * 256 + (i % 256)], c);
     }
     if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
-    if (threadIdx.x < 32) {
-      for (int sel = 0; sel < p.nsel; ++sel) {
+    {
+      // one warp per select
+      const int warp = threadIdx.x >> 5;
+      for (int sel = warp; sel < p.nsel; sel += kSWarps) {
         const unsigned int k = s_k[sel];
         if (k == 0u || k >= (unsigned int)p.L) continue;
         unsigned int above;
         int bin = find_bin(gh + (size_t)sel * ROUNDS * 256, s_rem[sel], above);
-        if (threadIdx.x == 0) {
+        if ((threadIdx.x & 31) == 0) {
           s_rem[sel] -= above;
           s_prefix[sel] |= ((unsigned int)bin) << shift;
           s_mask[sel] |= 255u << shift;
@@ -498,20 +510,29 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
     p.cnt[((size_t)ji.job * kMaxSel + threadIdx.x) * p.cpj + ji.part] =
         make_int2(s_cnt[threadIdx.x][0], s_cnt[threadIdx.x][1]);
   if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
-  if (threadIdx.x < p.nsel) {
-    const int sel = threadIdx.x;
+  // Rank offsets of this CTA: over the job's earlier CTAs c < part, the
+  // selected count is n_gt(c) + clamp(need - eq_before(c), 0, n_eq(c)).
+  // Block-parallel over c (chunks of the block size, carried prefix).
+  for (int sel = 0; sel < p.nsel; ++sel) {
     const int2* cj = p.cnt + ((size_t)ji.job * kMaxSel + sel) * p.cpj;
     const long long need = (long long)s_rem[sel];
-    long long base = 0, eqoff = 0;
-    for (int c = 0; c < ji.part; ++c) {
-      int2 v = cj[c];
-      long long eqsel = need - eqoff;
+    long long carry_eq = 0, base = 0;
+    for (int c0 = 0; c0 < ji.part; c0 += kSThreads) {
+      const int c = c0 + threadIdx.x;
+      const int2 v = c < ji.part ? cj[c] : make_int2(0, 0);
+      int eq_tot;
+      const int eq_ex = block_exclusive_scan(v.y, s_warp, eq_tot);
+      long long eqsel = need - (carry_eq + eq_ex);
       eqsel = eqsel < 0 ? 0 : (eqsel > v.y ? v.y : eqsel);
-      base += v.x + eqsel;
-      eqoff += v.y;
+      int sel_tot;
+      block_exclusive_scan(v.x + (int)eqsel, s_warp, sel_tot);
+      carry_eq += eq_tot;
+      base += sel_tot;
     }
-    s_base[sel] = (int)base;
-    s_eqoff[sel] = (int)min(eqoff, (long long)0x7fffffff);
+    if (threadIdx.x == 0) {
+      s_base[sel] = (int)base;
+      s_eqoff[sel] = (int)min(carry_eq, (long long)0x7fffffff);
+    }
   }
   __syncthreads();
 
