@@ -9,7 +9,7 @@
 namespace hc {
 
 // ---- fused scoring / selection (score_select.cu)
-constexpr int kSThreads = 256;
+constexpr int kSThreads = 512;  // one CTA per SM (cooperative grid)
 constexpr int kSWarps = kSThreads / 32;
 constexpr int kMargin = 16;
 constexpr int kMaxSel = 8;

@@ -271,9 +271,9 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
   __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq];
   __shared__ unsigned int s_prefix[kMaxSel], s_mask[kMaxSel], s_rem[kMaxSel], s_k[kMaxSel];
   __shared__ int s_sel_row[kMaxSel];
-  __shared__ int s_warp[32];
-  __shared__ int s_cnt[kMaxSel][2];
+  __shared__ int2 s_wcnt[kMaxSel][kSWarps];
   __shared__ int s_base[kMaxSel], s_eqoff[kMaxSel];
+  __shared__ unsigned int s_ov[kMaxRows];
   __shared__ int s_trigger;
 
   constexpr int KB = Elem<T>::kKeyBits;
@@ -488,48 +488,61 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
   }
   __syncthreads();
 
-  // ---- phase 4: per-CTA counts, then ranks in position order
+  // ---- phase 4: counts of keys above / at each threshold, per warp slice
+  // Each warp owns a contiguous, 32-aligned slice of the CTA's tokens, so
+  // ranks in position order need no block-wide scans: per 32 tokens one
+  // ballot for "above", one for "equal", and popc of the lanes below.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int TW = ((ntok + kSWarps - 1) / kSWarps + 31) & ~31;
+  const int w0 = min(ntok, warp * TW), w1 = min(ntok, w0 + TW);
+  const unsigned int lt_mask = (1u << lane) - 1u;
   for (int sel = 0; sel < p.nsel; ++sel) {
     const unsigned int thr = s_prefix[sel];
     const unsigned int* kr = keys + s_sel_row[sel] * p.T;
     int ngt = 0, neq = 0;
-    for (int i = threadIdx.x; i < ntok; i += kSThreads) {
-      unsigned int key = kr[i];
-      ngt += key > thr;
-      neq += key == thr;
+    for (int c = w0; c < w1; c += 32) {
+      const int i = c + lane;
+      const unsigned int key = i < w1 ? kr[i] : 0u;
+      ngt += __popc(__ballot_sync(0xffffffffu, i < w1 && key > thr));
+      neq += __popc(__ballot_sync(0xffffffffu, i < w1 && key == thr));
     }
-    int tot;
-    int dummy = block_exclusive_scan(ngt, s_warp, tot);
-    (void)dummy;
-    if (threadIdx.x == 0) s_cnt[sel][0] = tot;
-    dummy = block_exclusive_scan(neq, s_warp, tot);
-    if (threadIdx.x == 0) s_cnt[sel][1] = tot;
+    if (lane == 0) s_wcnt[sel][warp] = make_int2(ngt, neq);
   }
   __syncthreads();
-  if (threadIdx.x < p.nsel)
-    p.cnt[((size_t)ji.job * kMaxSel + threadIdx.x) * p.cpj + ji.part] =
-        make_int2(s_cnt[threadIdx.x][0], s_cnt[threadIdx.x][1]);
+  if (threadIdx.x < p.nsel) {
+    int gt = 0, eq = 0;
+    for (int w = 0; w < kSWarps; ++w) {
+      gt += s_wcnt[threadIdx.x][w].x;
+      eq += s_wcnt[threadIdx.x][w].y;
+    }
+    p.cnt[((size_t)ji.job * kMaxSel + threadIdx.x) * p.cpj + ji.part] = make_int2(gt, eq);
+  }
   if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
   // Rank offsets of this CTA: over the job's earlier CTAs c < part, the
   // selected count is n_gt(c) + clamp(need - eq_before(c), 0, n_eq(c)).
-  // Block-parallel over c (chunks of the block size, carried prefix).
-  for (int sel = 0; sel < p.nsel; ++sel) {
+  // One warp per select, lanes over c with a carried warp scan.
+  for (int sel = warp; sel < p.nsel; sel += kSWarps) {
     const int2* cj = p.cnt + ((size_t)ji.job * kMaxSel + sel) * p.cpj;
     const long long need = (long long)s_rem[sel];
     long long carry_eq = 0, base = 0;
-    for (int c0 = 0; c0 < ji.part; c0 += kSThreads) {
-      const int c = c0 + threadIdx.x;
+    for (int c0 = 0; c0 < ji.part; c0 += 32) {
+      const int c = c0 + lane;
       const int2 v = c < ji.part ? cj[c] : make_int2(0, 0);
-      int eq_tot;
-      const int eq_ex = block_exclusive_scan(v.y, s_warp, eq_tot);
-      long long eqsel = need - (carry_eq + eq_ex);
+      int incl = v.y;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      long long eqsel = need - (carry_eq + incl - v.y);
       eqsel = eqsel < 0 ? 0 : (eqsel > v.y ? v.y : eqsel);
-      int sel_tot;
-      block_exclusive_scan(v.x + (int)eqsel, s_warp, sel_tot);
-      carry_eq += eq_tot;
-      base += sel_tot;
+      int contrib = v.x + (int)eqsel;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
+      carry_eq += __shfl_sync(0xffffffffu, incl, 31);
+      base += contrib;
     }
-    if (threadIdx.x == 0) {
+    if (lane == 0) {
       s_base[sel] = (int)base;
       s_eqoff[sel] = (int)min(carry_eq, (long long)0x7fffffff);
     }
@@ -537,35 +550,40 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
   __syncthreads();
 
   // ---- phase 5: epilogues
-  // Walk own tokens in position order, 256 at a time; for select `sel`
-  // returns the rank of each selected token (or -1).
+  // Walk this warp's slice in position order; for select `sel` every lane
+  // gets its token (or -1 past the slice) and its rank (or -1).  Warp-uniform.
   auto rank_pass = [&](int sel, auto&& fn) {
     const unsigned int thr = s_prefix[sel];
-    const unsigned int need = s_rem[sel];
+    const long long need = (long long)s_rem[sel];
     const unsigned int* kr = keys + s_sel_row[sel] * p.T;
-    int run_sel = s_base[sel], run_eq = s_eqoff[sel];
-    for (int c0 = 0; c0 < ntok || c0 == 0; c0 += kSThreads) {
-      const int i = c0 + threadIdx.x;
-      const bool in = i < ntok;
+    long long run_eq = s_eqoff[sel];
+    int run_sel = s_base[sel];
+    for (int w = 0; w < warp; ++w) {  // warps before this one in the CTA
+      const int2 v = s_wcnt[sel][w];
+      long long e = need - run_eq;
+      e = e < 0 ? 0 : (e > v.y ? v.y : e);
+      run_sel += v.x + (int)e;
+      run_eq += v.y;
+    }
+    for (int c = w0; c < w1; c += 32) {
+      const int i = c + lane;
+      const bool in = i < w1;
       const unsigned int key = in ? kr[i] : 0u;
-      const int gt = in && key > thr;
-      const int eq = in && key == thr;
-      int eqtot;
-      const int eqx = block_exclusive_scan(eq, s_warp, eqtot);
-      const int is = gt || (eq && (unsigned int)(run_eq + eqx) < need);
-      int seltot;
-      const int sx = block_exclusive_scan(is, s_warp, seltot);
-      fn(in ? ji.t0 + i : -1, is ? run_sel + sx : -1);
-      run_sel += seltot;
-      run_eq += eqtot;
-      if (c0 + kSThreads >= ntok) break;
+      const unsigned int gtm = __ballot_sync(0xffffffffu, in && key > thr);
+      const unsigned int eqm = __ballot_sync(0xffffffffu, in && key == thr);
+      const bool is_eq = (eqm >> lane) & 1u;
+      const bool sel_me = ((gtm >> lane) & 1u) || (is_eq && run_eq + __popc(eqm & lt_mask) < need);
+      const unsigned int selm = __ballot_sync(0xffffffffu, sel_me);
+      fn(in ? ji.t0 + i : -1, sel_me ? run_sel + __popc(selm & lt_mask) : -1, c);
+      run_sel += __popc(selm);
+      run_eq += __popc(eqm);
     }
   };
 
   if (p.mode == MODE_PREFILL) {
     const int kk = (int)s_k[0];
     const int row = ji.b * p.KV + ji.h;
-    rank_pass(0, [&](int t, int rank) {
+    rank_pass(0, [&](int t, int rank, int) {
       if (rank < 0 || rank >= kk) return;
       if (p.out_indices) p.out_indices[(size_t)ji.job * p.max_keep + rank] = t;
       // flat slot from the row's first page (the row's prefill pages are contiguous)
@@ -593,33 +611,39 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
     const int slot = ji.job;
     const int kk = (int)s_k[0];
     uint32_t* bm = p.ref_bitmap + (size_t)slot * p.bitmap_words;
-    rank_pass(0, [&](int t, int rank) {
+    rank_pass(0, [&](int t, int rank, int c) {
       const bool sel = rank >= 0 && rank < kk;
       if (sel) p.ref_positions[(size_t)slot * p.topk + rank] = t;
-      unsigned int bits = __ballot_sync(0xffffffffu, sel);
-      if (t >= 0 && (threadIdx.x & 31) == 0) bm[t >> 5] = bits;
+      const unsigned int bits = __ballot_sync(0xffffffffu, sel);
+      if (lane == 0) bm[(ji.t0 + c) >> 5] = bits;
     });
   } else {
     // drift: overlap of each step's top-k with the reference bitmap
     const int slot = p.ref_slots[ji.job];
     uint32_t* bm = p.ref_bitmap + (size_t)slot * p.bitmap_words;
+    if (threadIdx.x < kMaxRows) s_ov[threadIdx.x] = 0u;
+    __syncthreads();
     for (int sel = 0; sel < p.S; ++sel) {
-      int local = 0;
-      rank_pass(sel, [&](int t, int rank) {
-        if (rank >= 0 && rank < (int)s_k[sel]) local += (bm[t >> 5] >> (t & 31)) & 1u;
+      const int kk = (int)s_k[sel];
+      unsigned int local = 0;
+      rank_pass(sel, [&](int t, int rank, int) {
+        if (rank >= 0 && rank < kk) local += (bm[t >> 5] >> (t & 31)) & 1u;
       });
-      int tot;
-      block_exclusive_scan(local, s_warp, tot);
-      if (threadIdx.x == 0 && tot) atomicAdd(&p.overlap[ji.job * kMaxRows + sel], (unsigned int)tot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
+      if (lane == 0 && local) atomicAdd(&s_ov[sel], local);
     }
     // retrieval list: last step's top-max_len, ascending
     {
       const int sel = p.S;
       const int kk = min((int)s_k[sel], p.max_len_cap);
-      rank_pass(sel, [&](int t, int rank) {
+      rank_pass(sel, [&](int t, int rank, int) {
         if (rank >= 0 && rank < kk) p.retrieve_positions[(size_t)ji.job * p.max_len_cap + rank] = t;
       });
     }
+    __syncthreads();
+    if (threadIdx.x < p.S && s_ov[threadIdx.x])
+      atomicAdd(&p.overlap[ji.job * kMaxRows + threadIdx.x], s_ov[threadIdx.x]);
     if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
     if (threadIdx.x == 0) {
       float c[kMaxRows];
@@ -645,11 +669,11 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
     if (s_trigger) {
       const int sel = p.S - 1;
       const int kk = (int)s_k[sel];
-      rank_pass(sel, [&](int t, int rank) {
+      rank_pass(sel, [&](int t, int rank, int c) {
         const bool on = rank >= 0 && rank < kk;
         if (on) p.ref_positions[(size_t)slot * p.topk + rank] = t;
-        unsigned int bits = __ballot_sync(0xffffffffu, on);
-        if (t >= 0 && (threadIdx.x & 31) == 0) bm[t >> 5] = bits;
+        const unsigned int bits = __ballot_sync(0xffffffffu, on);
+        if (lane == 0) bm[(ji.t0 + c) >> 5] = bits;
       });
     }
   }
@@ -790,24 +814,14 @@ static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws
 
 template <typename T>
 static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
-  ScorePlan pl = plan_score(std::is_same<T, float>::value ? HC_F32 : HC_BF16, p.n_jobs, p.L, p.Rq, p.S, 2);
-  // fall back to one CTA per SM if two do not fit
-  int rc = launch_score<T>(p, pl, ws, ws_bytes, st);
-  if (rc == HC_ERR_UNSUPPORTED) {
-    pl = plan_score(std::is_same<T, float>::value ? HC_F32 : HC_BF16, p.n_jobs, p.L, p.Rq, p.S, 1);
-    rc = launch_score<T>(p, pl, ws, ws_bytes, st);
-  }
-  return rc;
+  // one 512-thread CTA per SM
+  ScorePlan pl = plan_score(std::is_same<T, float>::value ? HC_F32 : HC_BF16, p.n_jobs, p.L, p.Rq, p.S, 1);
+  return launch_score<T>(p, pl, ws, ws_bytes, st);
 }
 
 size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S) {
-  size_t best = 0;
-  for (int per_sm = 1; per_sm <= 2; ++per_sm) {
-    ScorePlan pl = plan_score(dtype, n_jobs, L, Rq, S, per_sm);
-    ScoreWs w = score_ws_layout(n_jobs, pl, Rq);
-    best = w.total > best ? w.total : best;
-  }
-  return best;
+  ScorePlan pl = plan_score(dtype, n_jobs, L, Rq, S, 1);
+  return score_ws_layout(n_jobs, pl, Rq).total;
 }
 
 int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
