@@ -10,6 +10,7 @@ namespace hc {
 
 // ---- fused scoring / selection (score_select.cu)
 constexpr int kSThreads = 512;  // one CTA per SM (cooperative grid)
+constexpr int kRefWords = 512;  // reference-bitmap words staged per CTA (16K tokens)
 constexpr int kSWarps = kSThreads / 32;
 constexpr int kMargin = 16;
 constexpr int kMaxSel = 8;

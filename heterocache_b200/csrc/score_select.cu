@@ -226,6 +226,80 @@ __device__ void logits_fma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   }
 }
 
+// Softmax probability of logit x with row max M and row sum of exp S, in
+// fp32 (the reference's softmax(dtype=float32)).  fp32 models use the
+// accurate exp and an IEEE division; 16-bit models round the result to
+// their dtype right after, so the fast exp (a few ulp of fp32) and the
+// reciprocal are used there.
+template <typename T>
+__device__ __forceinline__ float softmax_prob(float x, float M, float S) {
+  if constexpr (std::is_same<T, float>::value) return expf(x - M) / S;
+  else return __expf(x - M) * __frcp_rn(S);
+}
+
+// Phase 2 for W == 1 and pooling half-width HALO <= 3, fused: each thread
+// takes a strip of 8 output tokens of one score row, computes the rounded
+// probabilities of the strip plus halo once per query head, pools each
+// output in the reference's order ((((p0+p1)+p2)+p3)+p4, divided by the
+// kernel size, count_include_pad) and keeps the max over the GQA group.
+template <typename T, int HALO>
+__device__ void pooled_keys_fused(const ScoreParams& p, const JobInfo& ji, const T* lg, unsigned int* keys,
+                                  const float* s_rowM, const float* s_rowS) {
+  constexpr int SW = 8;
+  constexpr int NP = SW + 2 * HALO;
+  constexpr float KS = (float)(2 * HALO + 1);
+  const int base = ji.t0 - kMargin;
+  const int ntok = ji.t1 - ji.t0;
+  const int nstrip = (ntok + SW - 1) / SW;
+  for (int it = threadIdx.x; it < p.S * nstrip; it += kSThreads) {
+    const int s = it / nstrip;
+    const int t0 = ji.t0 + (it - s * nstrip) * SW;
+    float best[SW];
+#pragma unroll
+    for (int o = 0; o < SW; ++o) best[o] = -INFINITY;
+    for (int g = 0; g < p.G; ++g) {
+      const int qi = s * p.G + g;
+      const float M = s_rowM[qi], S = s_rowS[qi];
+      const T* row = lg + (int64_t)qi * p.TB - base;
+      float pv[NP];
+#pragma unroll
+      for (int j = 0; j < NP; ++j) {
+        const int t = t0 - HALO + j;
+        float v = p.pooling == HC_AVGPOOL ? 0.f : -INFINITY;  // padding
+        if (t >= 0 && t < p.L) {
+          const float x = Elem<T>::to_f(row[t]);
+          v = (x == -INFINITY) ? 0.f : Elem<T>::rnd(softmax_prob<T>(x, M, S));
+        }
+        pv[j] = v;
+      }
+#pragma unroll
+      for (int o = 0; o < SW; ++o) {
+        float v;
+        if (p.pooling == HC_AVGPOOL) {
+          float acc = pv[o];
+#pragma unroll
+          for (int j = 1; j <= 2 * HALO; ++j) acc += pv[o + j];
+          v = Elem<T>::rnd(acc / KS);
+        } else {
+          v = pv[o];
+#pragma unroll
+          for (int j = 1; j <= 2 * HALO; ++j) v = fmaxf(v, pv[o + j]);
+        }
+        best[o] = fmaxf(best[o], v);
+      }
+    }
+#pragma unroll
+    for (int o = 0; o < SW; ++o) {
+      const int t = t0 + o;
+      if (t < ji.t1) {
+        keys[s * p.T + (t - ji.t0)] = Elem<T>::key(best[o]);
+        if (p.out_scores)
+          reinterpret_cast<T*>(p.out_scores)[((size_t)ji.job * p.S + s) * p.L + t] = Elem<T>::from_f(best[o]);
+      }
+    }
+  }
+}
+
 // Find the 8-bit digit bin holding the rem-th largest key (rem >= 1).
 // Returns the bin; `above` = number of keys in higher bins.  One warp.
 __device__ __forceinline__ int find_bin(const unsigned int* h, unsigned int rem, unsigned int& above) {
@@ -266,7 +340,7 @@ __device__ __forceinline__ int find_bin(const unsigned int* h, unsigned int rem,
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) {
+__global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq];
   __shared__ unsigned int s_prefix[kMaxSel], s_mask[kMaxSel], s_rem[kMaxSel], s_k[kMaxSel];
@@ -274,6 +348,7 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
   __shared__ int2 s_wcnt[kMaxSel][kSWarps];
   __shared__ int s_base[kMaxSel], s_eqoff[kMaxSel];
   __shared__ unsigned int s_ov[kMaxRows];
+  __shared__ uint32_t s_refw[kRefWords];
   __shared__ int s_trigger;
 
   constexpr int KB = Elem<T>::kKeyBits;
@@ -371,7 +446,14 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
     }
   }
   __syncthreads();
-  {
+  const bool fused = p.W == 1 && p.halo >= 1 && p.halo <= 3;
+  if (fused) {
+    switch (p.halo) {
+      case 1: pooled_keys_fused<T, 1>(p, ji, lg, keys, s_rowM, s_rowInv); break;
+      case 2: pooled_keys_fused<T, 2>(p, ji, lg, keys, s_rowM, s_rowInv); break;
+      default: pooled_keys_fused<T, 3>(p, ji, lg, keys, s_rowM, s_rowInv); break;
+    }
+  } else {
     const int base = ji.t0 - kMargin;
     const int lo = max(0, ji.t0 - p.halo), hi = min(p.L, ji.t1 + p.halo);
     const int span = hi - lo;
@@ -379,7 +461,7 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
       int qi = i / span, t = lo + i % span;
       T* cell = lg + (int64_t)qi * p.TB + (t - base);
       float x = Elem<T>::to_f(*cell);
-      float pr = (x == -INFINITY) ? 0.f : expf(x - s_rowM[qi]) / s_rowInv[qi];
+      float pr = (x == -INFINITY) ? 0.f : softmax_prob<T>(x, s_rowM[qi], s_rowInv[qi]);
       *cell = Elem<T>::from_f(pr);
     }
     __syncthreads();
@@ -579,27 +661,94 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
       run_eq += __popc(eqm);
     }
   };
+  // Same walk, one call per 32-token chunk with the selection mask and the
+  // rank of the chunk's first selected token (warp-uniform).
+  auto rank_walk = [&](int sel, auto&& fnw) {
+    const unsigned int thr = s_prefix[sel];
+    const long long need = (long long)s_rem[sel];
+    const unsigned int* kr = keys + s_sel_row[sel] * p.T;
+    long long run_eq = s_eqoff[sel];
+    int run_sel = s_base[sel];
+    for (int w = 0; w < warp; ++w) {
+      const int2 v = s_wcnt[sel][w];
+      long long e = need - run_eq;
+      e = e < 0 ? 0 : (e > v.y ? v.y : e);
+      run_sel += v.x + (int)e;
+      run_eq += v.y;
+    }
+    for (int c = w0; c < w1; c += 32) {
+      const int i = c + lane;
+      const bool in = i < w1;
+      const unsigned int key = in ? kr[i] : 0u;
+      const unsigned int gtm = __ballot_sync(0xffffffffu, in && key > thr);
+      const unsigned int eqm = __ballot_sync(0xffffffffu, in && key == thr);
+      const bool is_eq = (eqm >> lane) & 1u;
+      const bool sel_me = ((gtm >> lane) & 1u) || (is_eq && run_eq + __popc(eqm & lt_mask) < need);
+      const unsigned int selm = __ballot_sync(0xffffffffu, sel_me);
+      fnw(c, selm, run_sel);
+      run_sel += __popc(selm);
+      run_eq += __popc(eqm);
+    }
+  };
 
   if (p.mode == MODE_PREFILL) {
     const int kk = (int)s_k[0];
     const int row = ji.b * p.KV + ji.h;
-    rank_pass(0, [&](int t, int rank, int) {
-      if (rank < 0 || rank >= kk) return;
-      if (p.out_indices) p.out_indices[(size_t)ji.job * p.max_keep + rank] = t;
-      // flat slot from the row's first page (the row's prefill pages are contiguous)
-      const int start = p.bt[(int64_t)row * p.max_blocks];
-      const int64_t slot = (int64_t)start * kPage + rank;
-      if (start < 0 || slot >= (int64_t)p.n_blocks * kPage) { set_err(p.err, HC_ERR_RANGE); return; }
-      const int64_t dst = slot * kD;
-      const T* ks = reinterpret_cast<const T*>(p.k) + ji.b * p.ksb + (int64_t)ji.h * p.ksh + (int64_t)t * p.kst;
-      const T* vs = reinterpret_cast<const T*>(p.v) + ji.b * p.ksb + (int64_t)ji.h * p.ksh + (int64_t)t * p.kst;
-      T* kd = reinterpret_cast<T*>(p.k_pool_out) + dst;
-      T* vd = reinterpret_cast<T*>(p.v_pool_out) + dst;
-      constexpr int V = 16 / sizeof(T);
-#pragma unroll 4
-      for (int d = 0; d < kD; d += V) {
-        *reinterpret_cast<uint4*>(kd + d) = ldg128(ks + d);
-        *reinterpret_cast<uint4*>(vd + d) = ldg128(vs + d);
+    // flat slots from the row's first page (the row's prefill pages are contiguous)
+    const int start = p.bt[(int64_t)row * p.max_blocks];
+    const bool start_ok = start >= 0 && (int64_t)start * kPage + kk <= (int64_t)p.n_blocks * kPage;
+    if (!start_ok && kk > 0 && threadIdx.x == 0 && ji.part == 0) set_err(p.err, HC_ERR_RANGE);
+    const T* kbase = reinterpret_cast<const T*>(p.k) + ji.b * p.ksb + (int64_t)ji.h * p.ksh;
+    const T* vbase = reinterpret_cast<const T*>(p.v) + ji.b * p.ksb + (int64_t)ji.h * p.ksh;
+    T* kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)start * kPage * kD;
+    T* vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)start * kPage * kD;
+    constexpr int CH = kD * (int)sizeof(T) / 16;  // 16-byte chunks per row
+    constexpr int PER = (2 * CH + 31) / 32;        // chunks per lane per token (K and V)
+    rank_walk(0, [&](int c, unsigned int selm, int r0) {
+      if (p.out_indices && ((selm >> lane) & 1u)) {
+        const int rank = r0 + __popc(selm & lt_mask);
+        if (rank < kk) p.out_indices[(size_t)ji.job * p.max_keep + rank] = ji.t0 + c + lane;
+      }
+      if (!start_ok) return;
+      // warp-cooperative row copies, 4 tokens in flight
+      unsigned int m = selm;
+      int r = r0;
+      while (m) {
+        int tt[4], rr[4];
+        int nb = 0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          tt[q] = -1;
+          rr[q] = kk;
+          if (m) {
+            const int j = __ffs(m) - 1;
+            m &= m - 1;
+            tt[q] = ji.t0 + c + j;
+            rr[q] = r++;
+            ++nb;
+          }
+        }
+        uint4 buf[4][PER];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < PER; ++e) {
+            const int x = lane + 32 * e;
+            if (q < nb && rr[q] < kk && x < 2 * CH) {
+              const T* src = (x < CH ? kbase : vbase) + (int64_t)tt[q] * p.kst;
+              buf[q][e] = ldg128(reinterpret_cast<const uint4*>(src) + (x % CH));
+            }
+          }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < PER; ++e) {
+            const int x = lane + 32 * e;
+            if (q < nb && rr[q] < kk && x < 2 * CH) {
+              T* dst = (x < CH ? kdst : vdst) + (int64_t)rr[q] * kD;
+              reinterpret_cast<uint4*>(dst)[x % CH] = buf[q][e];
+            }
+          }
       }
     });
     if (ji.part == 0 && threadIdx.x == 0) p.heads_len[row] = kk;
@@ -622,12 +771,20 @@ __global__ void __launch_bounds__(kSThreads) score_select_kernel(ScoreParams p) 
     const int slot = p.ref_slots[ji.job];
     uint32_t* bm = p.ref_bitmap + (size_t)slot * p.bitmap_words;
     if (threadIdx.x < kMaxRows) s_ov[threadIdx.x] = 0u;
+    // this CTA's words of the reference bitmap, staged in shared memory
+    const int wbeg = ji.t0 >> 5, nwords = ((ji.t1 + 31) >> 5) - wbeg;
+    const bool staged = nwords <= kRefWords;
+    if (staged)
+      for (int w = threadIdx.x; w < nwords; w += kSThreads) s_refw[w] = bm[wbeg + w];
     __syncthreads();
     for (int sel = 0; sel < p.S; ++sel) {
       const int kk = (int)s_k[sel];
       unsigned int local = 0;
       rank_pass(sel, [&](int t, int rank, int) {
-        if (rank >= 0 && rank < kk) local += (bm[t >> 5] >> (t & 31)) & 1u;
+        if (rank >= 0 && rank < kk) {
+          const uint32_t word = staged ? s_refw[(t >> 5) - wbeg] : bm[t >> 5];
+          local += (word >> (t & 31)) & 1u;
+        }
       });
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
