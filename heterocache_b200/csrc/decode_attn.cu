@@ -32,7 +32,7 @@ __device__ __forceinline__ int row_prefix(const FDParams& p, int* s_start, int* 
     int r = c0 + threadIdx.x;
     int len = r < p.R ? p.heads_len[r] : 0;
     len = len < 0 ? 0 : len;
-    int l16 = (len + 15) & ~15;
+    int l16 = (len + p.gran - 1) / p.gran * p.gran;
     int tot;
     int ex = block_exclusive_scan(l16, s_warp, tot);
     if (r < p.R) s_start[r] = carry + ex;
@@ -44,9 +44,9 @@ __device__ __forceinline__ int row_prefix(const FDParams& p, int* s_start, int* 
   return carry;
 }
 
-__device__ __forceinline__ int span_of(int total, int nctas) {
+__device__ __forceinline__ int span_of(int total, int nctas, int gran) {
   int s = (total + nctas - 1) / nctas;
-  return (s + 15) & ~15;
+  return (s + gran - 1) / gran * gran;
 }
 
 template <typename T>
@@ -55,7 +55,12 @@ struct WarpState {
   float o[kGMax][4];    // dims 4*lane .. 4*lane+3 for every query head
 };
 
-// 16-bit dtypes: tensor-core q.K^T.
+template <typename T>
+__device__ __forceinline__ void fd_group_compute(const FDParams& p, WarpState<T>& st, const uint32_t (&qa)[8][2],
+                                                 const uint4 (&kf)[2][4], const uint2 (&vf)[16], int valid,
+                                                 float* sp, float* sc);
+
+// 16-bit dtypes: tensor-core q.K^T, loads from global memory.
 template <typename T>
 __device__ __forceinline__ void fd_group_mma(const FDParams& p, WarpState<T>& st, const uint32_t (&qa)[8][2],
                                              const T* kbase, const T* vbase, int valid, float* sp, float* sc) {
@@ -69,7 +74,18 @@ __device__ __forceinline__ void fd_group_mma(const FDParams& p, WarpState<T>& st
   uint2 vf[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) vf[i] = ld_stream64(vbase + i * kD + 4 * lane);
+  fd_group_compute<T>(p, st, qa, kf, vf, valid, sp, sc);
+}
 
+// The math of one 16-token group given its key fragments (kf: the lane's
+// 16-byte slices of rows gid and gid+8, dims 32s+8tig..) and value slices
+// (vf: dims 4*lane.. of the 16 rows).
+template <typename T>
+__device__ __forceinline__ void fd_group_compute(const FDParams& p, WarpState<T>& st, const uint32_t (&qa)[8][2],
+                                                 const uint4 (&kf)[2][4], const uint2 (&vf)[16], int valid,
+                                                 float* sp, float* sc) {
+  const int lane = threadIdx.x & 31;
+  const int gid = lane >> 2, tig = lane & 3;
   float acc[2][4];
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
@@ -191,7 +207,7 @@ __global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   const int total = row_prefix(p, s_start, s_warp);
-  const int span = span_of(total, gridDim.x);
+  const int span = span_of(total, gridDim.x, p.gran);
   const int beg = blockIdx.x * span;
   if (beg >= total) return;
   const int end = min(total, beg + span);
@@ -290,6 +306,192 @@ __global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pipelined variant for 16-bit pools.  Rows are padded to 64 tokens and the
+// flattened space is cut into 64-token tiles (a tile never crosses a page:
+// 256 % 64 == 0).  Warp kTConsumers is the producer: one lane streams each
+// tile's 16 KB of keys and 16 KB of values into a ring of kTStages shared
+// memory stages with two bulk copies (cp.async.bulk, completion counted on
+// the stage's "full" mbarrier).  Warps 0..kTConsumers-1 each take one
+// 16-token group of a tile from shared memory and release the stage on its
+// "empty" mbarrier.  Loads stay in flight while the consumers compute.
+// All waits are bounded; after a timeout a warp stops waiting but keeps the
+// same control flow (so the consumers' named barriers still meet) and the
+// producer waits, bounded, for the copies it issued before it exits.
+constexpr int kTTile = 64;
+constexpr int kTStages = 3;
+constexpr int kTConsumers = 4;
+constexpr int kTThreads = (kTConsumers + 1) * 32;
+
+template <typename T>
+__global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams p) {
+  constexpr int kTileBytes = kTTile * kD * (int)sizeof(T);
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char* stages = smem_raw;  // [kTStages][K tile, V tile]
+  int* s_start = reinterpret_cast<int*>(smem_raw + (size_t)kTStages * 2 * kTileBytes);
+  // per-warp partial outputs for the merge: [kTConsumers][G][kD] floats
+  float* s_ob = reinterpret_cast<float*>(smem_raw + (size_t)kTStages * 2 * kTileBytes +
+                                         (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15));
+  auto s_o = [&](int w, int g) { return s_ob + ((size_t)w * p.G + g) * kD; };
+  __shared__ __align__(8) uint64_t full_bar[kTStages], empty_bar[kTStages];
+  __shared__ int s_warp[32];
+  __shared__ __align__(16) float s_p[kTConsumers][kGMax * 16];
+  __shared__ float s_c[kTConsumers][kGMax];
+  __shared__ float s_m[kTConsumers][kGMax], s_l[kTConsumers][kGMax];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int gid = lane >> 2, tig = lane & 3;
+  const int total = row_prefix(p, s_start, s_warp);
+  const int span = span_of(total, gridDim.x, kTTile);
+  const int beg = blockIdx.x * span;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kTConsumers);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (beg >= total) return;
+  const int end = min(total, beg + span);
+  const int ntiles = (end - beg) / kTTile;
+  int r0 = 0, hi = p.R - 1;  // first row with s_start[r+1] > beg
+  while (r0 < hi) {
+    const int mid = (r0 + hi) >> 1;
+    if (s_start[mid + 1] > beg) hi = mid; else r0 = mid + 1;
+  }
+
+  if (warp == kTConsumers) {
+    // ---- producer
+    if (lane == 0) {
+      int r = r0, issued = 0;
+      bool dead = false;
+      for (int i = 0; i < ntiles && !dead; ++i) {
+        const int s = i % kTStages;
+        if (!mbar_wait(&empty_bar[s], ((i / kTStages) & 1) ^ 1)) {
+          set_err(p.err, HC_ERR_TIMEOUT);
+          dead = true;
+          break;
+        }
+        const int tok = beg + i * kTTile;
+        while (s_start[r + 1] <= tok) ++r;
+        const int t = tok - s_start[r];
+        const int page = t >> 8;
+        const int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
+        if (blk < 0 || blk >= p.n_blocks) {  // consumers skip this tile (same check)
+          set_err(p.err, HC_ERR_RANGE);
+          mbar_arrive(&full_bar[s]);
+          continue;
+        }
+        const int64_t off = ((int64_t)blk * kPage + (t & (kPage - 1))) * kD;
+        unsigned char* dst = stages + (size_t)s * 2 * kTileBytes;
+        mbar_arrive_expect_tx(&full_bar[s], 2 * kTileBytes);
+        bulk_g2s(dst, reinterpret_cast<const T*>(p.kp) + off, kTileBytes, &full_bar[s]);
+        bulk_g2s(dst + kTileBytes, reinterpret_cast<const T*>(p.vp) + off, kTileBytes, &full_bar[s]);
+        issued = i + 1;
+      }
+      if (dead) {  // let the copies this CTA issued land before it exits
+        for (int i = max(0, issued - kTStages); i < issued; ++i)
+          (void)mbar_wait(&full_bar[i % kTStages], (i / kTStages) & 1);
+      }
+    }
+    return;
+  }
+
+  // ---- consumers
+  WarpState<T> st;
+  uint32_t qa[8][2];
+  int cur = -1;
+  bool dead = false;
+  auto reset_state = [&]() {
+    st.m = -INFINITY;
+    st.l = 0.f;
+#pragma unroll
+    for (int g = 0; g < kGMax; ++g) st.o[g][0] = st.o[g][1] = st.o[g][2] = st.o[g][3] = 0.f;
+  };
+  auto load_q = [&](int r) {
+    const int b = r / p.KV, h = r % p.KV;
+    const T* qg = reinterpret_cast<const T*>(p.q) + b * p.qsb + (int64_t)(h * p.G + (gid < p.G ? gid : 0)) * p.qsh;
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const uint2 w = gid < p.G ? ldg64(qg + 32 * s + 8 * tig + 4 * u) : make_uint2(0u, 0u);
+        qa[2 * s + u][0] = w.x;
+        qa[2 * s + u][1] = w.y;
+      }
+  };
+  // merge the consumer warps' states of row r into partial slot (cta + r)
+  auto flush = [&](int r) {
+    if (tig == 0 && gid < kGMax) {
+      s_m[warp][gid] = st.m;
+      s_l[warp][gid] = st.l;
+    }
+#pragma unroll
+    for (int g = 0; g < kGMax; ++g)
+      if (g < p.G)
+        *reinterpret_cast<float4*>(s_o(warp, g) + 4 * lane) = make_float4(st.o[g][0], st.o[g][1], st.o[g][2], st.o[g][3]);
+    named_bar_sync(1, kTConsumers * 32);
+    const int slot = blockIdx.x + r;
+    for (int e = threadIdx.x; e < p.G * kD; e += kTConsumers * 32) {
+      const int g = e / kD, d = e % kD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kTConsumers; ++w) M = fmaxf(M, s_m[w][g]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int w = 0; w < kTConsumers; ++w) {
+        const float f = (s_m[w][g] == -INFINITY) ? 0.f : exp2f(s_m[w][g] - M);
+        L += f * s_l[w][g];
+        O += f * s_o(w, g)[d];
+      }
+      p.part_o[((size_t)slot * p.G + g) * kD + d] = O;
+      if (d == 0) p.part_ml[(size_t)slot * p.G + g] = make_float2(M, L);
+    }
+    named_bar_sync(1, kTConsumers * 32);
+  };
+
+  int r = r0;
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % kTStages;
+    const int tok = beg + i * kTTile;
+    while (s_start[r + 1] <= tok) ++r;
+    if (r != cur) {
+      if (cur >= 0) flush(cur);
+      load_q(r);
+      reset_state();
+      cur = r;
+    }
+    if (!dead && !mbar_wait(&full_bar[s], (i / kTStages) & 1)) {
+      if (lane == 0) set_err(p.err, HC_ERR_TIMEOUT);
+      dead = true;
+    }
+    if (!dead) {
+      const int t = tok - s_start[r];
+      const int page = t >> 8;
+      const int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
+      const int valid = (blk < 0 || blk >= p.n_blocks) ? 0 : min(16, p.heads_len[r] - t - 16 * warp);
+      if (valid > 0) {
+        const uint32_t kb = smem_u32(stages + (size_t)s * 2 * kTileBytes) + 16 * warp * kD * (int)sizeof(T);
+        const uint32_t vb = kb + kTileBytes;
+        uint4 kf[2][4];
+        uint2 vf[16];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            kf[nt][q] = lds128(kb + ((8 * nt + gid) * kD + 32 * q + 8 * tig) * (int)sizeof(T));
+#pragma unroll
+        for (int j = 0; j < 16; ++j) vf[j] = lds64(vb + (j * kD + 4 * lane) * (int)sizeof(T));
+        fd_group_compute<T>(p, st, qa, kf, vf, valid, s_p[warp], s_c[warp]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
+    }
+  }
+  if (cur >= 0) flush(cur);
+}
+
 // Merge of one (row, query head): block-parallel over the row's partials.
 // Phase A: lanes over partials -> max, weights exp2(m_c - M) (kept in shared
 // memory) and the weighted normaliser.  Phase B: each warp takes every 8th
@@ -306,7 +508,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   __shared__ float s_red[kCThreads / 32];
   __shared__ float4 s_acc[kCThreads / 32][kD / 4];
   const int total = row_prefix(p, s_start, s_warp);
-  const int span = span_of(total, nctas);
+  const int span = span_of(total, nctas, p.gran);
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD;
@@ -388,29 +590,80 @@ size_t flash_decode_ws_bytes(int R, int G) {
 }
 
 template <typename T>
-static int fd_launch(FDParams& p, int grid, size_t dsm, cudaStream_t st) {
-  flash_decode_kernel<T><<<grid, kFThreads, dsm, st>>>(p);
-  if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
-  const size_t csm = ((dsm + 15) & ~(size_t)15) + (size_t)grid * sizeof(float);
+static int fd_combine(FDParams& p, int grid, cudaStream_t st) {
+  const size_t csm = (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) + (size_t)grid * sizeof(float);
   flash_combine_kernel<T><<<p.R * p.G, kCThreads, csm, st>>>(p, grid);
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+// fp32 pools: the global-load kernel, rows padded to 16.
+static int fd_launch_f32(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  const int grid = fd_grid(HC_F32);
+  const size_t slots = (size_t)grid + p.R;
+  if (!ws || ws_bytes < slots * p.G * kD * sizeof(float) + slots * p.G * sizeof(float2)) return HC_ERR_WORKSPACE;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
+  p.gran = 16;
+  flash_decode_kernel<float><<<grid, kFThreads, (size_t)(p.R + 1) * sizeof(int), st>>>(p);
   if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
-  return HC_OK;
+  return fd_combine<float>(p, grid, st);
+}
+
+// 16-bit pools: the bulk-copy pipeline, rows padded to 64.  The attribute and
+// occupancy queries are made once per shared-memory size and cached.
+template <typename T>
+static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  static bool attr_set = false;
+  static size_t cache_smem[8];
+  static int cache_grid[8], n_cache = 0;
+  auto kern = flash_decode_tma_kernel<T>;
+  const size_t dsm = (size_t)kTStages * 2 * kTTile * kD * sizeof(T) +
+                     (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) +
+                     (size_t)kTConsumers * p.G * kD * sizeof(float);
+  if (!attr_set) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return HC_ERR_CUDA;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes) !=
+        cudaSuccess)
+      return HC_ERR_CUDA;
+    attr_set = true;
+  }
+  int grid = 0;
+  for (int i = 0; i < n_cache; ++i)
+    if (cache_smem[i] == dsm) grid = cache_grid[i];
+  if (grid == 0) {
+    int dev = 0, sms = 148, occ = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTThreads, dsm) != cudaSuccess) return HC_ERR_CUDA;
+    if (occ <= 0) return HC_ERR_UNSUPPORTED;
+    grid = sms * occ;
+    if (n_cache < 8) {
+      cache_smem[n_cache] = dsm;
+      cache_grid[n_cache] = grid;
+      ++n_cache;
+    }
+  }
+  const size_t slots = (size_t)grid + p.R;
+  if (!ws || ws_bytes < slots * p.G * kD * sizeof(float) + slots * p.G * sizeof(float2)) return HC_ERR_WORKSPACE;
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
+  p.gran = kTTile;
+  kern<<<grid, kTThreads, dsm, st>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
+  return fd_combine<T>(p, grid, st);
 }
 
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (p.R <= 0 || p.R > kMaxRowsFD) return HC_ERR_UNSUPPORTED;
   if (p.G <= 0 || p.G > kGMax) return HC_ERR_UNSUPPORTED;
-  const int grid = fd_grid(dtype);
-  const size_t slots = (size_t)grid + p.R;
-  const size_t need = slots * p.G * kD * sizeof(float) + slots * p.G * sizeof(float2);
-  if (!ws || ws_bytes < need) return HC_ERR_WORKSPACE;
-  p.part_o = reinterpret_cast<float*>(ws);
-  p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
-  const size_t dsm = (size_t)(p.R + 1) * sizeof(int);
   switch (dtype) {
-    case HC_F32: return fd_launch<float>(p, grid, dsm, st);
-    case HC_BF16: return fd_launch<__nv_bfloat16>(p, grid, dsm, st);
-    case HC_F16: return fd_launch<__half>(p, grid, dsm, st);
+    case HC_F32: return fd_launch_f32(p, ws, ws_bytes, st);
+    case HC_BF16: return fd_launch_tma<__nv_bfloat16>(p, ws, ws_bytes, st);
+    case HC_F16: return fd_launch_tma<__half>(p, ws, ws_bytes, st);
     default: return HC_ERR_DTYPE;
   }
 }

@@ -82,6 +82,7 @@ struct FDParams {
   int n_blocks;
   const int32_t* heads_len;
   int R, KV, G;
+  int gran;  // rows are padded to, and CTA spans cut at, multiples of this many tokens
   float scale_log2;
   float* part_o;
   float2* part_ml;
