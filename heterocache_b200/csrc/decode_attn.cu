@@ -19,6 +19,9 @@
 // query heads with two m16n8k16 MMAs per 16 dims (queries on M, padded to 16;
 // tokens on N), and accumulates P.V on the CUDA cores with each lane owning 4
 // of the 128 output dims.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "hc_params.cuh"
 
 namespace hc {
@@ -307,36 +310,152 @@ __global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Pipelined variant for 16-bit pools.  Rows are padded to 64 tokens and the
-// flattened space is cut into 64-token tiles (a tile never crosses a page:
-// 256 % 64 == 0).  Warp kTConsumers is the producer: one lane streams each
-// tile's 16 KB of keys and 16 KB of values into a ring of kTStages shared
-// memory stages with two bulk copies (cp.async.bulk, completion counted on
-// the stage's "full" mbarrier).  Warps 0..kTConsumers-1 each take one
-// 16-token group of a tile from shared memory and release the stage on its
-// "empty" mbarrier.  Loads stay in flight while the consumers compute.
-// All waits are bounded; after a timeout a warp stops waiting but keeps the
-// same control flow (so the consumers' named barriers still meet) and the
-// producer waits, bounded, for the copies it issued before it exits.
+// Pipelined tensor-core variant for 16-bit pools.
+//
+// Rows are padded to 64 tokens and the flattened space is cut into 64-token
+// tiles (a tile never crosses a page: 256 % 64 == 0).  Warp kTConsumers is the
+// producer: one lane loads each tile with four TMA tensor copies (keys and
+// values, dims 0-63 and 64-127, each a 64-row x 128-byte box with the 128-byte
+// swizzle) into a ring of kTStages shared-memory stages, completion counted on
+// the stage's "full" mbarrier.  Consumer warp w takes tokens 16w..16w+15 of a
+// tile:
+//   S  = Q K^T   m16n8k16, A = query rows (registers), B = key rows (ldmatrix)
+//   O^T += V^T P^T  m16n8k16, A = value rows transposed (ldmatrix.trans),
+//                 B = the probabilities straight from S's accumulators
+// and releases the stage on its "empty" mbarrier.  The swizzle makes every
+// ldmatrix conflict-free.  All waits are bounded; after a timeout a warp
+// stops waiting but keeps the same control flow (so the consumers' named
+// barriers still meet) and the producer waits, bounded, for the copies it
+// issued before it exits.
 constexpr int kTTile = 64;
 constexpr int kTStages = 3;
 constexpr int kTConsumers = 4;
 constexpr int kTThreads = (kTConsumers + 1) * 32;
+constexpr int kTBox = kTTile * 64 * 2;  // bytes of one 64-row x 64-element box
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// Address of 16-byte chunk `chunk` (0..15 over the 128 dims) of tile row
+// `row` (0..63), for a stage whose first box starts at `base` (1024-aligned).
+__device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
+  return base + (chunk >> 3) * kTBox + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct TcState {
+  float m, l;       // query row gid (same on the 4 lanes of the row)
+  float ot[8][4];   // O^T: dims 16mt+gid(+8), queries 2tig, 2tig+1
+};
+
+// One 16-token group; kst/vst = shared addresses of the stage's key/value
+// boxes, tok0 = first tile row of the group, valid = tokens to use.
+template <typename T>
+__device__ __forceinline__ void fd_group_tc(const FDParams& p, TcState& st, const uint32_t (&qa)[8][2],
+                                            uint32_t kst, uint32_t vst, int tok0, int valid) {
+  const int lane = threadIdx.x & 31;
+  const int tig = lane & 3;
+  const int mi = lane >> 3, j = lane & 7;
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const int krow = tok0 + 8 * (mi >> 1) + j;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t b[4];
+    ldsm_x4(b, swz(kst, krow, 2 * ks + (mi & 1)));
+    mma16816<T>(acc[0], qa[ks][0], 0u, qa[ks][1], 0u, b[0], b[1]);
+    mma16816<T>(acc[1], qa[ks][0], 0u, qa[ks][1], 0u, b[2], b[3]);
+  }
+  float sv[4];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int t = 8 * nt + 2 * tig + e;
+      const float x = t < valid ? acc[nt][e] * p.scale_log2 : -INFINITY;
+      sv[nt * 2 + e] = x;
+      mx = fmaxf(mx, x);
+    }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  const float mnew = fmaxf(st.m, mx);
+  const float corr = (mnew == -INFINITY) ? 1.f : exp2f(st.m - mnew);
+  float rs = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float pv = (sv[i] == -INFINITY) ? 0.f : exp2f(sv[i] - mnew);
+    sv[i] = pv;
+    rs += pv;
+  }
+  rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+  rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+  st.l = st.l * corr + rs;
+  st.m = mnew;
+  // rescale O^T columns (queries 2tig, 2tig+1) by their rows' corrections
+  const float c0 = __shfl_sync(0xffffffffu, corr, 8 * tig);
+  const float c1 = __shfl_sync(0xffffffffu, corr, 8 * tig + 4);
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    st.ot[mt][0] *= c0;
+    st.ot[mt][1] *= c1;
+    st.ot[mt][2] *= c0;
+    st.ot[mt][3] *= c1;
+  }
+  // P^T as the B operand: tokens 2tig.. (n-tile 0) and 8+2tig.. (n-tile 1)
+  const uint32_t b0 = pack2<T>(sv[0], sv[1]);
+  const uint32_t b1 = pack2<T>(sv[2], sv[3]);
+  const int vrow = tok0 + 8 * (mi >> 1) + j;
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    uint32_t a[4];
+    ldsm_x4_t(a, swz(vst, vrow, 2 * mt + (mi & 1)));
+    // a[0]: dims 16mt..+7 x tokens 0-7, a[1]: dims +8.. x tokens 0-7,
+    // a[2]: dims 16mt.. x tokens 8-15, a[3]: dims +8.. x tokens 8-15
+    mma16816<T>(st.ot[mt], a[0], a[1], a[2], a[3], b0, b1);
+  }
+}
 
 template <typename T>
-__global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams p) {
-  constexpr int kTileBytes = kTTile * kD * (int)sizeof(T);
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char* stages = smem_raw;  // [kTStages][K tile, V tile]
-  int* s_start = reinterpret_cast<int*>(smem_raw + (size_t)kTStages * 2 * kTileBytes);
-  // per-warp partial outputs for the merge: [kTConsumers][G][kD] floats
-  float* s_ob = reinterpret_cast<float*>(smem_raw + (size_t)kTStages * 2 * kTileBytes +
+__global__ void __launch_bounds__(kTThreads, 2)
+    flash_decode_tma_kernel(FDParams p, const __grid_constant__ CUtensorMap tmk,
+                            const __grid_constant__ CUtensorMap tmv) {
+  constexpr int kStageBytes = 4 * kTBox;  // K box 0, K box 1, V box 0, V box 1
+  extern __shared__ __align__(16) unsigned char smem_dyn[];
+  // the 128-byte swizzle pattern is taken from address bits 4-9: stages start
+  // on a 1024-byte boundary (the launch reserves 1024 bytes of slack)
+  unsigned char* smem_raw = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
+  unsigned char* stages = smem_raw;
+  int* s_start = reinterpret_cast<int*>(smem_raw + (size_t)kTStages * kStageBytes);
+  float* s_ob = reinterpret_cast<float*>(smem_raw + (size_t)kTStages * kStageBytes +
                                          (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15));
   auto s_o = [&](int w, int g) { return s_ob + ((size_t)w * p.G + g) * kD; };
   __shared__ __align__(8) uint64_t full_bar[kTStages], empty_bar[kTStages];
   __shared__ int s_warp[32];
-  __shared__ __align__(16) float s_p[kTConsumers][kGMax * 16];
-  __shared__ float s_c[kTConsumers][kGMax];
   __shared__ float s_m[kTConsumers][kGMax], s_l[kTConsumers][kGMax];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -366,7 +485,7 @@ __global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams
     if (lane == 0) {
       int r = r0, issued = 0;
       bool dead = false;
-      for (int i = 0; i < ntiles && !dead; ++i) {
+      for (int i = 0; i < ntiles; ++i) {
         const int s = i % kTStages;
         if (!mbar_wait(&empty_bar[s], ((i / kTStages) & 1) ^ 1)) {
           set_err(p.err, HC_ERR_TIMEOUT);
@@ -383,11 +502,13 @@ __global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams
           mbar_arrive(&full_bar[s]);
           continue;
         }
-        const int64_t off = ((int64_t)blk * kPage + (t & (kPage - 1))) * kD;
-        unsigned char* dst = stages + (size_t)s * 2 * kTileBytes;
-        mbar_arrive_expect_tx(&full_bar[s], 2 * kTileBytes);
-        bulk_g2s(dst, reinterpret_cast<const T*>(p.kp) + off, kTileBytes, &full_bar[s]);
-        bulk_g2s(dst + kTileBytes, reinterpret_cast<const T*>(p.vp) + off, kTileBytes, &full_bar[s]);
+        const int y = blk * kPage + (t & (kPage - 1));
+        unsigned char* dst = stages + (size_t)s * kStageBytes;
+        mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+        tma_load_2d(dst, &tmk, 0, y, &full_bar[s]);
+        tma_load_2d(dst + kTBox, &tmk, 64, y, &full_bar[s]);
+        tma_load_2d(dst + 2 * kTBox, &tmv, 0, y, &full_bar[s]);
+        tma_load_2d(dst + 3 * kTBox, &tmv, 64, y, &full_bar[s]);
         issued = i + 1;
       }
       if (dead) {  // let the copies this CTA issued land before it exits
@@ -399,7 +520,7 @@ __global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams
   }
 
   // ---- consumers
-  WarpState<T> st;
+  TcState st;
   uint32_t qa[8][2];
   int cur = -1;
   bool dead = false;
@@ -407,19 +528,16 @@ __global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams
     st.m = -INFINITY;
     st.l = 0.f;
 #pragma unroll
-    for (int g = 0; g < kGMax; ++g) st.o[g][0] = st.o[g][1] = st.o[g][2] = st.o[g][3] = 0.f;
+    for (int mt = 0; mt < 8; ++mt) st.ot[mt][0] = st.ot[mt][1] = st.ot[mt][2] = st.ot[mt][3] = 0.f;
   };
   auto load_q = [&](int r) {
     const int b = r / p.KV, h = r % p.KV;
     const T* qg = reinterpret_cast<const T*>(p.q) + b * p.qsb + (int64_t)(h * p.G + (gid < p.G ? gid : 0)) * p.qsh;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const uint2 w = gid < p.G ? ldg64(qg + 32 * s + 8 * tig + 4 * u) : make_uint2(0u, 0u);
-        qa[2 * s + u][0] = w.x;
-        qa[2 * s + u][1] = w.y;
-      }
+    for (int ks = 0; ks < 8; ++ks) {
+      qa[ks][0] = gid < p.G ? __ldg(reinterpret_cast<const uint32_t*>(qg + 16 * ks + 2 * tig)) : 0u;
+      qa[ks][1] = gid < p.G ? __ldg(reinterpret_cast<const uint32_t*>(qg + 16 * ks + 8 + 2 * tig)) : 0u;
+    }
   };
   // merge the consumer warps' states of row r into partial slot (cta + r)
   auto flush = [&](int r) {
@@ -428,9 +546,13 @@ __global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams
       s_l[warp][gid] = st.l;
     }
 #pragma unroll
-    for (int g = 0; g < kGMax; ++g)
-      if (g < p.G)
-        *reinterpret_cast<float4*>(s_o(warp, g) + 4 * lane) = make_float4(st.o[g][0], st.o[g][1], st.o[g][2], st.o[g][3]);
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = 2 * tig + (e & 1);
+        const int d = 16 * mt + gid + 8 * (e >> 1);
+        if (q < p.G) s_o(warp, q)[d] = st.ot[mt][e];
+      }
     named_bar_sync(1, kTConsumers * 32);
     const int slot = blockIdx.x + r;
     for (int e = threadIdx.x; e < p.G * kD; e += kTConsumers * 32) {
@@ -472,18 +594,8 @@ __global__ void __launch_bounds__(kTThreads, 2) flash_decode_tma_kernel(FDParams
       const int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
       const int valid = (blk < 0 || blk >= p.n_blocks) ? 0 : min(16, p.heads_len[r] - t - 16 * warp);
       if (valid > 0) {
-        const uint32_t kb = smem_u32(stages + (size_t)s * 2 * kTileBytes) + 16 * warp * kD * (int)sizeof(T);
-        const uint32_t vb = kb + kTileBytes;
-        uint4 kf[2][4];
-        uint2 vf[16];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            kf[nt][q] = lds128(kb + ((8 * nt + gid) * kD + 32 * q + 8 * tig) * (int)sizeof(T));
-#pragma unroll
-        for (int j = 0; j < 16; ++j) vf[j] = lds64(vb + (j * kD + 4 * lane) * (int)sizeof(T));
-        fd_group_compute<T>(p, st, qa, kf, vf, valid, s_p[warp], s_c[warp]);
+        const uint32_t kst = smem_u32(stages + (size_t)s * kStageBytes);
+        fd_group_tc<T>(p, st, qa, kst, kst + 2 * kTBox, 16 * warp, valid);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty_bar[s]);
@@ -609,7 +721,49 @@ static int fd_launch_f32(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   return fd_combine<float>(p, grid, st);
 }
 
-// 16-bit pools: the bulk-copy pipeline, rows padded to 64.  The attribute and
+// Tensor map of a pool viewed as a 2-D [n_blocks*256 rows, 128] array of
+// 16-bit elements, boxes of 64 rows x 64 elements, 128-byte swizzle.  Encoded
+// once per pool address (cached) through the driver entry point.
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int pool_tensor_map(CUtensorMap* out, const void* base, long long rows, int dtype) {
+  struct Entry { const void* base; long long rows; int dtype; CUtensorMap map; };
+  static Entry cache[256];
+  static int n = 0, next = 0;
+  for (int i = 0; i < n; ++i)
+    if (cache[i].base == base && cache[i].rows == rows && cache[i].dtype == dtype) {
+      *out = cache[i].map;
+      return HC_OK;
+    }
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return HC_ERR_CUDA;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kD * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kTTile};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType ty =
+      dtype == HC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (g_encode(&map, ty, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return HC_ERR_CUDA;
+  Entry& e = cache[n < 256 ? n++ : (next++ % 256)];
+  e.base = base;
+  e.rows = rows;
+  e.dtype = dtype;
+  e.map = map;
+  *out = map;
+  return HC_OK;
+}
+
+// 16-bit pools: the TMA pipeline, rows padded to 64.  The attribute and
 // occupancy queries are made once per shared-memory size and cached.
 template <typename T>
 static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -617,8 +771,12 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   static size_t cache_smem[8];
   static int cache_grid[8], n_cache = 0;
   auto kern = flash_decode_tma_kernel<T>;
-  const size_t dsm = (size_t)kTStages * 2 * kTTile * kD * sizeof(T) +
-                     (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) +
+  const int dtype = std::is_same<T, __nv_bfloat16>::value ? HC_BF16 : HC_F16;
+  CUtensorMap tmk, tmv;
+  const long long rows = (long long)p.n_blocks * kPage;
+  if (pool_tensor_map(&tmk, p.kp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
+  if (pool_tensor_map(&tmv, p.vp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
+  const size_t dsm = 1024 + (size_t)kTStages * 4 * kTBox + (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) +
                      (size_t)kTConsumers * p.G * kD * sizeof(float);
   if (!attr_set) {
     int dev = 0, optin = 0;
@@ -652,7 +810,7 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
   p.gran = kTTile;
-  kern<<<grid, kTThreads, dsm, st>>>(p);
+  kern<<<grid, kTThreads, dsm, st>>>(p, tmk, tmv);
   if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
   return fd_combine<T>(p, grid, st);
 }
