@@ -37,6 +37,9 @@ SIGNATURES = {
     "hc_flash_decode": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p,
                                 c_void_p, c_int, c_void_p, c_int, c_void_p, c_float, c_void_p, c_longlong,
                                 c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_flash_decode_noalloc": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p,
+                                        c_void_p, c_int, c_void_p, c_int, c_void_p, c_float, c_void_p, c_void_p,
+                                        c_void_p]),
     "hc_drift_check_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "hc_drift_check": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_double,
                                c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p,

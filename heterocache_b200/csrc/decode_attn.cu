@@ -815,6 +815,61 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   return fd_combine<T>(p, grid, st);
 }
 
+// ---------------------------------------------------------------------------
+// Fixed scratch for hc_flash_decode_noalloc: the split-K partials live in this
+// module-scope array instead of a caller workspace.  Host code must not use
+// the symbol as a device address; the address is fetched with
+// cudaGetSymbolAddress once per device (on that device's first call).
+static __device__ __align__(256) unsigned char g_noalloc_scratch[HC_NOALLOC_SCRATCH_BYTES];
+static void* g_noalloc_ptr[64] = {nullptr};
+
+size_t flash_decode_scratch_need(int dtype, int R, int G);
+
+int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_t* need_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HC_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return HC_ERR_UNSUPPORTED;
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return HC_ERR_CUDA;
+    g_noalloc_ptr[dev] = ptr;
+  }
+  const size_t need = flash_decode_scratch_need(dtype, p.R, p.G);
+  if (need_out) *need_out = need;
+  if (need == 0) return HC_ERR_CUDA;
+  if (need > (size_t)HC_NOALLOC_SCRATCH_BYTES) return HC_ERR_WORKSPACE;
+  return flash_decode_dispatch(dtype, p, g_noalloc_ptr[dev], HC_NOALLOC_SCRATCH_BYTES, st);
+}
+
+// Partials bytes one hc_flash_decode launch writes: (grid + rows) slots of
+// G x (128 + 2) floats; the grid is the device's co-resident CTA count.
+size_t flash_decode_scratch_need(int dtype, int R, int G) {
+  int grid = 0;
+  if (dtype == HC_F32) {
+    grid = fd_grid(HC_F32);
+  } else {
+    int dev = 0, sms = 148, occ = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t dsm = 1024 + (size_t)kTStages * 4 * kTBox + (((size_t)(R + 1) * sizeof(int) + 15) & ~(size_t)15) +
+                       (size_t)kTConsumers * G * kD * sizeof(float);
+    const void* kern = dtype == HC_BF16 ? (const void*)flash_decode_tma_kernel<__nv_bfloat16>
+                                        : (const void*)flash_decode_tma_kernel<__half>;
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes) !=
+        cudaSuccess)
+      return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTThreads, dsm) != cudaSuccess || occ <= 0)
+      return 0;
+    grid = sms * occ;
+  }
+  const size_t slots = (size_t)grid + R;
+  return slots * G * kD * sizeof(float) + slots * G * sizeof(float2);
+}
+
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (p.R <= 0 || p.R > kMaxRowsFD) return HC_ERR_UNSUPPORTED;
   if (p.G <= 0 || p.G > kGMax) return HC_ERR_UNSUPPORTED;

@@ -92,6 +92,7 @@ struct FDParams {
 
 size_t flash_decode_ws_bytes(int R, int G);
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
+int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_t* need_out);
 
 // ---- page copies (kv_copy.cu)
 int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k,

@@ -151,6 +151,36 @@ int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_d
                     void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Decode attention without a workspace.  No counterpart in the reference:
+ * this is an addition for callers that cannot allocate device memory, such as
+ * a host program whose device memory is entirely owned by another allocator,
+ * or a language binding with no device allocator to call, and that therefore
+ * cannot pass the workspace hc_flash_decode asks for.
+ *
+ * Same arguments, result and errors as hc_flash_decode, minus the workspace:
+ * the split-K partials go to a fixed array of HC_NOALLOC_SCRATCH_BYTES that
+ * the library defines at file scope in device memory.  Every GPU that loads
+ * the library holds that array until the process exits.  The entry point
+ * allocates nothing (no cudaMalloc, no cudaFree, no allocating library call).
+ *   - The first call on a device looks the array's device address up
+ *     (cudaGetSymbolAddress, with that device current); make that first
+ *     call before any stream capture.
+ *   - Requests whose partials need more than HC_NOALLOC_SCRATCH_BYTES (many
+ *     rows: about 1700 batch*KV rows for 4 query heads per KV head, about 700
+ *     for 8) return HC_ERR_WORKSPACE and launch nothing.
+ *   - All calls share the one array, and it keeps what the last call wrote.
+ *     Nothing in it has to start at zero (every partial is written before it
+ *     is read).  Calls that overlap on the GPU -- on different streams, or
+ *     from different host threads without ordering -- race on it; order them.
+ */
+#define HC_NOALLOC_SCRATCH_BYTES (4u << 20)
+int hc_flash_decode_noalloc(int dtype, int bsz, int num_kv_heads, int groups, int head_dim,
+                            const void* q, int64_t qsb, int64_t qsh,
+                            const void* k_pool, const void* v_pool, int n_pool_blocks,
+                            const int32_t* block_table, int max_blocks, const int32_t* heads_len,
+                            float scale, void* out, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Decode: pivot drift check.  Replaces the scoring and overlap part of
  * HeteroCache.decode_select (heterocache/cache_utils.py:1007-1082) for
  * batch size 1.  For each job j (a pivot with at least one satellite):
