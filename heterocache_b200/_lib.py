@@ -19,18 +19,20 @@ SIGNATURES = {
     "hc_status_string": (ctypes.c_char_p, [c_int]),
     "hc_last_cuda_error": (ctypes.c_char_p, []),
     "hc_prefill_keep": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
-                                c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
-                                c_void_p, c_void_p]),
+                                c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int,
+                                c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "hc_prefill_select_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "hc_prefill_select": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                                   c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
-                                  c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                  c_int64, c_int64, c_int64, c_int64,
+                                  c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "hc_pivot_init_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "hc_pivot_init": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                               c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
-    "hc_decode_append": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+    "hc_decode_append": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                 c_int64, c_void_p,
                                  c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
                                  c_void_p]),
     "hc_flash_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),

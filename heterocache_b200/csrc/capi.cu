@@ -50,18 +50,20 @@ const char* hc_status_string(int status) {
 const char* hc_last_cuda_error(void) { return g_last_err; }
 
 int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_dim, const int32_t* keep_heads,
-                    int n_keep, const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, void* k_pool,
-                    void* v_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks, int32_t* heads_len,
-                    int32_t* err_flag, void* stream) {
+                    int n_keep, const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb,
+                    int64_t vsh, int64_t vst, void* k_pool, void* v_pool, int n_pool_blocks,
+                    const int32_t* block_table, int max_blocks, int32_t* heads_len, int32_t* err_flag,
+                    void* stream) {
   if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
   if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || seq_len <= 0 || n_keep < 0) return HC_ERR_INVALID;
   if (n_keep == 0) return HC_OK;
   if (!aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool)) return HC_ERR_INVALID;
-  if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh) || !stride_ok(dtype, st)) return HC_ERR_INVALID;
+  if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh) || !stride_ok(dtype, st) || !stride_ok(dtype, vsb) ||
+      !stride_ok(dtype, vsh) || !stride_ok(dtype, vst))
+    return HC_ERR_INVALID;
   return note_cuda(hc::prefill_keep_dispatch(dtype, bsz, num_kv_heads, seq_len, keep_heads, n_keep, k, v, sb, sh, st,
-                                             k_pool, v_pool, n_pool_blocks, block_table, max_blocks, heads_len,
-                                             err_flag,
-                                             (cudaStream_t)stream));
+                                             vsb, vsh, vst, k_pool, v_pool, n_pool_blocks, block_table, max_blocks,
+                                             heads_len, err_flag, (cudaStream_t)stream));
 }
 
 size_t hc_prefill_select_workspace_size(int dtype, int bsz, int n_heads, int seq_len, int groups, int window) {
@@ -71,7 +73,8 @@ size_t hc_prefill_select_workspace_size(int dtype, int bsz, int n_heads, int seq
 
 int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_len, int head_dim, int n_heads,
                       int window, int pooling, int kernel_size, const void* q, int64_t qsb, int64_t qsh, int64_t qst,
-                      const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, const int32_t* keep_lens,
+                      const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh,
+                      int64_t vst, const int32_t* keep_lens,
                       int max_keep, void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table,
                       int max_blocks, int32_t* heads_len, int32_t* out_indices, void* out_scores, void* workspace,
                       size_t workspace_bytes, int32_t* err_flag, void* stream) {
@@ -86,11 +89,15 @@ int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool))
     return HC_ERR_INVALID;
   if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh) || !stride_ok(dtype, qst) || !stride_ok(dtype, sb) ||
-      !stride_ok(dtype, sh) || !stride_ok(dtype, st))
+      !stride_ok(dtype, sh) || !stride_ok(dtype, st) || !stride_ok(dtype, vsb) || !stride_ok(dtype, vsh) ||
+      !stride_ok(dtype, vst))
     return HC_ERR_INVALID;
   hc::ScoreParams p;
   std::memset(&p, 0, sizeof(p));
   p.mode = hc::MODE_PREFILL;
+  p.vsb = vsb;
+  p.vsh = vsh;
+  p.vst = vst;
   p.L = seq_len;
   p.G = groups;
   p.W = window;
@@ -186,17 +193,18 @@ int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len,
 }
 
 int hc_decode_append(int dtype, int bsz, int num_kv_heads, int head_dim, const void* k, const void* v, int64_t sb,
-                     int64_t sh, void* k_pool, void* v_pool, int n_pool_blocks, int32_t* block_table, int max_blocks,
-                     int32_t* heads_len, const int32_t* free_blocks, int n_free, int32_t* free_ptr,
-                     int32_t* err_flag, void* stream) {
+                     int64_t sh, int64_t vsb, int64_t vsh, void* k_pool, void* v_pool, int n_pool_blocks,
+                     int32_t* block_table, int max_blocks, int32_t* heads_len, const int32_t* free_blocks, int n_free,
+                     int32_t* free_ptr, int32_t* err_flag, void* stream) {
   if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
   if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || max_blocks <= 0 || n_free < 0)
     return HC_ERR_INVALID;
   if (!aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool)) return HC_ERR_INVALID;
-  if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh)) return HC_ERR_INVALID;
-  return note_cuda(hc::decode_append_dispatch(dtype, bsz * num_kv_heads, num_kv_heads, k, v, sb, sh, k_pool, v_pool,
-                                              n_pool_blocks, block_table, max_blocks, heads_len, free_blocks, n_free, free_ptr,
-                                              err_flag, (cudaStream_t)stream));
+  if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh) || !stride_ok(dtype, vsb) || !stride_ok(dtype, vsh))
+    return HC_ERR_INVALID;
+  return note_cuda(hc::decode_append_dispatch(dtype, bsz * num_kv_heads, num_kv_heads, k, v, sb, sh, vsb, vsh, k_pool,
+                                              v_pool, n_pool_blocks, block_table, max_blocks, heads_len, free_blocks,
+                                              n_free, free_ptr, err_flag, (cudaStream_t)stream));
 }
 
 size_t hc_flash_decode_workspace_size(int bsz, int num_kv_heads, int groups, int head_dim) {

@@ -33,6 +33,7 @@ struct ScoreParams {
   const void* k;
   const void* v;
   int64_t ksb, ksh, kst;
+  int64_t vsb, vsh, vst;
   const void* k_pool;
   const int32_t* bt;
   int max_blocks;
@@ -96,11 +97,12 @@ int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_
 
 // ---- page copies (kv_copy.cu)
 int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k,
-                          const void* v, int64_t sb, int64_t sh, int64_t st, void* kp, void* vp, int nblocks,
-                          const int32_t* bt, int mb, int32_t* hl, int32_t* err, cudaStream_t s);
-int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, void* kp,
-                           void* vp, int nblocks, int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf,
-                           int32_t* fp, int32_t* err, cudaStream_t s);
+                          const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh, int64_t vst,
+                          void* kp, void* vp, int nblocks, const int32_t* bt, int mb, int32_t* hl, int32_t* err,
+                          cudaStream_t s);
+int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh,
+                           int64_t vsb, int64_t vsh, void* kp, void* vp, int nblocks, int32_t* bt, int mb, int32_t* hl,
+                           const int32_t* fb, int nf, int32_t* fp, int32_t* err, cudaStream_t s);
 int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,
                       const int32_t* trig, const int32_t* pos, int pos_stride, const void* fk, const void* fv,
                       int64_t fsh, int64_t fst, void* kp, void* vp, int nblocks, const int32_t* bt, int mb,

@@ -11,7 +11,8 @@ namespace hc {
 // Prefill: copy keep heads' [L, D] rows into their pages; heads_len = L.
 template <typename T>
 __global__ void __launch_bounds__(256) prefill_keep_kernel(const T* __restrict__ k, const T* __restrict__ v,
-                                                           int64_t sb, int64_t sh, int64_t st, int L, int KV,
+                                                           int64_t sb, int64_t sh, int64_t st, int64_t vsb,
+                                                           int64_t vsh, int64_t vst, int L, int KV,
                                                            const int32_t* __restrict__ keep_heads, T* k_pool,
                                                            T* v_pool, int n_blocks, const int32_t* __restrict__ bt,
                                                            int max_blocks, int32_t* heads_len, int32_t* err) {
@@ -30,9 +31,10 @@ __global__ void __launch_bounds__(256) prefill_keep_kernel(const T* __restrict__
       continue;
     }
     const int64_t src = b * sb + (int64_t)h * sh + (int64_t)t * st;
+    const int64_t vsrc = b * vsb + (int64_t)h * vsh + (int64_t)t * vst;
     const int64_t dst = ((int64_t)blk * kPage + (t & (kPage - 1))) * kD;
     reinterpret_cast<uint4*>(k_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(k + src) + c);
-    reinterpret_cast<uint4*>(v_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(v + src) + c);
+    reinterpret_cast<uint4*>(v_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(v + vsrc) + c);
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) heads_len[row] = L;
 }
@@ -43,7 +45,8 @@ __global__ void __launch_bounds__(256) prefill_keep_kernel(const T* __restrict__
 // the boolean mask in order).
 template <typename T>
 __global__ void __launch_bounds__(256) decode_append_kernel(const T* __restrict__ k, const T* __restrict__ v,
-                                                            int64_t sb, int64_t sh, int R, int KV, T* k_pool,
+                                                            int64_t sb, int64_t sh, int64_t vsb, int64_t vsh, int R,
+                                                            int KV, T* k_pool,
                                                             T* v_pool, int n_blocks, int32_t* bt, int max_blocks,
                                                             int32_t* heads_len, const int32_t* __restrict__ free_blocks,
                                                             int n_free, int32_t* free_ptr, int32_t* err) {
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(256) decode_append_kernel(const T* __restrict_
     if (ok) {
       const int b = r / KV, h = r % KV;
       const uint4* ks = reinterpret_cast<const uint4*>(k + b * sb + (int64_t)h * sh);
-      const uint4* vs = reinterpret_cast<const uint4*>(v + b * sb + (int64_t)h * sh);
+      const uint4* vs = reinterpret_cast<const uint4*>(v + b * vsb + (int64_t)h * vsh);
       const int64_t dst = ((int64_t)phys * kPage + (len & (kPage - 1))) * kD;
       uint4* kd = reinterpret_cast<uint4*>(k_pool + dst);
       uint4* vd = reinterpret_cast<uint4*>(v_pool + dst);
@@ -166,41 +169,49 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
 // ---------------------------------------------------------------------------
 template <typename T>
 static int prefill_keep_t(int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k, const void* v,
-                          int64_t sb, int64_t sh, int64_t st, void* kp, void* vp, int nb, const int32_t* bt, int mb,
-                          int32_t* hl, int32_t* err, cudaStream_t s) {
+                          int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh, int64_t vst, void* kp,
+                          void* vp, int nb, const int32_t* bt, int mb, int32_t* hl, int32_t* err, cudaStream_t s) {
   dim3 grid((L + 63) / 64, n_keep, bsz);
-  prefill_keep_kernel<T><<<grid, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, st, L, KV, keep, (T*)kp, (T*)vp,
-                                              nb, bt, mb, hl, err);
+  prefill_keep_kernel<T><<<grid, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, st, vsb, vsh, vst, L, KV, keep,
+                                              (T*)kp, (T*)vp, nb, bt, mb, hl, err);
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
 int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k,
-                          const void* v, int64_t sb, int64_t sh, int64_t st, void* kp, void* vp, int nb,
-                          const int32_t* bt, int mb, int32_t* hl, int32_t* err, cudaStream_t s) {
+                          const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh, int64_t vst,
+                          void* kp, void* vp, int nb, const int32_t* bt, int mb, int32_t* hl, int32_t* err,
+                          cudaStream_t s) {
   switch (dtype) {
-    case HC_F32: return prefill_keep_t<float>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, kp, vp, nb, bt, mb, hl, err, s);
-    case HC_BF16: return prefill_keep_t<__nv_bfloat16>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, kp, vp, nb, bt, mb, hl, err, s);
-    case HC_F16: return prefill_keep_t<__half>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, kp, vp, nb, bt, mb, hl, err, s);
+    case HC_F32:
+      return prefill_keep_t<float>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, vsb, vsh, vst, kp, vp, nb, bt, mb, hl,
+                                   err, s);
+    case HC_BF16:
+      return prefill_keep_t<__nv_bfloat16>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, vsb, vsh, vst, kp, vp, nb, bt,
+                                           mb, hl, err, s);
+    case HC_F16:
+      return prefill_keep_t<__half>(bsz, KV, L, keep, n_keep, k, v, sb, sh, st, vsb, vsh, vst, kp, vp, nb, bt, mb, hl,
+                                    err, s);
     default: return HC_ERR_DTYPE;
   }
 }
 
 template <typename T>
-static int append_t(int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, void* kp, void* vp, int nb,
-                    int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf, int32_t* fp, int32_t* err,
-                    cudaStream_t s) {
-  decode_append_kernel<T><<<1, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, R, KV, (T*)kp, (T*)vp, nb, bt, mb, hl,
-                                            fb, nf, fp, err);
+static int append_t(int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, int64_t vsb, int64_t vsh,
+                    void* kp, void* vp, int nb, int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf,
+                    int32_t* fp, int32_t* err, cudaStream_t s) {
+  decode_append_kernel<T><<<1, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, vsb, vsh, R, KV, (T*)kp, (T*)vp, nb,
+                                            bt, mb, hl, fb, nf, fp, err);
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
-int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, void* kp,
-                           void* vp, int nb, int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf,
-                           int32_t* fp, int32_t* err, cudaStream_t s) {
+int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh,
+                           int64_t vsb, int64_t vsh, void* kp, void* vp, int nb, int32_t* bt, int mb, int32_t* hl,
+                           const int32_t* fb, int nf, int32_t* fp, int32_t* err, cudaStream_t s) {
   switch (dtype) {
-    case HC_F32: return append_t<float>(R, KV, k, v, sb, sh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
-    case HC_BF16: return append_t<__nv_bfloat16>(R, KV, k, v, sb, sh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
-    case HC_F16: return append_t<__half>(R, KV, k, v, sb, sh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    case HC_F32: return append_t<float>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    case HC_BF16:
+      return append_t<__nv_bfloat16>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    case HC_F16: return append_t<__half>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
     default: return HC_ERR_DTYPE;
   }
 }

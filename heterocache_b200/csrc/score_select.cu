@@ -699,7 +699,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     const bool start_ok = start >= 0 && (int64_t)start * kPage + kk <= (int64_t)p.n_blocks * kPage;
     if (!start_ok && kk > 0 && threadIdx.x == 0 && ji.part == 0) set_err(p.err, HC_ERR_RANGE);
     const T* kbase = reinterpret_cast<const T*>(p.k) + ji.b * p.ksb + (int64_t)ji.h * p.ksh;
-    const T* vbase = reinterpret_cast<const T*>(p.v) + ji.b * p.ksb + (int64_t)ji.h * p.ksh;
+    const T* vbase = reinterpret_cast<const T*>(p.v) + ji.b * p.vsb + (int64_t)ji.h * p.vsh;
     T* kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)start * kPage * kD;
     T* vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)start * kPage * kD;
     constexpr int CH = kD * (int)sizeof(T) / 16;  // 16-byte chunks per row
@@ -735,7 +735,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
           for (int e = 0; e < PER; ++e) {
             const int x = lane + 32 * e;
             if (q < nb && rr[q] < kk && x < 2 * CH) {
-              const T* src = (x < CH ? kbase : vbase) + (int64_t)tt[q] * p.kst;
+              const T* src = x < CH ? kbase + (int64_t)tt[q] * p.kst : vbase + (int64_t)tt[q] * p.vst;
               buf[q][e] = ldg128(reinterpret_cast<const uint4*>(src) + (x % CH));
             }
           }

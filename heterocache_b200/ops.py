@@ -48,6 +48,11 @@ def _rows(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"heterocache_b200: {name} must have a contiguous last dim of {HEAD_DIM}")
 
 
+def _same_shape(k: torch.Tensor, v: torch.Tensor) -> None:
+    if k.shape != v.shape or k.dtype != v.dtype:
+        raise ValueError("heterocache_b200: k and v must have the same shape and dtype")
+
+
 def _i32(t: torch.Tensor, name: str) -> None:
     if t.dtype != torch.int32 or not t.is_contiguous():
         raise ValueError(f"heterocache_b200: {name} must be a contiguous int32 tensor")
@@ -73,11 +78,11 @@ def prefill_keep(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err):
     _cuda(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err)
     _rows(k, "k"), _rows(v, "v")
     _i32(keep_heads, "keep_heads"), _i32(block_table, "block_table"), _i32(heads_len, "heads_len")
-    if k.stride() != v.stride():
-        raise ValueError("heterocache_b200: k and v must share strides")
+    _same_shape(k, v)
     bsz, KV, L, D = k.shape
     rc = lib().hc_prefill_keep(dtype_code(k), bsz, KV, L, D, _ptr(keep_heads), keep_heads.numel(),
                                _ptr(k), _ptr(v), k.stride(0), k.stride(1), k.stride(2),
+                               v.stride(0), v.stride(1), v.stride(2),
                                _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table), block_table.shape[1],
                                _ptr(heads_len), _ptr(err), _stream(k))
     check("hc_prefill_keep", rc)
@@ -90,8 +95,7 @@ def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, poo
     _cuda(q, k, v, keep_lens, k_pool, v_pool, block_table, heads_len, err)
     _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
     _i32(keep_lens, "keep_lens"), _i32(block_table, "block_table"), _i32(heads_len, "heads_len")
-    if k.stride() != v.stride():
-        raise ValueError("heterocache_b200: k and v must share strides")
+    _same_shape(k, v)
     bsz, KV, L, D = k.shape
     dt = dtype_code(k)
     nbytes = lib().hc_prefill_select_workspace_size(dt, bsz, n_heads, L, groups, window)
@@ -99,6 +103,7 @@ def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, poo
     rc = lib().hc_prefill_select(dt, bsz, KV, groups, L, D, n_heads, window, POOLING[pooling], kernel_size,
                                  _ptr(q), q.stride(0), q.stride(1), q.stride(2),
                                  _ptr(k), _ptr(v), k.stride(0), k.stride(1), k.stride(2),
+                                 v.stride(0), v.stride(1), v.stride(2),
                                  _ptr(keep_lens), int(max_keep), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
                                  _ptr(block_table), block_table.shape[1], _ptr(heads_len),
                                  _ptr(out_indices), _ptr(out_scores), _ptr(ws), ws.numel(), _ptr(err), _stream(k))
@@ -126,13 +131,12 @@ def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, top
 def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err):
     _cuda(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err)
     _rows(k, "k"), _rows(v, "v")
-    if k.stride() != v.stride():
-        raise ValueError("heterocache_b200: k and v must share strides")
+    _same_shape(k, v)
     bsz, KV, one, D = k.shape
     if one != 1:
         raise ValueError("heterocache_b200: decode append takes one token per row")
     rc = lib().hc_decode_append(dtype_code(k), bsz, KV, D, _ptr(k), _ptr(v), k.stride(0), k.stride(1),
-                                _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
+                                v.stride(0), v.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
                                 block_table.shape[1], _ptr(heads_len), _ptr(free_blocks), free_blocks.numel(),
                                 _ptr(free_ptr),
                                 _ptr(err), _stream(k))

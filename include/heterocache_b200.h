@@ -67,11 +67,13 @@ const char* hc_last_cuda_error(void);
  * Prefill: keep-head copy.  Replaces the prefill branch of HeteroCache.update
  * (heterocache/cache_utils.py:900-937): the volatile and pivot heads are
  * copied whole into their pages and heads_len[row] = L.
- *   k, v: [bsz, KV, L, D] strided (sb, sh, st).  keep_heads: device int32[n_keep].
+ *   k: [bsz, KV, L, D] strided (sb, sh, st); v likewise with (vsb, vsh, vst).
+ *   keep_heads: device int32[n_keep].
  */
 int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_dim,
                     const int32_t* keep_heads, int n_keep,
                     const void* k, const void* v, int64_t sb, int64_t sh, int64_t st,
+                    int64_t vsb, int64_t vsh, int64_t vst,
                     void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table,
                     int max_blocks, int32_t* heads_len, int32_t* err_flag, void* stream);
 
@@ -85,7 +87,8 @@ int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_
  * from flat pool slot block_table[row, 0]*256 on (the prefill pages of a row
  * are contiguous, as the reference lays them out and writes them,
  * cache_utils.py:735-747 and :862-877); heads_len[row] = keep_lens[h].
- *   q: [bsz, H, L, D] strided (qsb, qsh, qst), k/v: [bsz, KV, L, D] strided.
+ *   q: [bsz, H, L, D] strided (qsb, qsh, qst), k: [bsz, KV, L, D] strided
+ *   (sb, sh, st), v: same shape strided (vsb, vsh, vst).
  *   keep_lens: device int32[n_heads].
  *   out_indices (optional, may be NULL): int32 [bsz, n_heads, max_keep],
  *     kept positions ascending, -1 padded.
@@ -97,6 +100,7 @@ int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_
                       int n_heads, int window, int pooling, int kernel_size,
                       const void* q, int64_t qsb, int64_t qsh, int64_t qst,
                       const void* k, const void* v, int64_t sb, int64_t sh, int64_t st,
+                      int64_t vsb, int64_t vsh, int64_t vst,
                       const int32_t* keep_lens, int max_keep,
                       void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table,
                       int max_blocks, int32_t* heads_len, int32_t* out_indices, void* out_scores,
@@ -124,10 +128,10 @@ int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len,
  * slot falls in an unmapped page (-1) take pages from free_blocks in row
  * order starting at *free_ptr (device int32); if the free list would
  * overflow nothing is written and HC_ERR_OOM is OR-ed into err_flag.
- *   k, v: [bsz, KV, 1, D] strided (sb, sh).
+ *   k: [bsz, KV, 1, D] strided (sb, sh); v likewise with (vsb, vsh).
  */
 int hc_decode_append(int dtype, int bsz, int num_kv_heads, int head_dim,
-                     const void* k, const void* v, int64_t sb, int64_t sh,
+                     const void* k, const void* v, int64_t sb, int64_t sh, int64_t vsb, int64_t vsh,
                      void* k_pool, void* v_pool, int n_pool_blocks, int32_t* block_table, int max_blocks,
                      int32_t* heads_len, const int32_t* free_blocks, int n_free, int32_t* free_ptr,
                      int32_t* err_flag, void* stream);

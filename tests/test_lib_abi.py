@@ -53,7 +53,7 @@ def test_argument_validation_needs_no_gpu(built):
                                None, 0, None, None) == 2
     assert lib.hc_flash_decode(1, 1, 8, 4, 64, None, 0, 0, None, None, 1, None, 1, None, 0.0, None, 0,
                                None, 0, None, None) == 1
-    assert lib.hc_prefill_select(1, 1, 8, 4, 100, 128, 5, 200, 0, 5, None, 0, 0, 0, None, None, 0, 0, 0,
+    assert lib.hc_prefill_select(1, 1, 8, 4, 100, 128, 5, 200, 0, 5, None, 0, 0, 0, None, None, 0, 0, 0, 0, 0, 0,
                                  None, 0, None, None, 1, None, 1, None, None, None, None, 0, None, None) == 1
     assert lib.hc_drift_check(1, 8, 4, 128, 9, 1000, 0, 5, 10, 0.5, None, 0, 0, None, 1, None, 4, 1, None,
                               None, None, 1, None, None, None, None, None, None, None, None, 0, None, None) == 8
