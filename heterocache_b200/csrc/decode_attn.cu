@@ -29,12 +29,13 @@ namespace hc {
 
 
 // Padded prefix of row lengths into s_start[0..R]; returns total.
-__device__ __forceinline__ int row_prefix(const FDParams& p, int* s_start, int* s_warp) {
+__device__ __forceinline__ int row_prefix(const FDParams& p, int* s_start, int* s_warp, int* s_len = nullptr) {
   int carry = 0;
   for (int c0 = 0; c0 < p.R; c0 += blockDim.x) {
     int r = c0 + threadIdx.x;
     int len = r < p.R ? p.heads_len[r] : 0;
     len = len < 0 ? 0 : len;
+    if (s_len && r < p.R) s_len[r] = len;
     int l16 = (len + p.gran - 1) / p.gran * p.gran;
     int tot;
     int ex = block_exclusive_scan(l16, s_warp, tot);
@@ -440,6 +441,15 @@ __device__ __forceinline__ void fd_group_tc(const FDParams& p, TcState& st, cons
   }
 }
 
+__host__ __device__ constexpr int fd_round4(int n) { return (n + 3) & ~3; }
+
+// Dynamic shared memory of the TMA kernel: 1024 bytes of alignment slack,
+// the stages, row starts and lengths, and the per-warp partial outputs.
+__host__ __device__ constexpr size_t fd_tma_smem(int R, int G) {
+  return 1024 + (size_t)kTStages * 4 * kTBox + (size_t)(fd_round4(R + 1) + fd_round4(R)) * sizeof(int) +
+         (size_t)kTConsumers * G * kD * sizeof(float);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kTThreads, 2)
     flash_decode_tma_kernel(FDParams p, const __grid_constant__ CUtensorMap tmk,
@@ -451,16 +461,18 @@ __global__ void __launch_bounds__(kTThreads, 2)
   unsigned char* smem_raw = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
   unsigned char* stages = smem_raw;
   int* s_start = reinterpret_cast<int*>(smem_raw + (size_t)kTStages * kStageBytes);
-  float* s_ob = reinterpret_cast<float*>(smem_raw + (size_t)kTStages * kStageBytes +
-                                         (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15));
+  int* s_len = s_start + fd_round4(p.R + 1);
+  float* s_ob = reinterpret_cast<float*>(s_len + fd_round4(p.R));
   auto s_o = [&](int w, int g) { return s_ob + ((size_t)w * p.G + g) * kD; };
   __shared__ __align__(8) uint64_t full_bar[kTStages], empty_bar[kTStages];
+  __shared__ int s_tile_ok[kTStages];  // page id of the stage's tile was valid
   __shared__ int s_warp[32];
   __shared__ float s_m[kTConsumers][kGMax], s_l[kTConsumers][kGMax];
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  const int total = row_prefix(p, s_start, s_warp);
+  pdl_trigger();  // the combine may get resident now; it waits for this grid's results
+  const int total = row_prefix(p, s_start, s_warp, s_len);
   const int span = span_of(total, gridDim.x, kTTile);
   const int beg = blockIdx.x * span;
   if (threadIdx.x == 0) {
@@ -497,11 +509,13 @@ __global__ void __launch_bounds__(kTThreads, 2)
         const int t = tok - s_start[r];
         const int page = t >> 8;
         const int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
-        if (blk < 0 || blk >= p.n_blocks) {  // consumers skip this tile (same check)
+        if (blk < 0 || blk >= p.n_blocks) {  // consumers skip this tile
           set_err(p.err, HC_ERR_RANGE);
-          mbar_arrive(&full_bar[s]);
+          s_tile_ok[s] = 0;
+          mbar_arrive(&full_bar[s]);  // release: orders the flag before the consumers' wait
           continue;
         }
+        s_tile_ok[s] = 1;
         const int y = blk * kPage + (t & (kPage - 1));
         unsigned char* dst = stages + (size_t)s * kStageBytes;
         mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
@@ -590,9 +604,7 @@ __global__ void __launch_bounds__(kTThreads, 2)
     }
     if (!dead) {
       const int t = tok - s_start[r];
-      const int page = t >> 8;
-      const int blk = page < p.max_blocks ? p.bt[(int64_t)r * p.max_blocks + page] : -1;
-      const int valid = (blk < 0 || blk >= p.n_blocks) ? 0 : min(16, p.heads_len[r] - t - 16 * warp);
+      const int valid = s_tile_ok[s] ? min(16, s_len[r] - t - 16 * warp) : 0;
       if (valid > 0) {
         const uint32_t kst = smem_u32(stages + (size_t)s * kStageBytes);
         fd_group_tc<T>(p, st, qa, kst, kst + 2 * kTBox, 16 * warp, valid);
@@ -616,6 +628,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s_start = reinterpret_cast<int*>(smem_raw);
   float* s_w = reinterpret_cast<float*>(smem_raw + (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15));
+  float* s_l2 = s_w + nctas;
   __shared__ int s_warp[32];
   __shared__ float s_red[kCThreads / 32];
   __shared__ float4 s_acc[kCThreads / 32][kD / 4];
@@ -631,9 +644,16 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   }
   const int c0 = rs / span, n = (re - 1) / span - c0 + 1;
   const size_t slot0 = (size_t)(c0 + r);
-  // phase A
+  // the partials are written by the decode kernel launched just before
+  pdl_wait();
+  // phase A: one load round for (m, l); weights kept in s_w (m in s_w first)
   float M = -INFINITY;
-  for (int c = threadIdx.x; c < n; c += kCThreads) M = fmaxf(M, p.part_ml[(slot0 + c) * p.G + g].x);
+  for (int c = threadIdx.x; c < n; c += kCThreads) {
+    const float2 ml = p.part_ml[(slot0 + c) * p.G + g];
+    s_w[c] = ml.x;
+    s_l2[c] = ml.y;
+    M = fmaxf(M, ml.x);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   if (lane == 0) s_red[warp] = M;
@@ -644,10 +664,10 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   __syncthreads();
   float L = 0.f;
   for (int c = threadIdx.x; c < n; c += kCThreads) {
-    const float2 ml = p.part_ml[(slot0 + c) * p.G + g];
-    const float f = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+    const float m = s_w[c];
+    const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
     s_w[c] = f;
-    L += f * ml.y;
+    L += f * s_l2[c];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
@@ -656,16 +676,26 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   L = 0.f;
 #pragma unroll
   for (int w = 0; w < kCThreads / 32; ++w) L += s_red[w];
-  // phase B
+  // phase B: each warp every 8th partial, 8 independent loads in flight
+  constexpr int NW = kCThreads / 32, DEPTH = 8;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-  for (int c = warp; c < n; c += kCThreads / 32) {
-    const float f = s_w[c];
-    const float4 o = *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + 4 * lane);
-    acc.x = fmaf(f, o.x, acc.x);
-    acc.y = fmaf(f, o.y, acc.y);
-    acc.z = fmaf(f, o.z, acc.z);
-    acc.w = fmaf(f, o.w, acc.w);
+  for (int cb = warp; cb < n; cb += NW * DEPTH) {
+    float4 o[DEPTH];
+    float f[DEPTH];
+#pragma unroll
+    for (int u = 0; u < DEPTH; ++u) {
+      const int c = cb + u * NW;
+      f[u] = c < n ? s_w[c] : 0.f;
+      o[u] = c < n ? *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + 4 * lane)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < DEPTH; ++u) {
+      acc.x = fmaf(f[u], o[u].x, acc.x);
+      acc.y = fmaf(f[u], o[u].y, acc.y);
+      acc.z = fmaf(f[u], o[u].z, acc.z);
+      acc.w = fmaf(f[u], o[u].w, acc.w);
+    }
   }
   s_acc[warp][lane] = acc;
   __syncthreads();
@@ -703,9 +733,21 @@ size_t flash_decode_ws_bytes(int R, int G) {
 
 template <typename T>
 static int fd_combine(FDParams& p, int grid, cudaStream_t st) {
-  const size_t csm = (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) + (size_t)grid * sizeof(float);
-  flash_combine_kernel<T><<<p.R * p.G, kCThreads, csm, st>>>(p, grid);
-  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+  // launched as a programmatic dependent of the decode kernel: its CTAs may
+  // start early and wait (griddepcontrol.wait) for the partials
+  const size_t csm = (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) + 2 * (size_t)grid * sizeof(float);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.R * p.G);
+  cfg.blockDim = dim3(kCThreads);
+  cfg.dynamicSmemBytes = csm;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, flash_combine_kernel<T>, p, grid) != cudaSuccess) return HC_ERR_CUDA;
+  return HC_OK;
 }
 
 // fp32 pools: the global-load kernel, rows padded to 16.
@@ -776,8 +818,7 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   const long long rows = (long long)p.n_blocks * kPage;
   if (pool_tensor_map(&tmk, p.kp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
   if (pool_tensor_map(&tmv, p.vp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
-  const size_t dsm = 1024 + (size_t)kTStages * 4 * kTBox + (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) +
-                     (size_t)kTConsumers * p.G * kD * sizeof(float);
+  const size_t dsm = fd_tma_smem(p.R, p.G);
   if (!attr_set) {
     int dev = 0, optin = 0;
     cudaGetDevice(&dev);
@@ -851,8 +892,7 @@ size_t flash_decode_scratch_need(int dtype, int R, int G) {
     int dev = 0, sms = 148, occ = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t dsm = 1024 + (size_t)kTStages * 4 * kTBox + (((size_t)(R + 1) * sizeof(int) + 15) & ~(size_t)15) +
-                       (size_t)kTConsumers * G * kD * sizeof(float);
+    const size_t dsm = fd_tma_smem(R, G);
     const void* kern = dtype == HC_BF16 ? (const void*)flash_decode_tma_kernel<__nv_bfloat16>
                                         : (const void*)flash_decode_tma_kernel<__half>;
     int optin = 0;
