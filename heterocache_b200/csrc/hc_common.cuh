@@ -26,6 +26,7 @@ template <> struct Elem<float> {
   __device__ __forceinline__ static float to_f(float x) { return x; }
   __device__ __forceinline__ static float from_f(float x) { return x; }
   __device__ __forceinline__ static float rnd(float x) { return x; }
+  __device__ __forceinline__ static float pack(float x) { return x; }
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = __float_as_uint(x);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -40,7 +41,19 @@ template <> struct Elem<__nv_bfloat16> {
   static constexpr int kKeyBits = 16;
   __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
-  __device__ __forceinline__ static float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+  // Round to nearest even on the bit pattern: integer-pipe operations only
+  // (the conversion unit is the bottleneck of the scoring phases).  Finite
+  // values and infinities round exactly as the conversion does; a NaN stays
+  // a NaN.
+  __device__ __forceinline__ static float rnd(float x) {
+    const uint32_t b = __float_as_uint(x);
+    const uint32_t r = (b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u;
+    return __uint_as_float((b & 0x7fffffffu) > 0x7f800000u ? (b | 0x00400000u) & 0xffff0000u : r);
+  }
+  // x already holds a bf16 value: keep its upper half
+  __device__ __forceinline__ static __nv_bfloat16 pack(float x) {
+    return __ushort_as_bfloat16((unsigned short)(__float_as_uint(x) >> 16));
+  }
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = __float_as_uint(x) >> 16;  // exact: x is a bf16 value
     return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
@@ -56,6 +69,7 @@ template <> struct Elem<__half> {
   __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
   __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
   __device__ __forceinline__ static float rnd(float x) { return __half2float(__float2half_rn(x)); }
+  __device__ __forceinline__ static __half pack(float x) { return __float2half_rn(x); }  // exact
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = (uint32_t)__half_as_ushort(__float2half_rn(x));  // exact: x is an f16 value
     return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
@@ -95,6 +109,20 @@ template <> __device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// x / y rounded to nearest-even, for a divisor y known in advance with
+// r = 1/y rounded to nearest: Markstein's correction step (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Dev. 34(1), 1990): q = x*r, the exact residual
+// e = x - q*y from one fused multiply-add, then q + e*r.  Branch-free.  It is
+// exact for every fp32 x when y is 3, 5, 7 or 9, and for every bf16 / f16 x
+// divided by sqrt(128) whose quotient is a normal number (so callers send
+// |x| < 2^-120 to IEEE division); the unit tests check both exhaustively.
+__device__ __forceinline__ float div_known(float x, float y, float r) {
+  const float q = x * r;
+  const float e = fmaf(-q, y, x);
+  return fmaf(e, r, q);
 }
 
 __device__ __forceinline__ uint4 ldg128(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
@@ -154,15 +182,16 @@ __device__ __forceinline__ bool grid_sync(GridBarrier* gb, unsigned int nblocks,
   if (threadIdx.x == 0) {
     epoch += 1;
     const unsigned int target = epoch * nblocks;
-    __threadfence();
-    atomicAdd(&gb->count, 1u);
+    // release-add: the CTA's writes (ordered before by the block barrier)
+    // become visible to every CTA that acquires the count
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(&gb->count), "r"(1u) : "memory");
     int ok = 1;
     uint64_t t0 = 0;
     unsigned int spins = 0;
     while (true) {
       if (ld_acquire_u32(&gb->count) >= target) break;
-      if (ld_acquire_u32(&gb->abort)) { ok = 0; break; }
-      if ((++spins & 63u) == 0) {
+      if ((++spins & 31u) == 0) {
+        if (ld_acquire_u32(&gb->abort)) { ok = 0; break; }
         uint64_t now = globaltimer_ns();
         if (t0 == 0) t0 = now;
         else if (now - t0 > kBarrierTimeoutNs) {
@@ -172,7 +201,7 @@ __device__ __forceinline__ bool grid_sync(GridBarrier* gb, unsigned int nblocks,
           break;
         }
       }
-      __nanosleep(40);
+      __nanosleep(20);
     }
     __threadfence();
     s_ok = ok;

@@ -93,6 +93,22 @@ __device__ __forceinline__ bool masked(const ScoreParams& p, int qi, int t) {
   return false;
 }
 
+// Logit in the model dtype: rnd(rnd(q.k) / sqrt(d)), the division correctly
+// rounded.  16-bit models divide by the known divisor with one residual
+// correction (tiny operands, whose quotient would be subnormal, take IEEE
+// division); fp32 models always use IEEE division.
+template <typename T>
+__device__ __forceinline__ float scale_logit(float acc, float y, float r) {
+  const float x = Elem<T>::rnd(acc);
+  if constexpr (std::is_same<T, float>::value) {
+    return __fdiv_rn(x, y);
+  } else {
+    float q = div_known(x, y, r);
+    if (__builtin_expect(fabsf(x) < 0x1p-120f, 0)) q = __fdiv_rn(x, y);
+    return Elem<T>::rnd(q);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Phase 1, tensor-core path (16-bit dtypes, Rq <= 8*NT): a warp computes the
 // logits of 16 tokens x 8*NT query rows per iteration with m16n8k16 MMAs.
@@ -123,6 +139,7 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   float rmax[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) rmax[nt][0] = rmax[nt][1] = -INFINITY;
+  const float r_sqrt = __frcp_rn(p.sqrt_d);
 
   const int lo = max(0, ji.t0 - kMargin);
   const int hi = min(p.L, ji.t1 + kMargin);
@@ -155,9 +172,9 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
         const int qi = nt * 8 + 2 * tig + (e & 1);
         const int t = tg + gid + ((e >> 1) << 3);
         if (qi >= p.Rq || t >= hi) continue;
-        float x = Elem<T>::rnd(Elem<T>::rnd(acc[nt][e]) / p.sqrt_d);
+        float x = scale_logit<T>(acc[nt][e], p.sqrt_d, r_sqrt);
         if (masked(p, qi, t)) x = -INFINITY;
-        lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::from_f(x);
+        lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::pack(x);
         if (t >= ji.t0 && t < ji.t1) rmax[nt][e & 1] = fmaxf(rmax[nt][e & 1], x);
       }
     }
@@ -188,6 +205,7 @@ __device__ void logits_fma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   }
   float rmax[kMaxRq / kSWarps];
   for (int i = 0; i < kMaxRq / kSWarps; ++i) rmax[i] = -INFINITY;
+  const float r_sqrt = __frcp_rn(p.sqrt_d);
   const int lo = max(0, ji.t0 - kMargin);
   const int hi = min(p.L, ji.t1 + kMargin);
   const int base = ji.t0 - kMargin;
@@ -208,9 +226,9 @@ __device__ void logits_fma(const ScoreParams& p, const JobInfo& ji, T* lg, float
 #pragma unroll 8
       for (int d = 0; d < kD; ++d) acc = fmaf(qr[d], kr[d], acc);
       if (t < hi) {
-        float x = Elem<T>::rnd(Elem<T>::rnd(acc) / p.sqrt_d);
+        float x = scale_logit<T>(acc, p.sqrt_d, r_sqrt);
         if (masked(p, qi, t)) x = -INFINITY;
-        lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::from_f(x);
+        lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::pack(x);
         if (t >= ji.t0 && t < ji.t1) rmax[slot] = fmaxf(rmax[slot], x);
       }
     }
@@ -226,77 +244,187 @@ __device__ void logits_fma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   }
 }
 
-// Softmax probability of logit x with row max M and row sum of exp S, in
-// fp32 (the reference's softmax(dtype=float32)).  fp32 models use the
-// accurate exp and an IEEE division; 16-bit models round the result to
-// their dtype right after, so the fast exp (a few ulp of fp32) and the
-// reciprocal are used there.
+// Softmax probability of logit x with row max M, row sum of exp S and its
+// rounded reciprocal R, in fp32 (the reference's softmax(dtype=float32)).
+// fp32 models use the accurate exp and an IEEE division; 16-bit models round
+// the result to their dtype right after, so the fast exp (a few ulp of fp32)
+// and the reciprocal are used there.
 template <typename T>
-__device__ __forceinline__ float softmax_prob(float x, float M, float S) {
-  if constexpr (std::is_same<T, float>::value) return expf(x - M) / S;
-  else return __expf(x - M) * __frcp_rn(S);
+__device__ __forceinline__ float softmax_prob(float x, float M, float S, float R) {
+  if constexpr (std::is_same<T, float>::value) return __fdiv_rn(expf(x - M), S);
+  else return __expf(x - M) * R;
 }
 
-// Phase 2 for W == 1 and pooling half-width HALO <= 3, fused: each thread
-// takes a strip of 8 output tokens of one score row, computes the rounded
-// probabilities of the strip plus halo once per query head, pools each
-// output in the reference's order ((((p0+p1)+p2)+p3)+p4, divided by the
-// kernel size, count_include_pad) and keeps the max over the GQA group.
-template <typename T, int HALO>
-__device__ void pooled_keys_fused(const ScoreParams& p, const JobInfo& ji, const T* lg, unsigned int* keys,
-                                  const float* s_rowM, const float* s_rowS) {
-  constexpr int SW = 8;
-  constexpr int NP = SW + 2 * HALO;
+// exp for the row sums: the same exp the probabilities use
+template <typename T>
+__device__ __forceinline__ float row_exp(float x) {
+  if constexpr (std::is_same<T, float>::value) return expf(x);
+  else return __expf(x);
+}
+
+// Eight consecutive elements (16-byte aligned for 16-bit types, 32-byte for
+// fp32) as fp32.
+template <typename T>
+__device__ __forceinline__ void ld8(const T* src, float* v) {
+  if constexpr (std::is_same<T, float>::value) {
+    const float4 a = reinterpret_cast<const float4*>(src)[0];
+    const float4 b = reinterpret_cast<const float4*>(src)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4*>(src);
+    float2 f;
+    f = unpack2<T>(w.x); v[0] = f.x; v[1] = f.y;
+    f = unpack2<T>(w.y); v[2] = f.x; v[3] = f.y;
+    f = unpack2<T>(w.z); v[4] = f.x; v[5] = f.y;
+    f = unpack2<T>(w.w); v[6] = f.x; v[7] = f.y;
+  }
+}
+
+// Add one to bin `tag` of the shared histogram for every lane whose `valid`
+// is set; lanes with equal tags are combined into one atomic.
+__device__ __forceinline__ void hist_add_warp(unsigned int* h, bool valid, unsigned int tag) {
+  const unsigned int peers = __match_any_sync(0xffffffffu, valid ? tag : 0xffffffffu);
+  if (valid && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&h[tag], __popc(peers));
+}
+
+// Phase 2, pooled scores.  A group of GP lanes (GP = G rounded up to a power
+// of two) takes 8 consecutive tokens of one score row, one query head of the
+// GQA group per lane: the lane reads the 8 tokens and their neighbours (24
+// elements, three 16-byte loads), turns them into rounded probabilities
+// (INLINE: from the logits with the row's max, sum and reciprocal; else they
+// already are), pools them in the reference's order ((((p0+p1)+p2)+p3)+p4,
+// divided by the kernel size, count_include_pad; or max), and the group
+// takes the max over its lanes with butterfly shuffles.  Each lane then
+// keys 8/GP of the tokens into shared memory and into the round-0 radix
+// histogram of their score row.
+template <typename T, int HALO, bool INLINE>
+__device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* lg, unsigned int* keys,
+                             unsigned int* lhist, const float* s_rowM, const float* s_rowS, const float* s_rowR) {
+  constexpr int KB = Elem<T>::kKeyBits;
   constexpr float KS = (float)(2 * HALO + 1);
   const int base = ji.t0 - kMargin;
   const int ntok = ji.t1 - ji.t0;
-  const int nstrip = (ntok + SW - 1) / SW;
-  for (int it = threadIdx.x; it < p.S * nstrip; it += kSThreads) {
-    const int s = it / nstrip;
-    const int t0 = ji.t0 + (it - s * nstrip) * SW;
-    float best[SW];
+  const int nchunk = (ntok + 7) >> 3;
+  const int lgp = p.G <= 1 ? 0 : p.G <= 2 ? 1 : p.G <= 4 ? 2 : 3;
+  const int GP = 1 << lgp;
+  const int items = p.S * nchunk * GP;
+  const bool avg = p.pooling == HC_AVGPOOL;
+  const float pad = avg ? 0.f : -INFINITY;
+  const float rKS = __frcp_rn(KS);
+  // ci / nchunk as a multiply-high, exact while ci * nchunk < 2^32 (ci <
+  // S * nchunk); a slice of one chunk (multiplier 2^32) or a very long slice
+  // divides plainly
+  const bool by_magic = nchunk > 1 && (unsigned long long)p.S * nchunk * nchunk < (1ull << 32);
+  const unsigned int magic = by_magic ? 0xffffffffu / (unsigned int)nchunk + 1u : 0u;
+  for (int i0 = 0; i0 < items; i0 += kSThreads) {
+    const int it = i0 + threadIdx.x;
+    const bool on = it < items;
+    const int gl = it & (GP - 1);
+    const int ci = on ? it >> lgp : 0;
+    const int s = by_magic ? (int)__umulhi((unsigned int)ci, magic) : ci / nchunk;
+    const int c = ji.t0 + 8 * (ci - s * nchunk);
+    float best[8];
 #pragma unroll
-    for (int o = 0; o < SW; ++o) best[o] = -INFINITY;
-    for (int g = 0; g < p.G; ++g) {
-      const int qi = s * p.G + g;
-      const float M = s_rowM[qi], S = s_rowS[qi];
-      const T* row = lg + (int64_t)qi * p.TB - base;
-      float pv[NP];
+    for (int o = 0; o < 8; ++o) best[o] = -INFINITY;
+    if (on && gl < p.G) {
+      const int qi = (s * p.G + gl) * p.W;
+      const T* src = lg + (int64_t)qi * p.TB + (c - base);
+      float w[24];
+      ld8<T>(src - 8, w);
+      ld8<T>(src, w + 8);
+      ld8<T>(src + 8, w + 16);
+      if (INLINE) {
+        const float M = s_rowM[qi], S = s_rowS[qi], R = s_rowR[qi];
 #pragma unroll
-      for (int j = 0; j < NP; ++j) {
-        const int t = t0 - HALO + j;
-        float v = p.pooling == HC_AVGPOOL ? 0.f : -INFINITY;  // padding
-        if (t >= 0 && t < p.L) {
-          const float x = Elem<T>::to_f(row[t]);
-          v = (x == -INFINITY) ? 0.f : Elem<T>::rnd(softmax_prob<T>(x, M, S));
+        for (int i = 8 - HALO; i < 16 + HALO; ++i)
+          w[i] = (w[i] == -INFINITY) ? 0.f : Elem<T>::rnd(softmax_prob<T>(w[i], M, S, R));
+      }
+      if (c - HALO < 0 || c + 8 + HALO > p.L) {
+#pragma unroll
+        for (int i = 8 - HALO; i < 16 + HALO; ++i) {
+          const int t = c - 8 + i;
+          if (t < 0 || t >= p.L) w[i] = pad;
         }
-        pv[j] = v;
       }
 #pragma unroll
-      for (int o = 0; o < SW; ++o) {
+      for (int o = 0; o < 8; ++o) {
+        float v = w[8 + o - HALO];
+        if (avg) {
+#pragma unroll
+          for (int j = 1; j <= 2 * HALO; ++j) v += w[8 + o - HALO + j];
+          if constexpr (std::is_same<T, float>::value) v = __fdiv_rn(v, KS);
+          else v = Elem<T>::rnd(div_known(v, KS, rKS));
+        } else {
+#pragma unroll
+          for (int j = 1; j <= 2 * HALO; ++j) v = fmaxf(v, w[8 + o - HALO + j]);
+        }
+        best[o] = v;
+      }
+    }
+    // max over the group's lanes (groups are aligned within a warp)
+    for (int o = 1; o < GP; o <<= 1) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) best[k] = fmaxf(best[k], __shfl_xor_sync(0xffffffffu, best[k], o));
+    }
+    // lane gl keys tokens gl, gl+GP, ... (8/GP of them)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j * GP >= 8) break;
+      const int o = gl + j * GP;
+      float v = best[0];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) v = (o == k) ? best[k] : v;
+      const bool valid = on && c + o < ji.t1;
+      const unsigned int key = valid ? Elem<T>::key(v) : 0u;
+      if (on) {
+        keys[s * p.T + (c - ji.t0) + o] = key;
+        if (valid && p.out_scores)
+          reinterpret_cast<T*>(p.out_scores)[((size_t)ji.job * p.S + s) * p.L + c + o] = Elem<T>::pack(v);
+      }
+      hist_add_warp(lhist, valid, ((unsigned int)s << 8) | (key >> (KB - 8)));
+    }
+  }
+}
+
+// Phase 2, pooled scores for kernels wider than 7 (probabilities and window
+// sums already in place): one thread per (score row, token).
+template <typename T>
+__device__ void pooled_keys_wide(const ScoreParams& p, const JobInfo& ji, const T* lg, unsigned int* keys,
+                                 unsigned int* lhist) {
+  constexpr int KB = Elem<T>::kKeyBits;
+  const int base = ji.t0 - kMargin;
+  const int ntok = ji.t1 - ji.t0;
+  for (int i0 = 0; i0 < p.S * ntok; i0 += kSThreads) {
+    const int i = i0 + threadIdx.x;
+    const bool on = i < p.S * ntok;
+    const int s = on ? i / ntok : 0, t = ji.t0 + (on ? i % ntok : 0);
+    unsigned int key = 0u;
+    if (on) {
+      float best = -INFINITY;
+      for (int g = 0; g < p.G; ++g) {
+        const T* row = lg + (int64_t)((s * p.G + g) * p.W) * p.TB - base;
         float v;
         if (p.pooling == HC_AVGPOOL) {
-          float acc = pv[o];
-#pragma unroll
-          for (int j = 1; j <= 2 * HALO; ++j) acc += pv[o + j];
-          v = Elem<T>::rnd(acc / KS);
+          float acc = 0.f;
+          for (int j = t - p.halo; j <= t + p.halo; ++j)
+            if (j >= 0 && j < p.L) acc += Elem<T>::to_f(row[j]);
+          v = Elem<T>::rnd(acc / (float)p.ksize);
         } else {
-          v = pv[o];
-#pragma unroll
-          for (int j = 1; j <= 2 * HALO; ++j) v = fmaxf(v, pv[o + j]);
+          v = -INFINITY;
+          for (int j = t - p.halo; j <= t + p.halo; ++j)
+            if (j >= 0 && j < p.L) v = fmaxf(v, Elem<T>::to_f(row[j]));
         }
-        best[o] = fmaxf(best[o], v);
+        best = fmaxf(best, v);
+      }
+      key = Elem<T>::key(best);
+      keys[s * p.T + (t - ji.t0)] = key;
+      if (p.out_scores) {
+        T* os = reinterpret_cast<T*>(p.out_scores);
+        os[((size_t)ji.job * p.S + s) * p.L + t] = Elem<T>::from_f(best);
       }
     }
-#pragma unroll
-    for (int o = 0; o < SW; ++o) {
-      const int t = t0 + o;
-      if (t < ji.t1) {
-        keys[s * p.T + (t - ji.t0)] = Elem<T>::key(best[o]);
-        if (p.out_scores)
-          reinterpret_cast<T*>(p.out_scores)[((size_t)ji.job * p.S + s) * p.L + t] = Elem<T>::from_f(best[o]);
-      }
-    }
+    hist_add_warp(lhist, on, ((unsigned int)s << 8) | (key >> (KB - 8)));
   }
 }
 
@@ -342,11 +470,13 @@ __device__ __forceinline__ int find_bin(const unsigned int* h, unsigned int rem,
 template <typename T>
 __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq];
+  __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq], s_rowR[kMaxRq];
   __shared__ unsigned int s_prefix[kMaxSel], s_mask[kMaxSel], s_rem[kMaxSel], s_k[kMaxSel];
   __shared__ int s_sel_row[kMaxSel];
   __shared__ int2 s_wcnt[kMaxSel][kSWarps];
   __shared__ int s_base[kMaxSel], s_eqoff[kMaxSel];
+  __shared__ int s_wsel[kMaxSel][kSWarps], s_weq[kMaxSel][kSWarps];
+  __shared__ unsigned int s_gtc[kMaxSel];
   __shared__ unsigned int s_ov[kMaxRows];
   __shared__ uint32_t s_refw[kRefWords];
   __shared__ int s_trigger;
@@ -380,6 +510,14 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     for (int i = threadIdx.x; i < kMaxSel * ROUNDS * 256; i += kSThreads) hj[i] = 0u;
     if (p.mode == MODE_DRIFT && threadIdx.x < p.S) p.overlap[ji.job * kMaxRows + threadIdx.x] = 0u;
   }
+  if (p.mode == MODE_DRIFT) {
+    // the reference bitmap is only rewritten after the last grid barrier
+    if (threadIdx.x < kMaxRows) s_ov[threadIdx.x] = 0u;
+    const uint32_t* bm = p.ref_bitmap + (size_t)p.ref_slots[ji.job] * p.bitmap_words;
+    const int wbeg = ji.t0 >> 5, nwords = ((ji.t1 + 31) >> 5) - wbeg;
+    if (nwords <= kRefWords)
+      for (int w = threadIdx.x; w < nwords; w += kSThreads) s_refw[w] = bm[wbeg + w];
+  }
 
   // ---- phase 1: logits
   constexpr bool kTensor = !std::is_same<T, float>::value;
@@ -402,56 +540,90 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     s_rowM[qi] = m;
   }
   __syncthreads();
-  // partial sum of exp over own tokens
+  // partial sum of exp over own tokens (four independent accumulators)
   {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int base = ji.t0 - kMargin;
     for (int qi = warp; qi < p.Rq; qi += kSWarps) {
       const float m = s_rowM[qi];
-      float s = 0.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
       if (m != -INFINITY) {
-        for (int t = ji.t0 + lane; t < ji.t1; t += 32) {
-          float x = Elem<T>::to_f(lg[(int64_t)qi * p.TB + (t - base)]);
-          s += expf(x - m);
+        const T* row = lg + (int64_t)qi * p.TB - base;
+        for (int t = ji.t0 + lane; t < ji.t1; t += 128) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int tu = t + 32 * u;
+            if (tu < ji.t1) s4[u] += row_exp<T>(Elem<T>::to_f(row[tu]) - m);
+          }
         }
       }
+      float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) p.part[((size_t)ji.job * p.cpj + ji.part) * p.Rq + qi] = make_float2(m, s);
+      if (lane == 0) p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(m, s);
     }
   }
   if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
 
   // ---- phase 2: global softmax statistics, probabilities, pooling, keys
   {
-    // one warp per query row, lanes over the job's CTAs
+    // two rows per warp (a half-warp each), lanes over the job's CTAs (a
+    // row's partials are contiguous): each lane issues all its loads (up to
+    // 16 CTAs' partials) before using them, then an online merge of the
+    // (max, sum of exp) pairs
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const float2* pj = p.part + (size_t)ji.job * p.cpj * p.Rq;
-    for (int qi = warp; qi < p.Rq; qi += kSWarps) {
-      float M = -INFINITY;
-      for (int c = lane; c < p.cpj; c += 32) M = fmaxf(M, pj[c * p.Rq + qi].x);
+    const int hl = lane & 15;
+    const float2* pj = p.part + (size_t)ji.job * p.Rq * p.cpj;
+    for (int q0 = 2 * warp; q0 < p.Rq; q0 += 2 * kSWarps) {
+      const int qi = q0 + (lane >> 4);
+      const bool row_ok = qi < p.Rq;
+      float M = -INFINITY, S = 0.f;
+      for (int c0 = 0; c0 < p.cpj; c0 += 256) {
+        float2 v[16];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-      float S = 0.f;
-      for (int c = lane; c < p.cpj; c += 32) {
-        const float2 v = pj[c * p.Rq + qi];
-        if (v.x != -INFINITY) S += v.y * expf(v.x - M);
+        for (int j = 0; j < 16; ++j) {
+          const int c = c0 + hl + 16 * j;
+          v[j] = (row_ok && c < p.cpj) ? __ldcg(&pj[(size_t)qi * p.cpj + c]) : make_float2(-INFINITY, 0.f);
+        }
+        float Mb = M;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) Mb = fmaxf(Mb, v[j].x);
+        if (Mb != -INFINITY) {
+          float acc = M == -INFINITY ? 0.f : S * row_exp<T>(M - Mb);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc += v[j].x == -INFINITY ? 0.f : v[j].y * row_exp<T>(v[j].x - Mb);
+          S = acc;
+          M = Mb;
+        }
       }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-      if (lane == 0) {
+      for (int o = 8; o > 0; o >>= 1) {
+        const float M2 = __shfl_xor_sync(0xffffffffu, M, o);
+        const float S2 = __shfl_xor_sync(0xffffffffu, S, o);
+        const float Mn = fmaxf(M, M2);
+        if (Mn != -INFINITY) {
+          S = (M == -INFINITY ? 0.f : S * row_exp<T>(M - Mn)) + (M2 == -INFINITY ? 0.f : S2 * row_exp<T>(M2 - Mn));
+          M = Mn;
+        }
+      }
+      if (hl == 0 && row_ok) {
         s_rowM[qi] = M;
         s_rowInv[qi] = S;
+        s_rowR[qi] = __frcp_rn(S);
       }
     }
   }
   __syncthreads();
-  const bool fused = p.W == 1 && p.halo >= 1 && p.halo <= 3;
-  if (fused) {
+  // zero the round-0 histograms (one per score row) before the pooling pass
+  for (int i = threadIdx.x; i < kMaxSel * 256; i += kSThreads) lhist[i] = 0u;
+  __syncthreads();
+  if (p.W == 1 && p.halo <= 3) {
+    // probabilities computed inline from the logits
     switch (p.halo) {
-      case 1: pooled_keys_fused<T, 1>(p, ji, lg, keys, s_rowM, s_rowInv); break;
-      case 2: pooled_keys_fused<T, 2>(p, ji, lg, keys, s_rowM, s_rowInv); break;
-      default: pooled_keys_fused<T, 3>(p, ji, lg, keys, s_rowM, s_rowInv); break;
+      case 0: pooled_keys8<T, 0, true>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      case 1: pooled_keys8<T, 1, true>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      case 2: pooled_keys8<T, 2, true>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      default: pooled_keys8<T, 3, true>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
     }
   } else {
     const int base = ji.t0 - kMargin;
@@ -461,7 +633,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
       int qi = i / span, t = lo + i % span;
       T* cell = lg + (int64_t)qi * p.TB + (t - base);
       float x = Elem<T>::to_f(*cell);
-      float pr = (x == -INFINITY) ? 0.f : softmax_prob<T>(x, s_rowM[qi], s_rowInv[qi]);
+      float pr = (x == -INFINITY) ? 0.f : softmax_prob<T>(x, s_rowM[qi], s_rowInv[qi], s_rowR[qi]);
       *cell = Elem<T>::from_f(pr);
     }
     __syncthreads();
@@ -478,31 +650,12 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
       }
       __syncthreads();
     }
-    // pooled, GQA-max keys for own tokens
-    const int ntok = ji.t1 - ji.t0;
-    for (int i = threadIdx.x; i < p.S * ntok; i += kSThreads) {
-      int s = i / ntok, t = ji.t0 + i % ntok;
-      float best = -INFINITY;
-      for (int g = 0; g < p.G; ++g) {
-        const T* row = lg + (int64_t)((s * p.G + g) * p.W) * p.TB - base;
-        float v;
-        if (p.pooling == HC_AVGPOOL) {
-          float acc = 0.f;
-          for (int j = t - p.halo; j <= t + p.halo; ++j)
-            if (j >= 0 && j < p.L) acc += Elem<T>::to_f(row[j]);
-          v = Elem<T>::rnd(acc / (float)p.ksize);
-        } else {
-          v = -INFINITY;
-          for (int j = t - p.halo; j <= t + p.halo; ++j)
-            if (j >= 0 && j < p.L) v = fmaxf(v, Elem<T>::to_f(row[j]));
-        }
-        best = fmaxf(best, v);
-      }
-      keys[s * p.T + (t - ji.t0)] = Elem<T>::key(best);
-      if (p.out_scores) {
-        T* os = reinterpret_cast<T*>(p.out_scores);
-        os[((size_t)ji.job * p.S + s) * p.L + t] = Elem<T>::from_f(best);
-      }
+    switch (p.halo) {
+      case 0: pooled_keys8<T, 0, false>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      case 1: pooled_keys8<T, 1, false>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      case 2: pooled_keys8<T, 2, false>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      case 3: pooled_keys8<T, 3, false>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
+      default: pooled_keys_wide<T>(p, ji, lg, keys, lhist); break;
     }
   }
   // select descriptors
@@ -518,48 +671,140 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     s_prefix[sel] = 0u;
     s_mask[sel] = 0u;
     s_rem[sel] = (unsigned int)max(k, 0);
+    s_gtc[sel] = 0u;
   }
   __syncthreads();
 
-  // ---- phase 3: radix select
+  // ---- phase 3: radix select, 8-bit digits from the top.  The round-0
+  // histograms (per score row) came out of the pooling pass.  In the last
+  // round every CTA also publishes, per select and digit b, how many of its
+  // keys are above and equal to prefix|b, so that after the final barrier
+  // each CTA knows how many tokens the CTAs before it select.
   const int ntok = ji.t1 - ji.t0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int r = 0; r < ROUNDS; ++r) {
     const int shift = KB - 8 * (r + 1);
-    for (int i = threadIdx.x; i < p.nsel * 256; i += kSThreads) lhist[i] = 0u;
-    __syncthreads();
-    for (int sel = 0; sel < p.nsel; ++sel) {
-      const unsigned int k = s_k[sel];
-      if (k == 0u || k >= (unsigned int)p.L) continue;  // trivial selects
-      const unsigned int pre = s_prefix[sel], msk = s_mask[sel];
-      const unsigned int* kr = keys + s_sel_row[sel] * p.T;
-      for (int i = threadIdx.x; i < ntok; i += kSThreads) {
-        unsigned int key = kr[i];
-        if ((key & msk) == pre) atomicAdd(&lhist[sel * 256 + ((key >> shift) & 255u)], 1u);
+    const bool last = r == ROUNDS - 1;
+    if (r == 0) {
+      for (int i = threadIdx.x; i < p.S * 256; i += kSThreads) {
+        const unsigned int c = lhist[i];
+        if (c) atomicAdd(&p.hist[(((size_t)ji.job * kMaxSel + i / 256) * ROUNDS) * 256 + (i % 256)], c);
       }
-    }
-    __syncthreads();
-    unsigned int* gh = p.hist + ((size_t)ji.job * kMaxSel * ROUNDS + r) * 256;
-    for (int i = threadIdx.x; i < p.nsel * 256; i += kSThreads) {
-      unsigned int c = lhist[i];
-      if (c) atomicAdd(&gh[(size_t)(i / 256) * ROUNDS * 256 + (i % 256)], c);
-    }
-    if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
-    {
-      // one warp per select
-      const int warp = threadIdx.x >> 5;
-      for (int sel = warp; sel < p.nsel; sel += kSWarps) {
+    } else {
+      for (int i = threadIdx.x; i < p.nsel * 256; i += kSThreads) lhist[i] = 0u;
+      __syncthreads();
+      for (int sel = 0; sel < p.nsel; ++sel) {
         const unsigned int k = s_k[sel];
-        if (k == 0u || k >= (unsigned int)p.L) continue;
-        unsigned int above;
-        int bin = find_bin(gh + (size_t)sel * ROUNDS * 256, s_rem[sel], above);
-        if ((threadIdx.x & 31) == 0) {
-          s_rem[sel] -= above;
-          s_prefix[sel] |= ((unsigned int)bin) << shift;
-          s_mask[sel] |= 255u << shift;
+        if (k == 0u || k >= (unsigned int)p.L) continue;  // trivial selects
+        const unsigned int pre = s_prefix[sel], msk = s_mask[sel];
+        const unsigned int* kr = keys + s_sel_row[sel] * p.T;
+        unsigned int ngt = 0;
+        for (int c0 = 0; c0 < ntok; c0 += kSThreads) {
+          const int i = c0 + threadIdx.x;
+          const unsigned int key = i < ntok ? kr[i] : 0u;
+          const bool hit = i < ntok && (key & msk) == pre;
+          ngt += __popc(__ballot_sync(0xffffffffu, i < ntok && (key & msk) > pre));
+          // scores crowd into few bins: one atomic per distinct bin per warp
+          const unsigned int act = __ballot_sync(0xffffffffu, hit);
+          if (hit) {
+            const unsigned int bin = (key >> shift) & 255u;
+            const unsigned int peers = __match_any_sync(act, bin);
+            if (lane == __ffs(peers) - 1) atomicAdd(&lhist[sel * 256 + bin], __popc(peers));
+          }
+        }
+        if (last && lane == 0 && ngt) atomicAdd(&s_gtc[sel], ngt);
+      }
+      __syncthreads();
+      unsigned int* gh = p.hist + ((size_t)ji.job * kMaxSel * ROUNDS + r) * 256;
+      for (int i = threadIdx.x; i < p.nsel * 256; i += kSThreads) {
+        const unsigned int c = lhist[i];
+        if (c) atomicAdd(&gh[(size_t)(i / 256) * ROUNDS * 256 + (i % 256)], c);
+      }
+      if (last) {
+        // per digit b: (keys above prefix|b, keys equal to it), one warp per select
+        for (int sel = warp; sel < p.nsel; sel += kSWarps) {
+          const unsigned int k = s_k[sel];
+          if (k == 0u || k >= (unsigned int)p.L) continue;
+          unsigned int c8[8], tot = 0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            c8[i] = lhist[sel * 256 + lane * 8 + i];
+            tot += c8[i];
+          }
+          unsigned int suf = tot;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const unsigned int y = __shfl_down_sync(0xffffffffu, suf, o);
+            if (lane + o < 32) suf += y;
+          }
+          unsigned int run = s_gtc[sel] + (suf - tot);
+          int2* dst = p.cnt + (((size_t)ji.job * kMaxSel + sel) * 256 + lane * 8) * p.cpj + ji.part;
+#pragma unroll
+          for (int i = 7; i >= 0; --i) {
+            dst[(size_t)i * p.cpj] = make_int2((int)run, (int)c8[i]);
+            run += c8[i];
+          }
         }
       }
     }
+    if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+    // stage the job's global histograms of this round (one load round);
+    // round 0 was counted per score row
+    for (int i = threadIdx.x; i < p.nsel * 256; i += kSThreads) {
+      const int sel = i / 256;
+      const int slot = r == 0 ? s_sel_row[sel] : sel;
+      lhist[i] = __ldcg(&p.hist[(((size_t)ji.job * kMaxSel + slot) * ROUNDS + r) * 256 + (i % 256)]);
+    }
     __syncthreads();
+    // one warp per select
+    for (int sel = warp; sel < p.nsel; sel += kSWarps) {
+      const unsigned int k = s_k[sel];
+      if (k == 0u || k >= (unsigned int)p.L) continue;
+      unsigned int above;
+      int bin = find_bin(lhist + sel * 256, s_rem[sel], above);
+      if (lane == 0) {
+        s_rem[sel] -= above;
+        s_prefix[sel] |= ((unsigned int)bin) << shift;
+        s_mask[sel] |= 255u << shift;
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- phase 4: where this CTA's selected tokens start.  For a select with
+  // threshold key thr and `need` keys equal to thr still to take (in position
+  // order), the CTAs before this one select gt_before + min(need, eq_before).
+  for (int sel = warp; sel < p.nsel; sel += kSWarps) {
+    const unsigned int k = s_k[sel];
+    long long gtb = 0, eqb = 0;
+    if (k >= (unsigned int)p.L) {
+      gtb = (long long)ji.part * p.T;  // everything before is selected
+    } else if (k > 0u) {
+      const int b = (int)(s_prefix[sel] & 255u);
+      const int2* cj = p.cnt + (((size_t)ji.job * kMaxSel + sel) * 256 + b) * p.cpj;
+      for (int c0 = 0; c0 < ji.part; c0 += 256) {
+        int2 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = c0 + lane + 32 * j;
+          v[j] = c < ji.part ? __ldcg(&cj[c]) : make_int2(0, 0);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          gtb += v[j].x;
+          eqb += v[j].y;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        gtb += __shfl_xor_sync(0xffffffffu, gtb, o);
+        eqb += __shfl_xor_sync(0xffffffffu, eqb, o);
+      }
+    }
+    if (lane == 0) {
+      s_base[sel] = (int)gtb;
+      s_eqoff[sel] = (int)min(eqb, (long long)0x7fffffff);
+    }
   }
   // thresholds: trivial selects take everything / nothing
   if (threadIdx.x < p.nsel) {
@@ -569,12 +814,9 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     else if (k == 0u) { s_prefix[sel] = 0xffffffffu; s_rem[sel] = 0u; }
   }
   __syncthreads();
-
-  // ---- phase 4: counts of keys above / at each threshold, per warp slice
   // Each warp owns a contiguous, 32-aligned slice of the CTA's tokens, so
   // ranks in position order need no block-wide scans: per 32 tokens one
   // ballot for "above", one for "equal", and popc of the lanes below.
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int TW = ((ntok + kSWarps - 1) / kSWarps + 31) & ~31;
   const int w0 = min(ntok, warp * TW), w1 = min(ntok, w0 + TW);
   const unsigned int lt_mask = (1u << lane) - 1u;
@@ -591,43 +833,17 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     if (lane == 0) s_wcnt[sel][warp] = make_int2(ngt, neq);
   }
   __syncthreads();
-  if (threadIdx.x < p.nsel) {
-    int gt = 0, eq = 0;
-    for (int w = 0; w < kSWarps; ++w) {
-      gt += s_wcnt[threadIdx.x][w].x;
-      eq += s_wcnt[threadIdx.x][w].y;
+  // per-warp starting (selected rank, equal keys seen)
+  if (threadIdx.x < p.nsel * kSWarps) {
+    const int sel = threadIdx.x / kSWarps, w = threadIdx.x % kSWarps;
+    long long gt = s_base[sel], eq = s_eqoff[sel];
+    for (int x = 0; x < w; ++x) {
+      gt += s_wcnt[sel][x].x;
+      eq += s_wcnt[sel][x].y;
     }
-    p.cnt[((size_t)ji.job * kMaxSel + threadIdx.x) * p.cpj + ji.part] = make_int2(gt, eq);
-  }
-  if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
-  // Rank offsets of this CTA: over the job's earlier CTAs c < part, the
-  // selected count is n_gt(c) + clamp(need - eq_before(c), 0, n_eq(c)).
-  // One warp per select, lanes over c with a carried warp scan.
-  for (int sel = warp; sel < p.nsel; sel += kSWarps) {
-    const int2* cj = p.cnt + ((size_t)ji.job * kMaxSel + sel) * p.cpj;
     const long long need = (long long)s_rem[sel];
-    long long carry_eq = 0, base = 0;
-    for (int c0 = 0; c0 < ji.part; c0 += 32) {
-      const int c = c0 + lane;
-      const int2 v = c < ji.part ? cj[c] : make_int2(0, 0);
-      int incl = v.y;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      long long eqsel = need - (carry_eq + incl - v.y);
-      eqsel = eqsel < 0 ? 0 : (eqsel > v.y ? v.y : eqsel);
-      int contrib = v.x + (int)eqsel;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) contrib += __shfl_xor_sync(0xffffffffu, contrib, o);
-      carry_eq += __shfl_sync(0xffffffffu, incl, 31);
-      base += contrib;
-    }
-    if (lane == 0) {
-      s_base[sel] = (int)base;
-      s_eqoff[sel] = (int)min(carry_eq, (long long)0x7fffffff);
-    }
+    s_wsel[sel][w] = (int)(gt + (eq < need ? eq : need));
+    s_weq[sel][w] = (int)min(eq, (long long)0x7fffffff);
   }
   __syncthreads();
 
@@ -638,15 +854,8 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     const unsigned int thr = s_prefix[sel];
     const long long need = (long long)s_rem[sel];
     const unsigned int* kr = keys + s_sel_row[sel] * p.T;
-    long long run_eq = s_eqoff[sel];
-    int run_sel = s_base[sel];
-    for (int w = 0; w < warp; ++w) {  // warps before this one in the CTA
-      const int2 v = s_wcnt[sel][w];
-      long long e = need - run_eq;
-      e = e < 0 ? 0 : (e > v.y ? v.y : e);
-      run_sel += v.x + (int)e;
-      run_eq += v.y;
-    }
+    long long run_eq = s_weq[sel][warp];
+    int run_sel = s_wsel[sel][warp];
     for (int c = w0; c < w1; c += 32) {
       const int i = c + lane;
       const bool in = i < w1;
@@ -667,15 +876,8 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     const unsigned int thr = s_prefix[sel];
     const long long need = (long long)s_rem[sel];
     const unsigned int* kr = keys + s_sel_row[sel] * p.T;
-    long long run_eq = s_eqoff[sel];
-    int run_sel = s_base[sel];
-    for (int w = 0; w < warp; ++w) {
-      const int2 v = s_wcnt[sel][w];
-      long long e = need - run_eq;
-      e = e < 0 ? 0 : (e > v.y ? v.y : e);
-      run_sel += v.x + (int)e;
-      run_eq += v.y;
-    }
+    long long run_eq = s_weq[sel][warp];
+    int run_sel = s_wsel[sel][warp];
     for (int c = w0; c < w1; c += 32) {
       const int i = c + lane;
       const bool in = i < w1;
@@ -770,24 +972,18 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     // drift: overlap of each step's top-k with the reference bitmap
     const int slot = p.ref_slots[ji.job];
     uint32_t* bm = p.ref_bitmap + (size_t)slot * p.bitmap_words;
-    if (threadIdx.x < kMaxRows) s_ov[threadIdx.x] = 0u;
-    // this CTA's words of the reference bitmap, staged in shared memory
+    // this CTA's words of the reference bitmap were staged at kernel start
     const int wbeg = ji.t0 >> 5, nwords = ((ji.t1 + 31) >> 5) - wbeg;
     const bool staged = nwords <= kRefWords;
-    if (staged)
-      for (int w = threadIdx.x; w < nwords; w += kSThreads) s_refw[w] = bm[wbeg + w];
-    __syncthreads();
+    // every selected token counts (a select takes exactly min(k, L) tokens);
+    // 32-token chunks are bitmap words
     for (int sel = 0; sel < p.S; ++sel) {
-      const int kk = (int)s_k[sel];
       unsigned int local = 0;
-      rank_pass(sel, [&](int t, int rank, int) {
-        if (rank >= 0 && rank < kk) {
-          const uint32_t word = staged ? s_refw[(t >> 5) - wbeg] : bm[t >> 5];
-          local += (word >> (t & 31)) & 1u;
-        }
+      rank_walk(sel, [&](int c, unsigned int selm, int) {
+        const int wi = (ji.t0 + c) >> 5;
+        const uint32_t word = staged ? s_refw[wi - wbeg] : bm[wi];
+        local += __popc(selm & word);
       });
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) local += __shfl_xor_sync(0xffffffffu, local, o);
       if (lane == 0 && local) atomicAdd(&s_ov[sel], local);
     }
     // retrieval list: last step's top-max_len, ascending
@@ -802,10 +998,12 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     if (threadIdx.x < p.S && s_ov[threadIdx.x])
       atomicAdd(&p.overlap[ji.job * kMaxRows + threadIdx.x], s_ov[threadIdx.x]);
     if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+    if (threadIdx.x < p.S) s_ov[threadIdx.x] = __ldcg(&p.overlap[ji.job * kMaxRows + threadIdx.x]);
+    __syncthreads();
     if (threadIdx.x == 0) {
       float c[kMaxRows];
       const float kf = (float)p.topk;
-      for (int s = 0; s < p.S; ++s) c[s] = __fdiv_rn((float)p.overlap[ji.job * kMaxRows + s], kf);
+      for (int s = 0; s < p.S; ++s) c[s] = __fdiv_rn((float)s_ov[s], kf);
       float srt[kMaxRows];
       for (int s = 0; s < p.S; ++s) srt[s] = c[s];
       for (int a = 1; a < p.S; ++a)
@@ -906,7 +1104,7 @@ static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq) {
   w.off_gb = take(sizeof(GridBarrier));
   w.off_part = take((size_t)n_jobs * pl.cpj * Rq * sizeof(float2));
   w.off_hist = take((size_t)n_jobs * kMaxSel * 4 * 256 * sizeof(unsigned int));
-  w.off_cnt = take((size_t)n_jobs * kMaxSel * pl.cpj * sizeof(int2));
+  w.off_cnt = take((size_t)n_jobs * kMaxSel * pl.cpj * 256 * sizeof(int2));
   w.off_overlap = take((size_t)n_jobs * kMaxRows * sizeof(unsigned int));
   w.off_logits = take(pl.logits_bytes);
   w.total = o;
