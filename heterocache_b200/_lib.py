@@ -33,8 +33,8 @@ SIGNATURES = {
                               c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "hc_decode_append": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                  c_int64, c_void_p,
-                                 c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
-                                 c_void_p]),
+                                 c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                                 c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p]),
     "hc_flash_decode_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int]),
     "hc_flash_decode": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p,
                                 c_void_p, c_int, c_void_p, c_int, c_void_p, c_float, c_void_p, c_longlong,

@@ -96,7 +96,9 @@ class _HeteroAttention(nn.Module):
                                                  enable_gqa=self.num_key_value_groups > 1)
             out = out.transpose(1, 2).reshape(bsz, q_len, -1).contiguous()
             return self.o_proj(out), None
-        cache.update(k, v, self.layer_idx, {"cache_position": cache_position})
+        # the query rides along so the page-append launch also stores it for
+        # the drift check
+        cache.update(k, v, self.layer_idx, {"cache_position": cache_position, "query_states": q})
         if self.decode_select_before_attention:
             cache.decode_select(q, self.layer_idx)
         out = cache.attention(q, self.layer_idx, scale=self.scaling)  # [bsz, H, D]

@@ -162,6 +162,8 @@ class HeteroCache(_CacheBase):
         self._ref_bitmap: List[Optional[torch.Tensor]] = [None] * n
         self._qbuf: List[Optional[torch.Tensor]] = [None] * n
         self._qcount = [0] * n
+        # the decode append of this step already stored the query (see update)
+        self._q_staged = [False] * n
         self._jobs: List[Optional[_LayerJobs]] = [None] * n
         self._retrieve_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._side_stream: Optional[torch.cuda.Stream] = None
@@ -309,9 +311,19 @@ class HeteroCache(_CacheBase):
 
         self._append_bookkeeping(layer_idx)
         self._wait_retrieval(layer_idx)
+        # A caller that passes the step's query (cache_kwargs["query_states"],
+        # as the attention modules of this package do) has the append launch
+        # store it into the drift-check buffer; decode_select then skips its
+        # own copy.
+        q = (cache_kwargs or {}).get("query_states") if self.bsz == 1 else None
+        q_stage = None
+        if q is not None:
+            self._ensure_decode_state(layer_idx, q)
+            q_stage = self._qbuf[layer_idx][self._qcount[layer_idx]]
         ops.decode_append(key_states, value_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
                           self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
-                          self._free_ptr[layer_idx], self._err)
+                          self._free_ptr[layer_idx], self._err, q=q, q_stage=q_stage)
+        self._q_staged[layer_idx] = q_stage is not None
         return key_states, value_states
 
     def _append_bookkeeping(self, layer_idx: int) -> None:
@@ -430,7 +442,10 @@ class HeteroCache(_CacheBase):
         """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
         S = self.decode_step
         self._ensure_decode_state(layer_idx, query_states)
-        self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
+        if self._q_staged[layer_idx]:
+            self._q_staged[layer_idx] = False
+        else:
+            self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
         self._qcount[layer_idx] += 1
         if self._qcount[layer_idx] < S:
             return

@@ -195,16 +195,24 @@ int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len,
 int hc_decode_append(int dtype, int bsz, int num_kv_heads, int head_dim, const void* k, const void* v, int64_t sb,
                      int64_t sh, int64_t vsb, int64_t vsh, void* k_pool, void* v_pool, int n_pool_blocks,
                      int32_t* block_table, int max_blocks, int32_t* heads_len, const int32_t* free_blocks, int n_free,
-                     int32_t* free_ptr, int32_t* err_flag, void* stream) {
+                     int32_t* free_ptr, const void* q, int64_t qsh, int n_q_heads, void* q_stage, int32_t* err_flag,
+                     void* stream) {
   if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
   if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || max_blocks <= 0 || n_free < 0)
     return HC_ERR_INVALID;
   if (!aligned16(k) || !aligned16(v) || !aligned16(k_pool) || !aligned16(v_pool)) return HC_ERR_INVALID;
   if (!stride_ok(dtype, sb) || !stride_ok(dtype, sh) || !stride_ok(dtype, vsb) || !stride_ok(dtype, vsh))
     return HC_ERR_INVALID;
+  if (q_stage) {
+    if (bsz != 1 || !q || n_q_heads <= 0 || !aligned16(q) || !aligned16(q_stage) || !stride_ok(dtype, qsh))
+      return HC_ERR_INVALID;
+  } else {
+    n_q_heads = 0;
+  }
   return note_cuda(hc::decode_append_dispatch(dtype, bsz * num_kv_heads, num_kv_heads, k, v, sb, sh, vsb, vsh, k_pool,
                                               v_pool, n_pool_blocks, block_table, max_blocks, heads_len, free_blocks,
-                                              n_free, free_ptr, err_flag, (cudaStream_t)stream));
+                                              n_free, free_ptr, q, qsh, n_q_heads, q_stage, err_flag,
+                                              (cudaStream_t)stream));
 }
 
 size_t hc_flash_decode_workspace_size(int bsz, int num_kv_heads, int groups, int head_dim) {

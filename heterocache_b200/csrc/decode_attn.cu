@@ -22,6 +22,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <utility>
+
 #include "hc_params.cuh"
 
 namespace hc {
@@ -210,6 +212,8 @@ __global__ void __launch_bounds__(kFThreads) flash_decode_kernel(FDParams p) {
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
+  pdl_wait();  // as in the TMA kernel
+  pdl_trigger();
   const int total = row_prefix(p, s_start, s_warp);
   const int span = span_of(total, gridDim.x, p.gran);
   const int beg = blockIdx.x * span;
@@ -471,7 +475,11 @@ __global__ void __launch_bounds__(kTThreads, 2)
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  pdl_trigger();  // the combine may get resident now; it waits for this grid's results
+  // programmatic dependent launch: wait for the kernel before (the page
+  // append) to finish, then let the combine get resident; it reads row
+  // lengths before its own wait and waits for this grid's partials
+  pdl_wait();
+  pdl_trigger();
   const int total = row_prefix(p, s_start, s_warp, s_len);
   const int span = span_of(total, gridDim.x, kTTile);
   const int beg = blockIdx.x * span;
@@ -646,6 +654,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   const size_t slot0 = (size_t)(c0 + r);
   // the partials are written by the decode kernel launched just before
   pdl_wait();
+  pdl_trigger();  // the next kernel may get resident; it waits for this grid
   // phase A: one load round for (m, l); weights kept in s_w (m in s_w first)
   float M = -INFINITY;
   for (int c = threadIdx.x; c < n; c += kCThreads) {
@@ -750,6 +759,25 @@ static int fd_combine(FDParams& p, int grid, cudaStream_t st) {
   return HC_OK;
 }
 
+// Launch with programmatic stream serialization: the grid may start while the
+// previous kernel in the stream drains; every kernel launched this way
+// executes griddepcontrol.wait before it reads anything.
+template <typename... KArgs, typename... Args>
+static cudaError_t pdl_launch(void (*kern)(KArgs...), int grid, int threads, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // fp32 pools: the global-load kernel, rows padded to 16.
 static int fd_launch_f32(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
   const int grid = fd_grid(HC_F32);
@@ -758,8 +786,8 @@ static int fd_launch_f32(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
   p.gran = 16;
-  flash_decode_kernel<float><<<grid, kFThreads, (size_t)(p.R + 1) * sizeof(int), st>>>(p);
-  if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
+  if (pdl_launch(flash_decode_kernel<float>, grid, kFThreads, (size_t)(p.R + 1) * sizeof(int), st, p) != cudaSuccess)
+    return HC_ERR_CUDA;
   return fd_combine<float>(p, grid, st);
 }
 
@@ -851,8 +879,7 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float2*>(reinterpret_cast<unsigned char*>(ws) + slots * p.G * kD * sizeof(float));
   p.gran = kTTile;
-  kern<<<grid, kTThreads, dsm, st>>>(p, tmk, tmv);
-  if (cudaGetLastError() != cudaSuccess) return HC_ERR_CUDA;
+  if (pdl_launch(kern, grid, kTThreads, dsm, st, p, tmk, tmv) != cudaSuccess) return HC_ERR_CUDA;
   return fd_combine<T>(p, grid, st);
 }
 

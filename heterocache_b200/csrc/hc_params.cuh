@@ -102,7 +102,8 @@ int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep
                           cudaStream_t s);
 int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh,
                            int64_t vsb, int64_t vsh, void* kp, void* vp, int nblocks, int32_t* bt, int mb, int32_t* hl,
-                           const int32_t* fb, int nf, int32_t* fp, int32_t* err, cudaStream_t s);
+                           const int32_t* fb, int nf, int32_t* fp, const void* q, int64_t qsh, int nq, void* q_stage,
+                           int32_t* err, cudaStream_t s);
 int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,
                       const int32_t* trig, const int32_t* pos, int pos_stride, const void* fk, const void* fv,
                       int64_t fsh, int64_t fst, void* kp, void* vp, int nblocks, const int32_t* bt, int mb,

@@ -42,16 +42,89 @@ __global__ void __launch_bounds__(256) prefill_keep_kernel(const T* __restrict__
 // ---------------------------------------------------------------------------
 // Decode append.  One CTA; rows that need a page take one from the free list
 // in row order (the reference assigns free_blocks[ptr:ptr+n] to the rows of
-// the boolean mask in order).
+// the boolean mask in order).  Launched as a programmatic dependent: it waits
+// for the previous kernel's results, then lets the attention kernel after it
+// get resident.  With q_stage set it also stores the step's query rows.
+constexpr int kAppendThreads = 256;
+
 template <typename T>
-__global__ void __launch_bounds__(256) decode_append_kernel(const T* __restrict__ k, const T* __restrict__ v,
-                                                            int64_t sb, int64_t sh, int64_t vsb, int64_t vsh, int R,
-                                                            int KV, T* k_pool,
-                                                            T* v_pool, int n_blocks, int32_t* bt, int max_blocks,
-                                                            int32_t* heads_len, const int32_t* __restrict__ free_blocks,
-                                                            int n_free, int32_t* free_ptr, int32_t* err) {
+__device__ __forceinline__ void append_row_copies(const T* k, const T* v, int64_t sb, int64_t sh, int64_t vsb,
+                                                  int64_t vsh, int KV, T* k_pool, T* v_pool, int R,
+                                                  const int* s_phys, const int* s_off) {
+  constexpr int CH = kD * sizeof(T) / 16;
+  for (int i = threadIdx.x; i < R * 2 * CH; i += kAppendThreads) {
+    const int r = i / (2 * CH), x = i % (2 * CH);
+    const int phys = s_phys[r];
+    if (phys < 0) continue;
+    const int b = r / KV, h = r % KV, c = x % CH;
+    const int64_t dst = ((int64_t)phys * kPage + s_off[r]) * kD;
+    if (x < CH)
+      reinterpret_cast<uint4*>(k_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(k + b * sb + (int64_t)h * sh) + c);
+    else
+      reinterpret_cast<uint4*>(v_pool + dst)[c] = ldg128(reinterpret_cast<const uint4*>(v + b * vsb + (int64_t)h * vsh) + c);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kAppendThreads) decode_append_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, int64_t sb, int64_t sh, int64_t vsb, int64_t vsh, int R, int KV,
+    T* k_pool, T* v_pool, int n_blocks, int32_t* bt, int max_blocks, int32_t* heads_len,
+    const int32_t* __restrict__ free_blocks, int n_free, int32_t* free_ptr, const T* __restrict__ q, int64_t qsh,
+    int nq, T* q_stage, int32_t* err) {
+  constexpr int CH = kD * sizeof(T) / 16;
   __shared__ int s_warp[32];
   __shared__ int s_total, s_fail;
+  __shared__ int s_phys[32], s_off[32];
+  pdl_wait();
+  pdl_trigger();
+  // the step's query rows for the drift check (independent of the page work)
+  for (int i = threadIdx.x; i < nq * CH; i += kAppendThreads)
+    reinterpret_cast<uint4*>(q_stage)[i] = ldg128(reinterpret_cast<const uint4*>(q + (int64_t)(i / CH) * qsh) + i % CH);
+  if (R <= 32) {
+    // one warp does the bookkeeping: ballots replace the block scans
+    if (threadIdx.x < 32) {
+      const int r = threadIdx.x;
+      const int base_ptr = *free_ptr;
+      int len = 0, blk = 0, phys = -1, need = 0, fail = 0;
+      if (r < R) {
+        len = heads_len[r];
+        blk = len >> 8;
+        if (len < 0 || blk >= max_blocks) {
+          fail = HC_ERR_RANGE;
+        } else {
+          phys = bt[(int64_t)r * max_blocks + blk];
+          need = phys == -1;
+          if (phys < -1 || phys >= n_blocks) fail = HC_ERR_RANGE;
+        }
+      }
+      const unsigned int needm = __ballot_sync(0xffffffffu, need);
+      const int total = __popc(needm);
+      int f = __ballot_sync(0xffffffffu, fail != 0) ? HC_ERR_RANGE : 0;
+      if (!f && (base_ptr < 0 || base_ptr + total > n_free)) f = HC_ERR_OOM;
+      bool ok = r < R && !f;
+      if (ok && need) {
+        phys = free_blocks[base_ptr + __popc(needm & ((1u << r) - 1u))];
+        if (phys < 0 || phys >= n_blocks) {  // corrupt free list: leave the row untouched
+          set_err(err, HC_ERR_RANGE);
+          ok = false;
+        } else {
+          bt[(int64_t)r * max_blocks + blk] = phys;
+        }
+      }
+      if (ok) heads_len[r] = len + 1;
+      s_phys[r] = ok ? phys : -1;
+      s_off[r] = len & (kPage - 1);
+      if (r == 0) {
+        s_fail = f;
+        if (f) set_err(err, f);
+        else *free_ptr = base_ptr + total;
+      }
+    }
+    __syncthreads();
+    if (s_fail) return;
+    append_row_copies<T>(k, v, sb, sh, vsb, vsh, KV, k_pool, v_pool, R, s_phys, s_off);
+    return;
+  }
   const int base_ptr = *free_ptr;
   int carry = 0;
   if (threadIdx.x == 0) s_fail = 0;
@@ -114,7 +187,6 @@ __global__ void __launch_bounds__(256) decode_append_kernel(const T* __restrict_
       const int64_t dst = ((int64_t)phys * kPage + (len & (kPage - 1))) * kD;
       uint4* kd = reinterpret_cast<uint4*>(k_pool + dst);
       uint4* vd = reinterpret_cast<uint4*>(v_pool + dst);
-      constexpr int CH = kD * sizeof(T) / 16;
 #pragma unroll 4
       for (int c = 0; c < CH; ++c) {
         kd[c] = ks[c];
@@ -198,20 +270,38 @@ int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep
 template <typename T>
 static int append_t(int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh, int64_t vsb, int64_t vsh,
                     void* kp, void* vp, int nb, int32_t* bt, int mb, int32_t* hl, const int32_t* fb, int nf,
-                    int32_t* fp, int32_t* err, cudaStream_t s) {
-  decode_append_kernel<T><<<1, 256, 0, s>>>((const T*)k, (const T*)v, sb, sh, vsb, vsh, R, KV, (T*)kp, (T*)vp, nb,
-                                            bt, mb, hl, fb, nf, fp, err);
-  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+                    int32_t* fp, const void* q, int64_t qsh, int nq, void* q_stage, int32_t* err, cudaStream_t s) {
+  // programmatic dependent launch: the kernel starts while the previous one
+  // drains and waits (griddepcontrol.wait) before touching any data
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kAppendThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, decode_append_kernel<T>, (const T*)k, (const T*)v, sb, sh, vsb, vsh, R,
+                                           KV, (T*)kp, (T*)vp, nb, bt, mb, hl, fb, nf, fp, (const T*)q, qsh, nq,
+                                           (T*)q_stage, err);
+  return e == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
 int decode_append_dispatch(int dtype, int R, int KV, const void* k, const void* v, int64_t sb, int64_t sh,
                            int64_t vsb, int64_t vsh, void* kp, void* vp, int nb, int32_t* bt, int mb, int32_t* hl,
-                           const int32_t* fb, int nf, int32_t* fp, int32_t* err, cudaStream_t s) {
+                           const int32_t* fb, int nf, int32_t* fp, const void* q, int64_t qsh, int nq, void* q_stage,
+                           int32_t* err, cudaStream_t s) {
   switch (dtype) {
-    case HC_F32: return append_t<float>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+    case HC_F32:
+      return append_t<float>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, q, qsh, nq, q_stage, err,
+                             s);
     case HC_BF16:
-      return append_t<__nv_bfloat16>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
-    case HC_F16: return append_t<__half>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, err, s);
+      return append_t<__nv_bfloat16>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, q, qsh, nq,
+                                     q_stage, err, s);
+    case HC_F16:
+      return append_t<__half>(R, KV, k, v, sb, sh, vsb, vsh, kp, vp, nb, bt, mb, hl, fb, nf, fp, q, qsh, nq, q_stage,
+                              err, s);
     default: return HC_ERR_DTYPE;
   }
 }

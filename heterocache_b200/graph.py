@@ -65,7 +65,7 @@ class DecodeStepGraph:
     def _eager_step(self) -> None:
         c = self.cache
         for i, l in enumerate(self.layers):
-            c.update(self.k[i], self.v[i], l)
+            c.update(self.k[i], self.v[i], l, {"query_states": self.q[i]})
             if self.order == "qwen":
                 c.decode_select(self.q[i], l)
             c.attention(self.q[i], l, out=self.out[i])

@@ -128,17 +128,27 @@ def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, top
     LAUNCHES[0] += 1
 
 
-def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err):
-    _cuda(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err)
+def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err, q=None, q_stage=None):
+    """Append one token per row; with ``q`` [1, H, 1, D] and ``q_stage`` [H, D]
+    the same launch stores the step's query for the drift check."""
+    _cuda(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err, q, q_stage)
     _rows(k, "k"), _rows(v, "v")
     _same_shape(k, v)
     bsz, KV, one, D = k.shape
     if one != 1:
         raise ValueError("heterocache_b200: decode append takes one token per row")
+    nq, qsh = 0, 0
+    if q_stage is not None:
+        _rows(q, "q")
+        if q.shape[0] != 1 or q.shape[2] != 1 or q.dtype != k.dtype:
+            raise ValueError("heterocache_b200: the staged query must be [1, H, 1, D] in the cache dtype")
+        if not q_stage.is_contiguous() or tuple(q_stage.shape) != (q.shape[1], D):
+            raise ValueError("heterocache_b200: q_stage must be a contiguous [H, D] tensor")
+        nq, qsh = q.shape[1], q.stride(1)
     rc = lib().hc_decode_append(dtype_code(k), bsz, KV, D, _ptr(k), _ptr(v), k.stride(0), k.stride(1),
                                 v.stride(0), v.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
                                 block_table.shape[1], _ptr(heads_len), _ptr(free_blocks), free_blocks.numel(),
-                                _ptr(free_ptr),
+                                _ptr(free_ptr), _ptr(q if q_stage is not None else None), qsh, nq, _ptr(q_stage),
                                 _ptr(err), _stream(k))
     check("hc_decode_append", rc)
     LAUNCHES[0] += 1

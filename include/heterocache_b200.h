@@ -129,11 +129,18 @@ int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len,
  * order starting at *free_ptr (device int32); if the free list would
  * overflow nothing is written and HC_ERR_OOM is OR-ed into err_flag.
  *   k: [bsz, KV, 1, D] strided (sb, sh); v likewise with (vsb, vsh).
+ * Optionally (q_stage non-null, bsz == 1) the same launch also stores the
+ * step's query q [1, n_q_heads, 1, D] (head stride qsh) into q_stage
+ * [n_q_heads, D]: the slot of the per-step query buffer that decode_select
+ * keeps for the drift check (heterocache/cache_utils.py:1011-1017 appends
+ * each decode query and concatenates decode_step of them), so that store
+ * costs no launch of its own.
  */
 int hc_decode_append(int dtype, int bsz, int num_kv_heads, int head_dim,
                      const void* k, const void* v, int64_t sb, int64_t sh, int64_t vsb, int64_t vsh,
                      void* k_pool, void* v_pool, int n_pool_blocks, int32_t* block_table, int max_blocks,
                      int32_t* heads_len, const int32_t* free_blocks, int n_free, int32_t* free_ptr,
+                     const void* q, int64_t qsh, int n_q_heads, void* q_stage,
                      int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------

@@ -172,24 +172,28 @@ def test_flash_decode_strided_query(cuda_device):
     assert (out.float().cpu() - ref).abs().max().item() <= 2e-2
 
 
-def test_decode_append_allocates_in_row_order(cuda_device):
+@pytest.mark.parametrize("bsz", [1, 5])
+def test_decode_append_allocates_in_row_order(cuda_device, bsz):
+    """Up to 32 rows take the one-warp bookkeeping path, more the block-scan path."""
     dev = cuda_device
     KV, D = 8, 128
-    # rows 1,3,5 sit at a page boundary with the next page unmapped
-    lens = [10, 256, 300, 512, 0, 256, 7, 100]
+    # rows 1,3,5 (of each batch entry) sit at a page boundary with the next page unmapped
+    lens = [10, 256, 300, 512, 0, 256, 7, 100] * bsz
+    R = KV * bsz
     max_blocks = 4
-    bt = torch.full((KV, max_blocks), -1, dtype=torch.int32)
+    bt = torch.full((R, max_blocks), -1, dtype=torch.int32)
     ptr = 0
     for r, l in enumerate(lens):
         n = max(1, (l + 255) // 256) if l % 256 else l // 256
         bt[r, :n] = torch.arange(ptr, ptr + n, dtype=torch.int32)
         ptr += n
-    free = torch.arange(ptr, ptr + 6, dtype=torch.int32)
-    nb = ptr + 6
+    n_free = 6 * bsz
+    free = torch.arange(ptr, ptr + n_free, dtype=torch.int32)
+    nb = ptr + n_free
     kp = torch.zeros(nb, 256, 1, D, dtype=torch.bfloat16, device=dev)
     vp = torch.zeros_like(kp)
-    k = torch.randn(1, KV, 1, D).to(torch.bfloat16)
-    v = torch.randn(1, KV, 1, D).to(torch.bfloat16)
+    k = torch.randn(bsz, KV, 1, D).to(torch.bfloat16)
+    v = torch.randn(bsz, KV, 1, D).to(torch.bfloat16)
     btd, hld = bt.to(dev), torch.tensor(lens, dtype=torch.int32, device=dev)
     fp = torch.zeros(1, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -205,17 +209,41 @@ def test_decode_append_allocates_in_row_order(cuda_device):
     assert int(fp.item()) == len(need)
     for r, l in enumerate(lens):
         slot = int(exp_bt[r, l // 256]) * 256 + l % 256
-        assert torch.equal(kp.cpu().view(-1, D)[slot], k[0, r, 0])
-        assert torch.equal(vp.cpu().view(-1, D)[slot], v[0, r, 0])
+        assert torch.equal(kp.cpu().view(-1, D)[slot], k[r // KV, r % KV, 0])
+        assert torch.equal(vp.cpu().view(-1, D)[slot], v[r // KV, r % KV, 0])
     # exhaust the free list: nothing changes, OOM flag set
-    fp.fill_(6)
+    fp.fill_(n_free)
     before = (btd.clone(), hld.clone())
-    hld.copy_(torch.tensor([256 * 2] * KV, dtype=torch.int32))
+    hld.copy_(torch.tensor([256 * 2] * R, dtype=torch.int32))
     ops.decode_append(k.to(dev), v.to(dev), kp, vp, btd, hld, free.to(dev), fp, err)
     torch.cuda.synchronize()
     assert int(err.item()) & (1 << 3)
-    assert hld.cpu().tolist() == [512] * KV
+    assert hld.cpu().tolist() == [512] * R
     assert torch.equal(btd, before[0])
+
+
+def test_decode_append_stages_the_query(cuda_device):
+    """With q / q_stage the append launch also stores the step's query rows."""
+    dev = cuda_device
+    KV, H, D = 8, 32, 128
+    bt = torch.arange(KV, dtype=torch.int32, device=dev).view(KV, 1)
+    kp = torch.zeros(KV, 256, 1, D, dtype=torch.bfloat16, device=dev)
+    vp = torch.zeros_like(kp)
+    hl = torch.full((KV,), 3, dtype=torch.int32, device=dev)
+    fp = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    k = torch.randn(1, KV, 1, D, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, KV, 1, D, device=dev).to(torch.bfloat16)
+    # a transposed view, as the attention modules hand it over: head stride D
+    q = torch.randn(1, 1, H, D, device=dev).to(torch.bfloat16).transpose(1, 2)
+    qbuf = torch.zeros(5, H, D, dtype=torch.bfloat16, device=dev)
+    ops.decode_append(k, v, kp, vp, bt, hl, torch.zeros(1, dtype=torch.int32, device=dev), fp, err,
+                      q=q, q_stage=qbuf[2])
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(qbuf[2], q[0, :, 0, :])
+    assert not qbuf[[0, 1, 3, 4]].any()
+    assert torch.equal(kp[:, 3, 0], k[0, :, 0]) and hl.tolist() == [4] * KV
 
 
 @pytest.mark.parametrize("dtype,geo,L", [("bfloat16", LLAMA_8B, 8192), ("bfloat16", QWEN_7B, 3000),
