@@ -14,7 +14,7 @@ device run and a CPU check see identical bits.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -36,17 +36,23 @@ QWEN_7B = LayerGeometry(28, 4, 128)
 
 def prefill_inputs(geo: LayerGeometry, seq_len: int, *, bsz: int = 1, seed: int = 0,
                    window: int = 32, planted_frac: float = 0.01, planted_scale: float = 4.0,
-                   dtype: torch.dtype = torch.float32) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+                   dtype: torch.dtype = torch.float32,
+                   q_positions: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Seeded q/k/v [bsz, heads, seq_len, D] with planted heavy hitters.  With
+    ``q_positions`` only the last that many query positions are generated
+    (q is [bsz, H, q_positions, D]): the path reads the window queries only,
+    which keeps long-context inputs small."""
     g = torch.Generator("cpu").manual_seed(seed)
     H, KV, D, G = geo.num_heads, geo.num_kv_heads, geo.head_dim, geo.groups
-    q = torch.randn(bsz, H, seq_len, D, generator=g)
+    qn = seq_len if q_positions is None else min(q_positions, seq_len)
+    q = torch.randn(bsz, H, qn, D, generator=g)
     k = torch.randn(bsz, KV, seq_len, D, generator=g)
     v = torch.randn(bsz, KV, seq_len, D, generator=g)
     n_plant = max(1, int(round(planted_frac * seq_len)))
-    w = min(window, seq_len)
+    w = min(window, qn)
     for b in range(bsz):
         for h in range(KV):
-            mean_q = q[b, h * G:(h + 1) * G, seq_len - w:, :].mean(dim=(0, 1))
+            mean_q = q[b, h * G:(h + 1) * G, qn - w:, :].mean(dim=(0, 1))
             direction = mean_q / mean_q.norm().clamp_min(1e-12)
             pos = torch.randperm(seq_len, generator=g)[:n_plant]
             k[b, h, pos, :] += planted_scale * direction

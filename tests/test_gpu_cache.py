@@ -72,12 +72,26 @@ def _check_prefill(gpu, orc, sc, layer_inputs, dtype):
 
 def _run(name, real_offload=False):
     sc = SCENARIOS[name]
-    gpu, orc = _gpu_cache(sc, real_offload)
     geo, tdt, layer_inputs = scenario_inputs(sc)
+    run_lockstep(sc, geo, tdt, layer_inputs, real_offload)
+
+
+def _device_query(q, L, dev):
+    """The device query tensor [bsz, H, L, D]: zeros except the generated last
+    positions (the path reads only the window queries at the end)."""
+    if q.shape[2] == L:
+        return q.to(dev)
+    qd = torch.zeros(q.shape[0], q.shape[1], L, q.shape[3], dtype=q.dtype, device=dev)
+    qd[:, :, L - q.shape[2]:] = q.to(dev)
+    return qd
+
+
+def run_lockstep(sc, geo, tdt, layer_inputs, real_offload=False):
+    gpu, orc = _gpu_cache(sc, real_offload)
     dtype = sc["dtype"]
     dev = torch.device("cuda", 0)
     for layer, (q, k, v) in enumerate(layer_inputs):
-        qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+        qd, kd, vd = _device_query(q, k.shape[2], dev), k.to(dev), v.to(dev)
         gpu.update(kd, vd, layer)
         gpu.init_coefficient(qd, kd, layer)
         gpu.prefill_select(qd, kd, vd, layer)
@@ -162,3 +176,16 @@ def test_cache_lockstep_with_oracle(cuda_device, name):
 def test_cache_host_tier(cuda_device):
     """Full tier in pinned host memory, retrieval on a side stream."""
     _run("llama_bf16_avg5", real_offload=True)
+
+
+def test_config3_qwen_224k_host_tier(cuda_device):
+    """Config 3 at its full context: Qwen2.5-7B layer geometry (28 query / 4 KV
+    heads, G = 7), 229376 tokens, bf16, full tier in pinned host memory, in
+    lockstep with the oracle through prefill and 10 decode steps (two drift
+    checks; the threshold makes every check retrieve satellites from the host
+    tier)."""
+    from heterocache_b200.synthetic import QWEN_7B, prefill_inputs
+    sc = dict(geo=(28, 4, 128), L=229376, dtype="bfloat16", pooling="avgpool", k=5, thr=0.999, steps=5,
+              n_decode=10, gen=16, role_seed=21, seed=31, layers=1)
+    inputs = [prefill_inputs(QWEN_7B, sc["L"], seed=sc["seed"] * 100, dtype=torch.bfloat16, q_positions=32)]
+    run_lockstep(sc, QWEN_7B, torch.bfloat16, inputs, real_offload=True)
