@@ -18,6 +18,11 @@ output read back.
 
 --impl reference times the oracle restatement of the reference's own path
 (PyTorch on the host CPU) on the same workload, one sampled layer per step.
+
+--model qwen --host-tier runs the config-3 workload instead: Qwen2.5-7B
+attention geometry (28 layers, 28 query / 4 KV heads), 229376-token context,
+the full KV tier in pinned host memory (retrieval reads it over the host
+link), and Qwen's order (decode_select before attention).
 """
 from __future__ import annotations
 
@@ -38,6 +43,7 @@ import torch  # noqa: E402
 
 METRIC = "decode µs/layer & tokens/s at 128K ctx; HBM GB/s vs roofline, 1/2/4/8 B200"
 LAYERS, H, KV, D = 32, 32, 8, 128
+GEO = None  # the layer geometry (set by parse: Llama-3.1-8B unless --model qwen)
 STEPS_PER_CHECK = 5
 
 
@@ -47,17 +53,30 @@ def parse():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ctx", type=int, default=131072)
-    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--ctx", type=int, default=None, help="context (default 131072; 229376 with --model qwen)")
+    ap.add_argument("--layers", type=int, default=None, help="layers (default 32; 28 with --model qwen)")
+    ap.add_argument("--model", default="llama", choices=["llama", "qwen"])
+    ap.add_argument("--host-tier", action="store_true", help="full KV tier in pinned host memory")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    return ap.parse_args()
+    args = ap.parse_args()
+    global H, KV, GEO
+    if args.model == "qwen":
+        from heterocache_b200.synthetic import QWEN_7B
+        H, KV, GEO = 28, 4, QWEN_7B
+        args.ctx = args.ctx or 229376
+        args.layers = args.layers or 28
+    args.ctx = args.ctx or 131072
+    args.layers = args.layers or LAYERS
+    return args
 
 
 def config_dict(args, n):
-    return {"workload": f"llama-3.1-8b compressed-KV attention path, {args.layers} layers, decode at "
+    name = "qwen2.5-7b" if args.model == "qwen" else "llama-3.1-8b"
+    tier = ", full KV tier in pinned host memory" if args.host_tier else ""
+    return {"workload": f"{name} compressed-KV attention path, {args.layers} layers, decode at "
                         f"{args.ctx} ctx after HeteroCache prefill (ratio 0.5, steps 5, threshold 0.5, "
-                        "seeded roles), bsz 1 per GPU",
+                        f"seeded roles{tier}), bsz 1 per GPU",
             "context": args.ctx, "layers": args.layers, "batch_per_gpu": 1, "heads": [H, KV, D],
             "parallelism": f"sequence-sharded x{n} (independent sequences, no data-path collective)",
             "l2": "KV pools (~268 MB/layer) exceed the 126 MB L2; no flush needed"}
@@ -67,6 +86,11 @@ def config_dict(args, n):
 def build_roles(layers, seed=2026):
     from heterocache_b200.roles import derive_runtime_data, synthetic_roles
     return derive_runtime_data(synthetic_roles(layers, KV, seed), layers, KV)
+
+
+def geometry():
+    from heterocache_b200.synthetic import LLAMA_8B
+    return GEO or LLAMA_8B
 
 
 def make_cache(data, layers, real_offload=False):
@@ -79,13 +103,13 @@ def make_cache(data, layers, real_offload=False):
 
 def prefill(cache, args, dev, seed):
     """Prefill every layer on the device; returns per-layer prefill kernel ms."""
-    from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
+    from heterocache_b200.synthetic import prefill_kv_device
     g = torch.Generator(device=dev).manual_seed(seed)
     L = args.ctx
     q = torch.randn(1, H, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
     times = []
     for layer in range(args.layers):
-        k, v = prefill_kv_device(LLAMA_8B, L, q[:, :, -32:, :], seed=seed * 1000 + layer, device=dev)
+        k, v = prefill_kv_device(geometry(), L, q[:, :, -32:, :], seed=seed * 1000 + layer, device=dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         cache.update(k, v, layer)
@@ -114,12 +138,15 @@ def decode_inputs(n_steps, layers, q0, dev, seed):
     return qs, ks, vs
 
 
-def decode_step(cache, qs, ks, vs, s, layers, outs):
+def decode_step(cache, qs, ks, vs, s, layers, outs, order="llama"):
     for layer in range(layers):
         q = qs[s, layer]
-        cache.update(ks[s, layer], vs[s, layer], layer)
+        cache.update(ks[s, layer], vs[s, layer], layer, {"query_states": q})
+        if order == "qwen":
+            cache.decode_select(q, layer)
         cache.attention(q, layer, out=outs[layer])
-        cache.decode_select(q, layer)
+        if order == "llama":
+            cache.decode_select(q, layer)
 
 
 class Clocks:
@@ -184,10 +211,12 @@ def time_kernels(cache, layers, reps=5):
     res = {}
     for name, fn in (("flash_decode", attn), ("drift_check", drift)):
         fn()
+        cache.join_retrievals()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, capture_error_mode="thread_local"):
             fn()
+            cache.join_retrievals()
         g.replay()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -272,7 +301,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     from oracle.hc_oracle import OracleCache
-    from heterocache_b200.synthetic import LLAMA_8B, DriftingDecode, prefill_inputs
+    from heterocache_b200.synthetic import DriftingDecode, prefill_inputs
     torch.set_num_threads(os.cpu_count() or 1)
     data = build_roles(args.layers)
     from types import SimpleNamespace
@@ -284,11 +313,11 @@ def run_reference(args, rank, world):
     qs = {}
     t_pre = time.perf_counter()
     for layer in sample_layers:
-        q, k, v = prefill_inputs(LLAMA_8B, args.ctx, seed=7 + layer, dtype=torch.bfloat16)
+        q, k, v = prefill_inputs(geometry(), args.ctx, seed=7 + layer, dtype=torch.bfloat16, q_positions=32)
         orc.update(k, v, layer)
         orc.init_coefficient(q, k, layer)
         orc.prefill_select(q, k, v, layer)
-        qs[layer] = DriftingDecode(LLAMA_8B, seed=11 + layer, q0=q[:, :, -1:, :], dtype=torch.bfloat16)
+        qs[layer] = DriftingDecode(geometry(), seed=11 + layer, q0=q[:, :, -1:, :], dtype=torch.bfloat16)
         del q
     t_pre = time.perf_counter() - t_pre
     per_layer = []
@@ -324,7 +353,7 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     data = build_roles(args.layers)
-    cache = make_cache(data, args.layers)
+    cache = make_cache(data, args.layers, real_offload=args.host_tier)
     prefill_ms, q_last = prefill(cache, args, dev, seed=1234 + rank)
     cache.check_errors()
     total_steps = args.warmup + args.steps
@@ -333,10 +362,10 @@ def run_ours(args, rank, world, local_rank):
     outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
     # eager warm-up: sizes the workspaces and warms the launch caches
     for s in range(STEPS_PER_CHECK):
-        decode_step(cache, qs, ks, vs, s, args.layers, outs)
+        decode_step(cache, qs, ks, vs, s, args.layers, outs, order=args.model)
     torch.cuda.synchronize()
     from heterocache_b200.graph import DecodeStepGraph
-    graph = DecodeStepGraph(cache, list(range(args.layers)))
+    graph = DecodeStepGraph(cache, list(range(args.layers)), order=args.model)
     clocks = Clocks(local_rank) if rank == 0 else None
     time.sleep(0.5)  # let the sampler start before the timed region
     for s in range(STEPS_PER_CHECK, STEPS_PER_CHECK + args.warmup):

@@ -261,6 +261,13 @@ class HeteroCache(_CacheBase):
             torch.cuda.current_stream(self._dev).wait_event(ev)
             self._retrieve_done[layer_idx] = None
 
+    def join_retrievals(self) -> None:
+        """Make the current stream wait for every retrieval still running on the
+        side stream (host-tier mode).  A captured decode step ends with this, so
+        each CUDA graph joins the side-stream work it forked."""
+        for layer_idx in range(len(self._retrieve_done)):
+            self._wait_retrieval(layer_idx)
+
     # ------------------------------------------------------------------
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
         """heterocache/cache_utils.py:884-1005."""

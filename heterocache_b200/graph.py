@@ -46,6 +46,7 @@ class DecodeStepGraph:
         self.v = torch.zeros(n, bsz, KV, 1, D, dtype=dt, device=dev)
         self.out = torch.zeros(n, bsz, H, D, dtype=dt, device=dev)
         cache.prepare_decode(self.layers, self.q[0])
+        cache.join_retrievals()  # no capture may wait on work recorded outside it
         S = cache.decode_step
         self.graphs: List[torch.cuda.CUDAGraph] = []
         start = cache._qcount[self.layers[0]]
@@ -71,6 +72,7 @@ class DecodeStepGraph:
             c.attention(self.q[i], l, out=self.out[i])
             if self.order == "llama":
                 c.decode_select(self.q[i], l)
+        c.join_retrievals()
 
     def step(self) -> torch.Tensor:
         """Replay one decode step (inputs already in ``self.q/k/v``)."""
