@@ -53,6 +53,10 @@ class HeteroCacheConfig:
     ``window_size`` (default 1, the HeteroCache behaviour) extends the prefill
     scoring to an observation window of the last W queries with SnapKV's
     in-window causal mask and window sum (heterocache/kv_cluster.py:168-178).
+
+    ``total_kv_heads`` (default: layers x KV heads) is the model-wide KV head
+    count of the budget formula; a cache that holds only some of a layer's
+    heads (the head-sharded mode) sets it to the whole model's count.
     """
 
     def __init__(self, data: Optional[Dict], compression_ratio: Optional[float] = 0.5,
@@ -60,7 +64,8 @@ class HeteroCacheConfig:
                  max_gen_len: Optional[int] = 128, decode_step: Optional[int] = 4,
                  pooling: Optional[str] = "avgpool", kernel_size: Optional[int] = 5,
                  num_attn_heads: Optional[int] = 32, num_kv_heads: Optional[int] = 8,
-                 num_layers: Optional[int] = 32, window_size: int = 1):
+                 num_layers: Optional[int] = 32, window_size: int = 1,
+                 total_kv_heads: Optional[int] = None):
         self.data = data
         self.stable_threshold = stable_threshold
         self.compression_ratio = compression_ratio
@@ -74,22 +79,29 @@ class HeteroCacheConfig:
         self.num_kv_heads = num_kv_heads
         self.num_layers = num_layers
         self.window_size = window_size
+        self.total_kv_heads = total_kv_heads
 
 
 class _LayerJobs:
     """Device descriptors of one layer's drift-check jobs and satellites."""
 
-    def __init__(self, relations: Dict[str, List[int]], alloc: List[float], base: int, L: int, device):
+    def __init__(self, relations: Dict[str, List[int]], alloc: List[float], base: int, L: int, device,
+                 remote_alloc: Optional[Dict[str, List[float]]] = None):
+        """``remote_alloc[leader]``: allocations of that pivot's satellites held
+        by other caches (head-sharded mode); the pivot's position list is made
+        long enough for them too."""
         jobs, slots, max_len = [], [], []
         m_job, m_head, m_len = [], [], []
+        remote_alloc = remote_alloc or {}
         for idx, (leader, members) in enumerate(relations.items()):
-            if not members:
+            far = [min(int(base * a), L) for a in remote_alloc.get(leader, [])]
+            if not members and not far:
                 continue
             lengths = [min(int(base * alloc[m]), L) for m in members]
             j = len(jobs)
             jobs.append(int(leader))
             slots.append(idx)
-            max_len.append(max(lengths))
+            max_len.append(max(lengths + far))
             for m, n in zip(members, lengths):
                 if n == 0:
                     continue
@@ -97,6 +109,7 @@ class _LayerJobs:
                 m_head.append(int(m))
                 m_len.append(n)
         self.n_jobs = len(jobs)
+        self.pivot_list = list(jobs)
         self.max_len_cap = max(max_len) if max_len else 0
         self.max_member_len = max(m_len) if m_len else 0
         i32 = dict(dtype=torch.int32, device=device)
@@ -122,7 +135,8 @@ class HeteroCache(_CacheBase):
         self.num_layers = cache_config.num_layers
         self.gqa = self.num_kv_heads != self.num_attn_heads
         self.num_key_value_groups = self.num_attn_heads // self.num_kv_heads
-        self.total_kv_heads = self.num_kv_heads * self.num_layers
+        self.total_kv_heads = (getattr(cache_config, "total_kv_heads", None)
+                               or self.num_kv_heads * self.num_layers)
         self.page_size = PAGE
         self.compression_ratio = cache_config.compression_ratio
         self.window_size = getattr(cache_config, "window_size", 1)
@@ -422,8 +436,10 @@ class HeteroCache(_CacheBase):
             self._qbuf[layer_idx] = torch.empty(S, H, D, dtype=query_states.dtype, device=query_states.device)
         relations = self.data["leader_member_relations"][layer_idx]
         if self._jobs[layer_idx] is None and relations:
+            remote = self.data.get("remote_member_alloc")
             jobs = _LayerJobs(relations, self.data["allocation_matrix"][layer_idx], self.base_compress_len,
-                              self.prefill_len, query_states.device)
+                              self.prefill_len, query_states.device,
+                              remote_alloc=remote[layer_idx] if remote else None)
             if self.record_checks:
                 jobs.coeffs = torch.zeros(max(jobs.n_jobs, 1), S, dtype=torch.float32, device=query_states.device)
                 jobs.median = torch.zeros(max(jobs.n_jobs, 1), dtype=torch.float64, device=query_states.device)

@@ -1,0 +1,252 @@
+"""KV-head-sharded decode over several GPUs (the head-sharded variant of the
+multi-GPU configuration).
+
+A layer's KV heads, in the runtime order the role file's derivation produces
+(anchor -> satellite -> volatile -> pivot), are split into equal contiguous
+blocks, one per rank; a rank also holds the query heads of its KV heads
+(GQA groups stay whole).  Each rank runs the compressed-KV path for its heads
+with its own ``HeteroCache``; the budget formula still uses the model-wide
+head counts, so every head gets the capacity it would get on one GPU.
+
+Two steps cross ranks:
+
+* attention: each rank's output rows [bsz, H/world, D] are all-gathered
+  (one NCCL all-gather per layer and step) into [bsz, H, D] for o_proj;
+* retrieval: a pivot and its satellites may sit on different ranks.  The
+  pivot's rank runs the drift check; at each check step it broadcasts the
+  pivot's trigger and position list (the list heterocache/cache_utils.py:
+  1084-1101 builds from the pivot's last buffered step), and every rank
+  holding one of its satellites retrieves that satellite's first
+  ``lengths[m]`` positions from its own full tier.
+
+Every rank issues the same collectives in the same order: one all-gather per
+``attention`` call and, at check steps, one broadcast per star group of the
+layer (in relation order).
+"""
+from __future__ import annotations
+
+import copy
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from .cache import HeteroCache, HeteroCacheConfig
+
+
+def head_blocks(num_kv_heads: int, world: int) -> List[range]:
+    """Contiguous, equal blocks of KV heads per rank."""
+    if world < 1 or num_kv_heads % world:
+        raise ValueError(f"{num_kv_heads} KV heads do not split evenly over {world} ranks")
+    n = num_kv_heads // world
+    return [range(r * n, (r + 1) * n) for r in range(world)]
+
+
+def owner_of(head: int, num_kv_heads: int, world: int) -> int:
+    return head // (num_kv_heads // world)
+
+
+def local_runtime_data(data: Dict, num_layers: int, num_kv_heads: int, world: int, rank: int):
+    """Runtime role data of one rank's heads, plus its cross-rank retrieval specs.
+
+    Returns ``(local, remote)``.  ``local`` is a derived role document for the
+    rank's heads (local ids 0..n-1 in the same order): classification and
+    allocation rows sliced, relations kept for local pivots with their local
+    satellites, ``remote_member_alloc[layer][local pivot]`` = allocations of
+    that pivot's satellites held by other ranks (its position list must cover
+    them), and the four ``need_to_*`` lists derived from the sliced rows.
+    ``remote[layer]`` lists, in the layer's relation order, every star group
+    with satellites off its pivot's rank: ``{"src": pivot rank, "leader":
+    pivot's local id there, "alloc": allocations of all its satellites,
+    "members": [(local head id, allocation)] of this rank's satellites}``.
+    """
+    blocks = head_blocks(num_kv_heads, world)
+    mine = blocks[rank]
+    n = len(mine)
+    local = {"meta": copy.deepcopy(data["meta"]), "classification_matrix": [], "allocation_matrix": [],
+             "leader_member_relations": [], "remote_member_alloc": [], "need_to_update_counts": [],
+             "need_to_select_counts": [], "need_to_compress_counts": [], "need_to_keep_counts": []}
+    remote: List[List[Dict]] = []
+    for layer in range(num_layers):
+        cls = list(data["classification_matrix"][layer][mine.start:mine.stop])
+        alloc = list(data["allocation_matrix"][layer][mine.start:mine.stop])
+        local["classification_matrix"].append(cls)
+        local["allocation_matrix"].append(alloc)
+        local["need_to_compress_counts"].append(cls.count(1) + cls.count(4))
+        local["need_to_select_counts"].append([i for i, x in enumerate(cls) if x == 3])
+        local["need_to_update_counts"].append([i for i, x in enumerate(cls) if x == 4])
+        local["need_to_keep_counts"].append([i for i, x in enumerate(cls) if x in (2, 3)])
+        rel: Dict[str, List[int]] = {}
+        rem_alloc: Dict[str, List[float]] = {}
+        specs: List[Dict] = []
+        full_alloc = data["allocation_matrix"][layer]
+        for leader, members in data["leader_member_relations"][layer].items():
+            lg = int(leader)
+            src = owner_of(lg, num_kv_heads, world)
+            if src == rank:
+                rel[str(lg - mine.start)] = [m - mine.start for m in members if owner_of(m, num_kv_heads, world) == rank]
+                off = [full_alloc[m] for m in members if owner_of(m, num_kv_heads, world) != rank]
+                if off:
+                    rem_alloc[str(lg - mine.start)] = off
+            # a star group crossing ranks: every rank takes part in its broadcast
+            if any(owner_of(m, num_kv_heads, world) != src for m in members):
+                specs.append({"src": src, "leader": lg - blocks[src].start,
+                              "alloc": [full_alloc[m] for m in members],
+                              "members": [(m - mine.start, full_alloc[m]) for m in members
+                                          if owner_of(m, num_kv_heads, world) == rank and src != rank]})
+        pivots = [int(x) for x in data["leader_member_relations"][layer]]
+        owners = {owner_of(p, num_kv_heads, world) for p in pivots}
+        if len(owners) > 1 and pivots != sorted(pivots):
+            # the reference pairs relation entry i with the i-th pivot in sorted
+            # order (cache_utils.py:1027 with utils.py:326); split over ranks that
+            # pairing cannot be kept when the two orders differ
+            raise NotImplementedError(f"layer {layer}: pivots in non-sorted relation order span ranks")
+        local["leader_member_relations"].append(rel)
+        local["remote_member_alloc"].append(rem_alloc)
+        remote.append(specs)
+    return local, remote
+
+
+class HeadShardedCache:
+    """One rank's share of a head-sharded ``HeteroCache``.
+
+    Inputs are the rank's slices: q [bsz, H/world, L, D], k/v
+    [bsz, KV/world, L, D].  ``attention`` returns every head's output
+    [bsz, H, D].  Method names and call order follow the cache object.
+    """
+
+    def __init__(self, config: HeteroCacheConfig, rank: int, world: int, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        KV, H = config.num_kv_heads, config.num_attn_heads
+        if H % KV:
+            raise ValueError("query heads must be a multiple of KV heads")
+        local, self.remote = local_runtime_data(config.data, config.num_layers, KV, world, rank)
+        self.kv_local = KV // world
+        self.h_local = H // world
+        cfg = HeteroCacheConfig(local, compression_ratio=config.compression_ratio,
+                                stable_threshold=config.stable_threshold, real_offload=config.real_offload,
+                                max_gen_len=config.max_gen_len, decode_step=config.decode_step,
+                                pooling=config.pooling, kernel_size=config.kernel_size,
+                                num_attn_heads=self.h_local, num_kv_heads=self.kv_local,
+                                num_layers=config.num_layers, window_size=getattr(config, "window_size", 1),
+                                total_kv_heads=KV * config.num_layers)
+        self.cache = HeteroCache(cfg)
+        self.num_layers = config.num_layers
+        self.num_attn_heads = H
+        self._count = [0] * config.num_layers
+        self._gather: Dict = {}
+        self._bufs: Dict = {}
+
+    # -- prefill -------------------------------------------------------
+    def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
+        return self.cache.update(key_states, value_states, layer_idx, cache_kwargs)
+
+    def init_coefficient(self, query_states, key_states, layer_idx):
+        self.cache.init_coefficient(query_states, key_states, layer_idx)
+
+    def prefill_select(self, query_states, key_states, value_states, layer_idx):
+        self.cache.prefill_select(query_states, key_states, value_states, layer_idx)
+
+    # -- decode --------------------------------------------------------
+    def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):
+        """Local flash-decode, then one all-gather: returns [bsz, H, D]."""
+        local = self.cache.attention(query_states, layer_idx, scale=scale)
+        return gather_heads(local, self.world, self.group, out=out, cache=self._gather)
+
+    def decode_select(self, query_states, layer_idx):
+        """Local drift checks and retrievals; at a check step, one broadcast per
+        star group crossing ranks, then the retrievals of this rank's
+        satellites of remote pivots."""
+        if not self.select_local(query_states, layer_idx):
+            return
+        for si, spec in enumerate(self.remote[layer_idx]):
+            buf = self.stage_positions(layer_idx, si)
+            broadcast_retrieval(buf, spec["src"], self.group)
+            self.retrieve_remote(layer_idx, si)
+
+    # The three phases of decode_select, callable one by one (the broadcast
+    # between them is the only cross-rank step).
+    def select_local(self, query_states, layer_idx) -> bool:
+        """The local cache's decode_select; True at a check step with star
+        groups that cross ranks."""
+        S = self.cache.decode_step
+        self.cache.decode_select(query_states, layer_idx)
+        self._count[layer_idx] += 1
+        if self._count[layer_idx] < S:
+            return False
+        self._count[layer_idx] = 0
+        return bool(self.remote[layer_idx])
+
+    def _max_len(self, spec) -> int:
+        c = self.cache
+        return max(min(int(c.base_compress_len * a), c.prefill_len) for a in spec["alloc"])
+
+    def stage_positions(self, layer_idx, si) -> torch.Tensor:
+        """Buffer [1 + max_len] int32 of star group ``si``: trigger and position
+        list, filled on the pivot's rank (the broadcast source)."""
+        spec = self.remote[layer_idx][si]
+        max_len = self._max_len(spec)
+        c = self.cache
+        buf = self._bufs.get((layer_idx, si))
+        if buf is None:
+            buf = torch.zeros(1 + max(max_len, 1), dtype=torch.int32, device=c._dev)
+            self._bufs[(layer_idx, si)] = buf
+        if spec["src"] == self.rank:
+            jobs = c._jobs[layer_idx]
+            if jobs is None or spec["leader"] not in jobs.pivot_list:
+                raise RuntimeError("pivot job missing on its rank")
+            j = jobs.pivot_list.index(spec["leader"])
+            buf[0:1].copy_(jobs.trigger[j:j + 1])
+            buf[1:1 + max_len].copy_(jobs.retrieve_positions[j, :max_len])
+        return buf
+
+    def retrieve_remote(self, layer_idx, si) -> None:
+        """Retrieve this rank's satellites of star group ``si`` from the staged
+        trigger and positions."""
+        spec = self.remote[layer_idx][si]
+        if not spec["members"]:
+            return
+        c = self.cache
+        buf = self._bufs[(layer_idx, si)]
+        base, L = c.base_compress_len, c.prefill_len
+        heads = [h for h, _ in spec["members"]]
+        lens = [min(int(base * a), L) for _, a in spec["members"]]
+        i32 = dict(dtype=torch.int32, device=c._dev)
+        c._wait_retrieval(layer_idx)
+        ops.retrieve(member_job=torch.zeros(len(heads), **i32), member_head=torch.tensor(heads, **i32),
+                     member_len=torch.tensor(lens, **i32), max_member_len=max(lens), trigger=buf[0:1],
+                     retrieve_positions=buf[1:].view(1, -1), full_k=c.key_cache_cpu[layer_idx],
+                     full_v=c.value_cache_cpu[layer_idx], k_pool=c.key_pools[layer_idx],
+                     v_pool=c.value_pools[layer_idx], block_table=c.block_tables[layer_idx],
+                     num_kv_heads=c.num_kv_heads, err=c._err)
+
+    def check_errors(self):
+        self.cache.check_errors()
+
+
+def gather_heads(local: torch.Tensor, world: int, group=None, out: Optional[torch.Tensor] = None,
+                 cache: Optional[Dict] = None) -> torch.Tensor:
+    """All-gather of per-rank head outputs [bsz, h, D] -> [bsz, world*h, D]
+    (rank r's heads at rows r*h .. r*h+h-1)."""
+    bsz, h, D = local.shape
+    key = (bsz, h, D, local.dtype, local.device)
+    stage = cache.get(key) if cache is not None else None
+    if stage is None:
+        stage = torch.empty(world, bsz, h, D, dtype=local.dtype, device=local.device)
+        if cache is not None:
+            cache[key] = stage
+    if dist.get_backend(group) == "gloo":
+        dist.all_gather(list(stage.unbind(0)), local.contiguous(), group=group)
+    else:
+        dist.all_gather_into_tensor(stage, local.contiguous(), group=group)
+    full = stage.permute(1, 0, 2, 3).reshape(bsz, world * h, D)
+    if out is not None:
+        out.copy_(full)
+        return out
+    return full
+
+
+def broadcast_retrieval(buf: torch.Tensor, src: int, group=None) -> None:
+    """Trigger and position list of one pivot, from the pivot's rank to all."""
+    dist.broadcast(buf, src=src, group=group)

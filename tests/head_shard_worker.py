@@ -1,0 +1,68 @@
+"""Worker of tests/test_gpu_head_shard.py (launched by torch.distributed.run,
+one process per GPU): a 2-way head-sharded cache against the single-GPU cache
+on the same inputs; writes this rank's comparison to $HC_SHARD_OUT/rank<r>.json."""
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+sys.path.insert(0, HERE)
+
+from test_gpu_head_shard import _config, _rows, _setup  # noqa: E402
+from heterocache_b200.cache import HeteroCache  # noqa: E402
+from heterocache_b200.head_shard import HeadShardedCache  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    res = {"rank": rank}
+    try:
+        layers, KV, H, L = 2, 8, 32, 4096
+        full = HeteroCache(_config(layers, KV, H))
+        shard = HeadShardedCache(_config(layers, KV, H), rank, world)
+        # both ranks prefill the full cache and only their own shard
+        gens = _setup(dev, full.data, layers, KV, H, L, (full, [shard]))
+        print(f"rank {rank}: prefill done", flush=True)
+        kl, hl = KV // world, H // world
+        ks, hs = slice(rank * kl, (rank + 1) * kl), slice(rank * hl, (rank + 1) * hl)
+        max_diff, same_rows, same_trig, n_trig = 0.0, True, True, 0
+        for step in range(12):
+            for layer in range(layers):
+                q, k, v = (t.to(dev) for t in gens[layer].step())
+                full.update(k, v, layer)
+                shard.update(k[:, ks].contiguous(), v[:, ks].contiguous(), layer)
+                o_full = full.attention(q, layer)
+                o_shard = shard.attention(q[:, hs].contiguous(), layer)
+                max_diff = max(max_diff, (o_full.float() - o_shard.float()).abs().max().item())
+                full.decode_select(q, layer)
+                shard.decode_select(q[:, hs].contiguous(), layer)
+                torch.cuda.synchronize()
+                jf, js = full._jobs[layer], shard.cache._jobs[layer]
+                if jf is not None and js is not None and js.n_jobs:
+                    same_trig &= torch.equal(jf.trigger[:jf.n_jobs].cpu(), js.trigger[:js.n_jobs].cpu())
+                    n_trig += int(js.trigger[:js.n_jobs].sum())
+                for h in range(kl):
+                    a, b = _rows(full, layer, rank * kl + h), _rows(shard.cache, layer, h)
+                    same_rows &= bool(torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]))
+            print(f"rank {rank}: step {step} done", flush=True)
+        full.check_errors()
+        shard.check_errors()
+        res.update(max_diff=max_diff, same_rows=bool(same_rows), same_trig=bool(same_trig), n_trig=n_trig,
+                   crossing=sum(len(s) for s in shard.remote))
+    except Exception as e:  # reported through the result file
+        res["error"] = repr(e)
+    with open(os.path.join(os.environ["HC_SHARD_OUT"], f"rank{rank}.json"), "w") as f:
+        json.dump(res, f)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

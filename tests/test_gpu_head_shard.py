@@ -1,0 +1,144 @@
+"""Head-sharded mode on 2 GPUs (NCCL) against the single-GPU cache.
+
+Each rank holds 4 of the 8 KV heads (and their 16 query heads); the seeded
+roles put a pivot and some of its satellites on different ranks, so the
+drift check's position list crosses ranks by broadcast.  Per decode step:
+the all-gathered attention output matches the single-GPU cache's (same
+kernels; only the split-K partition differs), the drift triggers match, and
+every head's page contents (prefill selection, retrieved satellite rows,
+appended tokens) are bit-identical.  Skipped with fewer than 2 GPUs.
+"""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rows(cache, layer, head):
+    D = cache.head_dim
+    kp = cache.key_pools[layer].view(-1, D)
+    vp = cache.value_pools[layer].view(-1, D)
+    n = int(cache.heads_len[layer][head])
+    bt = cache.block_tables[layer][head]
+    idx = torch.arange(n, device=kp.device)
+    slots = bt[(idx // 256)].long() * 256 + idx % 256
+    return kp[slots], vp[slots]
+
+
+def _setup(dev, data, layers, KV, H, L, caches):
+    """Prefill the single-GPU cache and the shards on the same inputs."""
+    from heterocache_b200.synthetic import LLAMA_8B, DriftingDecode, prefill_inputs
+    full, shards = caches
+    gens = []
+    for layer in range(layers):
+        q, k, v = prefill_inputs(LLAMA_8B, L, seed=40 + layer, dtype=torch.bfloat16)
+        qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+        full.update(kd, vd, layer)
+        full.init_coefficient(qd, kd, layer)
+        full.prefill_select(qd, kd, vd, layer)
+        for sh in shards:
+            r, kl, hl = sh.rank, KV // sh.world, H // sh.world
+            qs, ksl, vsl = (qd[:, r * hl:(r + 1) * hl].contiguous(), kd[:, r * kl:(r + 1) * kl].contiguous(),
+                            vd[:, r * kl:(r + 1) * kl].contiguous())
+            sh.update(ksl, vsl, layer)
+            sh.init_coefficient(qs, ksl, layer)
+            sh.prefill_select(qs, ksl, vsl, layer)
+        gens.append(DriftingDecode(LLAMA_8B, seed=70 + layer, q0=q[:, :, -1:, :], dtype=torch.bfloat16))
+    return gens
+
+
+def _config(layers=2, KV=8, H=32):
+    from heterocache_b200.cache import HeteroCacheConfig
+    from heterocache_b200.roles import derive_runtime_data, synthetic_roles
+    # 8 KV heads, one star of 4: the role order puts satellites on both head
+    # blocks of 2 ranks and the pivot on the second, so the star crosses ranks
+    data = derive_runtime_data(synthetic_roles(layers, KV, 3), layers, KV)
+    return HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.999, real_offload=False,
+                             max_gen_len=32, decode_step=5, pooling="avgpool", kernel_size=5, num_attn_heads=H,
+                             num_kv_heads=KV, num_layers=layers)
+
+
+def test_head_sharded_emulated_on_one_gpu(cuda_device):
+    """Both ranks of a 2-way head split in one process on one GPU, with the two
+    collectives done as copies: the sharding logic (budgets, local roles,
+    cross-rank position lists, remote retrievals) against the single cache."""
+    from heterocache_b200.cache import HeteroCache
+    from heterocache_b200.head_shard import HeadShardedCache
+    dev = cuda_device
+    layers, KV, H, L, world = 2, 8, 32, 4096, 2
+    full = HeteroCache(_config(layers, KV, H))
+    shards = [HeadShardedCache(_config(layers, KV, H), r, world) for r in range(world)]
+    assert sum(len(s) for s in shards[0].remote) > 0
+    gens = _setup(dev, full.data, layers, KV, H, L, (full, shards))
+    kl, hl = KV // world, H // world
+    n_trig = 0
+    for step in range(12):
+        for layer in range(layers):
+            q, k, v = (t.to(dev) for t in gens[layer].step())
+            full.update(k, v, layer)
+            for sh in shards:
+                r = sh.rank
+                sh.update(k[:, r * kl:(r + 1) * kl].contiguous(), v[:, r * kl:(r + 1) * kl].contiguous(), layer)
+            o_full = full.attention(q, layer)
+            o = torch.cat([sh.cache.attention(q[:, sh.rank * hl:(sh.rank + 1) * hl].contiguous(), layer)
+                           for sh in shards], dim=1)
+            assert (o_full.float() - o.float()).abs().max().item() <= 2e-2, (step, layer)
+            full.decode_select(q, layer)
+            checks = [sh.select_local(q[:, sh.rank * hl:(sh.rank + 1) * hl].contiguous(), layer) for sh in shards]
+            assert len(set(checks)) == 1
+            if checks[0]:
+                for si, spec in enumerate(shards[0].remote[layer]):
+                    bufs = [sh.stage_positions(layer, si) for sh in shards]
+                    for r in range(world):
+                        if r != spec["src"]:
+                            bufs[r].copy_(bufs[spec["src"]])
+                    for sh in shards:
+                        sh.retrieve_remote(layer, si)
+            torch.cuda.synchronize()
+            jf = full._jobs[layer]
+            for sh in shards:
+                js = sh.cache._jobs[layer]
+                if jf is not None and js is not None and js.n_jobs:
+                    assert torch.equal(jf.trigger[:jf.n_jobs].cpu(), js.trigger[:js.n_jobs].cpu()), (step, layer)
+                    n_trig += int(js.trigger[:js.n_jobs].sum())
+                for h in range(kl):
+                    a, b = _rows(full, layer, sh.rank * kl + h), _rows(sh.cache, layer, h)
+                    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]), (step, layer, sh.rank, h)
+    full.check_errors()
+    for sh in shards:
+        sh.check_errors()
+    assert n_trig > 0
+
+
+def test_head_sharded_two_gpus_match_single_gpu(tmp_path):
+    """The real thing: 2 processes, one GPU each, NCCL all-gather and
+    broadcast (launched with torch.distributed.run; each rank writes its
+    comparison result to a file)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import json
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HC_SHARD_OUT=str(tmp_path))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(here, "head_shard_worker.py")]
+    proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=240)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    res = [json.load(open(tmp_path / f"rank{r}.json")) for r in range(2)]
+    for r in res:
+        assert "error" not in r, r
+        assert r["same_rows"] and r["same_trig"], r
+        assert r["max_diff"] <= 2e-2, r
+        assert r["crossing"] > 0, r
+    assert sum(r["n_trig"] for r in res) > 0
