@@ -19,6 +19,12 @@ output read back.
 --impl reference times the oracle restatement of the reference's own path
 (PyTorch on the host CPU) on the same workload, one sampled layer per step.
 
+--workload config4 [--shard sequences|heads] runs the multi-GPU configuration:
+one Llama-3.1-8B attention layer, a batch of 8 independent sequences of
+65536 tokens, decode; either whole sequences per GPU (no collective) or every
+sequence's 8 KV heads split over the GPUs (NCCL all-gather of head outputs,
+broadcast of pivot position lists).  Total work is fixed (strong scaling).
+
 --model qwen --host-tier runs the config-3 workload instead: Qwen2.5-7B
 attention geometry (28 layers, 28 query / 4 KV heads), 229376-token context,
 the full KV tier in pinned host memory (retrieval reads it over the host
@@ -57,9 +63,15 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="layers (default 32; 28 with --model qwen)")
     ap.add_argument("--model", default="llama", choices=["llama", "qwen"])
     ap.add_argument("--host-tier", action="store_true", help="full KV tier in pinned host memory")
+    ap.add_argument("--workload", default="llama128k", choices=["llama128k", "config4"])
+    ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"])
+    ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    if args.workload == "config4":
+        args.ctx = args.ctx or 65536
+        args.layers = 1
     global H, KV, GEO
     if args.model == "qwen":
         from heterocache_b200.synthetic import QWEN_7B
@@ -431,6 +443,191 @@ def run_ours(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+class PhaseGraphs:
+    """CUDA graphs of one decode step over several caches, one per phase of the
+    drift-check cycle (as DecodeStepGraph does for one cache's layers)."""
+
+    def __init__(self, caches, eager_step, S):
+        self.caches, self.S = caches, S
+        torch.cuda.synchronize()
+        self.graphs = []
+        start = [c._qcount[0] for c in caches]
+        for phase in range(S):
+            saved = [c._host_state() for c in caches]
+            for c in caches:
+                c._qcount[0] = phase
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                eager_step()
+            for c, st in zip(caches, saved):
+                c._restore_host_state(st)
+            self.graphs.append(g)
+        for c, q in zip(caches, start):
+            c._qcount[0] = q
+
+    def step(self):
+        phase = self.caches[0]._qcount[0]
+        for c in self.caches:
+            c._append_bookkeeping(0)
+        self.graphs[phase].replay()
+        for c in self.caches:
+            c._qcount[0] = (phase + 1) % self.S
+
+
+def run_config4(args, rank, world, local_rank):
+    """Config 4: one Llama layer, a batch of independent sequences, sharded by
+    sequence (no collective) or by KV head (all-gather + broadcasts)."""
+    from heterocache_b200.cache import HeteroCacheConfig
+    from heterocache_b200.head_shard import HeadShardedCache, gather_heads
+    from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    n_seq, L = args.seqs, args.ctx
+    data = build_roles(1)
+    heads_mode = args.shard == "heads"
+    if heads_mode:
+        seqs = list(range(n_seq))
+        cfg = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.5, real_offload=False,
+                                max_gen_len=1024, decode_step=STEPS_PER_CHECK, pooling="avgpool", kernel_size=5,
+                                num_attn_heads=H, num_kv_heads=KV, num_layers=1)
+        views = [HeadShardedCache(cfg, rank, world) for _ in seqs]
+        inner = [v.cache for v in views]
+        kl, hl = KV // world, H // world
+    else:
+        if n_seq % world:
+            raise SystemExit(f"{n_seq} sequences do not split over {world} GPUs")
+        seqs = list(range(rank * n_seq // world, (rank + 1) * n_seq // world))
+        views = [make_cache(data, 1) for _ in seqs]
+        inner = views
+        kl, hl = KV, H
+    ks, hs = slice(rank * kl, (rank + 1) * kl) if heads_mode else slice(None), \
+        slice(rank * hl, (rank + 1) * hl) if heads_mode else slice(None)
+    # prefill: every sequence's q/K/V from its own seed (identical on every
+    # rank in the head-sharded mode, which keeps its own heads)
+    q_last = []
+    for view, s in zip(views, seqs):
+        g = torch.Generator(device=dev).manual_seed(5000 + s)
+        q = torch.randn(1, H, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        k, v = prefill_kv_device(LLAMA_8B, L, q[:, :, -32:, :], seed=6000 + s, device=dev)
+        qq, kk, vv = q[:, hs].contiguous(), k[:, ks].contiguous(), v[:, ks].contiguous()
+        view.update(kk, vv, 0)
+        view.init_coefficient(qq, kk, 0)
+        view.prefill_select(qq, kk, vv, 0)
+        q_last.append(q[:, :, -1:, :].clone())
+        del q, k, v, qq, kk, vv
+    torch.cuda.empty_cache()
+    for c in inner:
+        c.check_errors()
+    n_local = len(seqs)
+    total = args.warmup + args.steps + 2 * STEPS_PER_CHECK
+    gq = torch.Generator(device=dev).manual_seed(77)
+    cur = torch.cat(q_last, 0).float()  # [n_local, H, 1, D]
+    qs = torch.empty(total, n_local, 1, H, 1, D, device=dev, dtype=torch.bfloat16)
+    for t in range(total):
+        cur = 0.9 * cur + 0.1 * torch.randn(cur.shape, generator=gq, device=dev)
+        qs[t] = cur.unsqueeze(1).to(torch.bfloat16)
+    kvs = torch.randn(2, total, n_local, 1, KV, 1, D, generator=gq, device=dev).to(torch.bfloat16)
+    qb = torch.zeros(n_local, 1, hl, 1, D, dtype=torch.bfloat16, device=dev)
+    kb = torch.zeros(n_local, 1, kl, 1, D, dtype=torch.bfloat16, device=dev)
+    vb = torch.zeros_like(kb)
+    out = torch.zeros(n_local, H, D, dtype=torch.bfloat16, device=dev)
+    stage = {}
+
+    def load(t):
+        qb.copy_(qs[t][:, :, hs])
+        kb.copy_(kvs[0, t][:, :, ks])
+        vb.copy_(kvs[1, t][:, :, ks])
+
+    local = torch.zeros(n_local, hl, D, dtype=torch.bfloat16, device=dev)
+    crossing = [False]
+
+    def local_step():
+        """Everything but the collectives: captured in the phase graphs."""
+        for i, view in enumerate(views):
+            view.update(kb[i], vb[i], 0, {"query_states": qb[i]})
+        if heads_mode:
+            for i, view in enumerate(views):
+                view.cache.attention(qb[i], 0, out=local[i:i + 1])
+            crossing[0] = any([view.select_local(qb[i], 0) for i, view in enumerate(views)])
+        else:
+            for i, view in enumerate(views):
+                view.attention(qb[i], 0, out=out[i:i + 1])
+                view.decode_select(qb[i], 0)
+        for c in inner:
+            c.join_retrievals()
+
+    def collectives(check):
+        """Head-sharded mode, eager (NCCL stays out of the graphs): the output
+        all-gather, and at a check step the position-list broadcasts and the
+        retrievals of satellites whose pivot sits on another GPU."""
+        if not heads_mode:
+            return
+        gather_heads(local, world, out=out, cache=stage)
+        if check:
+            for view in views:
+                view.remote_checks(0)
+
+    def eager_step():
+        check = inner[0]._qcount[0] + 1 >= STEPS_PER_CHECK
+        local_step()
+        collectives(check)
+
+    for t in range(STEPS_PER_CHECK):  # eager warm-up: workspaces, launch caches, NCCL
+        load(t)
+        eager_step()
+    for c in inner:
+        c.prepare_decode([0], qb[0])
+    graphs = PhaseGraphs(inner, local_step, STEPS_PER_CHECK)
+
+    def graph_step():
+        check = inner[0]._qcount[0] + 1 >= STEPS_PER_CHECK
+        graphs.step()
+        collectives(check)
+
+    t0 = STEPS_PER_CHECK
+    for t in range(t0, t0 + args.warmup):
+        load(t)
+        graph_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = Clocks(local_rank) if rank == 0 else None
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    first = t0 + args.warmup
+    for t in range(first, first + args.steps):
+        load(t)
+        graph_step()
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop() if clocks else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+        ms = float(tt.item())
+        torch.distributed.barrier()
+    for c in inner:
+        c.check_errors()
+    ms_step = ms / args.steps
+    del graphs
+    if rank == 0:
+        mode = (f"KV-head-sharded x{world} (NCCL all-gather of head outputs per step)" if heads_mode
+                else f"sequence-sharded x{world} ({n_seq // world} sequences per GPU, no data-path collective)")
+        line = {"metric": METRIC, "value": n_seq * 1000.0 / ms_step, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded N(0,1) K/V with planted heavy hitters; drifting decode queries)",
+                "config": {"workload": f"config 4: llama-3.1-8b single attention layer, batch of {n_seq} "
+                                       f"independent sequences of {L} tokens, HeteroCache decode",
+                           "context": L, "sequences": n_seq, "parallelism": mode},
+                "us_per_step": ms_step * 1e3, "roofline": None, "cpu_baseline": None, "e2e": None,
+                "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
 def run_e2e(args, graph, qs, ks, vs, dev, world):
     """The same decode loop through the public graph API with host buffers: per
     step, q/k/v of every layer copied from pinned host memory into the graph's
@@ -485,6 +682,17 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "config4":
+        if world > 1:
+            import datetime
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                                 device_id=torch.device("cuda", local_rank))
+        try:
+            run_config4(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                torch.distributed.destroy_process_group()
         return
     if world > 1:
         import datetime

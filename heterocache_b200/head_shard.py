@@ -134,7 +134,6 @@ class HeadShardedCache:
         self.cache = HeteroCache(cfg)
         self.num_layers = config.num_layers
         self.num_attn_heads = H
-        self._count = [0] * config.num_layers
         self._gather: Dict = {}
         self._bufs: Dict = {}
 
@@ -158,8 +157,12 @@ class HeadShardedCache:
         """Local drift checks and retrievals; at a check step, one broadcast per
         star group crossing ranks, then the retrievals of this rank's
         satellites of remote pivots."""
-        if not self.select_local(query_states, layer_idx):
-            return
+        if self.select_local(query_states, layer_idx):
+            self.remote_checks(layer_idx)
+
+    def remote_checks(self, layer_idx) -> None:
+        """The cross-rank part of a check step: per star group crossing ranks,
+        stage, broadcast and retrieve (every rank, same order)."""
         for si, spec in enumerate(self.remote[layer_idx]):
             buf = self.stage_positions(layer_idx, si)
             broadcast_retrieval(buf, spec["src"], self.group)
@@ -170,13 +173,11 @@ class HeadShardedCache:
     def select_local(self, query_states, layer_idx) -> bool:
         """The local cache's decode_select; True at a check step with star
         groups that cross ranks."""
-        S = self.cache.decode_step
+        # the local cache counts the buffered queries (its host state, which a
+        # captured decode step saves and restores)
+        check = self.cache._qcount[layer_idx] + 1 >= self.cache.decode_step
         self.cache.decode_select(query_states, layer_idx)
-        self._count[layer_idx] += 1
-        if self._count[layer_idx] < S:
-            return False
-        self._count[layer_idx] = 0
-        return bool(self.remote[layer_idx])
+        return check and bool(self.remote[layer_idx])
 
     def _max_len(self, spec) -> int:
         c = self.cache
@@ -209,13 +210,17 @@ class HeadShardedCache:
             return
         c = self.cache
         buf = self._bufs[(layer_idx, si)]
-        base, L = c.base_compress_len, c.prefill_len
-        heads = [h for h, _ in spec["members"]]
-        lens = [min(int(base * a), L) for _, a in spec["members"]]
-        i32 = dict(dtype=torch.int32, device=c._dev)
+        key = ("members", layer_idx, si)
+        if key not in self._bufs:  # device index arrays, made once
+            base, L = c.base_compress_len, c.prefill_len
+            heads = [h for h, _ in spec["members"]]
+            lens = [min(int(base * a), L) for _, a in spec["members"]]
+            i32 = dict(dtype=torch.int32, device=c._dev)
+            self._bufs[key] = (torch.zeros(len(heads), **i32), torch.tensor(heads, **i32),
+                               torch.tensor(lens, **i32), max(lens))
+        mj, mh, ml, max_len = self._bufs[key]
         c._wait_retrieval(layer_idx)
-        ops.retrieve(member_job=torch.zeros(len(heads), **i32), member_head=torch.tensor(heads, **i32),
-                     member_len=torch.tensor(lens, **i32), max_member_len=max(lens), trigger=buf[0:1],
+        ops.retrieve(member_job=mj, member_head=mh, member_len=ml, max_member_len=max_len, trigger=buf[0:1],
                      retrieve_positions=buf[1:].view(1, -1), full_k=c.key_cache_cpu[layer_idx],
                      full_v=c.value_cache_cpu[layer_idx], k_pool=c.key_pools[layer_idx],
                      v_pool=c.value_pools[layer_idx], block_table=c.block_tables[layer_idx],
@@ -230,6 +235,11 @@ def gather_heads(local: torch.Tensor, world: int, group=None, out: Optional[torc
     """All-gather of per-rank head outputs [bsz, h, D] -> [bsz, world*h, D]
     (rank r's heads at rows r*h .. r*h+h-1)."""
     bsz, h, D = local.shape
+    if world == 1:
+        if out is not None:
+            out.copy_(local)
+            return out
+        return local
     key = (bsz, h, D, local.dtype, local.device)
     stage = cache.get(key) if cache is not None else None
     if stage is None:
