@@ -97,8 +97,10 @@ class _HeteroAttention(nn.Module):
             out = out.transpose(1, 2).reshape(bsz, q_len, -1).contiguous()
             return self.o_proj(out), None
         # the query rides along so the page-append launch also stores it for
-        # the drift check
-        cache.update(k, v, self.layer_idx, {"cache_position": cache_position, "query_states": q})
+        # the drift check; the append itself is deferred: attention merges the
+        # new token from k/v and appends it on the side stream
+        cache.update(k, v, self.layer_idx, {"cache_position": cache_position, "query_states": q,
+                                            "defer_append": True})
         if self.decode_select_before_attention:
             cache.decode_select(q, self.layer_idx)
         out = cache.attention(q, self.layer_idx, scale=self.scaling)  # [bsz, H, D]

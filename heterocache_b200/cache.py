@@ -178,6 +178,11 @@ class HeteroCache(_CacheBase):
         self._qcount = [0] * n
         # the decode append of this step already stored the query (see update)
         self._q_staged = [False] * n
+        # deferred decode appends (update(..., {"defer_append": True})): the
+        # step's (k, v, q, query slot) until attention launches it, then the
+        # side-stream event of the launched append
+        self._pending: List = [None] * n
+        self._append_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._jobs: List[Optional[_LayerJobs]] = [None] * n
         self._retrieve_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._side_stream: Optional[torch.cuda.Stream] = None
@@ -275,12 +280,20 @@ class HeteroCache(_CacheBase):
             torch.cuda.current_stream(self._dev).wait_event(ev)
             self._retrieve_done[layer_idx] = None
 
+    def _wait_append(self, layer_idx: int) -> None:
+        ev = self._append_done[layer_idx]
+        if ev is not None:
+            torch.cuda.current_stream(self._dev).wait_event(ev)
+            self._append_done[layer_idx] = None
+
     def join_retrievals(self) -> None:
-        """Make the current stream wait for every retrieval still running on the
-        side stream (host-tier mode).  A captured decode step ends with this, so
-        each CUDA graph joins the side-stream work it forked."""
+        """Make the current stream wait for every side-stream job still running:
+        retrievals (host-tier mode) and deferred page appends.  A captured
+        decode step ends with this, so each CUDA graph joins the side-stream
+        work it forked."""
         for layer_idx in range(len(self._retrieve_done)):
             self._wait_retrieval(layer_idx)
+            self._wait_append(layer_idx)
 
     # ------------------------------------------------------------------
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
@@ -332,14 +345,23 @@ class HeteroCache(_CacheBase):
 
         self._append_bookkeeping(layer_idx)
         self._wait_retrieval(layer_idx)
+        self._wait_append(layer_idx)
+        kw = cache_kwargs or {}
         # A caller that passes the step's query (cache_kwargs["query_states"],
         # as the attention modules of this package do) has the append launch
         # store it into the drift-check buffer; decode_select then skips its
         # own copy.
-        q = (cache_kwargs or {}).get("query_states") if self.bsz == 1 else None
-        q_stage = None
+        q = kw.get("query_states") if self.bsz == 1 else None
         if q is not None:
             self._ensure_decode_state(layer_idx, q)
+        if kw.get("defer_append"):
+            # attention() attends over the pages plus this token, then appends
+            # it on the side stream, off the attention's critical path
+            # [k, v, q, query slot, decode_select of this step already ran]
+            self._pending[layer_idx] = [key_states, value_states, q, self._qcount[layer_idx], False]
+            return key_states, value_states
+        q_stage = None
+        if q is not None:
             q_stage = self._qbuf[layer_idx][self._qcount[layer_idx]]
         ops.decode_append(key_states, value_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
                           self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
@@ -454,19 +476,32 @@ class HeteroCache(_CacheBase):
         return {"hlen": [None if h is None else h.copy() for h in self._hlen],
                 "mapped": [None if m is None else m.copy() for m in self._mapped],
                 "free_ptr": list(self.free_block_pointers), "qcount": list(self._qcount),
-                "retrieve_done": list(self._retrieve_done), "seen": self._seen_tokens}
+                "retrieve_done": list(self._retrieve_done), "seen": self._seen_tokens,
+                "pending": [None if x is None else list(x) for x in self._pending],
+                "append_done": list(self._append_done),
+                "q_staged": list(self._q_staged)}
 
     def _restore_host_state(self, s) -> None:
         self._hlen, self._mapped = s["hlen"], s["mapped"]
         self.free_block_pointers, self._qcount = s["free_ptr"], s["qcount"]
         self._retrieve_done, self._seen_tokens = s["retrieve_done"], s["seen"]
+        self._pending, self._append_done, self._q_staged = s["pending"], s["append_done"], s["q_staged"]
 
     def decode_select(self, query_states, layer_idx):
         """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
         S = self.decode_step
         self._ensure_decode_state(layer_idx, query_states)
-        if self._q_staged[layer_idx]:
-            self._q_staged[layer_idx] = False
+        pend = self._pending[layer_idx]
+        check = self._qcount[layer_idx] + 1 >= S
+        if pend is not None:
+            # decode_select before attention (Qwen order): this step's append
+            # is still to come; it stores the query, except that a drift check
+            # now needs it at once
+            pend[4] = True
+            if check or pend[2] is None:
+                self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
+        elif self._q_staged[layer_idx]:
+            self._q_staged[layer_idx] = False  # this step's append stored it
         else:
             self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
         self._qcount[layer_idx] += 1
@@ -481,6 +516,7 @@ class HeteroCache(_CacheBase):
     def _drift_and_retrieve(self, layer_idx, jobs, query_states):
         S = self.decode_step
         self._wait_retrieval(layer_idx)
+        self._wait_append(layer_idx)  # a deferred append may hold this step's query
         scores = (torch.empty(jobs.n_jobs, S, self.prefill_len, dtype=query_states.dtype,
                               device=query_states.device) if self.record_checks else None)
         ops.drift_check(self._qbuf[layer_idx], self.key_pools[layer_idx], self.block_tables[layer_idx],
@@ -526,10 +562,41 @@ class HeteroCache(_CacheBase):
 
     # ------------------------------------------------------------------
     def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):
-        """Decode attention over this layer's pages: q [bsz, H, 1, D] -> [bsz, H, D]."""
+        """Decode attention over this layer's pages: q [bsz, H, 1, D] -> [bsz, H, D].
+
+        With a deferred append pending (update(..., {"defer_append": True})),
+        the step's token is merged from its k/v and then appended to the pages
+        on the side stream; the layer's next use waits for that append."""
         self._wait_retrieval(layer_idx)
+        self._wait_append(layer_idx)
         total = int(self._hlen[layer_idx].sum())
-        return ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
-                                self.block_tables[layer_idx], self.heads_len[layer_idx],
-                                num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
-                                err=self._err, total_tokens_hint=total)
+        pend = self._pending[layer_idx]
+        if pend is None:
+            return ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
+                                    self.block_tables[layer_idx], self.heads_len[layer_idx],
+                                    num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
+                                    err=self._err, total_tokens_hint=total)
+        self._pending[layer_idx] = None
+        k, v, q, slot, selected = pend
+        out = ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
+                               self.block_tables[layer_idx], self.heads_len[layer_idx],
+                               num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
+                               err=self._err, k_new=k, v_new=v)
+        main = torch.cuda.current_stream(self._dev)
+        side = self._side()
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            ops.decode_append(k, v, self.key_pools[layer_idx], self.value_pools[layer_idx],
+                              self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
+                              self._free_ptr[layer_idx], self._err, q=q,
+                              q_stage=self._qbuf[layer_idx][slot] if q is not None else None)
+        if not torch.cuda.is_current_stream_capturing():  # a graph's buffers are static
+            for t in (k, v, q):
+                if t is not None:
+                    t.record_stream(side)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        self._append_done[layer_idx] = ev
+        if q is not None and not selected:
+            self._q_staged[layer_idx] = True  # decode_select of this step comes next
+        return out

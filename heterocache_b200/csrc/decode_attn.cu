@@ -646,8 +646,30 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD;
   const int rs = s_start[r], re = s_start[r + 1];
-  if (re == rs || span == 0) {
-    if (threadIdx.x < kD) out[threadIdx.x] = Elem<T>::from_f(0.f);
+  // the step's token not in the pages yet: its score (log2 domain) and value.
+  // q and k_new come from before the decode kernel, which started after they
+  // were complete, so they are read ahead of the wait.
+  const bool has_new = p.k_new != nullptr;
+  float s_new = -INFINITY, v_new_d = 0.f;
+  if (has_new) {
+    const int b = r / p.KV, h = r % p.KV;
+    const T* qrow = reinterpret_cast<const T*>(p.q) + b * p.qsb + (int64_t)(h * p.G + g) * p.qsh;
+    const T* krow = reinterpret_cast<const T*>(p.k_new) + b * p.kn_sb + (int64_t)h * p.kn_sh;
+    float prod = threadIdx.x < kD ? Elem<T>::to_f(qrow[threadIdx.x]) * Elem<T>::to_f(krow[threadIdx.x]) : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) prod += __shfl_xor_sync(0xffffffffu, prod, o);
+    if (lane == 0) s_red[warp] = prod;
+    __syncthreads();
+    float dot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kD / 32; ++w) dot += s_red[w];
+    s_new = dot * p.scale_log2;
+    if (threadIdx.x < kD)
+      v_new_d = Elem<T>::to_f(reinterpret_cast<const T*>(p.v_new)[b * p.vn_sb + (int64_t)h * p.vn_sh + threadIdx.x]);
+    __syncthreads();
+  }
+  if (re == rs || span == 0) {  // no pages: the new token alone, or nothing
+    if (threadIdx.x < kD) out[threadIdx.x] = Elem<T>::from_f(has_new ? v_new_d : 0.f);
     return;
   }
   const int c0 = rs / span, n = (re - 1) / span - c0 + 1;
@@ -656,7 +678,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   pdl_wait();
   pdl_trigger();  // the next kernel may get resident; it waits for this grid
   // phase A: one load round for (m, l); weights kept in s_w (m in s_w first)
-  float M = -INFINITY;
+  float M = s_new;
   for (int c = threadIdx.x; c < n; c += kCThreads) {
     const float2 ml = p.part_ml[(slot0 + c) * p.G + g];
     s_w[c] = ml.x;
@@ -682,7 +704,8 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
   if (lane == 0) s_red[warp] = L;
   __syncthreads();
-  L = 0.f;
+  const float f_new = has_new ? exp2f(s_new - M) : 0.f;  // the new token's weight (its l is 1)
+  L = f_new;
 #pragma unroll
   for (int w = 0; w < kCThreads / 32; ++w) L += s_red[w];
   // phase B: each warp every 8th partial, 8 independent loads in flight
@@ -710,7 +733,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   __syncthreads();
   if (threadIdx.x < kD) {
     const int d = threadIdx.x;
-    float O = 0.f;
+    float O = f_new * v_new_d;
 #pragma unroll
     for (int w = 0; w < kCThreads / 32; ++w) O += reinterpret_cast<const float*>(&s_acc[w][d / 4])[d % 4];
     out[d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);

@@ -87,6 +87,11 @@ struct FDParams {
   float scale_log2;
   float* part_o;
   float2* part_ml;
+  // optional: one more token per row, not in the pages yet (k_new/v_new
+  // [bsz, KV, 1, D] with batch and head strides); the combine merges it
+  const void* k_new;
+  const void* v_new;
+  int64_t kn_sb, kn_sh, vn_sb, vn_sh;
   void* out;
   int32_t* err;
 };

@@ -7,6 +7,10 @@ flash-decode, ``decode_select`` -- as CUDA graphs and replays them.  The drift
 check runs on every ``decode_step``-th call, so there is one graph per phase
 of that cycle; a step replays the graph of the current phase.
 
+Each layer's page append is deferred: attention merges the step's token from
+its k/v, and the append runs on the side stream off the critical path (the
+graph joins it at the end of the step).
+
 Order per layer follows the patched attention: Llama runs ``decode_select``
 after attention (heterocache/llama_model.py:382-391), Qwen2 before it
 (heterocache/qwen_model.py:178-201).
@@ -66,7 +70,7 @@ class DecodeStepGraph:
     def _eager_step(self) -> None:
         c = self.cache
         for i, l in enumerate(self.layers):
-            c.update(self.k[i], self.v[i], l, {"query_states": self.q[i]})
+            c.update(self.k[i], self.v[i], l, {"query_states": self.q[i], "defer_append": True})
             if self.order == "qwen":
                 c.decode_select(self.q[i], l)
             c.attention(self.q[i], l, out=self.out[i])

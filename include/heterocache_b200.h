@@ -162,6 +162,25 @@ int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_d
                     void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Decode attention over each row's pages plus the step's own token, which is
+ * not in the pages yet: the form of flash_attn_with_kvcache that takes the
+ * new k and v with the cache (the call the patched attention makes is
+ * llama_model.py:382-389 / qwen_model.py:194-201, after HeteroCache.update
+ * has appended).  Row r attends over its heads_len[r] page tokens and
+ * k_new/v_new [bsz, KV, 1, D] (batch strides kn_sb / vn_sb, head strides
+ * kn_sh / vn_sh); the pages are not written, so the caller appends the token
+ * afterwards (hc_decode_append) -- which lets that append run off the
+ * attention's critical path.  Arguments otherwise as hc_flash_decode.
+ */
+int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, int head_dim,
+                             const void* q, int64_t qsb, int64_t qsh,
+                             const void* k_pool, const void* v_pool, int n_pool_blocks,
+                             const int32_t* block_table, int max_blocks, const int32_t* heads_len,
+                             const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh,
+                             int64_t vn_sb, int64_t vn_sh, float scale, void* out,
+                             void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Decode attention without a workspace.  No counterpart in the reference:
  * this is an addition for callers that cannot allocate device memory, such as
  * a host program whose device memory is entirely owned by another allocator,

@@ -189,3 +189,49 @@ def test_config3_qwen_224k_host_tier(cuda_device):
               n_decode=10, gen=16, role_seed=21, seed=31, layers=1)
     inputs = [prefill_inputs(QWEN_7B, sc["L"], seed=sc["seed"] * 100, dtype=torch.bfloat16, q_positions=32)]
     run_lockstep(sc, QWEN_7B, torch.bfloat16, inputs, real_offload=True)
+
+
+@pytest.mark.parametrize("order", ["llama", "qwen"])
+def test_deferred_append_matches_immediate(cuda_device, order):
+    """update(..., {"defer_append": True}): attention merges the step's token
+    from its k/v and the page append runs afterwards on the side stream.
+    Against the immediate append on the same inputs: attention outputs within
+    the bf16 tolerance, and lengths, page tables, every page row and the drift
+    triggers identical, in both call orders (Llama: decode_select after
+    attention; Qwen: before)."""
+    sc = SCENARIOS["llama_bf16_avg5"]
+    geo, tdt, layer_inputs = scenario_inputs(sc)
+    dev = torch.device("cuda", 0)
+    caches = [_gpu_cache(sc)[0] for _ in range(2)]
+    for c in caches:
+        for layer, (q, k, v) in enumerate(layer_inputs):
+            qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+            c.update(kd, vd, layer)
+            c.init_coefficient(qd, kd, layer)
+            c.prefill_select(qd, kd, vd, layer)
+    gens = DriftingDecode(geo, bsz=1, seed=sc["seed"] * 1000, q0=layer_inputs[0][0][:, :, -1:, :], dtype=tdt)
+    n_checks = 0
+    for step in range(12):
+        q, k, v = (t.to(dev) for t in gens.step())
+        outs = []
+        for c, defer in zip(caches, (False, True)):
+            kw = {"query_states": q, "defer_append": defer}
+            c.update(k, v, 0, kw)
+            if order == "qwen":
+                c.decode_select(q, 0)
+            outs.append(c.attention(q, 0).float())
+            if order == "llama":
+                c.decode_select(q, 0)
+            c.join_retrievals()
+        torch.cuda.synchronize()
+        assert (outs[0] - outs[1]).abs().max().item() <= 2e-2, step
+        a, b = caches
+        assert torch.equal(a.heads_len[0], b.heads_len[0]) and torch.equal(a.block_tables[0], b.block_tables[0])
+        assert torch.equal(a.key_pools[0], b.key_pools[0]) and torch.equal(a.value_pools[0], b.value_pools[0])
+        ja, jb = a._jobs[0], b._jobs[0]
+        if ja is not None:
+            assert torch.equal(ja.trigger, jb.trigger)
+            n_checks += int(step % sc["steps"] == sc["steps"] - 1)
+    for c in caches:
+        c.check_errors()
+    assert n_checks > 0
