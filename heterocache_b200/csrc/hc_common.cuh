@@ -27,6 +27,7 @@ template <> struct Elem<float> {
   __device__ __forceinline__ static float from_f(float x) { return x; }
   __device__ __forceinline__ static float rnd(float x) { return x; }
   __device__ __forceinline__ static float pack(float x) { return x; }
+  __device__ __forceinline__ static void rnd2(float&, float&) {}
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = __float_as_uint(x);
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
@@ -41,14 +42,13 @@ template <> struct Elem<__nv_bfloat16> {
   static constexpr int kKeyBits = 16;
   __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
-  // Round to nearest even on the bit pattern: integer-pipe operations only
-  // (the conversion unit is the bottleneck of the scoring phases).  Finite
-  // values and infinities round exactly as the conversion does; a NaN stays
-  // a NaN.
-  __device__ __forceinline__ static float rnd(float x) {
-    const uint32_t b = __float_as_uint(x);
-    const uint32_t r = (b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u;
-    return __uint_as_float((b & 0x7fffffffu) > 0x7f800000u ? (b | 0x00400000u) & 0xffff0000u : r);
+  __device__ __forceinline__ static float rnd(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+  // two values with one packed conversion (half the conversion-unit work)
+  __device__ __forceinline__ static void rnd2(float& a, float& b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(&h);
+    a = __uint_as_float(w << 16);
+    b = __uint_as_float(w & 0xffff0000u);
   }
   // x already holds a bf16 value: keep its upper half
   __device__ __forceinline__ static __nv_bfloat16 pack(float x) {
@@ -70,6 +70,12 @@ template <> struct Elem<__half> {
   __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
   __device__ __forceinline__ static float rnd(float x) { return __half2float(__float2half_rn(x)); }
   __device__ __forceinline__ static __half pack(float x) { return __float2half_rn(x); }  // exact
+  __device__ __forceinline__ static void rnd2(float& a, float& b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    a = f.x;
+    b = f.y;
+  }
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = (uint32_t)__half_as_ushort(__float2half_rn(x));  // exact: x is an f16 value
     return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);

@@ -109,6 +109,23 @@ __device__ __forceinline__ float scale_logit(float acc, float y, float r) {
   }
 }
 
+// The same for the two logits of a pair, with packed conversions.
+template <typename T>
+__device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float r) {
+  if constexpr (std::is_same<T, float>::value) {
+    a = __fdiv_rn(a, y);
+    b = __fdiv_rn(b, y);
+  } else {
+    Elem<T>::rnd2(a, b);
+    float qa = div_known(a, y, r), qb = div_known(b, y, r);
+    if (__builtin_expect(fabsf(a) < 0x1p-120f, 0)) qa = __fdiv_rn(a, y);
+    if (__builtin_expect(fabsf(b) < 0x1p-120f, 0)) qb = __fdiv_rn(b, y);
+    Elem<T>::rnd2(qa, qb);
+    a = qa;
+    b = qb;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Phase 1, tensor-core path (16-bit dtypes, Rq <= 8*NT): a warp computes the
 // logits of 16 tokens x 8*NT query rows per iteration with m16n8k16 MMAs.
@@ -167,12 +184,14 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
+      scale_logit2<T>(acc[nt][0], acc[nt][1], p.sqrt_d, r_sqrt);
+      scale_logit2<T>(acc[nt][2], acc[nt][3], p.sqrt_d, r_sqrt);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int qi = nt * 8 + 2 * tig + (e & 1);
         const int t = tg + gid + ((e >> 1) << 3);
         if (qi >= p.Rq || t >= hi) continue;
-        float x = scale_logit<T>(acc[nt][e], p.sqrt_d, r_sqrt);
+        float x = acc[nt][e];
         if (masked(p, qi, t)) x = -INFINITY;
         lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::pack(x);
         if (t >= ji.t0 && t < ji.t1) rmax[nt][e & 1] = fmaxf(rmax[nt][e & 1], x);
@@ -338,7 +357,13 @@ __device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* l
         const float M = s_rowM[qi], S = s_rowS[qi], R = s_rowR[qi];
 #pragma unroll
         for (int i = 8 - HALO; i < 16 + HALO; ++i)
-          w[i] = (w[i] == -INFINITY) ? 0.f : Elem<T>::rnd(softmax_prob<T>(w[i], M, S, R));
+          w[i] = (w[i] == -INFINITY) ? 0.f : softmax_prob<T>(w[i], M, S, R);
+        // rounded to the dtype in pairs (one packed conversion each)
+#pragma unroll
+        for (int i = 8 - HALO; i < 16 + HALO; i += 2) {
+          if (i + 1 < 16 + HALO) Elem<T>::rnd2(w[i], w[i + 1]);
+          else w[i] = Elem<T>::rnd(w[i]);
+        }
       }
       if (c - HALO < 0 || c + 8 + HALO > p.L) {
 #pragma unroll
@@ -354,12 +379,16 @@ __device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* l
 #pragma unroll
           for (int j = 1; j <= 2 * HALO; ++j) v += w[8 + o - HALO + j];
           if constexpr (std::is_same<T, float>::value) v = __fdiv_rn(v, KS);
-          else v = Elem<T>::rnd(div_known(v, KS, rKS));
+          else v = div_known(v, KS, rKS);
         } else {
 #pragma unroll
           for (int j = 1; j <= 2 * HALO; ++j) v = fmaxf(v, w[8 + o - HALO + j]);
         }
         best[o] = v;
+      }
+      if (avg) {  // pooled averages rounded to the dtype (max pooling keeps dtype values)
+#pragma unroll
+        for (int o = 0; o < 8; o += 2) Elem<T>::rnd2(best[o], best[o + 1]);
       }
     }
     // max over the group's lanes (groups are aligned within a warp)

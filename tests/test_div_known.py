@@ -68,19 +68,3 @@ def test_pooling_division_matches_ieee_division(ks):
     _check(np.arange(1, 1 << 23, dtype=np.uint32).view(np.float32), ks)  # subnormals
     _check(np.zeros(1, np.float32), ks)
 
-
-def test_bf16_rounding_on_the_bit_pattern():
-    """``Elem<bf16>::rnd``: (b + 0x7fff + lsb) & 0xffff0000 equals torch's float->bf16 conversion
-    (round to nearest even) on finite values and infinities, ties included."""
-    import torch
-    rng = np.random.default_rng(7)
-    hi = rng.integers(0, 1 << 16, size=1 << 20, dtype=np.uint32) << 16
-    lows = np.array([0, 1, 0x7fff, 0x8000, 0x8001, 0xffff], dtype=np.uint32)
-    b = (hi[:, None] | lows[None, :]).ravel()
-    b = np.concatenate([b, hi | rng.integers(0, 1 << 16, size=hi.size, dtype=np.uint32)])
-    x = b.view(np.float32)
-    b = b[np.isfinite(x) | np.isinf(x)]
-    b = b[~np.isnan(b.view(np.float32))]
-    got = (b + np.uint32(0x7fff) + ((b >> np.uint32(16)) & np.uint32(1))) & np.uint32(0xffff0000)
-    want = torch.from_numpy(b.view(np.float32).copy()).to(torch.bfloat16).to(torch.float32).numpy().view(np.uint32)
-    assert np.array_equal(got, want)
