@@ -37,7 +37,13 @@ namespace hc {
 
 struct JobInfo {
   int b, h, job, part, t0, t1;
+  // DRIFT mode: page ids of the CTA's token range, staged in shared memory
+  // (npages == 0: look them up in the block table)
+  const int* pages;
+  int page0, npages;
 };
+
+constexpr int kMaxPages = 64;
 
 __device__ __forceinline__ JobInfo job_info(const ScoreParams& p) {
   JobInfo ji;
@@ -55,6 +61,8 @@ __device__ __forceinline__ JobInfo job_info(const ScoreParams& p) {
   }
   ji.t0 = ji.part * p.T;
   ji.t1 = min(p.L, ji.t0 + p.T);
+  ji.pages = nullptr;
+  ji.page0 = ji.npages = 0;
   return ji;
 }
 
@@ -62,11 +70,20 @@ __device__ __forceinline__ JobInfo job_info(const ScoreParams& p) {
 template <typename T>
 __device__ __forceinline__ const T* key_row(const ScoreParams& p, const JobInfo& ji, int t) {
   if (p.mode == MODE_DRIFT) {
-    int row = ji.b * p.KV + ji.h;
-    int blk = p.bt[(int64_t)row * p.max_blocks + (t >> 8)];
-    if (blk < 0 || blk >= p.n_blocks) {  // keep the address inside the pool; report
-      set_err(p.err, HC_ERR_RANGE);
-      blk = 0;
+    int blk;
+    if (ji.npages) {
+      // rows past the staged range (a tile's tail beyond the CTA's keys) only
+      // feed discarded logits: clamp them to the last staged page
+      const int i = min((t >> 8) - ji.page0, ji.npages - 1);
+      blk = ji.pages[i];  // validated when staged (-1: reported, read page 0)
+      if (blk < 0) blk = 0;
+    } else {
+      const int row = ji.b * p.KV + ji.h;
+      blk = p.bt[(int64_t)row * p.max_blocks + (t >> 8)];
+      if (blk < 0 || blk >= p.n_blocks) {  // keep the address inside the pool; report
+        set_err(p.err, HC_ERR_RANGE);
+        blk = 0;
+      }
     }
     return reinterpret_cast<const T*>(p.k_pool) + ((int64_t)blk * kPage + (t & (kPage - 1))) * kD;
   }
@@ -512,7 +529,8 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
 
   constexpr int KB = Elem<T>::kKeyBits;
   constexpr int ROUNDS = KB / 8;
-  const JobInfo ji = job_info(p);
+  __shared__ int s_pages[kMaxPages];
+  JobInfo ji = job_info(p);
   const int nblocks = gridDim.x;
   unsigned int epoch = 0;
 
@@ -546,6 +564,27 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
     const int wbeg = ji.t0 >> 5, nwords = ((ji.t1 + 31) >> 5) - wbeg;
     if (nwords <= kRefWords)
       for (int w = threadIdx.x; w < nwords; w += kSThreads) s_refw[w] = bm[wbeg + w];
+  }
+
+  if (p.mode == MODE_DRIFT) {
+    // the page ids of this CTA's keys, once (instead of one dependent load per tile)
+    const int lo = max(0, ji.t0 - kMargin), hi = min(p.L, ji.t1 + kMargin);
+    const int pg0 = lo >> 8, npg = ((hi - 1) >> 8) - pg0 + 1;
+    if (npg <= kMaxPages) {
+      const int row = ji.b * p.KV + ji.h;
+      for (int i = threadIdx.x; i < npg; i += kSThreads) {
+        int blk = p.bt[(int64_t)row * p.max_blocks + pg0 + i];
+        if (blk < 0 || blk >= p.n_blocks) {
+          set_err(p.err, HC_ERR_RANGE);
+          blk = -1;
+        }
+        s_pages[i] = blk;
+      }
+      ji.pages = s_pages;
+      ji.page0 = pg0;
+      ji.npages = npg;
+    }
+    __syncthreads();
   }
 
   // ---- phase 1: logits
@@ -728,18 +767,13 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
         const unsigned int pre = s_prefix[sel], msk = s_mask[sel];
         const unsigned int* kr = keys + s_sel_row[sel] * p.T;
         unsigned int ngt = 0;
+        // below the top digit the keys of one prefix spread over many bins:
+        // plain shared-memory atomics (a warp-level match costs more here)
         for (int c0 = 0; c0 < ntok; c0 += kSThreads) {
           const int i = c0 + threadIdx.x;
           const unsigned int key = i < ntok ? kr[i] : 0u;
-          const bool hit = i < ntok && (key & msk) == pre;
           ngt += __popc(__ballot_sync(0xffffffffu, i < ntok && (key & msk) > pre));
-          // scores crowd into few bins: one atomic per distinct bin per warp
-          const unsigned int act = __ballot_sync(0xffffffffu, hit);
-          if (hit) {
-            const unsigned int bin = (key >> shift) & 255u;
-            const unsigned int peers = __match_any_sync(act, bin);
-            if (lane == __ffs(peers) - 1) atomicAdd(&lhist[sel * 256 + bin], __popc(peers));
-          }
+          if (i < ntok && (key & msk) == pre) atomicAdd(&lhist[sel * 256 + ((key >> shift) & 255u)], 1u);
         }
         if (last && lane == 0 && ngt) atomicAdd(&s_gtc[sel], ngt);
       }
