@@ -54,6 +54,10 @@ template <> struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static __nv_bfloat16 pack(float x) {
     return __ushort_as_bfloat16((unsigned short)(__float_as_uint(x) >> 16));
   }
+  // a and b already hold bf16 values: a in the low half, b in the high half
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
+  }
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = __float_as_uint(x) >> 16;  // exact: x is a bf16 value
     return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
@@ -70,6 +74,10 @@ template <> struct Elem<__half> {
   __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
   __device__ __forceinline__ static float rnd(float x) { return __half2float(__float2half_rn(x)); }
   __device__ __forceinline__ static __half pack(float x) { return __float2half_rn(x); }  // exact
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {  // exact: f16 values
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
   __device__ __forceinline__ static void rnd2(float& a, float& b) {
     const __half2 h = __floats2half2_rn(a, b);
     const float2 f = __half22float2(h);
@@ -282,6 +290,14 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
   return r;
 }
+// Store two 8x8 16-bit matrices held in the mma accumulator layout (lane l:
+// row l/4, columns 2(l%4), 2(l%4)+1 of each), transposed: memory row j of
+// matrix m (address from lane 8m + j) receives column j.
+__device__ __forceinline__ void stmatrix2_trans(uint32_t addr, uint32_t m0, uint32_t m1) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x2.trans.shared.b16 [%0], {%1, %2};\n" ::"r"(addr), "r"(m0), "r"(m1)
+               : "memory");
+}
+
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 r;
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "r"(addr));

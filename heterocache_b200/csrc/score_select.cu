@@ -110,18 +110,24 @@ __device__ __forceinline__ bool masked(const ScoreParams& p, int qi, int t) {
   return false;
 }
 
+// 0 < |x| < 2^-120: operands whose quotient by sqrt(d) may be subnormal.
+__device__ __forceinline__ bool tiny_nonzero(float x) {
+  return (__float_as_uint(x) & 0x7fffffffu) - 1u < 0x037fffffu;
+}
+
 // Logit in the model dtype: rnd(rnd(q.k) / sqrt(d)), the division correctly
 // rounded.  16-bit models divide by the known divisor with one residual
-// correction (tiny operands, whose quotient would be subnormal, take IEEE
-// division); fp32 models always use IEEE division.
+// correction (tiny nonzero operands take IEEE division; the sign of a zero
+// quotient is restored from the operand, as IEEE division keeps it); fp32
+// models always use IEEE division.
 template <typename T>
 __device__ __forceinline__ float scale_logit(float acc, float y, float r) {
   const float x = Elem<T>::rnd(acc);
   if constexpr (std::is_same<T, float>::value) {
     return __fdiv_rn(x, y);
   } else {
-    float q = div_known(x, y, r);
-    if (__builtin_expect(fabsf(x) < 0x1p-120f, 0)) q = __fdiv_rn(x, y);
+    float q = copysignf(div_known(x, y, r), x);
+    if (__builtin_expect(tiny_nonzero(x), 0)) q = __fdiv_rn(x, y);
     return Elem<T>::rnd(q);
   }
 }
@@ -134,9 +140,11 @@ __device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float 
     b = __fdiv_rn(b, y);
   } else {
     Elem<T>::rnd2(a, b);
-    float qa = div_known(a, y, r), qb = div_known(b, y, r);
-    if (__builtin_expect(fabsf(a) < 0x1p-120f, 0)) qa = __fdiv_rn(a, y);
-    if (__builtin_expect(fabsf(b) < 0x1p-120f, 0)) qb = __fdiv_rn(b, y);
+    float qa = copysignf(div_known(a, y, r), a), qb = copysignf(div_known(b, y, r), b);
+    if (__builtin_expect(tiny_nonzero(a) || tiny_nonzero(b), 0)) {
+      if (tiny_nonzero(a)) qa = __fdiv_rn(a, y);
+      if (tiny_nonzero(b)) qb = __fdiv_rn(b, y);
+    }
     Elem<T>::rnd2(qa, qb);
     a = qa;
     b = qb;
@@ -150,8 +158,9 @@ __device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float 
 // a permuted order so that each thread loads 16 contiguous bytes per row; the
 // query fragments use the same permutation, so the dot products are exact
 // sums over all 128 dims.
-template <typename T, int NT>
-__device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float* wmax) {
+template <typename T, int NT, typename Pre>
+__device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float* wmax, uint32_t* dummy,
+                           Pre&& pre) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   uint32_t qb[NT][8][2];
@@ -170,6 +179,7 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
       }
     }
   }
+  pre();  // block-wide work that overlaps the query loads (ends in a block barrier)
   float rmax[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) rmax[nt][0] = rmax[nt][1] = -INFINITY;
@@ -178,6 +188,22 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   const int lo = max(0, ji.t0 - kMargin);
   const int hi = min(p.L, ji.t1 + kMargin);
   const int base = ji.t0 - kMargin;  // lg column 0 <-> token base
+  // Tiles whose 16 tokens all lie in [t0, t1) (no window mask, logits in
+  // shared memory) store their logits transposed with stmatrix: lane 8h + j
+  // addresses query row nt*8 + j at the tile's token 8h.  Rows past Rq go to
+  // a scratch word.  Column offsets are multiples of 16 tokens (t0 is a
+  // multiple of 32, lo = t0 - 16 or 0) and TB a multiple of 8, so every row
+  // address is 16-byte aligned.
+  const bool fast_ok = p.logits_in_smem && p.W == 1;
+  uint32_t st_row[NT];
+  unsigned int st_valid = 0u;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int qi = nt * 8 + (lane & 7);
+    st_row[nt] = smem_u32(lg) + 2u * (uint32_t)(qi * p.TB - base + 8 * ((lane >> 3) & 1));
+    if (qi < p.Rq) st_valid |= 1u << nt;
+  }
+  const uint32_t st_dummy = smem_u32(dummy);
   for (int tg = lo + warp * 16; tg < hi; tg += kSWarps * 16) {
     const int ta = min(tg + gid, p.L - 1), tb = min(tg + gid + 8, p.L - 1);
     const T* ra = key_row<T>(p, ji, ta);
@@ -198,6 +224,18 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
         mma16816<T>(acc[nt], ka[s].x, kb[s].x, ka[s].y, kb[s].y, qb[nt][2 * s][0], qb[nt][2 * s][1]);
         mma16816<T>(acc[nt], ka[s].z, kb[s].z, ka[s].w, kb[s].w, qb[nt][2 * s + 1][0], qb[nt][2 * s + 1][1]);
       }
+    }
+    if (fast_ok && tg >= ji.t0 && tg + 16 <= ji.t1) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        scale_logit2<T>(acc[nt][0], acc[nt][1], p.sqrt_d, r_sqrt);
+        scale_logit2<T>(acc[nt][2], acc[nt][3], p.sqrt_d, r_sqrt);
+        rmax[nt][0] = fmaxf(rmax[nt][0], fmaxf(acc[nt][0], acc[nt][2]));
+        rmax[nt][1] = fmaxf(rmax[nt][1], fmaxf(acc[nt][1], acc[nt][3]));
+        const uint32_t a = ((st_valid >> nt) & 1u) ? st_row[nt] + 2u * (uint32_t)tg : st_dummy;
+        stmatrix2_trans(a, Elem<T>::pack2(acc[nt][0], acc[nt][1]), Elem<T>::pack2(acc[nt][2], acc[nt][3]));
+      }
+      continue;
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -530,6 +568,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
   constexpr int KB = Elem<T>::kKeyBits;
   constexpr int ROUNDS = KB / 8;
   __shared__ int s_pages[kMaxPages];
+  __shared__ __align__(16) uint32_t s_dummy[4];  // sink of stmatrix rows past Rq
   JobInfo ji = job_info(p);
   const int nblocks = gridDim.x;
   unsigned int epoch = 0;
@@ -566,8 +605,10 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
       for (int w = threadIdx.x; w < nwords; w += kSThreads) s_refw[w] = bm[wbeg + w];
   }
 
-  if (p.mode == MODE_DRIFT) {
-    // the page ids of this CTA's keys, once (instead of one dependent load per tile)
+  // the page ids of this CTA's keys, once (instead of one dependent load per
+  // tile); the tensor-core path runs this after issuing its query loads
+  auto stage_pages = [&]() {
+    if (p.mode != MODE_DRIFT) return;
     const int lo = max(0, ji.t0 - kMargin), hi = min(p.L, ji.t1 + kMargin);
     const int pg0 = lo >> 8, npg = ((hi - 1) >> 8) - pg0 + 1;
     if (npg <= kMaxPages) {
@@ -585,19 +626,20 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams 
       ji.npages = npg;
     }
     __syncthreads();
-  }
+  };
 
   // ---- phase 1: logits
   constexpr bool kTensor = !std::is_same<T, float>::value;
   bool used_mma = false;
   if constexpr (kTensor) {
-    if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax); used_mma = true; }
-    else if (p.Rq <= 16) { logits_mma<T, 2>(p, ji, lg, wmax); used_mma = true; }
-    else if (p.Rq <= 24) { logits_mma<T, 3>(p, ji, lg, wmax); used_mma = true; }
-    else if (p.Rq <= 32) { logits_mma<T, 4>(p, ji, lg, wmax); used_mma = true; }
-    else if (p.Rq <= 40) { logits_mma<T, 5>(p, ji, lg, wmax); used_mma = true; }
+    if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
+    else if (p.Rq <= 16) { logits_mma<T, 2>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
+    else if (p.Rq <= 24) { logits_mma<T, 3>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
+    else if (p.Rq <= 32) { logits_mma<T, 4>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
+    else if (p.Rq <= 40) { logits_mma<T, 5>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
   }
   if (!used_mma) {
+    stage_pages();
     float* sk = sq + p.Rq * kD;
     logits_fma<T>(p, ji, lg, wmax, sq, sk);
   }

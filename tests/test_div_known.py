@@ -8,9 +8,10 @@ IEEE division, so the replacement must agree bit for bit on the operands the
 kernels feed it:
 
 * logits of 16-bit models: every bf16 and f16 value divided by
-  float32(sqrt(128)); operands with |x| < 2^-120 (quotient near or below the
-  subnormal range) are sent to IEEE division by the kernel, so they are
-  excluded here;
+  float32(sqrt(128)), the quotient's sign then copied from the operand (which
+  only matters for -0); nonzero operands with |x| < 2^-120 (quotient near or
+  below the subnormal range) are sent to IEEE division by the kernel, so they
+  are excluded here;
 * pooled sums: fp32 values divided by the kernel size 3, 5 or 7 (half-widths
   1..3).  The quotient of a normal x depends only on its significand, so one
   full binade stands for all normal operands; two more binades and every
@@ -38,9 +39,11 @@ def _markstein(x32: np.ndarray, y32: np.float32):
     return res, mid
 
 
-def _check(x32: np.ndarray, y: float) -> None:
+def _check(x32: np.ndarray, y: float, copysign: bool = False) -> None:
     y32 = np.float32(y)
     res, mid = _markstein(x32, y32)
+    if copysign:
+        res = np.copysign(res, x32)
     assert not mid.any(), "float64 emulation hit an fp32 midpoint"
     want = x32 / y32
     bad = res.view(np.uint32) != want.view(np.uint32)
@@ -52,12 +55,14 @@ def _logit_operands(kind: str) -> np.ndarray:
         x = (np.arange(1 << 16, dtype=np.uint32) << 16).view(np.float32)
     else:
         x = np.arange(1 << 16, dtype=np.uint16).view(np.float16).astype(np.float32)
-    return x[np.isfinite(x) & (np.abs(x) >= np.float32(2.0 ** -120))]
+    return x[np.isfinite(x) & ((np.abs(x) >= np.float32(2.0 ** -120)) | (x == 0))]
 
 
 @pytest.mark.parametrize("kind", ["bf16", "f16"])
 def test_logit_scaling_matches_ieee_division(kind):
-    _check(_logit_operands(kind), float(np.float32(np.sqrt(128.0))))
+    x = _logit_operands(kind)
+    assert np.signbit(x[x == 0]).any() and not np.signbit(x[x == 0]).all()  # both zeros are covered
+    _check(x, float(np.float32(np.sqrt(128.0))), copysign=True)
 
 
 @pytest.mark.parametrize("ks", [3.0, 5.0, 7.0])
