@@ -551,8 +551,14 @@ __device__ __forceinline__ int find_bin(const unsigned int* h, unsigned int rem,
   return bin;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(ScoreParams p) {
+// One instantiation per mode: the mode (and, outside prefill, the window of
+// one query per row) are compile-time constants in a local copy of the
+// parameters, so each instantiation carries only its own mode's code.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreParams pin) {
+  ScoreParams p = pin;
+  p.mode = MODE;
+  if constexpr (MODE != MODE_PREFILL) p.W = 1;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq], s_rowR[kMaxRq];
   __shared__ unsigned int s_prefix[kMaxSel], s_mask[kMaxSel], s_rem[kMaxSel], s_k[kMaxSel];
@@ -1216,8 +1222,8 @@ static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq) {
   return w;
 }
 
-template <typename T>
-static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws_bytes, cudaStream_t st) {
+template <typename T, int MODE>
+static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws_bytes, cudaStream_t st) {
   ScoreWs w = score_ws_layout(p.n_jobs, pl, p.Rq);
   if (!ws || ws_bytes < w.total) return HC_ERR_WORKSPACE;
   unsigned char* base = reinterpret_cast<unsigned char*>(ws);
@@ -1231,7 +1237,7 @@ static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws
   p.cpj = pl.cpj;
   p.T = pl.T;
   p.TB = pl.TB;
-  auto kern = score_select_kernel<T>;
+  auto kern = score_select_kernel<T, MODE>;
   // Attribute and occupancy queries are made once per shared-memory size and
   // cached, so a launch issues no non-stream CUDA call (graph capture safe
   // after the first launch of a given shape).
@@ -1273,6 +1279,16 @@ static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return HC_ERR_CUDA;
   return HC_OK;
+}
+
+template <typename T>
+static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws_bytes, cudaStream_t st) {
+  switch (p.mode) {
+    case MODE_PREFILL: return launch_score_mode<T, MODE_PREFILL>(p, pl, ws, ws_bytes, st);
+    case MODE_PIVOT: return launch_score_mode<T, MODE_PIVOT>(p, pl, ws, ws_bytes, st);
+    case MODE_DRIFT: return launch_score_mode<T, MODE_DRIFT>(p, pl, ws, ws_bytes, st);
+    default: return HC_ERR_INVALID;
+  }
 }
 
 template <typename T>
