@@ -635,10 +635,9 @@ template <typename T>
 __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, int nctas) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s_start = reinterpret_cast<int*>(smem_raw);
-  float* s_w = reinterpret_cast<float*>(smem_raw + (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15));
-  float* s_l2 = s_w + nctas;
   __shared__ int s_warp[32];
   __shared__ float s_red[kCThreads / 32];
+  __shared__ float s_mrun;  // running maximum over the rounds of 64 partials
   __shared__ float4 s_acc[kCThreads / 32][kD / 4];
   const int total = row_prefix(p, s_start, s_warp);
   const int span = span_of(total, nctas, p.gran);
@@ -677,60 +676,58 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   // the partials are written by the decode kernel launched just before
   pdl_wait();
   pdl_trigger();  // the next kernel may get resident; it waits for this grid
-  // phase A: one load round for (m, l); weights kept in s_w (m in s_w first)
-  float M = s_new;
-  for (int c = threadIdx.x; c < n; c += kCThreads) {
-    const float2 ml = p.part_ml[(slot0 + c) * p.G + g];
-    s_w[c] = ml.x;
-    s_l2[c] = ml.y;
-    M = fmaxf(M, ml.x);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  if (lane == 0) s_red[warp] = M;
-  __syncthreads();
-  M = s_red[0];
-#pragma unroll
-  for (int w = 1; w < kCThreads / 32; ++w) M = fmaxf(M, s_red[w]);
-  __syncthreads();
-  float L = 0.f;
-  for (int c = threadIdx.x; c < n; c += kCThreads) {
-    const float m = s_w[c];
-    const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
-    s_w[c] = f;
-    L += f * s_l2[c];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-  if (lane == 0) s_red[warp] = L;
-  __syncthreads();
-  const float f_new = has_new ? exp2f(s_new - M) : 0.f;  // the new token's weight (its l is 1)
-  L = f_new;
-#pragma unroll
-  for (int w = 0; w < kCThreads / 32; ++w) L += s_red[w];
-  // phase B: each warp every 8th partial, 8 independent loads in flight
+  // One load round: each warp takes every 8th partial, its lanes a 4-dim
+  // slice of the output row, and the partial's (m, l) (one broadcast load)
+  // with it; then the block maximum, and each warp rescales its own partials.
   constexpr int NW = kCThreads / 32, DEPTH = 8;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int cb = warp; cb < n; cb += NW * DEPTH) {
+  float Lw = 0.f;
+  for (int cb0 = 0; cb0 < n; cb0 += NW * DEPTH) {
     float4 o[DEPTH];
-    float f[DEPTH];
+    float2 ml[DEPTH];
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) {
-      const int c = cb + u * NW;
-      f[u] = c < n ? s_w[c] : 0.f;
-      o[u] = c < n ? *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + 4 * lane)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int c = cb0 + warp + u * NW;
+      const bool ok = c < n;
+      ml[u] = ok ? p.part_ml[(slot0 + c) * p.G + g] : make_float2(-INFINITY, 0.f);
+      o[u] = ok ? *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + 4 * lane)
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float mw = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < DEPTH; ++u) mw = fmaxf(mw, ml[u].x);
+    if (lane == 0) s_red[warp] = mw;
+    __syncthreads();
+    float M = cb0 == 0 ? s_new : s_mrun;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, s_red[w]);
+    // rescale what earlier rounds accumulated (more than 64 partials only)
+    if (cb0 > 0) {
+      const float fo = (s_mrun == -INFINITY) ? 0.f : exp2f(s_mrun - M);
+      acc.x *= fo; acc.y *= fo; acc.z *= fo; acc.w *= fo;
+      Lw *= fo;
     }
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) {
-      acc.x = fmaf(f[u], o[u].x, acc.x);
-      acc.y = fmaf(f[u], o[u].y, acc.y);
-      acc.z = fmaf(f[u], o[u].z, acc.z);
-      acc.w = fmaf(f[u], o[u].w, acc.w);
+      const float f = (ml[u].x == -INFINITY) ? 0.f : exp2f(ml[u].x - M);
+      Lw = fmaf(f, ml[u].y, Lw);
+      acc.x = fmaf(f, o[u].x, acc.x);
+      acc.y = fmaf(f, o[u].y, acc.y);
+      acc.z = fmaf(f, o[u].z, acc.z);
+      acc.w = fmaf(f, o[u].w, acc.w);
     }
+    __syncthreads();  // every warp has read s_red and s_mrun
+    if (threadIdx.x == 0) s_mrun = M;
   }
+  __syncthreads();
+  const float M = s_mrun;
+  if (lane == 0) s_red[warp] = Lw;
   s_acc[warp][lane] = acc;
   __syncthreads();
+  const float f_new = has_new ? exp2f(s_new - M) : 0.f;  // the new token's weight (its l is 1)
+  float L = f_new;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) L += s_red[w];
   if (threadIdx.x < kD) {
     const int d = threadIdx.x;
     float O = f_new * v_new_d;
@@ -767,7 +764,7 @@ template <typename T>
 static int fd_combine(FDParams& p, int grid, cudaStream_t st) {
   // launched as a programmatic dependent of the decode kernel: its CTAs may
   // start early and wait (griddepcontrol.wait) for the partials
-  const size_t csm = (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15) + 2 * (size_t)grid * sizeof(float);
+  const size_t csm = (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.R * p.G);
   cfg.blockDim = dim3(kCThreads);
