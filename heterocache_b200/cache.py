@@ -348,16 +348,17 @@ class HeteroCache(_CacheBase):
         self._wait_append(layer_idx)
         kw = cache_kwargs or {}
         # A caller that passes the step's query (cache_kwargs["query_states"],
-        # as the attention modules of this package do) has the append launch
-        # store it into the drift-check buffer; decode_select then skips its
-        # own copy.
+        # as the attention modules of this package do) has a launch it makes
+        # anyway store it into the drift-check buffer (the page append, or with
+        # a deferred append the attention's combine kernel); decode_select
+        # then skips its own copy.
         q = kw.get("query_states") if self.bsz == 1 else None
         if q is not None:
             self._ensure_decode_state(layer_idx, q)
         if kw.get("defer_append"):
             # attention() attends over the pages plus this token, then appends
             # it on the side stream, off the attention's critical path
-            # [k, v, q, query slot, decode_select of this step already ran]
+            # [k, v, q (None once stored), query slot, decode_select of this step already ran]
             self._pending[layer_idx] = [key_states, value_states, q, self._qcount[layer_idx], False]
             return key_states, value_states
         q_stage = None
@@ -494,12 +495,13 @@ class HeteroCache(_CacheBase):
         pend = self._pending[layer_idx]
         check = self._qcount[layer_idx] + 1 >= S
         if pend is not None:
-            # decode_select before attention (Qwen order): this step's append
-            # is still to come; it stores the query, except that a drift check
-            # now needs it at once
+            # decode_select before attention (Qwen order): this step's
+            # attention is still to come; it stores the query, except that a
+            # drift check now needs it at once
             pend[4] = True
             if check or pend[2] is None:
                 self._qbuf[layer_idx][self._qcount[layer_idx]].copy_(query_states[0, :, 0, :])
+                pend[2] = None  # stored
         elif self._q_staged[layer_idx]:
             self._q_staged[layer_idx] = False  # this step's append stored it
         else:
@@ -515,8 +517,9 @@ class HeteroCache(_CacheBase):
 
     def _drift_and_retrieve(self, layer_idx, jobs, query_states):
         S = self.decode_step
+        # the step's query is in the buffer: stored on this stream by the
+        # attention (deferred append), by the append itself, or just above
         self._wait_retrieval(layer_idx)
-        self._wait_append(layer_idx)  # a deferred append may hold this step's query
         scores = (torch.empty(jobs.n_jobs, S, self.prefill_len, dtype=query_states.dtype,
                               device=query_states.device) if self.record_checks else None)
         ops.drift_check(self._qbuf[layer_idx], self.key_pools[layer_idx], self.block_tables[layer_idx],
@@ -578,22 +581,28 @@ class HeteroCache(_CacheBase):
                                     err=self._err, total_tokens_hint=total)
         self._pending[layer_idx] = None
         k, v, q, slot, selected = pend
+        # the step's query goes to the drift-check buffer on this stream (the
+        # combine kernel stores it when it is the query attended with), so a
+        # drift check right after need not wait for the side-stream append
+        same_q = (q is not None and q.data_ptr() == query_states.data_ptr() and q.shape == query_states.shape
+                  and q.stride() == query_states.stride())
+        if q is not None and not same_q:
+            self._qbuf[layer_idx][slot].copy_(q[0, :, 0, :])
         out = ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
                                self.block_tables[layer_idx], self.heads_len[layer_idx],
                                num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
-                               err=self._err, k_new=k, v_new=v)
+                               err=self._err, k_new=k, v_new=v,
+                               q_stage=self._qbuf[layer_idx][slot] if same_q else None)
         main = torch.cuda.current_stream(self._dev)
         side = self._side()
         side.wait_stream(main)
         with torch.cuda.stream(side):
             ops.decode_append(k, v, self.key_pools[layer_idx], self.value_pools[layer_idx],
                               self.block_tables[layer_idx], self.heads_len[layer_idx], self.free_blocks[layer_idx],
-                              self._free_ptr[layer_idx], self._err, q=q,
-                              q_stage=self._qbuf[layer_idx][slot] if q is not None else None)
+                              self._free_ptr[layer_idx], self._err)
         if not torch.cuda.is_current_stream_capturing():  # a graph's buffers are static
-            for t in (k, v, q):
-                if t is not None:
-                    t.record_stream(side)
+            for t in (k, v):
+                t.record_stream(side)
         ev = torch.cuda.Event()
         ev.record(side)
         self._append_done[layer_idx] = ev

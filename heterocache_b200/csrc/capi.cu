@@ -256,13 +256,14 @@ int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, i
                              int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
                              const int32_t* block_table, int max_blocks, const int32_t* heads_len,
                              const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh, int64_t vn_sb,
-                             int64_t vn_sh, float scale, void* out, void* workspace, size_t workspace_bytes,
-                             int32_t* err_flag, void* stream) {
+                             int64_t vn_sh, float scale, void* out, void* q_stage, void* workspace,
+                             size_t workspace_bytes, int32_t* err_flag, void* stream) {
   if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
   if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || groups <= 0 || max_blocks <= 0)
     return HC_ERR_INVALID;
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out)) return HC_ERR_INVALID;
   if (!k_new || !v_new) return HC_ERR_INVALID;
+  if (q_stage && bsz != 1) return HC_ERR_INVALID;
   if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh)) return HC_ERR_INVALID;
   hc::FDParams p;
   std::memset(&p, 0, sizeof(p));
@@ -288,6 +289,7 @@ int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, i
   p.kn_sh = kn_sh;
   p.vn_sb = vn_sb;
   p.vn_sh = vn_sh;
+  p.q_stage = q_stage;
   return note_cuda(hc::flash_decode_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
 }
 

@@ -649,6 +649,11 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   // q and k_new come from before the decode kernel, which started after they
   // were complete, so they are read ahead of the wait.
   const bool has_new = p.k_new != nullptr;
+  if (p.q_stage && threadIdx.x < kD) {  // the query row into the drift-check buffer
+    const int h = r % p.KV;
+    const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)(h * p.G + g) * p.qsh;
+    reinterpret_cast<T*>(p.q_stage)[(int64_t)(h * p.G + g) * kD + threadIdx.x] = qrow[threadIdx.x];
+  }
   float s_new = -INFINITY, v_new_d = 0.f;
   if (has_new) {
     const int b = r / p.KV, h = r % p.KV;

@@ -92,6 +92,8 @@ struct FDParams {
   const void* k_new;
   const void* v_new;
   int64_t kn_sb, kn_sh, vn_sb, vn_sh;
+  // optional (batch of one): the combine also stores the query rows here [H, D]
+  void* q_stage;
   void* out;
   int32_t* err;
 };

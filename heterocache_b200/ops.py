@@ -155,10 +155,12 @@ def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, fre
 
 
 def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out=None, scale: float = 0.0,
-                 workspace: Workspace, err, total_tokens_hint: int = 0, k_new=None, v_new=None):
+                 workspace: Workspace, err, total_tokens_hint: int = 0, k_new=None, v_new=None, q_stage=None):
     """q: [bsz, H, 1, D] -> out [bsz, H, D] (same dtype).  With k_new/v_new
-    [bsz, KV, 1, D] each row also attends to that token (not in the pages)."""
-    _cuda(q, k_pool, v_pool, block_table, heads_len, err, k_new, v_new)
+    [bsz, KV, 1, D] each row also attends to that token (not in the pages);
+    then q_stage (bsz 1: a contiguous [H, D] buffer) also receives the query
+    rows."""
+    _cuda(q, k_pool, v_pool, block_table, heads_len, err, k_new, v_new, q_stage)
     _rows(q, "q")
     bsz, H, one, D = q.shape
     if one != 1:
@@ -173,12 +175,15 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
         _same_shape(k_new, v_new)
         if tuple(k_new.shape) != (bsz, num_kv_heads, 1, D) or k_new.dtype != q.dtype:
             raise ValueError("heterocache_b200: k_new/v_new must be [bsz, KV, 1, D] in the query dtype")
+        if q_stage is not None and (bsz != 1 or tuple(q_stage.shape) != (H, D) or q_stage.dtype != q.dtype
+                                    or not q_stage.is_contiguous()):
+            raise ValueError("heterocache_b200: q_stage must be a contiguous [H, D] buffer in the query dtype (bsz 1)")
         rc = lib().hc_flash_decode_with_new(dtype_code(q), bsz, num_kv_heads, groups, D, _ptr(q), q.stride(0),
                                             q.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
                                             _ptr(block_table), block_table.shape[1], _ptr(heads_len), _ptr(k_new),
                                             _ptr(v_new), k_new.stride(0), k_new.stride(1), v_new.stride(0),
-                                            v_new.stride(1), float(scale), _ptr(out), _ptr(ws), ws.numel(),
-                                            _ptr(err), _stream(q))
+                                            v_new.stride(1), float(scale), _ptr(out), _ptr(q_stage), _ptr(ws),
+                                            ws.numel(), _ptr(err), _stream(q))
         check("hc_flash_decode_with_new", rc)
         LAUNCHES[0] += 2
         return out

@@ -170,14 +170,19 @@ int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_d
  * k_new/v_new [bsz, KV, 1, D] (batch strides kn_sb / vn_sb, head strides
  * kn_sh / vn_sh); the pages are not written, so the caller appends the token
  * afterwards (hc_decode_append) -- which lets that append run off the
- * attention's critical path.  Arguments otherwise as hc_flash_decode.
+ * attention's critical path.  q_stage: NULL, or (bsz 1 only) a [H,
+ * head_dim] buffer in the query dtype into which the call also stores the
+ * step's query rows -- the decode-step query buffer the drift check reads
+ * (heterocache/cache_utils.py:1011-1017 collects the last decode_step
+ * queries), so the check need not wait for the deferred append.  Arguments
+ * otherwise as hc_flash_decode.
  */
 int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, int head_dim,
                              const void* q, int64_t qsb, int64_t qsh,
                              const void* k_pool, const void* v_pool, int n_pool_blocks,
                              const int32_t* block_table, int max_blocks, const int32_t* heads_len,
                              const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh,
-                             int64_t vn_sb, int64_t vn_sh, float scale, void* out,
+                             int64_t vn_sb, int64_t vn_sh, float scale, void* out, void* q_stage,
                              void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------

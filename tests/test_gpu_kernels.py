@@ -158,6 +158,47 @@ def test_flash_decode_matches_oracle(cuda_device, dtype, geo):
     assert out.view(2, KV, -1)[0, 0].float().abs().max().item() == 0.0
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_flash_decode_with_new_token_and_query_stage(cuda_device, dtype):
+    """The step's token merged from k_new/v_new (not in the pages) equals the
+    oracle over the pages with that token appended; q_stage receives the
+    query rows bit for bit."""
+    geo = LLAMA_8B
+    KV, H, D = geo.num_kv_heads, geo.num_heads, geo.head_dim
+    tdt = DT[dtype]
+    dev = cuda_device
+    lens = [0, 1, 255, 256, 4099, 30000, 777, 12]
+    q, kp, vp, bt, hl = _random_paged(lens, geo, tdt, dev, seed=11)
+    g = torch.Generator().manual_seed(12)
+    kn = torch.randn(1, KV, 1, D, generator=g).to(tdt)
+    vn = torch.randn(1, KV, 1, D, generator=g).to(tdt)
+    stage = torch.zeros(H, D, dtype=tdt, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    out = ops.flash_decode(q.to(dev), kp.to(dev), vp.to(dev), bt.to(dev), hl.to(dev), num_kv_heads=KV,
+                           workspace=Workspace(dev), err=err, k_new=kn.to(dev), v_new=vn.to(dev), q_stage=stage)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(stage.cpu(), q[0, :, 0, :])
+    # oracle: the token written after each row's last page token (a fresh page
+    # where the row's pages are full)
+    n_extra = sum(1 for l in lens if l % 256 == 0)
+    kp2 = torch.cat([kp, torch.zeros(n_extra, *kp.shape[1:], dtype=tdt)])
+    vp2 = torch.cat([vp, torch.zeros(n_extra, *vp.shape[1:], dtype=tdt)])
+    bt2 = torch.cat([bt, torch.full((bt.shape[0], 1), -1, dtype=torch.int32)], dim=1)
+    nxt = kp.shape[0]
+    for r, l in enumerate(lens):
+        page, off = l // 256, l % 256
+        if off == 0:
+            bt2[r, page] = nxt
+            nxt += 1
+        blk = int(bt2[r, page])
+        kp2[blk, off, 0] = kn[0, r, 0]
+        vp2[blk, off, 0] = vn[0, r, 0]
+    ref = paged_attention(q, kp2, vp2, bt2, hl + 1, KV)
+    diff = (out.float().cpu() - ref).abs().max().item()
+    assert diff <= ATOL[dtype], diff
+
+
 def test_flash_decode_strided_query(cuda_device):
     """Queries as the attention layer produces them: a transposed projection view."""
     geo = LLAMA_8B
