@@ -201,6 +201,9 @@ __global__ void __launch_bounds__(kAppendThreads) decode_append_kernel(
 
 // ---------------------------------------------------------------------------
 // Retrieval gather: full tier (device or pinned host memory) -> satellite pages.
+// One CTA copies 64 rows of one member, K and V; each thread one 16-byte
+// chunk of NP rows: all position loads, then all row loads, then the stores
+// (two dependent load rounds per CTA).
 template <typename T>
 __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict__ member_job,
                                                        const int32_t* __restrict__ member_head,
@@ -210,8 +213,13 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
                                                        const T* full_k, const T* full_v, int64_t fsh, int64_t fst,
                                                        T* k_pool, T* v_pool, int n_blocks,
                                                        const int32_t* __restrict__ bt, int max_blocks, int32_t* err) {
-  constexpr int CH = kD * sizeof(T) / 16;
-  constexpr int RPP = 256 / CH;
+  constexpr int CH = kD * sizeof(T) / 16;  // 16-byte chunks per row
+  constexpr int RPP = 256 / CH;            // rows per pass of the CTA
+  constexpr int NP = 64 / RPP;             // passes (rows per thread)
+  // programmatic dependent launch: the trigger and positions come from the
+  // drift check just before; the next kernel may get resident meanwhile
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.y;
   const int job = member_job[m];
   if (!trigger[job]) return;
@@ -224,17 +232,38 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
     return;
   }
   const int c = threadIdx.x % CH;
-  const int i0 = blockIdx.x * 64;
-  for (int i = i0 + threadIdx.x / CH; i < min(n, i0 + 64); i += RPP) {
-    const int pos = positions[(size_t)job * pos_stride + i];
-    if (pos < 0) {
+  const int i0 = blockIdx.x * 64 + threadIdx.x / CH;
+  int pos[NP];
+  unsigned int rows = 0u;  // bit u: row i0 + u*RPP is one of the member's
+#pragma unroll
+  for (int u = 0; u < NP; ++u) {
+    const int i = i0 + u * RPP;
+    pos[u] = -1;
+    if (i < n) {
+      pos[u] = positions[(size_t)job * pos_stride + i];
+      rows |= 1u << u;
+    }
+  }
+  uint4 kr[NP], vr[NP];
+#pragma unroll
+  for (int u = 0; u < NP; ++u) {
+    if (pos[u] >= 0) {
+      const int64_t src = (int64_t)h * fsh + (int64_t)pos[u] * fst;
+      kr[u] = reinterpret_cast<const uint4*>(full_k + src)[c];
+      vr[u] = reinterpret_cast<const uint4*>(full_v + src)[c];
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < NP; ++u) {
+    const int i = i0 + u * RPP;
+    if (!((rows >> u) & 1u)) continue;
+    if (pos[u] < 0) {
       if (c == 0) set_err(err, HC_ERR_RANGE);
       continue;
     }
-    const int64_t src = (int64_t)h * fsh + (int64_t)pos * fst;
     const int64_t dst = ((int64_t)start * kPage + i) * kD;
-    reinterpret_cast<uint4*>(k_pool + dst)[c] = reinterpret_cast<const uint4*>(full_k + src)[c];
-    reinterpret_cast<uint4*>(v_pool + dst)[c] = reinterpret_cast<const uint4*>(full_v + src)[c];
+    reinterpret_cast<uint4*>(k_pool + dst)[c] = kr[u];
+    reinterpret_cast<uint4*>(v_pool + dst)[c] = vr[u];
   }
 }
 
@@ -312,10 +341,18 @@ static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const
                       int64_t fsh, int64_t fst, void* kp, void* vp, int nb, const int32_t* bt, int mb, int32_t* err,
                       cudaStream_t s) {
   if (n_members == 0 || max_len <= 0) return HC_OK;
-  dim3 grid((max_len + 63) / 64, n_members);
-  retrieve_kernel<T><<<grid, 256, 0, s>>>(mj, mh, ml, trig, pos, pos_stride, (const T*)fk, (const T*)fv, fsh, fst,
-                                          (T*)kp, (T*)vp, nb, bt, mb, err);
-  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((max_len + 63) / 64, n_members);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, retrieve_kernel<T>, mj, mh, ml, trig, pos, pos_stride, (const T*)fk,
+                                           (const T*)fv, fsh, fst, (T*)kp, (T*)vp, nb, bt, mb, err);
+  return e == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
 int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,
