@@ -348,11 +348,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+// The K/V stream is read with the evict-first L2 policy (l2_evict_first_policy).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-      "[%4];\n" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%2, %3}], [%4], %5;\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 // Address of 16-byte chunk `chunk` (0..15 over the 128 dims) of tile row
@@ -505,6 +507,7 @@ __global__ void __launch_bounds__(kTThreads, 2)
     if (lane == 0) {
       int r = r0, issued = 0;
       bool dead = false;
+      const uint64_t pol = l2_evict_first_policy();
       for (int i = 0; i < ntiles; ++i) {
         const int s = i % kTStages;
         if (!mbar_wait(&empty_bar[s], ((i / kTStages) & 1) ^ 1)) {
@@ -527,10 +530,10 @@ __global__ void __launch_bounds__(kTThreads, 2)
         const int y = blk * kPage + (t & (kPage - 1));
         unsigned char* dst = stages + (size_t)s * kStageBytes;
         mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
-        tma_load_2d(dst, &tmk, 0, y, &full_bar[s]);
-        tma_load_2d(dst + kTBox, &tmk, 64, y, &full_bar[s]);
-        tma_load_2d(dst + 2 * kTBox, &tmv, 0, y, &full_bar[s]);
-        tma_load_2d(dst + 3 * kTBox, &tmv, 64, y, &full_bar[s]);
+        tma_load_2d(dst, &tmk, 0, y, &full_bar[s], pol);
+        tma_load_2d(dst + kTBox, &tmk, 64, y, &full_bar[s], pol);
+        tma_load_2d(dst + 2 * kTBox, &tmv, 0, y, &full_bar[s], pol);
+        tma_load_2d(dst + 3 * kTBox, &tmv, 64, y, &full_bar[s], pol);
         issued = i + 1;
       }
       if (dead) {  // let the copies this CTA issued land before it exits

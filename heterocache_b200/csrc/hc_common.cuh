@@ -143,6 +143,22 @@ __device__ __forceinline__ uint4 ldg128(const void* p) { return __ldg(reinterpre
 __device__ __forceinline__ uint2 ldg64(const void* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
 
 // Streaming load that does not allocate in L1 (data read once).
+// L2 policy for data read once per step and larger than L2 (key/value
+// streams): its lines are evicted first, so that it does not push the
+// kernels' code, page tables and scratch out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+// Streaming load with an L2 policy (l2_evict_first_policy).
+__device__ __forceinline__ uint4 ld_stream128(const void* p, uint64_t pol) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p), "l"(pol));
+  return r;
+}
 __device__ __forceinline__ uint4 ld_stream128(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"

@@ -245,12 +245,13 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
     }
   }
   uint4 kr[NP], vr[NP];
+  const uint64_t pol = l2_evict_first_policy();  // full-tier rows are read once
 #pragma unroll
   for (int u = 0; u < NP; ++u) {
     if (pos[u] >= 0) {
       const int64_t src = (int64_t)h * fsh + (int64_t)pos[u] * fst;
-      kr[u] = reinterpret_cast<const uint4*>(full_k + src)[c];
-      vr[u] = reinterpret_cast<const uint4*>(full_v + src)[c];
+      kr[u] = ld_stream128(reinterpret_cast<const uint4*>(full_k + src) + c, pol);
+      vr[u] = ld_stream128(reinterpret_cast<const uint4*>(full_v + src) + c, pol);
     }
   }
 #pragma unroll

@@ -204,6 +204,7 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
     if (qi < p.Rq) st_valid |= 1u << nt;
   }
   const uint32_t st_dummy = smem_u32(dummy);
+  const uint64_t pol = l2_evict_first_policy();  // the keys are read once
   for (int tg = lo + warp * 16; tg < hi; tg += kSWarps * 16) {
     const int ta = min(tg + gid, p.L - 1), tb = min(tg + gid + 8, p.L - 1);
     const T* ra = key_row<T>(p, ji, ta);
@@ -211,8 +212,8 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
     uint4 ka[4], kb[4];
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
-      ka[s] = ld_stream128(ra + 32 * s + 8 * tig);
-      kb[s] = ld_stream128(rb + 32 * s + 8 * tig);
+      ka[s] = ld_stream128(ra + 32 * s + 8 * tig, pol);
+      kb[s] = ld_stream128(rb + 32 * s + 8 * tig, pol);
     }
     float acc[NT][4];
 #pragma unroll
