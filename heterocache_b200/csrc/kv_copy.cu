@@ -201,9 +201,11 @@ __global__ void __launch_bounds__(kAppendThreads) decode_append_kernel(
 
 // ---------------------------------------------------------------------------
 // Retrieval gather: full tier (device or pinned host memory) -> satellite pages.
-// One CTA copies 64 rows of one member, K and V; each thread one 16-byte
-// chunk of NP rows: all position loads, then all row loads, then the stores
-// (two dependent load rounds per CTA).
+// Work items of 64 rows of one member, K and V, taken by a grid of at most
+// one wave that strides over them (members whose pivot did not trigger cost
+// one check per item, not a CTA launch each).  In an item each thread copies
+// one 16-byte chunk of NP rows: all position loads, then all row loads, then
+// the stores (two dependent load rounds).
 template <typename T>
 __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict__ member_job,
                                                        const int32_t* __restrict__ member_head,
@@ -212,7 +214,8 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
                                                        const int32_t* __restrict__ positions, int pos_stride,
                                                        const T* full_k, const T* full_v, int64_t fsh, int64_t fst,
                                                        T* k_pool, T* v_pool, int n_blocks,
-                                                       const int32_t* __restrict__ bt, int max_blocks, int32_t* err) {
+                                                       const int32_t* __restrict__ bt, int max_blocks, int32_t* err,
+                                                       int n_members, int items_per_member) {
   constexpr int CH = kD * sizeof(T) / 16;  // 16-byte chunks per row
   constexpr int RPP = 256 / CH;            // rows per pass of the CTA
   constexpr int NP = 64 / RPP;             // passes (rows per thread)
@@ -220,51 +223,55 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
   // drift check just before; the next kernel may get resident meanwhile
   pdl_wait();
   pdl_trigger();
-  const int m = blockIdx.y;
-  const int job = member_job[m];
-  if (!trigger[job]) return;
-  const int n = member_len[m];
-  const int h = member_head[m];
-  const int start = bt[(int64_t)h * max_blocks];
-  if (start < 0) return;
-  if ((int64_t)start * kPage + n > (int64_t)n_blocks * kPage) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) set_err(err, HC_ERR_RANGE);
-    return;
-  }
-  const int c = threadIdx.x % CH;
-  const int i0 = blockIdx.x * 64 + threadIdx.x / CH;
-  int pos[NP];
-  unsigned int rows = 0u;  // bit u: row i0 + u*RPP is one of the member's
-#pragma unroll
-  for (int u = 0; u < NP; ++u) {
-    const int i = i0 + u * RPP;
-    pos[u] = -1;
-    if (i < n) {
-      pos[u] = positions[(size_t)job * pos_stride + i];
-      rows |= 1u << u;
-    }
-  }
-  uint4 kr[NP], vr[NP];
   const uint64_t pol = l2_evict_first_policy();  // full-tier rows are read once
-#pragma unroll
-  for (int u = 0; u < NP; ++u) {
-    if (pos[u] >= 0) {
-      const int64_t src = (int64_t)h * fsh + (int64_t)pos[u] * fst;
-      kr[u] = ld_stream128(reinterpret_cast<const uint4*>(full_k + src) + c, pol);
-      vr[u] = ld_stream128(reinterpret_cast<const uint4*>(full_v + src) + c, pol);
-    }
-  }
-#pragma unroll
-  for (int u = 0; u < NP; ++u) {
-    const int i = i0 + u * RPP;
-    if (!((rows >> u) & 1u)) continue;
-    if (pos[u] < 0) {
-      if (c == 0) set_err(err, HC_ERR_RANGE);
+  const int n_items = n_members * items_per_member;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int m = item / items_per_member, blk = item % items_per_member;
+    const int job = member_job[m];
+    if (!trigger[job]) continue;
+    const int n = member_len[m];
+    if (blk * 64 >= n) continue;
+    const int h = member_head[m];
+    const int start = bt[(int64_t)h * max_blocks];
+    if (start < 0) continue;
+    if ((int64_t)start * kPage + n > (int64_t)n_blocks * kPage) {
+      if (threadIdx.x == 0 && blk == 0) set_err(err, HC_ERR_RANGE);
       continue;
     }
-    const int64_t dst = ((int64_t)start * kPage + i) * kD;
-    reinterpret_cast<uint4*>(k_pool + dst)[c] = kr[u];
-    reinterpret_cast<uint4*>(v_pool + dst)[c] = vr[u];
+    const int c = threadIdx.x % CH;
+    const int i0 = blk * 64 + threadIdx.x / CH;
+    int pos[NP];
+    unsigned int rows = 0u;  // bit u: row i0 + u*RPP is one of the member's
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int i = i0 + u * RPP;
+      pos[u] = -1;
+      if (i < n) {
+        pos[u] = positions[(size_t)job * pos_stride + i];
+        rows |= 1u << u;
+      }
+    }
+    uint4 kr[NP], vr[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      if (pos[u] >= 0) {
+        const int64_t src = (int64_t)h * fsh + (int64_t)pos[u] * fst;
+        kr[u] = ld_stream128(reinterpret_cast<const uint4*>(full_k + src) + c, pol);
+        vr[u] = ld_stream128(reinterpret_cast<const uint4*>(full_v + src) + c, pol);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int i = i0 + u * RPP;
+      if (!((rows >> u) & 1u)) continue;
+      if (pos[u] < 0) {
+        if (c == 0) set_err(err, HC_ERR_RANGE);
+        continue;
+      }
+      const int64_t dst = ((int64_t)start * kPage + i) * kD;
+      reinterpret_cast<uint4*>(k_pool + dst)[c] = kr[u];
+      reinterpret_cast<uint4*>(v_pool + dst)[c] = vr[u];
+    }
   }
 }
 
@@ -342,8 +349,18 @@ static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const
                       int64_t fsh, int64_t fst, void* kp, void* vp, int nb, const int32_t* bt, int mb, int32_t* err,
                       cudaStream_t s) {
   if (n_members == 0 || max_len <= 0) return HC_OK;
+  // one wave: 8 CTAs of 256 threads per SM
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const int per_member = (max_len + 63) / 64;
+  const long long items = (long long)per_member * n_members;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((max_len + 63) / 64, n_members);
+  cfg.gridDim = dim3((unsigned)(items < 8LL * sms ? items : 8LL * sms));
   cfg.blockDim = dim3(256);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -351,8 +368,10 @@ static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (items > 0x7fffffffLL) return HC_ERR_UNSUPPORTED;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, retrieve_kernel<T>, mj, mh, ml, trig, pos, pos_stride, (const T*)fk,
-                                           (const T*)fv, fsh, fst, (T*)kp, (T*)vp, nb, bt, mb, err);
+                                           (const T*)fv, fsh, fst, (T*)kp, (T*)vp, nb, bt, mb, err, n_members,
+                                           per_member);
   return e == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
