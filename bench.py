@@ -205,7 +205,10 @@ def flash_decode_bytes(cache, layers):
 def time_kernels(cache, layers, reps=5):
     """Per-launch durations from CUDA events around graph replays that contain
     only one kind of launch for every layer: the flash-decode (decode +
-    combine kernels) and the drift check.  Same stream, same data as the run."""
+    combine kernels), the drift check and the satellite retrieval.  Same
+    stream, same data as the run."""
+    from heterocache_b200 import ops
+
     dev = cache._dev
     outs = [torch.empty(1, H, D, dtype=torch.bfloat16, device=dev) for _ in range(layers)]
     q = torch.randn(layers, 1, H, 1, D, device=dev).to(torch.bfloat16)
@@ -220,8 +223,25 @@ def time_kernels(cache, layers, reps=5):
             if jobs is not None and jobs.n_jobs:
                 cache._drift_and_retrieve(l, jobs, q[l])
 
+    # satellite retrieval alone, trigger forced on, positions of the last drift
+    # check: every member copies its num_tokens rows (K and V)
+    forced = {l: torch.ones_like(cache._jobs[l].trigger) for l in range(layers)
+              if cache._jobs[l] is not None and cache._jobs[l].member_job.numel()}
+
+    def retrieve():
+        for l, trig in forced.items():
+            jobs = cache._jobs[l]
+            ops.retrieve(member_job=jobs.member_job, member_head=jobs.member_head, member_len=jobs.member_len,
+                         max_member_len=jobs.max_member_len, trigger=trig,
+                         retrieve_positions=jobs.retrieve_positions, full_k=cache.key_cache_cpu[l],
+                         full_v=cache.value_cache_cpu[l], k_pool=cache.key_pools[l], v_pool=cache.value_pools[l],
+                         block_table=cache.block_tables[l], num_kv_heads=cache.num_kv_heads, err=cache._err)
+
     res = {}
-    for name, fn in (("flash_decode", attn), ("drift_check", drift)):
+    per_fn = {"flash_decode": layers, "drift_check": layers, "retrieve": max(len(forced), 1)}
+    for name, fn in (("flash_decode", attn), ("drift_check", drift), ("retrieve", retrieve)):
+        if name == "retrieve" and not forced:
+            continue
         fn()
         cache.join_retrievals()
         torch.cuda.synchronize()
@@ -237,11 +257,14 @@ def time_kernels(cache, layers, reps=5):
             g.replay()
         e1.record()
         torch.cuda.synchronize()
-        res[name] = e0.elapsed_time(e1) / (reps * layers)
+        res[name] = e0.elapsed_time(e1) / (reps * per_fn[name])
         del g
     bytes_per = [int(cache._hlen[l].sum()) * D * 2 * 2 + 2 * H * D * 2 for l in range(layers)]
     drift_bytes = [cache.prefill_len * D * 2 * (cache._jobs[l].n_jobs if cache._jobs[l] is not None else 0)
                    for l in range(layers)]
+    # read + write of K and V rows
+    ret_bytes = [int(cache._jobs[l].member_len.sum()) * D * 2 * 2 * 2 for l in forced]
+    res["retrieve_bytes"] = float(np.mean(ret_bytes)) if ret_bytes else 0.0
     return res, float(np.mean(bytes_per)), float(np.mean(drift_bytes))
 
 
@@ -421,6 +444,15 @@ def run_ours(args, rank, world, local_rank):
             "drift_check": {"avg_launch_us": kt["drift_check"] * 1e3,
                             "algorithmic_bytes_per_launch": drift_bytes,
                             "achieved_gbs": drift_bytes / (kt["drift_check"] * 1e-3) / 1e9}}
+    if "retrieve" in kt:
+        host = bool(getattr(args, "host_tier", False))
+        # host tier: the bytes that cross the host link (the reads)
+        rb = kt["retrieve_bytes"] / (2 if host else 1)
+        rg = rb / (kt["retrieve"] * 1e-3) / 1e9
+        roof["retrieve"] = {"avg_launch_us": kt["retrieve"] * 1e3, "trigger": "forced on",
+                            "algorithmic_bytes_per_launch": rb, "achieved_gbs": rg,
+                            "bound": "host link (pinned-host tier read)" if host else "hbm",
+                            "frac": None if host else rg / peak}
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, graph, qs, ks, vs, dev, world)
