@@ -54,6 +54,10 @@ SIGNATURES = {
     "hc_retrieve": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                             c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                             c_int, c_void_p, c_int, c_void_p, c_void_p]),
+    "hc_retrieve_delta": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64,
+                                  c_int64, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                  c_void_p, c_int64, c_void_p, c_void_p]),
 }
 
 _LIB = None

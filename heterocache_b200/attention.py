@@ -40,6 +40,18 @@ except Exception:  # pragma: no cover
         return q * cos + rot(q) * sin, k * cos + rot(k) * sin
 
 
+def _causal_attention(q, k, v, groups: int, scale: float) -> torch.Tensor:
+    """Causal attention over the uncompressed prompt.  K/V heads are expanded
+    to the query heads, so every SDPA backend (flash attention for long
+    prompts) can take it, not only those that accept grouped-query inputs."""
+    if groups > 1 and q.shape[-2] > 1:
+        k = k.repeat_interleave(groups, dim=1)
+        v = v.repeat_interleave(groups, dim=1)
+        return F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale)
+    return F.scaled_dot_product_attention(q, k, v, is_causal=q.shape[-2] > 1, scale=scale,
+                                          enable_gqa=groups > 1)
+
+
 class _HeteroAttention(nn.Module):
     decode_select_before_attention = False
     qkv_bias = False
@@ -92,8 +104,7 @@ class _HeteroAttention(nn.Module):
                 k, v = cache.update(k, v, self.layer_idx, {"cache_position": cache_position})
                 cache.init_coefficient(q, k, self.layer_idx)
                 cache.prefill_select(q, k, v, self.layer_idx)
-            out = F.scaled_dot_product_attention(q, k, v, is_causal=q_len > 1, scale=self.scaling,
-                                                 enable_gqa=self.num_key_value_groups > 1)
+            out = _causal_attention(q, k, v, self.num_key_value_groups, self.scaling)
             out = out.transpose(1, 2).reshape(bsz, q_len, -1).contiguous()
             return self.o_proj(out), None
         # the query rides along so the page-append launch also stores it for

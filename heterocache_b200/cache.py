@@ -119,6 +119,8 @@ class _LayerJobs:
         self.member_job = torch.tensor(m_job, **i32)
         self.member_head = torch.tensor(m_head, **i32)
         self.member_len = torch.tensor(m_len, **i32)
+        self.m_head_list, self.m_len_list = list(m_head), list(m_len)
+        self.delta = None  # slot maps of the delta retrieval (pinned-host tier)
         self.trigger = torch.zeros(max(self.n_jobs, 1), **i32)
         self.retrieve_positions = torch.zeros(max(self.n_jobs, 1), max(self.max_len_cap, 1), **i32)
         self.coeffs = None
@@ -184,6 +186,10 @@ class HeteroCache(_CacheBase):
         self._pending: List = [None] * n
         self._append_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._jobs: List[Optional[_LayerJobs]] = [None] * n
+        # pinned-host tier: prefill kept indices (until the layer's slot maps
+        # are built) and the retrieval staging area shared by all layers
+        self._kept: List[Optional[tuple]] = [None] * n
+        self._stage: Optional[tuple] = None
         self._retrieve_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._side_stream: Optional[torch.cuda.Stream] = None
         # host mirrors of deterministic bookkeeping
@@ -432,9 +438,13 @@ class HeteroCache(_CacheBase):
         dev = key_states.device
         keep_dev = keep_lens.to(device=dev, dtype=torch.int32)
         scores = idx = None
+        # a pinned-host tier keeps the satellites' kept indices: they seed the
+        # slot maps of the delta retrieval
+        keep_idx = self.real_offload and any(self.data["leader_member_relations"][layer_idx].values())
+        if self.record_checks or keep_idx:
+            idx = torch.empty(bsz, nc, max_k, dtype=torch.int32, device=dev)
         if self.record_checks:
             scores = torch.empty(bsz, nc, L, dtype=key_states.dtype, device=dev)
-            idx = torch.empty(bsz, nc, max_k, dtype=torch.int32, device=dev)
             self.recorded[("prefill_scores", layer_idx)] = scores
             self.recorded[("prefill_indices", layer_idx)] = idx
             self.recorded[("keep_lens", layer_idx)] = keep_lens.clone()
@@ -447,6 +457,8 @@ class HeteroCache(_CacheBase):
         kl = keep_lens.numpy().astype(np.int64)
         for b in range(bsz):
             self._hlen[layer_idx][b * self.num_kv_heads:b * self.num_kv_heads + nc] = kl
+        if keep_idx:
+            self._kept[layer_idx] = (idx, kl.copy())
 
     # ------------------------------------------------------------------
     def _ensure_decode_state(self, layer_idx, query_states) -> None:
@@ -467,6 +479,40 @@ class HeteroCache(_CacheBase):
                 jobs.coeffs = torch.zeros(max(jobs.n_jobs, 1), S, dtype=torch.float32, device=query_states.device)
                 jobs.median = torch.zeros(max(jobs.n_jobs, 1), dtype=torch.float64, device=query_states.device)
             self._jobs[layer_idx] = jobs
+            if self.real_offload and jobs.member_job.numel() and self._kept[layer_idx] is not None:
+                self._init_delta(layer_idx, jobs)
+
+    def _init_delta(self, layer_idx, jobs) -> None:
+        """Slot maps of the delta retrieval (pinned-host tier).  Member i holds
+        its prefill kept indices in slots [0, R_i), R_i = min(its prefill keep
+        length, its retrieval length): decode appends start at the keep length,
+        so only prefill selection and retrieval write those slots, and each
+        writes them in ascending position order."""
+        idx, kl = self._kept[layer_idx]
+        self._kept[layer_idx] = None
+        dev = idx.device
+        nc = idx.shape[1]
+        reuse = [min(int(kl[h]), n) if h < nc else 0 for h, n in zip(jobs.m_head_list, jobs.m_len_list)]
+        slot = torch.zeros(len(reuse), max(max(reuse), 1), dtype=torch.int32, device=dev)
+        for i, (h, r) in enumerate(zip(jobs.m_head_list, reuse)):
+            if r:
+                slot[i, :r].copy_(idx[0, h, :r])
+        offs = np.concatenate([[0], np.cumsum(jobs.m_len_list)[:-1]]).astype(np.int64)
+        i32 = dict(dtype=torch.int32, device=dev)
+        jobs.delta = {"slot": slot, "reuse": torch.tensor(reuse, **i32), "off": torch.tensor(offs, **i32)}
+        if self._stage is None:
+            # one staging area for every layer (their retrievals run in order
+            # on the side stream), sized for the largest layer
+            rows = 0
+            for l in range(self.num_layers):
+                alloc = self.data["allocation_matrix"][l]
+                rows = max(rows, sum(min(int(self.base_compress_len * alloc[m]), self.prefill_len)
+                                     for members in self.data["leader_member_relations"][l].values()
+                                     for m in members))
+            dt = self.key_pools[layer_idx].dtype
+            D = self.key_pools[layer_idx].shape[-1]
+            self._stage = (torch.empty(rows, D, dtype=dt, device=dev), torch.empty(rows, D, dtype=dt, device=dev),
+                           torch.empty(rows, **i32))
 
     def prepare_decode(self, layers, query_example) -> None:
         """Allocate every layer's decode-time buffers now (before graph capture)."""
@@ -546,12 +592,24 @@ class HeteroCache(_CacheBase):
             main = torch.cuda.current_stream(self._dev)
             side = self._side()
             side.wait_stream(main)
-            ops.retrieve(member_job=jobs.member_job, member_head=jobs.member_head, member_len=jobs.member_len,
-                         max_member_len=jobs.max_member_len, trigger=jobs.trigger,
-                         retrieve_positions=jobs.retrieve_positions, full_k=full_k, full_v=full_v,
-                         k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
-                         block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
-                         err=self._err, stream=side)
+            if jobs.delta is not None:
+                # only rows the satellites do not hold cross the host link
+                sk, sv, ss = self._stage
+                ops.retrieve_delta(member_job=jobs.member_job, member_head=jobs.member_head,
+                                   member_len=jobs.member_len, member_stage_offset=jobs.delta["off"],
+                                   reuse_len=jobs.delta["reuse"], max_member_len=jobs.max_member_len,
+                                   trigger=jobs.trigger, retrieve_positions=jobs.retrieve_positions,
+                                   slot_positions=jobs.delta["slot"], full_k=full_k, full_v=full_v,
+                                   k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
+                                   block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
+                                   stage_k=sk, stage_v=sv, stage_src=ss, err=self._err, stream=side)
+            else:
+                ops.retrieve(member_job=jobs.member_job, member_head=jobs.member_head, member_len=jobs.member_len,
+                             max_member_len=jobs.max_member_len, trigger=jobs.trigger,
+                             retrieve_positions=jobs.retrieve_positions, full_k=full_k, full_v=full_v,
+                             k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
+                             block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
+                             err=self._err, stream=side)
             ev = torch.cuda.Event()
             ev.record(side)
             self._retrieve_done[layer_idx] = ev

@@ -411,4 +411,28 @@ int hc_retrieve(int dtype, int num_kv_heads, int head_dim, int n_members, const 
                                          (cudaStream_t)stream));
 }
 
+int hc_retrieve_delta(int dtype, int num_kv_heads, int head_dim, int n_members, const int32_t* member_job,
+                      const int32_t* member_head, const int32_t* member_len, const int32_t* member_stage_offset,
+                      const int32_t* reuse_len, int max_member_len, const int32_t* trigger,
+                      const int32_t* retrieve_positions, int retrieve_stride, int32_t* slot_positions,
+                      int slot_stride, const void* full_k, const void* full_v, int64_t fsh, int64_t fst,
+                      void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks,
+                      void* stage_k, void* stage_v, int32_t* stage_src, int64_t stage_rows, int32_t* err_flag,
+                      void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || num_kv_heads <= 0 || n_members < 0 || max_blocks <= 0 || slot_stride < 0 ||
+      stage_rows < 0)
+    return HC_ERR_INVALID;
+  if (n_members == 0) return HC_OK;
+  if (!aligned16(full_k) || !aligned16(full_v) || !aligned16(k_pool) || !aligned16(v_pool) ||
+      !aligned16(stage_k) || !aligned16(stage_v))
+    return HC_ERR_INVALID;
+  if (!stride_ok(dtype, fsh) || !stride_ok(dtype, fst)) return HC_ERR_INVALID;
+  return note_cuda(hc::retrieve_delta_dispatch(dtype, member_job, member_head, member_len, member_stage_offset,
+                                               reuse_len, n_members, max_member_len, trigger, retrieve_positions,
+                                               retrieve_stride, slot_positions, slot_stride, full_k, full_v, fsh, fst,
+                                               k_pool, v_pool, n_pool_blocks, block_table, max_blocks, stage_k,
+                                               stage_v, stage_src, stage_rows, err_flag, (cudaStream_t)stream));
+}
+
 }  // extern "C"

@@ -116,4 +116,11 @@ int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t
                       int64_t fsh, int64_t fst, void* kp, void* vp, int nblocks, const int32_t* bt, int mb,
                       int32_t* err, cudaStream_t s);
 
+int retrieve_delta_dispatch(int dtype, const int32_t* mj, const int32_t* mh, const int32_t* ml, const int32_t* moff,
+                            const int32_t* reuse, int n_members, int max_len, const int32_t* trig, const int32_t* pos,
+                            int pos_stride, int32_t* slot_pos, int slot_stride, const void* fk, const void* fv,
+                            int64_t fsh, int64_t fst, void* kp, void* vp, int nb, const int32_t* bt, int mb,
+                            void* stage_k, void* stage_v, int32_t* stage_src, int64_t stage_rows, int32_t* err,
+                            cudaStream_t s);
+
 }  // namespace hc

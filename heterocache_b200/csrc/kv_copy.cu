@@ -276,6 +276,198 @@ __global__ void __launch_bounds__(256) retrieve_kernel(const int32_t* __restrict
 }
 
 // ---------------------------------------------------------------------------
+// Delta retrieval (pinned-host tier).  Same result as retrieve_kernel, but
+// rows a satellite already holds are copied on the device and only the other
+// rows cross the host link.  Each member m keeps a slot map: slot_pos[m][i] is
+// the full-tier position held in slot i, for i < reuse_len[m].  Those slots lie
+// below the satellite's prefill keep length, which only prefill selection and
+// retrieval write (decode appends start at that length), so the map stays
+// exact.  The map (kept indices, then retrieval lists) and every new list are
+// ascending, so a binary search finds a new position's old slot.
+//   pass 1 (delta_stage_kernel): per new slot i, the old slot holding its
+//     position (or -1) -> stage_src[off[m] + i]; held rows -> staging row
+//     off[m] + i.
+//   pass 2 (delta_write_kernel): every new slot from the staging area or the
+//     tier; then slot_pos[m][i] = new position for i < reuse_len[m].
+// Two launches: a slot can be the source of another slot that overwrites it.
+// Both passes skip the same work items (trigger off, unmapped or out-of-range
+// member), so pass 2 only reads what pass 1 wrote.
+
+// Old slot of `pos` among the ascending old[0, n), or -1.
+__device__ __forceinline__ int find_slot(const int32_t* old, int n, int pos) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(old + mid) < pos) lo = mid + 1;
+    else hi = mid;
+  }
+  return (lo < n && __ldg(old + lo) == pos) ? lo : -1;
+}
+
+struct DeltaArgs {
+  const int32_t* member_job;
+  const int32_t* member_head;
+  const int32_t* member_len;
+  const int32_t* member_off;
+  const int32_t* reuse_len;
+  const int32_t* trigger;
+  const int32_t* positions;
+  int pos_stride;
+  int32_t* slot_pos;
+  int slot_stride;
+  const void* full_k;
+  const void* full_v;
+  int64_t fsh, fst;
+  void* k_pool;
+  void* v_pool;
+  int n_blocks;
+  const int32_t* bt;
+  int max_blocks;
+  void* stage_k;
+  void* stage_v;
+  int32_t* stage_src;
+  int64_t stage_rows;
+  int32_t* err;
+  int n_members, items_per_member;
+};
+
+// Work item -> member geometry; false: nothing to do for this item.  Errors
+// are reported by pass 1 only (pass 2 takes the same decisions).
+struct DeltaItem {
+  int m, job, n, h, start, off, R;
+};
+__device__ __forceinline__ bool delta_item(const DeltaArgs& a, int item, bool report, DeltaItem& it) {
+  it.m = item / a.items_per_member;
+  const int blk = item % a.items_per_member;
+  it.job = a.member_job[it.m];
+  if (!a.trigger[it.job]) return false;
+  it.n = a.member_len[it.m];
+  if (blk * 64 >= it.n) return false;
+  it.h = a.member_head[it.m];
+  it.start = a.bt[(int64_t)it.h * a.max_blocks];
+  if (it.start < 0) return false;
+  it.off = a.member_off[it.m];
+  it.R = min(a.reuse_len[it.m], min(it.n, a.slot_stride));
+  if ((int64_t)it.start * kPage + it.n > (int64_t)a.n_blocks * kPage || it.off < 0 ||
+      (int64_t)it.off + it.n > a.stage_rows) {
+    if (report && threadIdx.x == 0 && blk == 0) set_err(a.err, HC_ERR_RANGE);
+    return false;
+  }
+  return true;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) delta_stage_kernel(const DeltaArgs a) {
+  constexpr int CH = kD * sizeof(T) / 16;  // 16-byte chunks per row
+  constexpr int RPP = 256 / CH;            // rows per pass of the CTA
+  constexpr int NP = 64 / RPP;             // passes (rows per thread)
+  pdl_wait();
+  pdl_trigger();
+  const T* kp = reinterpret_cast<const T*>(a.k_pool);
+  const T* vp = reinterpret_cast<const T*>(a.v_pool);
+  T* sk = reinterpret_cast<T*>(a.stage_k);
+  T* sv = reinterpret_cast<T*>(a.stage_v);
+  const int n_items = a.n_members * a.items_per_member;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    DeltaItem it;
+    if (!delta_item(a, item, true, it)) continue;
+    const int c = threadIdx.x % CH;
+    const int i0 = (item % a.items_per_member) * 64 + threadIdx.x / CH;
+    const int32_t* old = a.slot_pos + (int64_t)it.m * a.slot_stride;
+    int src[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int i = i0 + u * RPP;
+      src[u] = -1;
+      if (i < it.n) {
+        const int pos = a.positions[(size_t)it.job * a.pos_stride + i];
+        if (pos >= 0) src[u] = find_slot(old, it.R, pos);
+      }
+    }
+    uint4 kr[NP], vr[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      if (src[u] >= 0) {
+        const int64_t row = ((int64_t)it.start * kPage + src[u]) * kD;
+        kr[u] = ld_stream128(reinterpret_cast<const uint4*>(kp + row) + c);
+        vr[u] = ld_stream128(reinterpret_cast<const uint4*>(vp + row) + c);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int i = i0 + u * RPP;
+      if (i >= it.n) continue;
+      if (c == 0) a.stage_src[it.off + i] = src[u];
+      if (src[u] >= 0) {
+        const int64_t row = ((int64_t)it.off + i) * kD;
+        reinterpret_cast<uint4*>(sk + row)[c] = kr[u];
+        reinterpret_cast<uint4*>(sv + row)[c] = vr[u];
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) delta_write_kernel(const DeltaArgs a) {
+  constexpr int CH = kD * sizeof(T) / 16;
+  constexpr int RPP = 256 / CH;
+  constexpr int NP = 64 / RPP;
+  pdl_wait();  // pass 1 complete: staging rows, sources and the old map read
+  pdl_trigger();
+  const uint64_t pol = l2_evict_first_policy();  // full-tier rows are read once
+  const T* fk = reinterpret_cast<const T*>(a.full_k);
+  const T* fv = reinterpret_cast<const T*>(a.full_v);
+  const T* sk = reinterpret_cast<const T*>(a.stage_k);
+  const T* sv = reinterpret_cast<const T*>(a.stage_v);
+  T* kp = reinterpret_cast<T*>(a.k_pool);
+  T* vp = reinterpret_cast<T*>(a.v_pool);
+  const int n_items = a.n_members * a.items_per_member;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    DeltaItem it;
+    if (!delta_item(a, item, false, it)) continue;
+    const int c = threadIdx.x % CH;
+    const int i0 = (item % a.items_per_member) * 64 + threadIdx.x / CH;
+    int pos[NP], src[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int i = i0 + u * RPP;
+      pos[u] = -1;
+      src[u] = -1;
+      if (i < it.n) {
+        pos[u] = a.positions[(size_t)it.job * a.pos_stride + i];
+        src[u] = a.stage_src[it.off + i];
+      }
+    }
+    uint4 kr[NP], vr[NP];
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      if (src[u] >= 0) {
+        const int64_t row = ((int64_t)it.off + i0 + u * RPP) * kD;
+        kr[u] = ld_stream128(reinterpret_cast<const uint4*>(sk + row) + c);
+        vr[u] = ld_stream128(reinterpret_cast<const uint4*>(sv + row) + c);
+      } else if (pos[u] >= 0) {
+        const int64_t row = (int64_t)it.h * a.fsh + (int64_t)pos[u] * a.fst;
+        kr[u] = ld_stream128(reinterpret_cast<const uint4*>(fk + row) + c, pol);
+        vr[u] = ld_stream128(reinterpret_cast<const uint4*>(fv + row) + c, pol);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NP; ++u) {
+      const int i = i0 + u * RPP;
+      if (i >= it.n) continue;
+      if (pos[u] < 0) {
+        if (c == 0) set_err(a.err, HC_ERR_RANGE);
+        continue;
+      }
+      const int64_t dst = ((int64_t)it.start * kPage + i) * kD;
+      reinterpret_cast<uint4*>(kp + dst)[c] = kr[u];
+      reinterpret_cast<uint4*>(vp + dst)[c] = vr[u];
+      if (c == 0 && i < it.R) a.slot_pos[(int64_t)it.m * a.slot_stride + i] = pos[u];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 template <typename T>
 static int prefill_keep_t(int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k, const void* v,
                           int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh, int64_t vst, void* kp,
@@ -373,6 +565,74 @@ static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const
                                            (const T*)fv, fsh, fst, (T*)kp, (T*)vp, nb, bt, mb, err, n_members,
                                            per_member);
   return e == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+template <typename T>
+static int retrieve_delta_t(DeltaArgs& a, int max_len, cudaStream_t s) {
+  if (a.n_members == 0 || max_len <= 0) return HC_OK;
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  a.items_per_member = (max_len + 63) / 64;
+  const long long items = (long long)a.items_per_member * a.n_members;
+  if (items > 0x7fffffffLL) return HC_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(items < 8LL * sms ? items : 8LL * sms));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, delta_stage_kernel<T>, a) != cudaSuccess) return HC_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, delta_write_kernel<T>, a) != cudaSuccess) return HC_ERR_CUDA;
+  return HC_OK;
+}
+
+int retrieve_delta_dispatch(int dtype, const int32_t* mj, const int32_t* mh, const int32_t* ml, const int32_t* moff,
+                            const int32_t* reuse, int n_members, int max_len, const int32_t* trig, const int32_t* pos,
+                            int pos_stride, int32_t* slot_pos, int slot_stride, const void* fk, const void* fv,
+                            int64_t fsh, int64_t fst, void* kp, void* vp, int nb, const int32_t* bt, int mb,
+                            void* stage_k, void* stage_v, int32_t* stage_src, int64_t stage_rows, int32_t* err,
+                            cudaStream_t s) {
+  DeltaArgs a;
+  a.member_job = mj;
+  a.member_head = mh;
+  a.member_len = ml;
+  a.member_off = moff;
+  a.reuse_len = reuse;
+  a.trigger = trig;
+  a.positions = pos;
+  a.pos_stride = pos_stride;
+  a.slot_pos = slot_pos;
+  a.slot_stride = slot_stride;
+  a.full_k = fk;
+  a.full_v = fv;
+  a.fsh = fsh;
+  a.fst = fst;
+  a.k_pool = kp;
+  a.v_pool = vp;
+  a.n_blocks = nb;
+  a.bt = bt;
+  a.max_blocks = mb;
+  a.stage_k = stage_k;
+  a.stage_v = stage_v;
+  a.stage_src = stage_src;
+  a.stage_rows = stage_rows;
+  a.err = err;
+  a.n_members = n_members;
+  a.items_per_member = 0;
+  switch (dtype) {
+    case HC_F32: return retrieve_delta_t<float>(a, max_len, s);
+    case HC_BF16: return retrieve_delta_t<__nv_bfloat16>(a, max_len, s);
+    case HC_F16: return retrieve_delta_t<__half>(a, max_len, s);
+    default: return HC_ERR_DTYPE;
+  }
 }
 
 int retrieve_dispatch(int dtype, int n_members, const int32_t* mj, const int32_t* mh, const int32_t* ml, int max_len,

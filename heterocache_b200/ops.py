@@ -238,3 +238,39 @@ def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, re
                            _ptr(err), st)
     check("hc_retrieve", rc)
     LAUNCHES[0] += 1
+
+
+def retrieve_delta(*, member_job, member_head, member_len, member_stage_offset, reuse_len, max_member_len, trigger,
+                   retrieve_positions, slot_positions, full_k, full_v, k_pool, v_pool, block_table, num_kv_heads,
+                   stage_k, stage_v, stage_src, err, stream: Optional[torch.cuda.Stream] = None):
+    """Satellite retrieval from a pinned-host tier that moves only rows the
+    satellite does not hold yet (same pool contents as ``retrieve``).
+
+    slot_positions [n_members, R] int32: positions held in the first R slots
+    of each member (ascending; seeded with the prefill kept indices, kept up
+    to date here).  stage_k/stage_v [rows, D] and stage_src [rows] int32:
+    device scratch, member m at rows member_stage_offset[m] + [0, len)."""
+    _cuda(member_job, member_head, member_len, member_stage_offset, reuse_len, trigger, retrieve_positions,
+          slot_positions, k_pool, v_pool, block_table, stage_k, stage_v, stage_src, err)
+    _rows(full_k, "full_k"), _rows(full_v, "full_v")
+    _i32(slot_positions, "slot_positions"), _i32(stage_src, "stage_src")
+    if not full_k.is_pinned() or not full_v.is_pinned():
+        raise ValueError("heterocache_b200: retrieve_delta reads a pinned host-memory full tier")
+    if full_k.stride() != full_v.stride():
+        raise ValueError("heterocache_b200: full_k and full_v must share strides")
+    if (stage_k.dtype != k_pool.dtype or stage_v.dtype != k_pool.dtype or not stage_k.is_contiguous()
+            or not stage_v.is_contiguous() or stage_k.shape != stage_v.shape or stage_k.shape[-1] != k_pool.shape[-1]
+            or stage_src.numel() < stage_k.shape[0]):
+        raise ValueError("heterocache_b200: staging area must be contiguous [rows, D] in the pool dtype, "
+                         "with a stage_src entry per row")
+    st = (stream or torch.cuda.current_stream(k_pool.device)).cuda_stream
+    rc = lib().hc_retrieve_delta(dtype_code(k_pool), num_kv_heads, k_pool.shape[-1], member_job.numel(),
+                                 _ptr(member_job), _ptr(member_head), _ptr(member_len), _ptr(member_stage_offset),
+                                 _ptr(reuse_len), int(max_member_len), _ptr(trigger), _ptr(retrieve_positions),
+                                 retrieve_positions.shape[-1], _ptr(slot_positions), slot_positions.shape[-1],
+                                 _ptr(full_k), _ptr(full_v), full_k.stride(1), full_k.stride(2),
+                                 _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
+                                 block_table.shape[1], _ptr(stage_k), _ptr(stage_v), _ptr(stage_src),
+                                 stage_k.shape[0], _ptr(err), st)
+    check("hc_retrieve_delta", rc)
+    LAUNCHES[0] += 2

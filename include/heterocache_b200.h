@@ -261,6 +261,33 @@ int hc_retrieve(int dtype, int num_kv_heads, int head_dim, int n_members,
                 void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks,
                 int32_t* err_flag, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Decode: satellite retrieval from a pinned-host full tier, moving only the
+ * rows a satellite does not already hold.  Same pool contents as
+ * hc_retrieve (heterocache/cache_utils.py:1084-1147, the host-tier branch
+ * real_offload=True at :1095-1123); the reference copies every row over the
+ * host link.
+ *   slot_positions [n_members, slot_stride] int32: for member m, the full-tier
+ *     position held in flat slot i, i < reuse_len[m] (ascending).  The caller
+ *     seeds it with the satellite's prefill kept indices and must choose
+ *     reuse_len[m] <= min(the satellite's prefill keep length, member_len[m]);
+ *     this call keeps it up to date.
+ *   stage_k/stage_v [stage_rows, D], stage_src int32 [stage_rows]: device
+ *     scratch; member m uses rows member_stage_offset[m] + [0, member_len[m]).
+ * Two launches on `stream`: rows found in the slot map are copied from the
+ * pool to the staging area, then every slot is written from the staging area
+ * or from the tier.  Members whose pivot did not trigger do nothing.
+ */
+int hc_retrieve_delta(int dtype, int num_kv_heads, int head_dim, int n_members,
+                      const int32_t* member_job, const int32_t* member_head, const int32_t* member_len,
+                      const int32_t* member_stage_offset, const int32_t* reuse_len, int max_member_len,
+                      const int32_t* trigger, const int32_t* retrieve_positions, int retrieve_stride,
+                      int32_t* slot_positions, int slot_stride,
+                      const void* full_k, const void* full_v, int64_t fsh, int64_t fst,
+                      void* k_pool, void* v_pool, int n_pool_blocks, const int32_t* block_table, int max_blocks,
+                      void* stage_k, void* stage_v, int32_t* stage_src, int64_t stage_rows,
+                      int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

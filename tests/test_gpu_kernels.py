@@ -452,3 +452,67 @@ def test_retrieve_gathers_only_on_trigger(cuda_device, tier):
     assert torch.equal(kf[0:400], full_k[0, 2, pos])
     assert torch.equal(kf[512:712], full_k[0, 3, pos[:200]])
     assert torch.equal(vp.cpu().view(-1, D)[512:712], full_v[0, 3, pos[:200]])
+
+
+def test_retrieve_delta_matches_full_retrieval(cuda_device):
+    """Delta retrieval from a pinned-host tier: after each of several
+    retrievals (overlapping position lists, one with the trigger off) the
+    pools are bit-identical to the full retrieval's, and the slot maps hold
+    the positions of the retrieved rows."""
+    dev = cuda_device
+    KV, D, L = 8, 128, 3000
+    g = torch.Generator().manual_seed(7)
+    full_k = torch.randn(1, KV, L, D, generator=g).to(torch.bfloat16)
+    full_v = torch.randn(1, KV, L, D, generator=g).to(torch.bfloat16)
+    fk, fv = full_k.pin_memory(), full_v.pin_memory()
+    heads, lens, keep = [2, 5, 6], [700, 300, 1], [650, 300, 0]
+    bt = torch.full((KV, 6), -1, dtype=torch.int32)
+    bt[2, :4] = torch.tensor([0, 1, 2, 3])
+    bt[5, :2] = torch.tensor([4, 5])
+    bt[6, :1] = torch.tensor([6])
+    kp = torch.zeros(7, 256, 1, D, dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    # prefill: each satellite holds its kept rows in slots [0, keep)
+    kept = [sorted(torch.randperm(L, generator=g)[:n].tolist()) for n in keep]
+    for h, kh in zip(heads, kept):
+        s = int(bt[h, 0]) * 256
+        kp.view(-1, D)[s:s + len(kh)] = full_k[0, h, kh]
+        vp.view(-1, D)[s:s + len(kh)] = full_v[0, h, kh]
+    i32 = dict(dtype=torch.int32, device=dev)
+    reuse = [min(k, n) for k, n in zip(keep, lens)]
+    slot = torch.zeros(3, max(reuse), dtype=torch.int32)
+    for i, (kh, r) in enumerate(zip(kept, reuse)):
+        slot[i, :r] = torch.tensor(kh[:r], dtype=torch.int32)
+    slot = slot.to(dev)
+    offs = torch.tensor([0, 700, 1000], **i32)
+    rows = sum(lens)
+    stage = (torch.empty(rows, D, dtype=torch.bfloat16, device=dev),
+             torch.empty(rows, D, dtype=torch.bfloat16, device=dev), torch.empty(rows, **i32))
+    kp_d, vp_d = kp.to(dev), vp.to(dev)       # delta path
+    kp_f, vp_f = kp.to(dev), vp.to(dev)       # full-retrieval path
+    common = dict(member_job=torch.zeros(3, **i32), member_head=torch.tensor(heads, **i32),
+                  member_len=torch.tensor(lens, **i32), max_member_len=max(lens), full_k=fk, full_v=fv,
+                  block_table=bt.to(dev), num_kv_heads=KV)
+    err = torch.zeros(1, **i32)
+    # first list: many of the first satellite's kept rows plus new ones; then
+    # a list overlapping the first; then one with the trigger off
+    p1 = sorted(set(kept[0][:500]) | set(torch.randperm(L, generator=g)[:400].tolist()))[:700]
+    p2 = sorted(set(p1[::2]) | set(torch.randperm(L, generator=g)[:600].tolist()))[:700]
+    p3 = sorted(torch.randperm(L, generator=g)[:700].tolist())
+    for pos_list, trig in ((p1, 1), (p2, 1), (p3, 0)):
+        positions = torch.tensor([pos_list], **i32)
+        trigger = torch.tensor([trig], **i32)
+        ops.retrieve_delta(member_stage_offset=offs, reuse_len=torch.tensor(reuse, **i32), trigger=trigger,
+                           retrieve_positions=positions, slot_positions=slot, k_pool=kp_d, v_pool=vp_d,
+                           stage_k=stage[0], stage_v=stage[1], stage_src=stage[2], err=err, **common)
+        ops.retrieve(trigger=trigger, retrieve_positions=positions, k_pool=kp_f, v_pool=vp_f, err=err, **common)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert torch.equal(kp_d.cpu(), kp_f.cpu())
+        assert torch.equal(vp_d.cpu(), vp_f.cpu())
+        if trig:
+            sl = slot.cpu()
+            for i, r in enumerate(reuse):
+                assert sl[i, :r].tolist() == pos_list[:r]
+    # the pools hold the second list's rows
+    assert torch.equal(kp_d.cpu().view(-1, D)[0:700], full_k[0, 2, p2])

@@ -27,7 +27,7 @@ def built():
 def test_header_declares_expected_entry_points():
     names = declared_functions()
     for n in ("hc_prefill_keep", "hc_prefill_select", "hc_pivot_init", "hc_decode_append", "hc_flash_decode",
-              "hc_drift_check", "hc_retrieve"):
+              "hc_drift_check", "hc_retrieve", "hc_retrieve_delta"):
         assert n in names
 
 
@@ -60,6 +60,11 @@ def test_argument_validation_needs_no_gpu(built):
     # nothing to do is not an error
     assert lib.hc_retrieve(1, 8, 128, 0, None, None, None, 0, None, None, 0, None, None, 0, 0, None, None, 1,
                            None, 1, None, None) == 0
+    assert lib.hc_retrieve_delta(1, 8, 128, 0, None, None, None, None, None, 0, None, None, 0, None, 0, None, None,
+                                 0, 0, None, None, 1, None, 1, None, None, None, 0, None, None) == 0
+    # misaligned staging area
+    assert lib.hc_retrieve_delta(1, 8, 128, 1, None, None, None, None, None, 1, None, None, 1, None, 1, None, None,
+                                 0, 0, None, None, 1, None, 1, 8, None, None, 1, None, None) == 1
     # workspace sizes are pure host arithmetic
     assert lib.hc_prefill_select_workspace_size(1, 1, 5, 32768, 4, 1) > 0
     assert lib.hc_flash_decode_workspace_size(1, 8, 4, 128) > 0
