@@ -63,7 +63,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=None, help="layers (default 32; 28 with --model qwen)")
     ap.add_argument("--model", default="llama", choices=["llama", "qwen"])
     ap.add_argument("--host-tier", action="store_true", help="full KV tier in pinned host memory")
-    ap.add_argument("--workload", default="llama128k", choices=["llama128k", "config4"])
+    ap.add_argument("--workload", default="llama128k", choices=["llama128k", "config2", "config4"])
+    ap.add_argument("--gen", type=int, default=128, help="config2: greedy tokens timed after the warm-up tokens")
     ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"])
     ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
     ap.add_argument("--no-e2e", action="store_true")
@@ -707,6 +708,106 @@ def graph_launches(cache, layers):
     return [base] * (STEPS_PER_CHECK - 1) + [base + extra]
 
 
+def run_config2(args, rank, world, local_rank):
+    """Config 2: the full random-init Llama-3.1-8B (bf16) with the patched
+    attention classes and the HeteroCache drop-in: prefill on `ctx` uniform
+    random token ids, then greedy decode token by token through the
+    transformers model (eager: projections, MLP and LM head from PyTorch /
+    cuBLAS; the cache's kernels for the compressed-KV path).  `warmup`
+    tokens are decoded untimed, then `gen` tokens are timed (CUDA events).
+    Independent replicas on N GPUs (one sequence each)."""
+    import transformers
+
+    from heterocache_b200 import ops
+    from heterocache_b200.attention import patch_transformers
+    from heterocache_b200.cache import HeteroCache, HeteroCacheConfig
+    from heterocache_b200.roles import derive_runtime_data, synthetic_roles
+
+    patch_transformers()
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, n_layers = args.ctx, 32
+    cfg = transformers.LlamaConfig(hidden_size=4096, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                                   intermediate_size=14336, num_hidden_layers=n_layers, vocab_size=128256,
+                                   rope_theta=500000.0, max_position_embeddings=L + args.warmup + args.gen + 16,
+                                   rms_norm_eps=1e-5, tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(2026 + rank)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    with torch.device(dev):
+        model = transformers.LlamaForCausalLM(cfg)
+    torch.set_default_dtype(prev)
+    model.eval()
+    data = derive_runtime_data(synthetic_roles(n_layers, 8, 2026), n_layers, 8)
+    hc = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.5, real_offload=False,
+                           max_gen_len=args.warmup + args.gen + 16, decode_step=STEPS_PER_CHECK,
+                           pooling="avgpool", kernel_size=5, num_attn_heads=32, num_kv_heads=8,
+                           num_layers=n_layers)
+    cache = HeteroCache(hc)
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (1, L), generator=g, device=dev)
+    with torch.no_grad():
+        torch.cuda.synchronize()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        out = model(input_ids=ids, past_key_values=cache, use_cache=True, logits_to_keep=1)
+        p1.record()
+        tok = out.logits[:, -1:].argmax(-1)
+        del out
+        torch.cuda.synchronize()
+        prefill_ms = p0.elapsed_time(p1)
+        cache.check_errors()
+        pos = torch.full((1, 1), L, dtype=torch.long, device=dev)
+        toks = []
+
+        def step():
+            nonlocal tok
+            o = model(input_ids=tok, past_key_values=cache, use_cache=True, position_ids=pos,
+                      cache_position=pos[0], logits_to_keep=1)
+            tok = o.logits[:, -1:].argmax(-1)
+            toks.append(tok)
+            pos.add_(1)
+
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        launches0 = ops.LAUNCHES[0]
+        if world > 1:
+            torch.distributed.barrier()
+        clocks = Clocks(local_rank) if rank == 0 else None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.gen):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        clk = clocks.stop() if clocks else None
+        ms = e0.elapsed_time(e1)
+        launches = ops.LAUNCHES[0] - launches0
+    cache.check_errors()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    ms_step = ms / args.gen
+    if rank == 0:
+        generated = torch.cat(toks, dim=-1)[0].tolist()
+        line = {"metric": METRIC, "value": world * 1000.0 / ms_step, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.gen, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (uniform random token ids, random-init weights)",
+                "config": {"workload": "config 2: full random-init Llama-3.1-8B, prefill then greedy decode "
+                                       "through transformers with the patched attention",
+                           "context": L, "layers": n_layers, "batch_per_gpu": 1,
+                           "parallelism": f"independent replicas x{world}",
+                           "decode": "eager transformers forward per token (no CUDA graph)"},
+                "prefill_s": prefill_ms / 1000.0, "us_per_layer": ms_step * 1000.0 / n_layers,
+                "gpu_launches": launches, "first_tokens": generated[:8], "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -714,6 +815,17 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "config2":
+        if world > 1:
+            import datetime
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                                 device_id=torch.device("cuda", local_rank))
+        try:
+            run_config2(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                torch.distributed.destroy_process_group()
         return
     if args.workload == "config4":
         if world > 1:
