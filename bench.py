@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--host-tier", action="store_true", help="full KV tier in pinned host memory")
     ap.add_argument("--workload", default="llama128k", choices=["llama128k", "config2", "config4"])
     ap.add_argument("--gen", type=int, default=128, help="config2: greedy tokens timed after the warm-up tokens")
+    ap.add_argument("--eager", action="store_true", help="config2: eager transformers forward per token "
+                                                         "(default: CUDA-graph replay)")
     ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"])
     ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
     ap.add_argument("--no-e2e", action="store_true")
@@ -760,9 +762,19 @@ def run_config2(args, rank, world, local_rank):
         cache.check_errors()
         pos = torch.full((1, 1), L, dtype=torch.long, device=dev)
         toks = []
+        runner = None
+        if not args.eager:
+            from heterocache_b200.graph import ModelDecodeGraph
+            runner = ModelDecodeGraph(model, cache, tok, pos)
+        replayed = [0]
 
         def step():
             nonlocal tok
+            if runner is not None:
+                phase = cache._qcount[0]
+                toks.append(runner.step().clone())
+                replayed[0] += runner.launches_per_phase[phase]
+                return
             o = model(input_ids=tok, past_key_values=cache, use_cache=True, position_ids=pos,
                       cache_position=pos[0], logits_to_keep=1)
             tok = o.logits[:, -1:].argmax(-1)
@@ -772,6 +784,7 @@ def run_config2(args, rank, world, local_rank):
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
+        replayed[0] = 0
         launches0 = ops.LAUNCHES[0]
         if world > 1:
             torch.distributed.barrier()
@@ -784,7 +797,7 @@ def run_config2(args, rank, world, local_rank):
         torch.cuda.synchronize()
         clk = clocks.stop() if clocks else None
         ms = e0.elapsed_time(e1)
-        launches = ops.LAUNCHES[0] - launches0
+        launches = ops.LAUNCHES[0] - launches0 + replayed[0]
     cache.check_errors()
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -802,7 +815,9 @@ def run_config2(args, rank, world, local_rank):
                                        "through transformers with the patched attention",
                            "context": L, "layers": n_layers, "batch_per_gpu": 1,
                            "parallelism": f"independent replicas x{world}",
-                           "decode": "eager transformers forward per token (no CUDA graph)"},
+                           "decode": ("eager transformers forward per token" if args.eager else
+                                      "CUDA-graph replay of the whole transformers forward per token "
+                                      "(one graph per drift-cycle phase)")},
                 "prefill_s": prefill_ms / 1000.0, "us_per_layer": ms_step * 1000.0 / n_layers,
                 "gpu_launches": launches, "first_tokens": generated[:8], "clocks": clk}
         print(json.dumps(line), flush=True)

@@ -28,6 +28,7 @@ from typing import List
 
 import torch
 
+from . import ops
 from .cache import HeteroCache
 
 
@@ -89,3 +90,79 @@ class DecodeStepGraph:
         for l in self.layers:
             c._qcount[l] = nxt
         return self.out
+
+
+class ModelDecodeGraph:
+    """CUDA graphs of one greedy decode token through a whole transformers
+    causal LM whose attention layers are the patched classes of
+    ``heterocache_b200.attention`` over a ``HeteroCache``: embedding, every
+    layer (projections, RoPE, the cache's append / attention / drift check /
+    retrieval launches, MLP), final norm, LM head and argmax, one graph per
+    phase of the drift-check cycle (as ``DecodeStepGraph``).
+
+    The graph reads the current token and position from the static buffers
+    ``tok`` [bsz, 1] and ``pos`` [bsz, 1] (int64) and writes the greedy next
+    token into ``tok`` and ``pos + 1`` into ``pos``, so consecutive ``step()``
+    calls decode token after token with no host work but the cache's
+    mirrored bookkeeping.  Capture after prefill, with ``tok``/``pos`` set to
+    the first decode token and its position.  The model's own code must not
+    synchronise with the host in a decode forward (transformers' Llama and
+    Qwen2 do not when no attention mask is passed).
+    """
+
+    def __init__(self, model, cache: HeteroCache, tok: torch.Tensor, pos: torch.Tensor):
+        layers = [l for l in range(cache.num_layers) if cache.key_pools[l] is not None]
+        if len(layers) != cache.num_layers:
+            raise RuntimeError("capture after prefill")
+        phases = {cache._qcount[l] for l in layers}
+        if len(phases) != 1:
+            raise RuntimeError("all layers must be at the same position of the decode_step cycle")
+        self.model, self.cache = model, cache
+        self.tok, self.pos = tok, pos
+        dev = cache._dev
+        q_example = torch.zeros(cache.bsz, cache.num_attn_heads, 1, cache.head_dim,
+                                dtype=cache.key_pools[0].dtype, device=dev)
+        cache.prepare_decode(layers, q_example)
+        cache.join_retrievals()
+        self.layers = layers
+        S = cache.decode_step
+        start = cache._qcount[layers[0]]
+        self.graphs: List[torch.cuda.CUDAGraph] = []
+        # this library's kernel launches held by each phase's graph
+        self.launches_per_phase: List[int] = []
+        torch.cuda.synchronize(dev)
+        pool = None
+        for phase in range(S):
+            saved = cache._host_state()
+            for l in layers:
+                cache._qcount[l] = phase
+            g = torch.cuda.CUDAGraph()
+            n0 = ops.LAUNCHES[0]
+            with torch.no_grad(), torch.cuda.graph(g, pool=pool, capture_error_mode="thread_local"):
+                self._forward()
+            self.launches_per_phase.append(ops.LAUNCHES[0] - n0)
+            pool = g.pool()
+            cache._restore_host_state(saved)
+            self.graphs.append(g)
+        for l in layers:
+            cache._qcount[l] = start
+
+    def _forward(self) -> None:
+        out = self.model(input_ids=self.tok, position_ids=self.pos, cache_position=self.pos[0],
+                         past_key_values=self.cache, use_cache=True, logits_to_keep=1)
+        self.tok.copy_(out.logits[:, -1:].argmax(-1))
+        self.pos.add_(1)
+        self.cache.join_retrievals()
+
+    def step(self) -> torch.Tensor:
+        """Decode one token: returns ``tok`` (now the next token)."""
+        c = self.cache
+        phase = c._qcount[self.layers[0]]
+        for l in self.layers:
+            c._append_bookkeeping(l)
+        self.graphs[phase].replay()
+        nxt = (phase + 1) % c.decode_step
+        for l in self.layers:
+            c._qcount[l] = nxt
+        c._seen_tokens += 1
+        return self.tok

@@ -124,3 +124,54 @@ def test_tiny_model_prefill_and_greedy_decode(cuda_device, kind):
     assert cache.get_seq_length() == 607
     for layer in range(2):
         assert cache.heads_len[layer].cpu().tolist() == [int(x) for x in cache._hlen[layer]]
+
+
+@pytest.mark.parametrize("kind", ["llama", "qwen"])
+def test_model_decode_graph_matches_eager(cuda_device, kind):
+    """Whole-model decode replayed from CUDA graphs (ModelDecodeGraph) gives
+    the eager token-by-token run's tokens and cache state."""
+    import transformers
+
+    from heterocache_b200.graph import ModelDecodeGraph
+    patch_transformers()
+    torch.manual_seed(0)
+    cfg = _config(kind)
+    cfg._attn_implementation = "sdpa"
+    model_cls = transformers.LlamaForCausalLM if kind == "llama" else transformers.Qwen2ForCausalLM
+    model = model_cls(cfg).to(cuda_device, torch.bfloat16).eval()
+    data = derive_runtime_data(synthetic_roles(2, 4, seed=5, star_size=3), 2, 4)
+    ids = torch.randint(0, 512, (1, 600), device=cuda_device)
+    n_tok = 12  # two drift checks (decode_step 5)
+
+    def new_cache():
+        hc = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.9, real_offload=False,
+                               max_gen_len=32, decode_step=5, num_attn_heads=8, num_kv_heads=4, num_layers=2)
+        c = HeteroCache(hc)
+        with torch.no_grad():
+            out = model(input_ids=ids, past_key_values=c, use_cache=True, logits_to_keep=1)
+        return c, out.logits[:, -1:].argmax(-1)
+
+    eager, tok = new_cache()
+    toks_e = []
+    with torch.no_grad():
+        for t in range(n_tok):
+            pos = torch.tensor([[600 + t]], device=cuda_device)
+            out = model(input_ids=tok, past_key_values=eager, use_cache=True, position_ids=pos,
+                        cache_position=pos[0], logits_to_keep=1)
+            tok = out.logits[:, -1:].argmax(-1)
+            toks_e.append(int(tok.item()))
+    graphed, tok0 = new_cache()
+    tok_buf = tok0.clone()
+    pos_buf = torch.tensor([[600]], device=cuda_device)
+    runner = ModelDecodeGraph(model, graphed, tok_buf, pos_buf)
+    toks_g = [int(runner.step().item()) for _ in range(n_tok)]
+    torch.cuda.synchronize()
+    eager.check_errors()
+    graphed.check_errors()
+    assert toks_g == toks_e
+    assert int(pos_buf.item()) == 600 + n_tok
+    assert graphed.get_seq_length() == eager.get_seq_length() == 600 + n_tok
+    for layer in range(2):
+        assert torch.equal(graphed.heads_len[layer].cpu(), eager.heads_len[layer].cpu())
+        assert torch.equal(graphed.block_tables[layer].cpu(), eager.block_tables[layer].cpu())
+        assert (graphed.key_pools[layer].float() - eager.key_pools[layer].float()).abs().max().item() <= 2e-2
