@@ -158,28 +158,49 @@ __device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float 
 // a permuted order so that each thread loads 16 contiguous bytes per row; the
 // query fragments use the same permutation, so the dot products are exact
 // sums over all 128 dims.
+//
+// The B fragments (query rows) stay in registers for NT <= 2.  For more rows
+// they would take 16*NT registers of the 128 a thread of the 512-thread CTA
+// has and spill; they go to shared memory instead, in per-lane order
+// (fragment word pair [nt][k-step][lane], so a warp's 8-byte loads are
+// conflict-free), filled once per CTA.
+constexpr int kMaxNT = 5;
+
 template <typename T, int NT, typename Pre>
 __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float* wmax, uint32_t* dummy,
-                           Pre&& pre) {
+                           uint2* s_qf, Pre&& pre) {
+  constexpr bool QS = NT > 2;  // query fragments in shared memory (s_qf: kMaxNT * 8 * 32 entries)
+  static_assert(NT <= kMaxNT, "query tiles");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  uint32_t qb[NT][8][2];
+  uint32_t qb[QS ? 1 : NT][8][2];
+  if constexpr (QS) {
+    for (int i = threadIdx.x; i < NT * 8 * 32; i += kSThreads) {
+      const int nt = i >> 8, ks = (i >> 5) & 7, ln = i & 31;
+      const int qi = nt * 8 + (ln >> 2);
+      uint2 w2 = make_uint2(0u, 0u);
+      if (qi < p.Rq) w2 = ldg64(query_row<T>(p, ji, qi) + 32 * (ks >> 1) + 8 * (ln & 3) + 4 * (ks & 1));
+      s_qf[i] = w2;
+    }
+  } else {
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    int qi = nt * 8 + gid;
-    const T* qr = qi < p.Rq ? query_row<T>(p, ji, qi) : nullptr;
+    for (int nt = 0; nt < NT; ++nt) {
+      int qi = nt * 8 + gid;
+      const T* qr = qi < p.Rq ? query_row<T>(p, ji, qi) : nullptr;
 #pragma unroll
-    for (int s = 0; s < 4; ++s) {
+      for (int s = 0; s < 4; ++s) {
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        uint2 w2 = make_uint2(0u, 0u);
-        if (qr) w2 = ldg64(qr + 32 * s + 8 * tig + 4 * u);
-        qb[nt][2 * s + u][0] = w2.x;
-        qb[nt][2 * s + u][1] = w2.y;
+        for (int u = 0; u < 2; ++u) {
+          uint2 w2 = make_uint2(0u, 0u);
+          if (qr) w2 = ldg64(qr + 32 * s + 8 * tig + 4 * u);
+          qb[nt][2 * s + u][0] = w2.x;
+          qb[nt][2 * s + u][1] = w2.y;
+        }
       }
     }
   }
-  pre();  // block-wide work that overlaps the query loads (ends in a block barrier)
+  pre();  // block-wide work that overlaps the query loads
+  if constexpr (QS) __syncthreads();  // the fragments are in shared memory
   float rmax[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) rmax[nt][0] = rmax[nt][1] = -INFINITY;
@@ -205,16 +226,28 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   }
   const uint32_t st_dummy = smem_u32(dummy);
   const uint64_t pol = l2_evict_first_policy();  // the keys are read once
-  for (int tg = lo + warp * 16; tg < hi; tg += kSWarps * 16) {
-    const int ta = min(tg + gid, p.L - 1), tb = min(tg + gid + 8, p.L - 1);
-    const T* ra = key_row<T>(p, ji, ta);
-    const T* rb = key_row<T>(p, ji, tb);
+  // Two key tiles in flight per warp: each iteration first issues the loads
+  // of the warp's next tile, then computes on the current one.
+  constexpr int kStep = kSWarps * 16;
+  auto load_tile = [&](int t, uint4 (&a)[4], uint4 (&b)[4]) {
+    const T* ra = key_row<T>(p, ji, min(t + gid, p.L - 1));
+    const T* rb = key_row<T>(p, ji, min(t + gid + 8, p.L - 1));
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      a[s] = ld_stream128(ra + 32 * s + 8 * tig, pol);
+      b[s] = ld_stream128(rb + 32 * s + 8 * tig, pol);
+    }
+  };
+  uint4 na[4], nb[4];
+  if (lo + warp * 16 < hi) load_tile(lo + warp * 16, na, nb);
+  for (int tg = lo + warp * 16; tg < hi; tg += kStep) {
     uint4 ka[4], kb[4];
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
-      ka[s] = ld_stream128(ra + 32 * s + 8 * tig, pol);
-      kb[s] = ld_stream128(rb + 32 * s + 8 * tig, pol);
+      ka[s] = na[s];
+      kb[s] = nb[s];
     }
+    if (tg + kStep < hi) load_tile(tg + kStep, na, nb);
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
@@ -222,8 +255,16 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
     for (int s = 0; s < 4; ++s) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        mma16816<T>(acc[nt], ka[s].x, kb[s].x, ka[s].y, kb[s].y, qb[nt][2 * s][0], qb[nt][2 * s][1]);
-        mma16816<T>(acc[nt], ka[s].z, kb[s].z, ka[s].w, kb[s].w, qb[nt][2 * s + 1][0], qb[nt][2 * s + 1][1]);
+        uint2 b0, b1;
+        if constexpr (QS) {
+          b0 = s_qf[((nt * 8 + 2 * s) << 5) + lane];
+          b1 = s_qf[((nt * 8 + 2 * s + 1) << 5) + lane];
+        } else {
+          b0 = make_uint2(qb[nt][2 * s][0], qb[nt][2 * s][1]);
+          b1 = make_uint2(qb[nt][2 * s + 1][0], qb[nt][2 * s + 1][1]);
+        }
+        mma16816<T>(acc[nt], ka[s].x, kb[s].x, ka[s].y, kb[s].y, b0.x, b0.y);
+        mma16816<T>(acc[nt], ka[s].z, kb[s].z, ka[s].w, kb[s].w, b1.x, b1.y);
       }
     }
     if (fast_ok && tg >= ji.t0 && tg + 16 <= ji.t1) {
@@ -576,6 +617,8 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   constexpr int ROUNDS = KB / 8;
   __shared__ int s_pages[kMaxPages];
   __shared__ __align__(16) uint32_t s_dummy[4];  // sink of stmatrix rows past Rq
+  // query fragments of the tensor-core logits for more than 16 query rows
+  __shared__ uint2 s_qfrag[std::is_same<T, float>::value ? 1 : kMaxNT * 8 * 32];
   JobInfo ji = job_info(p);
   const int nblocks = gridDim.x;
   unsigned int epoch = 0;
@@ -639,11 +682,11 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   constexpr bool kTensor = !std::is_same<T, float>::value;
   bool used_mma = false;
   if constexpr (kTensor) {
-    if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
-    else if (p.Rq <= 16) { logits_mma<T, 2>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
-    else if (p.Rq <= 24) { logits_mma<T, 3>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
-    else if (p.Rq <= 32) { logits_mma<T, 4>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
-    else if (p.Rq <= 40) { logits_mma<T, 5>(p, ji, lg, wmax, s_dummy, stage_pages); used_mma = true; }
+    if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
+    else if (p.Rq <= 16) { logits_mma<T, 2>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
+    else if (p.Rq <= 24) { logits_mma<T, 3>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
+    else if (p.Rq <= 32) { logits_mma<T, 4>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
+    else if (p.Rq <= 40) { logits_mma<T, 5>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
   }
   if (!used_mma) {
     stage_pages();
