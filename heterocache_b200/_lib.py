@@ -41,8 +41,8 @@ SIGNATURES = {
                                 c_void_p, c_size_t, c_void_p, c_void_p]),
     "hc_flash_decode_with_new": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p,
                                          c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64,
-                                         c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_int, c_void_p,
-                                         c_size_t, c_void_p, c_void_p]),
+                                         c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p, c_size_t,
+                                         c_void_p, c_void_p]),
     "hc_flash_decode_noalloc": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_void_p,
                                         c_void_p, c_int, c_void_p, c_int, c_void_p, c_float, c_void_p, c_void_p,
                                         c_void_p]),

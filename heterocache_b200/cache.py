@@ -189,9 +189,6 @@ class HeteroCache(_CacheBase):
         # pinned-host tier: prefill kept indices (until the layer's slot maps
         # are built) and the retrieval staging area shared by all layers
         self._kept: List[Optional[tuple]] = [None] * n
-        # a retrieval into this layer's pages ran on the main stream since the
-        # layer's last attention (the attention then waits before its K/V copies)
-        self._pages_written: List[bool] = [False] * n
         self._stage: Optional[tuple] = None
         self._retrieve_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._side_stream: Optional[torch.cuda.Stream] = None
@@ -529,14 +526,13 @@ class HeteroCache(_CacheBase):
                 "retrieve_done": list(self._retrieve_done), "seen": self._seen_tokens,
                 "pending": [None if x is None else list(x) for x in self._pending],
                 "append_done": list(self._append_done),
-                "q_staged": list(self._q_staged), "pages_written": list(self._pages_written)}
+                "q_staged": list(self._q_staged)}
 
     def _restore_host_state(self, s) -> None:
         self._hlen, self._mapped = s["hlen"], s["mapped"]
         self.free_block_pointers, self._qcount = s["free_ptr"], s["qcount"]
         self._retrieve_done, self._seen_tokens = s["retrieve_done"], s["seen"]
         self._pending, self._append_done, self._q_staged = s["pending"], s["append_done"], s["q_staged"]
-        self._pages_written = s["pages_written"]
 
     def decode_select(self, query_states, layer_idx):
         """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
@@ -624,7 +620,6 @@ class HeteroCache(_CacheBase):
                          k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
                          block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
                          err=self._err)
-            self._pages_written[layer_idx] = True
 
     # ------------------------------------------------------------------
     def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):
@@ -651,16 +646,11 @@ class HeteroCache(_CacheBase):
                   and q.stride() == query_states.stride())
         if q is not None and not same_q:
             self._qbuf[layer_idx][slot].copy_(q[0, :, 0, :])
-        # the append is deferred and side-stream work is joined by events, so
-        # the kernel just before writes none of this layer's pages unless it
-        # is this layer's own retrieval on this stream
         out = ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
                                self.block_tables[layer_idx], self.heads_len[layer_idx],
                                num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
                                err=self._err, k_new=k, v_new=v,
-                               q_stage=self._qbuf[layer_idx][slot] if same_q else None,
-                               early_kv=not self._pages_written[layer_idx])
-        self._pages_written[layer_idx] = False
+                               q_stage=self._qbuf[layer_idx][slot] if same_q else None)
         main = torch.cuda.current_stream(self._dev)
         side = self._side()
         side.wait_stream(main)

@@ -256,7 +256,7 @@ int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, i
                              int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
                              const int32_t* block_table, int max_blocks, const int32_t* heads_len,
                              const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh, int64_t vn_sb,
-                             int64_t vn_sh, float scale, void* out, void* q_stage, int flags, void* workspace,
+                             int64_t vn_sh, float scale, void* out, void* q_stage, void* workspace,
                              size_t workspace_bytes, int32_t* err_flag, void* stream) {
   if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
   if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || groups <= 0 || max_blocks <= 0)
@@ -290,8 +290,6 @@ int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, i
   p.vn_sb = vn_sb;
   p.vn_sh = vn_sh;
   p.q_stage = q_stage;
-  if (flags & ~HC_FD_EARLY_KV) return HC_ERR_INVALID;
-  p.early_kv = (flags & HC_FD_EARLY_KV) ? 1 : 0;
   return note_cuda(hc::flash_decode_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
 }
 

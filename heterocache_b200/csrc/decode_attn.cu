@@ -479,15 +479,9 @@ __global__ void __launch_bounds__(kTThreads, 2)
   const int gid = lane >> 2, tig = lane & 3;
   // programmatic dependent launch: wait for the kernel before (the page
   // append) to finish, then let the combine get resident; it reads row
-  // lengths before its own wait and waits for this grid's partials.  With
-  // early_kv the page table, lengths and pages are not written by the kernel
-  // before: the producer streams K/V without waiting, and the consumers wait
-  // before reading the query.
-  const bool early = p.early_kv != 0;
-  if (!early) {
-    pdl_wait();
-    pdl_trigger();
-  }
+  // lengths before its own wait and waits for this grid's partials
+  pdl_wait();
+  pdl_trigger();
   const int total = row_prefix(p, s_start, s_warp, s_len);
   const int span = span_of(total, gridDim.x, kTTile);
   const int beg = blockIdx.x * span;
@@ -551,10 +545,6 @@ __global__ void __launch_bounds__(kTThreads, 2)
   }
 
   // ---- consumers
-  if (early) {
-    pdl_wait();
-    pdl_trigger();
-  }
   TcState st;
   uint32_t qa[8][2];
   int cur = -1;

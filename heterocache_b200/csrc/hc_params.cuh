@@ -94,10 +94,6 @@ struct FDParams {
   int64_t kn_sb, kn_sh, vn_sb, vn_sh;
   // optional (batch of one): the combine also stores the query rows here [H, D]
   void* q_stage;
-  // the kernel just before on the stream writes none of the pages, page
-  // table or lengths this call reads: K/V copies may start before the
-  // programmatic-launch wait (the query is still read after it)
-  int early_kv;
   void* out;
   int32_t* err;
 };

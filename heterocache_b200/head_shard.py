@@ -225,7 +225,6 @@ class HeadShardedCache:
                      full_v=c.value_cache_cpu[layer_idx], k_pool=c.key_pools[layer_idx],
                      v_pool=c.value_pools[layer_idx], block_table=c.block_tables[layer_idx],
                      num_kv_heads=c.num_kv_heads, err=c._err)
-        c._pages_written[layer_idx] = True  # the layer's next attention waits before its K/V copies
 
     def check_errors(self):
         self.cache.check_errors()

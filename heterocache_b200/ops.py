@@ -155,14 +155,11 @@ def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, fre
 
 
 def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out=None, scale: float = 0.0,
-                 workspace: Workspace, err, total_tokens_hint: int = 0, k_new=None, v_new=None, q_stage=None,
-                 early_kv: bool = False):
+                 workspace: Workspace, err, total_tokens_hint: int = 0, k_new=None, v_new=None, q_stage=None):
     """q: [bsz, H, 1, D] -> out [bsz, H, D] (same dtype).  With k_new/v_new
     [bsz, KV, 1, D] each row also attends to that token (not in the pages);
     then q_stage (bsz 1: a contiguous [H, D] buffer) also receives the query
-    rows, and ``early_kv`` (the kernel just before on the stream writes none
-    of these pages, page table or lengths) lets the K/V copies start before
-    that kernel has finished."""
+    rows."""
     _cuda(q, k_pool, v_pool, block_table, heads_len, err, k_new, v_new, q_stage)
     _rows(q, "q")
     bsz, H, one, D = q.shape
@@ -185,8 +182,8 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
                                             q.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
                                             _ptr(block_table), block_table.shape[1], _ptr(heads_len), _ptr(k_new),
                                             _ptr(v_new), k_new.stride(0), k_new.stride(1), v_new.stride(0),
-                                            v_new.stride(1), float(scale), _ptr(out), _ptr(q_stage),
-                                            1 if early_kv else 0, _ptr(ws), ws.numel(), _ptr(err), _stream(q))
+                                            v_new.stride(1), float(scale), _ptr(out), _ptr(q_stage), _ptr(ws),
+                                            ws.numel(), _ptr(err), _stream(q))
         check("hc_flash_decode_with_new", rc)
         LAUNCHES[0] += 2
         return out

@@ -174,23 +174,16 @@ int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_d
  * head_dim] buffer in the query dtype into which the call also stores the
  * step's query rows -- the decode-step query buffer the drift check reads
  * (heterocache/cache_utils.py:1011-1017 collects the last decode_step
- * queries), so the check need not wait for the deferred append.
- * flags: 0, or HC_FD_EARLY_KV when the kernel just before on `stream` writes
- * none of the pages, block table or heads_len this call reads (true with the
- * append deferred, unless that kernel is a retrieval into these pages): the
- * K/V copies then start before the programmatic-launch wait on that kernel,
- * overlapping its tail; the query is still read after the wait.  Arguments
+ * queries), so the check need not wait for the deferred append.  Arguments
  * otherwise as hc_flash_decode.
  */
-#define HC_FD_EARLY_KV 1
 int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, int head_dim,
                              const void* q, int64_t qsb, int64_t qsh,
                              const void* k_pool, const void* v_pool, int n_pool_blocks,
                              const int32_t* block_table, int max_blocks, const int32_t* heads_len,
                              const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh,
                              int64_t vn_sb, int64_t vn_sh, float scale, void* out, void* q_stage,
-                             int flags, void* workspace, size_t workspace_bytes, int32_t* err_flag,
-                             void* stream);
+                             void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Decode attention without a workspace.  No counterpart in the reference:

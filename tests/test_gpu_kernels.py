@@ -199,34 +199,6 @@ def test_flash_decode_with_new_token_and_query_stage(cuda_device, dtype):
     assert diff <= ATOL[dtype], diff
 
 
-def test_flash_decode_early_kv_copies_give_the_same_output(cuda_device):
-    """K/V copies started before the programmatic-launch wait (the caller
-    states that the kernel before writes none of these pages): the same
-    output, bit for bit, as with the wait first, also right after another
-    kernel on the stream that writes only the query."""
-    geo = LLAMA_8B
-    KV, D = geo.num_kv_heads, geo.head_dim
-    dev = cuda_device
-    lens = [131, 70000, 256, 9000, 1, 33000, 512, 4100]
-    q, kp, vp, bt, hl = _random_paged(lens, geo, torch.bfloat16, dev, seed=21)
-    g = torch.Generator().manual_seed(22)
-    kn = torch.randn(1, KV, 1, D, generator=g).to(torch.bfloat16).to(dev)
-    vn = torch.randn(1, KV, 1, D, generator=g).to(torch.bfloat16).to(dev)
-    args = (kp.to(dev), vp.to(dev), bt.to(dev), hl.to(dev))
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    ws = Workspace(dev)
-    q_src = q.to(dev)
-    outs = []
-    for early in (False, True, True):
-        qd = torch.empty_like(q_src)
-        qd.copy_(q_src)  # a kernel just before that writes the query only
-        outs.append(ops.flash_decode(qd, *args, num_kv_heads=KV, workspace=ws, err=err, k_new=kn, v_new=vn,
-                                     early_kv=early))
-    torch.cuda.synchronize()
-    assert int(err.item()) == 0
-    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
-
-
 def test_flash_decode_strided_query(cuda_device):
     """Queries as the attention layer produces them: a transposed projection view."""
     geo = LLAMA_8B
