@@ -888,6 +888,10 @@ def run_config2(args, rank, world, local_rank):
 
 def main():
     args = parse()
+    # rank 0's stdout carries exactly one JSON line: keep NCCL's version
+    # banner off it (an explicit INFO/TRACE request is left as it is)
+    if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+        os.environ["NCCL_DEBUG"] = "WARN"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
