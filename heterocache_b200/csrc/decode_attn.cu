@@ -640,7 +640,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   int* s_start = reinterpret_cast<int*>(smem_raw);
   __shared__ int s_warp[32];
   __shared__ float s_red[kCThreads / 32];
-  __shared__ float s_mrun;  // running maximum over the rounds of 64 partials
+  __shared__ float s_mrun;  // running maximum over the rounds of 128 partials
   __shared__ float4 s_acc[kCThreads / 32][kD / 4];
   const int total = row_prefix(p, s_start, s_warp);
   const int span = span_of(total, nctas, p.gran);
@@ -687,7 +687,9 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   // One load round: each warp takes every 8th partial, its lanes a 4-dim
   // slice of the output row, and the partial's (m, l) (one broadcast load)
   // with it; then the block maximum, and each warp rescales its own partials.
-  constexpr int NW = kCThreads / 32, DEPTH = 8;
+  // 16 partials per warp: rows of up to 128 partials (131072 tokens at the
+  // decode grid's spans) take a single round.
+  constexpr int NW = kCThreads / 32, DEPTH = 16;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float Lw = 0.f;
   for (int cb0 = 0; cb0 < n; cb0 += NW * DEPTH) {
@@ -709,7 +711,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
     float M = cb0 == 0 ? s_new : s_mrun;
 #pragma unroll
     for (int w = 0; w < NW; ++w) M = fmaxf(M, s_red[w]);
-    // rescale what earlier rounds accumulated (more than 64 partials only)
+    // rescale what earlier rounds accumulated (more than 128 partials only)
     if (cb0 > 0) {
       const float fo = (s_mrun == -INFINITY) ? 0.f : exp2f(s_mrun - M);
       acc.x *= fo; acc.y *= fo; acc.z *= fo; acc.w *= fo;
