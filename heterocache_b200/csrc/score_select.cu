@@ -700,27 +700,53 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
     s_rowM[qi] = m;
   }
   __syncthreads();
-  // partial sum of exp over own tokens (four independent accumulators)
+  // partial sum of exp over own tokens (four independent accumulators): one
+  // warp per row; with fewer rows than warps (prefill and pivot launches) a
+  // row's tokens are split into nch chunks so that every warp has work, and
+  // the chunk sums of a row are added in a fixed order (the per-warp maxima
+  // in wmax were consumed above, so it holds the chunk sums)
   {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int base = ji.t0 - kMargin;
-    for (int qi = warp; qi < p.Rq; qi += kSWarps) {
-      const float m = s_rowM[qi];
+    auto exp_sum = [&](int qi, float m, int tb, int te) {
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
       if (m != -INFINITY) {
         const T* row = lg + (int64_t)qi * p.TB - base;
-        for (int t = ji.t0 + lane; t < ji.t1; t += 128) {
+        for (int t = tb + lane; t < te; t += 128) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int tu = t + 32 * u;
-            if (tu < ji.t1) s4[u] += row_exp<T>(Elem<T>::to_f(row[tu]) - m);
+            if (tu < te) s4[u] += row_exp<T>(Elem<T>::to_f(row[tu]) - m);
           }
         }
       }
       float s = (s4[0] + s4[1]) + (s4[2] + s4[3]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(m, s);
+      return s;
+    };
+    if (p.Rq >= kSWarps) {
+      for (int qi = warp; qi < p.Rq; qi += kSWarps) {
+        const float m = s_rowM[qi];
+        const float s = exp_sum(qi, m, ji.t0, ji.t1);
+        if (lane == 0) p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(m, s);
+      }
+    } else {
+      const int nch = min(4, kSWarps / p.Rq);
+      const int clen = (((ji.t1 - ji.t0 + nch - 1) / nch) + 127) / 128 * 128;  // a multiple of 128
+      float* csum = wmax;  // [Rq][nch]
+      for (int it = warp; it < p.Rq * nch; it += kSWarps) {
+        const int qi = it / nch, qc = it - qi * nch;
+        const int tb = ji.t0 + qc * clen;
+        const float s = exp_sum(qi, s_rowM[qi], tb, min(ji.t1, tb + clen));
+        if (lane == 0) csum[it] = s;
+      }
+      __syncthreads();  // p.Rq is uniform over the block
+      for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
+        float s = 0.f;
+        for (int c = 0; c < nch; ++c) s += csum[qi * nch + c];
+        p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(s_rowM[qi], s);
+      }
     }
   }
   if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
