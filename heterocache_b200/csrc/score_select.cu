@@ -1093,14 +1093,15 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
         if (rank < kk) p.out_indices[(size_t)ji.job * p.max_keep + rank] = ji.t0 + c + lane;
       }
       if (!start_ok) return;
-      // warp-cooperative row copies, 4 tokens in flight
+      // warp-cooperative row copies, NQ tokens in flight
+      constexpr int NQ = std::is_same<T, float>::value ? 4 : 8;
       unsigned int m = selm;
       int r = r0;
       while (m) {
-        int tt[4], rr[4];
+        int tt[NQ], rr[NQ];
         int nb = 0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < NQ; ++q) {
           tt[q] = -1;
           rr[q] = kk;
           if (m) {
@@ -1111,9 +1112,9 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
             ++nb;
           }
         }
-        uint4 buf[4][PER];
+        uint4 buf[NQ][PER];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < NQ; ++q)
 #pragma unroll
           for (int e = 0; e < PER; ++e) {
             const int x = lane + 32 * e;
@@ -1123,7 +1124,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
             }
           }
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < NQ; ++q)
 #pragma unroll
           for (int e = 0; e < PER; ++e) {
             const int x = lane + 32 * e;
