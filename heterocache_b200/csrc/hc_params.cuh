@@ -42,6 +42,7 @@ struct ScoreParams {
   void* v_pool_out;
   int32_t* heads_len;
   int32_t* out_indices;
+  int32_t* keep_pos;  // workspace: prefill kept positions [job][rank] (set at launch)
   int max_keep;
   void* out_scores;
   const int32_t* ref_slots;

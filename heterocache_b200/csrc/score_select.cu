@@ -1075,70 +1075,84 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   };
 
   if (p.mode == MODE_PREFILL) {
-    const int kk = (int)s_k[0];
+    const int kk = (int)s_k[0];  // <= L (the host clamps keep lengths)
     const int row = ji.b * p.KV + ji.h;
-    // flat slots from the row's first page (the row's prefill pages are contiguous)
-    const int start = p.bt[(int64_t)row * p.max_blocks];
-    const bool start_ok = start >= 0 && (int64_t)start * kPage + kk <= (int64_t)p.n_blocks * kPage;
-    if (!start_ok && kk > 0 && threadIdx.x == 0 && ji.part == 0) set_err(p.err, HC_ERR_RANGE);
-    const T* kbase = reinterpret_cast<const T*>(p.k) + ji.b * p.ksb + (int64_t)ji.h * p.ksh;
-    const T* vbase = reinterpret_cast<const T*>(p.v) + ji.b * p.vsb + (int64_t)ji.h * p.vsh;
-    T* kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)start * kPage * kD;
-    T* vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)start * kPage * kD;
-    constexpr int CH = kD * (int)sizeof(T) / 16;  // 16-byte chunks per row
-    constexpr int PER = (2 * CH + 31) / 32;        // chunks per lane per token (K and V)
+    // 1. the job's kept positions in rank order -> the workspace list (and
+    //    out_indices when asked for)
+    int32_t* plist = p.keep_pos + (size_t)ji.job * p.L;
     rank_walk(0, [&](int c, unsigned int selm, int r0) {
-      if (p.out_indices && ((selm >> lane) & 1u)) {
+      if ((selm >> lane) & 1u) {
         const int rank = r0 + __popc(selm & lt_mask);
-        if (rank < kk) p.out_indices[(size_t)ji.job * p.max_keep + rank] = ji.t0 + c + lane;
-      }
-      if (!start_ok) return;
-      // warp-cooperative row copies, NQ tokens in flight
-      constexpr int NQ = std::is_same<T, float>::value ? 4 : 8;
-      unsigned int m = selm;
-      int r = r0;
-      while (m) {
-        int tt[NQ], rr[NQ];
-        int nb = 0;
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          tt[q] = -1;
-          rr[q] = kk;
-          if (m) {
-            const int j = __ffs(m) - 1;
-            m &= m - 1;
-            tt[q] = ji.t0 + c + j;
-            rr[q] = r++;
-            ++nb;
-          }
+        if (rank < kk) {
+          plist[rank] = ji.t0 + c + lane;
+          if (p.out_indices) p.out_indices[(size_t)ji.job * p.max_keep + rank] = ji.t0 + c + lane;
         }
-        uint4 buf[NQ][PER];
-#pragma unroll
-        for (int q = 0; q < NQ; ++q)
-#pragma unroll
-          for (int e = 0; e < PER; ++e) {
-            const int x = lane + 32 * e;
-            if (q < nb && rr[q] < kk && x < 2 * CH) {
-              const T* src = x < CH ? kbase + (int64_t)tt[q] * p.kst : vbase + (int64_t)tt[q] * p.vst;
-              buf[q][e] = ldg128(reinterpret_cast<const uint4*>(src) + (x % CH));
-            }
-          }
-#pragma unroll
-        for (int q = 0; q < NQ; ++q)
-#pragma unroll
-          for (int e = 0; e < PER; ++e) {
-            const int x = lane + 32 * e;
-            if (q < nb && rr[q] < kk && x < 2 * CH) {
-              T* dst = (x < CH ? kdst : vdst) + (int64_t)rr[q] * kD;
-              reinterpret_cast<uint4*>(dst)[x % CH] = buf[q][e];
-            }
-          }
       }
     });
     if (ji.part == 0 && threadIdx.x == 0) p.heads_len[row] = kk;
     if (p.out_indices && ji.part == p.cpj - 1) {
       for (int i = kk + threadIdx.x; i < p.max_keep; i += kSThreads)
         p.out_indices[(size_t)ji.job * p.max_keep + i] = -1;
+    }
+    // 2. every job's list is complete
+    if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+    // 3. kept K/V rows to their pages: the rows of all jobs (in job, then
+    //    rank order) split into equal contiguous shares, one per CTA, so that
+    //    CTAs whose tokens hold many kept positions do not set the end.
+    //    Flat slots from each row's first page (prefill pages are contiguous).
+    constexpr int CH = kD * (int)sizeof(T) / 16;  // 16-byte chunks per row
+    constexpr int PER = (2 * CH + 31) / 32;        // chunks per lane per row (K and V)
+    constexpr int NQ = std::is_same<T, float>::value ? 4 : 8;  // rows in flight per warp
+    long long total = 0;
+    for (int jb = 0; jb < p.n_jobs; ++jb) total += min(max(p.keep_lens[jb % p.nh], 0), p.L);
+    const long long share = (total + nblocks - 1) / nblocks;
+    const long long g0 = (long long)blockIdx.x * share, g1 = min(total, g0 + share);
+    long long off = 0;
+    for (int jb = 0; jb < p.n_jobs && off < g1; ++jb) {
+      const int bj = jb / p.nh, hj = jb % p.nh;
+      const int nj = min(max(p.keep_lens[hj], 0), p.L);
+      const long long a = max(g0, off), e = min(g1, off + nj);
+      if (a < e) {
+        const int rowj = bj * p.KV + hj;
+        const int start = p.bt[(int64_t)rowj * p.max_blocks];
+        if (start < 0 || (int64_t)start * kPage + nj > (int64_t)p.n_blocks * kPage) {
+          if (threadIdx.x == 0) set_err(p.err, HC_ERR_RANGE);
+        } else {
+          const int32_t* pl = p.keep_pos + (size_t)jb * p.L;
+          const T* kbase = reinterpret_cast<const T*>(p.k) + bj * p.ksb + (int64_t)hj * p.ksh;
+          const T* vbase = reinterpret_cast<const T*>(p.v) + bj * p.vsb + (int64_t)hj * p.vsh;
+          T* kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)start * kPage * kD;
+          T* vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)start * kPage * kD;
+          const int r_lo = (int)(a - off), r_hi = (int)(e - off);
+          for (int rb = r_lo + warp * NQ; rb < r_hi; rb += kSWarps * NQ) {
+            int tt[NQ];
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) tt[q] = rb + q < r_hi ? __ldcg(pl + rb + q) : -1;
+            uint4 buf[NQ][PER];
+#pragma unroll
+            for (int q = 0; q < NQ; ++q)
+#pragma unroll
+              for (int x8 = 0; x8 < PER; ++x8) {
+                const int x = lane + 32 * x8;
+                if (tt[q] >= 0 && tt[q] < p.L && x < 2 * CH) {
+                  const T* src = x < CH ? kbase + (int64_t)tt[q] * p.kst : vbase + (int64_t)tt[q] * p.vst;
+                  buf[q][x8] = ldg128(reinterpret_cast<const uint4*>(src) + (x % CH));
+                }
+              }
+#pragma unroll
+            for (int q = 0; q < NQ; ++q)
+#pragma unroll
+              for (int x8 = 0; x8 < PER; ++x8) {
+                const int x = lane + 32 * x8;
+                if (tt[q] >= 0 && tt[q] < p.L && x < 2 * CH) {
+                  T* dst = (x < CH ? kdst : vdst) + (int64_t)(rb + q) * kD;
+                  reinterpret_cast<uint4*>(dst)[x % CH] = buf[q][x8];
+                }
+              }
+          }
+        }
+      }
+      off += nj;
     }
   } else if (p.mode == MODE_PIVOT) {
     const int slot = ji.job;
@@ -1276,10 +1290,10 @@ static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int cta
 }
 
 struct ScoreWs {
-  size_t off_gb, off_part, off_hist, off_cnt, off_overlap, off_logits, total;
+  size_t off_gb, off_part, off_hist, off_cnt, off_overlap, off_logits, off_keep, total;
 };
 
-static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq) {
+static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq, int L) {
   ScoreWs w;
   size_t o = 0;
   auto take = [&](size_t n) { size_t r = o; o += (n + 255) & ~(size_t)255; return r; };
@@ -1289,13 +1303,14 @@ static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq) {
   w.off_cnt = take((size_t)n_jobs * kMaxSel * pl.cpj * 256 * sizeof(int2));
   w.off_overlap = take((size_t)n_jobs * kMaxRows * sizeof(unsigned int));
   w.off_logits = take(pl.logits_bytes);
+  w.off_keep = take((size_t)n_jobs * L * sizeof(int32_t));
   w.total = o;
   return w;
 }
 
 template <typename T, int MODE>
 static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws_bytes, cudaStream_t st) {
-  ScoreWs w = score_ws_layout(p.n_jobs, pl, p.Rq);
+  ScoreWs w = score_ws_layout(p.n_jobs, pl, p.Rq, p.L);
   if (!ws || ws_bytes < w.total) return HC_ERR_WORKSPACE;
   unsigned char* base = reinterpret_cast<unsigned char*>(ws);
   p.gb = reinterpret_cast<GridBarrier*>(base + w.off_gb);
@@ -1304,6 +1319,7 @@ static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size
   p.cnt = reinterpret_cast<int2*>(base + w.off_cnt);
   p.overlap = reinterpret_cast<unsigned int*>(base + w.off_overlap);
   p.glogits = pl.logits_in_smem ? nullptr : (void*)(base + w.off_logits);
+  p.keep_pos = reinterpret_cast<int32_t*>(base + w.off_keep);
   p.logits_in_smem = pl.logits_in_smem ? 1 : 0;
   p.cpj = pl.cpj;
   p.T = pl.T;
@@ -1371,7 +1387,7 @@ static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st)
 
 size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S) {
   ScorePlan pl = plan_score(dtype, n_jobs, L, Rq, S, 1);
-  return score_ws_layout(n_jobs, pl, Rq).total;
+  return score_ws_layout(n_jobs, pl, Rq, L).total;
 }
 
 int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
