@@ -488,19 +488,30 @@ __device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* l
         for (int o = 0; o < 8; o += 2) Elem<T>::rnd2(best[o], best[o + 1]);
       }
     }
-    // max over the group's lanes (groups are aligned within a warp)
-    for (int o = 1; o < GP; o <<= 1) {
+    // max over the group's lanes (groups are aligned within a warp) as a
+    // reduce-scatter: in the round with lane mask m each lane keeps one half
+    // of its values (the upper half if gl & m) and takes the max with its
+    // partner's copy of that half; after log2(GP) rounds lane gl holds the
+    // group maxima of tokens gl*8/GP .. (gl+1)*8/GP - 1 in best[0 ..)
+    auto rs_round = [&](auto half, int m) {  // half: a compile-time 4, 2 or 1
+      constexpr int H = decltype(half)::value;
+      const bool upper = (gl & m) != 0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) best[k] = fmaxf(best[k], __shfl_xor_sync(0xffffffffu, best[k], o));
-    }
-    // lane gl keys tokens gl, gl+GP, ... (8/GP of them)
+      for (int i = 0; i < H; ++i) {
+        const float send = upper ? best[i] : best[i + H];
+        const float keep = upper ? best[i + H] : best[i];
+        best[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, m));
+      }
+    };
+    if (GP >= 2) rs_round(std::integral_constant<int, 4>{}, GP >> 1);  // GP is uniform over the warp
+    if (GP >= 4) rs_round(std::integral_constant<int, 2>{}, GP >> 2);
+    if (GP >= 8) rs_round(std::integral_constant<int, 1>{}, GP >> 3);
+    // lane gl keys its 8/GP consecutive tokens
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       if (j * GP >= 8) break;
-      const int o = gl + j * GP;
-      float v = best[0];
-#pragma unroll
-      for (int k = 1; k < 8; ++k) v = (o == k) ? best[k] : v;
+      const int o = gl * (8 / GP) + j;
+      const float v = best[j];
       const bool valid = on && c + o < ji.t1;
       const unsigned int key = valid ? Elem<T>::key(v) : 0u;
       if (on) {
