@@ -46,6 +46,10 @@ def _contiguous_pages(lengths, bsz, KV, max_blocks):
     ("bfloat16", 4096, "maxpool", 7, 32, LLAMA_8B),
     ("bfloat16", 1536, "avgpool", 5, 1, QWEN_7B),
     ("bfloat16", 32768, "avgpool", 5, 1, LLAMA_8B),
+    # GQA group sizes 1, 2 and 8 (the pooling's group max over 1, 2 and 8 lanes)
+    ("bfloat16", 2048, "avgpool", 5, 1, LayerGeometry(8, 8, 128)),
+    ("float16", 2500, "avgpool", 5, 1, LayerGeometry(16, 8, 128)),
+    ("bfloat16", 2048, "maxpool", 7, 1, LayerGeometry(64, 8, 128)),
 ])
 def test_prefill_select_matches_oracle(cuda_device, dtype, L, pooling, ks, window, geo):
     tdt = DT[dtype]
@@ -288,7 +292,12 @@ def test_decode_append_stages_the_query(cuda_device):
 
 
 @pytest.mark.parametrize("dtype,geo,L", [("bfloat16", LLAMA_8B, 8192), ("bfloat16", QWEN_7B, 3000),
-                                         ("float32", LLAMA_8B, 2048)])
+                                         ("float32", LLAMA_8B, 2048),
+                                         # 5 and 10 query rows; 40 rows (G = 8, the largest
+                                         # tensor-core case, query fragments in shared memory)
+                                         ("bfloat16", LayerGeometry(8, 8, 128), 4096),
+                                         ("float16", LayerGeometry(16, 8, 128), 3000),
+                                         ("bfloat16", LayerGeometry(64, 8, 128), 5000)])
 def test_drift_check_matches_oracle(cuda_device, dtype, geo, L):
     """Scoring of S buffered queries over a pivot's pages, overlap, median, trigger."""
     tdt = DT[dtype]
