@@ -89,6 +89,8 @@ class DecodeStepGraph:
         nxt = (phase + 1) % c.decode_step
         for l in self.layers:
             c._qcount[l] = nxt
+        if 0 in self.layers:  # as update() of layer 0 counts the token
+            c._seen_tokens += 1
         return self.out
 
 

@@ -89,6 +89,18 @@ def prefill_keep(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err):
     LAUNCHES[0] += 1
 
 
+def _query_rows(q, L: int, rows: int) -> int:
+    """Device address of ``q`` for the scoring launches.  They read query
+    token positions L - rows .. L - 1, the token axis aligned with the keys'
+    (in the reference q and k come from the same prompt).  A query with Lq
+    positions is rebased by Lq - L rows, so that those reads are q's own last
+    ``rows`` positions, inside the tensor, whatever its length."""
+    Lq = q.shape[2]
+    if Lq < rows:
+        raise ValueError(f"heterocache_b200: the query has {Lq} positions, the scoring reads the last {rows}")
+    return q.data_ptr() + (Lq - L) * q.stride(2) * q.element_size()
+
+
 def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, pooling, kernel_size,
                    k_pool, v_pool, block_table, heads_len, workspace: Workspace, err,
                    out_indices=None, out_scores=None):
@@ -101,7 +113,7 @@ def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, poo
     nbytes = lib().hc_prefill_select_workspace_size(dt, bsz, n_heads, L, groups, window)
     ws = workspace.get(nbytes)
     rc = lib().hc_prefill_select(dt, bsz, KV, groups, L, D, n_heads, window, POOLING[pooling], kernel_size,
-                                 _ptr(q), q.stride(0), q.stride(1), q.stride(2),
+                                 _query_rows(q, L, window), q.stride(0), q.stride(1), q.stride(2),
                                  _ptr(k), _ptr(v), k.stride(0), k.stride(1), k.stride(2),
                                  v.stride(0), v.stride(1), v.stride(2),
                                  _ptr(keep_lens), int(max_keep), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
@@ -120,7 +132,7 @@ def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, top
     nbytes = lib().hc_pivot_init_workspace_size(dt, bsz, n_pivots, L, groups)
     ws = workspace.get(nbytes)
     rc = lib().hc_pivot_init(dt, bsz, KV, groups, L, D, first_pivot, n_pivots, POOLING[pooling], kernel_size,
-                             int(topk), _ptr(q), q.stride(0), q.stride(1), q.stride(2),
+                             int(topk), _query_rows(q, L, 1), q.stride(0), q.stride(1), q.stride(2),
                              _ptr(k), k.stride(0), k.stride(1), k.stride(2),
                              _ptr(ref_positions), _ptr(ref_bitmap), _ptr(out_scores), _ptr(ws), ws.numel(),
                              _ptr(err), _stream(k))

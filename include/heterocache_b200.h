@@ -88,7 +88,10 @@ int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_
  * are contiguous, as the reference lays them out and writes them,
  * cache_utils.py:735-747 and :862-877); heads_len[row] = keep_lens[h].
  *   q: [bsz, H, L, D] strided (qsb, qsh, qst), k: [bsz, KV, L, D] strided
- *   (sb, sh, st), v: same shape strided (vsb, vsh, vst).
+ *   (sb, sh, st), v: same shape strided (vsb, vsh, vst).  Only query token
+ *   positions L - window .. L - 1 are read (q's token axis aligned with k's);
+ *   a caller holding only the last queries passes q rebased by that many
+ *   positions so that those reads stay inside its buffer.
  *   keep_lens: device int32[n_heads].
  *   out_indices (optional, may be NULL): int32 [bsz, n_heads, max_keep],
  *     kept positions ascending, -1 padded.
@@ -113,6 +116,7 @@ int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_
  * from the last query and their top-`topk` positions become the reference
  * set, stored both as ascending positions ref_positions [bsz, n_pivots, topk]
  * and as a bitmap ref_bitmap [bsz, n_pivots, ceil(L/32)] (uint32 words).
+ * q is read at token position L - 1 only (as in hc_prefill_select).
  */
 size_t hc_pivot_init_workspace_size(int dtype, int bsz, int n_pivots, int seq_len, int groups);
 int hc_pivot_init(int dtype, int bsz, int num_kv_heads, int groups, int seq_len, int head_dim,

@@ -525,3 +525,50 @@ def test_retrieve_delta_matches_full_retrieval(cuda_device):
                 assert sl[i, :r].tolist() == pos_list[:r]
     # the pools hold the second list's rows
     assert torch.equal(kp_d.cpu().view(-1, D)[0:700], full_k[0, 2, p2])
+
+
+@pytest.mark.parametrize("window", [1, 8])
+def test_scoring_reads_the_last_queries_of_a_short_query(cuda_device, window):
+    """A query holding only the last positions (the scoring reads only those)
+    gives the same pivot sets and prefill selection as the full-length query,
+    reading inside its own buffer."""
+    geo = LLAMA_8B
+    G, KV, D = geo.groups, geo.num_kv_heads, geo.head_dim
+    dev = cuda_device
+    L, nc = 3000, 3
+    q, k, v = prefill_inputs(geo, L, seed=91, dtype=torch.bfloat16)
+    q_short = q[:, :, -32:, :].contiguous()
+    kd, vd = k.to(dev), v.to(dev)
+    keep = [700, 300, 1500]
+    results = []
+    for qq in (q.to(dev), q_short.to(dev)):
+        n = sum((x + 255) // 256 for x in keep)
+        bt = torch.full((KV, (L + 255) // 256 + 1), -1, dtype=torch.int32)
+        ptr = 0
+        for h, x in enumerate(keep):
+            pages = (x + 255) // 256
+            bt[h, :pages] = torch.arange(ptr, ptr + pages, dtype=torch.int32)
+            ptr += pages
+        kp = torch.zeros(n, 256, 1, D, dtype=torch.bfloat16, device=dev)
+        vp = torch.zeros_like(kp)
+        hl = torch.zeros(KV, dtype=torch.int32, device=dev)
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        idx = torch.empty(1, nc, max(keep), dtype=torch.int32, device=dev)
+        ops.prefill_select(qq, kd, vd, torch.tensor(keep, dtype=torch.int32, device=dev), max(keep), n_heads=nc,
+                           groups=G, window=window, pooling="avgpool", kernel_size=5, k_pool=kp, v_pool=vp,
+                           block_table=bt.to(dev), heads_len=hl, workspace=Workspace(dev), err=err,
+                           out_indices=idx)
+        K = 600
+        pos = torch.empty(1, 1, K, dtype=torch.int32, device=dev)
+        bm = torch.zeros(1, 1, (L + 31) // 32, dtype=torch.int32, device=dev)
+        ops.pivot_init(qq, kd, first_pivot=KV - 1, n_pivots=1, groups=G, pooling="avgpool", kernel_size=5,
+                       topk=K, ref_positions=pos, ref_bitmap=bm, workspace=Workspace(dev), err=err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        results.append((idx.cpu(), kp.cpu(), pos.cpu(), bm.cpu()))
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
+    with pytest.raises(ValueError):
+        ops.pivot_init(q_short[:, :, :0].to(dev), kd, first_pivot=KV - 1, n_pivots=1, groups=G, pooling="avgpool",
+                       kernel_size=5, topk=600, ref_positions=pos, ref_bitmap=bm, workspace=Workspace(dev),
+                       err=err)
