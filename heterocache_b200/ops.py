@@ -89,6 +89,13 @@ def prefill_keep(k, v, keep_heads, k_pool, v_pool, block_table, heads_len, err):
     LAUNCHES[0] += 1
 
 
+def _need(ok: bool, what: str) -> None:
+    """Host-side size check of an argument the kernels index by another
+    argument's size (a short buffer would be read or written out of bounds)."""
+    if not ok:
+        raise ValueError(f"heterocache_b200: {what}")
+
+
 def _query_rows(q, L: int, rows: int) -> int:
     """Device address of ``q`` for the scoring launches.  They read query
     token positions L - rows .. L - 1, the token axis aligned with the keys'
@@ -104,6 +111,13 @@ def _query_rows(q, L: int, rows: int) -> int:
 def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, pooling, kernel_size,
                    k_pool, v_pool, block_table, heads_len, workspace: Workspace, err,
                    out_indices=None, out_scores=None):
+    bsz, KV, L = k.shape[0], k.shape[1], k.shape[-2]
+    _need(keep_lens.numel() >= n_heads, "keep_lens needs one entry per scored head")
+    _need(block_table.shape[0] >= bsz * KV and heads_len.numel() >= bsz * KV,
+          "block_table and heads_len need a row per (batch row, KV head)")
+    _need(out_indices is None or out_indices.numel() >= bsz * n_heads * max_keep,
+          "out_indices needs [bsz, n_heads, max_keep] entries")
+    _need(out_scores is None or out_scores.numel() >= bsz * n_heads * L, "out_scores needs [bsz, n_heads, L]")
     _cuda(q, k, v, keep_lens, k_pool, v_pool, block_table, heads_len, err)
     _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
     _i32(keep_lens, "keep_lens"), _i32(block_table, "block_table"), _i32(heads_len, "heads_len")
@@ -125,6 +139,10 @@ def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, poo
 
 def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, topk, ref_positions, ref_bitmap,
                workspace: Workspace, err, out_scores=None):
+    bsz, L = k.shape[0], k.shape[-2]
+    _need(ref_positions.numel() >= bsz * n_pivots * topk, "ref_positions needs [bsz, n_pivots, topk] entries")
+    _need(ref_bitmap.numel() >= bsz * n_pivots * ((L + 31) // 32), "ref_bitmap needs [bsz, n_pivots, ceil(L/32)] words")
+    _need(out_scores is None or out_scores.numel() >= bsz * n_pivots * L, "out_scores needs [bsz, n_pivots, L]")
     _cuda(q, k, ref_positions, ref_bitmap, err)
     _rows(q, "q"), _rows(k, "k")
     bsz, KV, L, D = k.shape
@@ -213,6 +231,19 @@ def drift_check(qbuf, k_pool, block_table, *, num_kv_heads, groups, steps, seq_l
                 threshold, pivot_heads, ref_slots, max_len, max_len_cap, ref_bitmap, ref_positions, trigger,
                 retrieve_positions, workspace: Workspace, err, coeffs=None, median=None, out_scores=None):
     """qbuf: [S, H, D] (strided)."""
+    n = pivot_heads.numel()
+    _need(qbuf.dim() == 3 and qbuf.shape[0] >= steps and qbuf.shape[1] == num_kv_heads * groups,
+          "qbuf needs [steps, num_kv_heads * groups, D]")
+    _need(block_table.shape[1] * 256 >= seq_len, "block_table rows must cover seq_len tokens")
+    _need(ref_slots.numel() >= n and max_len.numel() >= n and trigger.numel() >= n,
+          "ref_slots, max_len and trigger need an entry per pivot job")
+    _need(ref_positions.shape[-1] >= topk, "ref_positions rows need topk entries")
+    _need(ref_bitmap.shape[-1] >= (seq_len + 31) // 32, "ref_bitmap rows need ceil(seq_len/32) words")
+    _need(retrieve_positions.numel() >= n * max_len_cap and retrieve_positions.shape[-1] >= max_len_cap,
+          "retrieve_positions needs [jobs, max_len_cap]")
+    _need(coeffs is None or coeffs.numel() >= n * steps, "coeffs needs [jobs, steps]")
+    _need(median is None or median.numel() >= n, "median needs an entry per job")
+    _need(out_scores is None or out_scores.numel() >= n * steps * seq_len, "out_scores needs [jobs, steps, seq_len]")
     _cuda(qbuf, k_pool, block_table, pivot_heads, ref_slots, max_len, ref_bitmap, ref_positions, trigger,
           retrieve_positions, err)
     _rows(qbuf, "qbuf")
@@ -235,6 +266,9 @@ def drift_check(qbuf, k_pool, block_table, *, num_kv_heads, groups, steps, seq_l
 def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, retrieve_positions, full_k, full_v,
              k_pool, v_pool, block_table, num_kv_heads, err, stream: Optional[torch.cuda.Stream] = None):
     """full_k/full_v: [1, KV, L, D] on the device or in pinned host memory."""
+    _need(retrieve_positions.shape[-1] >= max_member_len, "retrieve_positions rows need max_member_len entries")
+    _need(member_head.numel() >= member_job.numel() and member_len.numel() >= member_job.numel(),
+          "member_head and member_len need an entry per member")
     _cuda(member_job, member_head, member_len, trigger, retrieve_positions, k_pool, v_pool, block_table, err)
     _rows(full_k, "full_k"), _rows(full_v, "full_v")
     if not full_k.is_cuda and not full_k.is_pinned():
@@ -262,6 +296,11 @@ def retrieve_delta(*, member_job, member_head, member_len, member_stage_offset, 
     of each member (ascending; seeded with the prefill kept indices, kept up
     to date here).  stage_k/stage_v [rows, D] and stage_src [rows] int32:
     device scratch, member m at rows member_stage_offset[m] + [0, len)."""
+    m = member_job.numel()
+    _need(retrieve_positions.shape[-1] >= max_member_len, "retrieve_positions rows need max_member_len entries")
+    _need(member_head.numel() >= m and member_len.numel() >= m and member_stage_offset.numel() >= m
+          and reuse_len.numel() >= m and slot_positions.shape[0] >= m,
+          "member arrays and slot_positions need an entry per member")
     _cuda(member_job, member_head, member_len, member_stage_offset, reuse_len, trigger, retrieve_positions,
           slot_positions, k_pool, v_pool, block_table, stage_k, stage_v, stage_src, err)
     _rows(full_k, "full_k"), _rows(full_v, "full_v")

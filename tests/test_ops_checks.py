@@ -1,0 +1,59 @@
+"""Host-side size checks of the op wrappers: a buffer that a kernel indexes by
+another argument's size must be large enough, or the call raises before any
+launch (these run without a GPU: the size checks come before the device
+checks)."""
+import pytest
+import torch
+
+from heterocache_b200 import ops
+
+i32 = torch.int32
+
+
+def test_drift_check_rejects_a_short_query_buffer():
+    with pytest.raises(ValueError, match="qbuf needs"):
+        ops.drift_check(torch.zeros(4, 32, 128), torch.zeros(4, 256, 1, 128), torch.zeros(8, 5, dtype=i32),
+                        num_kv_heads=8, groups=4, steps=5, seq_len=1000, pooling="avgpool", kernel_size=5,
+                        topk=200, threshold=0.5, pivot_heads=torch.zeros(1, dtype=i32),
+                        ref_slots=torch.zeros(1, dtype=i32), max_len=torch.zeros(1, dtype=i32), max_len_cap=16,
+                        ref_bitmap=torch.zeros(1, 32, dtype=i32), ref_positions=torch.zeros(1, 200, dtype=i32),
+                        trigger=torch.zeros(1, dtype=i32), retrieve_positions=torch.zeros(1, 16, dtype=i32),
+                        workspace=None, err=torch.zeros(1, dtype=i32))
+
+
+def test_drift_check_rejects_a_page_table_shorter_than_the_keys():
+    with pytest.raises(ValueError, match="block_table rows"):
+        ops.drift_check(torch.zeros(5, 32, 128), torch.zeros(4, 256, 1, 128), torch.zeros(8, 3, dtype=i32),
+                        num_kv_heads=8, groups=4, steps=5, seq_len=1000, pooling="avgpool", kernel_size=5,
+                        topk=200, threshold=0.5, pivot_heads=torch.zeros(1, dtype=i32),
+                        ref_slots=torch.zeros(1, dtype=i32), max_len=torch.zeros(1, dtype=i32), max_len_cap=16,
+                        ref_bitmap=torch.zeros(1, 32, dtype=i32), ref_positions=torch.zeros(1, 200, dtype=i32),
+                        trigger=torch.zeros(1, dtype=i32), retrieve_positions=torch.zeros(1, 16, dtype=i32),
+                        workspace=None, err=torch.zeros(1, dtype=i32))
+
+
+def test_pivot_init_rejects_a_short_bitmap():
+    with pytest.raises(ValueError, match="ref_bitmap needs"):
+        ops.pivot_init(torch.zeros(1, 32, 1, 128), torch.zeros(1, 8, 3000, 128), first_pivot=7, n_pivots=1,
+                       groups=4, pooling="avgpool", kernel_size=5, topk=600,
+                       ref_positions=torch.zeros(1, 1, 600, dtype=i32), ref_bitmap=torch.zeros(1, 1, 93, dtype=i32),
+                       workspace=None, err=torch.zeros(1, dtype=i32))
+
+
+def test_prefill_select_rejects_short_outputs():
+    with pytest.raises(ValueError, match="out_indices needs"):
+        ops.prefill_select(torch.zeros(1, 32, 1, 128), torch.zeros(1, 8, 1000, 128), torch.zeros(1, 8, 1000, 128),
+                           torch.zeros(3, dtype=i32), 400, n_heads=3, groups=4, window=1, pooling="avgpool",
+                           kernel_size=5, k_pool=torch.zeros(4, 256, 1, 128), v_pool=torch.zeros(4, 256, 1, 128),
+                           block_table=torch.zeros(8, 5, dtype=i32), heads_len=torch.zeros(8, dtype=i32),
+                           workspace=None, err=torch.zeros(1, dtype=i32), out_indices=torch.zeros(1, 3, 399, dtype=i32))
+
+
+def test_retrieve_rejects_position_rows_shorter_than_the_members():
+    with pytest.raises(ValueError, match="retrieve_positions rows"):
+        ops.retrieve(member_job=torch.zeros(2, dtype=i32), member_head=torch.zeros(2, dtype=i32),
+                     member_len=torch.zeros(2, dtype=i32), max_member_len=400, trigger=torch.zeros(1, dtype=i32),
+                     retrieve_positions=torch.zeros(1, 300, dtype=i32), full_k=torch.zeros(1, 8, 1000, 128),
+                     full_v=torch.zeros(1, 8, 1000, 128), k_pool=torch.zeros(4, 256, 1, 128),
+                     v_pool=torch.zeros(4, 256, 1, 128), block_table=torch.zeros(8, 5, dtype=i32), num_kv_heads=8,
+                     err=torch.zeros(1, dtype=i32))
