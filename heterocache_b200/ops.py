@@ -198,6 +198,10 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
     groups = H // num_kv_heads
     if out is None:
         out = torch.empty(bsz, H, D, dtype=q.dtype, device=q.device)
+    _need(out.is_contiguous() and out.numel() == bsz * H * D and out.dtype == q.dtype,
+          "out must be a contiguous [bsz, H, D] buffer in the query dtype")
+    _need(block_table.shape[0] >= bsz * num_kv_heads and heads_len.numel() >= bsz * num_kv_heads,
+          "block_table and heads_len need a row per (batch row, KV head)")
     nbytes = lib().hc_flash_decode_workspace_size(bsz, num_kv_heads, groups, D)
     ws = workspace.get(nbytes)
     if k_new is not None:
