@@ -68,3 +68,38 @@ def test_argument_validation_needs_no_gpu(built):
     # workspace sizes are pure host arithmetic
     assert lib.hc_prefill_select_workspace_size(1, 1, 5, 32768, 4, 1) > 0
     assert lib.hc_flash_decode_workspace_size(1, 8, 4, 128) > 0
+
+
+def declared_parameters():
+    """Parameter types of every declared entry point, in order."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for m in re.finditer(r"^\s*(?:const\s+)?\w+\**\s+\**(hc_\w+)\s*\(([^)]*)\)\s*;", src, flags=re.M):
+        params = [p.strip() for p in m.group(2).split(",") if p.strip()]
+        out[m.group(1)] = [] if params == ["void"] else params
+    return out
+
+
+def _ctype_for(param: str):
+    """The ctypes type a C parameter declaration maps to."""
+    from ctypes import c_double, c_float, c_int, c_int64, c_size_t, c_void_p
+    decl = param.rsplit(" ", 1)[0] if " " in param else param
+    if "*" in param:
+        return c_void_p
+    return {"int": c_int, "int64_t": c_int64, "long long": c_int64, "size_t": c_size_t, "float": c_float,
+            "double": c_double}[decl.strip()]
+
+
+def test_ctypes_argument_lists_match_the_header_declarations():
+    """Every entry point's ctypes argument list has the header's parameter
+    count and types (a drift between the two would pass wrong arguments)."""
+    from ctypes import c_int64, c_longlong
+    params = declared_parameters()
+    assert sorted(params) == declared_functions()
+    for name, (_, argtypes) in _lib.SIGNATURES.items():
+        want = [_ctype_for(p) for p in params[name]]
+        assert len(argtypes) == len(want), (name, len(argtypes), len(want))
+        for i, (got, exp) in enumerate(zip(argtypes, want)):
+            same = got is exp or {got, exp} <= {c_int64, c_longlong}
+            assert same, (name, i, params[name][i], got, exp)
