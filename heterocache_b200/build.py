@@ -2,9 +2,9 @@
 
     python -m heterocache_b200.build
 
-Compiles every ``csrc/*.cu`` for ``sm_100a`` with nvcc into one shared
-library exporting the C ABI of ``include/heterocache_b200.h``.  No GPU is
-needed to build.
+Compiles every ``csrc/*.cu`` for ``sm_100a`` with nvcc (one object per source,
+compiled in parallel) and links them into one shared library exporting the C
+ABI of ``include/heterocache_b200.h``.  No GPU is needed to build.
 """
 from __future__ import annotations
 
@@ -12,18 +12,17 @@ import glob
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 OUT = os.path.join(PKG, "libhcb200.so")
+OBJ_DIR = os.path.join(PKG, "_build")
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
-    "-O3", "-lineinfo", "-std=c++17",
-    "-Xcompiler", "-fPIC", "-shared",
-]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMPILE_FLAGS = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC"]
 
 
 def sources():
@@ -34,20 +33,31 @@ def _stale() -> bool:
     if not os.path.exists(OUT):
         return True
     t = os.path.getmtime(OUT)
-    deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(INCLUDE, "heterocache_b200.h")]
+    deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(INCLUDE, "heterocache_b200.h"),
+                                                                  os.path.abspath(__file__)]
     return any(os.path.getmtime(d) > t for d in deps)
+
+
+def _run(cmd, verbose):
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError("nvcc failed:\n" + " ".join(cmd) + "\n" + res.stdout + res.stderr)
+    return res
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return OUT
     nvcc = os.environ.get("NVCC", "nvcc")
-    cmd = [nvcc, *NVCC_FLAGS, "-I" + INCLUDE, "-o", OUT + ".tmp", *sources()]
-    if verbose:
-        print(" ".join(cmd))
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    srcs = sources()
+    objs = [os.path.join(OBJ_DIR, os.path.basename(s)[:-3] + ".o") for s in srcs]
+    cmds = [[nvcc, *COMPILE_FLAGS, "-I" + INCLUDE, "-c", s, "-o", o] for s, o in zip(srcs, objs)]
+    with ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        list(ex.map(lambda c: _run(c, verbose), cmds))
+    _run([nvcc, *ARCH, "-shared", "-o", OUT + ".tmp", *objs], verbose)
     os.replace(OUT + ".tmp", OUT)
     return OUT
 

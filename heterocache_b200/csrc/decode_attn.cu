@@ -24,6 +24,7 @@
 
 #include <utility>
 
+#include "hc_host.cuh"
 #include "hc_params.cuh"
 
 namespace hc {
@@ -747,12 +748,17 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   }
 }
 
+// Co-resident CTAs of the fp32 decode kernel on the current device (cached
+// per device).
 static int fd_grid(int dtype) {
-  static int cached[3] = {0, 0, 0};
-  if (cached[dtype]) return cached[dtype];
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static int cached[kMaxDevices][3];
+  const int dev = current_device();
+  if (dev < 0) return 0;
+  {
+    std::lock_guard<std::mutex> g(host_lock());
+    if (cached[dev][dtype]) return cached[dev][dtype];
+  }
+  const int sms = device_sms(dev);
   int occ = 0;
   size_t dsm = (kMaxRowsFD + 1) * sizeof(int);
   switch (dtype) {
@@ -761,8 +767,9 @@ static int fd_grid(int dtype) {
     default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, flash_decode_kernel<__half>, kFThreads, dsm); break;
   }
   if (occ <= 0) occ = 1;
-  cached[dtype] = sms * occ;
-  return cached[dtype];
+  std::lock_guard<std::mutex> g(host_lock());
+  cached[dev][dtype] = sms * occ;
+  return cached[dev][dtype];
 }
 
 size_t flash_decode_ws_bytes(int R, int G) {
@@ -823,15 +830,19 @@ static int fd_launch_f32(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
 
 // Tensor map of a pool viewed as a 2-D [n_blocks*256 rows, 128] array of
 // 16-bit elements, boxes of 64 rows x 64 elements, 128-byte swizzle.  Encoded
-// once per pool address (cached) through the driver entry point.
+// once per (device, pool address, rows, dtype) through the driver entry point
+// and cached.
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 static int pool_tensor_map(CUtensorMap* out, const void* base, long long rows, int dtype) {
-  struct Entry { const void* base; long long rows; int dtype; CUtensorMap map; };
+  struct Entry { int dev; const void* base; long long rows; int dtype; CUtensorMap map; };
   static Entry cache[256];
   static int n = 0, next = 0;
+  const int dev = current_device();
+  if (dev < 0) return HC_ERR_CUDA;
+  std::lock_guard<std::mutex> g(host_lock());
   for (int i = 0; i < n; ++i)
-    if (cache[i].base == base && cache[i].rows == rows && cache[i].dtype == dtype) {
+    if (cache[i].dev == dev && cache[i].base == base && cache[i].rows == rows && cache[i].dtype == dtype) {
       *out = cache[i].map;
       return HC_OK;
     }
@@ -855,6 +866,7 @@ static int pool_tensor_map(CUtensorMap* out, const void* base, long long rows, i
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return HC_ERR_CUDA;
   Entry& e = cache[n < 256 ? n++ : (next++ % 256)];
+  e.dev = dev;
   e.base = base;
   e.rows = rows;
   e.dtype = dtype;
@@ -863,13 +875,40 @@ static int pool_tensor_map(CUtensorMap* out, const void* base, long long rows, i
   return HC_OK;
 }
 
-// 16-bit pools: the TMA pipeline, rows padded to 64.  The attribute and
-// occupancy queries are made once per shared-memory size and cached.
+// Co-resident CTAs of the 16-bit TMA decode kernel for `dsm` bytes of dynamic
+// shared memory on the current device, 0 if it cannot run.  The kernel's
+// shared-memory limit is raised and the occupancy queried once per device and
+// size; later calls make no CUDA call but cudaGetDevice.
+template <typename T>
+static int fd_tma_grid(size_t dsm) {
+  static bool attr_set[kMaxDevices];
+  static ShapeCache<8> grids;
+  auto kern = flash_decode_tma_kernel<T>;
+  const int dev = current_device();
+  if (dev < 0) return 0;
+  std::lock_guard<std::mutex> g(host_lock());
+  long long v = 0;
+  if (attr_set[dev] && grids.find(dev, (long long)dsm, v)) return (int)v;
+  if (!attr_set[dev]) {
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes) !=
+        cudaSuccess)
+      return 0;
+    attr_set[dev] = true;
+  }
+  int occ = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTThreads, dsm) != cudaSuccess || occ <= 0) return 0;
+  grids.put(dev, (long long)dsm, (long long)sms * occ);
+  return sms * occ;
+}
+
+// 16-bit pools: the TMA pipeline, rows padded to 64.
 template <typename T>
 static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
-  static bool attr_set = false;
-  static size_t cache_smem[8];
-  static int cache_grid[8], n_cache = 0;
   auto kern = flash_decode_tma_kernel<T>;
   const int dtype = std::is_same<T, __nv_bfloat16>::value ? HC_BF16 : HC_F16;
   CUtensorMap tmk, tmv;
@@ -877,33 +916,8 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   if (pool_tensor_map(&tmk, p.kp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
   if (pool_tensor_map(&tmv, p.vp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
   const size_t dsm = fd_tma_smem(p.R, p.G);
-  if (!attr_set) {
-    int dev = 0, optin = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return HC_ERR_CUDA;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes) !=
-        cudaSuccess)
-      return HC_ERR_CUDA;
-    attr_set = true;
-  }
-  int grid = 0;
-  for (int i = 0; i < n_cache; ++i)
-    if (cache_smem[i] == dsm) grid = cache_grid[i];
-  if (grid == 0) {
-    int dev = 0, sms = 148, occ = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTThreads, dsm) != cudaSuccess) return HC_ERR_CUDA;
-    if (occ <= 0) return HC_ERR_UNSUPPORTED;
-    grid = sms * occ;
-    if (n_cache < 8) {
-      cache_smem[n_cache] = dsm;
-      cache_grid[n_cache] = grid;
-      ++n_cache;
-    }
-  }
+  const int grid = fd_tma_grid<T>(dsm);
+  if (grid <= 0) return HC_ERR_UNSUPPORTED;
   const size_t slots = (size_t)grid + p.R;
   if (!ws || ws_bytes < slots * p.G * kD * sizeof(float) + slots * p.G * sizeof(float2)) return HC_ERR_WORKSPACE;
   p.part_o = reinterpret_cast<float*>(ws);
@@ -919,52 +933,47 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
 // the symbol as a device address; the address is fetched with
 // cudaGetSymbolAddress once per device (on that device's first call).
 static __device__ __align__(256) unsigned char g_noalloc_scratch[HC_NOALLOC_SCRATCH_BYTES];
-static void* g_noalloc_ptr[64] = {nullptr};
+static void* g_noalloc_ptr[kMaxDevices] = {nullptr};
 
-size_t flash_decode_scratch_need(int dtype, int R, int G);
+// Partials bytes one hc_flash_decode launch writes: (grid + rows) slots of
+// G x (128 + 2) floats, the grid being the device's co-resident CTA count
+// (from the same per-device cache the launch uses).  0 if the kernel cannot
+// run.
+static size_t flash_decode_scratch_need(int dtype, int R, int G) {
+  int grid = 0;
+  switch (dtype) {
+    case HC_F32: grid = fd_grid(HC_F32); break;
+    case HC_BF16: grid = fd_tma_grid<__nv_bfloat16>(fd_tma_smem(R, G)); break;
+    case HC_F16: grid = fd_tma_grid<__half>(fd_tma_smem(R, G)); break;
+    default: return 0;
+  }
+  if (grid <= 0) return 0;
+  const size_t slots = (size_t)grid + R;
+  return slots * G * kD * sizeof(float) + slots * G * sizeof(float2);
+}
 
 int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_t* need_out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return HC_ERR_CUDA;
-  if (dev < 0 || dev >= 64) return HC_ERR_UNSUPPORTED;
-  if (!g_noalloc_ptr[dev]) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return HC_ERR_CUDA;
-    g_noalloc_ptr[dev] = ptr;
+  // the same argument checks, in the same order, as flash_decode_dispatch
+  if (p.R <= 0 || p.R > kMaxRowsFD) return HC_ERR_UNSUPPORTED;
+  if (p.G <= 0 || p.G > kGMax) return HC_ERR_UNSUPPORTED;
+  if (dtype != HC_F32 && dtype != HC_BF16 && dtype != HC_F16) return HC_ERR_DTYPE;
+  const int dev = current_device();
+  if (dev < 0) return HC_ERR_UNSUPPORTED;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> g(host_lock());
+    if (!g_noalloc_ptr[dev]) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || !ptr) return HC_ERR_CUDA;
+      g_noalloc_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_ptr[dev];
   }
   const size_t need = flash_decode_scratch_need(dtype, p.R, p.G);
   if (need_out) *need_out = need;
-  if (need == 0) return HC_ERR_CUDA;
+  if (need == 0) return HC_ERR_UNSUPPORTED;
   if (need > (size_t)HC_NOALLOC_SCRATCH_BYTES) return HC_ERR_WORKSPACE;
-  return flash_decode_dispatch(dtype, p, g_noalloc_ptr[dev], HC_NOALLOC_SCRATCH_BYTES, st);
-}
-
-// Partials bytes one hc_flash_decode launch writes: (grid + rows) slots of
-// G x (128 + 2) floats; the grid is the device's co-resident CTA count.
-size_t flash_decode_scratch_need(int dtype, int R, int G) {
-  int grid = 0;
-  if (dtype == HC_F32) {
-    grid = fd_grid(HC_F32);
-  } else {
-    int dev = 0, sms = 148, occ = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t dsm = fd_tma_smem(R, G);
-    const void* kern = dtype == HC_BF16 ? (const void*)flash_decode_tma_kernel<__nv_bfloat16>
-                                        : (const void*)flash_decode_tma_kernel<__half>;
-    int optin = 0;
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return 0;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes) !=
-        cudaSuccess)
-      return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kTThreads, dsm) != cudaSuccess || occ <= 0)
-      return 0;
-    grid = sms * occ;
-  }
-  const size_t slots = (size_t)grid + R;
-  return slots * G * kD * sizeof(float) + slots * G * sizeof(float2);
+  return flash_decode_dispatch(dtype, p, scratch, HC_NOALLOC_SCRATCH_BYTES, st);
 }
 
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {

@@ -3,6 +3,7 @@
 //   decode append            (heterocache/cache_utils.py:970-1005)
 //   satellite retrieval      (heterocache/cache_utils.py:1084-1147)
 // All three move whole 128-element rows with 16-byte vector accesses.
+#include "hc_host.cuh"
 #include "hc_params.cuh"
 
 namespace hc {
@@ -542,13 +543,7 @@ static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const
                       cudaStream_t s) {
   if (n_members == 0 || max_len <= 0) return HC_OK;
   // one wave: 8 CTAs of 256 threads per SM
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = device_sms(current_device());
   const int per_member = (max_len + 63) / 64;
   const long long items = (long long)per_member * n_members;
   cudaLaunchConfig_t cfg = {};
@@ -570,13 +565,7 @@ static int retrieve_t(int n_members, const int32_t* mj, const int32_t* mh, const
 template <typename T>
 static int retrieve_delta_t(DeltaArgs& a, int max_len, cudaStream_t s) {
   if (a.n_members == 0 || max_len <= 0) return HC_OK;
-  static int sms = 0;
-  if (sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
+  const int sms = device_sms(current_device());
   a.items_per_member = (max_len + 63) / 64;
   const long long items = (long long)a.items_per_member * a.n_members;
   if (items > 0x7fffffffLL) return HC_ERR_UNSUPPORTED;

@@ -29,6 +29,7 @@
 // Rounding points follow the reference exactly: q.K^T rounded to the model
 // dtype, then divided by sqrt(d) and rounded, fp32 softmax rounded to the
 // dtype, the window sum rounded, the pooling output rounded.
+#include "hc_host.cuh"
 #include "hc_params.cuh"
 
 namespace hc {
@@ -1250,17 +1251,7 @@ struct ScorePlan {
   bool logits_in_smem;
 };
 
-static int g_num_sms = 0;
-
-static int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
+static int num_sms() { return device_sms(current_device()); }
 
 template <typename T>
 static size_t smem_bytes(int Rq, int S, int T_, int TB, bool logits_in_smem, bool fma) {
@@ -1336,32 +1327,33 @@ static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size
   p.T = pl.T;
   p.TB = pl.TB;
   auto kern = score_select_kernel<T, MODE>;
-  // Attribute and occupancy queries are made once per shared-memory size and
-  // cached, so a launch issues no non-stream CUDA call (graph capture safe
-  // after the first launch of a given shape).
-  static bool attr_set = false;
-  static int cache_smem[16], cache_occ[16], n_cache = 0;
-  if (!attr_set) {
-    int dev = 0, optin = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return HC_ERR_CUDA;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)fa.sharedSizeBytes) != cudaSuccess)
-      return HC_ERR_CUDA;
-    attr_set = true;
-  }
+  // Attribute and occupancy queries are made once per device and shared-memory
+  // size and cached, so a launch issues no non-stream CUDA call (graph capture
+  // safe after the first launch of a given shape).
+  static bool attr_set[kMaxDevices];
+  static ShapeCache<16> occs;
+  const int dev = current_device();
+  if (dev < 0) return HC_ERR_CUDA;
   int occ = -1;
-  for (int i = 0; i < n_cache; ++i)
-    if (cache_smem[i] == (int)pl.smem) occ = cache_occ[i];
-  if (occ < 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSThreads, pl.smem) != cudaSuccess)
-      return HC_ERR_CUDA;
-    if (n_cache < 16) {
-      cache_smem[n_cache] = (int)pl.smem;
-      cache_occ[n_cache] = occ;
-      ++n_cache;
+  {
+    std::lock_guard<std::mutex> g(host_lock());
+    if (!attr_set[dev]) {
+      int optin = 0;
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return HC_ERR_CUDA;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               optin - (int)fa.sharedSizeBytes) != cudaSuccess)
+        return HC_ERR_CUDA;
+      attr_set[dev] = true;
+    }
+    long long v = 0;
+    if (occs.find(dev, (long long)pl.smem, v)) {
+      occ = (int)v;
+    } else {
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSThreads, pl.smem) != cudaSuccess)
+        return HC_ERR_CUDA;
+      occs.put(dev, (long long)pl.smem, occ);
     }
   }
   if ((long long)occ * num_sms() < pl.grid) return HC_ERR_UNSUPPORTED;

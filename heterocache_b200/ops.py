@@ -190,6 +190,9 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
     [bsz, KV, 1, D] each row also attends to that token (not in the pages);
     then q_stage (bsz 1: a contiguous [H, D] buffer) also receives the query
     rows."""
+    H = q.shape[1]
+    _need(num_kv_heads > 0 and H % num_kv_heads == 0,
+          f"the {H} query heads do not split evenly over {num_kv_heads} KV heads")
     _cuda(q, k_pool, v_pool, block_table, heads_len, err, k_new, v_new, q_stage)
     _rows(q, "q")
     bsz, H, one, D = q.shape

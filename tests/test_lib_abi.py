@@ -57,6 +57,12 @@ def test_argument_validation_needs_no_gpu(built):
                                  None, 0, None, None, 1, None, 1, None, None, None, None, 0, None, None) == 1
     assert lib.hc_drift_check(1, 8, 4, 128, 9, 1000, 0, 5, 10, 0.5, None, 0, 0, None, 1, None, 4, 1, None,
                               None, None, 1, None, None, None, None, None, None, None, None, 0, None, None) == 8
+    # the entry point without a workspace checks rows and groups first, with
+    # the same codes as hc_flash_decode (8 = unsupported configuration)
+    assert lib.hc_flash_decode_noalloc(1, 1000, 8, 4, 128, None, 0, 0, None, None, 1, None, 1, None, 0.0, None,
+                                       None, None) == 8
+    assert lib.hc_flash_decode_noalloc(1, 1, 8, 16, 128, None, 0, 0, None, None, 1, None, 1, None, 0.0, None,
+                                       None, None) == 8
     # nothing to do is not an error
     assert lib.hc_retrieve(1, 8, 128, 0, None, None, None, 0, None, None, 0, None, None, 0, 0, None, None, 1,
                            None, 1, None, None) == 0

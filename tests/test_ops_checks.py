@@ -57,3 +57,12 @@ def test_retrieve_rejects_position_rows_shorter_than_the_members():
                      full_v=torch.zeros(1, 8, 1000, 128), k_pool=torch.zeros(4, 256, 1, 128),
                      v_pool=torch.zeros(4, 256, 1, 128), block_table=torch.zeros(8, 5, dtype=i32), num_kv_heads=8,
                      err=torch.zeros(1, dtype=i32))
+
+
+def test_flash_decode_rejects_query_heads_that_do_not_split_over_the_kv_heads():
+    """30 query heads over 8 KV heads: the kernels would write only 8 x 3 of
+    the 30 output heads, so the call raises before allocating or launching."""
+    with pytest.raises(ValueError, match="do not split evenly"):
+        ops.flash_decode(torch.zeros(1, 30, 1, 128), torch.zeros(4, 256, 1, 128), torch.zeros(4, 256, 1, 128),
+                         torch.zeros(8, 5, dtype=i32), torch.zeros(8, dtype=i32), num_kv_heads=8, workspace=None,
+                         err=torch.zeros(1, dtype=i32))
