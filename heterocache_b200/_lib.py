@@ -27,6 +27,11 @@ SIGNATURES = {
                                   c_int64, c_int64, c_int64, c_int64,
                                   c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_snapkv_update_kv_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "hc_snapkv_update_kv": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                    c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                                    c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_size_t, c_void_p, c_void_p]),
     "hc_pivot_init_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "hc_pivot_init": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
                               c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64,

@@ -135,6 +135,73 @@ int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_
   return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
 }
 
+size_t hc_snapkv_update_kv_workspace_size(int dtype, int bsz, int num_heads, int seq_len, int window) {
+  if (bsz <= 0 || num_heads <= 0 || seq_len <= 0 || window <= 0) return 0;
+  return hc::score_workspace_size(dtype, bsz * num_heads, seq_len, window, 1);
+}
+
+int hc_snapkv_update_kv(int dtype, int bsz, int num_heads, int seq_len, int head_dim, int window, int pooling,
+                        int kernel_size, int capacity, const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                        const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh,
+                        int64_t vst, void* out_k, void* out_v, int32_t* out_indices, void* out_scores,
+                        void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_heads <= 0 || seq_len <= 0) return HC_ERR_INVALID;
+  if (window < 1 || window >= seq_len) return HC_ERR_INVALID;
+  if (capacity < window || capacity > seq_len) return HC_ERR_INVALID;
+  if (pooling != HC_AVGPOOL && pooling != HC_MAXPOOL) return HC_ERR_INVALID;
+  if (kernel_size < 1 || (kernel_size & 1) == 0 || kernel_size / 2 > 16) return HC_ERR_INVALID;
+  if (window > 256) return HC_ERR_UNSUPPORTED;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out_k) || !aligned16(out_v))
+    return HC_ERR_INVALID;
+  if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh) || !stride_ok(dtype, qst) || !stride_ok(dtype, sb) ||
+      !stride_ok(dtype, sh) || !stride_ok(dtype, st) || !stride_ok(dtype, vsb) || !stride_ok(dtype, vsh) ||
+      !stride_ok(dtype, vst))
+    return HC_ERR_INVALID;
+  hc::ScoreParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.mode = hc::MODE_PREFILL;
+  p.L = seq_len;
+  p.Lsel = seq_len - window;
+  p.G = 1;
+  p.W = window;
+  p.S = 1;
+  p.Rq = window;
+  p.pooling = pooling;
+  p.ksize = kernel_size;
+  p.halo = kernel_size / 2;
+  p.sqrt_d = div_sqrt_d(head_dim);
+  p.n_jobs = bsz * num_heads;
+  p.KV = num_heads;
+  p.nh = num_heads;
+  p.nsel = 1;
+  p.keep_lens = nullptr;
+  p.keep_const = capacity - window;
+  p.tail = window;
+  p.out_job_rows = capacity;
+  p.q = q;
+  p.qsb = qsb;
+  p.qsh = qsh;
+  p.qst = qst;
+  p.q_tok0 = seq_len - window;
+  p.k = k;
+  p.v = v;
+  p.ksb = sb;
+  p.ksh = sh;
+  p.kst = st;
+  p.vsb = vsb;
+  p.vsh = vsh;
+  p.vst = vst;
+  p.k_pool_out = out_k;
+  p.v_pool_out = out_v;
+  p.heads_len = nullptr;
+  p.out_indices = out_indices;
+  p.max_keep = capacity - window;
+  p.out_scores = out_scores;
+  p.err = err_flag;
+  return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
 size_t hc_pivot_init_workspace_size(int dtype, int bsz, int n_pivots, int seq_len, int groups) {
   if (bsz <= 0 || n_pivots <= 0 || seq_len <= 0) return 0;
   return hc::score_workspace_size(dtype, bsz * n_pivots, seq_len, groups, 1);

@@ -44,6 +44,16 @@ struct ScoreParams {
   int32_t* out_indices;
   int32_t* keep_pos;  // workspace: prefill kept positions [job][rank] (set at launch)
   int max_keep;
+  // PREFILL only.  Lsel: positions [0, Lsel) are pooled and may be selected
+  // (L for HeteroCache; L - window for SnapKV, whose window rows are kept
+  // whole).  keep_const: the keep length of every head when keep_lens is
+  // null.  tail: the last `tail` key/value rows follow each head's kept rows.
+  // out_job_rows > 0: dense output, job j's rows start at row j*out_job_rows
+  // of k_pool_out / v_pool_out (else flat slots from the row's first page).
+  int Lsel;
+  int keep_const;
+  int tail;
+  int64_t out_job_rows;
   void* out_scores;
   const int32_t* ref_slots;
   uint32_t* ref_bitmap;

@@ -463,11 +463,11 @@ __device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* l
           else w[i] = Elem<T>::rnd(w[i]);
         }
       }
-      if (c - HALO < 0 || c + 8 + HALO > p.L) {
+      if (c - HALO < 0 || c + 8 + HALO > p.Lsel) {
 #pragma unroll
         for (int i = 8 - HALO; i < 16 + HALO; ++i) {
           const int t = c - 8 + i;
-          if (t < 0 || t >= p.L) w[i] = pad;
+          if (t < 0 || t >= p.Lsel) w[i] = pad;
         }
       }
 #pragma unroll
@@ -513,7 +513,7 @@ __device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* l
       if (j * GP >= 8) break;
       const int o = gl * (8 / GP) + j;
       const float v = best[j];
-      const bool valid = on && c + o < ji.t1;
+      const bool valid = on && c + o < ji.t1 && c + o < p.Lsel;
       const unsigned int key = valid ? Elem<T>::key(v) : 0u;
       if (on) {
         keys[s * p.T + (c - ji.t0) + o] = key;
@@ -537,8 +537,9 @@ __device__ void pooled_keys_wide(const ScoreParams& p, const JobInfo& ji, const 
     const int i = i0 + threadIdx.x;
     const bool on = i < p.S * ntok;
     const int s = on ? i / ntok : 0, t = ji.t0 + (on ? i % ntok : 0);
+    const bool valid = on && t < p.Lsel;
     unsigned int key = 0u;
-    if (on) {
+    if (valid) {
       float best = -INFINITY;
       for (int g = 0; g < p.G; ++g) {
         const T* row = lg + (int64_t)((s * p.G + g) * p.W) * p.TB - base;
@@ -546,12 +547,12 @@ __device__ void pooled_keys_wide(const ScoreParams& p, const JobInfo& ji, const 
         if (p.pooling == HC_AVGPOOL) {
           float acc = 0.f;
           for (int j = t - p.halo; j <= t + p.halo; ++j)
-            if (j >= 0 && j < p.L) acc += Elem<T>::to_f(row[j]);
+            if (j >= 0 && j < p.Lsel) acc += Elem<T>::to_f(row[j]);
           v = Elem<T>::rnd(acc / (float)p.ksize);
         } else {
           v = -INFINITY;
           for (int j = t - p.halo; j <= t + p.halo; ++j)
-            if (j >= 0 && j < p.L) v = fmaxf(v, Elem<T>::to_f(row[j]));
+            if (j >= 0 && j < p.Lsel) v = fmaxf(v, Elem<T>::to_f(row[j]));
         }
         best = fmaxf(best, v);
       }
@@ -562,7 +563,8 @@ __device__ void pooled_keys_wide(const ScoreParams& p, const JobInfo& ji, const 
         os[((size_t)ji.job * p.S + s) * p.L + t] = Elem<T>::from_f(best);
       }
     }
-    hist_add_warp(lhist, on, ((unsigned int)s << 8) | (key >> (KB - 8)));
+    if (on && !valid) keys[s * p.T + (t - ji.t0)] = 0u;
+    hist_add_warp(lhist, valid, ((unsigned int)s << 8) | (key >> (KB - 8)));
   }
 }
 
@@ -613,6 +615,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   ScoreParams p = pin;
   p.mode = MODE;
   if constexpr (MODE != MODE_PREFILL) p.W = 1;
+  if (MODE != MODE_PREFILL || p.Lsel <= 0 || p.Lsel > p.L) p.Lsel = p.L;
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq], s_rowR[kMaxRq];
   __shared__ unsigned int s_prefix[kMaxSel], s_mask[kMaxSel], s_rem[kMaxSel], s_k[kMaxSel];
@@ -860,7 +863,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   if (threadIdx.x < p.nsel) {
     const int sel = threadIdx.x;
     int k, row;
-    if (p.mode == MODE_PREFILL) { k = p.keep_lens[ji.h]; row = 0; }
+    if (p.mode == MODE_PREFILL) { k = p.keep_lens ? p.keep_lens[ji.h] : p.keep_const; row = 0; }
     else if (p.mode == MODE_PIVOT) { k = p.topk; row = 0; }
     else if (sel < p.S) { k = p.topk; row = sel; }
     else { k = p.max_len[ji.job]; row = p.S - 1; }
@@ -893,7 +896,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
       __syncthreads();
       for (int sel = 0; sel < p.nsel; ++sel) {
         const unsigned int k = s_k[sel];
-        if (k == 0u || k >= (unsigned int)p.L) continue;  // trivial selects
+        if (k == 0u || k >= (unsigned int)p.Lsel) continue;  // trivial selects
         const unsigned int pre = s_prefix[sel], msk = s_mask[sel];
         const unsigned int* kr = keys + s_sel_row[sel] * p.T;
         unsigned int ngt = 0;
@@ -917,7 +920,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
         // per digit b: (keys above prefix|b, keys equal to it), one warp per select
         for (int sel = warp; sel < p.nsel; sel += kSWarps) {
           const unsigned int k = s_k[sel];
-          if (k == 0u || k >= (unsigned int)p.L) continue;
+          if (k == 0u || k >= (unsigned int)p.Lsel) continue;
           unsigned int c8[8], tot = 0;
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -952,7 +955,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
     // one warp per select
     for (int sel = warp; sel < p.nsel; sel += kSWarps) {
       const unsigned int k = s_k[sel];
-      if (k == 0u || k >= (unsigned int)p.L) continue;
+      if (k == 0u || k >= (unsigned int)p.Lsel) continue;
       unsigned int above;
       int bin = find_bin(lhist + sel * 256, s_rem[sel], above);
       if (lane == 0) {
@@ -970,8 +973,8 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   for (int sel = warp; sel < p.nsel; sel += kSWarps) {
     const unsigned int k = s_k[sel];
     long long gtb = 0, eqb = 0;
-    if (k >= (unsigned int)p.L) {
-      gtb = (long long)ji.part * p.T;  // everything before is selected
+    if (k >= (unsigned int)p.Lsel) {
+      gtb = min((long long)ji.part * p.T, (long long)p.Lsel);  // everything eligible before is selected
     } else if (k > 0u) {
       const int b = (int)(s_prefix[sel] & 255u);
       const int2* cj = p.cnt + (((size_t)ji.job * kMaxSel + sel) * 256 + b) * p.cpj;
@@ -1003,7 +1006,13 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   if (threadIdx.x < p.nsel) {
     const int sel = threadIdx.x;
     const unsigned int k = s_k[sel];
-    if (k >= (unsigned int)p.L) { s_prefix[sel] = 0u; s_rem[sel] = 0x7fffffffu; }
+    // take everything: every key at or above 0 (all of them), or, with
+    // ineligible positions (key 0), every key above 1 (scores are
+    // non-negative, so eligible keys are at least the key of +0)
+    if (k >= (unsigned int)p.Lsel) {
+      if (p.Lsel == p.L) { s_prefix[sel] = 0u; s_rem[sel] = 0x7fffffffu; }
+      else { s_prefix[sel] = 1u; s_rem[sel] = 0u; }
+    }
     else if (k == 0u) { s_prefix[sel] = 0xffffffffu; s_rem[sel] = 0u; }
   }
   __syncthreads();
@@ -1101,7 +1110,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
         }
       }
     });
-    if (ji.part == 0 && threadIdx.x == 0) p.heads_len[row] = kk;
+    if (p.heads_len && ji.part == 0 && threadIdx.x == 0) p.heads_len[row] = kk;
     if (p.out_indices && ji.part == p.cpj - 1) {
       for (int i = kk + threadIdx.x; i < p.max_keep; i += kSThreads)
         p.out_indices[(size_t)ji.job * p.max_keep + i] = -1;
@@ -1111,35 +1120,52 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
     // 3. kept K/V rows to their pages: the rows of all jobs (in job, then
     //    rank order) split into equal contiguous shares, one per CTA, so that
     //    CTAs whose tokens hold many kept positions do not set the end.
-    //    Flat slots from each row's first page (prefill pages are contiguous).
+    //    Flat slots from each row's first page (prefill pages are contiguous),
+    //    or, with a dense output, rows from job * out_job_rows.  Each job's
+    //    kept rows are followed by its last `tail` rows (SnapKV's window).
     constexpr int CH = kD * (int)sizeof(T) / 16;  // 16-byte chunks per row
     constexpr int PER = (2 * CH + 31) / 32;        // chunks per lane per row (K and V)
     constexpr int NQ = std::is_same<T, float>::value ? 4 : 8;  // rows in flight per warp
+    auto keep_of = [&](int h) { return min(max(p.keep_lens ? p.keep_lens[h] : p.keep_const, 0), p.Lsel); };
     long long total = 0;
-    for (int jb = 0; jb < p.n_jobs; ++jb) total += min(max(p.keep_lens[jb % p.nh], 0), p.L);
+    for (int jb = 0; jb < p.n_jobs; ++jb) total += keep_of(jb % p.nh) + p.tail;
     const long long share = (total + nblocks - 1) / nblocks;
     const long long g0 = (long long)blockIdx.x * share, g1 = min(total, g0 + share);
     long long off = 0;
     for (int jb = 0; jb < p.n_jobs && off < g1; ++jb) {
       const int bj = jb / p.nh, hj = jb % p.nh;
-      const int nj = min(max(p.keep_lens[hj], 0), p.L);
+      const int keepj = keep_of(hj);
+      const int nj = keepj + p.tail;
       const long long a = max(g0, off), e = min(g1, off + nj);
       if (a < e) {
-        const int rowj = bj * p.KV + hj;
-        const int start = p.bt[(int64_t)rowj * p.max_blocks];
-        if (start < 0 || (int64_t)start * kPage + nj > (int64_t)p.n_blocks * kPage) {
+        T* kdst;
+        T* vdst;
+        bool ok;
+        if (p.out_job_rows > 0) {
+          ok = nj <= p.out_job_rows;
+          kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)jb * p.out_job_rows * kD;
+          vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)jb * p.out_job_rows * kD;
+        } else {
+          const int rowj = bj * p.KV + hj;
+          const int start = p.bt[(int64_t)rowj * p.max_blocks];
+          ok = !(start < 0 || (int64_t)start * kPage + nj > (int64_t)p.n_blocks * kPage);
+          kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)max(start, 0) * kPage * kD;
+          vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)max(start, 0) * kPage * kD;
+        }
+        if (!ok) {
           if (threadIdx.x == 0) set_err(p.err, HC_ERR_RANGE);
         } else {
           const int32_t* pl = p.keep_pos + (size_t)jb * p.L;
           const T* kbase = reinterpret_cast<const T*>(p.k) + bj * p.ksb + (int64_t)hj * p.ksh;
           const T* vbase = reinterpret_cast<const T*>(p.v) + bj * p.vsb + (int64_t)hj * p.vsh;
-          T* kdst = reinterpret_cast<T*>(p.k_pool_out) + (int64_t)start * kPage * kD;
-          T* vdst = reinterpret_cast<T*>(p.v_pool_out) + (int64_t)start * kPage * kD;
           const int r_lo = (int)(a - off), r_hi = (int)(e - off);
           for (int rb = r_lo + warp * NQ; rb < r_hi; rb += kSWarps * NQ) {
             int tt[NQ];
 #pragma unroll
-            for (int q = 0; q < NQ; ++q) tt[q] = rb + q < r_hi ? __ldcg(pl + rb + q) : -1;
+            for (int q = 0; q < NQ; ++q) {
+              const int r = rb + q;
+              tt[q] = r >= r_hi ? -1 : r < keepj ? __ldcg(pl + r) : p.L - p.tail + (r - keepj);
+            }
             uint4 buf[NQ][PER];
 #pragma unroll
             for (int q = 0; q < NQ; ++q)

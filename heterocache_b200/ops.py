@@ -137,6 +137,46 @@ def prefill_select(q, k, v, keep_lens, max_keep, *, n_heads, groups, window, poo
     LAUNCHES[0] += 1
 
 
+def snapkv_update_kv(q, k, v, *, window, pooling, kernel_size, capacity, workspace: Workspace, err,
+                     out_indices=None, out_scores=None):
+    """SnapKV compression (heterocache/kv_cluster.py:155-199) of one layer:
+    q, k, v [bsz, H, L, D] -> (k_out, v_out) [bsz, H, capacity, D], the kept
+    rows of each head in ascending position order followed by its last
+    ``window`` rows."""
+    if pooling not in POOLING:
+        raise ValueError("Pooling method not supported")
+    _same_shape(k, v)
+    bsz, H, L, D = k.shape
+    if q.shape[1] != H:
+        raise RuntimeError(f"heterocache_b200: SnapKV scores every query head against its own key head "
+                           f"({q.shape[1]} query heads, {H} key heads)")
+    _need(1 <= window < L, f"window {window} must lie in [1, {L})")
+    _need(window <= capacity <= L, f"capacity {capacity} must lie in [window, {L}]")
+    _need(out_indices is None or (out_indices.dtype == torch.int32 and out_indices.is_contiguous()
+                                  and out_indices.numel() >= bsz * H * (capacity - window)),
+          "out_indices needs a contiguous int32 [bsz, H, capacity - window]")
+    _need(out_scores is None or (out_scores.dtype == k.dtype and out_scores.is_contiguous()
+                                 and out_scores.numel() >= bsz * H * L),
+          "out_scores needs a contiguous [bsz, H, L] in the key dtype")
+    _cuda(q, k, v, err, out_indices, out_scores)
+    _rows(q, "q"), _rows(k, "k"), _rows(v, "v")
+    if q.dtype != k.dtype:
+        raise ValueError("heterocache_b200: q and k must share a dtype")
+    k_out = torch.empty(bsz, H, capacity, D, dtype=k.dtype, device=k.device)
+    v_out = torch.empty_like(k_out)
+    dt = dtype_code(k)
+    nbytes = lib().hc_snapkv_update_kv_workspace_size(dt, bsz, H, L, window)
+    ws = workspace.get(nbytes)
+    rc = lib().hc_snapkv_update_kv(dt, bsz, H, L, D, int(window), POOLING[pooling], int(kernel_size), int(capacity),
+                                   _query_rows(q, L, window), q.stride(0), q.stride(1), q.stride(2),
+                                   _ptr(k), _ptr(v), k.stride(0), k.stride(1), k.stride(2),
+                                   v.stride(0), v.stride(1), v.stride(2), _ptr(k_out), _ptr(v_out),
+                                   _ptr(out_indices), _ptr(out_scores), _ptr(ws), ws.numel(), _ptr(err), _stream(k))
+    check("hc_snapkv_update_kv", rc)
+    LAUNCHES[0] += 1
+    return k_out, v_out
+
+
 def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, topk, ref_positions, ref_bitmap,
                workspace: Workspace, err, out_scores=None):
     bsz, L = k.shape[0], k.shape[-2]

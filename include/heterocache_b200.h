@@ -110,6 +110,40 @@ int hc_prefill_select(int dtype, int bsz, int num_kv_heads, int groups, int seq_
                       void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Prefill: SnapKV compression of one layer.  Replaces
+ * SnapKVCluster.update_kv (heterocache/kv_cluster.py:155-199) once the
+ * caller has decided to compress (capacity <= seq_len; the reference returns
+ * its inputs unchanged otherwise).  For every (batch row, head): the last
+ * `window` queries score all seq_len keys (q.K^T / sqrt(D) in the model
+ * dtype, the in-window causal mask, fp32 softmax cast to the dtype), the
+ * window rows are summed, the sums of positions 0 .. seq_len-window-1 are
+ * pooled (avg_pool1d with count_include_pad, or max_pool1d; kernel_size odd,
+ * padding kernel_size/2) and the top (capacity - window) of them are kept.
+ *   q: [bsz, H, L, D] strided (qsb, qsh, qst; only the last `window`
+ *   positions are read, aligned with k as in hc_prefill_select); k, v:
+ *   [bsz, H, L, D] strided (one key head per query head, as the reference's
+ *   matmul requires).
+ *   out_k, out_v: contiguous [bsz, H, capacity, D]: per head the kept rows
+ *   in ascending position order, then the last `window` rows.  (The
+ *   reference orders the kept rows by descending score; attention over the
+ *   rows does not depend on their order.)
+ *   out_indices (optional): int32 [bsz, H, capacity - window], kept
+ *   positions ascending.  out_scores (optional): [bsz, H, L] pooled scores in
+ *   the model dtype at positions 0 .. L-window-1 (the rest is not written).
+ * Ties at the k-th score go to the lowest positions (torch.topk leaves their
+ * order unspecified).  1 <= window < seq_len, window <= 256,
+ * window <= capacity <= seq_len.
+ */
+size_t hc_snapkv_update_kv_workspace_size(int dtype, int bsz, int num_heads, int seq_len, int window);
+int hc_snapkv_update_kv(int dtype, int bsz, int num_heads, int seq_len, int head_dim, int window, int pooling,
+                        int kernel_size, int capacity,
+                        const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                        const void* k, const void* v, int64_t sb, int64_t sh, int64_t st,
+                        int64_t vsb, int64_t vsh, int64_t vst,
+                        void* out_k, void* out_v, int32_t* out_indices, void* out_scores,
+                        void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Prefill: pivot reference sets.  Replaces HeteroCache.init_coefficient
  * (heterocache/cache_utils.py:1149-1190): pivot heads first_pivot ..
  * first_pivot+n_pivots-1 (contiguous after the role permutation) are scored

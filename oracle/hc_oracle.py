@@ -76,11 +76,11 @@ def window_scores(q_win: torch.Tensor, k: torch.Tensor, *, groups: int, pooling:
     return pooled.view(bsz, nh, groups, L).max(dim=-2).values
 
 
-def snapkv_indices(q: torch.Tensor, k: torch.Tensor, *, window: int, kernel_size: int,
-                   pooling: str, capacity: int) -> torch.Tensor:
-    """SnapKV's selection (heterocache/kv_cluster.py:160-186) for per-query-head
-    keys [bsz, H, L, D]: top-(capacity - window) of the pooled window sum over
-    the first L - window positions.  Used only to pin the window math."""
+def snapkv_scores(q: torch.Tensor, k: torch.Tensor, *, window: int, kernel_size: int,
+                  pooling: str) -> torch.Tensor:
+    """SnapKV's pooled window sums (heterocache/kv_cluster.py:168-184) for
+    per-query-head keys [bsz, H, L, D]: the scores its top-k ranks, over the
+    first L - window positions, in the model dtype."""
     W = window
     D = q.shape[-1]
     logits = torch.matmul(q[..., -W:, :], k.transpose(2, 3)) / math.sqrt(D)
@@ -90,8 +90,15 @@ def snapkv_indices(q: torch.Tensor, k: torch.Tensor, *, window: int, kernel_size
     logits[:, :, -W:, -W:] += mask[None, None].to(logits.dtype)
     p = F.softmax(logits, dim=-1, dtype=torch.float32).to(q.dtype)
     s = p[:, :, -W:, :-W].sum(dim=-2)
-    pooled = _pool(s, pooling, kernel_size)
-    return pooled.topk(capacity - W, dim=-1).indices
+    return _pool(s, pooling, kernel_size)
+
+
+def snapkv_indices(q: torch.Tensor, k: torch.Tensor, *, window: int, kernel_size: int,
+                   pooling: str, capacity: int) -> torch.Tensor:
+    """SnapKV's selection (heterocache/kv_cluster.py:160-186): top-(capacity -
+    window) of the pooled window sums, in the reference's (score) order."""
+    pooled = snapkv_scores(q, k, window=window, kernel_size=kernel_size, pooling=pooling)
+    return pooled.topk(capacity - window, dim=-1).indices
 
 
 def paged_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_table: torch.Tensor,

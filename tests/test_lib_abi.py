@@ -63,6 +63,12 @@ def test_argument_validation_needs_no_gpu(built):
                                        None, None) == 8
     assert lib.hc_flash_decode_noalloc(1, 1, 8, 16, 128, None, 0, 0, None, None, 1, None, 1, None, 0.0, None,
                                        None, None) == 8
+    # SnapKV: the window must leave positions to select from, and the
+    # capacity must hold the window (the reference's topk would fail)
+    snap = (None, 0, 0, 0, None, None, 0, 0, 0, 0, 0, 0, None, None, None, None, None, 0, None, None)
+    assert lib.hc_snapkv_update_kv(1, 1, 4, 100, 128, 100, 0, 5, 100, *snap) == 1
+    assert lib.hc_snapkv_update_kv(1, 1, 4, 100, 128, 8, 0, 5, 7, *snap) == 1
+    assert lib.hc_snapkv_update_kv(1, 1, 4, 100, 128, 8, 0, 4, 50, *snap) == 1
     # nothing to do is not an error
     assert lib.hc_retrieve(1, 8, 128, 0, None, None, None, 0, None, None, 0, None, None, 0, 0, None, None, 1,
                            None, 1, None, None) == 0
