@@ -18,6 +18,7 @@ SIGNATURES = {
     "hc_abi_version": (c_int, []),
     "hc_status_string": (ctypes.c_char_p, [c_int]),
     "hc_last_cuda_error": (ctypes.c_char_p, []),
+    "hc_set_wait_limits": (c_int, [ctypes.c_ulonglong, c_int]),
     "hc_prefill_keep": (c_int, [c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                 c_int64, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int,
                                 c_void_p, c_int, c_void_p, c_void_p, c_void_p]),

@@ -333,11 +333,16 @@ class HeteroCache(_CacheBase):
                 self.key_cache_cpu.append(None)
                 self.value_cache_cpu.append(None)
             elif self.real_offload:
+                try:
+                    kc = torch.empty(key_states.shape, dtype=key_states.dtype, pin_memory=True)
+                    vc = torch.empty(value_states.shape, dtype=value_states.dtype, pin_memory=True)
+                except RuntimeError as e:
+                    nbytes = 2 * key_states.numel() * key_states.element_size()
+                    raise RuntimeError(f"Layer {layer_idx}: pinned host allocation of {nbytes} bytes for the "
+                                       f"full KV tier failed ({e})") from e
                 side = self._side()
                 side.wait_stream(torch.cuda.current_stream(key_states.device))
                 with torch.cuda.stream(side):
-                    kc = torch.empty(key_states.shape, dtype=key_states.dtype, pin_memory=True)
-                    vc = torch.empty(value_states.shape, dtype=value_states.dtype, pin_memory=True)
                     kc.copy_(key_states.detach(), non_blocking=True)
                     vc.copy_(value_states.detach(), non_blocking=True)
                 key_states.record_stream(side)

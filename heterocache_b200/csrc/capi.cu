@@ -4,7 +4,23 @@
 
 #include <cstdio>
 
+#include <atomic>
+
 #include "hc_params.cuh"
+
+namespace hc {
+
+static std::atomic<unsigned long long> g_wait_limit_ns{0};
+static std::atomic<int> g_stall{0};
+
+uint64_t wait_limit_ns(uint64_t dflt) {
+  const unsigned long long v = g_wait_limit_ns.load(std::memory_order_relaxed);
+  return v ? (uint64_t)v : dflt;
+}
+
+unsigned int injected_stall() { return g_stall.load(std::memory_order_relaxed) ? 1u : 0u; }
+
+}  // namespace hc
 
 namespace {
 
@@ -48,6 +64,12 @@ const char* hc_status_string(int status) {
 }
 
 const char* hc_last_cuda_error(void) { return g_last_err; }
+
+int hc_set_wait_limits(unsigned long long limit_ns, int inject_stall) {
+  hc::g_wait_limit_ns.store(limit_ns, std::memory_order_relaxed);
+  hc::g_stall.store(inject_stall ? 1 : 0, std::memory_order_relaxed);
+  return HC_OK;
+}
 
 int hc_prefill_keep(int dtype, int bsz, int num_kv_heads, int seq_len, int head_dim, const int32_t* keep_heads,
                     int n_keep, const void* k, const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb,

@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kTThreads, 2)
       const uint64_t pol = l2_evict_first_policy();
       for (int i = 0; i < ntiles; ++i) {
         const int s = i % kTStages;
-        if (!mbar_wait(&empty_bar[s], ((i / kTStages) & 1) ^ 1)) {
+        if (!mbar_wait(&empty_bar[s], ((i / kTStages) & 1) ^ 1, p.wait_ns)) {
           set_err(p.err, HC_ERR_TIMEOUT);
           dead = true;
           break;
@@ -539,7 +539,7 @@ __global__ void __launch_bounds__(kTThreads, 2)
       }
       if (dead) {  // let the copies this CTA issued land before it exits
         for (int i = max(0, issued - kTStages); i < issued; ++i)
-          (void)mbar_wait(&full_bar[i % kTStages], (i / kTStages) & 1);
+          (void)mbar_wait(&full_bar[i % kTStages], (i / kTStages) & 1, p.wait_ns);
       }
     }
     return;
@@ -610,7 +610,7 @@ __global__ void __launch_bounds__(kTThreads, 2)
       reset_state();
       cur = r;
     }
-    if (!dead && !mbar_wait(&full_bar[s], (i / kTStages) & 1)) {
+    if (!dead && !mbar_wait(&full_bar[s], (i / kTStages) & 1, p.wait_ns)) {
       if (lane == 0) set_err(p.err, HC_ERR_TIMEOUT);
       dead = true;
     }
@@ -977,6 +977,7 @@ int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_
 }
 
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  p.wait_ns = wait_limit_ns(kMbarTimeoutNs);
   if (p.R <= 0 || p.R > kMaxRowsFD) return HC_ERR_UNSUPPORTED;
   if (p.G <= 0 || p.G > kGMax) return HC_ERR_UNSUPPORTED;
   switch (dtype) {

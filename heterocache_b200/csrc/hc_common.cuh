@@ -184,11 +184,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // ---------------------------------------------------------------------------
 // Grid barrier for cooperative launches (all CTAs co-resident).  Monotonic
-// arrival counter: barrier number e completes when count >= e * nblocks.
-// Every wait is bounded (kBarrierTimeoutNs); on timeout the CTA sets `abort`
-// and HC_ERR_TIMEOUT and every CTA leaves the kernel at its next barrier.
-// The state resets itself: after the final barrier each CTA increments
-// `depart`, and the last to depart zeroes the counters.
+// arrival counter: barrier number e completes when count >= e * nblocks
+// (+ `extra`, an injected arrival that never comes: 0 in normal use).
+// Every wait is bounded (limit_ns, by default kBarrierTimeoutNs); on timeout
+// the CTA sets `abort` and HC_ERR_TIMEOUT and every CTA leaves the kernel at
+// its next barrier.  The state resets itself: after the final barrier each
+// CTA increments `depart`, and the last to depart zeroes the counters (an
+// aborted launch leaves the state for the caller to zero).
 struct GridBarrier {
   unsigned int count;
   unsigned int depart;
@@ -206,12 +208,13 @@ __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
 
 // Returns false if the grid aborted (caller must return).
 __device__ __forceinline__ bool grid_sync(GridBarrier* gb, unsigned int nblocks, unsigned int& epoch,
-                                          int32_t* err) {
+                                          int32_t* err, uint64_t limit_ns = kBarrierTimeoutNs,
+                                          unsigned int extra = 0u) {
   __shared__ int s_ok;
   __syncthreads();
   if (threadIdx.x == 0) {
     epoch += 1;
-    const unsigned int target = epoch * nblocks;
+    const unsigned int target = epoch * nblocks + extra;
     // release-add: the CTA's writes (ordered before by the block barrier)
     // become visible to every CTA that acquires the count
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(&gb->count), "r"(1u) : "memory");
@@ -224,7 +227,7 @@ __device__ __forceinline__ bool grid_sync(GridBarrier* gb, unsigned int nblocks,
         if (ld_acquire_u32(&gb->abort)) { ok = 0; break; }
         uint64_t now = globaltimer_ns();
         if (t0 == 0) t0 = now;
-        else if (now - t0 > kBarrierTimeoutNs) {
+        else if (now - t0 > limit_ns) {
           atomicExch(&gb->abort, 1u);
           set_err(err, HC_ERR_TIMEOUT);
           ok = 0;
@@ -254,8 +257,9 @@ __device__ __forceinline__ void grid_depart(GridBarrier* gb, unsigned int nblock
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk-copy (TMA engine, non-tensor) helpers.  Every wait is
-// bounded by kMbarTimeoutNs; callers turn a timeout into HC_ERR_TIMEOUT.
+// mbarrier + bulk-copy (TMA engine) helpers.  Every wait is bounded
+// (limit_ns, by default kMbarTimeoutNs); callers turn a timeout into
+// HC_ERR_TIMEOUT.
 constexpr uint64_t kMbarTimeoutNs = 1000000000ull;  // 1 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -284,11 +288,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Wait for the phase with the given parity to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kMbarTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer_ns() - t0 > kMbarTimeoutNs) return false;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
   }
   return true;
 }

@@ -73,7 +73,14 @@ struct ScoreParams {
   void* glogits;
   int logits_in_smem;
   int32_t* err;
+  uint64_t wait_ns;    // grid-barrier wait limit (set at dispatch)
+  unsigned int stall;  // injected grid-barrier arrival that never comes (tests of the timeout path)
 };
+
+// Process-wide limits of the device-side waits (hc_set_wait_limits): the
+// limit to use given a wait's default, and the injected stall (0 or 1).
+uint64_t wait_limit_ns(uint64_t dflt);
+unsigned int injected_stall();
 
 size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S);
 int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -107,6 +114,7 @@ struct FDParams {
   void* q_stage;
   void* out;
   int32_t* err;
+  uint64_t wait_ns;  // mbarrier wait limit (set at dispatch)
 };
 
 size_t flash_decode_ws_bytes(int R, int G);

@@ -363,20 +363,20 @@ __device__ void logits_fma(const ScoreParams& p, const JobInfo& ji, T* lg, float
 
 // Softmax probability of logit x with row max M, row sum of exp S and its
 // rounded reciprocal R, in fp32 (the reference's softmax(dtype=float32)).
-// fp32 models use the accurate exp and an IEEE division; 16-bit models round
-// the result to their dtype right after, so the fast exp (a few ulp of fp32)
-// and the reciprocal are used there.
+// The accurate exp in both cases (the fast one's error grows with |x - M|
+// and flips more 16-bit roundings); fp32 models divide by the sum, 16-bit
+// models multiply by its reciprocal (as the CPU softmax the reference runs
+// does) and round to their dtype right after.
 template <typename T>
 __device__ __forceinline__ float softmax_prob(float x, float M, float S, float R) {
   if constexpr (std::is_same<T, float>::value) return __fdiv_rn(expf(x - M), S);
-  else return __expf(x - M) * R;
+  else return expf(x - M) * R;
 }
 
 // exp for the row sums: the same exp the probabilities use
 template <typename T>
 __device__ __forceinline__ float row_exp(float x) {
-  if constexpr (std::is_same<T, float>::value) return expf(x);
-  else return __expf(x);
+  return expf(x);
 }
 
 // Eight consecutive elements (16-byte aligned for 16-bit types, 32-byte for
@@ -764,7 +764,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
       }
     }
   }
-  if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+  if (!grid_sync(p.gb, nblocks, epoch, p.err, p.wait_ns, p.stall)) return;
 
   // ---- phase 2: global softmax statistics, probabilities, pooling, keys
   {
@@ -943,7 +943,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
         }
       }
     }
-    if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+    if (!grid_sync(p.gb, nblocks, epoch, p.err, p.wait_ns, p.stall)) return;
     // stage the job's global histograms of this round (one load round);
     // round 0 was counted per score row
     for (int i = threadIdx.x; i < p.nsel * 256; i += kSThreads) {
@@ -1116,7 +1116,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
         p.out_indices[(size_t)ji.job * p.max_keep + i] = -1;
     }
     // 2. every job's list is complete
-    if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+    if (!grid_sync(p.gb, nblocks, epoch, p.err, p.wait_ns, p.stall)) return;
     // 3. kept K/V rows to their pages: the rows of all jobs (in job, then
     //    rank order) split into equal contiguous shares, one per CTA, so that
     //    CTAs whose tokens hold many kept positions do not set the end.
@@ -1231,7 +1231,7 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
     __syncthreads();
     if (threadIdx.x < p.S && s_ov[threadIdx.x])
       atomicAdd(&p.overlap[ji.job * kMaxRows + threadIdx.x], s_ov[threadIdx.x]);
-    if (!grid_sync(p.gb, nblocks, epoch, p.err)) return;
+    if (!grid_sync(p.gb, nblocks, epoch, p.err, p.wait_ns, p.stall)) return;
     if (threadIdx.x < p.S) s_ov[threadIdx.x] = __ldcg(&p.overlap[ji.job * kMaxRows + threadIdx.x]);
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1349,6 +1349,8 @@ static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size
   p.glogits = pl.logits_in_smem ? nullptr : (void*)(base + w.off_logits);
   p.keep_pos = reinterpret_cast<int32_t*>(base + w.off_keep);
   p.logits_in_smem = pl.logits_in_smem ? 1 : 0;
+  p.wait_ns = wait_limit_ns(kBarrierTimeoutNs);
+  p.stall = injected_stall();
   p.cpj = pl.cpj;
   p.T = pl.T;
   p.TB = pl.TB;

@@ -63,6 +63,20 @@ const char* hc_status_string(int status);
 /* Last CUDA error string seen by this library on the calling thread. */
 const char* hc_last_cuda_error(void);
 
+/* Limits of the device-side waits.  Every wait of this library's kernels --
+ * the scoring kernels' grid barriers, flash-decode's mbarrier waits on its
+ * TMA ring -- gives up after `limit_ns` nanoseconds, ORs HC_ERR_TIMEOUT into
+ * the launch's err_flag and leaves the kernel (no wait is unbounded).
+ * limit_ns = 0 restores the defaults (2 s for a grid barrier, 1 s for an
+ * mbarrier).  inject_stall != 0 makes every grid barrier of the scoring
+ * kernels wait for one arrival that never comes, so the limit runs out:
+ * fault injection for tests of the timeout path (a workspace of a launch
+ * that timed out must be zero-filled again before its next use).  Process-
+ * wide, for launches made after the call (a captured graph keeps the values
+ * of its capture).  No counterpart in the reference, whose waits are those
+ * of PyTorch and flash-attn.  Returns HC_OK. */
+int hc_set_wait_limits(unsigned long long limit_ns, int inject_stall);
+
 /* ---------------------------------------------------------------------------
  * Prefill: keep-head copy.  Replaces the prefill branch of HeteroCache.update
  * (heterocache/cache_utils.py:900-937): the volatile and pivot heads are

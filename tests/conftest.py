@@ -20,3 +20,21 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda", 0)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    """With HC_PARITY_REPORT set, write the selection comparisons of the
+    session (flips, boundary ties, set differences per test) as JSON there."""
+    path = os.environ.get("HC_PARITY_REPORT")
+    if not path:
+        return
+    try:
+        import parity
+    except Exception:
+        return
+    if not parity.RECORDS:
+        return
+    import json
+    os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
+    with open(path, "w") as f:
+        json.dump({"summary": parity.summary(), "records": parity.RECORDS}, f, indent=1)

@@ -1,25 +1,27 @@
 """End-to-end parity of the drop-in cache: GPU ``HeteroCache`` in lockstep with
 the CPU oracle on the golden scenarios.
 
-Per step: lengths and page tables bit-exact; prefill selections, pivot sets,
-drift triggers and retrieval lists under the selection rule of
-``tests/parity.py``; decode attention within 2e-2 (bf16) / 1e-5 (fp32) of the
-oracle's attention over the same pages.
+Per step: lengths and page tables bit-exact; prefill selections, pivot sets
+and retrieval lists under the selection rule of ``tests/parity.py``; decode
+attention within 2e-2 (bf16) / 1e-5 (fp32) of the oracle's attention over the
+same pages.  Drift coefficients (overlap / K) may differ from the oracle's
+only by the positions the parity rule leaves open: the exempt positions of
+the step's top-K plus the positions where the two reference sets already
+differ, divided by K; the triggers must agree unless the oracle's median lies
+within that bound of the threshold.
 """
-import numpy as np
 import pytest
 import torch
 
 from heterocache_b200.cache import HeteroCache, HeteroCacheConfig
 from heterocache_b200.synthetic import DriftingDecode
 from oracle.hc_oracle import OracleCache, paged_attention
-from parity import compare_selection, scores_close
+from parity import compare_selection, exempt_count, scores_close
 from scenarios import SCENARIOS, make_config, scenario_inputs
 
 pytestmark = pytest.mark.gpu
 
 ATOL = {"float32": 1e-5, "bfloat16": 2e-2, "float16": 2e-2}
-MEDIAN_MARGIN = 0.01  # triggers must agree unless the oracle's median is this close to the threshold
 
 
 def _gpu_cache(sc, real_offload=False):
@@ -86,8 +88,12 @@ def _device_query(q, L, dev):
     return qd
 
 
+CHECKS = []  # drift decisions of the last lockstep run (device vs oracle)
+
+
 def run_lockstep(sc, geo, tdt, layer_inputs, real_offload=False):
     gpu, orc = _gpu_cache(sc, real_offload)
+    CHECKS.clear()
     dtype = sc["dtype"]
     dev = torch.device("cuda", 0)
     for layer, (q, k, v) in enumerate(layer_inputs):
@@ -130,6 +136,10 @@ def run_lockstep(sc, geo, tdt, layer_inputs, real_offload=False):
             diff = (out.float().cpu() - ref).abs().max().item()
             assert diff <= ATOL[dtype], (step, layer, diff)
             before = len(gpu.check_log)
+            dev_sets = gpu.prefill_topk_set[layer]
+            dev_sets = dev_sets.cpu() if isinstance(dev_sets, torch.Tensor) else None
+            orc_sets = orc.prefill_topk_set[layer]
+            orc_sets = orc_sets.clone() if isinstance(orc_sets, torch.Tensor) else None
             gpu.decode_select(q.to(dev), layer)
             n_before = len(orc.checks)
             orc.decode_select(q, layer)
@@ -141,23 +151,32 @@ def run_lockstep(sc, geo, tdt, layer_inputs, real_offload=False):
             if len(gpu.check_log) > before:
                 log = gpu.check_log[-1]
                 assert len(new) == len(log["pivots"])
+                K = gpu.base_compress_len
                 for j, rec in enumerate(new):
                     n_checks += 1
                     trig = bool(log["trigger"][j].item())
-                    if trig != rec["trigger"]:
-                        assert abs(rec["median"] - sc["thr"]) <= MEDIAN_MARGIN, (step, rec["median"])
-                        continue
-                    coeff = log["coeffs"][j].cpu().tolist()
-                    assert np.allclose(coeff, rec["coeffs"], atol=0.02), (coeff, rec["coeffs"])
+                    slot = log["slots"][j]
+                    # positions where the two reference sets already differ
+                    set_diff = len(set(dev_sets[0, slot].tolist()) ^ set(orc_sets[0, slot].tolist()))
                     dsc = log["scores"][j].float().cpu()
                     S = dsc.shape[0]
+                    coeff = log["coeffs"][j].cpu().tolist()
+                    bound = []
+                    for s_ in range(S):
+                        ex = exempt_count(rec["scores"][0, s_].float().numpy(), dsc[s_].numpy(), K, dtype)
+                        bound.append((ex + set_diff) / K + 1e-7)
+                        assert abs(coeff[s_] - rec["coeffs"][s_]) <= bound[-1], (step, s_, coeff, rec["coeffs"])
+                    CHECKS.append({"trigger_dev": trig, "trigger_ref": bool(rec["trigger"]),
+                                   "median_ref": float(rec["median"]), "bound": max(bound)})
+                    if trig != rec["trigger"]:
+                        assert abs(rec["median"] - sc["thr"]) <= max(bound), (step, rec["median"], max(bound))
+                        continue
                     if trig:
                         ml = log["max_len"][j]
                         sel = log["retrieved"][j, :ml].cpu().tolist()
                         res = compare_selection(rec["scores"][0, -1].float().numpy(), dsc[S - 1].numpy(), sel, ml,
                                                 dtype)
                         assert res["ok"], (step, res)
-                        slot = log["slots"][j]
                         res = compare_selection(rec["scores"][0, -1].float().numpy(), dsc[S - 1].numpy(),
                                                 log["ref_after"][0, slot].cpu().tolist(), gpu.base_compress_len,
                                                 dtype)
@@ -189,6 +208,23 @@ def test_config3_qwen_224k_host_tier(cuda_device):
               n_decode=10, gen=16, role_seed=21, seed=31, layers=1)
     inputs = [prefill_inputs(QWEN_7B, sc["L"], seed=sc["seed"] * 100, dtype=torch.bfloat16, q_positions=32)]
     run_lockstep(sc, QWEN_7B, torch.bfloat16, inputs, real_offload=True)
+
+
+def test_config1_llama_32k_256_drifting_steps(cuda_device):
+    """Config 1 exactly: one Llama-3.1-8B attention layer (32 query / 8 KV
+    heads), 32768 tokens, bf16, compression ratio 0.5, the full KV in HBM,
+    then 256 decode steps with drifting queries (q_t = 0.9 q_{t-1} + 0.1
+    noise), a drift check every 5 steps (threshold 0.5, overlap K =
+    base_compress_len), in lockstep with the oracle at every step."""
+    from heterocache_b200.synthetic import LLAMA_8B, prefill_inputs
+    sc = dict(geo=(32, 8, 128), L=32768, dtype="bfloat16", pooling="avgpool", k=5, thr=0.5, steps=5,
+              n_decode=256, gen=264, role_seed=41, seed=43, layers=1)
+    inputs = [prefill_inputs(LLAMA_8B, sc["L"], seed=sc["seed"] * 100, dtype=torch.bfloat16, q_positions=32)]
+    run_lockstep(sc, LLAMA_8B, torch.bfloat16, inputs)
+    assert len(CHECKS) >= 256 // 5
+    agree = sum(c["trigger_dev"] == c["trigger_ref"] for c in CHECKS)
+    print(f"config 1: {len(CHECKS)} drift checks, {sum(c['trigger_ref'] for c in CHECKS)} oracle triggers, "
+          f"{agree} decisions agree, largest coefficient bound {max(c['bound'] for c in CHECKS):.2e}")
 
 
 @pytest.mark.parametrize("order", ["llama", "qwen"])

@@ -95,12 +95,12 @@ def declared_parameters():
 
 def _ctype_for(param: str):
     """The ctypes type a C parameter declaration maps to."""
-    from ctypes import c_double, c_float, c_int, c_int64, c_size_t, c_void_p
+    from ctypes import c_double, c_float, c_int, c_int64, c_size_t, c_ulonglong, c_void_p
     decl = param.rsplit(" ", 1)[0] if " " in param else param
     if "*" in param:
         return c_void_p
     return {"int": c_int, "int64_t": c_int64, "long long": c_int64, "size_t": c_size_t, "float": c_float,
-            "double": c_double}[decl.strip()]
+            "double": c_double, "unsigned long long": c_ulonglong}[decl.strip()]
 
 
 def test_ctypes_argument_lists_match_the_header_declarations():
