@@ -142,7 +142,16 @@ class OracleCache:
     coefficients, medians, triggers and retrieval index lists.
     """
 
-    def __init__(self, cfg):
+    def __init__(self, cfg, ties: str = "topk"):
+        """``ties``: how a top-k orders positions whose scores are equal, which
+        the reference leaves to ``torch.topk`` (unspecified order).  "topk"
+        calls it exactly as the reference does (the mode the golden fixtures
+        pin); "lowest" breaks such ties toward the lowest positions, one of
+        the reference's valid outcomes and the rule the device kernels
+        document, so that a lockstep run can require identical selections."""
+        if ties not in ("topk", "lowest"):
+            raise ValueError("ties must be 'topk' or 'lowest'")
+        self.ties = ties
         self.cfg = cfg
         self.data = cfg.data
         self.num_attn_heads = cfg.num_attn_heads
@@ -180,6 +189,14 @@ class OracleCache:
         self.prefill_keep_lens: Dict[int, torch.Tensor] = {}
         self.pivot_scores: Dict[int, torch.Tensor] = {}
         self.checks: List[Dict] = []
+
+    def _topk(self, scores: torch.Tensor, k: int) -> torch.Tensor:
+        """Indices of the k largest scores along the last dim, by descending
+        score (``torch.topk(k, sorted=True)``; with ties="lowest", equal
+        scores in ascending position order)."""
+        if self.ties == "topk":
+            return scores.topk(k, dim=-1, sorted=True).indices
+        return torch.sort(scores, dim=-1, descending=True, stable=True).indices[..., :k]
 
     # -- storage ---------------------------------------------------------
     def _init_layer_storage(self, layer: int, dtype: torch.dtype) -> None:
@@ -292,7 +309,7 @@ class OracleCache:
         k = key_states[:, pivots, :, :]
         scores = window_scores(q, k, groups=G, pooling=self.pooling, kernel_size=self.kernel_size)
         self.pivot_scores[layer] = scores
-        self.prefill_topk_set.append(scores.topk(self.base_compress_len, dim=-1, sorted=True).indices)
+        self.prefill_topk_set.append(self._topk(scores, self.base_compress_len))
 
     def prefill_select(self, query_states, key_states, value_states, layer):
         """Compressed heads' selection and page write (heterocache/cache_utils.py:782-882)."""
@@ -315,7 +332,7 @@ class OracleCache:
         scores = window_scores(q, k, groups=G, pooling=self.pooling, kernel_size=self.kernel_size)
         self.prefill_scores[layer] = scores
         safe_k = min(max_k, scores.shape[-1])
-        _, idx = scores.topk(safe_k, dim=-1, sorted=True)
+        idx = self._topk(scores, safe_k)
         grid = torch.arange(safe_k).view(1, 1, -1)
         excess = (grid >= keep_lens.view(1, -1, 1)).expand(bsz, -1, -1)
         idx = idx.masked_fill(excess, L + 1000).sort(dim=-1).values.clamp(max=L - 1)
@@ -358,7 +375,7 @@ class OracleCache:
             shp = p.shape
             p = _pool(p.reshape(-1, shp[-1]).unsqueeze(1), self.pooling, self.kernel_size).squeeze(1).view(shp)
             scores = p.max(dim=1).values  # [bsz,S,L]
-            cur = scores.topk(K, dim=-1).indices
+            cur = self._topk(scores, K)
             ref = self.prefill_topk_set[layer][:, idx, :].unsqueeze(1).sort(dim=-1).values
             ref = ref.expand(-1, S, -1).contiguous()
             pos = torch.searchsorted(ref, cur).clamp(max=K - 1)
@@ -374,7 +391,7 @@ class OracleCache:
                 lengths = [min(int(K * self.data["allocation_matrix"][layer][m]), self.prefill_len)
                            for m in members]
                 max_len = max(lengths)
-                sel = scores[:, -1, :].topk(max_len, dim=-1).indices.sort(dim=-1).values.squeeze()
+                sel = self._topk(scores[:, -1, :], max_len).sort(dim=-1).values.squeeze()
                 rec["retrieved"] = sel.clone()
                 rec["lengths"] = list(lengths)
                 for m, n_tok in zip(members, lengths):
