@@ -98,7 +98,9 @@ def exempt_mask(ref: np.ndarray, dev: Optional[np.ndarray], k: int, dtype: str, 
 
 
 def compare_selection(ref: np.ndarray, dev: Optional[np.ndarray], sel: Iterable[int], k: int, dtype: str,
-                      rtol: float = SEL_RTOL) -> Dict:
+                      rtol: float = SEL_RTOL, scores_only: bool = False) -> Dict:
+    """The tie-aware rule above.  scores_only: the caller compares the scores
+    alone (no selection to check); the record says so."""
     ref = np.asarray(ref, dtype=np.float64)
     sel = np.asarray(sorted(set(int(i) for i in sel)), dtype=np.int64)
     L = ref.size
@@ -124,9 +126,12 @@ def compare_selection(ref: np.ndarray, dev: Optional[np.ndarray], sel: Iterable[
         ref_set[np.argsort(-ref, kind="stable")[:k]] = True
     out["set_diff"] = int(np.count_nonzero(ref_set != mask))
     out["ok"] = out["missing"] == 0 and out["extra"] == 0 and sel.size == min(k, L)
-    RECORDS.append({"test": os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0], "dtype": dtype,
-                    **{key: out[key] for key in ("L", "k", "flips", "flips_near_boundary", "boundary", "set_diff",
-                                                  "max_rel", "ok")}})
+    rec = {"test": os.environ.get("PYTEST_CURRENT_TEST", "").split(" ")[0], "dtype": dtype,
+           **{key: out[key] for key in ("L", "k", "flips", "flips_near_boundary", "boundary", "set_diff",
+                                         "max_rel", "ok")}}
+    if scores_only:
+        rec.update(scores_only=True, ok=None, set_diff=None)
+    RECORDS.append(rec)
     return out
 
 
@@ -174,7 +179,7 @@ def summary() -> Dict:
         s["comparisons"] += 1
         s["positions"] += r["L"]
         for key in ("flips", "flips_near_boundary", "boundary", "set_diff"):
-            s[key] += r[key]
+            s[key] += r[key] or 0
         s["max_flip_frac"] = max(s["max_flip_frac"], r["flips"] / max(r["L"], 1))
     for s in out.values():
         s["flip_frac"] = s["flips"] / max(s["positions"], 1)
