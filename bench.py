@@ -176,7 +176,21 @@ def time_prefill_kernels(cache, q, k, v, layer, reps=5):
                                workspace=cache._ws_score, err=cache._err)
         # keys read once per head; kept K/V rows gathered and written
         calls["prefill_select"] = (select, nc * L * D * 2 + int(keep.sum().item()) * D * 2 * 2 * 2)
-    for name, (fn, nbytes) in calls.items():
+
+        def select_w32():
+            ops.prefill_select(q, k, v, keep, max_k, n_heads=nc, groups=cache.num_key_value_groups,
+                               window=32, pooling="maxpool", kernel_size=7,
+                               k_pool=cache.key_pools[layer], v_pool=cache.value_pools[layer],
+                               block_table=cache.block_tables[layer], heads_len=cache.heads_len[layer],
+                               workspace=cache._ws_score, err=cache._err)
+        # the observation-window scoring (SnapKV window 32, max-pool 7) on the
+        # same keys: 128 query rows per KV head on the tensor cores
+        calls["prefill_select_w32"] = (select_w32, nc * L * D * 2 + int(keep.sum().item()) * D * 2 * 2 * 2
+                                       + nc * 32 * cache.num_key_value_groups * D * 2)
+    # the window-32 selection rewrites the compressed heads' pages with its own
+    # kept rows: time it before the HeteroCache selection, which restores them
+    order = [n for n in ("pivot_init", "prefill_select_w32", "prefill_select") if n in calls]
+    for name, (fn, nbytes) in ((n, calls[n]) for n in order):
         fn()
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -193,6 +207,10 @@ def time_prefill_kernels(cache, q, k, v, layer, reps=5):
         us = e0.elapsed_time(e1) * 1e3 / reps
         res[name] = {"avg_launch_us": us, "algorithmic_bytes_per_launch": float(nbytes),
                      "achieved_gbs": nbytes / (us * 1e-6) / 1e9}
+        if name == "prefill_select_w32":
+            flops = 2.0 * nc * L * 32 * cache.num_key_value_groups * D
+            res[name].update(tensor_flops_per_launch=flops, achieved_tflops=flops / (us * 1e-6) / 1e12,
+                             logits_path="tcgen05.mma (TMA-fed key tiles, TMEM accumulators)")
         del g
     cache.check_errors()
     return res

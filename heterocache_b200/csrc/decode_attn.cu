@@ -26,6 +26,7 @@
 
 #include "hc_host.cuh"
 #include "hc_params.cuh"
+#include "umma.cuh"
 
 namespace hc {
 
@@ -349,15 +350,8 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
 }
-// The K/V stream is read with the evict-first L2 policy (l2_evict_first_policy).
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
-                                            uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
-      "{%2, %3}], [%4], %5;\n" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
+// The K/V stream is read with the evict-first L2 policy (l2_evict_first_policy),
+// through tma_load_2d (umma.cuh).
 // Address of 16-byte chunk `chunk` (0..15 over the 128 dims) of tile row
 // `row` (0..63), for a stage whose first box starts at `base` (1024-aligned).
 __device__ __forceinline__ uint32_t swz(uint32_t base, int row, int chunk) {
@@ -828,53 +822,6 @@ static int fd_launch_f32(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   return fd_combine<float>(p, grid, st);
 }
 
-// Tensor map of a pool viewed as a 2-D [n_blocks*256 rows, 128] array of
-// 16-bit elements, boxes of 64 rows x 64 elements, 128-byte swizzle.  Encoded
-// once per (device, pool address, rows, dtype) through the driver entry point
-// and cached.
-static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-
-static int pool_tensor_map(CUtensorMap* out, const void* base, long long rows, int dtype) {
-  struct Entry { int dev; const void* base; long long rows; int dtype; CUtensorMap map; };
-  static Entry cache[256];
-  static int n = 0, next = 0;
-  const int dev = current_device();
-  if (dev < 0) return HC_ERR_CUDA;
-  std::lock_guard<std::mutex> g(host_lock());
-  for (int i = 0; i < n; ++i)
-    if (cache[i].dev == dev && cache[i].base == base && cache[i].rows == rows && cache[i].dtype == dtype) {
-      *out = cache[i].map;
-      return HC_OK;
-    }
-  if (!g_encode) {
-    cudaDriverEntryPointQueryResult q;
-    void* fn = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess || !fn)
-      return HC_ERR_CUDA;
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  }
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)kD, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)kD * 2};
-  const cuuint32_t box[2] = {64, (cuuint32_t)kTTile};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType ty =
-      dtype == HC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  if (g_encode(&map, ty, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return HC_ERR_CUDA;
-  Entry& e = cache[n < 256 ? n++ : (next++ % 256)];
-  e.dev = dev;
-  e.base = base;
-  e.rows = rows;
-  e.dtype = dtype;
-  e.map = map;
-  *out = map;
-  return HC_OK;
-}
-
 // Co-resident CTAs of the 16-bit TMA decode kernel for `dsm` bytes of dynamic
 // shared memory on the current device, 0 if it cannot run.  The kernel's
 // shared-memory limit is raised and the occupancy queried once per device and
@@ -913,8 +860,8 @@ static int fd_launch_tma(FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st
   const int dtype = std::is_same<T, __nv_bfloat16>::value ? HC_BF16 : HC_F16;
   CUtensorMap tmk, tmv;
   const long long rows = (long long)p.n_blocks * kPage;
-  if (pool_tensor_map(&tmk, p.kp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
-  if (pool_tensor_map(&tmv, p.vp, rows, dtype) != HC_OK) return HC_ERR_CUDA;
+  if (!pool_tensor_map(&tmk, p.kp, rows, dtype, kTTile)) return HC_ERR_CUDA;
+  if (!pool_tensor_map(&tmv, p.vp, rows, dtype, kTTile)) return HC_ERR_CUDA;
   const size_t dsm = fd_tma_smem(p.R, p.G);
   const int grid = fd_tma_grid<T>(dsm);
   if (grid <= 0) return HC_ERR_UNSUPPORTED;

@@ -72,6 +72,10 @@ struct ScoreParams {
   unsigned int* overlap;
   void* glogits;
   int logits_in_smem;
+  // tensor-core logits (16-bit dtypes): tcgen05.mma from TMA-fed key tiles;
+  // n_stages shared-memory stages of 128 keys, NP query rows padded to 16,
+  // tmem_cols tensor-memory columns (two accumulators of NP columns)
+  int umma, n_stages, NP, tmem_cols;
   int32_t* err;
   uint64_t wait_ns;    // grid-barrier wait limit (set at dispatch)
   unsigned int stall;  // injected grid-barrier arrival that never comes (tests of the timeout path)

@@ -29,8 +29,11 @@
 // Rounding points follow the reference exactly: q.K^T rounded to the model
 // dtype, then divided by sqrt(d) and rounded, fp32 softmax rounded to the
 // dtype, the window sum rounded, the pooling output rounded.
+#include <cstring>
+
 #include "hc_host.cuh"
 #include "hc_params.cuh"
+#include "umma.cuh"
 
 namespace hc {
 
@@ -111,6 +114,10 @@ __device__ __forceinline__ bool masked(const ScoreParams& p, int qi, int t) {
   return false;
 }
 
+// IEEE division for the rare operands the known-divisor path cannot take,
+// out of line so that the hot loops that may need it stay small.
+__device__ __noinline__ float div_ieee(float x, float y) { return __fdiv_rn(x, y); }
+
 // 0 < |x| < 2^-120: operands whose quotient by sqrt(d) may be subnormal.
 __device__ __forceinline__ bool tiny_nonzero(float x) {
   return (__float_as_uint(x) & 0x7fffffffu) - 1u < 0x037fffffu;
@@ -128,7 +135,7 @@ __device__ __forceinline__ float scale_logit(float acc, float y, float r) {
     return __fdiv_rn(x, y);
   } else {
     float q = copysignf(div_known(x, y, r), x);
-    if (__builtin_expect(tiny_nonzero(x), 0)) q = __fdiv_rn(x, y);
+    if (__builtin_expect(tiny_nonzero(x), 0)) q = div_ieee(x, y);
     return Elem<T>::rnd(q);
   }
 }
@@ -143,8 +150,8 @@ __device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float 
     Elem<T>::rnd2(a, b);
     float qa = copysignf(div_known(a, y, r), a), qb = copysignf(div_known(b, y, r), b);
     if (__builtin_expect(tiny_nonzero(a) || tiny_nonzero(b), 0)) {
-      if (tiny_nonzero(a)) qa = __fdiv_rn(a, y);
-      if (tiny_nonzero(b)) qb = __fdiv_rn(b, y);
+      if (tiny_nonzero(a)) qa = div_ieee(a, y);
+      if (tiny_nonzero(b)) qb = div_ieee(b, y);
     }
     Elem<T>::rnd2(qa, qb);
     a = qa;
@@ -309,6 +316,321 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
       if (gid == 0 && qi < p.Rq) wmax[warp * kMaxRq + qi] = m;
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Phase 1, tcgen05 path (16-bit dtypes, any row count up to 256): the keys
+// stream through shared memory in tiles of 128 tokens loaded by TMA, the
+// tensor core computes D[token, query row] = K_tile . Q^T (M = 128 tokens,
+// N = NP query rows, K = 128 dims in eight 16-deep steps) into one of two
+// tensor-memory accumulators, and the epilogue warps read D back (thread =
+// token, registers = query rows), round and scale the logits exactly as the
+// other paths do and store them to the logits buffer.  The CTA's token range
+// [t0, t1) is a multiple of 128 tokens from a 128-aligned t0 (a tile never
+// crosses a 256-token page); the pooling margins either side are 16-row
+// tiles (rows 16..127 of such a tile are left over from earlier tiles: their
+// results are discarded).
+//
+// Roles: warp 0 lane 0 issues the TMA loads (stages released by the MMA's
+// completion), warp 1 allocates the tensor memory and its lane 0 issues the
+// MMAs, warps 2-15 read the accumulators: a warp may only read the TMEM lanes
+// 32 * (warp % 4) .. + 31, so the work items of a tile are (lane quarter,
+// 8-column chunk) pairs, each quarter's chunks dealt round-robin over its
+// three or four warps (more warps in flight hide the epilogue's dependent
+// arithmetic; it would otherwise set the pace).  Every wait is bounded; a wait that gives up marks
+// the launch failed (HC_ERR_TIMEOUT) and its role stops, the others run out
+// their own bounded waits, in-flight copies and MMAs are waited for (bounded)
+// and the tensor memory is released before the phase ends.
+constexpr int kUStage = 2 * 128 * 128;  // bytes of one stage: two 128-row x 128-byte boxes
+constexpr int kMaxStages = 6;
+constexpr int kUBox = 128 * 128;
+
+constexpr int kUColMax = 48;  // query rows whose maxima the epilogue keeps in registers
+
+struct UmmaSmem {
+  uint64_t full[kMaxStages], empty[kMaxStages], accf[2], acce[2];
+  uint32_t tmem;
+  int issued, consumed, fail;
+  float colmax[kSWarps][kUColMax];  // per-warp row maxima (reg_max)
+  int pages[kMaxPages];             // drift checks: page ids of the CTA's keys
+};
+
+// Eight logits of one token: x holds q.k dot products (fp32) and receives
+// rnd(rnd(x) / sqrt(d)) as scale_logit does, branch-free except for one
+// vote-free fix-up branch taken when any operand is 0 or tiny (the fast
+// division does not keep the sign of a zero; a subnormal quotient needs IEEE
+// division).
+template <typename T>
+__device__ __forceinline__ void scale_logit8(float (&x)[8], float y, float r) {
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) Elem<T>::rnd2(x[j], x[j + 1]);
+  float q[8];
+  bool fix = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    q[j] = div_known(x[j], y, r);
+    fix |= (__float_as_uint(x[j]) & 0x7fffffffu) < 0x03800000u;  // |x| < 2^-120, zeros included
+  }
+  if (__builtin_expect(fix, 0)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t a = __float_as_uint(x[j]) & 0x7fffffffu;
+      if (a == 0u) q[j] = x[j];
+      else if (a < 0x03800000u) q[j] = div_ieee(x[j], y);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    Elem<T>::rnd2(q[j], q[j + 1]);
+    x[j] = q[j];
+    x[j + 1] = q[j + 1];
+  }
+}
+
+template <typename T, int MODE>
+__device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsigned char* stages,
+                            unsigned char* qop, UmmaSmem& u, const CUtensorMap* tm_rows,
+                            const CUtensorMap* tm_edge) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int NS = p.n_stages, NP = p.NP, Rq = p.Rq;
+  const int nchunk = (Rq + 7) >> 3;  // 8-column chunks holding query rows (the rest of NP is padding)
+  // epilogue warps of a lane quarter q: {q, q+4, q+8, q+12} less warps 0 and
+  // 1; how many of them have chunks
+  auto quarter_warps = [](int q) { return q < 2 ? 3 : 4; };
+  auto active = [&](int q) { return min(quarter_warps(q), nchunk); };
+  const int n_epi = active(0) + active(1) + active(2) + active(3);
+  // with at most two chunks per warp the row maxima over the CTA's own tokens
+  // are kept in registers and published per warp in u.colmax[warp][row]
+  const bool reg_max = nchunk <= 6;
+  float (*colmax)[kUColMax] = u.colmax;
+  const int lo = max(0, ji.t0 - kMargin), hi = min(p.L, ji.t1 + kMargin);
+  const bool left = ji.t0 > 0, right = ji.t1 < p.L;
+  const int nmain = (ji.t1 - ji.t0 + 127) >> 7;
+  const int ntiles = (left ? 1 : 0) + nmain + (right ? 1 : 0);
+  auto tile_of = [&](int i, int& start, int& rows) {
+    if (left) {
+      if (i == 0) { start = ji.t0 - kMargin; rows = kMargin; return; }
+      --i;
+    }
+    if (i < nmain) { start = ji.t0 + 128 * i; rows = 128; return; }
+    start = ji.t1;
+    rows = kMargin;
+  };
+  // ---- set-up: barriers first, so that the key stream starts at once
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&u.full[s], 1);
+      mbar_init(&u.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&u.accf[b], 1);
+      mbar_init(&u.acce[b], n_epi);
+    }
+    u.issued = u.consumed = u.fail = 0;
+    fence_mbar_init();
+  }
+  if (reg_max)
+    for (int i = threadIdx.x; i < kSWarps * Rq; i += kSThreads) colmax[i / Rq][i % Rq] = -INFINITY;
+  __syncthreads();
+
+  uint32_t tmem = 0;
+  if (warp == 0) {
+    // ---- TMA producer.  Drift checks: the page ids of the CTA's keys first,
+    // loaded by the whole warp at once (kMaxPages of them; beyond that each
+    // tile reads its own)
+    int npg = 0, pg0 = 0;
+    if constexpr (MODE == MODE_DRIFT) {
+      pg0 = lo >> 8;
+      npg = ((hi - 1) >> 8) - pg0 + 1;
+      if (npg <= kMaxPages) {
+        const int row = ji.b * p.KV + ji.h;
+        for (int j = lane; j < npg; j += 32) {
+          int blk = p.bt[(int64_t)row * p.max_blocks + pg0 + j];
+          if (blk < 0 || blk >= p.n_blocks) {
+            set_err(p.err, HC_ERR_RANGE);
+            blk = 0;  // keep the copy inside the pool (the launch reports the error)
+          }
+          u.pages[j] = blk;
+        }
+      } else {
+        npg = 0;
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      int i = 0;
+      for (; i < ntiles; ++i) {
+        const int s = i % NS;
+        if (!mbar_wait_sleep(&u.empty[s], ((i / NS) & 1) ^ 1, p.wait_ns)) {
+          atomicExch(&u.fail, 1);
+          break;
+        }
+        int start, rows;
+        tile_of(i, start, rows);
+        const CUtensorMap* m = rows == 128 ? tm_rows : tm_edge;
+        unsigned char* dst = stages + (size_t)s * kUStage;
+        mbar_arrive_expect_tx(&u.full[s], (uint32_t)rows * 256u);
+        if constexpr (MODE == MODE_DRIFT) {
+          int blk;
+          if (npg) {
+            blk = u.pages[min((start >> 8) - pg0, npg - 1)];
+          } else {
+            blk = p.bt[(int64_t)(ji.b * p.KV + ji.h) * p.max_blocks + (start >> 8)];
+            if (blk < 0 || blk >= p.n_blocks) {  // reported; read page 0 instead
+              set_err(p.err, HC_ERR_RANGE);
+              blk = 0;
+            }
+          }
+          const int y = blk * kPage + (start & (kPage - 1));
+          tma_load_2d(dst, m, 0, y, &u.full[s], pol);
+          tma_load_2d(dst + kUBox, m, 64, y, &u.full[s], pol);
+        } else {
+          tma_load_4d(dst, m, 0, start, ji.h, ji.b, &u.full[s], pol);
+          tma_load_4d(dst + kUBox, m, 64, start, ji.h, ji.b, &u.full[s], pol);
+        }
+      }
+      u.issued = i;
+    }
+  } else {
+    // ---- tensor memory and the query operand, while the first tiles load
+    if (warp == 1) {
+      tmem_alloc(&u.tmem, (uint32_t)p.tmem_cols);
+      tmem_relinquish();
+    }
+    // query rows as the B operand: NP rows x 128 dims, K-major, 128-byte
+    // swizzle, rows past Rq zero
+    for (int i = threadIdx.x - 32; i < NP * 16; i += kSThreads - 32) {
+      const int r = i >> 4, c16 = i & 15;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < Rq) v = ldg128(query_row<T>(p, ji, r) + 8 * c16);
+      *reinterpret_cast<uint4*>(qop + (c16 >> 3) * (NP * 128) + swz128(r, c16 & 7)) = v;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    named_bar_sync(1, kSThreads - 32);
+    tc_fence_after();
+    tmem = u.tmem;
+    if (warp == 1) {
+      // ---- MMA issuer
+      if (lane == 0) {
+        const uint32_t idesc = idesc_f16_m128(std::is_same<T, __nv_bfloat16>::value, NP);
+        const uint32_t q0 = smem_u32(qop);
+        int i = 0;
+        for (; i < ntiles; ++i) {
+          const int s = i % NS, b = i & 1;
+          if (!mbar_wait_sleep(&u.full[s], (i / NS) & 1, p.wait_ns)) {
+            atomicExch(&u.fail, 1);
+            break;
+          }
+          u.consumed = i + 1;
+          if (!mbar_wait_sleep(&u.acce[b], ((i >> 1) & 1) ^ 1, p.wait_ns)) {
+            atomicExch(&u.fail, 1);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(stages + (size_t)s * kUStage);
+          const uint32_t d = tmem + (uint32_t)(b * NP);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t ao = a0 + (kk >> 2) * kUBox + (kk & 3) * 32;
+            const uint32_t bo = q0 + (kk >> 2) * (NP * 128) + (kk & 3) * 32;
+            umma_f16(d, smem_desc_sw128(ao), smem_desc_sw128(bo), idesc, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&u.empty[s]);
+          umma_commit(&u.accf[b]);
+        }
+        // every MMA issued has completed before the tensor memory is released
+        if (i > 0) (void)mbar_wait_sleep(&u.accf[(i - 1) & 1], ((i - 1) >> 1) & 1, p.wait_ns);
+      }
+    } else {
+      // ---- epilogue: accumulators -> rounded logits
+      const int q4 = warp & 3;
+      const int k = q4 < 2 ? (warp >> 2) - 1 : (warp >> 2);  // index among the quarter's warps
+      const int m = quarter_warps(q4);
+      if (k < active(q4)) {
+        // launch constants in registers (the loop stores through a pointer the
+        // compiler cannot separate from the parameter block)
+        const int TB = p.TB, W = p.W, L = p.L;
+        const float sqd = p.sqrt_d, r_sqrt = __frcp_rn(sqd);
+        const int base = ji.t0 - kMargin;
+        const int r = 32 * q4 + lane;  // tile row = TMEM lane
+        const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+        float cmax[2][8];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cmax[cc][j] = -INFINITY;
+        for (int i = 0; i < ntiles; ++i) {
+          const int b = i & 1;
+          int start, rows;
+          tile_of(i, start, rows);
+          const bool ok = mbar_wait_sleep(&u.accf[b], (i >> 1) & 1, p.wait_ns);
+          if (!ok) atomicExch(&u.fail, 1);
+          tc_fence_after();
+          const int t = start + r;
+          const bool valid = ok && r < rows && t >= lo && t < hi;
+          const bool own = valid && t >= ji.t0 && t < ji.t1;
+          T* __restrict__ out = lg + (t - base);
+          // in-window causal mask (W > 1): query row qi = sg * W + w sees
+          // tokens t <= L - W + w
+          const int wlim = t - (L - W);
+          int cc = 0;
+          for (int c = k; c < nchunk; c += m, ++cc) {
+            uint32_t v[8];
+            tmem_ld8(tmem + lane_off + (uint32_t)(b * NP + 8 * c), v);
+            tmem_ld_wait();
+            if (valid) {
+              float x[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) x[j] = __uint_as_float(v[j]);
+              scale_logit8<T>(x, sqd, r_sqrt);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int qi = 8 * c + j;
+                if (W > 1 && wlim > qi % W) x[j] = -INFINITY;
+                if (qi < Rq) out[(int64_t)qi * TB] = Elem<T>::pack(x[j]);
+              }
+              if (own && cc < 2) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) cmax[cc & 1][j] = fmaxf(cmax[cc & 1][j], x[j]);
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&u.acce[b]);
+          if (!ok) break;
+        }
+        if (reg_max) {
+          int cc = 0;
+          for (int c = k; c < nchunk && cc < 2; c += m, ++cc) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float mx = cmax[cc][j];
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+              const int qi = 8 * c + j;
+              if (lane == 0 && qi < Rq) colmax[warp][qi] = mx;
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && u.fail) {
+    set_err(p.err, HC_ERR_TIMEOUT);
+    // copies still in flight land before the stages can be reused
+    for (int i = u.consumed; i < u.issued; ++i) (void)mbar_wait_sleep(&u.full[i % NS], (i / NS) & 1, p.wait_ns);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+  }
+  return reg_max;
 }
 
 // Phase 1, CUDA-core path (fp32, or many query rows): 32-token tiles of keys
@@ -611,7 +933,9 @@ __device__ __forceinline__ int find_bin(const unsigned int* h, unsigned int rem,
 // one query per row) are compile-time constants in a local copy of the
 // parameters, so each instantiation carries only its own mode's code.
 template <typename T, int MODE>
-__global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreParams pin) {
+__global__ void __launch_bounds__(kSThreads, 1)
+    score_select_kernel(const ScoreParams pin, const __grid_constant__ CUtensorMap tm_rows,
+                        const __grid_constant__ CUtensorMap tm_edge) {
   ScoreParams p = pin;
   p.mode = MODE;
   if constexpr (MODE != MODE_PREFILL) p.W = 1;
@@ -647,6 +971,19 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   } else {
     lg = reinterpret_cast<T*>(p.glogits) + (size_t)blockIdx.x * p.Rq * p.TB;
   }
+  // tcgen05 path: the query operand, then the ring of key stages, 1024-byte
+  // aligned (the launch reserves the slack); the ring is dead after phase 1,
+  // so the arrays of the later phases (keys, histograms, row partials) share
+  // its memory
+  __shared__ UmmaSmem s_umma;
+  unsigned char* u_stages = nullptr;
+  unsigned char* u_qop = nullptr;
+  if (p.umma) {
+    const uint32_t a = smem_u32(sp);
+    u_qop = sp + ((1024u - (a & 1023u)) & 1023u);
+    u_stages = u_qop + (size_t)p.NP * 256;
+    sp = u_stages;
+  }
   unsigned int* keys = reinterpret_cast<unsigned int*>(sp);
   sp += (size_t)p.S * p.T * sizeof(unsigned int);
   unsigned int* lhist = reinterpret_cast<unsigned int*>(sp);
@@ -654,6 +991,19 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
   float* wmax = reinterpret_cast<float*>(sp);
   sp += (size_t)kSWarps * kMaxRq * sizeof(float);
   float* sq = reinterpret_cast<float*>(sp);  // fma path only
+
+  // ---- phase 1 on the tensor cores comes first, so that its key stream
+  // starts before any other global access of the launch (the page ids are
+  // read per tile by the TMA producer)
+  constexpr bool kTensor = !std::is_same<T, float>::value;
+  bool used_mma = false, used_umma = false, umma_regmax = false;
+  if constexpr (kTensor) {
+    if (p.umma) {
+      // row maxima: per warp in s_umma.colmax, or from a pass over the logits
+      umma_regmax = logits_umma<T, MODE>(p, ji, lg, u_stages, u_qop, s_umma, &tm_rows, &tm_edge);
+      used_mma = used_umma = true;
+    }
+  }
 
   // ---- zero the per-launch accumulators (ordered before use by barrier 1)
   if (ji.part == 0) {
@@ -693,11 +1043,10 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
     __syncthreads();
   };
 
-  // ---- phase 1: logits
-  constexpr bool kTensor = !std::is_same<T, float>::value;
-  bool used_mma = false;
+  // ---- phase 1, legacy paths: logits
   if constexpr (kTensor) {
-    if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
+    if (used_umma) {
+    } else if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
     else if (p.Rq <= 16) { logits_mma<T, 2>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
     else if (p.Rq <= 24) { logits_mma<T, 3>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
     else if (p.Rq <= 32) { logits_mma<T, 4>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
@@ -709,10 +1058,31 @@ __global__ void __launch_bounds__(kSThreads, 1) score_select_kernel(const ScoreP
     logits_fma<T>(p, ji, lg, wmax, sq, sk);
   }
   __syncthreads();
-  for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
-    float m = -INFINITY;
-    for (int w = 0; w < kSWarps; ++w) m = fmaxf(m, wmax[w * kMaxRq + qi]);
-    s_rowM[qi] = m;
+  if (umma_regmax) {
+    for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
+      float m = -INFINITY;
+      for (int w = 0; w < kSWarps; ++w) m = fmaxf(m, s_umma.colmax[w][qi]);
+      s_rowM[qi] = m;
+    }
+  } else if (used_umma) {
+    // row maxima over the CTA's own tokens (tcgen05 path with many rows): one
+    // warp per row
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int base = ji.t0 - kMargin;
+    for (int qi = warp; qi < p.Rq; qi += kSWarps) {
+      const T* row = lg + (int64_t)qi * p.TB - base;
+      float m = -INFINITY;
+      for (int t = ji.t0 + lane; t < ji.t1; t += 32) m = fmaxf(m, Elem<T>::to_f(row[t]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) s_rowM[qi] = m;
+    }
+  } else {
+    for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
+      float m = -INFINITY;
+      for (int w = 0; w < kSWarps; ++w) m = fmaxf(m, wmax[w * kMaxRq + qi]);
+      s_rowM[qi] = m;
+    }
   }
   __syncthreads();
   // partial sum of exp over own tokens (four independent accumulators): one
@@ -1275,9 +1645,15 @@ struct ScorePlan {
   int cpj, T, TB, grid;
   size_t smem, logits_bytes;
   bool logits_in_smem;
+  bool umma;  // tcgen05 logits: tokens per CTA a multiple of 128
+  int n_stages, NP, tmem_cols;
 };
 
 static int num_sms() { return device_sms(current_device()); }
+
+// Dynamic shared memory a launch may use (the opt-in limit less the kernel's
+// static shared memory, with room to spare).
+constexpr size_t kDynSmemCap = 203 * 1024;
 
 template <typename T>
 static size_t smem_bytes(int Rq, int S, int T_, int TB, bool logits_in_smem, bool fma) {
@@ -1290,28 +1666,65 @@ static size_t smem_bytes(int Rq, int S, int T_, int TB, bool logits_in_smem, boo
   return b;
 }
 
-static bool uses_fma(int dtype, int Rq) { return dtype == HC_F32 || Rq > 40; }
-
 static size_t elem_size(int dtype) { return dtype == HC_F32 ? 4 : 2; }
 
-// Plan the partition: as many CTAs per job as fit co-resident (2 per SM by
-// default), token ranges a multiple of 32 (bitmap words stay CTA-private).
-static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int ctas_per_sm) {
+// Plan the partition: as many CTAs per job as fit co-resident (1 per SM),
+// token ranges a multiple of 32 (bitmap words stay CTA-private), of 128 for
+// the tcgen05 path (whole key tiles).
+//
+// Logits paths, 16-bit dtypes: up to 40 query rows (one observation window:
+// pivot sets, drift checks, HeteroCache prefill selection) the mma.sync path,
+// whose plain vector loads stream the keys faster than the TMA ring at these
+// row counts (measured at 128K tokens: drift check 49.7 vs 53.7 us, pivot set
+// 27.5 vs 31.5 us, the key stream being the limit of both); more rows (an
+// observation window of W > 1 queries) the tcgen05 path, when the keys'
+// tensor maps could be made (3.4x faster than the CUDA-core path at W = 32).
+// The tcgen05 path takes 2-6 shared-memory stages of 128 keys plus the query
+// operand; its logits stay in shared memory when that leaves four stages.
+// fp32: the CUDA-core path.
+static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int ctas_per_sm, bool umma) {
   ScorePlan pl;
+  pl.umma = umma && dtype != HC_F32 && Rq > 40;
+  const int gran = pl.umma ? 128 : 32;
   const int max_ctas = num_sms() * ctas_per_sm;
   int cpj = max(1, max_ctas / max(n_jobs, 1));
-  cpj = min(cpj, (L + 31) / 32);
-  int T_ = ((L + cpj - 1) / cpj + 31) / 32 * 32;
+  cpj = min(cpj, (L + gran - 1) / gran);
+  int T_ = ((L + cpj - 1) / cpj + gran - 1) / gran * gran;
   cpj = (L + T_ - 1) / T_;
   pl.cpj = cpj;
   pl.T = T_;
   pl.TB = T_ + 2 * kMargin;
   pl.grid = cpj * n_jobs;
-  const bool fma = uses_fma(dtype, Rq);
   const size_t es = elem_size(dtype);
-  size_t with = (size_t)Rq * pl.TB * es;
+  const size_t with = (size_t)Rq * pl.TB * es;
+  pl.n_stages = pl.NP = pl.tmem_cols = 0;
+  if (pl.umma) {
+    pl.NP = max(16, (Rq + 15) / 16 * 16);
+    pl.tmem_cols = 32;
+    while (pl.tmem_cols < 2 * pl.NP) pl.tmem_cols *= 2;
+    // the stage ring shares memory with the later phases' arrays
+    const size_t later = smem_bytes<float>(Rq, S, T_, pl.TB, false, false);
+    const size_t fixed = 1024 + (size_t)pl.NP * 256;
+    const size_t lgb = (with + 15) & ~(size_t)15;
+    auto stages_for = [&](bool lsm) {
+      const size_t used = fixed + (lsm ? lgb : 0);
+      return used >= kDynSmemCap ? 0 : (int)min((size_t)kMaxStages, (kDynSmemCap - used) / kUStage);
+    };
+    // logits in shared memory if that leaves at least four stages
+    pl.logits_in_smem = stages_for(true) >= 4;
+    pl.n_stages = stages_for(pl.logits_in_smem);
+    const size_t region = max((size_t)pl.n_stages * kUStage, later);
+    const size_t total = fixed + (pl.logits_in_smem ? lgb : 0) + region;
+    if (pl.n_stages >= 2 && total <= kDynSmemCap) {
+      pl.smem = total;
+      pl.logits_bytes = pl.logits_in_smem ? 0 : (size_t)pl.grid * Rq * pl.TB * es;
+      return pl;
+    }
+    pl.umma = false;  // no room: the legacy paths (128-token ranges are valid there too)
+  }
+  const bool fma = dtype == HC_F32 || Rq > 40;
   size_t rest = smem_bytes<float>(Rq, S, T_, pl.TB, false, fma);
-  pl.logits_in_smem = (with + rest + 64) <= 200 * 1024;
+  pl.logits_in_smem = (with + rest + 64) <= kDynSmemCap;
   pl.smem = rest + (pl.logits_in_smem ? ((with + 15) & ~(size_t)15) : 0);
   pl.logits_bytes = pl.logits_in_smem ? 0 : (size_t)pl.grid * Rq * pl.TB * es;
   return pl;
@@ -1337,7 +1750,8 @@ static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq, int L) {
 }
 
 template <typename T, int MODE>
-static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws_bytes, cudaStream_t st) {
+static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, const CUtensorMap* maps, void* ws,
+                             size_t ws_bytes, cudaStream_t st) {
   ScoreWs w = score_ws_layout(p.n_jobs, pl, p.Rq, p.L);
   if (!ws || ws_bytes < w.total) return HC_ERR_WORKSPACE;
   unsigned char* base = reinterpret_cast<unsigned char*>(ws);
@@ -1354,6 +1768,10 @@ static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size
   p.cpj = pl.cpj;
   p.T = pl.T;
   p.TB = pl.TB;
+  p.umma = pl.umma ? 1 : 0;
+  p.n_stages = pl.n_stages;
+  p.NP = pl.NP;
+  p.tmem_cols = pl.tmem_cols;
   auto kern = score_select_kernel<T, MODE>;
   // Attribute and occupancy queries are made once per device and shared-memory
   // size and cached, so a launch issues no non-stream CUDA call (graph capture
@@ -1395,30 +1813,53 @@ static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, void* ws, size
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return HC_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1]) != cudaSuccess) return HC_ERR_CUDA;
   return HC_OK;
 }
 
 template <typename T>
-static int launch_score(ScoreParams& p, const ScorePlan& pl, void* ws, size_t ws_bytes, cudaStream_t st) {
+static int launch_score(ScoreParams& p, const ScorePlan& pl, const CUtensorMap* maps, void* ws, size_t ws_bytes,
+                        cudaStream_t st) {
   switch (p.mode) {
-    case MODE_PREFILL: return launch_score_mode<T, MODE_PREFILL>(p, pl, ws, ws_bytes, st);
-    case MODE_PIVOT: return launch_score_mode<T, MODE_PIVOT>(p, pl, ws, ws_bytes, st);
-    case MODE_DRIFT: return launch_score_mode<T, MODE_DRIFT>(p, pl, ws, ws_bytes, st);
+    case MODE_PREFILL: return launch_score_mode<T, MODE_PREFILL>(p, pl, maps, ws, ws_bytes, st);
+    case MODE_PIVOT: return launch_score_mode<T, MODE_PIVOT>(p, pl, maps, ws, ws_bytes, st);
+    case MODE_DRIFT: return launch_score_mode<T, MODE_DRIFT>(p, pl, maps, ws, ws_bytes, st);
     default: return HC_ERR_INVALID;
   }
 }
 
-template <typename T>
-static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
-  // one 512-thread CTA per SM
-  ScorePlan pl = plan_score(std::is_same<T, float>::value ? HC_F32 : HC_BF16, p.n_jobs, p.L, p.Rq, p.S, 1);
-  return launch_score<T>(p, pl, ws, ws_bytes, st);
+// Tensor maps of the keys for the tcgen05 path: 128-row tiles and 16-row
+// margin tiles, over the paged pool (drift checks) or the dense [bsz, KV, L,
+// 128] keys (prefill scoring, pivot sets).  False if either cannot be made.
+static bool key_tensor_maps(const ScoreParams& p, int dtype, CUtensorMap* maps) {
+  if (p.mode == MODE_DRIFT) {
+    const long long rows = (long long)p.n_blocks * kPage;
+    return pool_tensor_map(&maps[0], p.k_pool, rows, dtype, 128) &&
+           pool_tensor_map(&maps[1], p.k_pool, rows, dtype, kMargin);
+  }
+  const int bsz = p.n_jobs / max(p.nh, 1);
+  return dense_tensor_map(&maps[0], p.k, bsz, p.KV, p.L, p.ksb, p.ksh, p.kst, dtype, 128) &&
+         dense_tensor_map(&maps[1], p.k, bsz, p.KV, p.L, p.ksb, p.ksh, p.kst, dtype, kMargin);
 }
 
+template <typename T>
+static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+  constexpr bool f32 = std::is_same<T, float>::value;
+  const int dtype = f32 ? HC_F32 : std::is_same<T, __half>::value ? HC_F16 : HC_BF16;
+  CUtensorMap maps[2];
+  std::memset(maps, 0, sizeof(maps));
+  const bool umma = !f32 && key_tensor_maps(p, dtype, maps);
+  // one 512-thread CTA per SM
+  ScorePlan pl = plan_score(dtype, p.n_jobs, p.L, p.Rq, p.S, 1, umma);
+  return launch_score<T>(p, pl, maps, ws, ws_bytes, st);
+}
+
+// Large enough for either plan (whether the keys' tensor maps can be made is
+// known only at launch).
 size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S) {
-  ScorePlan pl = plan_score(dtype, n_jobs, L, Rq, S, 1);
-  return score_ws_layout(n_jobs, pl, Rq, L).total;
+  const ScorePlan a = plan_score(dtype, n_jobs, L, Rq, S, 1, true);
+  const ScorePlan b = plan_score(dtype, n_jobs, L, Rq, S, 1, false);
+  return max(score_ws_layout(n_jobs, a, Rq, L).total, score_ws_layout(n_jobs, b, Rq, L).total);
 }
 
 int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {

@@ -1,0 +1,131 @@
+// 5th-generation tensor core (tcgen05) and TMA helpers for sm_100a.
+//
+// Operand layout used throughout: K-major tiles of 16-bit elements with the
+// 128-byte swizzle -- a tile of R rows x 128 elements is two "boxes" of
+// R rows x 64 elements (128 bytes per row); row r of a box sits at byte
+// r * 128 with its eight 16-byte chunks XOR-permuted by (r & 7).  TMA writes
+// exactly this layout for a tensor map with CU_TENSOR_MAP_SWIZZLE_128B and a
+// 64-element inner box; threads that stage an operand by hand use swz128().
+// Box bases are 1024-byte aligned (the swizzle phase comes from address
+// bits 7-9), so the shared-memory descriptors carry a base offset of 0.
+//
+// Bit layouts of the two descriptors (tcgen05 "matrix descriptor" and
+// "instruction descriptor", PTX ISA 8.6; the same fields CUTLASS's
+// cute/arch/mma_sm100_desc.hpp names):
+//   shared-memory descriptor (64 bit): [0,14) start address >> 4,
+//     [16,30) leading byte offset >> 4 (unused for swizzled K-major: 1),
+//     [32,46) stride byte offset >> 4 (8-row groups: 1024 B -> 64),
+//     [46,48) version = 1, [49,52) base offset, [52] LBO mode,
+//     [61,64) layout: 2 = 128-byte swizzle.
+//   instruction descriptor, kind::f16 (32 bit): [4,6) D format (1 = f32),
+//     [7,10) A format, [10,13) B format (0 = f16, 1 = bf16), [15] A major,
+//     [16] B major (0 = K-major), [17,23) N >> 3, [24,29) M >> 4.
+#pragma once
+
+#include <cuda.h>
+
+#include "hc_common.cuh"
+
+namespace hc {
+
+// ---------------------------------------------------------------------------
+// TMA tile loads (no multicast: every map covers this GPU's own memory),
+// completing on an mbarrier, with an L2 cache-policy hint.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%2, %3}], [%4], %5;\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, "
+      "{%2, %3, %4, %5}], [%6], %7;\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+// Generic-proxy writes to shared memory (operands staged by threads) become
+// visible to the async proxy (the tensor core's operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128-byte
+// swizzled box.
+__device__ __forceinline__ uint32_t swz128(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// ---------------------------------------------------------------------------
+// Tensor memory.  Allocation and release are warp-wide (.sync.aligned): one
+// warp allocates `ncols` columns (a power of two >= 32) and writes the base
+// address to shared memory; the same warp releases them.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Order tcgen05 operations against thread synchronisation (barriers).
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// UMMA (tcgen05.mma, one CTA).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+// M = 128, f32 accumulators, A and B K-major, both f16 (bf16 = false) or both bf16.
+__host__ __device__ constexpr uint32_t idesc_f16_m128(bool bf16, int N) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+// D[tmem] (+)= A[smem] * B[smem]^T; accumulate = 0 overwrites D.  Issued by one thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// The mbarrier receives one arrival once every tcgen05.mma this thread issued
+// before has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+// 16 consecutive f32 columns of this warp's 32 TMEM lanes: thread t receives
+// lane (32 * (warp % 4) + t) -- the caller puts that lane offset in taddr.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+// The same for 8 columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+
+}  // namespace hc

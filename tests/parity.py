@@ -62,10 +62,13 @@ def rounding_step(x: float, dtype: str) -> float:
     return 2.0 ** (e - m)
 
 
-def scores_close(res: Dict, dtype: str) -> bool:
+def scores_close(res: Dict, dtype: str, terms: int = 1) -> bool:
+    """``terms``: rounded probabilities summed into each score (the
+    observation window); a flip of any one of them can flip the sum, so the
+    16-bit bound scales with it."""
     if dtype == "float32":
         return res["max_rel"] <= FP32_MAX_REL
-    return res["flips"] <= max(FLIP_FRAC_16 * res["L"], FLIP_FLOOR_16)
+    return res["flips"] <= max(FLIP_FRAC_16 * res["L"] * terms, FLIP_FLOOR_16)
 
 
 def kth_largest(x: np.ndarray, k: int) -> float:

@@ -50,6 +50,9 @@ def _contiguous_pages(lengths, bsz, KV, max_blocks):
     ("bfloat16", 2048, "avgpool", 5, 1, LayerGeometry(8, 8, 128)),
     ("float16", 2500, "avgpool", 5, 1, LayerGeometry(16, 8, 128)),
     ("bfloat16", 2048, "maxpool", 7, 1, LayerGeometry(64, 8, 128)),
+    # observation window of 32 (128 query rows per KV head) at long context
+    ("bfloat16", 131072, "maxpool", 7, 32, LLAMA_8B),
+    ("float16", 20000, "avgpool", 5, 32, QWEN_7B),
 ])
 def test_prefill_select_matches_oracle(cuda_device, dtype, L, pooling, ks, window, geo):
     tdt = DT[dtype]
@@ -85,7 +88,7 @@ def test_prefill_select_matches_oracle(cuda_device, dtype, L, pooling, ks, windo
         assert idx[0, h, keep[h]:].eq(-1).all()
         res = compare_selection(ref[0, h].float().numpy(), dsc[0, h].numpy(), sel, keep[h], dtype)
         assert res["ok"], res
-        assert scores_close(res, dtype), res
+        assert scores_close(res, dtype, terms=window), {k: res[k] for k in ("flips", "L", "max_rel")}
         start = int(bt[h, 0]) * 256
         assert torch.equal(kflat[start:start + keep[h]], k[0, h, sel]), h
         assert torch.equal(vflat[start:start + keep[h]], v[0, h, sel]), h
