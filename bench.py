@@ -448,15 +448,24 @@ def run_reference(args, rank, world):
             per_layer.append(dt)
     us_layer = float(np.mean(per_layer)) * 1e6
     tok_s = 1e6 / (us_layer * args.layers)
+    # a step of this arm is one layer of one decode token (the sampled layer):
+    # ms_per_step x steps is the time actually measured; tokens/s scales the
+    # mean layer time to the model's layers
     line = {"impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer * args.layers / 1e3,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": us_layer / 1e3,
+            "step": f"one decode layer-step of the sampled layers; tokens/s = 1 / (mean layer-step time x "
+                    f"{args.layers} layers)",
+            "timed_region_s": float(np.sum(per_layer)),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) with planted heavy hitters; drifting decode queries)",
             "config": config_dict(args, world), "us_per_layer": us_layer,
             "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                              "sample": f"oracle decode (append + paged attention + decode_select) of one layer per "
                                        f"step, layers {sample_layers} alternating, {args.steps} timed steps; "
-                                       f"tokens/s = 1 / (mean layer time x {args.layers})"},
+                                       f"tokens/s = 1 / (mean layer time x {args.layers})",
+                             "why_port": "the reference is Python and its checkout is not on the GPU host; its "
+                                         "restatement (oracle/hc_oracle.py), pinned bit for bit to outputs of the "
+                                         "unmodified reference (tests/golden), is what runs here"},
             "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "prefill_s_sampled_layers": t_pre}
     print(json.dumps(line), flush=True)
