@@ -70,6 +70,8 @@ def parse():
     ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"])
     ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-head-sharded", action="store_true",
+                    help="skip the head-sharded config-4 measurement the default workload also reports")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     if args.workload == "config4":
@@ -549,6 +551,13 @@ def run_ours(args, rank, world, local_rank):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, graph, qs, ks, vs, dev, world)
+    # the multi-GPU configuration's head-sharded mode (config 4: one Llama
+    # layer, 8 sequences x 65536 tokens, every sequence's KV heads split over
+    # the ranks, one NCCL all-gather of head outputs per step), so that a
+    # scaling run over N GPUs also measures the collective
+    head_sharded = None
+    if not args.no_head_sharded and args.model == "llama":
+        head_sharded = measure_config4(args, rank, world, local_rank, True, 8, 65536, args.steps, args.warmup)
     cpu = None
     if rank == 0 and not args.no_cpu:
         times, cores = cpu_baseline(cache, 0, 2 * STEPS_PER_CHECK, qs, ks, vs)
@@ -565,6 +574,8 @@ def run_ours(args, rank, world, local_rank):
                 "config": config_dict(args, world), "us_per_layer": ms_step * 1000.0 / args.layers,
                 "prefill_ms_per_layer": float(np.mean(prefill_ms)), "roofline": roof, "cpu_baseline": cpu,
                 "e2e": e2e, "gpu_launches": launches, "clocks": clk}
+        if head_sharded is not None:
+            line["head_sharded"] = head_sharded
         print(json.dumps(line), flush=True)
 
 
@@ -599,17 +610,19 @@ class PhaseGraphs:
             c._qcount[0] = (phase + 1) % self.S
 
 
-def run_config4(args, rank, world, local_rank):
-    """Config 4: one Llama layer, a batch of independent sequences, sharded by
-    sequence (no collective) or by KV head (all-gather + broadcasts)."""
+def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, warmup):
+    """Config 4: one Llama layer, a batch of `n_seq` independent sequences of
+    `L` tokens, sharded by sequence (no collective) or by KV head (every
+    sequence's 8 KV heads split over the ranks: an NCCL all-gather of the
+    head outputs per step, broadcasts of pivot position lists at check
+    steps).  Returns the measurement (all ranks take part; the timings are
+    the max over ranks)."""
     from heterocache_b200.cache import HeteroCacheConfig
     from heterocache_b200.head_shard import HeadShardedCache, gather_heads
     from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    n_seq, L = args.seqs, args.ctx
     data = build_roles(1)
-    heads_mode = args.shard == "heads"
     if heads_mode:
         seqs = list(range(n_seq))
         cfg = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.5, real_offload=False,
@@ -644,7 +657,7 @@ def run_config4(args, rank, world, local_rank):
     for c in inner:
         c.check_errors()
     n_local = len(seqs)
-    total = args.warmup + args.steps + 2 * STEPS_PER_CHECK
+    total = warmup + steps + 2 * STEPS_PER_CHECK
     gq = torch.Generator(device=dev).manual_seed(77)
     cur = torch.cat(q_last, 0).float()  # [n_local, H, 1, D]
     qs = torch.empty(total, n_local, 1, H, 1, D, device=dev, dtype=torch.bfloat16)
@@ -664,7 +677,6 @@ def run_config4(args, rank, world, local_rank):
         vb.copy_(kvs[1, t][:, :, ks])
 
     local = torch.zeros(n_local, hl, D, dtype=torch.bfloat16, device=dev)
-    crossing = [False]
 
     def local_step():
         """Everything but the collectives: captured in the phase graphs."""
@@ -673,7 +685,8 @@ def run_config4(args, rank, world, local_rank):
         if heads_mode:
             for i, view in enumerate(views):
                 view.cache.attention(qb[i], 0, out=local[i:i + 1])
-            crossing[0] = any([view.select_local(qb[i], 0) for i, view in enumerate(views)])
+            for i, view in enumerate(views):
+                view.select_local(qb[i], 0)
         else:
             for i, view in enumerate(views):
                 view.attention(qb[i], 0, out=out[i:i + 1])
@@ -681,13 +694,22 @@ def run_config4(args, rank, world, local_rank):
         for c in inner:
             c.join_retrievals()
 
-    def collectives(check):
+    gather_events = []
+
+    def collectives(check, timed=False):
         """Head-sharded mode, eager (NCCL stays out of the graphs): the output
-        all-gather, and at a check step the position-list broadcasts and the
-        retrievals of satellites whose pivot sits on another GPU."""
+        all-gather of every sequence in one call, and at a check step the
+        position-list broadcasts and the retrievals of satellites whose pivot
+        sits on another GPU."""
         if not heads_mode:
             return
+        if timed:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
         gather_heads(local, world, out=out, cache=stage)
+        if timed:
+            e1.record()
+            gather_events.append((e0, e1))
         if check:
             for view in views:
                 view.remote_checks(0)
@@ -704,52 +726,70 @@ def run_config4(args, rank, world, local_rank):
         c.prepare_decode([0], qb[0])
     graphs = PhaseGraphs(inner, local_step, STEPS_PER_CHECK)
 
-    def graph_step():
+    def graph_step(timed=False):
         check = inner[0]._qcount[0] + 1 >= STEPS_PER_CHECK
         graphs.step()
-        collectives(check)
+        collectives(check, timed)
 
     t0 = STEPS_PER_CHECK
-    for t in range(t0, t0 + args.warmup):
+    for t in range(t0, t0 + warmup):
         load(t)
         graph_step()
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    clocks = Clocks(local_rank) if rank == 0 else None
-    time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record()
-    first = t0 + args.warmup
-    for t in range(first, first + args.steps):
+    first = t0 + warmup
+    for t in range(first, first + steps):
         load(t)
-        graph_step()
+        graph_step(timed=True)
     e1.record()
     torch.cuda.synchronize()
-    clk = clocks.stop() if clocks else None
     ms = e0.elapsed_time(e1)
+    ag_ms = sum(a.elapsed_time(b) for a, b in gather_events)
     if world > 1:
-        tt = torch.tensor([ms], device=dev)
+        tt = torch.tensor([ms, ag_ms], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms = float(tt.item())
+        ms, ag_ms = float(tt[0].item()), float(tt[1].item())
         torch.distributed.barrier()
     for c in inner:
         c.check_errors()
-    ms_step = ms / args.steps
     del graphs
+    ms_step = ms / steps
+    mode = (f"KV-head-sharded x{world} (each GPU {KV // world} of the 8 KV heads of every sequence; NCCL "
+            f"all-gather of the head outputs per step)" if heads_mode
+            else f"sequence-sharded x{world} ({n_seq // world} sequences per GPU, no data-path collective)")
+    res = {"value": n_seq * 1000.0 / ms_step, "unit": "tokens/s", "ms_per_step": ms_step, "steps": steps,
+           "sequences": n_seq, "context": L, "parallelism": mode}
+    if heads_mode:
+        res["allgather_us_per_step"] = ag_ms * 1e3 / steps
+        res["allgather_share"] = ag_ms / ms if ms > 0 else None
+        res["collective"] = ("torch.distributed.all_gather_into_tensor (NCCL)" if world > 1
+                             else "none (one rank holds every head)")
+    return res
+
+
+def run_config4(args, rank, world, local_rank):
+    """Config 4 on its own: one JSON line (strong scaling)."""
+    heads_mode = args.shard == "heads"
+    clocks = Clocks(local_rank) if rank == 0 else None
+    r = measure_config4(args, rank, world, local_rank, heads_mode, args.seqs, args.ctx, args.steps, args.warmup)
+    clk = clocks.stop() if clocks else None
     if rank == 0:
-        mode = (f"KV-head-sharded x{world} (NCCL all-gather of head outputs per step)" if heads_mode
-                else f"sequence-sharded x{world} ({n_seq // world} sequences per GPU, no data-path collective)")
-        line = {"metric": METRIC, "value": n_seq * 1000.0 / ms_step, "unit": "tokens/s", "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        line = {"metric": METRIC, "value": r["value"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": "synthetic (seeded N(0,1) K/V with planted heavy hitters; drifting decode queries)",
-                "config": {"workload": f"config 4: llama-3.1-8b single attention layer, batch of {n_seq} "
-                                       f"independent sequences of {L} tokens, HeteroCache decode",
-                           "context": L, "sequences": n_seq, "parallelism": mode},
-                "us_per_step": ms_step * 1e3, "roofline": None, "cpu_baseline": None, "e2e": None,
+                "config": {"workload": f"config 4: llama-3.1-8b single attention layer, batch of {args.seqs} "
+                                       f"independent sequences of {args.ctx} tokens, HeteroCache decode",
+                           "context": args.ctx, "sequences": args.seqs, "parallelism": r["parallelism"]},
+                "us_per_step": r["ms_per_step"] * 1e3, "roofline": None, "cpu_baseline": None, "e2e": None,
                 "clocks": clk}
+        for key in ("allgather_us_per_step", "allgather_share", "collective"):
+            if key in r:
+                line[key] = r[key]
         print(json.dumps(line), flush=True)
 
 
