@@ -312,11 +312,13 @@ def time_kernels(cache, layers, reps=5):
     def retrieve():
         for l, trig in forced.items():
             jobs = cache._jobs[l]
+            fk, fv, first = cache.full_tier(l)
             ops.retrieve(member_job=jobs.member_job, member_head=jobs.member_head, member_len=jobs.member_len,
                          max_member_len=jobs.max_member_len, trigger=trig,
-                         retrieve_positions=jobs.retrieve_positions, full_k=cache.key_cache_cpu[l],
-                         full_v=cache.value_cache_cpu[l], k_pool=cache.key_pools[l], v_pool=cache.value_pools[l],
-                         block_table=cache.block_tables[l], num_kv_heads=cache.num_kv_heads, err=cache._err)
+                         retrieve_positions=jobs.retrieve_positions, full_k=fk, full_v=fv,
+                         k_pool=cache.key_pools[l], v_pool=cache.value_pools[l],
+                         block_table=cache.block_tables[l], num_kv_heads=cache.num_kv_heads, err=cache._err,
+                         tier_first_head=first)
 
     res = {}
     per_fn = {"flash_decode": layers, "drift_check": layers, "retrieve": max(len(forced), 1)}
@@ -373,9 +375,15 @@ def cpu_baseline(cache, layer, n_steps, qs, ks, vs):
     orc.free_blocks[layer] = cache.free_blocks[layer].cpu()
     orc.free_ptr = [0] * n
     orc.free_ptr[layer] = cache.free_block_pointers[layer]
-    if cache.key_cache_cpu[layer] is not None:
-        orc.full_k[layer] = cache.key_cache_cpu[layer].cpu()
-        orc.full_v[layer] = cache.value_cache_cpu[layer].cpu()
+    tier = cache.full_tier(layer)
+    if tier is not None:
+        # the oracle reads a [bsz, KV, L, D] tier by head id
+        fk, fv, first = tier
+        shape = (fk.shape[0], cfg.num_kv_heads) + tuple(fk.shape[2:])
+        orc.full_k[layer] = torch.zeros(shape, dtype=fk.dtype)
+        orc.full_v[layer] = torch.zeros(shape, dtype=fv.dtype)
+        orc.full_k[layer][:, first:first + fk.shape[1]] = fk.cpu()
+        orc.full_v[layer][:, first:first + fv.shape[1]] = fv.cpu()
     orc.prefill_topk_set = [None] * n
     if isinstance(cache.prefill_topk_set[layer], torch.Tensor):
         orc.prefill_topk_set[layer] = cache.prefill_topk_set[layer].cpu().long()

@@ -190,6 +190,9 @@ class HeteroCache(_CacheBase):
         # are built) and the retrieval staging area shared by all layers
         self._kept: List[Optional[tuple]] = [None] * n
         self._stage: Optional[tuple] = None
+        # head id held in row 0 of each layer's full tier (pinned-host tier:
+        # the first satellite; a device tier keeps every head)
+        self._tier_first: List[int] = [0] * n
         self._retrieve_done: List[Optional[torch.cuda.Event]] = [None] * n
         self._side_stream: Optional[torch.cuda.Stream] = None
         # host mirrors of deterministic bookkeeping
@@ -333,22 +336,33 @@ class HeteroCache(_CacheBase):
                 self.key_cache_cpu.append(None)
                 self.value_cache_cpu.append(None)
             elif self.real_offload:
+                # only the satellites' rows are ever read back (retrieval):
+                # after the load-time role permutation they are contiguous
+                # heads, so the pinned tier holds [bsz, n_sat, L, D] from
+                # head `first` on (the reference backs up every head,
+                # cache_utils.py:953-960)
+                first, n_tier = 0, self.num_kv_heads
+                if list(upd) == list(range(upd[0], upd[0] + len(upd))):
+                    first, n_tier = upd[0], len(upd)
+                ks = key_states.detach()[:, first:first + n_tier]
+                vs = value_states.detach()[:, first:first + n_tier]
                 try:
-                    kc = torch.empty(key_states.shape, dtype=key_states.dtype, pin_memory=True)
-                    vc = torch.empty(value_states.shape, dtype=value_states.dtype, pin_memory=True)
+                    kc = torch.empty(ks.shape, dtype=key_states.dtype, pin_memory=True)
+                    vc = torch.empty(vs.shape, dtype=value_states.dtype, pin_memory=True)
                 except RuntimeError as e:
-                    nbytes = 2 * key_states.numel() * key_states.element_size()
+                    nbytes = 2 * ks.numel() * key_states.element_size()
                     raise RuntimeError(f"Layer {layer_idx}: pinned host allocation of {nbytes} bytes for the "
                                        f"full KV tier failed ({e})") from e
                 side = self._side()
                 side.wait_stream(torch.cuda.current_stream(key_states.device))
                 with torch.cuda.stream(side):
-                    kc.copy_(key_states.detach(), non_blocking=True)
-                    vc.copy_(value_states.detach(), non_blocking=True)
+                    kc.copy_(ks, non_blocking=True)
+                    vc.copy_(vs, non_blocking=True)
                 key_states.record_stream(side)
                 value_states.record_stream(side)
                 self.key_cache_cpu.append(kc)
                 self.value_cache_cpu.append(vc)
+                self._tier_first[layer_idx] = first
             else:
                 self.key_cache_cpu.append(key_states.detach())
                 self.value_cache_cpu.append(value_states.detach())
@@ -593,6 +607,10 @@ class HeteroCache(_CacheBase):
             return
         full_k = self.key_cache_cpu[layer_idx]
         full_v = self.value_cache_cpu[layer_idx]
+        first = self._tier_first[layer_idx]
+        if jobs.m_head_list and not (first <= min(jobs.m_head_list) and
+                                     max(jobs.m_head_list) < first + full_k.shape[1]):
+            raise RuntimeError(f"Layer {layer_idx}: a satellite lies outside the full tier's heads")
         if self.real_offload:
             main = torch.cuda.current_stream(self._dev)
             side = self._side()
@@ -605,6 +623,7 @@ class HeteroCache(_CacheBase):
                                    reuse_len=jobs.delta["reuse"], max_member_len=jobs.max_member_len,
                                    trigger=jobs.trigger, retrieve_positions=jobs.retrieve_positions,
                                    slot_positions=jobs.delta["slot"], full_k=full_k, full_v=full_v,
+                                   tier_first_head=first,
                                    k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
                                    block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
                                    stage_k=sk, stage_v=sv, stage_src=ss, err=self._err, stream=side)
@@ -614,7 +633,7 @@ class HeteroCache(_CacheBase):
                              retrieve_positions=jobs.retrieve_positions, full_k=full_k, full_v=full_v,
                              k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
                              block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
-                             err=self._err, stream=side)
+                             err=self._err, stream=side, tier_first_head=first)
             ev = torch.cuda.Event()
             ev.record(side)
             self._retrieve_done[layer_idx] = ev
@@ -624,7 +643,15 @@ class HeteroCache(_CacheBase):
                          retrieve_positions=jobs.retrieve_positions, full_k=full_k, full_v=full_v,
                          k_pool=self.key_pools[layer_idx], v_pool=self.value_pools[layer_idx],
                          block_table=self.block_tables[layer_idx], num_kv_heads=self.num_kv_heads,
-                         err=self._err)
+                         err=self._err, tier_first_head=first)
+
+    def full_tier(self, layer_idx):
+        """(k, v, first_head): the layer's full KV tier and the head id of its
+        row 0 ([bsz, heads, L, D] on the device, or the satellites' rows in
+        pinned host memory), or None for a layer without satellites."""
+        if self.key_cache_cpu[layer_idx] is None:
+            return None
+        return self.key_cache_cpu[layer_idx], self.value_cache_cpu[layer_idx], self._tier_first[layer_idx]
 
     # ------------------------------------------------------------------
     def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):

@@ -220,11 +220,12 @@ class HeadShardedCache:
                                torch.tensor(lens, **i32), max(lens))
         mj, mh, ml, max_len = self._bufs[key]
         c._wait_retrieval(layer_idx)
+        full_k, full_v, first = c.full_tier(layer_idx)
         ops.retrieve(member_job=mj, member_head=mh, member_len=ml, max_member_len=max_len, trigger=buf[0:1],
-                     retrieve_positions=buf[1:].view(1, -1), full_k=c.key_cache_cpu[layer_idx],
-                     full_v=c.value_cache_cpu[layer_idx], k_pool=c.key_pools[layer_idx],
-                     v_pool=c.value_pools[layer_idx], block_table=c.block_tables[layer_idx],
-                     num_kv_heads=c.num_kv_heads, err=c._err)
+                     retrieve_positions=buf[1:].view(1, -1), full_k=full_k, full_v=full_v,
+                     k_pool=c.key_pools[layer_idx], v_pool=c.value_pools[layer_idx],
+                     block_table=c.block_tables[layer_idx], num_kv_heads=c.num_kv_heads, err=c._err,
+                     tier_first_head=first)
 
     def check_errors(self):
         self.cache.check_errors()

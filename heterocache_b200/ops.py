@@ -318,9 +318,19 @@ def drift_check(qbuf, k_pool, block_table, *, num_kv_heads, groups, steps, seq_l
     LAUNCHES[0] += 1
 
 
+def _tier_base(full: torch.Tensor, first_head: int) -> int:
+    """Address the kernels index as head 0 of a full tier whose row 0 holds
+    head `first_head` (a tier of the satellites only): they read head h at
+    base + h * head_stride, so only heads >= first_head are ever addressed."""
+    return full.data_ptr() - first_head * full.stride(1) * full.element_size()
+
+
 def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, retrieve_positions, full_k, full_v,
-             k_pool, v_pool, block_table, num_kv_heads, err, stream: Optional[torch.cuda.Stream] = None):
-    """full_k/full_v: [1, KV, L, D] on the device or in pinned host memory."""
+             k_pool, v_pool, block_table, num_kv_heads, err, stream: Optional[torch.cuda.Stream] = None,
+             tier_first_head: int = 0):
+    """full_k/full_v: [1, heads, L, D] on the device or in pinned host memory,
+    row 0 holding head `tier_first_head` (every member's head lies in the
+    tier)."""
     _need(retrieve_positions.shape[-1] >= max_member_len, "retrieve_positions rows need max_member_len entries")
     _need(member_head.numel() >= member_job.numel() and member_len.numel() >= member_job.numel(),
           "member_head and member_len need an entry per member")
@@ -334,7 +344,8 @@ def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, re
     rc = lib().hc_retrieve(dtype_code(k_pool), num_kv_heads, k_pool.shape[-1], member_job.numel(),
                            _ptr(member_job), _ptr(member_head), _ptr(member_len), int(max_member_len),
                            _ptr(trigger), _ptr(retrieve_positions), retrieve_positions.shape[-1],
-                           _ptr(full_k), _ptr(full_v), full_k.stride(1), full_k.stride(2),
+                           _tier_base(full_k, tier_first_head), _tier_base(full_v, tier_first_head),
+                           full_k.stride(1), full_k.stride(2),
                            _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table), block_table.shape[1],
                            _ptr(err), st)
     check("hc_retrieve", rc)
@@ -343,7 +354,8 @@ def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, re
 
 def retrieve_delta(*, member_job, member_head, member_len, member_stage_offset, reuse_len, max_member_len, trigger,
                    retrieve_positions, slot_positions, full_k, full_v, k_pool, v_pool, block_table, num_kv_heads,
-                   stage_k, stage_v, stage_src, err, stream: Optional[torch.cuda.Stream] = None):
+                   stage_k, stage_v, stage_src, err, stream: Optional[torch.cuda.Stream] = None,
+                   tier_first_head: int = 0):
     """Satellite retrieval from a pinned-host tier that moves only rows the
     satellite does not hold yet (same pool contents as ``retrieve``).
 
@@ -374,7 +386,8 @@ def retrieve_delta(*, member_job, member_head, member_len, member_stage_offset, 
                                  _ptr(member_job), _ptr(member_head), _ptr(member_len), _ptr(member_stage_offset),
                                  _ptr(reuse_len), int(max_member_len), _ptr(trigger), _ptr(retrieve_positions),
                                  retrieve_positions.shape[-1], _ptr(slot_positions), slot_positions.shape[-1],
-                                 _ptr(full_k), _ptr(full_v), full_k.stride(1), full_k.stride(2),
+                                 _tier_base(full_k, tier_first_head), _tier_base(full_v, tier_first_head),
+                                 full_k.stride(1), full_k.stride(2),
                                  _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
                                  block_table.shape[1], _ptr(stage_k), _ptr(stage_v), _ptr(stage_src),
                                  stage_k.shape[0], _ptr(err), st)

@@ -293,3 +293,27 @@ def test_deferred_append_matches_immediate(cuda_device, order):
     for c in caches:
         c.check_errors()
     assert n_checks > 0
+
+
+def test_host_tier_holds_only_the_satellites(cuda_device):
+    """The pinned-host full tier keeps the satellites' rows only (the reference
+    backs up every KV head, cache_utils.py:953-960; only satellites are read
+    back): [bsz, n_sat, L, D] from the first satellite head on, bit-equal to
+    the prefill K/V of those heads."""
+    sc = SCENARIOS["llama_bf16_2layer_star8"]
+    geo, tdt, layer_inputs = scenario_inputs(sc)
+    gpu, _ = _gpu_cache(sc, real_offload=True)
+    dev = cuda_device
+    for layer, (q, k, v) in enumerate(layer_inputs):
+        gpu.update(k.to(dev), v.to(dev), layer)
+    torch.cuda.synchronize()
+    for layer, (q, k, v) in enumerate(layer_inputs):
+        sats = gpu.data["need_to_update_counts"][layer]
+        tier = gpu.full_tier(layer)
+        if not sats:
+            assert tier is None
+            continue
+        fk, fv, first = tier
+        assert fk.is_pinned() and fv.is_pinned()
+        assert first == sats[0] and fk.shape[1] == len(sats) == sats[-1] - sats[0] + 1
+        assert torch.equal(fk, k[:, sats[0]:sats[-1] + 1]) and torch.equal(fv, v[:, sats[0]:sats[-1] + 1])
