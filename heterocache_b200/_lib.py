@@ -57,6 +57,10 @@ SIGNATURES = {
                                c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p, c_int, c_int, c_void_p,
                                c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_drift_check_batch_per_launch": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "hc_drift_check_batch_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "hc_drift_check_batch": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_double,
+                                     c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
     "hc_retrieve": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                             c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                             c_int, c_void_p, c_int, c_void_p, c_void_p]),
@@ -65,6 +69,17 @@ SIGNATURES = {
                                   c_int64, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                   c_void_p, c_int64, c_void_p, c_void_p]),
 }
+
+
+
+class DriftJob(ctypes.Structure):
+    """``hc_drift_job``: one drift check of a batch (device pointers)."""
+    _fields_ = [("qbuf", c_void_p), ("qss", c_int64), ("qsh", c_int64), ("k_pool", c_void_p),
+                ("block_table", c_void_p), ("n_pool_blocks", c_int), ("max_blocks", c_int),
+                ("pivot_head", c_int), ("max_len", c_int), ("ref_bitmap", c_void_p),
+                ("ref_positions", c_void_p), ("trigger", c_void_p), ("retrieve_positions", c_void_p),
+                ("coeffs", c_void_p), ("median", c_void_p), ("out_scores", c_void_p)]
+
 
 _LIB = None
 

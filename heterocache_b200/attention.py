@@ -116,7 +116,12 @@ class _HeteroAttention(nn.Module):
             cache.decode_select(q, self.layer_idx)
         out = cache.attention(q, self.layer_idx, scale=self.scaling)  # [bsz, H, D]
         if not self.decode_select_before_attention:
-            cache.decode_select(q, self.layer_idx)
+            # the layer's attention is done: its drift check may wait for the
+            # batch at the end of the step (or the next step's first update)
+            if getattr(cache, "defer_checks", False):
+                cache.decode_select(q, self.layer_idx, defer=True)
+            else:
+                cache.decode_select(q, self.layer_idx)
         return self.o_proj(out.reshape(bsz, 1, -1)), None
 
 

@@ -121,6 +121,8 @@ class _LayerJobs:
         self.member_len = torch.tensor(m_len, **i32)
         self.m_head_list, self.m_len_list = list(m_head), list(m_len)
         self.delta = None  # slot maps of the delta retrieval (pinned-host tier)
+        self.slot_list, self.max_len_list = list(slots), list(max_len)
+        self.batch_descs = None  # drift-check batch descriptors (HeteroCache._drift_descs)
         self.trigger = torch.zeros(max(self.n_jobs, 1), **i32)
         self.retrieve_positions = torch.zeros(max(self.n_jobs, 1), max(self.max_len_cap, 1), **i32)
         self.coeffs = None
@@ -200,6 +202,16 @@ class HeteroCache(_CacheBase):
         self._mapped: List[Optional[np.ndarray]] = [None] * n
         # opt-in diagnostics for parity tests: pooled scores and selections
         self.record_checks = bool(getattr(cache_config, "record_checks", False))
+        # drift checks put off by decode_select(..., defer=True) until
+        # flush_checks(), which runs them as one batch.  Off by default with
+        # the pinned-host tier: there a layer's retrieval should start right
+        # after its check, to overlap the following layers
+        self.defer_checks = bool(getattr(cache_config, "defer_checks",
+                                         not getattr(cache_config, "real_offload", False)))
+        self._deferred: List[int] = []
+        self._batch_arrays: Dict = {}
+        # checks per batch launch (0: the library's choice)
+        self.drift_batch_per_launch = int(getattr(cache_config, "drift_batch_per_launch", 0))
         self.check_log: List[Dict] = []
         self.recorded: Dict = {}
 
@@ -300,6 +312,7 @@ class HeteroCache(_CacheBase):
         retrievals (host-tier mode) and deferred page appends.  A captured
         decode step ends with this, so each CUDA graph joins the side-stream
         work it forked."""
+        self.flush_checks()
         for layer_idx in range(len(self._retrieve_done)):
             self._wait_retrieval(layer_idx)
             self._wait_append(layer_idx)
@@ -307,6 +320,8 @@ class HeteroCache(_CacheBase):
     # ------------------------------------------------------------------
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):
         """heterocache/cache_utils.py:884-1005."""
+        if self._deferred and layer_idx in self._deferred:
+            self.flush_checks()  # the put-off check reads this layer's query buffer
         if layer_idx == 0:
             self._seen_tokens += key_states.shape[-2]
         self._ensure_device(key_states.device)
@@ -534,9 +549,20 @@ class HeteroCache(_CacheBase):
                            torch.empty(rows, **i32))
 
     def prepare_decode(self, layers, query_example) -> None:
-        """Allocate every layer's decode-time buffers now (before graph capture)."""
+        """Allocate every layer's decode-time buffers now (before graph capture),
+        the scoring workspace included: large enough for a drift-check batch
+        of all these layers and for each layer's own check."""
         for l in layers:
             self._ensure_decode_state(l, query_example)
+        n = sum(self._jobs[l].n_jobs for l in layers if self._jobs[l] is not None)
+        if n and self._ws_score is not None:
+            dt = ops.DTYPES[query_example.dtype]
+            S, G = self.decode_step, self.num_key_value_groups
+            need = max(ops.lib().hc_drift_check_batch_workspace_size(dt, n, S, self.prefill_len, G,
+                                                                     self.drift_batch_per_launch),
+                       max(ops.lib().hc_drift_check_workspace_size(dt, self._jobs[l].n_jobs, S, self.prefill_len, G)
+                           for l in layers if self._jobs[l] is not None))
+            self._ws_score.get(need)
 
     def _host_state(self):
         return {"hlen": [None if h is None else h.copy() for h in self._hlen],
@@ -545,16 +571,25 @@ class HeteroCache(_CacheBase):
                 "retrieve_done": list(self._retrieve_done), "seen": self._seen_tokens,
                 "pending": [None if x is None else list(x) for x in self._pending],
                 "append_done": list(self._append_done),
-                "q_staged": list(self._q_staged)}
+                "q_staged": list(self._q_staged), "deferred": list(self._deferred)}
 
     def _restore_host_state(self, s) -> None:
         self._hlen, self._mapped = s["hlen"], s["mapped"]
         self.free_block_pointers, self._qcount = s["free_ptr"], s["qcount"]
         self._retrieve_done, self._seen_tokens = s["retrieve_done"], s["seen"]
         self._pending, self._append_done, self._q_staged = s["pending"], s["append_done"], s["q_staged"]
+        self._deferred = s["deferred"]
 
-    def decode_select(self, query_states, layer_idx):
-        """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147)."""
+    def decode_select(self, query_states, layer_idx, defer: bool = False):
+        """Pivot drift check and satellite retrieval (heterocache/cache_utils.py:1007-1147).
+
+        ``defer=True`` (with ``defer_checks`` on) puts a due check off until
+        ``flush_checks()``, which runs every put-off layer's check in one
+        batch.  The caller guarantees that the layer's attention does not run
+        before that (the Llama order, where decode_select follows attention);
+        the layer's next update, attention or decode_select flushes first."""
+        if self._deferred and layer_idx in self._deferred:
+            self.flush_checks()
         S = self.decode_step
         self._ensure_decode_state(layer_idx, query_states)
         pend = self._pending[layer_idx]
@@ -578,7 +613,65 @@ class HeteroCache(_CacheBase):
         jobs = self._jobs[layer_idx]
         if jobs is None or jobs.n_jobs == 0:
             return
+        if defer and self.defer_checks:
+            self._deferred.append(layer_idx)
+            return
         self._drift_and_retrieve(layer_idx, jobs, query_states)
+
+    def flush_checks(self) -> None:
+        """Run the drift checks put off by decode_select(..., defer=True): all
+        put-off layers' pivots in one hc_drift_check_batch call (a few
+        launches instead of one per layer), then each layer's retrieval.
+        Every result is the one the check gives where it was put off: no
+        update, attention or decode_select of such a layer runs before this."""
+        layers, self._deferred = self._deferred, []
+        if not layers:
+            return
+        for l in layers:
+            self._wait_retrieval(l)
+        key = tuple(layers)
+        arr = self._batch_arrays.get(key)
+        if arr is None:
+            descs = []
+            for l in layers:
+                descs.extend(self._drift_descs(l))
+            arr = ops.drift_jobs_array(descs)
+            self._batch_arrays[key] = arr
+        dt = self.key_pools[layers[0]].dtype
+        ops.drift_check_batch(arr, dtype=dt, device=self._dev, num_kv_heads=self.num_kv_heads,
+                              groups=self.num_key_value_groups, steps=self.decode_step, seq_len=self.prefill_len,
+                              pooling=self.pooling, kernel_size=self.kernel_size, topk=self.base_compress_len,
+                              threshold=self.stable_threshold, workspace=self._ws_score, err=self._err,
+                              jobs_per_launch=self.drift_batch_per_launch)
+        for l in layers:
+            jobs = self._jobs[l]
+            if self.record_checks:
+                self._log_check(l, jobs, None)
+            self._retrieve_layer(l, jobs)
+
+    def _drift_descs(self, layer_idx):
+        """The layer's drift-check descriptors (built once: every tensor they
+        point into lives as long as the cache)."""
+        jobs = self._jobs[layer_idx]
+        if jobs.batch_descs is None:
+            bm, ref = self._ref_bitmap[layer_idx], self.prefill_topk_set[layer_idx]
+            jobs.batch_descs = [
+                ops.drift_job(self._qbuf[layer_idx], self.key_pools[layer_idx], self.block_tables[layer_idx],
+                              pivot_head=jobs.pivot_list[j], max_len=jobs.max_len_list[j],
+                              ref_bitmap=bm[0, jobs.slot_list[j]], ref_positions=ref[0, jobs.slot_list[j]],
+                              trigger=jobs.trigger[j:j + 1], retrieve_positions=jobs.retrieve_positions[j],
+                              coeffs=None if jobs.coeffs is None else jobs.coeffs[j],
+                              median=None if jobs.median is None else jobs.median[j:j + 1])
+                for j in range(jobs.n_jobs)]
+        return jobs.batch_descs
+
+    def _log_check(self, layer_idx, jobs, scores) -> None:
+        self.check_log.append({"layer": layer_idx, "trigger": jobs.trigger.clone(),
+                               "coeffs": jobs.coeffs.clone(), "median": jobs.median.clone(),
+                               "retrieved": jobs.retrieve_positions.clone(),
+                               "pivots": jobs.pivot_heads.tolist(), "slots": jobs.ref_slots.tolist(),
+                               "max_len": jobs.max_len.tolist(), "scores": scores,
+                               "ref_after": self.prefill_topk_set[layer_idx].clone()})
 
     def _drift_and_retrieve(self, layer_idx, jobs, query_states):
         S = self.decode_step
@@ -597,12 +690,11 @@ class HeteroCache(_CacheBase):
                         retrieve_positions=jobs.retrieve_positions, workspace=self._ws_score, err=self._err,
                         coeffs=jobs.coeffs, median=jobs.median, out_scores=scores)
         if self.record_checks:
-            self.check_log.append({"layer": layer_idx, "trigger": jobs.trigger.clone(),
-                                   "coeffs": jobs.coeffs.clone(), "median": jobs.median.clone(),
-                                   "retrieved": jobs.retrieve_positions.clone(),
-                                   "pivots": jobs.pivot_heads.tolist(), "slots": jobs.ref_slots.tolist(),
-                                   "max_len": jobs.max_len.tolist(), "scores": scores,
-                                   "ref_after": self.prefill_topk_set[layer_idx].clone()})
+            self._log_check(layer_idx, jobs, scores)
+        self._retrieve_layer(layer_idx, jobs)
+
+    def _retrieve_layer(self, layer_idx, jobs) -> None:
+        """The satellites' retrieval after the layer's drift check."""
         if jobs.member_job.numel() == 0:
             return
         full_k = self.key_cache_cpu[layer_idx]
@@ -660,6 +752,8 @@ class HeteroCache(_CacheBase):
         With a deferred append pending (update(..., {"defer_append": True})),
         the step's token is merged from its k/v and then appended to the pages
         on the side stream; the layer's next use waits for that append."""
+        if self._deferred and layer_idx in self._deferred:
+            self.flush_checks()
         self._wait_retrieval(layer_idx)
         self._wait_append(layer_idx)
         total = int(self._hlen[layer_idx].sum())

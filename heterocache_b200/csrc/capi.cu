@@ -4,6 +4,7 @@
 
 #include <cstdio>
 
+#include <algorithm>
 #include <atomic>
 
 #include "hc_params.cuh"
@@ -482,6 +483,99 @@ int hc_drift_check(int dtype, int num_kv_heads, int groups, int head_dim, int st
   p.out_scores = out_scores;
   p.err = err_flag;
   return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+int hc_drift_check_batch_per_launch(int dtype, int n_jobs, int steps, int seq_len, int groups,
+                                    int jobs_per_launch) {
+  if (!valid_dtype(dtype) || steps < 1 || steps > 7 || groups <= 0 || steps * groups > 256) return 0;
+  return hc::drift_batch_per_launch(dtype, n_jobs, seq_len, steps * groups, steps, jobs_per_launch);
+}
+
+size_t hc_drift_check_batch_workspace_size(int dtype, int n_jobs, int steps, int seq_len, int groups,
+                                           int jobs_per_launch) {
+  const int per = hc_drift_check_batch_per_launch(dtype, n_jobs, steps, seq_len, groups, jobs_per_launch);
+  if (per <= 0) return 0;
+  // the launches take `per` jobs, the last one the remainder
+  size_t ws = hc::score_workspace_size(dtype, per, seq_len, steps * groups, steps);
+  const int rem = n_jobs % per;
+  if (rem) ws = std::max(ws, hc::score_workspace_size(dtype, rem, seq_len, steps * groups, steps));
+  return ws;
+}
+
+int hc_drift_check_batch(int dtype, int num_kv_heads, int groups, int head_dim, int steps, int seq_len, int pooling,
+                         int kernel_size, int topk, double threshold, const hc_drift_job* jobs, int n_jobs,
+                         int jobs_per_launch, void* workspace, size_t workspace_bytes, int32_t* err_flag,
+                         void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (head_dim != HC_HEAD_DIM || num_kv_heads <= 0 || groups <= 0 || seq_len <= 0) return HC_ERR_INVALID;
+  if (n_jobs == 0) return HC_OK;
+  if (n_jobs < 0 || !jobs || steps < 1 || steps > 7) return steps > 7 ? HC_ERR_UNSUPPORTED : HC_ERR_INVALID;
+  if (topk < 0 || topk > seq_len) return HC_ERR_INVALID;
+  if (pooling != HC_AVGPOOL && pooling != HC_MAXPOOL) return HC_ERR_INVALID;
+  if (kernel_size < 1 || (kernel_size & 1) == 0 || kernel_size / 2 > 16) return HC_ERR_INVALID;
+  if (steps * groups > 256) return HC_ERR_UNSUPPORTED;
+  const int pages = (seq_len + HC_PAGE_SIZE - 1) / HC_PAGE_SIZE;
+  for (int j = 0; j < n_jobs; ++j) {
+    const hc_drift_job& d = jobs[j];
+    if (!aligned16(d.qbuf) || !aligned16(d.k_pool) || !d.block_table || d.n_pool_blocks <= 0) return HC_ERR_INVALID;
+    if (!stride_ok(dtype, d.qss) || !stride_ok(dtype, d.qsh)) return HC_ERR_INVALID;
+    if (pages > d.max_blocks || d.pivot_head < 0 || d.pivot_head >= num_kv_heads) return HC_ERR_INVALID;
+    if (d.max_len < 0 || d.max_len > seq_len || (d.max_len > 0 && !d.retrieve_positions)) return HC_ERR_INVALID;
+    if (!d.ref_bitmap || (topk > 0 && !d.ref_positions) || !d.trigger) return HC_ERR_INVALID;
+    for (int i = 0; i < j; ++i)
+      if (jobs[i].ref_bitmap == d.ref_bitmap) return HC_ERR_INVALID;
+  }
+  const int per = hc::drift_batch_per_launch(dtype, n_jobs, seq_len, steps * groups, steps, jobs_per_launch);
+  if (per <= 0) return HC_ERR_INVALID;
+  for (int j0 = 0; j0 < n_jobs; j0 += per) {
+    const int n = std::min(per, n_jobs - j0);
+    hc::DriftBatch b;
+    std::memset(&b, 0, sizeof(b));
+    b.n = n;
+    for (int i = 0; i < n; ++i) {
+      const hc_drift_job& d = jobs[j0 + i];
+      hc::DriftJob& o = b.job[i];
+      o.q = d.qbuf;
+      o.qst = d.qss;
+      o.qsh = d.qsh;
+      o.k_pool = d.k_pool;
+      o.bt = d.block_table;
+      o.n_blocks = d.n_pool_blocks;
+      o.max_blocks = d.max_blocks;
+      o.head = d.pivot_head;
+      o.max_len = d.max_len;
+      o.bitmap = d.ref_bitmap;
+      o.ref_pos = d.ref_positions;
+      o.trigger = d.trigger;
+      o.retr = d.retrieve_positions;
+      o.coeffs = d.coeffs;
+      o.median = d.median;
+      o.out_scores = d.out_scores;
+    }
+    hc::ScoreParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.mode = hc::MODE_DRIFT;
+    p.L = seq_len;
+    p.G = groups;
+    p.W = 1;
+    p.S = steps;
+    p.Rq = steps * groups;
+    p.pooling = pooling;
+    p.ksize = kernel_size;
+    p.halo = kernel_size / 2;
+    p.sqrt_d = div_sqrt_d(head_dim);
+    p.n_jobs = n;
+    p.KV = num_kv_heads;
+    p.nh = n;
+    p.nsel = steps + 1;
+    p.topk = topk;
+    p.bitmap_words = (seq_len + 31) / 32;
+    p.threshold = threshold;
+    p.err = err_flag;
+    const int rc = hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream, &b);
+    if (rc != HC_OK) return note_cuda(rc);
+  }
+  return HC_OK;
 }
 
 int hc_retrieve(int dtype, int num_kv_heads, int head_dim, int n_members, const int32_t* member_job,

@@ -55,6 +55,7 @@ struct ScoreParams {
   int tail;
   int64_t out_job_rows;
   void* out_scores;
+  int64_t out_job_stride;  // elements between jobs' score rows (set in the kernel)
   const int32_t* ref_slots;
   uint32_t* ref_bitmap;
   int32_t* ref_positions;
@@ -81,13 +82,47 @@ struct ScoreParams {
   unsigned int stall;  // injected grid-barrier arrival that never comes (tests of the timeout path)
 };
 
+// A batch of drift checks (hc_drift_check_batch): per job its own query
+// buffer, key pool, page table, reference set and outputs.  Passed to the
+// kernel by value (kernel parameter space), so a captured graph holds it.
+struct DriftJob {
+  const void* q;
+  int64_t qst, qsh;
+  const void* k_pool;
+  const int32_t* bt;
+  int n_blocks, max_blocks;
+  int head, max_len;
+  uint32_t* bitmap;   // reference bitmap row
+  int32_t* ref_pos;   // reference position row (topk entries)
+  int32_t* trigger;   // one entry
+  int32_t* retr;      // max_len entries
+  float* coeffs;      // S entries or null
+  double* median;     // one entry or null
+  void* out_scores;   // [S, L] pooled scores or null
+};
+constexpr int kDriftBatchMax = 16;
+struct DriftBatch {
+  int n;  // 0: a single hc_drift_check launch (job-indexed arrays of ScoreParams)
+  DriftJob job[kDriftBatchMax];
+};
+struct NoBatch {
+  int n;
+};
+
 // Process-wide limits of the device-side waits (hc_set_wait_limits): the
 // limit to use given a wait's default, and the injected stall (0 or 1).
 uint64_t wait_limit_ns(uint64_t dflt);
 unsigned int injected_stall();
 
 size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S);
-int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
+// Jobs per drift-check batch launch: `want` (or the default when <= 0),
+// capped at kDriftBatchMax and n_jobs, lowered until the plan's shared memory
+// fits.
+int drift_batch_per_launch(int dtype, int n_jobs, int L, int Rq, int S, int want);
+// batch: the jobs of one drift-check batch launch (MODE_DRIFT, p.n_jobs ==
+// batch->n), else null.
+int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st,
+                   const DriftBatch* batch = nullptr);
 
 // ---- paged flash-decode (decode_attn.cu)
 constexpr int kFThreads = 128;

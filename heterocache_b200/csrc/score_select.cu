@@ -39,6 +39,22 @@ namespace hc {
 
 
 
+// Kernel parameter carrying a drift-check batch (DRIFT mode only).
+template <int MODE>
+using BatchOf = typename std::conditional<MODE == MODE_DRIFT, DriftBatch, NoBatch>::type;
+
+// DRIFT mode: the job's result locations.
+struct DriftView {
+  uint32_t* bitmap;
+  int32_t* ref_pos;
+  int32_t* trigger;
+  int32_t* retr;
+  int retr_cap;
+  float* coeffs;
+  double* median;
+  int max_len;
+};
+
 struct JobInfo {
   int b, h, job, part, t0, t1;
   // DRIFT mode: page ids of the CTA's token range, staged in shared memory
@@ -61,7 +77,7 @@ __device__ __forceinline__ JobInfo job_info(const ScoreParams& p) {
     ji.h = p.first_head + ji.job % p.nh;
   } else {
     ji.b = 0;
-    ji.h = p.job_heads[ji.job];
+    ji.h = p.job_heads ? p.job_heads[ji.job] : 0;  // a batch sets it from the job
   }
   ji.t0 = ji.part * p.T;
   ji.t1 = min(p.L, ji.t0 + p.T);
@@ -172,7 +188,39 @@ __device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float 
 // has and spill; they go to shared memory instead, in per-lane order
 // (fragment word pair [nt][k-step][lane], so a warp's 8-byte loads are
 // conflict-free), filled once per CTA.
+// exp for the row sums: the same exp the probabilities use
+template <typename T>
+__device__ __forceinline__ float row_exp(float x) {
+  if constexpr (std::is_same<T, float>::value) return expf(x);
+  else return __expf(x);
+}
+
+// Running (max, sum of exp(x - max)) of one score row over the logits a
+// thread produces, two at a time: the sum is rescaled when the max grows.
+template <typename T>
+__device__ __forceinline__ void online_add2(float& m, float& sum, float x0, float x1) {
+  const float tm = fmaxf(x0, x1);
+  if (tm == -INFINITY) return;
+  if (tm > m) {
+    sum *= row_exp<T>(m - tm);  // 0 while m is still -inf
+    m = tm;
+  }
+  sum += row_exp<T>(x0 - m) + row_exp<T>(x1 - m);
+}
+// Merge of two such pairs (m2, s2) into (m, s).
+template <typename T>
+__device__ __forceinline__ void online_merge(float& m, float& sum, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  sum = (m == -INFINITY ? 0.f : sum * row_exp<T>(m - mn)) + (m2 == -INFINITY ? 0.f : s2 * row_exp<T>(m2 - mn));
+  m = mn;
+}
+
 constexpr int kMaxNT = 5;
+// the mma path's per-warp row sums sit in the upper part of each warp's
+// kMaxRq-entry row of wmax (its rows number at most 8 * kMaxNT)
+constexpr int kWarpSumOff = 128;
+static_assert(kWarpSumOff >= 8 * kMaxNT && kWarpSumOff + 8 * kMaxNT <= kMaxRq, "wmax layout");
 
 template <typename T, int NT, typename Pre>
 __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float* wmax, uint32_t* dummy,
@@ -209,9 +257,14 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   }
   pre();  // block-wide work that overlaps the query loads
   if constexpr (QS) __syncthreads();  // the fragments are in shared memory
-  float rmax[NT][2];
+  // per query row: running max and sum of exp over the CTA's own tokens
+  // (the row statistics need no second pass over the logits)
+  float rmax[NT][2], rsum[NT][2];
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) rmax[nt][0] = rmax[nt][1] = -INFINITY;
+  for (int nt = 0; nt < NT; ++nt) {
+    rmax[nt][0] = rmax[nt][1] = -INFINITY;
+    rsum[nt][0] = rsum[nt][1] = 0.f;
+  }
   const float r_sqrt = __frcp_rn(p.sqrt_d);
 
   const int lo = max(0, ji.t0 - kMargin);
@@ -280,8 +333,8 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
       for (int nt = 0; nt < NT; ++nt) {
         scale_logit2<T>(acc[nt][0], acc[nt][1], p.sqrt_d, r_sqrt);
         scale_logit2<T>(acc[nt][2], acc[nt][3], p.sqrt_d, r_sqrt);
-        rmax[nt][0] = fmaxf(rmax[nt][0], fmaxf(acc[nt][0], acc[nt][2]));
-        rmax[nt][1] = fmaxf(rmax[nt][1], fmaxf(acc[nt][1], acc[nt][3]));
+        online_add2<T>(rmax[nt][0], rsum[nt][0], acc[nt][0], acc[nt][2]);
+        online_add2<T>(rmax[nt][1], rsum[nt][1], acc[nt][1], acc[nt][3]);
         const uint32_t a = ((st_valid >> nt) & 1u) ? st_row[nt] + 2u * (uint32_t)tg : st_dummy;
         stmatrix2_trans(a, Elem<T>::pack2(acc[nt][0], acc[nt][1]), Elem<T>::pack2(acc[nt][2], acc[nt][3]));
       }
@@ -291,29 +344,37 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
     for (int nt = 0; nt < NT; ++nt) {
       scale_logit2<T>(acc[nt][0], acc[nt][1], p.sqrt_d, r_sqrt);
       scale_logit2<T>(acc[nt][2], acc[nt][3], p.sqrt_d, r_sqrt);
+      float own[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int qi = nt * 8 + 2 * tig + (e & 1);
         const int t = tg + gid + ((e >> 1) << 3);
+        own[e] = -INFINITY;
         if (qi >= p.Rq || t >= hi) continue;
         float x = acc[nt][e];
         if (masked(p, qi, t)) x = -INFINITY;
         lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::pack(x);
-        if (t >= ji.t0 && t < ji.t1) rmax[nt][e & 1] = fmaxf(rmax[nt][e & 1], x);
+        if (t >= ji.t0 && t < ji.t1) own[e] = x;
       }
+      online_add2<T>(rmax[nt][0], rsum[nt][0], own[0], own[2]);
+      online_add2<T>(rmax[nt][1], rsum[nt][1], own[1], own[3]);
     }
   }
-  // reduce the running maxima over the 8 lanes sharing tig, then publish
+  // merge the running pairs over the 8 lanes sharing tig, then publish:
+  // wmax[warp][qi] the warp's row max, wmax[warp][kWarpSumOff + qi] its sum
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
-      float m = rmax[nt][c];
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 8));
-      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+      float m = rmax[nt][c], sm = rsum[nt][c];
+#pragma unroll
+      for (int o = 4; o <= 16; o <<= 1)
+        online_merge<T>(m, sm, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, sm, o));
       const int qi = nt * 8 + 2 * tig + c;
-      if (gid == 0 && qi < p.Rq) wmax[warp * kMaxRq + qi] = m;
+      if (gid == 0 && qi < p.Rq) {
+        wmax[warp * kMaxRq + qi] = m;
+        wmax[warp * kMaxRq + kWarpSumOff + qi] = sm;
+      }
     }
   }
 }
@@ -698,13 +759,6 @@ __device__ __forceinline__ float softmax_prob(float x, float M, float S, float R
   else return __expf(x - M) * R;
 }
 
-// exp for the row sums: the same exp the probabilities use
-template <typename T>
-__device__ __forceinline__ float row_exp(float x) {
-  if constexpr (std::is_same<T, float>::value) return expf(x);
-  else return __expf(x);
-}
-
 // Eight consecutive elements (16-byte aligned for 16-bit types, 32-byte for
 // fp32) as fp32.
 template <typename T>
@@ -844,7 +898,7 @@ __device__ void pooled_keys8(const ScoreParams& p, const JobInfo& ji, const T* l
       if (on) {
         keys[s * p.T + (c - ji.t0) + o] = key;
         if (valid && p.out_scores)
-          reinterpret_cast<T*>(p.out_scores)[((size_t)ji.job * p.S + s) * p.L + c + o] = Elem<T>::pack(v);
+          reinterpret_cast<T*>(p.out_scores)[(size_t)ji.job * p.out_job_stride + (size_t)s * p.L + c + o] = Elem<T>::pack(v);
       }
       hist_add_warp(lhist, valid, ((unsigned int)s << 8) | (key >> (KB - 8)));
     }
@@ -886,7 +940,7 @@ __device__ void pooled_keys_wide(const ScoreParams& p, const JobInfo& ji, const 
       keys[s * p.T + (t - ji.t0)] = key;
       if (p.out_scores) {
         T* os = reinterpret_cast<T*>(p.out_scores);
-        os[((size_t)ji.job * p.S + s) * p.L + t] = Elem<T>::from_f(best);
+        os[(size_t)ji.job * p.out_job_stride + (size_t)s * p.L + t] = Elem<T>::from_f(best);
       }
     }
     if (on && !valid) keys[s * p.T + (t - ji.t0)] = 0u;
@@ -939,7 +993,8 @@ __device__ __forceinline__ int find_bin(const unsigned int* h, unsigned int rem,
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kSThreads, 1)
     score_select_kernel(const ScoreParams pin, const __grid_constant__ CUtensorMap tm_rows,
-                        const __grid_constant__ CUtensorMap tm_edge) {
+                        const __grid_constant__ CUtensorMap tm_edge,
+                        const __grid_constant__ BatchOf<MODE> batch) {
   ScoreParams p = pin;
   p.mode = MODE;
   if constexpr (MODE != MODE_PREFILL) p.W = 1;
@@ -963,6 +1018,54 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // query fragments of the tensor-core logits for more than 16 query rows
   __shared__ uint2 s_qfrag[std::is_same<T, float>::value ? 1 : kMaxNT * 8 * 32];
   JobInfo ji = job_info(p);
+  p.out_job_stride = (int64_t)p.S * p.L;
+  // DRIFT, batch: the job's query buffer, pool, page table and score output
+  // replace the launch-wide ones
+  if constexpr (MODE == MODE_DRIFT) {
+    if (batch.n > 0) {
+      const DriftJob& d = batch.job[ji.job];
+      p.out_scores = d.out_scores;
+      p.out_job_stride = 0;
+      ji.h = d.head;
+      p.q = d.q;
+      p.qst = d.qst;
+      p.qsh = d.qsh;
+      p.k_pool = d.k_pool;
+      p.bt = d.bt;
+      p.n_blocks = d.n_blocks;
+      p.max_blocks = d.max_blocks;
+    }
+  }
+  // DRIFT: where this job's results go -- rows of the job-indexed arrays of
+  // one hc_drift_check launch, or the job's own descriptor in a batch
+  // (formed where used: parameter-space and cached loads, no live registers)
+  auto drift_view = [&]() {
+    DriftView dv{};
+    if constexpr (MODE == MODE_DRIFT) {
+      if (batch.n > 0) {
+        const DriftJob& d = batch.job[ji.job];
+        dv.bitmap = d.bitmap;
+        dv.ref_pos = d.ref_pos;
+        dv.trigger = d.trigger;
+        dv.retr = d.retr;
+        dv.retr_cap = d.max_len;
+        dv.coeffs = d.coeffs;
+        dv.median = d.median;
+        dv.max_len = d.max_len;
+      } else {
+        const int slot = p.ref_slots[ji.job];
+        dv.bitmap = p.ref_bitmap + (size_t)slot * p.bitmap_words;
+        dv.ref_pos = p.ref_positions + (size_t)slot * p.topk;
+        dv.trigger = p.trigger + ji.job;
+        dv.retr = p.retrieve_positions + (size_t)ji.job * p.max_len_cap;
+        dv.retr_cap = p.max_len_cap;
+        dv.coeffs = p.coeffs ? p.coeffs + (size_t)ji.job * p.S : nullptr;
+        dv.median = p.median ? p.median + ji.job : nullptr;
+        dv.max_len = p.max_len[ji.job];
+      }
+    }
+    return dv;
+  };
   const int nblocks = gridDim.x;
   unsigned int epoch = 0;
 
@@ -1018,7 +1121,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
   if (p.mode == MODE_DRIFT) {
     // the reference bitmap is only rewritten after the last grid barrier
     if (threadIdx.x < kMaxRows) s_ov[threadIdx.x] = 0u;
-    const uint32_t* bm = p.ref_bitmap + (size_t)p.ref_slots[ji.job] * p.bitmap_words;
+    const uint32_t* bm = drift_view().bitmap;
     const int wbeg = ji.t0 >> 5, nwords = ((ji.t1 + 31) >> 5) - wbeg;
     if (nwords <= kRefWords)
       for (int w = threadIdx.x; w < nwords; w += kSThreads) s_refw[w] = bm[wbeg + w];
@@ -1061,6 +1164,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     float* sk = sq + p.Rq * kD;
     logits_fma<T>(p, ji, lg, wmax, sq, sk);
   }
+  const bool online_sums = used_mma && !used_umma;  // logits_mma also summed exp
   __syncthreads();
   if (umma_regmax) {
     for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
@@ -1086,6 +1190,16 @@ __global__ void __launch_bounds__(kSThreads, 1)
       float m = -INFINITY;
       for (int w = 0; w < kSWarps; ++w) m = fmaxf(m, wmax[w * kMaxRq + qi]);
       s_rowM[qi] = m;
+      if (online_sums) {
+        // the mma.sync path brought each warp's row sum along: rescale the
+        // warps' sums to the CTA's max, in warp order
+        float sum = 0.f;
+        for (int w = 0; w < kSWarps; ++w) {
+          const float mw = wmax[w * kMaxRq + qi];
+          if (mw != -INFINITY) sum += wmax[w * kMaxRq + kWarpSumOff + qi] * row_exp<T>(mw - m);
+        }
+        p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(m, sum);
+      }
     }
   }
   __syncthreads();
@@ -1094,7 +1208,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // row's tokens are split into nch chunks so that every warp has work, and
   // the chunk sums of a row are added in a fixed order (the per-warp maxima
   // in wmax were consumed above, so it holds the chunk sums)
-  {
+  if (!online_sums) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int base = ji.t0 - kMargin;
     auto exp_sum = [&](int qi, float m, int tb, int te) {
@@ -1240,7 +1354,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     if (p.mode == MODE_PREFILL) { k = p.keep_lens ? p.keep_lens[ji.h] : p.keep_const; row = 0; }
     else if (p.mode == MODE_PIVOT) { k = p.topk; row = 0; }
     else if (sel < p.S) { k = p.topk; row = sel; }
-    else { k = p.max_len[ji.job]; row = p.S - 1; }
+    else { k = drift_view().max_len; row = p.S - 1; }
     s_sel_row[sel] = row;
     s_k[sel] = (unsigned int)max(k, 0);
     s_prefix[sel] = 0u;
@@ -1578,8 +1692,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
     });
   } else {
     // drift: overlap of each step's top-k with the reference bitmap
-    const int slot = p.ref_slots[ji.job];
-    uint32_t* bm = p.ref_bitmap + (size_t)slot * p.bitmap_words;
+    uint32_t* bm = drift_view().bitmap;
     // this CTA's words of the reference bitmap were staged at kernel start
     const int wbeg = ji.t0 >> 5, nwords = ((ji.t1 + 31) >> 5) - wbeg;
     const bool staged = nwords <= kRefWords;
@@ -1597,9 +1710,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
     // retrieval list: last step's top-max_len, ascending
     {
       const int sel = p.S;
-      const int kk = min((int)s_k[sel], p.max_len_cap);
+      const DriftView dv = drift_view();
+      const int kk = min((int)s_k[sel], dv.retr_cap);
       rank_pass(sel, [&](int t, int rank, int) {
-        if (rank >= 0 && rank < kk) p.retrieve_positions[(size_t)ji.job * p.max_len_cap + rank] = t;
+        if (rank >= 0 && rank < kk) dv.retr[rank] = t;
       });
     }
     __syncthreads();
@@ -1623,18 +1737,20 @@ __global__ void __launch_bounds__(kSThreads, 1)
       const int trig = med < p.threshold;
       s_trigger = trig;
       if (ji.part == 0) {
-        p.trigger[ji.job] = trig;
-        if (p.coeffs) for (int s = 0; s < p.S; ++s) p.coeffs[ji.job * p.S + s] = c[s];
-        if (p.median) p.median[ji.job] = med;
+        const DriftView dv = drift_view();
+        *dv.trigger = trig;
+        if (dv.coeffs) for (int s = 0; s < p.S; ++s) dv.coeffs[s] = c[s];
+        if (dv.median) *dv.median = med;
       }
     }
     __syncthreads();
     if (s_trigger) {
       const int sel = p.S - 1;
       const int kk = (int)s_k[sel];
+      int32_t* ref_pos = drift_view().ref_pos;
       rank_pass(sel, [&](int t, int rank, int c) {
         const bool on = rank >= 0 && rank < kk;
-        if (on) p.ref_positions[(size_t)slot * p.topk + rank] = t;
+        if (on) ref_pos[rank] = t;
         const unsigned int bits = __ballot_sync(0xffffffffu, on);
         if (lane == 0) bm[(ji.t0 + c) >> 5] = bits;
       });
@@ -1755,7 +1871,7 @@ static ScoreWs score_ws_layout(int n_jobs, const ScorePlan& pl, int Rq, int L) {
 
 template <typename T, int MODE>
 static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, const CUtensorMap* maps, void* ws,
-                             size_t ws_bytes, cudaStream_t st) {
+                             size_t ws_bytes, cudaStream_t st, const DriftBatch* batch) {
   ScoreWs w = score_ws_layout(p.n_jobs, pl, p.Rq, p.L);
   if (!ws || ws_bytes < w.total) return HC_ERR_WORKSPACE;
   unsigned char* base = reinterpret_cast<unsigned char*>(ws);
@@ -1817,17 +1933,24 @@ static int launch_score_mode(ScoreParams& p, const ScorePlan& pl, const CUtensor
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1]) != cudaSuccess) return HC_ERR_CUDA;
+  BatchOf<MODE> bp;
+  if constexpr (MODE == MODE_DRIFT) {
+    if (batch) bp = *batch;
+    else bp.n = 0;
+  } else {
+    bp.n = 0;
+  }
+  if (cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1], bp) != cudaSuccess) return HC_ERR_CUDA;
   return HC_OK;
 }
 
 template <typename T>
 static int launch_score(ScoreParams& p, const ScorePlan& pl, const CUtensorMap* maps, void* ws, size_t ws_bytes,
-                        cudaStream_t st) {
+                        cudaStream_t st, const DriftBatch* batch) {
   switch (p.mode) {
-    case MODE_PREFILL: return launch_score_mode<T, MODE_PREFILL>(p, pl, maps, ws, ws_bytes, st);
-    case MODE_PIVOT: return launch_score_mode<T, MODE_PIVOT>(p, pl, maps, ws, ws_bytes, st);
-    case MODE_DRIFT: return launch_score_mode<T, MODE_DRIFT>(p, pl, maps, ws, ws_bytes, st);
+    case MODE_PREFILL: return launch_score_mode<T, MODE_PREFILL>(p, pl, maps, ws, ws_bytes, st, nullptr);
+    case MODE_PIVOT: return launch_score_mode<T, MODE_PIVOT>(p, pl, maps, ws, ws_bytes, st, nullptr);
+    case MODE_DRIFT: return launch_score_mode<T, MODE_DRIFT>(p, pl, maps, ws, ws_bytes, st, batch);
     default: return HC_ERR_INVALID;
   }
 }
@@ -1847,15 +1970,17 @@ static bool key_tensor_maps(const ScoreParams& p, int dtype, CUtensorMap* maps) 
 }
 
 template <typename T>
-static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st, const DriftBatch* batch) {
   constexpr bool f32 = std::is_same<T, float>::value;
   const int dtype = f32 ? HC_F32 : std::is_same<T, __half>::value ? HC_F16 : HC_BF16;
   CUtensorMap maps[2];
   std::memset(maps, 0, sizeof(maps));
-  const bool umma = !f32 && key_tensor_maps(p, dtype, maps);
+  // a batch's jobs read different pools: the CUDA-core/mma.sync paths (its
+  // query rows, steps x groups <= 40, never take the tensor-map path anyway)
+  const bool umma = !f32 && !batch && key_tensor_maps(p, dtype, maps);
   // one 512-thread CTA per SM
   ScorePlan pl = plan_score(dtype, p.n_jobs, p.L, p.Rq, p.S, 1, umma);
-  return launch_score<T>(p, pl, maps, ws, ws_bytes, st);
+  return launch_score<T>(p, pl, maps, ws, ws_bytes, st, batch);
 }
 
 // Large enough for either plan (whether the keys' tensor maps can be made is
@@ -1866,11 +1991,24 @@ size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S) {
   return max(score_ws_layout(n_jobs, a, Rq, L).total, score_ws_layout(n_jobs, b, Rq, L).total);
 }
 
-int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st) {
+// Drift checks per batch launch when the caller does not say.
+constexpr int kDriftBatchDefault = 8;
+
+int drift_batch_per_launch(int dtype, int n_jobs, int L, int Rq, int S, int want) {
+  if (n_jobs <= 0 || L <= 0 || Rq <= 0 || S <= 0) return 0;
+  int per = want > 0 ? want : kDriftBatchDefault;
+  per = min(min(per, kDriftBatchMax), n_jobs);
+  while (per > 1 && plan_score(dtype, per, L, Rq, S, 1, false).smem > kDynSmemCap) --per;
+  return per;
+}
+
+int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st, const DriftBatch* batch) {
+  if (batch && (p.mode != MODE_DRIFT || batch->n != p.n_jobs || batch->n < 1 || batch->n > kDriftBatchMax))
+    return HC_ERR_INVALID;
   switch (dtype) {
-    case HC_F32: return run_score<float>(p, ws, ws_bytes, st);
-    case HC_BF16: return run_score<__nv_bfloat16>(p, ws, ws_bytes, st);
-    case HC_F16: return run_score<__half>(p, ws, ws_bytes, st);
+    case HC_F32: return run_score<float>(p, ws, ws_bytes, st, batch);
+    case HC_BF16: return run_score<__nv_bfloat16>(p, ws, ws_bytes, st, batch);
+    case HC_F16: return run_score<__half>(p, ws, ws_bytes, st, batch);
     default: return HC_ERR_DTYPE;
   }
 }

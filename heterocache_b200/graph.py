@@ -13,7 +13,9 @@ graph joins it at the end of the step).
 
 Order per layer follows the patched attention: Llama runs ``decode_select``
 after attention (heterocache/llama_model.py:382-391), Qwen2 before it
-(heterocache/qwen_model.py:178-201).
+(heterocache/qwen_model.py:178-201).  In the Llama order a due drift check
+is put off to the end of the step, where every layer's check runs in one
+batch (``HeteroCache.flush_checks``) before the retrievals.
 
 Inputs and outputs are static device buffers owned by the graph object:
 ``q`` [layers, bsz, H, 1, D], ``k``/``v`` [layers, bsz, KV, 1, D] and ``out``
@@ -54,6 +56,8 @@ class DecodeStepGraph:
         cache.join_retrievals()  # no capture may wait on work recorded outside it
         S = cache.decode_step
         self.graphs: List[torch.cuda.CUDAGraph] = []
+        # this library's kernel launches held by each phase's graph
+        self.launches_per_phase: List[int] = []
         start = cache._qcount[self.layers[0]]
         torch.cuda.synchronize(dev)
         for phase in range(S):
@@ -61,8 +65,10 @@ class DecodeStepGraph:
             for l in self.layers:
                 cache._qcount[l] = phase
             g = torch.cuda.CUDAGraph()
+            n0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
                 self._eager_step()
+            self.launches_per_phase.append(ops.LAUNCHES[0] - n0)
             cache._restore_host_state(saved)
             self.graphs.append(g)
         for l in self.layers:
@@ -76,8 +82,8 @@ class DecodeStepGraph:
                 c.decode_select(self.q[i], l)
             c.attention(self.q[i], l, out=self.out[i])
             if self.order == "llama":
-                c.decode_select(self.q[i], l)
-        c.join_retrievals()
+                c.decode_select(self.q[i], l, defer=True)
+        c.join_retrievals()  # runs the put-off drift checks as one batch first
 
     def step(self) -> torch.Tensor:
         """Replay one decode step (inputs already in ``self.q/k/v``)."""

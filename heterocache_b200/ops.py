@@ -11,7 +11,7 @@ from typing import Optional
 
 import torch
 
-from ._lib import check, lib
+from ._lib import DriftJob, check, lib
 
 DTYPES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 POOLING = {"avgpool": 0, "maxpool": 1}
@@ -323,6 +323,60 @@ def _tier_base(full: torch.Tensor, first_head: int) -> int:
     head `first_head` (a tier of the satellites only): they read head h at
     base + h * head_stride, so only heads >= first_head are ever addressed."""
     return full.data_ptr() - first_head * full.stride(1) * full.element_size()
+
+
+def drift_job(qbuf, k_pool, block_table, *, pivot_head, max_len, ref_bitmap, ref_positions, trigger,
+              retrieve_positions, coeffs=None, median=None, out_scores=None) -> DriftJob:
+    """One check of a drift-check batch: a pivot's query buffer qbuf [S, H, D],
+    its layer's key pool and page table, its reference bitmap row and
+    reference position row, and its output slots (trigger: one int32,
+    retrieve_positions: max_len int32, coeffs: S floats, median: one double,
+    out_scores: [S, seq_len] pooled scores in qbuf's dtype).  The tensors must
+    stay alive, unmoved, while the batch is in use."""
+    _cuda(qbuf, k_pool, block_table, ref_bitmap, ref_positions, trigger, retrieve_positions, coeffs, median,
+          out_scores)
+    _need(out_scores is None or (out_scores.dtype == qbuf.dtype and out_scores.is_contiguous()),
+          "out_scores must be contiguous, in qbuf's dtype")
+    _rows(qbuf, "qbuf")
+    _need(qbuf.dim() == 3, "qbuf needs [steps, num_kv_heads * groups, D]")
+    _i32(block_table, "block_table")
+    _need(ref_bitmap.dtype == torch.int32 and ref_bitmap.is_contiguous(), "ref_bitmap must be contiguous 32-bit words")
+    for t, name in ((ref_positions, "ref_positions"), (trigger, "trigger"), (retrieve_positions, "retrieve_positions")):
+        _i32(t, name)
+    _need(trigger.numel() >= 1 and retrieve_positions.numel() >= max_len, "retrieve_positions needs max_len entries")
+    _need(coeffs is None or (coeffs.dtype == torch.float32 and coeffs.is_contiguous()), "coeffs must be float32")
+    _need(median is None or (median.dtype == torch.float64 and median.numel() >= 1), "median must be float64")
+    return DriftJob(_ptr(qbuf), qbuf.stride(0), qbuf.stride(1), _ptr(k_pool), _ptr(block_table), k_pool.shape[0],
+                    block_table.shape[1], int(pivot_head), int(max_len), _ptr(ref_bitmap), _ptr(ref_positions),
+                    _ptr(trigger), _ptr(retrieve_positions), _ptr(coeffs), _ptr(median), _ptr(out_scores))
+
+
+def drift_jobs_array(jobs) -> "ctypes.Array":
+    """A ctypes array of drift_job descriptors, for drift_check_batch."""
+    import ctypes
+    return (DriftJob * len(jobs))(*jobs)
+
+
+def drift_check_batch(jobs, *, dtype, device, num_kv_heads, groups, steps, seq_len, pooling, kernel_size, topk,
+                      threshold, workspace: Workspace, err, jobs_per_launch: int = 0, stream=None):
+    """hc_drift_check_batch: every job's drift check (the computation of
+    drift_check, per job) in ceil(n / per-launch) launches.  ``jobs``: a
+    drift_jobs_array; the check lengths and outputs are the jobs' own."""
+    n = len(jobs)
+    if n == 0:
+        return
+    _cuda(err)
+    dt = DTYPES[dtype]
+    nbytes = lib().hc_drift_check_batch_workspace_size(dt, n, steps, seq_len, groups, int(jobs_per_launch))
+    _need(nbytes > 0, "drift_check_batch: invalid sizes")
+    per = lib().hc_drift_check_batch_per_launch(dt, n, steps, seq_len, groups, int(jobs_per_launch))
+    ws = workspace.get(nbytes)
+    st = (stream if stream is not None else torch.cuda.current_stream(device)).cuda_stream
+    rc = lib().hc_drift_check_batch(dt, num_kv_heads, groups, HEAD_DIM, steps, seq_len, POOLING[pooling],
+                                    kernel_size, int(topk), float(threshold), jobs, n, int(jobs_per_launch),
+                                    _ptr(ws), ws.numel(), _ptr(err), st)
+    check("hc_drift_check_batch", rc)
+    LAUNCHES[0] += (n + per - 1) // per
 
 
 def retrieve(*, member_job, member_head, member_len, max_member_len, trigger, retrieve_positions, full_k, full_v,

@@ -296,6 +296,49 @@ int hc_drift_check(int dtype, int num_kv_heads, int groups, int head_dim, int st
                    void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Decode: a batch of drift checks in few launches.  Each job is the
+ * computation of hc_drift_check for one pivot, with its own query buffer,
+ * key pool, page table, reference set and outputs -- e.g. the checks of all
+ * layers that fall due in one decode step, which the reference runs one
+ * layer at a time (HeteroCache.decode_select, heterocache/cache_utils.py:
+ * 1007-1082).  dtype, geometry, steps, seq_len, pooling, kernel_size, topk
+ * and threshold are common to all jobs.
+ *   jobs: HOST array of n_jobs descriptors, read during the call (the
+ *   pointers in them are device memory).  The call launches
+ *   ceil(n_jobs / per_launch) kernels on `stream`, in job order, per_launch =
+ *   hc_drift_check_batch_per_launch(...).  Two jobs must not share a
+ *   reference bitmap row.  The workspace is reused by the launches in turn.
+ */
+#define HC_DRIFT_BATCH_MAX 16
+typedef struct hc_drift_job {
+  const void* qbuf;            /* [S, H, D] strided, 16-byte aligned */
+  int64_t qss, qsh;            /* element strides of qbuf's step and head dims */
+  const void* k_pool;          /* the job's key pool [n_pool_blocks, 256, D] */
+  const int32_t* block_table;  /* [num_kv_heads, max_blocks] */
+  int n_pool_blocks, max_blocks;
+  int pivot_head;              /* the KV head scored */
+  int max_len;                 /* retrieval list length (0..seq_len) */
+  uint32_t* ref_bitmap;        /* the pivot's reference bitmap: ceil(seq_len/32) words */
+  int32_t* ref_positions;      /* the pivot's reference set: topk int32 */
+  int32_t* trigger;            /* one int32 */
+  int32_t* retrieve_positions; /* max_len int32 (the last step's top-max_len, ascending) */
+  float* coeffs;               /* steps floats, or null */
+  double* median;              /* one double, or null */
+  void* out_scores;            /* [steps, seq_len] pooled scores (dtype), or null */
+} hc_drift_job;
+/* Jobs per launch: jobs_per_launch (1..HC_DRIFT_BATCH_MAX), or the
+ * library's choice when <= 0, lowered until a launch's shared memory fits;
+ * 0 for invalid sizes. */
+int hc_drift_check_batch_per_launch(int dtype, int n_jobs, int steps, int seq_len, int groups,
+                                    int jobs_per_launch);
+size_t hc_drift_check_batch_workspace_size(int dtype, int n_jobs, int steps, int seq_len, int groups,
+                                           int jobs_per_launch);
+int hc_drift_check_batch(int dtype, int num_kv_heads, int groups, int head_dim, int steps, int seq_len,
+                         int pooling, int kernel_size, int topk, double threshold,
+                         const hc_drift_job* jobs, int n_jobs, int jobs_per_launch,
+                         void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Decode: satellite retrieval.  Replaces the retrieval part of
  * HeteroCache.decode_select (heterocache/cache_utils.py:1084-1147) for batch
  * size 1.  For member m (job member_job[m], KV head member_head[m],

@@ -55,7 +55,7 @@ def test_graph_decode_matches_eager(cuda_device, order, geo):
                 eager.decode_select(q, l)
             eager.attention(q, l, out=out)
             if order == "llama":
-                eager.decode_select(q, l)
+                eager.decode_select(q, l, defer=True)  # as the graph: one batch at the step's end
             row.append(out)
         eager.join_retrievals()
         outs_e.append(torch.stack(row).clone())
@@ -81,3 +81,62 @@ def test_graph_decode_matches_eager(cuda_device, order, geo):
         assert torch.equal(graphed.value_pools[l], eager.value_pools[l])
         if len(eager.prefill_topk_set[l]):
             assert torch.equal(graphed.prefill_topk_set[l], eager.prefill_topk_set[l])
+
+
+@pytest.mark.parametrize("per_launch", [1, 0])
+def test_deferred_checks_match_per_layer_checks(cuda_device, per_launch):
+    """Llama order: drift checks put off to one batch (run by the next step's
+    first update, and by join_retrievals at the end) against each layer's
+    check run where it falls due.  One check per launch splits every check
+    over the SMs as a single check does: bit-identical results.  The default
+    batching splits each check over fewer CTAs, so its softmax sums are added
+    in another order (fp32 rounding): same triggers, attention outputs within
+    the bf16 tolerance, reference sets within a few boundary swaps."""
+    dev, geo = cuda_device, LLAMA_8B
+    layers, L, n_steps = 4, 3000, 11  # two checks per layer (decode_step 5)
+    per_layer, q_last = _cache(geo, layers, L, dev, threshold=0.9)
+    batched, _ = _cache(geo, layers, L, dev, threshold=0.9)
+    batched.drift_batch_per_launch = per_launch
+    gens = [DriftingDecode(geo, seed=90 + l, q0=q_last[l], dtype=torch.bfloat16) for l in range(layers)]
+    steps = [[tuple(t.to(dev) for t in g.step()) for g in gens] for _ in range(n_steps)]
+    H, D = geo.num_heads, geo.head_dim
+    outs = {}
+    for name, cache, defer in (("per_layer", per_layer, False), ("batched", batched, True)):
+        outs[name] = []
+        for s in range(n_steps):
+            row = []
+            for l in range(layers):
+                q, k, v = steps[s][l]
+                out = torch.empty(1, H, D, dtype=torch.bfloat16, device=dev)
+                cache.update(k, v, l, {"query_states": q, "defer_append": True})
+                cache.attention(q, l, out=out)
+                cache.decode_select(q, l, defer=defer)
+                row.append(out)
+            outs[name].append(torch.stack(row).clone())
+        cache.join_retrievals()
+    torch.cuda.synchronize()
+    per_layer.check_errors()
+    batched.check_errors()
+    assert not batched._deferred
+    for l in range(layers):
+        assert torch.equal(batched.heads_len[l], per_layer.heads_len[l])
+        assert torch.equal(batched.block_tables[l], per_layer.block_tables[l])
+        jb, jp = batched._jobs[l], per_layer._jobs[l]
+        if jp is not None:
+            assert torch.equal(jb.trigger, jp.trigger)
+    for s in range(n_steps):
+        if per_launch == 1:
+            assert torch.equal(outs["batched"][s], outs["per_layer"][s]), f"step {s}"
+        else:
+            err = (outs["batched"][s].float() - outs["per_layer"][s].float()).abs().max().item()
+            assert err <= 2e-2, (s, err)
+    for l in range(layers):
+        if not len(per_layer.prefill_topk_set[l]):
+            continue
+        a, b = batched.prefill_topk_set[l], per_layer.prefill_topk_set[l]
+        if per_launch == 1:
+            assert torch.equal(a, b)
+            assert torch.equal(batched.key_pools[l], per_layer.key_pools[l])
+        else:
+            for x, y in zip(a.reshape(-1, a.shape[-1]).tolist(), b.reshape(-1, b.shape[-1]).tolist()):
+                assert len(set(x) ^ set(y)) <= max(4, len(x) // 100), l

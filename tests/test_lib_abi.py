@@ -115,3 +115,51 @@ def test_ctypes_argument_lists_match_the_header_declarations():
         for i, (got, exp) in enumerate(zip(argtypes, want)):
             same = got is exp or {got, exp} <= {c_int64, c_longlong}
             assert same, (name, i, params[name][i], got, exp)
+
+
+def test_drift_job_struct_matches_the_header(tmp_path):
+    """The ctypes mirror of hc_drift_job has the C struct's size and field
+    offsets (gcc compiles the header and prints them)."""
+    import ctypes
+    fields = [f for f, _ in _lib.DriftJob._fields_]
+    prog = tmp_path / "layout.c"
+    prog.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"heterocache_b200.h\"\n"
+                    "int main(void) {\n  printf(\"%zu\\n\", sizeof(hc_drift_job));\n"
+                    + "".join(f"  printf(\"%zu\\n\", offsetof(hc_drift_job, {f}));\n" for f in fields)
+                    + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(prog), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert got[0] == ctypes.sizeof(_lib.DriftJob)
+    assert got[1:] == [getattr(_lib.DriftJob, f).offset for f in fields]
+
+
+def test_drift_batch_validation_needs_no_gpu(built):
+    """hc_drift_check_batch rejects bad sizes and descriptors on the host."""
+    lib = _lib.lib()
+    jobs = (_lib.DriftJob * 2)()
+    args = (0, 5, 10, 0.5)
+    # more than 7 steps: unsupported; no jobs: nothing to do
+    assert lib.hc_drift_check_batch(1, 8, 4, 128, 9, 1000, *args, jobs, 2, 0, None, 0, None, None) == 8
+    assert lib.hc_drift_check_batch(1, 8, 4, 128, 5, 1000, *args, jobs, 0, 0, None, 0, None, None) == 0
+    # null descriptors (no pool, no page table) and a misaligned query buffer
+    assert lib.hc_drift_check_batch(1, 8, 4, 128, 5, 1000, *args, jobs, 2, 0, None, 0, None, None) == 1
+    for j in jobs:
+        j.qbuf, j.k_pool, j.block_table, j.n_pool_blocks, j.max_blocks = 256, 512, 1024, 4, 4
+        j.pivot_head, j.max_len, j.trigger, j.retrieve_positions, j.ref_positions = 7, 10, 64, 128, 192
+    jobs[0].ref_bitmap, jobs[1].ref_bitmap = 4096, 8192
+    jobs[1].qbuf = 264
+    assert lib.hc_drift_check_batch(1, 8, 4, 128, 5, 1000, *args, jobs, 2, 0, None, 0, None, None) == 1
+    jobs[1].qbuf = 256
+    # a pivot head outside the layer, a retrieval longer than the context,
+    # a page table too short for the context, a shared reference bitmap
+    for field, bad in (("pivot_head", 8), ("max_len", 1001), ("max_blocks", 3), ("ref_bitmap", 4096)):
+        good = getattr(jobs[1], field)
+        setattr(jobs[1], field, bad)
+        assert lib.hc_drift_check_batch(1, 8, 4, 128, 5, 1000, *args, jobs, 2, 0, None, 0, None, None) == 1, field
+        setattr(jobs[1], field, good)
+    # jobs per launch: capped where a launch's shared memory runs out
+    assert lib.hc_drift_check_batch_per_launch(1, 32, 5, 131072, 4, 0) == 8
+    assert 1 < lib.hc_drift_check_batch_per_launch(1, 32, 5, 131072, 4, 16) < 16
+    assert lib.hc_drift_check_batch_per_launch(1, 3, 5, 4096, 4, 0) == 3
+    assert lib.hc_drift_check_batch_workspace_size(1, 32, 5, 131072, 4, 0) > 0
