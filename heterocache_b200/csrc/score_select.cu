@@ -222,9 +222,18 @@ constexpr int kMaxNT = 5;
 constexpr int kWarpSumOff = 128;
 static_assert(kWarpSumOff >= 8 * kMaxNT && kWarpSumOff + 8 * kMaxNT <= kMaxRq, "wmax layout");
 
-template <typename T, int NT, typename Pre>
+// Logits in global memory leave a warp through `stg` (kSWarps tiles of
+// kStgBytes, free shared memory during phase 1): stmatrix transposes a
+// tile's 16 tokens x 8*NT rows into rows of kStgRow bytes (16 bytes of padding
+// keep the eight row addresses of a matrix on distinct banks), then each row
+// goes out as two 16-byte stores.
+constexpr int kStgRow = 48;
+constexpr int kStgBytes = 8 * kMaxNT * kStgRow;
+
+// GLOBAL: the logits buffer is global memory (else shared memory).
+template <typename T, int NT, bool GLOBAL, typename Pre>
 __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float* wmax, uint32_t* dummy,
-                           uint2* s_qf, Pre&& pre) {
+                           uint2* s_qf, unsigned char* stg, Pre&& pre) {
   constexpr bool QS = NT > 2;  // query fragments in shared memory (s_qf: kMaxNT * 8 * 32 entries)
   static_assert(NT <= kMaxNT, "query tiles");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -257,8 +266,8 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   }
   pre();  // block-wide work that overlaps the query loads
   if constexpr (QS) __syncthreads();  // the fragments are in shared memory
-  // per query row: running max and sum of exp over the CTA's own tokens
-  // (the row statistics need no second pass over the logits)
+  // per query row: running max and, for logits in global memory, sum of exp
+  // over the CTA's own tokens (saving a second pass over the logits)
   float rmax[NT][2], rsum[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -276,7 +285,11 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
   // a scratch word.  Column offsets are multiples of 16 tokens (t0 is a
   // multiple of 32, lo = t0 - 16 or 0) and TB a multiple of 8, so every row
   // address is 16-byte aligned.
-  const bool fast_ok = p.logits_in_smem && p.W == 1;
+  const bool fast_ok = !GLOBAL && p.W == 1;
+  // global logits: staged stores (W == 1: no in-window mask)
+  const bool stage_ok = GLOBAL && p.W == 1 && stg != nullptr;
+  unsigned char* my_stg = stg ? stg + warp * kStgBytes : nullptr;
+  const uint32_t stg_row = stg ? smem_u32(my_stg) + (uint32_t)((lane & 7) * kStgRow + 16 * ((lane >> 3) & 1)) : 0u;
   uint32_t st_row[NT];
   unsigned int st_valid = 0u;
 #pragma unroll
@@ -328,16 +341,45 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
         mma16816<T>(acc[nt], ka[s].z, kb[s].z, ka[s].w, kb[s].w, b1.x, b1.y);
       }
     }
-    if (fast_ok && tg >= ji.t0 && tg + 16 <= ji.t1) {
+    if (!GLOBAL && fast_ok && tg >= ji.t0 && tg + 16 <= ji.t1) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         scale_logit2<T>(acc[nt][0], acc[nt][1], p.sqrt_d, r_sqrt);
         scale_logit2<T>(acc[nt][2], acc[nt][3], p.sqrt_d, r_sqrt);
-        online_add2<T>(rmax[nt][0], rsum[nt][0], acc[nt][0], acc[nt][2]);
-        online_add2<T>(rmax[nt][1], rsum[nt][1], acc[nt][1], acc[nt][3]);
+        // logits in shared memory: the exp sums come from a pass over them
+        rmax[nt][0] = fmaxf(rmax[nt][0], fmaxf(acc[nt][0], acc[nt][2]));
+        rmax[nt][1] = fmaxf(rmax[nt][1], fmaxf(acc[nt][1], acc[nt][3]));
         const uint32_t a = ((st_valid >> nt) & 1u) ? st_row[nt] + 2u * (uint32_t)tg : st_dummy;
         stmatrix2_trans(a, Elem<T>::pack2(acc[nt][0], acc[nt][1]), Elem<T>::pack2(acc[nt][2], acc[nt][3]));
       }
+      continue;
+    }
+    if (GLOBAL && stage_ok && tg + 16 <= hi) {
+      // tiles are wholly own tokens or wholly margin (t0, t1 and lo are
+      // multiples of 16 apart)
+      const bool own_tile = tg >= ji.t0 && tg + 16 <= ji.t1;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        scale_logit2<T>(acc[nt][0], acc[nt][1], p.sqrt_d, r_sqrt);
+        scale_logit2<T>(acc[nt][2], acc[nt][3], p.sqrt_d, r_sqrt);
+        if (own_tile) {
+          online_add2<T>(rmax[nt][0], rsum[nt][0], acc[nt][0], acc[nt][2]);
+          online_add2<T>(rmax[nt][1], rsum[nt][1], acc[nt][1], acc[nt][3]);
+        }
+        stmatrix2_trans(stg_row + (uint32_t)(nt * 8 * kStgRow), Elem<T>::pack2(acc[nt][0], acc[nt][1]),
+                        Elem<T>::pack2(acc[nt][2], acc[nt][3]));
+      }
+      __syncwarp();
+      T* dst = lg + (tg - base);
+#pragma unroll
+      for (int i0 = 0; i0 < NT * 16; i0 += 32) {
+        const int i = i0 + lane;
+        const int row = i >> 1, half = i & 1;
+        if (i < NT * 16 && row < p.Rq)
+          *reinterpret_cast<uint4*>(dst + (int64_t)row * p.TB + 8 * half) =
+              *reinterpret_cast<const uint4*>(my_stg + row * kStgRow + 16 * half);
+      }
+      __syncwarp();
       continue;
     }
 #pragma unroll
@@ -356,8 +398,13 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
         lg[(int64_t)qi * p.TB + (t - base)] = Elem<T>::pack(x);
         if (t >= ji.t0 && t < ji.t1) own[e] = x;
       }
-      online_add2<T>(rmax[nt][0], rsum[nt][0], own[0], own[2]);
-      online_add2<T>(rmax[nt][1], rsum[nt][1], own[1], own[3]);
+      if constexpr (GLOBAL) {
+        online_add2<T>(rmax[nt][0], rsum[nt][0], own[0], own[2]);
+        online_add2<T>(rmax[nt][1], rsum[nt][1], own[1], own[3]);
+      } else {
+        rmax[nt][0] = fmaxf(rmax[nt][0], fmaxf(own[0], own[2]));
+        rmax[nt][1] = fmaxf(rmax[nt][1], fmaxf(own[1], own[3]));
+      }
     }
   }
   // merge the running pairs over the 8 lanes sharing tig, then publish:
@@ -367,9 +414,14 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       float m = rmax[nt][c], sm = rsum[nt][c];
+      if constexpr (GLOBAL) {
 #pragma unroll
-      for (int o = 4; o <= 16; o <<= 1)
-        online_merge<T>(m, sm, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, sm, o));
+        for (int o = 4; o <= 16; o <<= 1)
+          online_merge<T>(m, sm, __shfl_xor_sync(0xffffffffu, m, o), __shfl_xor_sync(0xffffffffu, sm, o));
+      } else {
+#pragma unroll
+        for (int o = 4; o <= 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      }
       const int qi = nt * 8 + 2 * tig + c;
       if (gid == 0 && qi < p.Rq) {
         wmax[warp * kMaxRq + qi] = m;
@@ -1151,20 +1203,29 @@ __global__ void __launch_bounds__(kSThreads, 1)
   };
 
   // ---- phase 1, legacy paths: logits
+  // staging of global logits: the keys' array is free until the pooling pass
+  unsigned char* stg = (!p.logits_in_smem && (size_t)p.S * p.T * sizeof(unsigned int) >= (size_t)kSWarps * kStgBytes)
+                           ? reinterpret_cast<unsigned char*>(keys) : nullptr;
   if constexpr (kTensor) {
     if (used_umma) {
-    } else if (p.Rq <= 8) { logits_mma<T, 1>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
-    else if (p.Rq <= 16) { logits_mma<T, 2>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
-    else if (p.Rq <= 24) { logits_mma<T, 3>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
-    else if (p.Rq <= 32) { logits_mma<T, 4>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
-    else if (p.Rq <= 40) { logits_mma<T, 5>(p, ji, lg, wmax, s_dummy, s_qfrag, stage_pages); used_mma = true; }
+    } else if (p.Rq <= 8) { (p.logits_in_smem ? logits_mma<T, 1, false>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)
+                       : logits_mma<T, 1, true>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)); used_mma = true; }
+    else if (p.Rq <= 16) { (p.logits_in_smem ? logits_mma<T, 2, false>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)
+                       : logits_mma<T, 2, true>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)); used_mma = true; }
+    else if (p.Rq <= 24) { (p.logits_in_smem ? logits_mma<T, 3, false>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)
+                       : logits_mma<T, 3, true>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)); used_mma = true; }
+    else if (p.Rq <= 32) { (p.logits_in_smem ? logits_mma<T, 4, false>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)
+                       : logits_mma<T, 4, true>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)); used_mma = true; }
+    else if (p.Rq <= 40) { (p.logits_in_smem ? logits_mma<T, 5, false>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)
+                       : logits_mma<T, 5, true>(p, ji, lg, wmax, s_dummy, s_qfrag, stg, stage_pages)); used_mma = true; }
   }
   if (!used_mma) {
     stage_pages();
     float* sk = sq + p.Rq * kD;
     logits_fma<T>(p, ji, lg, wmax, sq, sk);
   }
-  const bool online_sums = used_mma && !used_umma;  // logits_mma also summed exp
+  // the logits pass also summed exp (mma.sync path, logits in global memory)
+  const bool online_sums = used_mma && !used_umma && !p.logits_in_smem;
   __syncthreads();
   if (umma_regmax) {
     for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
@@ -1975,8 +2036,9 @@ static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st,
   const int dtype = f32 ? HC_F32 : std::is_same<T, __half>::value ? HC_F16 : HC_BF16;
   CUtensorMap maps[2];
   std::memset(maps, 0, sizeof(maps));
-  // a batch's jobs read different pools: the CUDA-core/mma.sync paths (its
-  // query rows, steps x groups <= 40, never take the tensor-map path anyway)
+  // a batch's jobs read different pools, and its query rows (steps x groups
+  // <= 40) take the mma.sync path, which needs no tensor maps: measured on a
+  // batch of 8 checks at 128K, the tcgen05 path's logits took 3.4x as long
   const bool umma = !f32 && !batch && key_tensor_maps(p, dtype, maps);
   // one 512-thread CTA per SM
   ScorePlan pl = plan_score(dtype, p.n_jobs, p.L, p.Rq, p.S, 1, umma);
