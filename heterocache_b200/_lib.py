@@ -61,6 +61,9 @@ SIGNATURES = {
     "hc_drift_check_batch_workspace_size": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
     "hc_drift_check_batch": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_double,
                                      c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "hc_prefill_attention": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_int64,
+                                     c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64,
+                                     c_float, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "hc_retrieve": (c_int, [c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p,
                             c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
                             c_int, c_void_p, c_int, c_void_p, c_void_p]),

@@ -12,9 +12,10 @@ Same projections, RoPE and call order as the reference's patched classes
 
 Decode attention is ``HeteroCache.attention`` (the sm_100a split-K kernel) in
 place of ``flash_attn_with_kvcache``.  The prefill attention over the full
-prompt is not part of the compressed-KV path; it uses PyTorch's
-``scaled_dot_product_attention`` (causal, grouped-query) in place of the
-reference's flash-attn varlen call.
+prompt (the reference's flash-attn forward, llama_model.py:353-361,
+qwen_model.py:161-169) is ``ops.prefill_attention``, a causal grouped-query
+attention on the tcgen05 tensor cores, for 16-bit models; fp32 models use
+PyTorch's ``scaled_dot_product_attention``.
 
 ``patch_transformers()`` installs the classes the way the reference's loader
 does (heterocache/utils.py:195-197); call it before building the model.
@@ -26,6 +27,8 @@ from typing import Optional, Tuple
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
+
+from . import ops
 
 try:
     from transformers.models.llama.modeling_llama import apply_rotary_pos_emb
@@ -41,15 +44,23 @@ except Exception:  # pragma: no cover
 
 
 def _causal_attention(q, k, v, groups: int, scale: float) -> torch.Tensor:
-    """Causal attention over the uncompressed prompt.  K/V heads are expanded
-    to the query heads, so every SDPA backend (flash attention for long
-    prompts) can take it, not only those that accept grouped-query inputs."""
+    """Causal attention over the uncompressed prompt, [bsz, L, H, D] out.
+
+    16-bit CUDA inputs with head_dim 128 (the models of this path) run the
+    sm_100a kernel (``ops.prefill_attention``: tcgen05 tensor cores, TMA,
+    grouped-query without expanding K/V).  fp32 models take PyTorch's SDPA,
+    with K/V heads expanded to the query heads so every SDPA backend can take
+    it."""
+    if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and q.shape[-1] == ops.HEAD_DIM:
+        return ops.prefill_attention(q, k, v, scale=scale)
     if groups > 1 and q.shape[-2] > 1:
         k = k.repeat_interleave(groups, dim=1)
         v = v.repeat_interleave(groups, dim=1)
-        return F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale)
-    return F.scaled_dot_product_attention(q, k, v, is_causal=q.shape[-2] > 1, scale=scale,
-                                          enable_gqa=groups > 1)
+        out = F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=scale)
+    else:
+        out = F.scaled_dot_product_attention(q, k, v, is_causal=q.shape[-2] > 1, scale=scale,
+                                             enable_gqa=groups > 1)
+    return out.transpose(1, 2)
 
 
 class _HeteroAttention(nn.Module):
@@ -105,8 +116,7 @@ class _HeteroAttention(nn.Module):
                 cache.init_coefficient(q, k, self.layer_idx)
                 cache.prefill_select(q, k, v, self.layer_idx)
             out = _causal_attention(q, k, v, self.num_key_value_groups, self.scaling)
-            out = out.transpose(1, 2).reshape(bsz, q_len, -1).contiguous()
-            return self.o_proj(out), None
+            return self.o_proj(out.reshape(bsz, q_len, -1).contiguous()), None
         # the query rides along so the page-append launch also stores it for
         # the drift check; the append itself is deferred: attention merges the
         # new token from k/v and appends it on the side stream

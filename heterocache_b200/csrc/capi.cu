@@ -485,6 +485,37 @@ int hc_drift_check(int dtype, int num_kv_heads, int groups, int head_dim, int st
   return note_cuda(hc::score_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
 }
 
+int hc_prefill_attention(int dtype, int bsz, int num_heads, int num_kv_heads, int seq_len, int head_dim,
+                         const void* q, int64_t qsb, int64_t qsh, int64_t qst, const void* k, int64_t ksb,
+                         int64_t ksh, int64_t kst, const void* v, int64_t vsb, int64_t vsh, int64_t vst, float scale,
+                         void* out, int64_t osb, int64_t osh, int64_t ost, int32_t* err_flag, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (dtype == HC_F32) return HC_ERR_UNSUPPORTED;
+  if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_heads <= 0 || num_kv_heads <= 0 || seq_len < 0) return HC_ERR_INVALID;
+  if (num_heads % num_kv_heads != 0) return HC_ERR_INVALID;
+  if (seq_len == 0) return HC_OK;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return HC_ERR_INVALID;
+  const int64_t strides[] = {qsb, qsh, qst, ksb, ksh, kst, vsb, vsh, vst, osb, osh, ost};
+  for (int64_t x : strides)
+    if (x <= 0 || !stride_ok(dtype, x)) return HC_ERR_INVALID;
+  hc::PAParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.out = out;
+  p.osb = osb;
+  p.osh = osh;
+  p.ost = ost;
+  p.L = seq_len;
+  p.H = num_heads;
+  p.KV = num_kv_heads;
+  p.G = num_heads / num_kv_heads;
+  p.bsz = bsz;
+  const double sc = scale > 0.f ? (double)scale : 1.0 / std::sqrt((double)head_dim);
+  p.scale_log2 = (float)(sc * 1.4426950408889634);
+  p.err = err_flag;
+  return note_cuda(hc::prefill_attn_dispatch(dtype, p, q, qsb, qsh, qst, k, ksb, ksh, kst, v, vsb, vsh, vst,
+                                             (cudaStream_t)stream));
+}
+
 int hc_drift_check_batch_per_launch(int dtype, int n_jobs, int steps, int seq_len, int groups,
                                     int jobs_per_launch) {
   if (!valid_dtype(dtype) || steps < 1 || steps > 7 || groups <= 0 || steps * groups > 256) return 0;

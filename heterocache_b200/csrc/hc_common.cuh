@@ -58,6 +58,11 @@ template <> struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static uint32_t pack2(float a, float b) {
     return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
   }
+  // any two floats, rounded to nearest: a in the low half, b in the high half
+  __device__ __forceinline__ static uint32_t cvt2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
   __device__ __forceinline__ static uint32_t key(float x) {
     uint32_t b = __float_as_uint(x) >> 16;  // exact: x is a bf16 value
     return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
@@ -78,6 +83,7 @@ template <> struct Elem<__half> {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
   }
+  __device__ __forceinline__ static uint32_t cvt2(float a, float b) { return pack2(a, b); }  // rounds to nearest
   __device__ __forceinline__ static void rnd2(float& a, float& b) {
     const __half2 h = __floats2half2_rn(a, b);
     const float2 f = __half22float2(h);

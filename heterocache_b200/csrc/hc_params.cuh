@@ -160,6 +160,20 @@ size_t flash_decode_ws_bytes(int R, int G);
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
 int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_t* need_out);
 
+// ---- causal prefill attention (prefill_attn.cu)
+struct PAParams {
+  void* out;
+  int64_t osb, osh, ost;  // element strides of out [bsz, heads, L, D] (any order)
+  int L, H, KV, G, bsz;
+  int n_qt;               // 128-query tiles (set at dispatch)
+  float scale_log2;       // softmax scale times log2(e)
+  int32_t* err;
+  uint64_t wait_ns;       // mbarrier wait limit (set at dispatch)
+};
+int prefill_attn_dispatch(int dtype, PAParams& p, const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                          const void* k, int64_t ksb, int64_t ksh, int64_t kst, const void* v, int64_t vsb,
+                          int64_t vsh, int64_t vst, cudaStream_t st);
+
 // ---- page copies (kv_copy.cu)
 int prefill_keep_dispatch(int dtype, int bsz, int KV, int L, const int32_t* keep, int n_keep, const void* k,
                           const void* v, int64_t sb, int64_t sh, int64_t st, int64_t vsb, int64_t vsh, int64_t vst,

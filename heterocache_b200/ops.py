@@ -206,6 +206,33 @@ def pivot_init(q, k, *, first_pivot, n_pivots, groups, pooling, kernel_size, top
     LAUNCHES[0] += 1
 
 
+def prefill_attention(q, k, v, *, scale: float = 0.0, out=None, err=None):
+    """hc_prefill_attention: causal grouped-query attention of q [bsz, H, L, D]
+    over k, v [bsz, KV, L, D] (16-bit, strided, contiguous last dim) on the
+    tcgen05 tensor cores.  Returns out [bsz, L, H, D] (the layout the output
+    projection reads), or writes the given ``out`` of that shape."""
+    _cuda(q, k, v, out, err)
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _rows(t, name)
+    _same_shape(k, v)
+    _need(q.dtype in (torch.bfloat16, torch.float16) and k.dtype == q.dtype,
+          "prefill_attention takes bf16 or fp16 q, k, v of one dtype")
+    bsz, H, L, D = q.shape
+    _need(k.shape[0] == bsz and k.shape[2] == L and H % k.shape[1] == 0, "k/v need [bsz, KV, L, D], KV dividing H")
+    if out is None:
+        out = torch.empty(bsz, L, H, D, dtype=q.dtype, device=q.device)
+    _need(out.shape == (bsz, L, H, D) and out.dtype == q.dtype and out.stride(-1) == 1, "out needs [bsz, L, H, D]")
+    if err is None:
+        err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    rc = lib().hc_prefill_attention(dtype_code(q), bsz, H, k.shape[1], L, D, _ptr(q), q.stride(0), q.stride(1),
+                                    q.stride(2), _ptr(k), k.stride(0), k.stride(1), k.stride(2), _ptr(v),
+                                    v.stride(0), v.stride(1), v.stride(2), float(scale), _ptr(out), out.stride(0),
+                                    out.stride(2), out.stride(1), _ptr(err), _stream(q))
+    check("hc_prefill_attention", rc)
+    LAUNCHES[0] += 1
+    return out
+
+
 def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, free_ptr, err, q=None, q_stage=None):
     """Append one token per row; with ``q`` [1, H, 1, D] and ``q_stage`` [H, D]
     the same launch stores the step's query for the drift check."""

@@ -339,6 +339,26 @@ int hc_drift_check_batch(int dtype, int num_kv_heads, int groups, int head_dim, 
                          void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Prefill: causal attention over the uncompressed prompt.  Replaces the
+ * flash-attn forward of the patched attention's prefill branch
+ * (heterocache/llama_model.py:353-361, heterocache/qwen_model.py:161-169):
+ *   out[b, h, t, :] = sum_{j <= t} softmax_j(q[b,h,t] . k[b,h/G,j] * scale) v[b,h/G,j]
+ * with G = num_heads / num_kv_heads (grouped-query), fp32 accumulation,
+ * output in the input dtype.  16-bit dtypes only (HC_ERR_UNSUPPORTED for
+ * fp32).  scale <= 0 selects 1/sqrt(D).
+ *   q: [bsz, num_heads, seq_len, D] strided (qsb, qsh, qst); k, v:
+ *   [bsz, num_kv_heads, seq_len, D] strided; out: strided (osb, osh, ost) --
+ *   e.g. [bsz, seq_len, num_heads, D] for the o_proj input.  All strides
+ *   positive multiples of 16 bytes, pointers 16-byte aligned.
+ */
+int hc_prefill_attention(int dtype, int bsz, int num_heads, int num_kv_heads, int seq_len, int head_dim,
+                         const void* q, int64_t qsb, int64_t qsh, int64_t qst,
+                         const void* k, int64_t ksb, int64_t ksh, int64_t kst,
+                         const void* v, int64_t vsb, int64_t vsh, int64_t vst,
+                         float scale, void* out, int64_t osb, int64_t osh, int64_t ost,
+                         int32_t* err_flag, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Decode: satellite retrieval.  Replaces the retrieval part of
  * HeteroCache.decode_select (heterocache/cache_utils.py:1084-1147) for batch
  * size 1.  For member m (job member_job[m], KV head member_head[m],

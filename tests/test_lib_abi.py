@@ -77,6 +77,14 @@ def test_argument_validation_needs_no_gpu(built):
     # misaligned staging area
     assert lib.hc_retrieve_delta(1, 8, 128, 1, None, None, None, None, None, 1, None, None, 1, None, 1, None, None,
                                  0, 0, None, None, 1, None, 1, 8, None, None, 1, None, None) == 1
+    # prefill attention: 16-bit only, head_dim 128, KV heads dividing the
+    # query heads, aligned pointers; an empty prompt is not an error
+    pa = (None, 8, 8, 8, None, 8, 8, 8, None, 8, 8, 8, 0.0, None, 8, 8, 8, None, None)
+    assert lib.hc_prefill_attention(0, 1, 8, 8, 16, 128, *pa) == 8
+    assert lib.hc_prefill_attention(1, 1, 8, 8, 16, 64, *pa) == 1
+    assert lib.hc_prefill_attention(1, 1, 8, 3, 16, 128, *pa) == 1
+    assert lib.hc_prefill_attention(1, 1, 8, 8, 0, 128, *pa) == 0
+    assert lib.hc_prefill_attention(1, 1, 8, 8, 16, 128, 8, 8, 8, 8, *pa[4:]) == 1
     # workspace sizes are pure host arithmetic
     assert lib.hc_prefill_select_workspace_size(1, 1, 5, 32768, 4, 1) > 0
     assert lib.hc_flash_decode_workspace_size(1, 8, 4, 128) > 0
