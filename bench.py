@@ -189,9 +189,17 @@ def time_prefill_kernels(cache, q, k, v, layer, reps=5):
         # same keys: 128 query rows per KV head on the tensor cores
         calls["prefill_select_w32"] = (select_w32, nc * L * D * 2 + int(keep.sum().item()) * D * 2 * 2 * 2
                                        + nc * 32 * cache.num_key_value_groups * D * 2)
+    # the causal prompt attention over the uncompressed prompt (the patched
+    # classes' prefill attention), and PyTorch's SDPA on the same inputs for
+    # context (K/V expanded to the query heads, as SDPA needs)
+    att_out = torch.empty(1, L, H, D, dtype=q.dtype, device=dev)
+
+    def attention():
+        ops.prefill_attention(q, k, v, scale=1.0 / math.sqrt(D), out=att_out, err=cache._err)
+    calls["prefill_attention"] = (attention, (q.numel() + k.numel() + v.numel() + att_out.numel()) * 2)
     # the window-32 selection rewrites the compressed heads' pages with its own
     # kept rows: time it before the HeteroCache selection, which restores them
-    order = [n for n in ("pivot_init", "prefill_select_w32", "prefill_select") if n in calls]
+    order = [n for n in ("pivot_init", "prefill_select_w32", "prefill_select", "prefill_attention") if n in calls]
     for name, (fn, nbytes) in ((n, calls[n]) for n in order):
         fn()
         torch.cuda.synchronize()
@@ -213,7 +221,28 @@ def time_prefill_kernels(cache, q, k, v, layer, reps=5):
             flops = 2.0 * nc * L * 32 * cache.num_key_value_groups * D
             res[name].update(tensor_flops_per_launch=flops, achieved_tflops=flops / (us * 1e-6) / 1e12,
                              logits_path="tcgen05.mma (TMA-fed key tiles, TMEM accumulators)")
+        if name == "prefill_attention":
+            # causal: q.k^T and p.v over the lower triangle, 2 flops per multiply-add
+            flops = 2.0 * 2.0 * H * L * L * D / 2.0
+            res[name].update(tensor_flops_per_launch=flops, achieved_tflops=flops / (us * 1e-6) / 1e12,
+                             path="tcgen05.mma: S = Q K^T and O += P V in tensor memory, TMA-fed K/V rings")
         del g
+    if "prefill_attention" in res:
+        G = H // k.shape[1]
+        kk, vv = k.repeat_interleave(G, dim=1), v.repeat_interleave(G, dim=1)
+        sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(q, kk, vv, is_causal=True,
+                                                                        scale=1.0 / math.sqrt(D))
+        sdpa()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            sdpa()
+        e1.record()
+        torch.cuda.synchronize()
+        res["prefill_attention"]["torch_sdpa_us"] = e0.elapsed_time(e1) * 1e3 / reps
+        del kk, vv
+    del att_out
     cache.check_errors()
     return res
 
@@ -417,6 +446,15 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 TFLOP/s: the measured cuBLAS burst figure (a kernel timed
+    alone), else the fallback measurement."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        return float(json.load(open(path))["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def profiled_traffic():
     """dram bytes per flash-decode launch from the committed ncu summary, scaled
     to this run's tokens (profiles/flash_decode_128k.md, if present)."""
@@ -566,6 +604,9 @@ def run_ours(args, rank, world, local_rank):
                                   "frac": drift_bytes / (kt["drift_check_batch"] * 1e-3) / 1e9 / peak}}
     for name, r in getattr(prefill, "stages", {}).items():
         roof[name] = dict(r, frac=r["achieved_gbs"] / peak)
+        if name == "prefill_attention":
+            tpk, tkind = tensor_peak()
+            roof[name].update(bound="tensor", frac=r["achieved_tflops"] / tpk, peak_tflops=tpk, peak_kind=tkind)
     if "retrieve" in kt:
         host = bool(getattr(args, "host_tier", False))
         # host tier: the bytes that cross the host link (the reads)

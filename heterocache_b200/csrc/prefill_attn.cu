@@ -10,22 +10,24 @@
 // One CTA per (128-query tile, query head, batch row); the tiles with the
 // longest causal spans are launched first.  Roles (12 warps):
 //   warp 0, lane 0: TMA producer of the query tile and the key tiles (a
-//     two-stage ring, each stage released as soon as its scores are
+//     three-stage ring, each stage released as soon as its scores are
 //     computed); warp 2, lane 0: producer of the value tiles (two stages,
 //     released by O += P V).  128-token tiles, 64-dim boxes, 128-byte
 //     swizzle; the maps cover this GPU's memory only, no multicast;
 //   warp 1: allocates the tensor memory (512 columns: two score
-//     accumulators of 128 columns and the output accumulator); lane 0
-//     issues the MMAs
+//     accumulators of 128 columns, the output accumulator, two P buffers
+//     of 64 columns); lane 0 issues the MMAs
 //       S_j = Q K_j^T  (M = 128 queries, N = 128 keys, A and B K-major)
-//       O  += P_j V_j  (M = 128 queries, N = 128 dims; A = P, K-major, written
-//                       by the softmax warps; B = V_j, MN-major as loaded)
+//       O  += P_j V_j  (M = 128 queries, N = 128 dims; A = P_j from tensor
+//                       memory, written there by the softmax warps; B = V_j,
+//                       MN-major as loaded)
 //     S_{j+1} is issued before O += P_j V_j, so the tensor core computes the
 //     next scores while the softmax warps work on the current ones;
 //   warps 4-11: softmax, two threads per query row (= TMEM lane), one for
 //     each half of the row's keys and output dims: read S_j, mask the
 //     diagonal tile, trade the halves' maxima, running max in the log2
-//     domain, P = exp2(s * scale - m) into shared memory in the 16-bit type.
+//     domain, P = exp2(s * scale - m) into tensor memory in the 16-bit type
+//     (two buffers: writing P_{j+1} waits only for O += P_{j-1} V_{j-1}).
 //     O and the row sum are rescaled only when the max has grown by more
 //     than 8 (a factor 256) since the last rescale: P stays below 256 and
 //     the final division uses the same reference, so most tiles leave O
@@ -48,10 +50,13 @@ constexpr int kPaTile = 128;
 constexpr int kPaBox = 128 * 128;         // bytes: 128 rows x 64 16-bit elements
 constexpr int kPaTileBytes = 2 * kPaBox;  // one 128 x 128 tile
 constexpr int kPaTmemCols = 512;
-constexpr int kPaKStages = 2, kPaVStages = 2;
+constexpr int kPaKStages = 3, kPaVStages = 2;
+// tensor-memory columns: S buffers at 0 and 128, O at 256, P buffers at 384
+// and 448 (64 columns: 128 16-bit keys per lane)
+constexpr uint32_t kPaColO = 256, kPaColP = 384;
 // dynamic shared memory: 1024 bytes of alignment slack, Q, the K stages, the
-// V stages, P
-constexpr size_t kPaSmem = 1024 + (size_t)(2 + kPaKStages + kPaVStages) * kPaTileBytes;
+// V stages
+constexpr size_t kPaSmem = 1024 + (size_t)(1 + kPaKStages + kPaVStages) * kPaTileBytes;
 
 __device__ __forceinline__ void tma_load_4d_plain(void* dst, const CUtensorMap* map, int x, int y, int z, int w,
                                                   uint64_t* bar) {
@@ -80,9 +85,10 @@ __global__ void __launch_bounds__(kPaThreads, 1)
   unsigned char* sq = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
   unsigned char* sk = sq + kPaTileBytes;
   unsigned char* sv = sk + kPaKStages * kPaTileBytes;
-  unsigned char* sp = sv + kPaVStages * kPaTileBytes;
+  // o_done[b]: completions of O += P_j V_j for j of parity b (two barriers, so
+  // that a wait for the one before last cannot be passed by the last)
   __shared__ __align__(8) uint64_t q_full, k_full[kPaKStages], k_empty[kPaKStages], v_full[kPaVStages],
-      v_empty[kPaVStages], s_full[2], s_free[2], p_ready, o_done, x_bar;
+      v_empty[kPaVStages], s_full[2], s_free[2], p_ready, o_done[2], x_bar;
   __shared__ float s_hmax[2][2][kPaTile], s_hsum[2][kPaTile];  // halves' row maxima and sums
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail, s_kissued, s_vissued;
@@ -111,7 +117,8 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       mbar_init(&s_free[s], kPaSoftmaxWarps);
     }
     mbar_init(&p_ready, kPaSoftmaxWarps);
-    mbar_init(&o_done, 1);
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
     mbar_init(&x_bar, kPaSoftmaxWarps);
     s_fail = 0;
     s_kissued = s_vissued = 0;
@@ -162,7 +169,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
       const uint32_t id_s = idesc_f16_m128(kBf16, 128);
       const uint32_t id_o = idesc_f16_m128(kBf16, 128) | kIdescBMajorMN;
-      const uint32_t aq = smem_u32(sq), ap = smem_u32(sp);
+      const uint32_t aq = smem_u32(sq);
       int last_s = -1, last_pv = -1;
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1, ks = j % kPaKStages;
@@ -187,16 +194,16 @@ __global__ void __launch_bounds__(kPaThreads, 1)
         if (!mbar_wait(&p_ready, j & 1, p.wait_ns)) return false;
         tc_fence_after();
         const uint32_t bv = smem_u32(sv + vs * kPaTileBytes);
-        const uint32_t d = tmem + 256u;
+        const uint32_t d = tmem + kPaColO;
+        const uint32_t pa = tmem + kPaColP + (uint32_t)((j & 1) * 64);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          // A = P, keys 16kk.. (64-key boxes); B = V, key rows 16kk.. (128
-          // bytes a row, the second 64 dims one box further)
-          const uint32_t aoff = (uint32_t)((kk >> 2) * kPaBox + (kk & 3) * 32);
-          umma_f16(d, smem_desc_sw128(ap + aoff), smem_desc_sw128_mn(bv + (uint32_t)(kk * 16 * 128), kPaBox), id_o,
-                   (j > 0 || kk > 0) ? 1u : 0u);
+          // A = P_j, keys 16kk.. (8 columns each); B = V, key rows 16kk..
+          // (128 bytes a row, the second 64 dims one box further)
+          umma_f16_ts(d, pa + (uint32_t)(8 * kk), smem_desc_sw128_mn(bv + (uint32_t)(kk * 16 * 128), kPaBox), id_o,
+                      (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&o_done);
+        umma_commit(&o_done[j & 1]);
         umma_commit(&v_empty[vs]);
         last_pv = j;
         return true;
@@ -210,7 +217,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       if (!ok) atomicExch(&s_fail, 1);
       // every MMA issued has completed before the tensor memory is released
       if (last_s >= 0) (void)mbar_wait_sleep(&s_full[last_s & 1], (last_s >> 1) & 1, p.wait_ns);
-      if (last_pv >= 0) (void)mbar_wait_sleep(&o_done, last_pv & 1, p.wait_ns);
+      if (last_pv >= 0) (void)mbar_wait_sleep(&o_done[last_pv & 1], (last_pv >> 1) & 1, p.wait_ns);
     }
   } else if (warp >= 4) {
     // ---- softmax and output: two threads per query row (TMEM lane), warps
@@ -263,23 +270,22 @@ __global__ void __launch_bounds__(kPaThreads, 1)
       }
       mx = fmaxf(mx, s_hmax[j & 1][half ^ 1][row]);
       const float m_new = fmaxf(m_used, mx * sl2);  // log2 domain (scale > 0)
-      if (j > 0) {
-        // O += P_{j-1} V_{j-1} has completed: O is stable and P is free
-        if (!mbar_wait(&o_done, (j - 1) & 1, p.wait_ns)) {
+      const bool resc = j > 0 && m_new > m_used + 8.f;  // the same in both halves
+      const bool any_resc = __any_sync(0xffffffffu, resc);
+      if (j == 0) m_used = m_new;
+      if (any_resc) {
+        // O += P_{j-1} V_{j-1} (and every product before it) has completed:
+        // O is stable, and P's buffer (last read by O += P_{j-2} V_{j-2}) free
+        if (!mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.wait_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
-      const bool resc = m_new > m_used + 8.f;  // the same in both halves
-      if (j == 0) {
-        m_used = m_new;
-      } else if (__any_sync(0xffffffffu, resc)) {
         const float alpha = resc ? exp2_approx(m_used - m_new) : 1.f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t v[16];
-          const uint32_t ta = tmem + lane_off + 256u + (uint32_t)(col0 + 16 * c);
+          const uint32_t ta = tmem + lane_off + kPaColO + (uint32_t)(col0 + 16 * c);
           tmem_ld16(ta, v);
           tmem_ld_wait();
 #pragma unroll
@@ -291,33 +297,35 @@ __global__ void __launch_bounds__(kPaThreads, 1)
           l *= alpha;
           m_used = m_new;
         }
+      } else if (j >= 2) {
+        // P's buffer was last read by O += P_{j-2} V_{j-2}
+        if (!mbar_wait(&o_done[j & 1], ((j - 2) >> 1) & 1, p.wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
       }
-      // P = exp2(s * scale_log2 - m) in the 16-bit type, K-major with the
-      // 128-byte swizzle (masked scores give exp2(-inf) = 0)
+      // P = exp2(s * scale_log2 - m) in the 16-bit type into this half's 32
+      // columns of P buffer j & 1, keys in pairs (masked scores give
+      // exp2(-inf) = 0)
       const float nm = -m_used;
       float ps = 0.f;
+      uint32_t pw[32];
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        float e[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = exp2_approx(fmaf(x[8 * c8 + i], sl2, nm));
-          ps += e[i];
-        }
-        uint4 w;
-        w.x = Elem<T>::cvt2(e[0], e[1]);
-        w.y = Elem<T>::cvt2(e[2], e[3]);
-        w.z = Elem<T>::cvt2(e[4], e[5]);
-        w.w = Elem<T>::cvt2(e[6], e[7]);
-        *reinterpret_cast<uint4*>(sp + half * kPaBox + swz128(row, c8)) = w;
+      for (int c = 0; c < 32; ++c) {
+        const float e0 = exp2_approx(fmaf(x[2 * c], sl2, nm));
+        const float e1 = exp2_approx(fmaf(x[2 * c + 1], sl2, nm));
+        ps += e0 + e1;
+        pw[c] = Elem<T>::cvt2(e0, e1);
       }
+      tmem_st32(tmem + lane_off + kPaColP + (uint32_t)((j & 1) * 64 + 32 * half), pw);
       l += ps;
-      fence_proxy_async_smem();
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready);
     }
-    if (ok) ok = mbar_wait(&o_done, (nkv - 1) & 1, p.wait_ns);
+    if (ok) ok = mbar_wait(&o_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1, p.wait_ns);
     if (ok) {
       s_hsum[half][row] = l;
       ok = meet(nkv);
@@ -333,7 +341,7 @@ __global__ void __launch_bounds__(kPaThreads, 1)
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[16];
-        tmem_ld16(tmem + lane_off + 256u + (uint32_t)(col0 + 16 * c), v);
+        tmem_ld16(tmem + lane_off + kPaColO + (uint32_t)(col0 + 16 * c), v);
         tmem_ld_wait();
         if (t < p.L) {
           uint4 w0, w1;
