@@ -169,6 +169,7 @@ struct PAParams {
   float scale_log2;       // softmax scale times log2(e)
   int32_t* err;
   uint64_t wait_ns;       // mbarrier wait limit (set at dispatch)
+  unsigned int stall;     // injected stall: no key tile is loaded (tests of the timeout path)
 };
 int prefill_attn_dispatch(int dtype, PAParams& p, const void* q, int64_t qsb, int64_t qsh, int64_t qst,
                           const void* k, int64_t ksb, int64_t ksh, int64_t kst, const void* v, int64_t vsb,

@@ -155,7 +155,10 @@ __global__ void __launch_bounds__(kPaThreads, 1)
           tma_load_4d_plain(sq + kPaTileBytes + kPaBox, &tmq, 64, qb0, h, b, &q_full);
         }
       }
-      for (int j = 0; j < nkv; ++j) {
+      // an injected stall (hc_set_wait_limits) loads no key tile: every wait
+      // on one runs out, for tests of the timeout path
+      const int ntiles = (keys && p.stall) ? 0 : nkv;
+      for (int j = 0; j < ntiles; ++j) {
         const int s = j % NS;
         if (!mbar_wait_sleep(&empty[s], ((j / NS) & 1) ^ 1, p.wait_ns)) {
           atomicExch(&s_fail, 1);
@@ -417,6 +420,7 @@ int prefill_attn_dispatch(int dtype, PAParams& p, const void* q, int64_t qsb, in
     return HC_ERR_INVALID;
   p.n_qt = (p.L + kPaTile - 1) / kPaTile;
   p.wait_ns = wait_limit_ns(kMbarTimeoutNs);
+  p.stall = injected_stall();
   return dtype == HC_BF16 ? prefill_attn_launch<__nv_bfloat16>(p, maps, st) : prefill_attn_launch<__half>(p, maps, st);
 }
 

@@ -78,7 +78,8 @@ def set_wait_limits(limit_ns: int = 0, inject_stall: bool = False) -> None:
     """Limit of every device-side wait of the library's kernels (0: the
     defaults, 2 s per grid barrier and 1 s per mbarrier wait); with
     ``inject_stall`` the scoring kernels' grid barriers wait for an arrival
-    that never comes, so the limit runs out (tests of the timeout path)."""
+    that never comes and the prefill attention loads no key tile, so the
+    limit runs out (tests of the timeout path)."""
     check("hc_set_wait_limits", lib().hc_set_wait_limits(int(limit_ns), 1 if inject_stall else 0))
 
 

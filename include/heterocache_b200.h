@@ -69,7 +69,8 @@ const char* hc_last_cuda_error(void);
  * the launch's err_flag and leaves the kernel (no wait is unbounded).
  * limit_ns = 0 restores the defaults (2 s for a grid barrier, 1 s for an
  * mbarrier).  inject_stall != 0 makes every grid barrier of the scoring
- * kernels wait for one arrival that never comes, so the limit runs out:
+ * kernels wait for one arrival that never comes, and the prefill attention
+ * load no key tile, so the limit runs out:
  * fault injection for tests of the timeout path (a workspace of a launch
  * that timed out must be zero-filled again before its next use).  Process-
  * wide, for launches made after the call (a captured graph keeps the values
