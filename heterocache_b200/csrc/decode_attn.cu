@@ -622,35 +622,44 @@ __global__ void __launch_bounds__(kTThreads, 2)
   if (cur >= 0) flush(cur);
 }
 
-// Merge of one (row, query head): block-parallel over the row's partials.
-// Phase A: lanes over partials -> max, weights exp2(m_c - M) (kept in shared
-// memory) and the weighted normaliser.  Phase B: each warp takes every 8th
-// partial with lanes over 4-dim slices (512-byte coalesced rows), then the
-// 8 warp sums are added in shared memory.
+// Merge of one (row, query head, 32-dim slice of the output): four CTAs per
+// (row, query head), so that the merge after the decode kernel's last CTA is
+// spread over 4 x R x G CTAs, each loading a quarter of every partial.  One
+// load round: lanes in groups of 8 (one 16-byte quarter of the slice each)
+// take a partial, 4 per warp and 8 warps, 4 deep: 128 partials (rows of up
+// to 131072 tokens at the decode grid's spans); the partial's (m, l) comes
+// with it (a broadcast load); then the block maximum, each thread rescales
+// its own partials, and the 32 groups' sums are added in shared memory.
 constexpr int kCThreads = 256;
+constexpr int kCSlices = 4;
+constexpr int kCSliceDims = kD / kCSlices;  // 32
 
 template <typename T>
 __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, int nctas) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s_start = reinterpret_cast<int*>(smem_raw);
+  constexpr int NW = kCThreads / 32, NG = NW * 4, DEPTH = 4;
   __shared__ int s_warp[32];
-  __shared__ float s_red[kCThreads / 32];
+  __shared__ float s_red[NW], s_redl[NW];
   __shared__ float s_mrun;  // running maximum over the rounds of 128 partials
-  __shared__ float4 s_acc[kCThreads / 32][kD / 4];
+  __shared__ float4 s_acc[NG][kCSliceDims / 4];
   const int total = row_prefix(p, s_start, s_warp);
   const int span = span_of(total, nctas, p.gran);
-  const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
+  const int rg = blockIdx.x / kCSlices, sl = blockIdx.x % kCSlices;
+  const int r = rg / p.G, g = rg % p.G;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD;
+  const int sub = lane >> 3, q4 = lane & 7;  // partial group within the warp, 16-byte quarter of the slice
+  const int d0 = kCSliceDims * sl;           // the slice's first dim
+  T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD + d0;
   const int rs = s_start[r], re = s_start[r + 1];
   // the step's token not in the pages yet: its score (log2 domain) and value.
   // q and k_new come from before the decode kernel, which started after they
   // were complete, so they are read ahead of the wait.
   const bool has_new = p.k_new != nullptr;
-  if (p.q_stage && threadIdx.x < kD) {  // the query row into the drift-check buffer
+  if (p.q_stage && threadIdx.x < kCSliceDims) {  // the query row into the drift-check buffer
     const int h = r % p.KV;
     const T* qrow = reinterpret_cast<const T*>(p.q) + (int64_t)(h * p.G + g) * p.qsh;
-    reinterpret_cast<T*>(p.q_stage)[(int64_t)(h * p.G + g) * kD + threadIdx.x] = qrow[threadIdx.x];
+    reinterpret_cast<T*>(p.q_stage)[(int64_t)(h * p.G + g) * kD + d0 + threadIdx.x] = qrow[d0 + threadIdx.x];
   }
   float s_new = -INFINITY, v_new_d = 0.f;
   if (has_new) {
@@ -666,12 +675,13 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
 #pragma unroll
     for (int w = 0; w < kD / 32; ++w) dot += s_red[w];
     s_new = dot * p.scale_log2;
-    if (threadIdx.x < kD)
-      v_new_d = Elem<T>::to_f(reinterpret_cast<const T*>(p.v_new)[b * p.vn_sb + (int64_t)h * p.vn_sh + threadIdx.x]);
+    if (threadIdx.x < kCSliceDims)
+      v_new_d = Elem<T>::to_f(
+          reinterpret_cast<const T*>(p.v_new)[b * p.vn_sb + (int64_t)h * p.vn_sh + d0 + threadIdx.x]);
     __syncthreads();
   }
   if (re == rs || span == 0) {  // no pages: the new token alone, or nothing
-    if (threadIdx.x < kD) out[threadIdx.x] = Elem<T>::from_f(has_new ? v_new_d : 0.f);
+    if (threadIdx.x < kCSliceDims) out[threadIdx.x] = Elem<T>::from_f(has_new ? v_new_d : 0.f);
     return;
   }
   const int c0 = rs / span, n = (re - 1) / span - c0 + 1;
@@ -679,28 +689,24 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   // the partials are written by the decode kernel launched just before
   pdl_wait();
   pdl_trigger();  // the next kernel may get resident; it waits for this grid
-  // One load round: each warp takes every 8th partial, its lanes a 4-dim
-  // slice of the output row, and the partial's (m, l) (one broadcast load)
-  // with it; then the block maximum, and each warp rescales its own partials.
-  // 16 partials per warp: rows of up to 128 partials (131072 tokens at the
-  // decode grid's spans) take a single round.
-  constexpr int NW = kCThreads / 32, DEPTH = 16;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float Lw = 0.f;
-  for (int cb0 = 0; cb0 < n; cb0 += NW * DEPTH) {
+  for (int cb0 = 0; cb0 < n; cb0 += NG * DEPTH) {
     float4 o[DEPTH];
     float2 ml[DEPTH];
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) {
-      const int c = cb0 + warp + u * NW;
+      const int c = cb0 + (warp * 4 + sub) + u * NG;
       const bool ok = c < n;
       ml[u] = ok ? p.part_ml[(slot0 + c) * p.G + g] : make_float2(-INFINITY, 0.f);
-      o[u] = ok ? *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + 4 * lane)
+      o[u] = ok ? *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + d0 + 4 * q4)
                 : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float mw = -INFINITY;
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) mw = fmaxf(mw, ml[u].x);
+#pragma unroll
+    for (int off = 8; off < 32; off <<= 1) mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, off));
     if (lane == 0) s_red[warp] = mw;
     __syncthreads();
     float M = cb0 == 0 ? s_new : s_mrun;
@@ -726,18 +732,21 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   }
   __syncthreads();
   const float M = s_mrun;
-  if (lane == 0) s_red[warp] = Lw;
-  s_acc[warp][lane] = acc;
+  // the normaliser: every lane of a group holds its group's sum; one per group
+#pragma unroll
+  for (int off = 8; off < 32; off <<= 1) Lw += __shfl_xor_sync(0xffffffffu, Lw, off);
+  if (lane == 0) s_redl[warp] = Lw;
+  s_acc[warp * 4 + sub][q4] = acc;
   __syncthreads();
   const float f_new = has_new ? exp2f(s_new - M) : 0.f;  // the new token's weight (its l is 1)
   float L = f_new;
 #pragma unroll
-  for (int w = 0; w < NW; ++w) L += s_red[w];
-  if (threadIdx.x < kD) {
+  for (int w = 0; w < NW; ++w) L += s_redl[w];
+  if (threadIdx.x < kCSliceDims) {
     const int d = threadIdx.x;
     float O = f_new * v_new_d;
 #pragma unroll
-    for (int w = 0; w < kCThreads / 32; ++w) O += reinterpret_cast<const float*>(&s_acc[w][d / 4])[d % 4];
+    for (int k = 0; k < NG; ++k) O += reinterpret_cast<const float*>(&s_acc[k][d / 4])[d % 4];
     out[d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
   }
 }
@@ -777,7 +786,7 @@ static int fd_combine(FDParams& p, int grid, cudaStream_t st) {
   // start early and wait (griddepcontrol.wait) for the partials
   const size_t csm = (((size_t)(p.R + 1) * sizeof(int) + 15) & ~(size_t)15);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.R * p.G);
+  cfg.gridDim = dim3(p.R * p.G * kCSlices);
   cfg.blockDim = dim3(kCThreads);
   cfg.dynamicSmemBytes = csm;
   cfg.stream = st;
