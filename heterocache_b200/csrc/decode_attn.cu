@@ -638,7 +638,9 @@ template <typename T>
 __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, int nctas) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   int* s_start = reinterpret_cast<int*>(smem_raw);
-  constexpr int NW = kCThreads / 32, NG = NW * 4, DEPTH = 4;
+  // LG lanes per partial group (16 bytes of the slice each), GPW groups a warp
+  constexpr int LG = kCSliceDims / 4, GPW = 32 / LG;
+  constexpr int NW = kCThreads / 32, NG = NW * GPW, DEPTH = 128 / NG;
   __shared__ int s_warp[32];
   __shared__ float s_red[NW], s_redl[NW];
   __shared__ float s_mrun;  // running maximum over the rounds of 128 partials
@@ -648,7 +650,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   const int rg = blockIdx.x / kCSlices, sl = blockIdx.x % kCSlices;
   const int r = rg / p.G, g = rg % p.G;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int sub = lane >> 3, q4 = lane & 7;  // partial group within the warp, 16-byte quarter of the slice
+  const int sub = lane / LG, q4 = lane % LG;  // partial group within the warp, 16-byte piece of the slice
   const int d0 = kCSliceDims * sl;           // the slice's first dim
   T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD + d0;
   const int rs = s_start[r], re = s_start[r + 1];
@@ -696,7 +698,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
     float2 ml[DEPTH];
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) {
-      const int c = cb0 + (warp * 4 + sub) + u * NG;
+      const int c = cb0 + (warp * GPW + sub) + u * NG;
       const bool ok = c < n;
       ml[u] = ok ? p.part_ml[(slot0 + c) * p.G + g] : make_float2(-INFINITY, 0.f);
       o[u] = ok ? *reinterpret_cast<const float4*>(p.part_o + ((slot0 + c) * p.G + g) * kD + d0 + 4 * q4)
@@ -706,7 +708,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
 #pragma unroll
     for (int u = 0; u < DEPTH; ++u) mw = fmaxf(mw, ml[u].x);
 #pragma unroll
-    for (int off = 8; off < 32; off <<= 1) mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, off));
+    for (int off = LG; off < 32; off <<= 1) mw = fmaxf(mw, __shfl_xor_sync(0xffffffffu, mw, off));
     if (lane == 0) s_red[warp] = mw;
     __syncthreads();
     float M = cb0 == 0 ? s_new : s_mrun;
@@ -734,9 +736,9 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   const float M = s_mrun;
   // the normaliser: every lane of a group holds its group's sum; one per group
 #pragma unroll
-  for (int off = 8; off < 32; off <<= 1) Lw += __shfl_xor_sync(0xffffffffu, Lw, off);
+  for (int off = LG; off < 32; off <<= 1) Lw += __shfl_xor_sync(0xffffffffu, Lw, off);
   if (lane == 0) s_redl[warp] = Lw;
-  s_acc[warp * 4 + sub][q4] = acc;
+  s_acc[warp * GPW + sub][q4] = acc;
   __syncthreads();
   const float f_new = has_new ? exp2f(s_new - M) : 0.f;  // the new token's weight (its l is 1)
   float L = f_new;
