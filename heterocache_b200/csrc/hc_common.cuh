@@ -182,6 +182,15 @@ __device__ __forceinline__ void set_err(int32_t* err, int code) {
   if (err) atomicOr(err, 1 << code);
 }
 
+// 2^x on the multi-function unit (ex2.approx.ftz: relative error about
+// 2^-22, far below the 16-bit rounding the probabilities get; 2^-inf = 0).
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

@@ -68,14 +68,6 @@ __device__ __forceinline__ void tma_load_4d_plain(void* dst, const CUtensorMap* 
       : "memory");
 }
 
-// 2^x on the multi-function unit (ex2.approx.ftz: relative error about
-// 2^-22, far below the 16-bit rounding P gets; 2^-inf = 0).
-__device__ __forceinline__ float exp2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
-  return y;
-}
-
 template <typename T>
 __global__ void __launch_bounds__(kPaThreads, 1)
     prefill_attn_kernel(const PAParams p, const __grid_constant__ CUtensorMap tmq,

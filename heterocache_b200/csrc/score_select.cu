@@ -139,17 +139,30 @@ __device__ __forceinline__ bool tiny_nonzero(float x) {
   return (__float_as_uint(x) & 0x7fffffffu) - 1u < 0x037fffffu;
 }
 
+// sqrt(128) in fp32: the divisor of every logit (head dim 128).  For bf16
+// logits, rnd(x * r) with r the correctly rounded 1 / sqrt(128) equals
+// rnd(x / sqrt(128)) with the correctly rounded division, for every finite
+// bf16 x (all 2^16 bit patterns checked, tests/test_scale_exact.py), so bf16
+// models scale with one multiply.  fp16 (52 of its values round differently)
+// and fp32 keep the division.
+constexpr float kSqrtD = 11.313708305358887f;
+template <typename T>
+__device__ __forceinline__ bool scale_by_recip(float y) {
+  return std::is_same<T, __nv_bfloat16>::value && y == kSqrtD;
+}
+
 // Logit in the model dtype: rnd(rnd(q.k) / sqrt(d)), the division correctly
 // rounded.  16-bit models divide by the known divisor with one residual
 // correction (tiny nonzero operands take IEEE division; the sign of a zero
-// quotient is restored from the operand, as IEEE division keeps it); fp32
-// models always use IEEE division.
+// quotient is restored from the operand, as IEEE division keeps it), or for
+// bf16 and d = 128 multiply (above); fp32 models always use IEEE division.
 template <typename T>
 __device__ __forceinline__ float scale_logit(float acc, float y, float r) {
   const float x = Elem<T>::rnd(acc);
   if constexpr (std::is_same<T, float>::value) {
     return __fdiv_rn(x, y);
   } else {
+    if (scale_by_recip<T>(y)) return Elem<T>::rnd(x * r);
     float q = copysignf(div_known(x, y, r), x);
     if (__builtin_expect(tiny_nonzero(x), 0)) q = div_ieee(x, y);
     return Elem<T>::rnd(q);
@@ -164,6 +177,13 @@ __device__ __forceinline__ void scale_logit2(float& a, float& b, float y, float 
     b = __fdiv_rn(b, y);
   } else {
     Elem<T>::rnd2(a, b);
+    if (scale_by_recip<T>(y)) {
+      float qa = a * r, qb = b * r;
+      Elem<T>::rnd2(qa, qb);
+      a = qa;
+      b = qb;
+      return;
+    }
     float qa = copysignf(div_known(a, y, r), a), qb = copysignf(div_known(b, y, r), b);
     if (__builtin_expect(tiny_nonzero(a) || tiny_nonzero(b), 0)) {
       if (tiny_nonzero(a)) qa = div_ieee(a, y);
@@ -193,6 +213,21 @@ template <typename T>
 __device__ __forceinline__ float row_exp(float x) {
   if constexpr (std::is_same<T, float>::value) return expf(x);
   else return __expf(x);
+}
+
+// Softmax probability of logit x with row max M, row sum of exp S and its
+// rounded reciprocal R, in fp32 (the reference's softmax(dtype=float32)).
+// fp32 models use the accurate exp and an IEEE division.  16-bit models
+// multiply by the reciprocal (as the CPU softmax the reference runs does) and
+// round to their dtype right after, so they use the fast exp: over every
+// 16-bit parity test (5.5 M scored positions) the fast and the accurate exp
+// give the same rate of scores that differ from the oracle's by one rounding
+// step (0.021 % and 0.021 %), and the accurate one costs 5.6 us per drift
+// check at 128K (47.5 vs 53.1 us, measured).
+template <typename T>
+__device__ __forceinline__ float softmax_prob(float x, float M, float S, float R) {
+  if constexpr (std::is_same<T, float>::value) return __fdiv_rn(expf(x - M), S);
+  else return __expf(x - M) * R;
 }
 
 // Running (max, sum of exp(x - max)) of one score row over the logits a
@@ -432,51 +467,81 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
 }
 
 // ---------------------------------------------------------------------------
-// Phase 1, tcgen05 path (16-bit dtypes, any row count up to 256): the keys
-// stream through shared memory in tiles of 128 tokens loaded by TMA, the
-// tensor core computes D[token, query row] = K_tile . Q^T (M = 128 tokens,
-// N = NP query rows, K = 128 dims in eight 16-deep steps) into one of two
-// tensor-memory accumulators, and the epilogue warps read D back (thread =
-// token, registers = query rows), round and scale the logits exactly as the
-// other paths do and store them to the logits buffer.  The CTA's token range
-// [t0, t1) is a multiple of 128 tokens from a 128-aligned t0 (a tile never
-// crosses a 256-token page); the pooling margins either side are 16-row
-// tiles (rows 16..127 of such a tile are left over from earlier tiles: their
-// results are discarded).
+// Phase 1 and the window sums, tcgen05 path (16-bit dtypes, launches of more
+// than 40 query rows: observation windows).  The CTA's keys stream through
+// shared memory twice, in tiles of 128 tokens loaded by TMA, and the tensor
+// core recomputes the logits on each pass (K = 128 dims in eight 16-deep
+// steps) into one of two tensor-memory accumulators; no logit is stored:
+//
+//  * PASS_STATS: D[query row, token] = Q . K_tile^T (M = 128 query rows per
+//    row block, N = 128 tokens).  A thread reads one query row's logits of 32
+//    tokens per load (its TMEM lane is the row), rounds and scales them as
+//    the other paths do, and keeps that row's running (max, sum of exp) over
+//    the CTA's own tokens; the warps of a lane quarter split the token
+//    columns, and after the pass their pairs are merged in warp order into
+//    the CTA's softmax partials (p.part).  Margin tiles are not loaded.
+//  * PASS_SUMS, after the grid-wide softmax statistics: D[token, query row]
+//    = K_tile . Q^T (M = 128 tokens, N = NP query rows).  A thread holds one
+//    token's logits of every row of a score row's window, turns them into
+//    probabilities rounded to the dtype, adds them in window order (w = 0 ..
+//    W-1, fp32) and stores the rounded window sum -- the probability itself
+//    when W = 1 -- into row sg of the compact buffer lg [S * G][TB], for the
+//    CTA's tokens and the pooling margins either side (16-row tiles; rows
+//    16..127 of such a tile are left over from earlier tiles and discarded).
+//
+// The CTA's token range [t0, t1) is a multiple of 128 tokens from a
+// 128-aligned t0 (a tile never crosses a 256-token page).  Tiles are numbered
+// across the two passes (the sums pass's first tile follows the statistics
+// pass's last), so the ring's and the accumulators' mbarriers run on without
+// being initialised again.
 //
 // Roles: warp 0 lane 0 issues the TMA loads (stages released by the MMA's
 // completion), warp 1 allocates the tensor memory and its lane 0 issues the
 // MMAs, warps 2-15 read the accumulators: a warp may only read the TMEM lanes
-// 32 * (warp % 4) .. + 31, so the work items of a tile are (lane quarter,
-// 8-column chunk) pairs, each quarter's chunks dealt round-robin over its
-// three or four warps (more warps in flight hide the epilogue's dependent
-// arithmetic; it would otherwise set the pace).  Every wait is bounded; a wait that gives up marks
-// the launch failed (HC_ERR_TIMEOUT) and its role stops, the others run out
-// their own bounded waits, in-flight copies and MMAs are waited for (bounded)
-// and the tensor memory is released before the phase ends.
+// 32 * (warp % 4) .. + 31, so each lane quarter's work of a tile is dealt
+// round-robin over its three or four warps, and every one of the 14 warps
+// releases each accumulator.  Every wait is bounded; a wait that gives up
+// marks the launch failed (HC_ERR_TIMEOUT) and its role stops, the others run
+// out their own bounded waits, in-flight copies and MMAs are waited for
+// (bounded) and the tensor memory is released before the pass ends; after a
+// failed statistics pass the sums pass does nothing.
 constexpr int kUStage = 2 * 128 * 128;  // bytes of one stage: two 128-row x 128-byte boxes
 constexpr int kMaxStages = 6;
 constexpr int kUBox = 128 * 128;
-
-constexpr int kUColMax = 48;  // query rows whose maxima the epilogue keeps in registers
+constexpr int kUEpi = kSWarps - 2;  // accumulator readers (warps 2-15)
 
 struct UmmaSmem {
   uint64_t full[kMaxStages], empty[kMaxStages], accf[2], acce[2];
   uint32_t tmem;
   int issued, consumed, fail;
-  float colmax[kSWarps][kUColMax];  // per-warp row maxima (reg_max)
-  int pages[kMaxPages];             // drift checks: page ids of the CTA's keys
+  int pages[kMaxPages];  // drift checks: page ids of the CTA's keys
 };
 
-// Eight logits of one token: x holds q.k dot products (fp32) and receives
-// rnd(rnd(x) / sqrt(d)) as scale_logit does, branch-free except for one
-// vote-free fix-up branch taken when any operand is 0 or tiny (the fast
-// division does not keep the sign of a zero; a subnormal quotient needs IEEE
-// division).
+enum { PASS_STATS = 0, PASS_SUMS = 1 };
+
+// Rows of the query operand in shared memory: NP for the sums pass's B
+// operand, whole 128-row blocks for the statistics pass's A operand.
+__host__ __device__ constexpr int umma_query_rows(int Rq) { return (Rq + 127) / 128 * 128; }
+
+// Eight logits: x holds q.k dot products (fp32) and receives rnd(rnd(x) /
+// sqrt(d)) as scale_logit does (bf16 and d = 128: one multiply each), else
+// branch-free except for one vote-free fix-up branch taken when any operand
+// is 0 or tiny (the fast division does not keep the sign of a zero; a
+// subnormal quotient needs IEEE division).
 template <typename T>
-__device__ __forceinline__ void scale_logit8(float (&x)[8], float y, float r) {
+__device__ __forceinline__ void scale_logit8(float* x, float y, float r) {
 #pragma unroll
   for (int j = 0; j < 8; j += 2) Elem<T>::rnd2(x[j], x[j + 1]);
+  if (scale_by_recip<T>(y)) {
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      float a = x[j] * r, b = x[j + 1] * r;
+      Elem<T>::rnd2(a, b);
+      x[j] = a;
+      x[j + 1] = b;
+    }
+    return;
+  }
   float q[8];
   bool fix = false;
 #pragma unroll
@@ -500,26 +565,24 @@ __device__ __forceinline__ void scale_logit8(float (&x)[8], float y, float r) {
   }
 }
 
-template <typename T, int MODE>
-__device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsigned char* stages,
-                            unsigned char* qop, UmmaSmem& u, const CUtensorMap* tm_rows,
-                            const CUtensorMap* tm_edge) {
+// One pass (see above).  wpart: PASS_STATS's per-warp row pairs [4][kMaxRq]
+// (memory of the later phases, free here).  s_rowM / s_rowS / s_rowR:
+// PASS_SUMS's global row statistics.
+template <typename T, int MODE, int PASS>
+__device__ void umma_pass(const ScoreParams& p, const JobInfo& ji, T* lg, unsigned char* stages,
+                          unsigned char* qop, UmmaSmem& u, const CUtensorMap* tm_rows, const CUtensorMap* tm_edge,
+                          float2* wpart, const float* s_rowM, const float* s_rowS, const float* s_rowR) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int NS = p.n_stages, NP = p.NP, Rq = p.Rq;
-  const int nchunk = (Rq + 7) >> 3;  // 8-column chunks holding query rows (the rest of NP is padding)
-  // epilogue warps of a lane quarter q: {q, q+4, q+8, q+12} less warps 0 and
-  // 1; how many of them have chunks
+  const int QR = umma_query_rows(Rq);
+  const int nrb = QR >> 7;  // 128-row blocks of query rows
   auto quarter_warps = [](int q) { return q < 2 ? 3 : 4; };
-  auto active = [&](int q) { return min(quarter_warps(q), nchunk); };
-  const int n_epi = active(0) + active(1) + active(2) + active(3);
-  // with at most two chunks per warp the row maxima over the CTA's own tokens
-  // are kept in registers and published per warp in u.colmax[warp][row]
-  const bool reg_max = nchunk <= 6;
-  float (*colmax)[kUColMax] = u.colmax;
   const int lo = max(0, ji.t0 - kMargin), hi = min(p.L, ji.t1 + kMargin);
-  const bool left = ji.t0 > 0, right = ji.t1 < p.L;
+  constexpr bool kMargins = PASS == PASS_SUMS;
+  const bool left = kMargins && ji.t0 > 0, right = kMargins && ji.t1 < p.L;
   const int nmain = (ji.t1 - ji.t0 + 127) >> 7;
   const int ntiles = (left ? 1 : 0) + nmain + (right ? 1 : 0);
+  const int tile0 = PASS == PASS_SUMS ? nmain : 0;  // the statistics pass's tiles come first
   auto tile_of = [&](int i, int& start, int& rows) {
     if (left) {
       if (i == 0) { start = ji.t0 - kMargin; rows = kMargin; return; }
@@ -529,24 +592,31 @@ __device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsi
     start = ji.t1;
     rows = kMargin;
   };
+  // accumulator columns: two buffers of 128 columns per row block (statistics)
+  // or of NP columns (sums)
+  const int acc_cols = PASS == PASS_STATS ? QR : NP;
+  const uint32_t ncols = PASS == PASS_STATS ? (nrb == 1 ? 256u : 512u) : (uint32_t)p.tmem_cols;
   // ---- set-up: barriers first, so that the key stream starts at once
-  if (threadIdx.x == 0) {
+  if (PASS == PASS_STATS && threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&u.full[s], 1);
       mbar_init(&u.empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&u.accf[b], 1);
-      mbar_init(&u.acce[b], n_epi);
+      mbar_init(&u.acce[b], kUEpi);
     }
     u.issued = u.consumed = u.fail = 0;
     fence_mbar_init();
   }
-  if (reg_max)
-    for (int i = threadIdx.x; i < kSWarps * Rq; i += kSThreads) colmax[i / Rq][i % Rq] = -INFINITY;
+  // the ring held the statistics pass's row pairs (generic stores) before the
+  // copies of this pass write it
+  if (PASS == PASS_SUMS) fence_proxy_async_smem();
   __syncthreads();
+  if (PASS == PASS_SUMS && u.fail) return;  // the statistics pass gave up (block-uniform)
 
   uint32_t tmem = 0;
+  float rm[2] = {-INFINITY, -INFINITY}, rs[2] = {0.f, 0.f};  // statistics: (max, sum) per row block
   if (warp == 0) {
     // ---- TMA producer.  Drift checks: the page ids of the CTA's keys first,
     // loaded by the whole warp at once (kMaxPages of them; beyond that each
@@ -574,8 +644,8 @@ __device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsi
       const uint64_t pol = l2_evict_first_policy();
       int i = 0;
       for (; i < ntiles; ++i) {
-        const int s = i % NS;
-        if (!mbar_wait_sleep(&u.empty[s], ((i / NS) & 1) ^ 1, p.wait_ns)) {
+        const int g = tile0 + i, s = g % NS;
+        if (!mbar_wait_sleep(&u.empty[s], ((g / NS) & 1) ^ 1, p.wait_ns)) {
           atomicExch(&u.fail, 1);
           break;
         }
@@ -603,23 +673,26 @@ __device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsi
           tma_load_4d(dst + kUBox, m, 64, start, ji.h, ji.b, &u.full[s], pol);
         }
       }
-      u.issued = i;
+      u.issued = tile0 + i;
     }
   } else {
-    // ---- tensor memory and the query operand, while the first tiles load
+    // ---- tensor memory and (first pass) the query operand, while the first
+    // tiles load
     if (warp == 1) {
-      tmem_alloc(&u.tmem, (uint32_t)p.tmem_cols);
-      tmem_relinquish();
+      tmem_alloc(&u.tmem, ncols);
+      if (PASS == PASS_SUMS) tmem_relinquish();  // the CTA's last allocation
     }
-    // query rows as the B operand: NP rows x 128 dims, K-major, 128-byte
-    // swizzle, rows past Rq zero
-    for (int i = threadIdx.x - 32; i < NP * 16; i += kSThreads - 32) {
-      const int r = i >> 4, c16 = i & 15;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < Rq) v = ldg128(query_row<T>(p, ji, r) + 8 * c16);
-      *reinterpret_cast<uint4*>(qop + (c16 >> 3) * (NP * 128) + swz128(r, c16 & 7)) = v;
+    if (PASS == PASS_STATS) {
+      // query rows: QR rows x 128 dims, K-major, 128-byte swizzle, rows past
+      // Rq zero; the two 64-dim halves QR * 128 bytes apart
+      for (int i = threadIdx.x - 32; i < QR * 16; i += kSThreads - 32) {
+        const int r = i >> 4, c16 = i & 15;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (r < Rq) v = ldg128(query_row<T>(p, ji, r) + 8 * c16);
+        *reinterpret_cast<uint4*>(qop + (c16 >> 3) * (QR * 128) + swz128(r, c16 & 7)) = v;
+      }
+      fence_proxy_async_smem();
     }
-    fence_proxy_async_smem();
     tc_fence_before();
     named_bar_sync(1, kSThreads - 32);
     tc_fence_after();
@@ -627,107 +700,172 @@ __device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsi
     if (warp == 1) {
       // ---- MMA issuer
       if (lane == 0) {
-        const uint32_t idesc = idesc_f16_m128(std::is_same<T, __nv_bfloat16>::value, NP);
+        const bool bf = std::is_same<T, __nv_bfloat16>::value;
+        const uint32_t idesc = idesc_f16_m128(bf, PASS == PASS_STATS ? 128 : NP);
         const uint32_t q0 = smem_u32(qop);
         int i = 0;
         for (; i < ntiles; ++i) {
-          const int s = i % NS, b = i & 1;
-          if (!mbar_wait_sleep(&u.full[s], (i / NS) & 1, p.wait_ns)) {
+          const int g = tile0 + i, s = g % NS, b = g & 1;
+          if (!mbar_wait_sleep(&u.full[s], (g / NS) & 1, p.wait_ns)) {
             atomicExch(&u.fail, 1);
             break;
           }
-          u.consumed = i + 1;
-          if (!mbar_wait_sleep(&u.acce[b], ((i >> 1) & 1) ^ 1, p.wait_ns)) {
+          u.consumed = g + 1;
+          if (!mbar_wait_sleep(&u.acce[b], ((g >> 1) & 1) ^ 1, p.wait_ns)) {
             atomicExch(&u.fail, 1);
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(stages + (size_t)s * kUStage);
-          const uint32_t d = tmem + (uint32_t)(b * NP);
+          const uint32_t k0 = smem_u32(stages + (size_t)s * kUStage);
+          const uint32_t d = tmem + (uint32_t)(b * acc_cols);
+          if (PASS == PASS_STATS) {
+            for (int rb = 0; rb < nrb; ++rb) {
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t ao = a0 + (kk >> 2) * kUBox + (kk & 3) * 32;
-            const uint32_t bo = q0 + (kk >> 2) * (NP * 128) + (kk & 3) * 32;
-            umma_f16(d, smem_desc_sw128(ao), smem_desc_sw128(bo), idesc, kk > 0 ? 1u : 0u);
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t ao = q0 + (kk >> 2) * (QR * 128) + rb * (128 * 128) + (kk & 3) * 32;
+                const uint32_t bo = k0 + (kk >> 2) * kUBox + (kk & 3) * 32;
+                umma_f16(d + (uint32_t)(rb * 128), smem_desc_sw128(ao), smem_desc_sw128(bo), idesc,
+                         kk > 0 ? 1u : 0u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t ao = k0 + (kk >> 2) * kUBox + (kk & 3) * 32;
+              const uint32_t bo = q0 + (kk >> 2) * (QR * 128) + (kk & 3) * 32;
+              umma_f16(d, smem_desc_sw128(ao), smem_desc_sw128(bo), idesc, kk > 0 ? 1u : 0u);
+            }
           }
           umma_commit(&u.empty[s]);
           umma_commit(&u.accf[b]);
         }
         // every MMA issued has completed before the tensor memory is released
-        if (i > 0) (void)mbar_wait_sleep(&u.accf[(i - 1) & 1], ((i - 1) >> 1) & 1, p.wait_ns);
+        if (i > 0) {
+          const int g = tile0 + i - 1;
+          (void)mbar_wait_sleep(&u.accf[g & 1], (g >> 1) & 1, p.wait_ns);
+        }
       }
     } else {
-      // ---- epilogue: accumulators -> rounded logits
+      // ---- accumulator readers
       const int q4 = warp & 3;
       const int k = q4 < 2 ? (warp >> 2) - 1 : (warp >> 2);  // index among the quarter's warps
       const int m = quarter_warps(q4);
-      if (k < active(q4)) {
-        // launch constants in registers (the loop stores through a pointer the
-        // compiler cannot separate from the parameter block)
-        const int TB = p.TB, W = p.W, L = p.L;
-        const float sqd = p.sqrt_d, r_sqrt = __frcp_rn(sqd);
-        const int base = ji.t0 - kMargin;
-        const int r = 32 * q4 + lane;  // tile row = TMEM lane
-        const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
-        float cmax[2][8];
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) cmax[cc][j] = -INFINITY;
-        for (int i = 0; i < ntiles; ++i) {
-          const int b = i & 1;
-          int start, rows;
-          tile_of(i, start, rows);
-          const bool ok = mbar_wait_sleep(&u.accf[b], (i >> 1) & 1, p.wait_ns);
-          if (!ok) atomicExch(&u.fail, 1);
-          tc_fence_after();
-          const int t = start + r;
-          const bool valid = ok && r < rows && t >= lo && t < hi;
-          const bool own = valid && t >= ji.t0 && t < ji.t1;
-          T* __restrict__ out = lg + (t - base);
-          // in-window causal mask (W > 1): query row qi = sg * W + w sees
-          // tokens t <= L - W + w
-          const int wlim = t - (L - W);
-          int cc = 0;
-          for (int c = k; c < nchunk; c += m, ++cc) {
-            uint32_t v[8];
-            tmem_ld8(tmem + lane_off + (uint32_t)(b * NP + 8 * c), v);
+      const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+      // launch constants in registers (the loops store through pointers the
+      // compiler cannot separate from the parameter block)
+      const int W = p.W, L = p.L, TB = p.TB, t1 = ji.t1;
+      const float sqd = p.sqrt_d, r_sqrt = __frcp_rn(sqd);
+      for (int i = 0; i < ntiles; ++i) {
+        const int g = tile0 + i, b = g & 1;
+        int start, rows;
+        tile_of(i, start, rows);
+        const bool ok = mbar_wait_sleep(&u.accf[b], (g >> 1) & 1, p.wait_ns);
+        if (!ok) atomicExch(&u.fail, 1);
+        tc_fence_after();
+        if (ok && PASS == PASS_STATS) {
+          // work items (row block, 32-token chunk), dealt over the quarter's warps
+          for (int it = k; it < 4 * nrb; it += m) {
+            const int rb = it >> 2, kc = it & 3;
+            if (rb * 128 + 32 * q4 >= Rq) continue;  // no row on this warp's lanes (warp-uniform)
+            const int qi = rb * 128 + 32 * q4 + lane;
+            uint32_t v[32];
+            tmem_ld32(tmem + lane_off + (uint32_t)(b * acc_cols + rb * 128 + 32 * kc), v);
             tmem_ld_wait();
-            if (valid) {
-              float x[8];
+            float x[4][8];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) x[j] = __uint_as_float(v[j]);
-              scale_logit8<T>(x, sqd, r_sqrt);
+            for (int j = 0; j < 32; ++j) x[j >> 3][j & 7] = __uint_as_float(v[j]);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int qi = 8 * c + j;
-                if (W > 1 && wlim > qi % W) x[j] = -INFINITY;
-                if (qi < Rq) out[(int64_t)qi * TB] = Elem<T>::pack(x[j]);
+            for (int c = 0; c < 4; ++c) scale_logit8<T>(x[c], sqd, r_sqrt);
+            // tokens counted: the CTA's own (t < t1) that the row may see (in
+            // an observation window row qi = sg * W + w sees t <= L - W + w)
+            const int tk = start + 32 * kc;
+            const int lim = W > 1 ? min(t1, L - W + qi % W + 1) : t1;
+            if (tk + 32 > lim) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (tk + j >= lim) x[j >> 3][j & 7] = -INFINITY;
+            }
+            float cm = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) cm = fmaxf(cm, x[j >> 3][j & 7]);
+            if (cm != -INFINITY) {
+              float& M = rm[rb];
+              float& S = rs[rb];
+              if (cm > M) {
+                S *= exp2_approx((M - cm) * kLog2e);  // 0 while M is still -inf
+                M = cm;
               }
-              if (own && cc < 2) {
+              // exp(x - M) as 2^(x log2 e - M log2 e), one multiply-add each
+              const float nm = -M * kLog2e;
+              float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int j = 0; j < 8; ++j) cmax[cc & 1][j] = fmaxf(cmax[cc & 1][j], x[j]);
-              }
+              for (int j = 0; j < 32; ++j) s4[j & 3] += exp2_approx(fmaf(x[j >> 3][j & 7], kLog2e, nm));
+              S += (s4[0] + s4[1]) + (s4[2] + s4[3]);
             }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&u.acce[b]);
-          if (!ok) break;
-        }
-        if (reg_max) {
-          int cc = 0;
-          for (int c = k; c < nchunk && cc < 2; c += m, ++cc) {
+        } else if (ok) {
+          // sums: thread = token; the quarter's warps take score rows sg = k,
+          // k + m, ... (window columns sg * W .. + W - 1)
+          const int r = 32 * q4 + lane;
+          const int t = start + r;
+          const bool valid = r < rows && t >= lo && t < hi;
+          const int nsg = Rq / W;
+          const int base = ji.t0 - kMargin;
+          // per-column checks only where a chunk straddles a window's edge
+          // (W not a multiple of 8) or a token of the tile is masked for
+          // some row (t > L - W); tile-uniform
+          const bool checked = (W & 7) != 0 || (W > 1 && start + rows - 1 > L - W);
+          for (int sg = k; sg < nsg; sg += m) {
+            const int c0 = sg * W, c1 = c0 + W;
+            float acc = 0.f;
+            for (int cb = c0 & ~7; cb < c1; cb += 32) {
+              // up to four 8-column loads in flight per wait
+              const int nl = min(4, (c1 - cb + 7) >> 3);
+              uint32_t v[4][8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float mx = cmax[cc][j];
+              for (int c = 0; c < 4; ++c)
+                if (c < nl) tmem_ld8(tmem + lane_off + (uint32_t)(b * acc_cols + cb + 8 * c), v[c]);
+              tmem_ld_wait();
+              if (valid) {
 #pragma unroll
-              for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-              const int qi = 8 * c + j;
-              if (lane == 0 && qi < Rq) colmax[warp][qi] = mx;
+                for (int c = 0; c < 4; ++c) {
+                  if (c >= nl) break;
+                  float x[8];
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) x[j] = __uint_as_float(v[c][j]);
+                  scale_logit8<T>(x, sqd, r_sqrt);
+                  const int q8 = cb + 8 * c;  // first query row of the chunk (8-aligned)
+                  const float4 Ma = *reinterpret_cast<const float4*>(s_rowM + q8);
+                  const float4 Mb = *reinterpret_cast<const float4*>(s_rowM + q8 + 4);
+                  const float4 Ra = *reinterpret_cast<const float4*>(s_rowR + q8);
+                  const float4 Rb = *reinterpret_cast<const float4*>(s_rowR + q8 + 4);
+                  const float Mv[8] = {Ma.x, Ma.y, Ma.z, Ma.w, Mb.x, Mb.y, Mb.z, Mb.w};
+                  const float Rv[8] = {Ra.x, Ra.y, Ra.z, Ra.w, Rb.x, Rb.y, Rb.z, Rb.w};
+                  float pr[8];
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) pr[j] = softmax_prob<T>(x[j], Mv[j], s_rowS[q8 + j], Rv[j]);
+                  if (checked) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                      const int qi = q8 + j;
+                      // outside this window, or masked: no contribution
+                      if (qi < c0 || qi >= c1 || (W > 1 && t > L - W + (qi - c0))) pr[j] = 0.f;
+                    }
+                  }
+#pragma unroll
+                  for (int j = 0; j < 8; j += 2) Elem<T>::rnd2(pr[j], pr[j + 1]);
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) acc += pr[j];
+                }
+              }
             }
+            if (valid) lg[(int64_t)sg * TB + (t - base)] = Elem<T>::from_f(acc);
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&u.acce[b]);
+        if (!ok) break;
       }
     }
   }
@@ -741,9 +879,30 @@ __device__ bool logits_umma(const ScoreParams& p, const JobInfo& ji, T* lg, unsi
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, (uint32_t)p.tmem_cols);
+    tmem_dealloc(tmem, ncols);
   }
-  return reg_max;
+  if (PASS == PASS_STATS) {
+    // the ring is idle: each reader warp's row pairs, then per row the merge
+    // of its quarter's warps in warp order into the CTA's partial
+    if (warp >= 2) {
+      const int q4 = warp & 3;
+      const int k = q4 < 2 ? (warp >> 2) - 1 : (warp >> 2);
+      for (int rb = 0; rb < nrb; ++rb) {
+        const int qi = rb * 128 + 32 * q4 + lane;
+        if (qi < Rq) wpart[k * kMaxRq + qi] = make_float2(rm[rb], rs[rb]);
+      }
+    }
+    __syncthreads();
+    for (int qi = threadIdx.x; qi < Rq; qi += kSThreads) {
+      const int mq = quarter_warps((qi & 127) >> 5);
+      float M = -INFINITY, S = 0.f;
+      for (int k = 0; k < mq; ++k) {
+        const float2 v = wpart[k * kMaxRq + qi];
+        online_merge<T>(M, S, v.x, v.y);
+      }
+      p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(M, S);
+    }
+  }
 }
 
 // Phase 1, CUDA-core path (fp32, or many query rows): 32-token tiles of keys
@@ -794,21 +953,6 @@ __device__ void logits_fma(const ScoreParams& p, const JobInfo& ji, T* lg, float
       for (int w = 0; w < kSWarps; ++w) wmax[w * kMaxRq + qi] = (w == warp) ? m : -INFINITY;
     }
   }
-}
-
-// Softmax probability of logit x with row max M, row sum of exp S and its
-// rounded reciprocal R, in fp32 (the reference's softmax(dtype=float32)).
-// fp32 models use the accurate exp and an IEEE division.  16-bit models
-// multiply by the reciprocal (as the CPU softmax the reference runs does) and
-// round to their dtype right after, so they use the fast exp: over every
-// 16-bit parity test (5.5 M scored positions) the fast and the accurate exp
-// give the same rate of scores that differ from the oracle's by one rounding
-// step (0.021 % and 0.021 %), and the accurate one costs 5.6 us per drift
-// check at 128K (47.5 vs 53.1 us, measured).
-template <typename T>
-__device__ __forceinline__ float softmax_prob(float x, float M, float S, float R) {
-  if constexpr (std::is_same<T, float>::value) return __fdiv_rn(expf(x - M), S);
-  else return __expf(x - M) * R;
 }
 
 // Eight consecutive elements (16-byte aligned for 16-bit types, 32-byte for
@@ -1052,7 +1196,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
   if constexpr (MODE != MODE_PREFILL) p.W = 1;
   if (MODE != MODE_PREFILL || p.Lsel <= 0 || p.Lsel > p.L) p.Lsel = p.L;
   extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ float s_rowM[kMaxRq], s_rowInv[kMaxRq], s_rowR[kMaxRq];
+  __shared__ __align__(16) float s_rowM[kMaxRq], s_rowInv[kMaxRq], s_rowR[kMaxRq];  // 16-byte loads (tcgen05 sums)
   __shared__ unsigned int s_prefix[kMaxSel], s_mask[kMaxSel], s_rem[kMaxSel], s_k[kMaxSel];
   __shared__ int s_sel_row[kMaxSel];
   __shared__ int2 s_wcnt[kMaxSel][kSWarps];
@@ -1121,26 +1265,29 @@ __global__ void __launch_bounds__(kSThreads, 1)
   const int nblocks = gridDim.x;
   unsigned int epoch = 0;
 
-  // ---- shared memory carve-up
+  // ---- shared memory carve-up.  The logits buffer: every query row's
+  // logits, or on the tcgen05 path (which stores no logits) one window-summed
+  // probability row per score row
   unsigned char* sp = smem;
+  const int lg_rows = p.umma ? p.S * p.G : p.Rq;
   T* lg;
   if (p.logits_in_smem) {
     lg = reinterpret_cast<T*>(sp);
-    sp += ((size_t)p.Rq * p.TB * sizeof(T) + 15) & ~(size_t)15;
+    sp += ((size_t)lg_rows * p.TB * sizeof(T) + 15) & ~(size_t)15;
   } else {
-    lg = reinterpret_cast<T*>(p.glogits) + (size_t)blockIdx.x * p.Rq * p.TB;
+    lg = reinterpret_cast<T*>(p.glogits) + (size_t)blockIdx.x * lg_rows * p.TB;
   }
   // tcgen05 path: the query operand, then the ring of key stages, 1024-byte
-  // aligned (the launch reserves the slack); the ring is dead after phase 1,
-  // so the arrays of the later phases (keys, histograms, row partials) share
-  // its memory
+  // aligned (the launch reserves the slack); the ring is idle between the two
+  // passes and dead after the second, so the arrays of the later phases
+  // (keys, histograms, row partials) share its memory
   __shared__ UmmaSmem s_umma;
   unsigned char* u_stages = nullptr;
   unsigned char* u_qop = nullptr;
   if (p.umma) {
     const uint32_t a = smem_u32(sp);
     u_qop = sp + ((1024u - (a & 1023u)) & 1023u);
-    u_stages = u_qop + (size_t)p.NP * 256;
+    u_stages = u_qop + (size_t)umma_query_rows(p.Rq) * 256;
     sp = u_stages;
   }
   unsigned int* keys = reinterpret_cast<unsigned int*>(sp);
@@ -1155,11 +1302,12 @@ __global__ void __launch_bounds__(kSThreads, 1)
   // starts before any other global access of the launch (the page ids are
   // read per tile by the TMA producer)
   constexpr bool kTensor = !std::is_same<T, float>::value;
-  bool used_mma = false, used_umma = false, umma_regmax = false;
+  bool used_mma = false, used_umma = false;
   if constexpr (kTensor) {
     if (p.umma) {
-      // row maxima: per warp in s_umma.colmax, or from a pass over the logits
-      umma_regmax = logits_umma<T, MODE>(p, ji, lg, u_stages, u_qop, s_umma, &tm_rows, &tm_edge);
+      // the CTA's softmax partials (max, sum of exp) per query row, into p.part
+      umma_pass<T, MODE, PASS_STATS>(p, ji, lg, u_stages, u_qop, s_umma, &tm_rows, &tm_edge,
+                                     reinterpret_cast<float2*>(wmax), nullptr, nullptr, nullptr);
       used_mma = used_umma = true;
     }
   }
@@ -1224,29 +1372,11 @@ __global__ void __launch_bounds__(kSThreads, 1)
     float* sk = sq + p.Rq * kD;
     logits_fma<T>(p, ji, lg, wmax, sq, sk);
   }
-  // the logits pass also summed exp (mma.sync path, logits in global memory)
-  const bool online_sums = used_mma && !used_umma && !p.logits_in_smem;
+  // the logits pass also summed exp (mma.sync path, logits in global memory;
+  // the tcgen05 statistics pass published the CTA's partials itself)
+  const bool online_sums = used_umma || (used_mma && !p.logits_in_smem);
   __syncthreads();
-  if (umma_regmax) {
-    for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
-      float m = -INFINITY;
-      for (int w = 0; w < kSWarps; ++w) m = fmaxf(m, s_umma.colmax[w][qi]);
-      s_rowM[qi] = m;
-    }
-  } else if (used_umma) {
-    // row maxima over the CTA's own tokens (tcgen05 path with many rows): one
-    // warp per row
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int base = ji.t0 - kMargin;
-    for (int qi = warp; qi < p.Rq; qi += kSWarps) {
-      const T* row = lg + (int64_t)qi * p.TB - base;
-      float m = -INFINITY;
-      for (int t = ji.t0 + lane; t < ji.t1; t += 32) m = fmaxf(m, Elem<T>::to_f(row[t]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) s_rowM[qi] = m;
-    }
-  } else {
+  if (!used_umma) {
     for (int qi = threadIdx.x; qi < p.Rq; qi += kSThreads) {
       float m = -INFINITY;
       for (int w = 0; w < kSWarps; ++w) m = fmaxf(m, wmax[w * kMaxRq + qi]);
@@ -1364,10 +1494,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
     }
   }
   __syncthreads();
+  if constexpr (kTensor) {
+    if (used_umma) {
+      // second pass over the keys: one window-summed probability row per
+      // score row in lg (row sg, so the pooling below reads it as W = 1)
+      umma_pass<T, MODE, PASS_SUMS>(p, ji, lg, u_stages, u_qop, s_umma, &tm_rows, &tm_edge, nullptr, s_rowM,
+                                    s_rowInv, s_rowR);
+      p.W = 1;
+    }
+  }
   // zero the round-0 histograms (one per score row) before the pooling pass
   for (int i = threadIdx.x; i < kMaxSel * 256; i += kSThreads) lhist[i] = 0u;
   __syncthreads();
-  if (p.W == 1 && p.halo <= 3) {
+  if (!used_umma && p.W == 1 && p.halo <= 3) {
     // probabilities computed inline from the logits
     switch (p.halo) {
       case 0: pooled_keys8<T, 0, true>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
@@ -1376,9 +1515,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
       default: pooled_keys8<T, 3, true>(p, ji, lg, keys, lhist, s_rowM, s_rowInv, s_rowR); break;
     }
   } else {
+    // probabilities and window sums in place (the tcgen05 path wrote them)
     const int base = ji.t0 - kMargin;
     const int lo = max(0, ji.t0 - p.halo), hi = min(p.L, ji.t1 + p.halo);
-    const int span = hi - lo;
+    const int span = used_umma ? 0 : hi - lo;
     for (int i = threadIdx.x; i < p.Rq * span; i += kSThreads) {
       int qi = i / span, t = lo + i % span;
       T* cell = lg + (int64_t)qi * p.TB + (t - base);
@@ -1387,7 +1527,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
       *cell = Elem<T>::from_f(pr);
     }
     __syncthreads();
-    if (p.W > 1) {
+    if (p.W > 1 && !used_umma) {
       const int nsg = p.S * p.G;
       for (int i = threadIdx.x; i < nsg * span; i += kSThreads) {
         int sg = i / span, t = lo + i % span;
@@ -1863,7 +2003,10 @@ static size_t elem_size(int dtype) { return dtype == HC_F32 ? 4 : 2; }
 // The tcgen05 path takes 2-6 shared-memory stages of 128 keys plus the query
 // operand; its logits stay in shared memory when that leaves four stages.
 // fp32: the CUDA-core path.
-static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int ctas_per_sm, bool umma) {
+// lg_rows: rows of the logits buffer on the tcgen05 path (one window-summed
+// row per score row; Rq when not given).
+static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int ctas_per_sm, bool umma,
+                            int lg_rows = 0) {
   ScorePlan pl;
   pl.umma = umma && dtype != HC_F32 && Rq > 40;
   const int gran = pl.umma ? 128 : 32;
@@ -1885,8 +2028,9 @@ static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int cta
     while (pl.tmem_cols < 2 * pl.NP) pl.tmem_cols *= 2;
     // the stage ring shares memory with the later phases' arrays
     const size_t later = smem_bytes<float>(Rq, S, T_, pl.TB, false, false);
-    const size_t fixed = 1024 + (size_t)pl.NP * 256;
-    const size_t lgb = (with + 15) & ~(size_t)15;
+    const size_t fixed = 1024 + (size_t)umma_query_rows(Rq) * 256;
+    const size_t lgr = (size_t)(lg_rows > 0 ? lg_rows : Rq);
+    const size_t lgb = (lgr * pl.TB * es + 15) & ~(size_t)15;
     auto stages_for = [&](bool lsm) {
       const size_t used = fixed + (lsm ? lgb : 0);
       return used >= kDynSmemCap ? 0 : (int)min((size_t)kMaxStages, (kDynSmemCap - used) / kUStage);
@@ -1898,7 +2042,7 @@ static ScorePlan plan_score(int dtype, int n_jobs, int L, int Rq, int S, int cta
     const size_t total = fixed + (pl.logits_in_smem ? lgb : 0) + region;
     if (pl.n_stages >= 2 && total <= kDynSmemCap) {
       pl.smem = total;
-      pl.logits_bytes = pl.logits_in_smem ? 0 : (size_t)pl.grid * Rq * pl.TB * es;
+      pl.logits_bytes = pl.logits_in_smem ? 0 : (size_t)pl.grid * lgr * pl.TB * es;
       return pl;
     }
     pl.umma = false;  // no room: the legacy paths (128-token ranges are valid there too)
@@ -2041,14 +2185,17 @@ static int run_score(ScoreParams& p, void* ws, size_t ws_bytes, cudaStream_t st,
   // batch of 8 checks at 128K, the tcgen05 path's logits took 3.4x as long
   const bool umma = !f32 && !batch && key_tensor_maps(p, dtype, maps);
   // one 512-thread CTA per SM
-  ScorePlan pl = plan_score(dtype, p.n_jobs, p.L, p.Rq, p.S, 1, umma);
+  ScorePlan pl = plan_score(dtype, p.n_jobs, p.L, p.Rq, p.S, 1, umma, p.S * p.G);
   return launch_score<T>(p, pl, maps, ws, ws_bytes, st, batch);
 }
 
 // Large enough for either plan (whether the keys' tensor maps can be made is
 // known only at launch).
 size_t score_workspace_size(int dtype, int n_jobs, int L, int Rq, int S) {
-  const ScorePlan a = plan_score(dtype, n_jobs, L, Rq, S, 1, true);
+  // the tcgen05 plan's buffer holds between one and Rq rows (score rows are
+  // not known here): reserve Rq rows in global memory, whichever it picks
+  ScorePlan a = plan_score(dtype, n_jobs, L, Rq, S, 1, true);
+  if (a.umma) a.logits_bytes = (size_t)a.grid * Rq * a.TB * elem_size(dtype);
   const ScorePlan b = plan_score(dtype, n_jobs, L, Rq, S, 1, false);
   return max(score_ws_layout(n_jobs, a, Rq, L).total, score_ws_layout(n_jobs, b, Rq, L).total);
 }

@@ -11,7 +11,11 @@ benchmark:
   heads as pivots) at 131072 tokens, Llama-3.1-8B geometry, bf16, one launch;
 * ``drift_single``  -- hc_drift_check: one pivot at 131072 tokens;
 * ``prefill_attention`` -- hc_prefill_attention: causal, 32 query / 8 KV
-  heads, 8192 tokens, bf16.
+  heads, 8192 tokens, bf16;
+* ``prefill_select_w32`` -- hc_prefill_select with an observation window of
+  32 queries (128 query rows per KV head, the tcgen05 path): 5 compressed KV
+  heads of a Llama-3.1-8B layer at 131072 tokens, max-pool 7, keep 0.4 L,
+  bf16.
 """
 from __future__ import annotations
 
@@ -89,7 +93,32 @@ def prefill_attention(dev, reps):
     return int(err.item())
 
 
-CASES = {"drift_batch": drift_batch, "drift_single": drift_single, "prefill_attention": prefill_attention}
+def prefill_select_w32(dev, reps):
+    L, H, nc = L_DRIFT, KV * G, 5
+    gen = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(1, H, 64, D, device=dev, generator=gen).to(torch.bfloat16)
+    k = torch.randn(1, KV, L, D, device=dev, generator=gen).to(torch.bfloat16)
+    v = torch.randn(1, KV, L, D, device=dev, generator=gen).to(torch.bfloat16)
+    keep_len = int(0.4 * L)
+    keep = torch.full((nc,), keep_len, dtype=torch.int32, device=dev)
+    npg = (keep_len + 255) // 256
+    bt = torch.full((KV, L // 256 + 2), -1, dtype=torch.int32)
+    for h in range(nc):
+        bt[h, :npg] = torch.arange(h * npg, (h + 1) * npg, dtype=torch.int32)
+    bt = bt.to(dev)
+    kp = torch.zeros(nc * npg, 256, 1, D, dtype=torch.bfloat16, device=dev)
+    vp = torch.zeros_like(kp)
+    hl = torch.zeros(KV, dtype=torch.int32, device=dev)
+    ws, err = Workspace(dev), torch.zeros(1, dtype=torch.int32, device=dev)
+    for _ in range(reps):
+        ops.prefill_select(q, k, v, keep, keep_len, n_heads=nc, groups=G, window=32, pooling="maxpool",
+                           kernel_size=7, k_pool=kp, v_pool=vp, block_table=bt, heads_len=hl, workspace=ws, err=err)
+    torch.cuda.synchronize()
+    return int(err.item())
+
+
+CASES = {"drift_batch": drift_batch, "drift_single": drift_single, "prefill_attention": prefill_attention,
+         "prefill_select_w32": prefill_select_w32}
 
 
 def main():
