@@ -490,30 +490,32 @@ __device__ void logits_mma(const ScoreParams& p, const JobInfo& ji, T* lg, float
 //    16..127 of such a tile are left over from earlier tiles and discarded).
 //
 // The CTA's token range [t0, t1) is a multiple of 128 tokens from a
-// 128-aligned t0 (a tile never crosses a 256-token page).  Tiles are numbered
-// across the two passes (the sums pass's first tile follows the statistics
-// pass's last), so the ring's and the accumulators' mbarriers run on without
-// being initialised again.
+// 128-aligned t0 (a tile never crosses a 256-token page).
 //
-// Roles: warp 0 lane 0 issues the TMA loads (stages released by the MMA's
-// completion), warp 1 allocates the tensor memory and its lane 0 issues the
-// MMAs, warps 2-15 read the accumulators: a warp may only read the TMEM lanes
-// 32 * (warp % 4) .. + 31, so each lane quarter's work of a tile is dealt
-// round-robin over its three or four warps, and every one of the 14 warps
-// releases each accumulator.  Every wait is bounded; a wait that gives up
-// marks the launch failed (HC_ERR_TIMEOUT) and its role stops, the others run
-// out their own bounded waits, in-flight copies and MMAs are waited for
-// (bounded) and the tensor memory is released before the pass ends; after a
-// failed statistics pass the sums pass does nothing.
+// All 16 warps read the accumulators, four per TMEM lane quarter (a warp may
+// only read lanes 32 * (warp % 4) .. + 31), so every quarter's share of a
+// tile is split four ways.  There are no producer or MMA warps: at the start
+// of tile i (its MMAs seen complete) lane 0 of warp i % 16 refills tile i's
+// stage with tile i + NS, and lane 0 of warp (i + 8) % 16 issues the MMAs of
+// tile i + D into the accumulator that tile i + D - NB used, once every warp
+// has released it; with NB = 4 accumulators (where the tensor memory holds
+// them) D = 2, so the MMAs run two tiles ahead of the readers and wait for a
+// release two tiles old; with 2, D = 1.  Every wait is bounded; a wait that gives up
+// marks the launch failed (HC_ERR_TIMEOUT) and the warps stop, copies and
+// MMAs still in flight are waited for (bounded) and the tensor memory is
+// released before the pass ends; after a failed statistics pass the sums
+// pass does nothing.  Each pass initialises its own mbarriers (the previous
+// pass's copies, MMAs and arrivals have all completed).
 constexpr int kUStage = 2 * 128 * 128;  // bytes of one stage: two 128-row x 128-byte boxes
 constexpr int kMaxStages = 6;
 constexpr int kUBox = 128 * 128;
-constexpr int kUEpi = kSWarps - 2;  // accumulator readers (warps 2-15)
+
+constexpr int kUAcc = 4;  // tensor-memory accumulators at most
 
 struct UmmaSmem {
-  uint64_t full[kMaxStages], empty[kMaxStages], accf[2], acce[2];
+  uint64_t full[kMaxStages], accf[kUAcc], acce[kUAcc];
   uint32_t tmem;
-  int issued, consumed, fail;
+  int issued, consumed, mma_last, fail;
   int pages[kMaxPages];  // drift checks: page ids of the CTA's keys
 };
 
@@ -576,13 +578,11 @@ __device__ void umma_pass(const ScoreParams& p, const JobInfo& ji, T* lg, unsign
   const int NS = p.n_stages, NP = p.NP, Rq = p.Rq;
   const int QR = umma_query_rows(Rq);
   const int nrb = QR >> 7;  // 128-row blocks of query rows
-  auto quarter_warps = [](int q) { return q < 2 ? 3 : 4; };
   const int lo = max(0, ji.t0 - kMargin), hi = min(p.L, ji.t1 + kMargin);
   constexpr bool kMargins = PASS == PASS_SUMS;
   const bool left = kMargins && ji.t0 > 0, right = kMargins && ji.t1 < p.L;
   const int nmain = (ji.t1 - ji.t0 + 127) >> 7;
   const int ntiles = (left ? 1 : 0) + nmain + (right ? 1 : 0);
-  const int tile0 = PASS == PASS_SUMS ? nmain : 0;  // the statistics pass's tiles come first
   auto tile_of = [&](int i, int& start, int& rows) {
     if (left) {
       if (i == 0) { start = ji.t0 - kMargin; rows = kMargin; return; }
@@ -592,21 +592,32 @@ __device__ void umma_pass(const ScoreParams& p, const JobInfo& ji, T* lg, unsign
     start = ji.t1;
     rows = kMargin;
   };
-  // accumulator columns: two buffers of 128 columns per row block (statistics)
-  // or of NP columns (sums)
+  // accumulators: NB buffers of 128 columns per row block (statistics) or of
+  // NP columns (sums), as many as the 512 columns hold up to kUAcc and no
+  // more than the stages (so that an MMA's keys were requested a tile ago)
   const int acc_cols = PASS == PASS_STATS ? QR : NP;
-  const uint32_t ncols = PASS == PASS_STATS ? (nrb == 1 ? 256u : 512u) : (uint32_t)p.tmem_cols;
-  // ---- set-up: barriers first, so that the key stream starts at once
-  if (PASS == PASS_STATS && threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(&u.full[s], 1);
-      mbar_init(&u.empty[s], 1);
+  const int NB = min(min(kUAcc, 512 / acc_cols), NS);
+  uint32_t ncols = 32;
+  while (ncols < (uint32_t)(NB * acc_cols)) ncols <<= 1;
+  // ---- set-up: this pass's barriers
+  if (threadIdx.x == 0) {
+    if (PASS == PASS_SUMS) {
+      // retire the statistics pass's barriers (its accumulator count)
+      const int nb_a = min(min(kUAcc, 512 / QR), NS);
+      for (int s = 0; s < NS; ++s) mbar_inval(&u.full[s]);
+      for (int b = 0; b < nb_a; ++b) {
+        mbar_inval(&u.accf[b]);
+        mbar_inval(&u.acce[b]);
+      }
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int s = 0; s < NS; ++s) mbar_init(&u.full[s], 1);
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&u.accf[b], 1);
-      mbar_init(&u.acce[b], kUEpi);
+      mbar_init(&u.acce[b], kSWarps);
     }
-    u.issued = u.consumed = u.fail = 0;
+    if (PASS == PASS_STATS) u.fail = 0;
+    u.issued = u.consumed = 0;
+    u.mma_last = -1;
     fence_mbar_init();
   }
   // the ring held the statistics pass's row pairs (generic stores) before the
@@ -615,17 +626,14 @@ __device__ void umma_pass(const ScoreParams& p, const JobInfo& ji, T* lg, unsign
   __syncthreads();
   if (PASS == PASS_SUMS && u.fail) return;  // the statistics pass gave up (block-uniform)
 
-  uint32_t tmem = 0;
-  float rm[2] = {-INFINITY, -INFINITY}, rs[2] = {0.f, 0.f};  // statistics: (max, sum) per row block
-  if (warp == 0) {
-    // ---- TMA producer.  Drift checks: the page ids of the CTA's keys first,
-    // loaded by the whole warp at once (kMaxPages of them; beyond that each
-    // tile reads its own)
-    int npg = 0, pg0 = 0;
-    if constexpr (MODE == MODE_DRIFT) {
-      pg0 = lo >> 8;
-      npg = ((hi - 1) >> 8) - pg0 + 1;
-      if (npg <= kMaxPages) {
+  // drift checks: the page ids of the CTA's keys, loaded by warp 0 at once
+  // (kMaxPages of them; beyond that each tile reads its own)
+  int npg = 0, pg0 = 0;
+  if constexpr (MODE == MODE_DRIFT) {
+    pg0 = lo >> 8;
+    npg = ((hi - 1) >> 8) - pg0 + 1;
+    if (npg <= kMaxPages) {
+      if (warp == 0) {
         const int row = ji.b * p.KV + ji.h;
         for (int j = lane; j < npg; j += 32) {
           int blk = p.bt[(int64_t)row * p.max_blocks + pg0 + j];
@@ -635,246 +643,262 @@ __device__ void umma_pass(const ScoreParams& p, const JobInfo& ji, T* lg, unsign
           }
           u.pages[j] = blk;
         }
+        __syncwarp();
+      }
+    } else {
+      npg = 0;
+    }
+  }
+  // thread 0: TMA copies of tile i into its stage
+  auto load_tile = [&](int i) {
+    const int s = i % NS;
+    int start, rows;
+    tile_of(i, start, rows);
+    const CUtensorMap* m = rows == 128 ? tm_rows : tm_edge;
+    unsigned char* dst = stages + (size_t)s * kUStage;
+    const uint64_t pol = l2_evict_first_policy();
+    mbar_arrive_expect_tx(&u.full[s], (uint32_t)rows * 256u);
+    if constexpr (MODE == MODE_DRIFT) {
+      int blk;
+      if (npg) {
+        blk = u.pages[min((start >> 8) - pg0, npg - 1)];
       } else {
-        npg = 0;
-      }
-      __syncwarp();
-    }
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first_policy();
-      int i = 0;
-      for (; i < ntiles; ++i) {
-        const int g = tile0 + i, s = g % NS;
-        if (!mbar_wait_sleep(&u.empty[s], ((g / NS) & 1) ^ 1, p.wait_ns)) {
-          atomicExch(&u.fail, 1);
-          break;
-        }
-        int start, rows;
-        tile_of(i, start, rows);
-        const CUtensorMap* m = rows == 128 ? tm_rows : tm_edge;
-        unsigned char* dst = stages + (size_t)s * kUStage;
-        mbar_arrive_expect_tx(&u.full[s], (uint32_t)rows * 256u);
-        if constexpr (MODE == MODE_DRIFT) {
-          int blk;
-          if (npg) {
-            blk = u.pages[min((start >> 8) - pg0, npg - 1)];
-          } else {
-            blk = p.bt[(int64_t)(ji.b * p.KV + ji.h) * p.max_blocks + (start >> 8)];
-            if (blk < 0 || blk >= p.n_blocks) {  // reported; read page 0 instead
-              set_err(p.err, HC_ERR_RANGE);
-              blk = 0;
-            }
-          }
-          const int y = blk * kPage + (start & (kPage - 1));
-          tma_load_2d(dst, m, 0, y, &u.full[s], pol);
-          tma_load_2d(dst + kUBox, m, 64, y, &u.full[s], pol);
-        } else {
-          tma_load_4d(dst, m, 0, start, ji.h, ji.b, &u.full[s], pol);
-          tma_load_4d(dst + kUBox, m, 64, start, ji.h, ji.b, &u.full[s], pol);
+        blk = p.bt[(int64_t)(ji.b * p.KV + ji.h) * p.max_blocks + (start >> 8)];
+        if (blk < 0 || blk >= p.n_blocks) {  // reported; read page 0 instead
+          set_err(p.err, HC_ERR_RANGE);
+          blk = 0;
         }
       }
-      u.issued = tile0 + i;
+      const int y = blk * kPage + (start & (kPage - 1));
+      tma_load_2d(dst, m, 0, y, &u.full[s], pol);
+      tma_load_2d(dst + kUBox, m, 64, y, &u.full[s], pol);
+    } else {
+      tma_load_4d(dst, m, 0, start, ji.h, ji.b, &u.full[s], pol);
+      tma_load_4d(dst + kUBox, m, 64, start, ji.h, ji.b, &u.full[s], pol);
     }
-  } else {
-    // ---- tensor memory and (first pass) the query operand, while the first
-    // tiles load
-    if (warp == 1) {
-      tmem_alloc(&u.tmem, ncols);
-      if (PASS == PASS_SUMS) tmem_relinquish();  // the CTA's last allocation
+    u.issued = i + 1;
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(ntiles, NS); ++i) load_tile(i);
+  // tensor memory and (first pass) the query operand, while the first tiles load
+  if (warp == 1) {
+    tmem_alloc(&u.tmem, ncols);
+    if (PASS == PASS_SUMS) tmem_relinquish();  // the CTA's last allocation
+  }
+  if (PASS == PASS_STATS) {
+    // query rows: QR rows x 128 dims, K-major, 128-byte swizzle, rows past
+    // Rq zero; the two 64-dim halves QR * 128 bytes apart
+    for (int i = threadIdx.x; i < QR * 16; i += kSThreads) {
+      const int r = i >> 4, c16 = i & 15;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < Rq) v = ldg128(query_row<T>(p, ji, r) + 8 * c16);
+      *reinterpret_cast<uint4*>(qop + (c16 >> 3) * (QR * 128) + swz128(r, c16 & 7)) = v;
     }
-    if (PASS == PASS_STATS) {
-      // query rows: QR rows x 128 dims, K-major, 128-byte swizzle, rows past
-      // Rq zero; the two 64-dim halves QR * 128 bytes apart
-      for (int i = threadIdx.x - 32; i < QR * 16; i += kSThreads - 32) {
-        const int r = i >> 4, c16 = i & 15;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (r < Rq) v = ldg128(query_row<T>(p, ji, r) + 8 * c16);
-        *reinterpret_cast<uint4*>(qop + (c16 >> 3) * (QR * 128) + swz128(r, c16 & 7)) = v;
-      }
-      fence_proxy_async_smem();
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = u.tmem;
+  // thread 0: the MMAs of tile i into its accumulator, once its keys are in
+  const uint32_t idesc =
+      idesc_f16_m128(std::is_same<T, __nv_bfloat16>::value, PASS == PASS_STATS ? 128 : NP);
+  auto issue_mma = [&](int i) {
+    const int s = i % NS, b = i % NB;
+    if (!mbar_wait(&u.full[s], (i / NS) & 1, p.wait_ns)) {
+      atomicExch(&u.fail, 1);
+      return;
     }
-    tc_fence_before();
-    named_bar_sync(1, kSThreads - 32);
+    u.consumed = i + 1;
     tc_fence_after();
-    tmem = u.tmem;
-    if (warp == 1) {
-      // ---- MMA issuer
-      if (lane == 0) {
-        const bool bf = std::is_same<T, __nv_bfloat16>::value;
-        const uint32_t idesc = idesc_f16_m128(bf, PASS == PASS_STATS ? 128 : NP);
-        const uint32_t q0 = smem_u32(qop);
-        int i = 0;
-        for (; i < ntiles; ++i) {
-          const int g = tile0 + i, s = g % NS, b = g & 1;
-          if (!mbar_wait_sleep(&u.full[s], (g / NS) & 1, p.wait_ns)) {
-            atomicExch(&u.fail, 1);
-            break;
-          }
-          u.consumed = g + 1;
-          if (!mbar_wait_sleep(&u.acce[b], ((g >> 1) & 1) ^ 1, p.wait_ns)) {
-            atomicExch(&u.fail, 1);
-            break;
-          }
-          tc_fence_after();
-          const uint32_t k0 = smem_u32(stages + (size_t)s * kUStage);
-          const uint32_t d = tmem + (uint32_t)(b * acc_cols);
-          if (PASS == PASS_STATS) {
-            for (int rb = 0; rb < nrb; ++rb) {
+    const uint32_t q0 = smem_u32(qop);
+    const uint32_t k0 = smem_u32(stages + (size_t)s * kUStage);
+    const uint32_t d = tmem + (uint32_t)(b * acc_cols);
+    if (PASS == PASS_STATS) {
+      for (int rb = 0; rb < nrb; ++rb) {
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t ao = q0 + (kk >> 2) * (QR * 128) + rb * (128 * 128) + (kk & 3) * 32;
-                const uint32_t bo = k0 + (kk >> 2) * kUBox + (kk & 3) * 32;
-                umma_f16(d + (uint32_t)(rb * 128), smem_desc_sw128(ao), smem_desc_sw128(bo), idesc,
-                         kk > 0 ? 1u : 0u);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint32_t ao = k0 + (kk >> 2) * kUBox + (kk & 3) * 32;
-              const uint32_t bo = q0 + (kk >> 2) * (QR * 128) + (kk & 3) * 32;
-              umma_f16(d, smem_desc_sw128(ao), smem_desc_sw128(bo), idesc, kk > 0 ? 1u : 0u);
-            }
-          }
-          umma_commit(&u.empty[s]);
-          umma_commit(&u.accf[b]);
-        }
-        // every MMA issued has completed before the tensor memory is released
-        if (i > 0) {
-          const int g = tile0 + i - 1;
-          (void)mbar_wait_sleep(&u.accf[g & 1], (g >> 1) & 1, p.wait_ns);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ao = q0 + (kk >> 2) * (QR * 128) + rb * (128 * 128) + (kk & 3) * 32;
+          const uint32_t bo = k0 + (kk >> 2) * kUBox + (kk & 3) * 32;
+          umma_f16(d + (uint32_t)(rb * 128), smem_desc_sw128(ao), smem_desc_sw128(bo), idesc, kk > 0 ? 1u : 0u);
         }
       }
     } else {
-      // ---- accumulator readers
-      const int q4 = warp & 3;
-      const int k = q4 < 2 ? (warp >> 2) - 1 : (warp >> 2);  // index among the quarter's warps
-      const int m = quarter_warps(q4);
-      const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
-      // launch constants in registers (the loops store through pointers the
-      // compiler cannot separate from the parameter block)
-      const int W = p.W, L = p.L, TB = p.TB, t1 = ji.t1;
-      const float sqd = p.sqrt_d, r_sqrt = __frcp_rn(sqd);
-      for (int i = 0; i < ntiles; ++i) {
-        const int g = tile0 + i, b = g & 1;
-        int start, rows;
-        tile_of(i, start, rows);
-        const bool ok = mbar_wait_sleep(&u.accf[b], (g >> 1) & 1, p.wait_ns);
-        if (!ok) atomicExch(&u.fail, 1);
-        tc_fence_after();
-        if (ok && PASS == PASS_STATS) {
-          // work items (row block, 32-token chunk), dealt over the quarter's warps
-          for (int it = k; it < 4 * nrb; it += m) {
-            const int rb = it >> 2, kc = it & 3;
-            if (rb * 128 + 32 * q4 >= Rq) continue;  // no row on this warp's lanes (warp-uniform)
-            const int qi = rb * 128 + 32 * q4 + lane;
-            uint32_t v[32];
-            tmem_ld32(tmem + lane_off + (uint32_t)(b * acc_cols + rb * 128 + 32 * kc), v);
-            tmem_ld_wait();
-            float x[4][8];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) x[j >> 3][j & 7] = __uint_as_float(v[j]);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) scale_logit8<T>(x[c], sqd, r_sqrt);
-            // tokens counted: the CTA's own (t < t1) that the row may see (in
-            // an observation window row qi = sg * W + w sees t <= L - W + w)
-            const int tk = start + 32 * kc;
-            const int lim = W > 1 ? min(t1, L - W + qi % W + 1) : t1;
-            if (tk + 32 > lim) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (tk + j >= lim) x[j >> 3][j & 7] = -INFINITY;
-            }
-            float cm = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) cm = fmaxf(cm, x[j >> 3][j & 7]);
-            if (cm != -INFINITY) {
-              float& M = rm[rb];
-              float& S = rs[rb];
-              if (cm > M) {
-                S *= exp2_approx((M - cm) * kLog2e);  // 0 while M is still -inf
-                M = cm;
-              }
-              // exp(x - M) as 2^(x log2 e - M log2 e), one multiply-add each
-              const float nm = -M * kLog2e;
-              float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-              for (int j = 0; j < 32; ++j) s4[j & 3] += exp2_approx(fmaf(x[j >> 3][j & 7], kLog2e, nm));
-              S += (s4[0] + s4[1]) + (s4[2] + s4[3]);
-            }
-          }
-        } else if (ok) {
-          // sums: thread = token; the quarter's warps take score rows sg = k,
-          // k + m, ... (window columns sg * W .. + W - 1)
-          const int r = 32 * q4 + lane;
-          const int t = start + r;
-          const bool valid = r < rows && t >= lo && t < hi;
-          const int nsg = Rq / W;
-          const int base = ji.t0 - kMargin;
-          // per-column checks only where a chunk straddles a window's edge
-          // (W not a multiple of 8) or a token of the tile is masked for
-          // some row (t > L - W); tile-uniform
-          const bool checked = (W & 7) != 0 || (W > 1 && start + rows - 1 > L - W);
-          for (int sg = k; sg < nsg; sg += m) {
-            const int c0 = sg * W, c1 = c0 + W;
-            float acc = 0.f;
-            for (int cb = c0 & ~7; cb < c1; cb += 32) {
-              // up to four 8-column loads in flight per wait
-              const int nl = min(4, (c1 - cb + 7) >> 3);
-              uint32_t v[4][8];
-#pragma unroll
-              for (int c = 0; c < 4; ++c)
-                if (c < nl) tmem_ld8(tmem + lane_off + (uint32_t)(b * acc_cols + cb + 8 * c), v[c]);
-              tmem_ld_wait();
-              if (valid) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                  if (c >= nl) break;
-                  float x[8];
-#pragma unroll
-                  for (int j = 0; j < 8; ++j) x[j] = __uint_as_float(v[c][j]);
-                  scale_logit8<T>(x, sqd, r_sqrt);
-                  const int q8 = cb + 8 * c;  // first query row of the chunk (8-aligned)
-                  const float4 Ma = *reinterpret_cast<const float4*>(s_rowM + q8);
-                  const float4 Mb = *reinterpret_cast<const float4*>(s_rowM + q8 + 4);
-                  const float4 Ra = *reinterpret_cast<const float4*>(s_rowR + q8);
-                  const float4 Rb = *reinterpret_cast<const float4*>(s_rowR + q8 + 4);
-                  const float Mv[8] = {Ma.x, Ma.y, Ma.z, Ma.w, Mb.x, Mb.y, Mb.z, Mb.w};
-                  const float Rv[8] = {Ra.x, Ra.y, Ra.z, Ra.w, Rb.x, Rb.y, Rb.z, Rb.w};
-                  float pr[8];
-#pragma unroll
-                  for (int j = 0; j < 8; ++j) pr[j] = softmax_prob<T>(x[j], Mv[j], s_rowS[q8 + j], Rv[j]);
-                  if (checked) {
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                      const int qi = q8 + j;
-                      // outside this window, or masked: no contribution
-                      if (qi < c0 || qi >= c1 || (W > 1 && t > L - W + (qi - c0))) pr[j] = 0.f;
-                    }
-                  }
-#pragma unroll
-                  for (int j = 0; j < 8; j += 2) Elem<T>::rnd2(pr[j], pr[j + 1]);
-#pragma unroll
-                  for (int j = 0; j < 8; ++j) acc += pr[j];
-                }
-              }
-            }
-            if (valid) lg[(int64_t)sg * TB + (t - base)] = Elem<T>::from_f(acc);
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&u.acce[b]);
-        if (!ok) break;
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t ao = k0 + (kk >> 2) * kUBox + (kk & 3) * 32;
+        const uint32_t bo = q0 + (kk >> 2) * (QR * 128) + (kk & 3) * 32;
+        umma_f16(d, smem_desc_sw128(ao), smem_desc_sw128(bo), idesc, kk > 0 ? 1u : 0u);
       }
     }
+    umma_commit(&u.accf[b]);
+    u.mma_last = i;
+  };
+  // MMAs run D tiles ahead of the tile being read: the first D now
+  const int D = max(1, NB - 2);
+  if (threadIdx.x == 0)
+    for (int i = 0; i < min(ntiles, D) && !u.fail; ++i) issue_mma(i);
+
+  // ---- every warp: read the accumulators tile by tile
+  const int q4 = warp & 3, k = warp >> 2;  // lane quarter, index among its four warps
+  const uint32_t lane_off = (uint32_t)(32 * q4) << 16;
+  // launch constants in registers (the loops store through pointers the
+  // compiler cannot separate from the parameter block)
+  const int W = p.W, L = p.L, TB = p.TB, t1 = ji.t1;
+  const float sqd = p.sqrt_d, r_sqrt = __frcp_rn(sqd);
+  float rm[2] = {-INFINITY, -INFINITY}, rs[2] = {0.f, 0.f};  // statistics: (max, sum) per row block
+  for (int i = 0; i < ntiles; ++i) {
+    const int b = i % NB;
+    int start, rows;
+    tile_of(i, start, rows);
+    const bool ok = mbar_wait_sleep(&u.accf[b], (i / NB) & 1, p.wait_ns);
+    if (!ok) atomicExch(&u.fail, 1);
+    tc_fence_after();
+    // the duties of tile i rotate over the warps (issuing a tile's copies or
+    // MMAs takes a fraction of a microsecond of one thread, which would
+    // otherwise hold back one warp on every tile):
+    if (ok && lane == 0) {
+      // warp i % 16: tile i's MMAs have read its stage, refill it with tile
+      // i + NS
+      if (warp == (i & (kSWarps - 1)) && i + NS < ntiles) load_tile(i + NS);
+      // warp (i + 8) % 16: the MMAs of tile i + D into the accumulator tile
+      // i + D - NB used, once every warp has released it (D tiles ahead, so
+      // that the wait is for a tile the slowest warp finished a while ago)
+      const int j = i + D;
+      if (warp == ((i + kSWarps / 2) & (kSWarps - 1)) && j < ntiles) {
+        const int r = j - NB;
+        if (r >= 0 && !mbar_wait(&u.acce[r % NB], (r / NB) & 1, p.wait_ns)) {
+          atomicExch(&u.fail, 1);
+        } else {
+          tc_fence_after();
+          issue_mma(j);
+        }
+      }
+    }
+    if (ok && PASS == PASS_STATS) {
+      // work items (row block, 32-token chunk), dealt over the quarter's warps
+      for (int it = k; it < 4 * nrb; it += 4) {
+        const int rb = it >> 2, kc = it & 3;
+        if (rb * 128 + 32 * q4 >= Rq) continue;  // no row on this warp's lanes (warp-uniform)
+        const int qi = rb * 128 + 32 * q4 + lane;
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + (uint32_t)(b * acc_cols + rb * 128 + 32 * kc), v);
+        tmem_ld_wait();
+        float x[4][8];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) x[j >> 3][j & 7] = __uint_as_float(v[j]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) scale_logit8<T>(x[c], sqd, r_sqrt);
+        // tokens counted: the CTA's own (t < t1) that the row may see (in an
+        // observation window row qi = sg * W + w sees t <= L - W + w)
+        const int tk = start + 32 * kc;
+        const int lim = W > 1 ? min(t1, L - W + qi % W + 1) : t1;
+        if (tk + 32 > lim) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (tk + j >= lim) x[j >> 3][j & 7] = -INFINITY;
+        }
+        // the chunk's max as a tree (short dependency chains)
+        float m8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m8[j] = fmaxf(fmaxf(x[0][j], x[1][j]), fmaxf(x[2][j], x[3][j]));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m8[j] = fmaxf(m8[j], m8[j + 4]);
+        const float cm = fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3]));
+        if (cm != -INFINITY) {
+          float& M = rm[rb];
+          float& S = rs[rb];
+          if (cm > M) {
+            S *= exp2_approx((M - cm) * kLog2e);  // 0 while M is still -inf
+            M = cm;
+          }
+          // exp(x - M) as 2^(x log2 e - M log2 e), one multiply-add each
+          const float nm = -M * kLog2e;
+          float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 32; ++j) s4[j & 3] += exp2_approx(fmaf(x[j >> 3][j & 7], kLog2e, nm));
+          S += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        }
+      }
+    } else if (ok) {
+      // sums: thread = token; the quarter's warps take score rows sg = k,
+      // k + 4, ... (window columns sg * W .. + W - 1)
+      const int r = 32 * q4 + lane;
+      const int t = start + r;
+      const bool valid = r < rows && t >= lo && t < hi;
+      const int nsg = Rq / W;
+      const int base = ji.t0 - kMargin;
+      // per-column checks only where a chunk straddles a window's edge (W not
+      // a multiple of 8) or a token of the tile is masked for some row
+      // (t > L - W); tile-uniform
+      const bool checked = (W & 7) != 0 || (W > 1 && start + rows - 1 > L - W);
+      for (int sg = k; sg < nsg; sg += 4) {
+        const int c0 = sg * W, c1 = c0 + W;
+        float acc = 0.f;
+        for (int cb = c0 & ~7; cb < c1; cb += 32) {
+          // 32 columns in one load where they lie in the window, else up to
+          // four 8-column loads; one wait
+          const int nl = min(4, (c1 - cb + 7) >> 3);
+          uint32_t v[4][8];
+          if (nl == 4 && cb >= c0) {
+            tmem_ld32(tmem + lane_off + (uint32_t)(b * acc_cols + cb), &v[0][0]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              if (c < nl) tmem_ld8(tmem + lane_off + (uint32_t)(b * acc_cols + cb + 8 * c), v[c]);
+          }
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              if (c >= nl) break;
+              float x[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) x[j] = __uint_as_float(v[c][j]);
+              scale_logit8<T>(x, sqd, r_sqrt);
+              const int q8 = cb + 8 * c;  // first query row of the chunk (8-aligned)
+              const float4 Ma = *reinterpret_cast<const float4*>(s_rowM + q8);
+              const float4 Mb = *reinterpret_cast<const float4*>(s_rowM + q8 + 4);
+              const float4 Ra = *reinterpret_cast<const float4*>(s_rowR + q8);
+              const float4 Rb = *reinterpret_cast<const float4*>(s_rowR + q8 + 4);
+              const float Mv[8] = {Ma.x, Ma.y, Ma.z, Ma.w, Mb.x, Mb.y, Mb.z, Mb.w};
+              const float Rv[8] = {Ra.x, Ra.y, Ra.z, Ra.w, Rb.x, Rb.y, Rb.z, Rb.w};
+              float pr[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) pr[j] = softmax_prob<T>(x[j], Mv[j], s_rowS[q8 + j], Rv[j]);
+              if (checked) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const int qi = q8 + j;
+                  // outside this window, or masked: no contribution
+                  if (qi < c0 || qi >= c1 || (W > 1 && t > L - W + (qi - c0))) pr[j] = 0.f;
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 8; j += 2) Elem<T>::rnd2(pr[j], pr[j + 1]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc += pr[j];
+            }
+          }
+        }
+        if (valid) lg[(int64_t)sg * TB + (t - base)] = Elem<T>::from_f(acc);
+      }
+    }
+    // release the accumulator
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&u.acce[b]);
+    if (!ok) break;
   }
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0 && u.fail) {
     set_err(p.err, HC_ERR_TIMEOUT);
-    // copies still in flight land before the stages can be reused
+    // copies still in flight land before the stages can be reused, and the
+    // last MMAs issued into each accumulator complete before it is released
     for (int i = u.consumed; i < u.issued; ++i) (void)mbar_wait_sleep(&u.full[i % NS], (i / NS) & 1, p.wait_ns);
+    for (int i = max(0, u.mma_last - NB + 1); i <= u.mma_last; ++i)
+      (void)mbar_wait_sleep(&u.accf[i % NB], (i / NB) & 1, p.wait_ns);
   }
   __syncthreads();
   if (warp == 1) {
@@ -882,22 +906,18 @@ __device__ void umma_pass(const ScoreParams& p, const JobInfo& ji, T* lg, unsign
     tmem_dealloc(tmem, ncols);
   }
   if (PASS == PASS_STATS) {
-    // the ring is idle: each reader warp's row pairs, then per row the merge
-    // of its quarter's warps in warp order into the CTA's partial
-    if (warp >= 2) {
-      const int q4 = warp & 3;
-      const int k = q4 < 2 ? (warp >> 2) - 1 : (warp >> 2);
-      for (int rb = 0; rb < nrb; ++rb) {
-        const int qi = rb * 128 + 32 * q4 + lane;
-        if (qi < Rq) wpart[k * kMaxRq + qi] = make_float2(rm[rb], rs[rb]);
-      }
+    // the ring is idle: each warp's row pairs, then per row the merge of its
+    // quarter's four warps in warp order into the CTA's partial
+    for (int rb = 0; rb < nrb; ++rb) {
+      const int qi = rb * 128 + 32 * q4 + lane;
+      if (qi < Rq) wpart[k * kMaxRq + qi] = make_float2(rm[rb], rs[rb]);
     }
     __syncthreads();
     for (int qi = threadIdx.x; qi < Rq; qi += kSThreads) {
-      const int mq = quarter_warps((qi & 127) >> 5);
       float M = -INFINITY, S = 0.f;
-      for (int k = 0; k < mq; ++k) {
-        const float2 v = wpart[k * kMaxRq + qi];
+#pragma unroll
+      for (int kw = 0; kw < 4; ++kw) {
+        const float2 v = wpart[kw * kMaxRq + qi];
         online_merge<T>(M, S, v.x, v.y);
       }
       p.part[((size_t)ji.job * p.Rq + qi) * p.cpj + ji.part] = make_float2(M, S);
