@@ -647,7 +647,71 @@ def run_ours(args, rank, world, local_rank):
                 "e2e": e2e, "gpu_launches": launches, "clocks": clk}
         if head_sharded is not None:
             line["head_sharded"] = head_sharded
+        if not args.no_cpu:
+            line["offline_profiler"] = measure_offline_profiler(dev)
         print(json.dumps(line), flush=True)
+
+
+def measure_offline_profiler(dev, reps=20):
+    """The offline head profiler's per-dump work (tools/get_cluster.py:13-60,
+    :62-69) on the GPU -- top-k bitmaps of every head's last attention row
+    (hc_profile_topk) and the overlaps of a step (diagonal with the prefill
+    sets and all pairs, hc_profile_overlap) -- against the same work with the
+    torch CPU ops the reference calls (mean, avg_pool1d, topk, Python sets),
+    on dumps of 32 query heads (8 KV heads) at two sizes: the reference's
+    defaults (5000 positions, top 1024) and a 131072-token context (top 20%)."""
+    import torch.nn.functional as F
+    from heterocache_b200 import ops
+    from heterocache_b200.ops import Workspace
+    out = {}
+    for label, L, topk, dt in (("5000 positions, top 1024, fp16", 5000, 1024, torch.float16),
+                               ("131072 positions, top 26214, bf16", 131072, 26214, torch.bfloat16)):
+        gen = torch.Generator().manual_seed(L)
+        attn = torch.softmax(torch.randn(1, 32, 1, L + 1, generator=gen) * 3, dim=-1).to(dt)
+        base_attn = torch.softmax(torch.randn(1, 32, 1, L + 1, generator=gen) * 3, dim=-1).to(dt)
+        ad, bd = attn.to(dev), base_attn.to(dev)
+        ws = Workspace(dev)
+
+        def gpu_once():
+            bits = ops.profile_topk(ad, groups=4, topk=topk, max_length=L, workspace=ws)
+            base = ops.profile_topk(bd, groups=4, topk=topk, max_length=L, workspace=ws)
+            a2, b2 = bits.view(8, -1), base.view(8, -1)
+            ops.profile_overlap(b2, a2, diagonal=True)
+            ops.profile_overlap(a2, a2, diagonal=False)
+        for _ in range(3):
+            gpu_once()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gpu_once()
+        e1.record()
+        torch.cuda.synchronize()
+        gpu_us = e0.elapsed_time(e1) * 1e3 / reps
+
+        def cpu_once():
+            sets = []
+            for t in (attn, base_attn):
+                rows = torch.mean(t.view(1, 8, 4, -1, L + 1), dim=2)
+                hs = []
+                for h in range(8):
+                    vec = F.avg_pool1d(rows[:, h, -1:, :L].sum(-2).float(), kernel_size=5, padding=2, stride=1)
+                    hs.append(set(torch.topk(vec, topk, dim=-1).indices[0].tolist()))
+                sets.append(hs)
+            a, b = sets
+            [len(a[h] & b[h]) for h in range(8)]
+            [[len(a[i] & a[j]) for j in range(8)] for i in range(8)]
+        cpu_once()
+        n_cpu = 3
+        t0 = time.perf_counter()
+        for _ in range(n_cpu):
+            cpu_once()
+        cpu_us = (time.perf_counter() - t0) * 1e6 / n_cpu
+        out[label] = {"gpu_us_per_two_dumps": gpu_us, "cpu_us_per_two_dumps": cpu_us,
+                      "cpu_threads": torch.get_num_threads(),
+                      "work": "two dumps' top-k sets (8 GQA-mean rows each) + their diagonal and all-pairs "
+                              "overlaps"}
+    return out
 
 
 class PhaseGraphs:

@@ -71,6 +71,11 @@ SIGNATURES = {
                                   c_int, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64,
                                   c_int64, c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                   c_void_p, c_int64, c_void_p, c_void_p]),
+    "hc_profile_topk_workspace_size": (c_size_t, [c_int, c_int, c_int]),
+    "hc_profile_topk": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_int64, c_int64,
+                                c_int64, c_int, c_int, c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
+    "hc_profile_overlap": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_int64, c_int, c_int64, c_int, c_void_p,
+                                   c_void_p]),
 }
 
 

@@ -649,4 +649,44 @@ int hc_retrieve_delta(int dtype, int num_kv_heads, int head_dim, int n_members, 
                                                stage_v, stage_src, stage_rows, err_flag, (cudaStream_t)stream));
 }
 
+size_t hc_profile_topk_workspace_size(int bsz, int effective_heads, int use_len) {
+  if (bsz <= 0 || effective_heads <= 0 || use_len <= 0) return 0;
+  return hc::profile_topk_ws_bytes(bsz * effective_heads, use_len + 1);
+}
+
+int hc_profile_topk(int dtype, int bsz, int saved_heads, int groups, int q_len, int seq_len, const void* attn,
+                    int64_t sb, int64_t sh, int64_t sq, int64_t st, int use_len, int topk, uint32_t* bitmaps,
+                    int64_t words, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
+  if (bsz < 0 || saved_heads <= 0 || groups <= 0 || saved_heads % groups != 0 || q_len <= 0 || seq_len < 0 ||
+      use_len < 0 || use_len > seq_len || topk < 0 || words < 0)
+    return HC_ERR_INVALID;
+  const int He = saved_heads / groups;
+  const int64_t rows = (int64_t)bsz * He;
+  if (rows == 0) return HC_OK;
+  if (!bitmaps) return HC_ERR_INVALID;
+  if (rows > 0x7fffffff) return HC_ERR_INVALID;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (use_len == 0) {  // every set empty
+    if (words == 0) return HC_OK;
+    return note_cuda(cudaMemsetAsync(bitmaps, 0, (size_t)rows * words * sizeof(uint32_t), s) == cudaSuccess
+                         ? HC_OK : HC_ERR_CUDA);
+  }
+  const int ksz = use_len < 5 ? use_len : 5;
+  const int plen = use_len + 2 * (ksz / 2) - ksz + 1;
+  if (words < (plen + 31) / 32) return HC_ERR_INVALID;
+  if (!attn || sb <= 0 || sh <= 0 || sq <= 0 || st <= 0) return HC_ERR_INVALID;
+  return note_cuda(hc::profile_topk_dispatch(dtype, attn, sb, sh, sq, st, q_len - 1, bsz, He, groups, use_len, topk,
+                                             bitmaps, words, workspace, workspace_bytes, s));
+}
+
+int hc_profile_overlap(const uint32_t* a, int64_t a_stride, int na, const uint32_t* b, int64_t b_stride, int nb,
+                       int64_t words, int diagonal, int32_t* counts, void* stream) {
+  if (na < 0 || nb < 0 || words < 0 || (diagonal && na != nb)) return HC_ERR_INVALID;
+  if (na == 0 || nb == 0) return HC_OK;
+  if (!a || !b || !counts || a_stride < words || b_stride < words) return HC_ERR_INVALID;
+  return note_cuda(hc::profile_overlap_dispatch(a, a_stride, na, b, b_stride, nb, words, diagonal, counts,
+                                                (cudaStream_t)stream));
+}
+
 }  // extern "C"

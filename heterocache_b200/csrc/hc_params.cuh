@@ -196,4 +196,12 @@ int retrieve_delta_dispatch(int dtype, const int32_t* mj, const int32_t* mh, con
                             void* stage_k, void* stage_v, int32_t* stage_src, int64_t stage_rows, int32_t* err,
                             cudaStream_t s);
 
+// ---- offline head profiler (profile.cu)
+size_t profile_topk_ws_bytes(int rows, int plen);
+int profile_topk_dispatch(int dtype, const void* attn, int64_t sb, int64_t sh, int64_t sq, int64_t st, int q_last,
+                          int bsz, int He, int G, int use_len, int topk, uint32_t* bits, int64_t words, void* ws,
+                          size_t ws_bytes, cudaStream_t s);
+int profile_overlap_dispatch(const uint32_t* a, int64_t as, int na, const uint32_t* b, int64_t bs, int nb,
+                             int64_t words, int diagonal, int32_t* counts, cudaStream_t s);
+
 }  // namespace hc

@@ -475,3 +475,61 @@ def retrieve_delta(*, member_job, member_head, member_len, member_stage_offset, 
                                  stage_k.shape[0], _ptr(err), st)
     check("hc_retrieve_delta", rc)
     LAUNCHES[0] += 2
+
+
+def profile_topk(attn: torch.Tensor, *, groups: int, topk: int, max_length: int,
+                 workspace: Workspace) -> torch.Tensor:
+    """Top-k sets of the heads' last-query attention rows as bitmaps (the
+    per-dump step of tools/get_cluster.py:13-60).
+
+    ``attn`` [bsz, saved heads, q_len, keys] (or [bsz, heads, keys]) on the
+    GPU, any strides; ``groups`` > 1 averages that many consecutive saved
+    heads per effective head (GQA dumps of every query head).  Returns int32
+    bitmaps [bsz, heads // groups, words] (bit t of word t // 32); the set of
+    a row is empty when ``min(max_length, keys)`` is 0.
+    """
+    _cuda(attn)
+    if attn.dim() == 3:
+        attn = attn.unsqueeze(2)
+    if attn.dim() != 4:
+        raise ValueError("heterocache_b200: attn must be [bsz, heads, q_len, keys]")
+    B, Hs, Q, L = attn.shape
+    if groups < 1 or Hs % groups:
+        raise ValueError("heterocache_b200: saved heads must be a multiple of groups")
+    use_len = max(0, min(int(max_length), L))
+    He = Hs // groups
+    words = (use_len + 1 + 31) // 32 if use_len else 1
+    bits = torch.empty(B, He, words, dtype=torch.int32, device=attn.device)
+    if B == 0:
+        return bits
+    nbytes = lib().hc_profile_topk_workspace_size(B, He, use_len)
+    ws = workspace.get(nbytes) if nbytes else workspace.get(16)
+    sb, sh, sq, st = attn.stride()
+    check("hc_profile_topk",
+          lib().hc_profile_topk(dtype_code(attn), B, Hs, groups, Q, L, attn.data_ptr(), sb, sh, sq, st, use_len,
+                                int(topk), bits.data_ptr(), words, ws.data_ptr(), ws.numel(), _stream(attn)))
+    LAUNCHES[0] += 1
+    return bits
+
+
+def profile_overlap(a: torch.Tensor, b: torch.Tensor, *, diagonal: bool) -> torch.Tensor:
+    """Intersection sizes of bitmap rows (numerators of the reference's
+    calculate_overlap_ratio, tools/get_cluster.py:62-69): ``a`` [na, words],
+    ``b`` [nb, words] int32 on the GPU; returns int32 [na, nb], or [na] with
+    ``diagonal`` (row i with row i)."""
+    _cuda(a, b)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("heterocache_b200: bitmaps must be [rows, words] with equal words")
+    if a.dtype != torch.int32 or b.dtype != torch.int32 or a.stride(1) != 1 or b.stride(1) != 1:
+        raise ValueError("heterocache_b200: bitmaps must be int32 with contiguous words")
+    na, nb, words = a.shape[0], b.shape[0], a.shape[1]
+    if diagonal and na != nb:
+        raise ValueError("heterocache_b200: diagonal overlaps need equal row counts")
+    out = torch.empty((na,) if diagonal else (na, nb), dtype=torch.int32, device=a.device)
+    if na == 0 or nb == 0:
+        return out
+    check("hc_profile_overlap",
+          lib().hc_profile_overlap(a.data_ptr(), a.stride(0), na, b.data_ptr(), b.stride(0), nb, words,
+                                   1 if diagonal else 0, out.data_ptr(), _stream(a)))
+    LAUNCHES[0] += 1
+    return out

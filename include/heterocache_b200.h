@@ -404,6 +404,44 @@ int hc_retrieve_delta(int dtype, int num_kv_heads, int head_dim, int n_members,
                       void* stage_k, void* stage_v, int32_t* stage_src, int64_t stage_rows,
                       int32_t* err_flag, void* stream);
 
+/*
+ * Offline head profiler: top-k sets of the heads' last-query attention rows
+ * (replaces get_head_topk_exact, tools/get_cluster.py:13-60, which the
+ * profiler runs once per dumped layer and step).
+ *   attn: one dump, [bsz, saved_heads, q_len, seq_len] with element strides
+ *     (sb, sh, sq, st); only query row q_len - 1 is read.
+ *   groups: 1, or num_q_heads / num_kv_heads when a GQA model's dump holds
+ *     every query head (the reference's `is_gqa and num_saved_heads ==
+ *     num_q_heads`): effective head h is then the mean of saved heads
+ *     h * groups .. + groups - 1, taken in the dump's dtype (fp32 sum in head
+ *     order divided by groups, rounded to the dtype).
+ *   use_len: positions used, min(max_length, seq_len) (the reference's
+ *     `[..., :max_length]`); 0 leaves every set empty.
+ * Per (batch row, effective head): avg_pool1d over the row as fp32 with
+ * kernel k = min(5, use_len), padding k / 2, stride 1 (zero padding counted),
+ * then the top min(topk, pooled length) positions, equal values at the
+ * boundary taken at the lowest positions.  Written as bitmaps
+ * [bsz][saved_heads / groups][words] (bit t of word t / 32, LSB first);
+ * words >= ceil((use_len + 1) / 32); bits past the pooled length are 0.
+ * Workspace: hc_profile_topk_workspace_size bytes.  dtype: HC_F32 (the fp32
+ * mean of more than 4 heads may differ from torch's, whose summation order is
+ * vectorized, by one unit in the last place), HC_F16 or HC_BF16.
+ */
+size_t hc_profile_topk_workspace_size(int bsz, int effective_heads, int use_len);
+int hc_profile_topk(int dtype, int bsz, int saved_heads, int groups, int q_len, int seq_len,
+                    const void* attn, int64_t sb, int64_t sh, int64_t sq, int64_t st,
+                    int use_len, int topk, uint32_t* bitmaps, int64_t words,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Intersection sizes of top-k bitmaps (the numerators of
+ * calculate_overlap_ratio, tools/get_cluster.py:62-69): counts[i * nb + j] =
+ * |a_i & b_j| for every pair, or with diagonal != 0 counts[i] = |a_i & b_i|
+ * (na == nb).  a_i starts at a + i * a_stride words, b_j likewise.
+ */
+int hc_profile_overlap(const uint32_t* a, int64_t a_stride, int na, const uint32_t* b, int64_t b_stride, int nb,
+                       int64_t words, int diagonal, int32_t* counts, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
