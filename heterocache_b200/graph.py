@@ -99,6 +99,63 @@ class DecodeStepGraph:
             c._seen_tokens += 1
         return self.out
 
+    def run_host(self, host_q: torch.Tensor, host_k: torch.Tensor, host_v: torch.Tensor,
+                 host_out: torch.Tensor) -> None:
+        """Decode ``len(host_q)`` steps from host inputs into host outputs
+        (pinned memory: ``host_q[s]`` shaped as ``self.q``, ``host_out[s]`` as
+        ``self.out``), the host-link copies overlapped with the replays: step
+        s + 1's inputs cross into a staging buffer on a copy stream while step
+        s runs, and step s's outputs leave from a staging buffer on another
+        while step s + 1 runs.  Work already queued on the current stream
+        comes first; the current stream waits for the last copy back."""
+        n = host_q.shape[0]
+        if n == 0:
+            return
+        dev = self.q.device
+        cur = torch.cuda.current_stream(dev)
+        if not hasattr(self, "_h2d"):
+            self._h2d, self._d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+            self._stage_in = [(torch.empty_like(self.q), torch.empty_like(self.k), torch.empty_like(self.v))
+                              for _ in range(2)]
+            self._stage_out = [torch.empty_like(self.out) for _ in range(2)]
+        h2d, d2h = self._h2d, self._d2h
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
+        in_ready = [torch.cuda.Event() for _ in range(2)]
+        in_free = [torch.cuda.Event() for _ in range(2)]
+        out_ready = [torch.cuda.Event() for _ in range(2)]
+        out_done = [torch.cuda.Event() for _ in range(2)]
+
+        def load(s: int) -> None:
+            j = s % 2
+            with torch.cuda.stream(h2d):
+                if s >= 2:
+                    h2d.wait_event(in_free[j])  # step s - 2 took its inputs from this buffer
+                for dst, src in zip(self._stage_in[j], (host_q[s], host_k[s], host_v[s])):
+                    dst.copy_(src, non_blocking=True)
+                in_ready[j].record(h2d)
+
+        load(0)
+        for s in range(n):
+            i = s % 2
+            if s + 1 < n:
+                load(s + 1)
+            cur.wait_event(in_ready[i])
+            for dst, src in zip((self.q, self.k, self.v), self._stage_in[i]):
+                dst.copy_(src)
+            in_free[i].record(cur)
+            out = self.step()
+            if s >= 2:
+                cur.wait_event(out_done[i])  # step s - 2's outputs have left this buffer
+            self._stage_out[i].copy_(out)
+            out_ready[i].record(cur)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(out_ready[i])
+                host_out[s].copy_(self._stage_out[i], non_blocking=True)
+                out_done[i].record(d2h)
+        cur.wait_stream(d2h)
+        cur.wait_stream(h2d)
+
 
 class ModelDecodeGraph:
     """CUDA graphs of one greedy decode token through a whole transformers

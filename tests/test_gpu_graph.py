@@ -140,3 +140,34 @@ def test_deferred_checks_match_per_layer_checks(cuda_device, per_launch):
         else:
             for x, y in zip(a.reshape(-1, a.shape[-1]).tolist(), b.reshape(-1, b.shape[-1]).tolist()):
                 assert len(set(x) ^ set(y)) <= max(4, len(x) // 100), l
+
+
+def test_run_host_matches_step_by_step(cuda_device):
+    """DecodeStepGraph.run_host (copies overlapped with the replays on two
+    copy streams, the path the benchmark's end-to-end figure times) gives the
+    outputs and cache state of copying each step in and out around step()."""
+    dev, geo = cuda_device, LLAMA_8B
+    layers, L, n_steps = 2, 3000, 13
+    a, q_last = _cache(geo, layers, L, dev, threshold=0.9)
+    b, _ = _cache(geo, layers, L, dev, threshold=0.9)
+    gens = [DriftingDecode(geo, seed=50 + l, q0=q_last[l], dtype=torch.bfloat16) for l in range(layers)]
+    steps = [[g.step() for g in gens] for _ in range(n_steps)]
+    hq = torch.stack([torch.stack([st[l][0] for l in range(layers)]) for st in steps]).pin_memory()
+    hk = torch.stack([torch.stack([st[l][1] for l in range(layers)]) for st in steps]).pin_memory()
+    hv = torch.stack([torch.stack([st[l][2] for l in range(layers)]) for st in steps]).pin_memory()
+    ga = DecodeStepGraph(a, list(range(layers)))
+    gb = DecodeStepGraph(b, list(range(layers)))
+    out_a = torch.empty((n_steps,) + tuple(ga.out.shape), dtype=ga.out.dtype).pin_memory()
+    ga.run_host(hq, hk, hv, out_a)
+    out_b = []
+    for s in range(n_steps):
+        gb.q.copy_(hq[s]), gb.k.copy_(hk[s]), gb.v.copy_(hv[s])
+        out_b.append(gb.step().cpu())
+    torch.cuda.synchronize()
+    a.check_errors()
+    b.check_errors()
+    for s in range(n_steps):
+        assert torch.equal(out_a[s], out_b[s]), f"step {s}"
+    for l in range(layers):
+        assert torch.equal(a.key_pools[l], b.key_pools[l])
+        assert torch.equal(a.heads_len[l], b.heads_len[l])
