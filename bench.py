@@ -69,6 +69,9 @@ def parse():
                                                          "(default: CUDA-graph replay)")
     ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"])
     ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="head-sharded mode: head outputs gathered by the decode kernels over NVLink (peer) or "
+                         "by an NCCL all-gather")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-head-sharded", action="store_true",
                     help="skip the head-sharded config-4 measurement the default workload also reports")
@@ -748,12 +751,14 @@ class PhaseGraphs:
 def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, warmup):
     """Config 4: one Llama layer, a batch of `n_seq` independent sequences of
     `L` tokens, sharded by sequence (no collective) or by KV head (every
-    sequence's 8 KV heads split over the ranks: an NCCL all-gather of the
-    head outputs per step, broadcasts of pivot position lists at check
-    steps).  Returns the measurement (all ranks take part; the timings are
-    the max over ranks)."""
+    sequence's 8 KV heads split over the ranks; the head outputs gathered by
+    the decode combine kernels themselves over NVLink with two device-side
+    barriers a step, all inside the step's CUDA graph -- or, with
+    ``--gather nccl``, by an eager NCCL all-gather after each replay --, and
+    broadcasts of pivot position lists at check steps).  Returns the
+    measurement (all ranks take part; the timings are the max over ranks)."""
     from heterocache_b200.cache import HeteroCacheConfig
-    from heterocache_b200.head_shard import HeadShardedCache, gather_heads
+    from heterocache_b200.head_shard import HeadShardedCache, PeerGather, gather_heads
     from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -812,14 +817,22 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         vb.copy_(kvs[1, t][:, :, ks])
 
     local = torch.zeros(n_local, hl, D, dtype=torch.bfloat16, device=dev)
+    peer = None
+    if heads_mode and getattr(args, "gather", "peer") == "peer":
+        peer = PeerGather(n_local, hl, D, torch.bfloat16, rank, world, device=dev)
 
     def local_step():
-        """Everything but the collectives: captured in the phase graphs."""
+        """Everything but the NCCL calls: captured in the phase graphs."""
         for i, view in enumerate(views):
             view.update(kb[i], vb[i], 0, {"query_states": qb[i]})
         if heads_mode:
+            if peer is not None:
+                peer.barrier()  # every rank has read the previous step's gathered output
             for i, view in enumerate(views):
-                view.cache.attention(qb[i], 0, out=local[i:i + 1])
+                if peer is not None:
+                    view.attention(qb[i], 0, peer=peer, row0=i)
+                else:
+                    view.cache.attention(qb[i], 0, out=local[i:i + 1])
             for i, view in enumerate(views):
                 view.select_local(qb[i], 0)
         else:
@@ -828,6 +841,8 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
                 view.decode_select(qb[i], 0)
         for c in inner:
             c.join_retrievals()
+        if peer is not None:
+            peer.barrier()  # every rank's head rows have landed in every rank's peer.out
 
     gather_events = []
 
@@ -838,13 +853,14 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         sits on another GPU."""
         if not heads_mode:
             return
-        if timed:
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-        gather_heads(local, world, out=out, cache=stage)
-        if timed:
-            e1.record()
-            gather_events.append((e0, e1))
+        if peer is None:
+            if timed:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            gather_heads(local, world, out=out, cache=stage)
+            if timed:
+                e1.record()
+                gather_events.append((e0, e1))
         if check:
             for view in views:
                 view.remote_checks(0)
@@ -891,18 +907,31 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         torch.distributed.barrier()
     for c in inner:
         c.check_errors()
+    if peer is not None:
+        peer.check_errors()
     del graphs
+    if peer is not None:
+        peer.close()
+        if world > 1:
+            torch.distributed.barrier()
     ms_step = ms / steps
-    mode = (f"KV-head-sharded x{world} (each GPU {KV // world} of the 8 KV heads of every sequence; NCCL "
-            f"all-gather of the head outputs per step)" if heads_mode
+    gather = ("the decode combine kernels store their head rows into every GPU's gathered output over "
+              "NVLink, two device-side barriers a step, inside the step's CUDA graph" if peer is not None
+              else "NCCL all-gather of the head outputs per step")
+    mode = (f"KV-head-sharded x{world} (each GPU {KV // world} of the 8 KV heads of every sequence; {gather})"
+            if heads_mode
             else f"sequence-sharded x{world} ({n_seq // world} sequences per GPU, no data-path collective)")
     res = {"value": n_seq * 1000.0 / ms_step, "unit": "tokens/s", "ms_per_step": ms_step, "steps": steps,
            "sequences": n_seq, "context": L, "parallelism": mode}
-    if heads_mode:
+    if heads_mode and peer is None:
         res["allgather_us_per_step"] = ag_ms * 1e3 / steps
         res["allgather_share"] = ag_ms / ms if ms > 0 else None
         res["collective"] = ("torch.distributed.all_gather_into_tensor (NCCL)" if world > 1
                              else "none (one rank holds every head)")
+    elif heads_mode:
+        res["collective"] = ("hc_flash_decode_peer output mirrors (P2P stores over NVLink to CUDA IPC mappings) "
+                             "+ hc_peer_barrier x2 per step" if world > 1 else
+                             "hc_flash_decode_peer into the rank's own gathered output (one rank)")
     return res
 
 

@@ -746,12 +746,16 @@ class HeteroCache(_CacheBase):
         return self.key_cache_cpu[layer_idx], self.value_cache_cpu[layer_idx], self._tier_first[layer_idx]
 
     # ------------------------------------------------------------------
-    def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):
+    def attention(self, query_states, layer_idx, scale: float = 0.0, out=None, mirrors=None,
+                  mirror_batch_stride: int = 0):
         """Decode attention over this layer's pages: q [bsz, H, 1, D] -> [bsz, H, D].
 
         With a deferred append pending (update(..., {"defer_append": True})),
         the step's token is merged from its k/v and then appended to the pages
-        on the side stream; the layer's next use waits for that append."""
+        on the side stream; the layer's next use waits for that append.
+        ``mirrors`` (device addresses) each receive a copy of the output (see
+        ``ops.flash_decode``): the head-sharded mode's gathered outputs on
+        every GPU."""
         if self._deferred and layer_idx in self._deferred:
             self.flush_checks()
         self._wait_retrieval(layer_idx)
@@ -762,7 +766,8 @@ class HeteroCache(_CacheBase):
             return ops.flash_decode(query_states, self.key_pools[layer_idx], self.value_pools[layer_idx],
                                     self.block_tables[layer_idx], self.heads_len[layer_idx],
                                     num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
-                                    err=self._err, total_tokens_hint=total)
+                                    err=self._err, total_tokens_hint=total, mirrors=mirrors,
+                                    mirror_batch_stride=mirror_batch_stride)
         self._pending[layer_idx] = None
         k, v, q, slot, selected = pend
         # the step's query goes to the drift-check buffer on this stream (the
@@ -776,7 +781,8 @@ class HeteroCache(_CacheBase):
                                self.block_tables[layer_idx], self.heads_len[layer_idx],
                                num_kv_heads=self.num_kv_heads, scale=scale, out=out, workspace=self._ws_fd,
                                err=self._err, k_new=k, v_new=v,
-                               q_stage=self._qbuf[layer_idx][slot] if same_q else None)
+                               q_stage=self._qbuf[layer_idx][slot] if same_q else None, mirrors=mirrors,
+                               mirror_batch_stride=mirror_batch_stride)
         main = torch.cuda.current_stream(self._dev)
         side = self._side()
         side.wait_stream(main)

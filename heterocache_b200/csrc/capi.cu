@@ -6,6 +6,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <mutex>
+
+#include <cuda.h>
 
 #include "hc_params.cuh"
 
@@ -342,20 +345,23 @@ int hc_flash_decode(int dtype, int bsz, int num_kv_heads, int groups, int head_d
   return note_cuda(hc::flash_decode_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
 }
 
-int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q,
-                             int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
-                             const int32_t* block_table, int max_blocks, const int32_t* heads_len,
-                             const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh, int64_t vn_sb,
-                             int64_t vn_sh, float scale, void* out, void* q_stage, void* workspace,
-                             size_t workspace_bytes, int32_t* err_flag, void* stream) {
+}  // extern "C"
+
+namespace {
+// The parameters of a decode launch that also attends to the step's new token
+// (hc_flash_decode_with_new, hc_flash_decode_peer); HC_OK or the error.
+int with_new_params(hc::FDParams& p, int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q,
+                    int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
+                    const int32_t* block_table, int max_blocks, const int32_t* heads_len, const void* k_new,
+                    const void* v_new, int64_t kn_sb, int64_t kn_sh, int64_t vn_sb, int64_t vn_sh, float scale,
+                    void* out, void* q_stage, int32_t* err_flag, bool need_new = true) {
   if (!valid_dtype(dtype)) return HC_ERR_DTYPE;
   if (head_dim != HC_HEAD_DIM || bsz <= 0 || num_kv_heads <= 0 || groups <= 0 || max_blocks <= 0)
     return HC_ERR_INVALID;
   if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out)) return HC_ERR_INVALID;
-  if (!k_new || !v_new) return HC_ERR_INVALID;
-  if (q_stage && bsz != 1) return HC_ERR_INVALID;
+  if (need_new ? (!k_new || !v_new) : (!k_new != !v_new)) return HC_ERR_INVALID;
+  if (q_stage && (bsz != 1 || !k_new)) return HC_ERR_INVALID;
   if (!stride_ok(dtype, qsb) || !stride_ok(dtype, qsh)) return HC_ERR_INVALID;
-  hc::FDParams p;
   std::memset(&p, 0, sizeof(p));
   p.q = q;
   p.qsb = qsb;
@@ -380,7 +386,117 @@ int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, i
   p.vn_sb = vn_sb;
   p.vn_sh = vn_sh;
   p.q_stage = q_stage;
+  return HC_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q,
+                             int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
+                             const int32_t* block_table, int max_blocks, const int32_t* heads_len,
+                             const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh, int64_t vn_sb,
+                             int64_t vn_sh, float scale, void* out, void* q_stage, void* workspace,
+                             size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  hc::FDParams p;
+  const int rc = with_new_params(p, dtype, bsz, num_kv_heads, groups, head_dim, q, qsb, qsh, k_pool, v_pool,
+                                 n_pool_blocks, block_table, max_blocks, heads_len, k_new, v_new, kn_sb, kn_sh,
+                                 vn_sb, vn_sh, scale, out, q_stage, err_flag);
+  if (rc != HC_OK) return rc;
   return note_cuda(hc::flash_decode_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+int hc_flash_decode_peer(int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q,
+                         int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
+                         const int32_t* block_table, int max_blocks, const int32_t* heads_len, const void* k_new,
+                         const void* v_new, int64_t kn_sb, int64_t kn_sh, int64_t vn_sb, int64_t vn_sh, float scale,
+                         void* out, void* q_stage, int n_mirrors, void* const* mirrors, int64_t mirror_batch_stride,
+                         void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream) {
+  hc::FDParams p;
+  const int rc = with_new_params(p, dtype, bsz, num_kv_heads, groups, head_dim, q, qsb, qsh, k_pool, v_pool,
+                                 n_pool_blocks, block_table, max_blocks, heads_len, k_new, v_new, kn_sb, kn_sh,
+                                 vn_sb, vn_sh, scale, out, q_stage, err_flag, false);
+  if (rc != HC_OK) return rc;
+  if (n_mirrors < 0 || n_mirrors > HC_MAX_PEERS || (n_mirrors > 0 && !mirrors)) return HC_ERR_INVALID;
+  if (n_mirrors > 0 && mirror_batch_stride < (int64_t)num_kv_heads * groups * head_dim && bsz > 1)
+    return HC_ERR_INVALID;
+  for (int m = 0; m < n_mirrors; ++m) {
+    if (!mirrors[m] || (reinterpret_cast<uintptr_t>(mirrors[m]) % elem_bytes(dtype)) != 0) return HC_ERR_INVALID;
+    p.mirror[m] = mirrors[m];
+  }
+  p.n_mirror = n_mirrors;
+  p.mirror_sb = mirror_batch_stride;
+  return note_cuda(hc::flash_decode_dispatch(dtype, p, workspace, workspace_bytes, (cudaStream_t)stream));
+}
+
+int hc_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  if (!ptr || !handle || !offset) return HC_ERR_INVALID;
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_range = reinterpret_cast<GetRange>(f);
+  });
+  if (!get_range) return HC_ERR_UNSUPPORTED;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, (CUdeviceptr)ptr) != CUDA_SUCCESS) return HC_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return note_cuda(HC_ERR_CUDA);
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = (int64_t)((CUdeviceptr)ptr - base);
+  return HC_OK;
+}
+
+int hc_ipc_open(const void* handle, void** base) {
+  if (!handle || !base) return HC_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return note_cuda(HC_ERR_CUDA);
+  // the mapping must be known to this process as device memory
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+    (void)cudaGetLastError();
+    (void)cudaIpcCloseMemHandle(p);
+    return HC_ERR_UNSUPPORTED;
+  }
+  *base = p;
+  return HC_OK;
+}
+
+int hc_ipc_close(void* base) {
+  if (!base) return HC_ERR_INVALID;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? HC_OK : note_cuda(HC_ERR_CUDA);
+}
+
+int hc_enable_peer_access(int peer_device) {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaGetDeviceCount(&n) != cudaSuccess) return note_cuda(HC_ERR_CUDA);
+  if (peer_device < 0 || peer_device >= n) return HC_ERR_INVALID;
+  if (peer_device == dev) return HC_OK;
+  int can = 0;
+  if (cudaDeviceCanAccessPeer(&can, dev, peer_device) != cudaSuccess) return note_cuda(HC_ERR_CUDA);
+  if (!can) return HC_ERR_UNSUPPORTED;
+  const cudaError_t e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();  // not an error here
+    return HC_OK;
+  }
+  return e == cudaSuccess ? HC_OK : note_cuda(HC_ERR_CUDA);
+}
+
+int hc_peer_barrier(int rank, int world, int32_t* const* peer_flags, int32_t* counter, int32_t* err_flag,
+                    void* stream) {
+  if (world <= 0 || world > HC_MAX_PEERS || rank < 0 || rank >= world || !peer_flags || !counter || !err_flag)
+    return HC_ERR_INVALID;
+  for (int r = 0; r < world; ++r)
+    if (!peer_flags[r] || (reinterpret_cast<uintptr_t>(peer_flags[r]) & 3u) != 0) return HC_ERR_INVALID;
+  return note_cuda(hc::peer_barrier_dispatch(rank, world, peer_flags, counter, err_flag, (cudaStream_t)stream));
 }
 
 int hc_flash_decode_noalloc(int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q,

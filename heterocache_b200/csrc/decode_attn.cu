@@ -653,6 +653,18 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
   const int sub = lane / LG, q4 = lane % LG;  // partial group within the warp, 16-byte piece of the slice
   const int d0 = kCSliceDims * sl;           // the slice's first dim
   T* out = reinterpret_cast<T*>(p.out) + ((size_t)r * p.G + g) * kD + d0;
+  // the output element d of this slice, here and in the mirrors (peer GPUs'
+  // gathered outputs, written over NVLink), then a system-scope fence so that
+  // a later step barrier publishes them
+  auto store = [&](int d, float x) {
+    const T val = Elem<T>::from_f(x);
+    out[d] = val;
+    if (p.n_mirror > 0) {
+      const int64_t off = (int64_t)(r / p.KV) * p.mirror_sb + ((int64_t)(r % p.KV) * p.G + g) * kD + d0 + d;
+      for (int m = 0; m < p.n_mirror; ++m) reinterpret_cast<T*>(p.mirror[m])[off] = val;
+      __threadfence_system();
+    }
+  };
   const int rs = s_start[r], re = s_start[r + 1];
   // the step's token not in the pages yet: its score (log2 domain) and value.
   // q and k_new come from before the decode kernel, which started after they
@@ -683,7 +695,7 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
     __syncthreads();
   }
   if (re == rs || span == 0) {  // no pages: the new token alone, or nothing
-    if (threadIdx.x < kCSliceDims) out[threadIdx.x] = Elem<T>::from_f(has_new ? v_new_d : 0.f);
+    if (threadIdx.x < kCSliceDims) store(threadIdx.x, has_new ? v_new_d : 0.f);
     return;
   }
   const int c0 = rs / span, n = (re - 1) / span - c0 + 1;
@@ -749,8 +761,63 @@ __global__ void __launch_bounds__(kCThreads) flash_combine_kernel(FDParams p, in
     float O = f_new * v_new_d;
 #pragma unroll
     for (int k = 0; k < NG; ++k) O += reinterpret_cast<const float*>(&s_acc[k][d / 4])[d % 4];
-    out[d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
+    store(d, L > 0.f ? O / L : 0.f);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Step barrier of a head-sharded cache's GPUs (the output mirrors above make
+// the all-gather of head outputs part of the attention's combine).  One warp:
+// lane 0 takes the next value of the rank's counter; lane q < world stores it
+// into slot `rank` of rank q's flags (release, system scope: after the
+// mirrored stores of earlier kernels), then lane q waits until slot q of this
+// rank's flags reaches it (acquire).  Every wait is bounded: after the limit
+// the lane ORs HC_ERR_TIMEOUT into err and returns.
+__device__ __forceinline__ void st_release_sys(int32_t* a, int32_t v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* a) {
+  int32_t v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+
+struct PeerFlags {
+  int32_t* f[kMaxPeers];
+};
+
+__global__ void __launch_bounds__(32) peer_barrier_kernel(int rank, int world, PeerFlags flags, int32_t* counter,
+                                                          int32_t* err, uint64_t wait_ns) {
+  const int lane = threadIdx.x;
+  int32_t v = 0;
+  if (lane == 0) {
+    v = *counter + 1;
+    *counter = v;
+  }
+  v = __shfl_sync(0xffffffffu, v, 0);
+  __threadfence_system();
+  if (lane < world) st_release_sys(flags.f[lane] + rank, v);
+  if (lane < world && lane != rank) {
+    const int32_t* mine = flags.f[rank] + lane;
+    if (ld_acquire_sys(mine) < v) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(mine) < v) {
+        if (globaltimer_ns() - t0 > wait_ns) {
+          set_err(err, HC_ERR_TIMEOUT);
+          return;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+}
+
+int peer_barrier_dispatch(int rank, int world, int32_t* const* peer_flags, int32_t* counter, int32_t* err,
+                          cudaStream_t st) {
+  PeerFlags f;
+  for (int i = 0; i < kMaxPeers; ++i) f.f[i] = i < world ? peer_flags[i] : nullptr;
+  peer_barrier_kernel<<<1, 32, 0, st>>>(rank, world, f, counter, err, wait_limit_ns(kBarrierTimeoutNs));
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 
 // Co-resident CTAs of the fp32 decode kernel on the current device (cached

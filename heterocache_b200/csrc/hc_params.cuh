@@ -125,6 +125,7 @@ int score_dispatch(int dtype, ScoreParams& p, void* ws, size_t ws_bytes, cudaStr
                    const DriftBatch* batch = nullptr);
 
 // ---- paged flash-decode (decode_attn.cu)
+constexpr int kMaxPeers = 8;  // GPUs of one node a head-sharded output is mirrored to
 constexpr int kFThreads = 128;
 constexpr int kFWarps = 4;
 constexpr int kGMax = 8;
@@ -152,11 +153,22 @@ struct FDParams {
   // optional (batch of one): the combine also stores the query rows here [H, D]
   void* q_stage;
   void* out;
+  // optional: copies of the output in other GPUs' memory (peer pointers over
+  // NVLink): element (b, query head j, d) also goes to mirror[m] + b *
+  // mirror_sb + j * D + d
+  int n_mirror;
+  int64_t mirror_sb;
+  void* mirror[kMaxPeers];
   int32_t* err;
   uint64_t wait_ns;  // mbarrier wait limit (set at dispatch)
 };
 
 size_t flash_decode_ws_bytes(int R, int G);
+// One step barrier across the GPUs of a head-sharded cache: the caller's
+// counter + 1 stored into slot `rank` of every rank's flags, then a wait
+// until every slot of this rank's flags holds at least that value.
+int peer_barrier_dispatch(int rank, int world, int32_t* const* peer_flags, int32_t* counter, int32_t* err,
+                          cudaStream_t st);
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st);
 int flash_decode_noalloc_dispatch(int dtype, FDParams& p, cudaStream_t st, size_t* need_out);
 

@@ -11,7 +11,11 @@ head counts, so every head gets the capacity it would get on one GPU.
 Two steps cross ranks:
 
 * attention: each rank's output rows [bsz, H/world, D] are all-gathered
-  (one NCCL all-gather per layer and step) into [bsz, H, D] for o_proj;
+  into [bsz, H, D] for o_proj: by one NCCL all-gather per layer and step, or
+  (``PeerGather``) by the decode combine kernel itself, which stores its rows
+  into every rank's gathered buffer over NVLink, two device-side barriers a
+  step ordering the stores (no collective call on the host, so a whole step
+  replays from one CUDA graph);
 * retrieval: a pivot and its satellites may sit on different ranks.  The
   pivot's rank runs the drift check; at each check step it broadcasts the
   pivot's trigger and position list (the list heterocache/cache_utils.py:
@@ -148,8 +152,18 @@ class HeadShardedCache:
         self.cache.prefill_select(query_states, key_states, value_states, layer_idx)
 
     # -- decode --------------------------------------------------------
-    def attention(self, query_states, layer_idx, scale: float = 0.0, out=None):
-        """Local flash-decode, then one all-gather: returns [bsz, H, D]."""
+    def attention(self, query_states, layer_idx, scale: float = 0.0, out=None, peer: "PeerGather" = None,
+                  row0: int = 0):
+        """Local flash-decode, then one all-gather: returns [bsz, H, D].
+
+        With ``peer`` the decode kernels store this rank's head rows straight
+        into every rank's ``peer.out`` (rows ``row0`` ..) instead, and nothing
+        is returned before ``peer.barrier()``: the caller issues one barrier
+        before a step's attention calls and one after them, then reads
+        ``peer.out``."""
+        if peer is not None:
+            return self.cache.attention(query_states, layer_idx, scale=scale, mirrors=peer.mirrors(row0),
+                                        mirror_batch_stride=peer.mirror_batch_stride)
         local = self.cache.attention(query_states, layer_idx, scale=scale)
         return gather_heads(local, self.world, self.group, out=out, cache=self._gather)
 
@@ -261,3 +275,93 @@ def gather_heads(local: torch.Tensor, world: int, group=None, out: Optional[torc
 def broadcast_retrieval(buf: torch.Tensor, src: int, group=None) -> None:
     """Trigger and position list of one pivot, from the pivot's rank to all."""
     dist.broadcast(buf, src=src, group=group)
+
+
+class PeerGather:
+    """The all-gather of head outputs done by the attention kernels: every
+    rank's gathered output, written by every rank over NVLink.
+
+    Each rank allocates ``out`` [rows, world * h, D] (rows: the batch rows of
+    the caches that share it, e.g. one per sequence) and an int32 flag array,
+    maps the other ranks' two buffers into its address space through CUDA
+    IPC (hc_ipc_export / hc_ipc_open: plain peer mappings for this rank's
+    device, no multicast object), and gives each attention call the address of its own
+    head block in every rank's ``out`` (``mirrors(row0)``): the decode
+    combine kernel stores each output row there as it finishes it.
+    ``barrier()`` (hc_peer_barrier) before a step's attention calls and after
+    them orders the stores: after the second, ``out`` holds every rank's
+    heads on every rank.  All ranks construct it together (one object
+    exchange over the process group) and call ``barrier`` equally often.
+    """
+
+    def __init__(self, rows: int, h: int, D: int, dtype: torch.dtype, rank: int, world: int, group=None,
+                 device=None):
+        if not 1 <= world <= 8:
+            raise ValueError("PeerGather: 1 to 8 ranks")
+        self.rank, self.world, self.h, self.D, self.rows = rank, world, h, D, rows
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.out = torch.zeros(rows, world * h, D, dtype=dtype, device=dev)
+        self.flags = torch.zeros(world, dtype=torch.int32, device=dev)
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._opened: List[int] = []  # this process's mappings of the other ranks' allocations
+        if world == 1:
+            self.out_ptrs, self.flag_ptrs = [self.out.data_ptr()], [self.flags.data_ptr()]
+        else:
+            import ctypes
+            from ._lib import check, lib
+            torch.cuda.synchronize(dev)  # the buffers are zero before a peer maps them
+
+            def export(t):
+                h, off = ctypes.create_string_buffer(64), ctypes.c_int64(0)
+                check("hc_ipc_export", lib().hc_ipc_export(t.data_ptr(), h, ctypes.byref(off)))
+                return h.raw, off.value
+
+            mine = (export(self.out), export(self.flags))
+            allh: List = [None] * world
+            dist.all_gather_object(allh, mine, group=group)
+            opened: Dict[bytes, int] = {}  # one mapping per allocation (out and flags may share one)
+
+            def mapped(handle: bytes, off: int) -> int:
+                if handle not in opened:
+                    base = ctypes.c_void_p()
+                    with torch.cuda.device(dev):  # mapped for this device, peer access enabled as needed
+                        check("hc_ipc_open", lib().hc_ipc_open(ctypes.create_string_buffer(handle, 64),
+                                                               ctypes.byref(base)))
+                    opened[handle] = base.value
+                return opened[handle] + off
+
+            self.out_ptrs, self.flag_ptrs = [], []
+            for r, ((ho, oo), (hf, of)) in enumerate(allh):
+                if r == rank:
+                    self.out_ptrs.append(self.out.data_ptr())
+                    self.flag_ptrs.append(self.flags.data_ptr())
+                else:
+                    self.out_ptrs.append(mapped(ho, oo))
+                    self.flag_ptrs.append(mapped(hf, of))
+            self._opened = list(opened.values())
+        self.mirror_batch_stride = world * h * D
+        self._esz = self.out.element_size()
+
+    def mirrors(self, row0: int = 0) -> List[int]:
+        """Where this rank's heads of batch row ``row0`` go in every rank's ``out``."""
+        off = (row0 * self.world * self.h + self.rank * self.h) * self.D * self._esz
+        return [p + off for p in self.out_ptrs]
+
+    def barrier(self) -> None:
+        ops.peer_barrier(self.rank, self.world, self.flag_ptrs, self.counter, self.err)
+
+    def close(self) -> None:
+        """Unmap the other ranks' buffers (after this rank's last barrier; every
+        rank's own buffers stay until every rank has closed)."""
+        if self._opened:
+            from ._lib import check, lib
+            torch.cuda.synchronize(self.out.device)
+            for base in self._opened:
+                check("hc_ipc_close", lib().hc_ipc_close(base))
+            self._opened = []
+
+    def check_errors(self) -> None:
+        e = int(self.err.item())
+        if e:
+            raise RuntimeError(f"heterocache_b200: peer barrier error flag {e} (a rank did not arrive in time)")

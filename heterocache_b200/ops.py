@@ -261,11 +261,14 @@ def decode_append(k, v, k_pool, v_pool, block_table, heads_len, free_blocks, fre
 
 
 def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out=None, scale: float = 0.0,
-                 workspace: Workspace, err, total_tokens_hint: int = 0, k_new=None, v_new=None, q_stage=None):
+                 workspace: Workspace, err, total_tokens_hint: int = 0, k_new=None, v_new=None, q_stage=None,
+                 mirrors=None, mirror_batch_stride: int = 0):
     """q: [bsz, H, 1, D] -> out [bsz, H, D] (same dtype).  With k_new/v_new
     [bsz, KV, 1, D] each row also attends to that token (not in the pages);
     then q_stage (bsz 1: a contiguous [H, D] buffer) also receives the query
-    rows."""
+    rows, and ``mirrors`` (device addresses, e.g. other GPUs' gathered
+    outputs) each receive a copy of the output: element (b, head j, d) at
+    mirror + (b * mirror_batch_stride + j * D + d) elements."""
     H = q.shape[1]
     _need(num_kv_heads > 0 and H % num_kv_heads == 0,
           f"the {H} query heads do not split evenly over {num_kv_heads} KV heads")
@@ -291,6 +294,20 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
         if q_stage is not None and (bsz != 1 or tuple(q_stage.shape) != (H, D) or q_stage.dtype != q.dtype
                                     or not q_stage.is_contiguous()):
             raise ValueError("heterocache_b200: q_stage must be a contiguous [H, D] buffer in the query dtype (bsz 1)")
+        if mirrors:
+            import ctypes
+            _need(len(mirrors) <= 8, "at most 8 output mirrors")
+            arr = (ctypes.c_void_p * len(mirrors))(*[int(m) for m in mirrors])
+            rc = lib().hc_flash_decode_peer(dtype_code(q), bsz, num_kv_heads, groups, D, _ptr(q), q.stride(0),
+                                            q.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
+                                            _ptr(block_table), block_table.shape[1], _ptr(heads_len), _ptr(k_new),
+                                            _ptr(v_new), k_new.stride(0), k_new.stride(1), v_new.stride(0),
+                                            v_new.stride(1), float(scale), _ptr(out), _ptr(q_stage), len(mirrors),
+                                            arr, int(mirror_batch_stride), _ptr(ws), ws.numel(), _ptr(err),
+                                            _stream(q))
+            check("hc_flash_decode_peer", rc)
+            LAUNCHES[0] += 2
+            return out
         rc = lib().hc_flash_decode_with_new(dtype_code(q), bsz, num_kv_heads, groups, D, _ptr(q), q.stride(0),
                                             q.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0],
                                             _ptr(block_table), block_table.shape[1], _ptr(heads_len), _ptr(k_new),
@@ -298,6 +315,18 @@ def flash_decode(q, k_pool, v_pool, block_table, heads_len, *, num_kv_heads, out
                                             v_new.stride(1), float(scale), _ptr(out), _ptr(q_stage), _ptr(ws),
                                             ws.numel(), _ptr(err), _stream(q))
         check("hc_flash_decode_with_new", rc)
+        LAUNCHES[0] += 2
+        return out
+    if mirrors:
+        import ctypes
+        _need(len(mirrors) <= 8, "at most 8 output mirrors")
+        arr = (ctypes.c_void_p * len(mirrors))(*[int(m) for m in mirrors])
+        rc = lib().hc_flash_decode_peer(dtype_code(q), bsz, num_kv_heads, groups, D, _ptr(q), q.stride(0),
+                                        q.stride(1), _ptr(k_pool), _ptr(v_pool), k_pool.shape[0], _ptr(block_table),
+                                        block_table.shape[1], _ptr(heads_len), None, None, 0, 0, 0, 0, float(scale),
+                                        _ptr(out), None, len(mirrors), arr, int(mirror_batch_stride), _ptr(ws),
+                                        ws.numel(), _ptr(err), _stream(q))
+        check("hc_flash_decode_peer", rc)
         LAUNCHES[0] += 2
         return out
     rc = lib().hc_flash_decode(dtype_code(q), bsz, num_kv_heads, groups, D, _ptr(q), q.stride(0), q.stride(1),
@@ -533,3 +562,15 @@ def profile_overlap(a: torch.Tensor, b: torch.Tensor, *, diagonal: bool) -> torc
                                    1 if diagonal else 0, out.data_ptr(), _stream(a)))
     LAUNCHES[0] += 1
     return out
+
+
+def peer_barrier(rank: int, world: int, flag_ptrs, counter: torch.Tensor, err: torch.Tensor) -> None:
+    """One step barrier of a head-sharded cache's ranks (hc_peer_barrier):
+    ``flag_ptrs`` the device addresses of every rank's int32 flag array,
+    ``counter`` this rank's int32 counter."""
+    import ctypes
+    _cuda(counter, err)
+    _need(1 <= world <= 8 and 0 <= rank < world and len(flag_ptrs) == world, "bad rank or world")
+    arr = (ctypes.c_void_p * world)(*[int(p) for p in flag_ptrs])
+    check("hc_peer_barrier", lib().hc_peer_barrier(rank, world, arr, _ptr(counter), _ptr(err), _stream(counter)))
+    LAUNCHES[0] += 1

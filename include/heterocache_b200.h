@@ -239,6 +239,65 @@ int hc_flash_decode_with_new(int dtype, int bsz, int num_kv_heads, int groups, i
                              void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Head-sharded decode: the all-gather of head outputs done by the attention
+ * kernels themselves.  Replaces the NCCL all-gather of per-rank head outputs
+ * (the head-sharded mode has no reference counterpart: the reference runs
+ * one GPU; its attention output feeds o_proj, llama_model.py:398-405).
+ *
+ * hc_flash_decode_peer: hc_flash_decode_with_new (k_new / v_new may both be
+ * NULL: hc_flash_decode then, without q_stage), whose combine kernel also
+ * stores every output element into n_mirrors other buffers (up to
+ * HC_MAX_PEERS device pointers, typically other GPUs' memory mapped with
+ * CUDA IPC, written over NVLink): element (b, query head j, d) goes to
+ * mirrors[m] + b * mirror_batch_stride + j * head_dim + d (elements).  A
+ * rank of a head-sharded cache passes, for every rank, the address of its
+ * own heads' rows in that rank's gathered output.  The stores are fenced at
+ * system scope; hc_peer_barrier publishes them.
+ *
+ * hc_peer_barrier: step barrier of `world` ranks, one launch per rank, each
+ * on its own GPU (never several ranks on one GPU: they would wait on each
+ * other's launches).  peer_flags[r] is rank r's int32 flag array (at least
+ * `world` entries, zero at start, the same order on every rank); counter is
+ * this rank's own int32 (zero at start).  The kernel stores counter + 1 into
+ * slot `rank` of every rank's flags (release, system scope) and waits until
+ * every slot of peer_flags[rank] holds at least that value (acquire); all
+ * ranks must issue the same number of barriers.  A wait that exceeds the
+ * limit of hc_set_wait_limits (default 2 s) ORs HC_ERR_TIMEOUT into err_flag
+ * and returns.  Issue one before a step's mirrored stores (every rank has
+ * finished reading the previous step's gathered output) and one after them
+ * (every rank's output rows have landed everywhere).
+ */
+#define HC_MAX_PEERS 8
+/* Lets kernels on the current device read and write memory that lives on
+ * peer_device (cudaDeviceEnablePeerAccess), e.g. another rank's buffer mapped
+ * with CUDA IPC under that device: HC_OK (also when already enabled or the
+ * same device), HC_ERR_UNSUPPORTED when the two devices cannot reach each
+ * other.  Call before handing such addresses to hc_flash_decode_peer or
+ * hc_peer_barrier. */
+int hc_enable_peer_access(int peer_device);
+/* CUDA IPC of one rank's buffers, for the output mirrors and flags above.
+ * hc_ipc_export: the 64-byte handle (HC_IPC_HANDLE_BYTES) of the device
+ * allocation that holds `ptr` (a caching allocator's segment) and ptr's byte
+ * offset in it.  hc_ipc_open (in another process): maps that allocation for
+ * the current device, enabling peer access as needed, and returns its base
+ * (add the offset); one open per allocation and process, undone by
+ * hc_ipc_close. */
+#define HC_IPC_HANDLE_BYTES 64
+int hc_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int hc_ipc_open(const void* handle, void** base);
+int hc_ipc_close(void* base);
+int hc_flash_decode_peer(int dtype, int bsz, int num_kv_heads, int groups, int head_dim,
+                         const void* q, int64_t qsb, int64_t qsh,
+                         const void* k_pool, const void* v_pool, int n_pool_blocks,
+                         const int32_t* block_table, int max_blocks, const int32_t* heads_len,
+                         const void* k_new, const void* v_new, int64_t kn_sb, int64_t kn_sh,
+                         int64_t vn_sb, int64_t vn_sh, float scale, void* out, void* q_stage,
+                         int n_mirrors, void* const* mirrors, int64_t mirror_batch_stride,
+                         void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
+int hc_peer_barrier(int rank, int world, int32_t* const* peer_flags, int32_t* counter, int32_t* err_flag,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
  * Decode attention without a workspace.  No counterpart in the reference:
  * this is an addition for callers that cannot allocate device memory, such as
  * a host program whose device memory is entirely owned by another allocator,

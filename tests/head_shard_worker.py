@@ -15,7 +15,7 @@ sys.path.insert(0, HERE)
 
 from test_gpu_head_shard import _config, _rows, _setup  # noqa: E402
 from heterocache_b200.cache import HeteroCache  # noqa: E402
-from heterocache_b200.head_shard import HeadShardedCache  # noqa: E402
+from heterocache_b200.head_shard import HeadShardedCache, PeerGather  # noqa: E402
 
 
 def main():
@@ -28,22 +28,34 @@ def main():
         layers, KV, H, L = 2, 8, 32, 4096
         full = HeteroCache(_config(layers, KV, H))
         shard = HeadShardedCache(_config(layers, KV, H), rank, world)
-        # both ranks prefill the full cache and only their own shard
-        gens = _setup(dev, full.data, layers, KV, H, L, (full, [shard]))
+        # a second shard whose head outputs are gathered by the decode kernels
+        # over NVLink (PeerGather) instead of the NCCL all-gather
+        shard_p = HeadShardedCache(_config(layers, KV, H), rank, world)
+        peer = PeerGather(1, H // world, 128, torch.bfloat16, rank, world, device=dev)
+        # both ranks prefill the full cache and only their own shards
+        gens = _setup(dev, full.data, layers, KV, H, L, (full, [shard, shard_p]))
         print(f"rank {rank}: prefill done", flush=True)
         kl, hl = KV // world, H // world
         ks, hs = slice(rank * kl, (rank + 1) * kl), slice(rank * hl, (rank + 1) * hl)
         max_diff, same_rows, same_trig, n_trig = 0.0, True, True, 0
+        peer_exact, peer_diff = True, 0.0
         for step in range(12):
             for layer in range(layers):
                 q, k, v = (t.to(dev) for t in gens[layer].step())
                 full.update(k, v, layer)
                 shard.update(k[:, ks].contiguous(), v[:, ks].contiguous(), layer)
+                shard_p.update(k[:, ks].contiguous(), v[:, ks].contiguous(), layer)
                 o_full = full.attention(q, layer)
                 o_shard = shard.attention(q[:, hs].contiguous(), layer)
                 max_diff = max(max_diff, (o_full.float() - o_shard.float()).abs().max().item())
+                peer.barrier()
+                shard_p.attention(q[:, hs].contiguous(), layer, peer=peer, row0=0)
+                peer.barrier()
+                peer_exact &= bool(torch.equal(peer.out, o_shard))
+                peer_diff = max(peer_diff, (o_full.float() - peer.out.float()).abs().max().item())
                 full.decode_select(q, layer)
                 shard.decode_select(q[:, hs].contiguous(), layer)
+                shard_p.decode_select(q[:, hs].contiguous(), layer)
                 torch.cuda.synchronize()
                 jf, js = full._jobs[layer], shard.cache._jobs[layer]
                 if jf is not None and js is not None and js.n_jobs:
@@ -55,12 +67,16 @@ def main():
             print(f"rank {rank}: step {step} done", flush=True)
         full.check_errors()
         shard.check_errors()
-        res.update(max_diff=max_diff, same_rows=bool(same_rows), same_trig=bool(same_trig), n_trig=n_trig,
+        shard_p.check_errors()
+        peer.check_errors()
+        peer.close()
+        res.update(peer_exact=bool(peer_exact), peer_diff=peer_diff, max_diff=max_diff, same_rows=bool(same_rows), same_trig=bool(same_trig), n_trig=n_trig,
                    crossing=sum(len(s) for s in shard.remote))
     except Exception as e:  # reported through the result file
         res["error"] = repr(e)
     with open(os.path.join(os.environ["HC_SHARD_OUT"], f"rank{rank}.json"), "w") as f:
         json.dump(res, f)
+    dist.barrier()  # every rank has unmapped the others' buffers before any frees its own
     dist.destroy_process_group()
 
 

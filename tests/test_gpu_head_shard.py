@@ -134,11 +134,66 @@ def test_head_sharded_two_gpus_match_single_gpu(tmp_path):
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(here, "head_shard_worker.py")]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=240)
-    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    (tmp_path / "workers.log").write_text(proc.stdout + proc.stderr)
+    errs = [ln for ln in (proc.stdout + proc.stderr).splitlines() if "rror" in ln or "what()" in ln]
+    assert proc.returncode == 0, "\n".join(errs[:40]) + proc.stderr[-2000:]
     res = [json.load(open(tmp_path / f"rank{r}.json")) for r in range(2)]
     for r in res:
         assert "error" not in r, r
         assert r["same_rows"] and r["same_trig"], r
         assert r["max_diff"] <= 2e-2, r
         assert r["crossing"] > 0, r
+        # the gather by the decode kernels over NVLink: the NCCL result bit for bit
+        assert r["peer_exact"] and r["peer_diff"] <= 2e-2, r
     assert sum(r["n_trig"] for r in res) > 0
+
+
+def test_peer_gather_one_rank_writes_the_gathered_output(cuda_device):
+    """PeerGather on one rank: the decode combine's mirror stores land in the
+    gathered buffer, equal to the returned output (the 2-GPU test covers
+    stores into another GPU's memory)."""
+    from heterocache_b200.cache import HeteroCache
+    from heterocache_b200.head_shard import HeadShardedCache, PeerGather
+    dev = cuda_device
+    layers, KV, H, L = 1, 8, 32, 2048
+    shard = HeadShardedCache(_config(layers, KV, H), 0, 1)
+    ref = HeteroCache(_config(layers, KV, H))
+    gens = _setup(dev, ref.data, layers, KV, H, L, (ref, [shard]))
+    peer = PeerGather(1, H, 128, torch.bfloat16, 0, 1, device=dev)
+    for step in range(7):
+        q, k, v = (t.to(dev) for t in gens[0].step())
+        ref.update(k, v, 0)
+        shard.update(k, v, 0)
+        o = ref.attention(q, 0)
+        peer.barrier()
+        shard.attention(q, 0, peer=peer, row0=0)
+        peer.barrier()
+        torch.cuda.synchronize()
+        assert torch.equal(peer.out, o), step
+        ref.decode_select(q, 0)
+        shard.decode_select(q, 0)
+    peer.check_errors()
+    assert int(peer.counter.item()) == 14
+
+
+def test_peer_barrier_times_out_when_a_rank_never_arrives(cuda_device):
+    """A 2-rank barrier whose other rank never signals (its flag slot is a
+    buffer nothing writes): the bounded wait gives up and reports
+    HC_ERR_TIMEOUT; the context stays usable."""
+    from heterocache_b200 import ops
+    dev = cuda_device
+    flags = torch.zeros(2, dtype=torch.int32, device=dev)
+    other = torch.zeros(2, dtype=torch.int32, device=dev)  # stands for rank 1's flags
+    counter = torch.zeros(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ops.set_wait_limits(50_000_000)  # 50 ms
+    try:
+        ops.peer_barrier(0, 2, [flags.data_ptr(), other.data_ptr()], counter, err)
+        torch.cuda.synchronize()
+    finally:
+        ops.set_wait_limits(0)
+    assert int(err.item()) & (1 << 7)  # HC_ERR_TIMEOUT in the error flag
+    assert int(other[0].item()) == 1 and int(flags[0].item()) == 1  # this rank signalled both
+    assert int(counter.item()) == 1
+    x = torch.ones(4, device=dev)
+    assert float((x * 2).sum().item()) == 8.0
