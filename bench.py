@@ -969,6 +969,7 @@ def run_e2e(args, graph, qs, ks, vs, dev, world):
     hk = ks[:n].cpu().pin_memory()
     hv = vs[:n].cpu().pin_memory()
     hout = torch.empty((n,) + tuple(graph.out.shape), dtype=graph.out.dtype).pin_memory()
+    graph.prepare_host()  # the second buffer set's graphs, captured outside the timed region
     torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()

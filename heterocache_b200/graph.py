@@ -54,70 +54,97 @@ class DecodeStepGraph:
         self.out = torch.zeros(n, bsz, H, D, dtype=dt, device=dev)
         cache.prepare_decode(self.layers, self.q[0])
         cache.join_retrievals()  # no capture may wait on work recorded outside it
-        S = cache.decode_step
-        self.graphs: List[torch.cuda.CUDAGraph] = []
         # this library's kernel launches held by each phase's graph
         self.launches_per_phase: List[int] = []
+        self.graphs = self._capture((self.q, self.k, self.v, self.out), self.launches_per_phase)
+        self._alt = None  # a second buffer set and its graphs (run_host)
+
+    def _capture(self, bufs, launches=None) -> List[torch.cuda.CUDAGraph]:
+        """One graph per phase of the drift-check cycle, reading q/k/v from and
+        writing out to ``bufs``."""
+        cache = self.cache
         start = cache._qcount[self.layers[0]]
-        torch.cuda.synchronize(dev)
-        for phase in range(S):
+        torch.cuda.synchronize(cache._dev)
+        graphs = []
+        for phase in range(cache.decode_step):
             saved = cache._host_state()
             for l in self.layers:
                 cache._qcount[l] = phase
             g = torch.cuda.CUDAGraph()
             n0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g, capture_error_mode="thread_local"):
-                self._eager_step()
-            self.launches_per_phase.append(ops.LAUNCHES[0] - n0)
+                self._eager_step(*bufs)
+            if launches is not None:
+                launches.append(ops.LAUNCHES[0] - n0)
             cache._restore_host_state(saved)
-            self.graphs.append(g)
+            graphs.append(g)
         for l in self.layers:
             cache._qcount[l] = start
+        return graphs
 
-    def _eager_step(self) -> None:
+    def _eager_step(self, q=None, k=None, v=None, out=None) -> None:
         c = self.cache
+        q = self.q if q is None else q
+        k = self.k if k is None else k
+        v = self.v if v is None else v
+        out = self.out if out is None else out
         for i, l in enumerate(self.layers):
-            c.update(self.k[i], self.v[i], l, {"query_states": self.q[i], "defer_append": True})
+            c.update(k[i], v[i], l, {"query_states": q[i], "defer_append": True})
             if self.order == "qwen":
-                c.decode_select(self.q[i], l)
-            c.attention(self.q[i], l, out=self.out[i])
+                c.decode_select(q[i], l)
+            c.attention(q[i], l, out=out[i])
             if self.order == "llama":
-                c.decode_select(self.q[i], l, defer=True)
+                c.decode_select(q[i], l, defer=True)
         c.join_retrievals()  # runs the put-off drift checks as one batch first
 
     def step(self) -> torch.Tensor:
         """Replay one decode step (inputs already in ``self.q/k/v``)."""
+        return self._step(self.graphs, self.out)
+
+    def _step(self, graphs, out) -> torch.Tensor:
         c = self.cache
         phase = c._qcount[self.layers[0]]
         for l in self.layers:
             c._append_bookkeeping(l)
-        self.graphs[phase].replay()
+        graphs[phase].replay()
         nxt = (phase + 1) % c.decode_step
         for l in self.layers:
             c._qcount[l] = nxt
         if 0 in self.layers:  # as update() of layer 0 counts the token
             c._seen_tokens += 1
-        return self.out
+        return out
+
+    def prepare_host(self) -> None:
+        """Capture the second buffer set's graphs that ``run_host`` alternates
+        with (once; ``run_host`` does it on its first call otherwise)."""
+        if self._alt is not None:
+            return
+        dev = self.q.device
+        bufs = (torch.zeros_like(self.q), torch.zeros_like(self.k), torch.zeros_like(self.v),
+                torch.zeros_like(self.out))
+        self.cache.join_retrievals()  # no capture may wait on work recorded outside it
+        self._alt = (bufs, self._capture(bufs))
+        self._h2d, self._d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
 
     def run_host(self, host_q: torch.Tensor, host_k: torch.Tensor, host_v: torch.Tensor,
                  host_out: torch.Tensor) -> None:
         """Decode ``len(host_q)`` steps from host inputs into host outputs
         (pinned memory: ``host_q[s]`` shaped as ``self.q``, ``host_out[s]`` as
-        ``self.out``), the host-link copies overlapped with the replays: step
-        s + 1's inputs cross into a staging buffer on a copy stream while step
-        s runs, and step s's outputs leave from a staging buffer on another
-        while step s + 1 runs.  Work already queued on the current stream
-        comes first; the current stream waits for the last copy back."""
+        ``self.out``), the host-link copies overlapped with the replays.  Steps
+        alternate between two buffer sets, each with its own graphs (the
+        second set is captured by ``prepare_host`` or on the first call): step s + 1's inputs cross
+        into its set on a copy stream while step s runs, and step s's outputs
+        leave from its set on another copy stream while step s + 1 runs; no
+        device-side copy is added to the step.  Work already queued on the
+        current stream comes first; the current stream waits for the last
+        copy back."""
         n = host_q.shape[0]
         if n == 0:
             return
         dev = self.q.device
         cur = torch.cuda.current_stream(dev)
-        if not hasattr(self, "_h2d"):
-            self._h2d, self._d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-            self._stage_in = [(torch.empty_like(self.q), torch.empty_like(self.k), torch.empty_like(self.v))
-                              for _ in range(2)]
-            self._stage_out = [torch.empty_like(self.out) for _ in range(2)]
+        self.prepare_host()
+        sets = [((self.q, self.k, self.v, self.out), self.graphs), self._alt]
         h2d, d2h = self._h2d, self._d2h
         h2d.wait_stream(cur)
         d2h.wait_stream(cur)
@@ -128,30 +155,29 @@ class DecodeStepGraph:
 
         def load(s: int) -> None:
             j = s % 2
+            (q, k, v, _), _ = sets[j]
             with torch.cuda.stream(h2d):
                 if s >= 2:
-                    h2d.wait_event(in_free[j])  # step s - 2 took its inputs from this buffer
-                for dst, src in zip(self._stage_in[j], (host_q[s], host_k[s], host_v[s])):
+                    h2d.wait_event(in_free[j])  # step s - 2 has run on this set
+                for dst, src in zip((q, k, v), (host_q[s], host_k[s], host_v[s])):
                     dst.copy_(src, non_blocking=True)
                 in_ready[j].record(h2d)
 
         load(0)
         for s in range(n):
             i = s % 2
+            (_, _, _, out), graphs = sets[i]
             if s + 1 < n:
                 load(s + 1)
             cur.wait_event(in_ready[i])
-            for dst, src in zip((self.q, self.k, self.v), self._stage_in[i]):
-                dst.copy_(src)
-            in_free[i].record(cur)
-            out = self.step()
             if s >= 2:
-                cur.wait_event(out_done[i])  # step s - 2's outputs have left this buffer
-            self._stage_out[i].copy_(out)
+                cur.wait_event(out_done[i])  # step s - 2's outputs have left this set
+            self._step(graphs, out)
+            in_free[i].record(cur)
             out_ready[i].record(cur)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(out_ready[i])
-                host_out[s].copy_(self._stage_out[i], non_blocking=True)
+                host_out[s].copy_(out, non_blocking=True)
                 out_done[i].record(d2h)
         cur.wait_stream(d2h)
         cur.wait_stream(h2d)
