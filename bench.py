@@ -757,7 +757,7 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     ``--gather nccl``, by an eager NCCL all-gather after each replay --, and
     broadcasts of pivot position lists at check steps).  Returns the
     measurement (all ranks take part; the timings are the max over ranks)."""
-    from heterocache_b200.cache import HeteroCacheConfig
+    from heterocache_b200.cache import HeteroCacheConfig, flush_checks_together
     from heterocache_b200.head_shard import HeadShardedCache, PeerGather, gather_heads
     from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
     dev = torch.device("cuda", local_rank)
@@ -834,11 +834,13 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
                 else:
                     view.cache.attention(qb[i], 0, out=local[i:i + 1])
             for i, view in enumerate(views):
-                view.select_local(qb[i], 0)
+                view.select_local(qb[i], 0, defer=True)
         else:
             for i, view in enumerate(views):
                 view.attention(qb[i], 0, out=out[i:i + 1])
-                view.decode_select(qb[i], 0)
+                view.decode_select(qb[i], 0, defer=True)
+        # every sequence's due drift check in one batched launch
+        flush_checks_together(inner)
         for c in inner:
             c.join_retrievals()
         if peer is not None:

@@ -799,3 +799,50 @@ class HeteroCache(_CacheBase):
         if q is not None and not selected:
             self._q_staged[layer_idx] = True  # decode_select of this step comes next
         return out
+
+
+def flush_checks_together(caches) -> None:
+    """``flush_checks`` over several caches at once: every drift check the
+    caches put off (``decode_select(..., defer=True)``) in one
+    hc_drift_check_batch call, then each cache's retrievals -- e.g. the
+    independent sequences of one batch, each with its own cache, whose
+    checks would otherwise take a launch each.  The caches must share the
+    check's shape: dtype, KV heads, GQA groups, ``decode_step``, prefill
+    length, budget, pooling and stable threshold (the same model and prompt
+    length).  Results equal per-cache flushes; a device-side error of the
+    batch is reported in the first cache's error flag."""
+    pend = [(c, c._deferred) for c in caches if c._deferred]
+    if not pend:
+        return
+    first = pend[0][0]
+    shape = lambda c: (c.key_pools[c._deferred[0]].dtype, c.num_kv_heads, c.num_key_value_groups,  # noqa: E731
+                       c.decode_step, c.prefill_len, c.base_compress_len, c.pooling, c.kernel_size,
+                       c.stable_threshold, c._dev)
+    want = shape(first)
+    for c, _ in pend:
+        if shape(c) != want:
+            raise ValueError("flush_checks_together: the caches' drift checks differ in shape")
+    for c, layers in pend:
+        c._deferred = []
+        for l in layers:
+            c._wait_retrieval(l)
+    key = tuple((id(c), tuple(layers)) for c, layers in pend)
+    arr = first._batch_arrays.get(key)
+    if arr is None:
+        descs = []
+        for c, layers in pend:
+            for l in layers:
+                descs.extend(c._drift_descs(l))
+        arr = ops.drift_jobs_array(descs)
+        first._batch_arrays[key] = arr
+    ops.drift_check_batch(arr, dtype=want[0], device=first._dev, num_kv_heads=first.num_kv_heads,
+                          groups=first.num_key_value_groups, steps=first.decode_step, seq_len=first.prefill_len,
+                          pooling=first.pooling, kernel_size=first.kernel_size, topk=first.base_compress_len,
+                          threshold=first.stable_threshold, workspace=first._ws_score, err=first._err,
+                          jobs_per_launch=first.drift_batch_per_launch)
+    for c, layers in pend:
+        for l in layers:
+            jobs = c._jobs[l]
+            if c.record_checks:
+                c._log_check(l, jobs, None)
+            c._retrieve_layer(l, jobs)

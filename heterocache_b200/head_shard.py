@@ -184,13 +184,15 @@ class HeadShardedCache:
 
     # The three phases of decode_select, callable one by one (the broadcast
     # between them is the only cross-rank step).
-    def select_local(self, query_states, layer_idx) -> bool:
+    def select_local(self, query_states, layer_idx, defer: bool = False) -> bool:
         """The local cache's decode_select; True at a check step with star
-        groups that cross ranks."""
+        groups that cross ranks.  With ``defer`` a due check is put off (see
+        ``HeteroCache.decode_select``); it must be flushed before
+        ``remote_checks``."""
         # the local cache counts the buffered queries (its host state, which a
         # captured decode step saves and restores)
         check = self.cache._qcount[layer_idx] + 1 >= self.cache.decode_step
-        self.cache.decode_select(query_states, layer_idx)
+        self.cache.decode_select(query_states, layer_idx, defer=defer)
         return check and bool(self.remote[layer_idx])
 
     def _max_len(self, spec) -> int:

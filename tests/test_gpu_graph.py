@@ -171,3 +171,68 @@ def test_run_host_matches_step_by_step(cuda_device):
     for l in range(layers):
         assert torch.equal(a.key_pools[l], b.key_pools[l])
         assert torch.equal(a.heads_len[l], b.heads_len[l])
+
+
+@pytest.mark.parametrize("per_launch", [1, 0])
+def test_checks_of_several_caches_in_one_batch(cuda_device, per_launch):
+    """flush_checks_together: the put-off drift checks of three independent
+    caches (three sequences) in one batch, against each cache flushing its
+    own.  One check per launch: bit-identical; the default batching adds the
+    softmax sums in another order: same triggers, outputs within the bf16
+    tolerance."""
+    from heterocache_b200.cache import flush_checks_together
+    dev, geo = cuda_device, LLAMA_8B
+    KV, H, D, L, n_steps = geo.num_kv_heads, geo.num_heads, geo.head_dim, 3000, 11
+
+    def make(seed):
+        data = derive_runtime_data(synthetic_roles(1, KV, seed=13), 1, KV)
+        cfg = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.9, real_offload=False,
+                                max_gen_len=32, decode_step=5, pooling="avgpool", kernel_size=5,
+                                num_attn_heads=H, num_kv_heads=KV, num_layers=1)
+        c = HeteroCache(cfg)
+        q, k, v = prefill_inputs(geo, L, seed=seed, dtype=torch.bfloat16, q_positions=32)
+        qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+        c.update(kd, vd, 0)
+        c.init_coefficient(qd, kd, 0)
+        c.prefill_select(qd, kd, vd, 0)
+        return c, q[:, :, -1:, :]
+
+    seeds = (201, 202, 203)
+    own = [make(s)[0] for s in seeds]
+    both = [make(s) for s in seeds]
+    tog = [c for c, _ in both]
+    tog[0].drift_batch_per_launch = per_launch
+    for c in own:
+        c.drift_batch_per_launch = per_launch
+    gens = [DriftingDecode(geo, seed=s + 7, q0=q0, dtype=torch.bfloat16) for s, (_, q0) in zip(seeds, both)]
+    n_trig = 0
+    for step in range(n_steps):
+        qkv = [tuple(t.to(dev) for t in g.step()) for g in gens]
+        outs = {}
+        for name, caches in (("own", own), ("tog", tog)):
+            res = []
+            for c, (q, k, v) in zip(caches, qkv):
+                c.update(k, v, 0)
+                res.append(c.attention(q, 0))
+                c.decode_select(q, 0, defer=True)
+            if name == "own":
+                for c in caches:
+                    c.flush_checks()
+            else:
+                flush_checks_together(caches)
+            outs[name] = torch.stack(res)
+        torch.cuda.synchronize()
+        if per_launch == 1:
+            assert torch.equal(outs["own"], outs["tog"]), step
+        else:
+            assert (outs["own"].float() - outs["tog"].float()).abs().max().item() <= 2e-2, step
+        for a, b in zip(own, tog):
+            ja, jb = a._jobs[0], b._jobs[0]
+            assert torch.equal(ja.trigger[:ja.n_jobs], jb.trigger[:jb.n_jobs]), step
+            n_trig += int(jb.trigger[:jb.n_jobs].sum())
+            if per_launch == 1:
+                assert torch.equal(a.key_pools[0], b.key_pools[0]), step
+                assert torch.equal(a.prefill_topk_set[0], b.prefill_topk_set[0]), step
+    for c in own + tog:
+        c.check_errors()
+    assert n_trig > 0
