@@ -69,6 +69,8 @@ def parse():
                                                          "(default: CUDA-graph replay)")
     ap.add_argument("--shard", default="sequences", choices=["sequences", "heads"])
     ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
+    ap.add_argument("--serial-sequences", action="store_true",
+                    help="config4: the sequences' kernels one after another on one stream (default: a stream each)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="head-sharded mode: head outputs gathered by the decode kernels over NVLink (peer) or "
                          "by an NCCL all-gather")
@@ -821,24 +823,41 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     if heads_mode and getattr(args, "gather", "peer") == "peer":
         peer = PeerGather(n_local, hl, D, torch.bfloat16, rank, world, device=dev)
 
-    def local_step():
-        """Everything but the NCCL calls: captured in the phase graphs."""
-        for i, view in enumerate(views):
-            view.update(kb[i], vb[i], 0, {"query_states": qb[i]})
+    # the sequences are independent: each runs its update, attention and
+    # drift-check bookkeeping on a stream of its own, so that their chains of
+    # small, latency-bound kernels overlap on the GPU (the fork and join are
+    # captured in the phase graphs); the batched drift checks and the peer
+    # barriers run on the step's stream
+    seq_streams = None if getattr(args, "serial_sequences", False) else [torch.cuda.Stream(dev) for _ in views]
+
+    def one_sequence(i, view):
+        view.update(kb[i], vb[i], 0, {"query_states": qb[i]})
         if heads_mode:
             if peer is not None:
-                peer.barrier()  # every rank has read the previous step's gathered output
-            for i, view in enumerate(views):
-                if peer is not None:
-                    view.attention(qb[i], 0, peer=peer, row0=i)
-                else:
-                    view.cache.attention(qb[i], 0, out=local[i:i + 1])
-            for i, view in enumerate(views):
-                view.select_local(qb[i], 0, defer=True)
+                view.attention(qb[i], 0, peer=peer, row0=i)
+            else:
+                view.cache.attention(qb[i], 0, out=local[i:i + 1])
+            view.select_local(qb[i], 0, defer=True)
         else:
+            view.attention(qb[i], 0, out=out[i:i + 1])
+            view.decode_select(qb[i], 0, defer=True)
+
+    def local_step():
+        """Everything but the NCCL calls: captured in the phase graphs."""
+        cur = torch.cuda.current_stream(dev)
+        if peer is not None:
+            peer.barrier()  # every rank has read the previous step's gathered output
+        if seq_streams is None:
             for i, view in enumerate(views):
-                view.attention(qb[i], 0, out=out[i:i + 1])
-                view.decode_select(qb[i], 0, defer=True)
+                one_sequence(i, view)
+        else:
+            for st in seq_streams:
+                st.wait_stream(cur)
+            for i, view in enumerate(views):
+                with torch.cuda.stream(seq_streams[i]):
+                    one_sequence(i, view)
+            for st in seq_streams:
+                cur.wait_stream(st)
         # every sequence's due drift check in one batched launch
         flush_checks_together(inner)
         for c in inner:
