@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--seqs", type=int, default=8, help="config4: sequences in the batch")
     ap.add_argument("--serial-sequences", action="store_true",
                     help="config4: the sequences' kernels one after another on one stream (default: a stream each)")
+    ap.add_argument("--per-sequence-launches", action="store_true",
+                    help="config4: each sequence's own decode launch (default: the sequences' pages in one "
+                         "CacheGroup pool per GPU, attended in one launch)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="head-sharded mode: head outputs gathered by the decode kernels over NVLink (peer) or "
                          "by an NCCL all-gather")
@@ -759,7 +762,7 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     ``--gather nccl``, by an eager NCCL all-gather after each replay --, and
     broadcasts of pivot position lists at check steps).  Returns the
     measurement (all ranks take part; the timings are the max over ranks)."""
-    from heterocache_b200.cache import HeteroCacheConfig, flush_checks_together
+    from heterocache_b200.cache import CacheGroup, HeteroCacheConfig, attention_together, flush_checks_together
     from heterocache_b200.head_shard import HeadShardedCache, PeerGather, gather_heads
     from heterocache_b200.synthetic import LLAMA_8B, prefill_kv_device
     dev = torch.device("cuda", local_rank)
@@ -780,6 +783,9 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         views = [make_cache(data, 1) for _ in seqs]
         inner = views
         kl, hl = KV, H
+    # the GPU's sequences' pages in one pool: one decode launch a step covers
+    # them all (adopted before the prefill)
+    group = None if getattr(args, "per_sequence_launches", False) else CacheGroup(inner)
     ks, hs = slice(rank * kl, (rank + 1) * kl) if heads_mode else slice(None), \
         slice(rank * hl, (rank + 1) * hl) if heads_mode else slice(None)
     # prefill: every sequence's q/K/V from its own seed (identical on every
@@ -828,7 +834,8 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     # small, latency-bound kernels overlap on the GPU (the fork and join are
     # captured in the phase graphs); the batched drift checks and the peer
     # barriers run on the step's stream
-    seq_streams = None if getattr(args, "serial_sequences", False) else [torch.cuda.Stream(dev) for _ in views]
+    seq_streams = (None if getattr(args, "serial_sequences", False) or group is not None
+                   else [torch.cuda.Stream(dev) for _ in views])
 
     def one_sequence(i, view):
         view.update(kb[i], vb[i], 0, {"query_states": qb[i]})
@@ -847,7 +854,24 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         cur = torch.cuda.current_stream(dev)
         if peer is not None:
             peer.barrier()  # every rank has read the previous step's gathered output
-        if seq_streams is None:
+        if group is not None:
+            # each sequence's token pending; one launch attends over every
+            # sequence's pages plus its token, then each sequence's append
+            # runs on its side stream
+            for i, view in enumerate(views):
+                view.update(kb[i], vb[i], 0, {"query_states": qb[i], "defer_append": True})
+            q_all = qb[:, 0]
+            if peer is not None:
+                attention_together(group, q_all, 0, mirrors=peer.mirrors(0),
+                                   mirror_batch_stride=peer.mirror_batch_stride)
+            else:
+                attention_together(group, q_all, 0, out=local if heads_mode else out)
+            for i, view in enumerate(views):
+                if heads_mode:
+                    view.select_local(qb[i], 0, defer=True)
+                else:
+                    view.decode_select(qb[i], 0, defer=True)
+        elif seq_streams is None:
             for i, view in enumerate(views):
                 one_sequence(i, view)
         else:
@@ -942,6 +966,8 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     mode = (f"KV-head-sharded x{world} (each GPU {KV // world} of the 8 KV heads of every sequence; {gather})"
             if heads_mode
             else f"sequence-sharded x{world} ({n_seq // world} sequences per GPU, no data-path collective)")
+    mode += ("; the GPU's sequences in one CacheGroup pool, one decode launch a step" if group is not None
+             else "; a decode launch per sequence")
     res = {"value": n_seq * 1000.0 / ms_step, "unit": "tokens/s", "ms_per_step": ms_step, "steps": steps,
            "sequences": n_seq, "context": L, "parallelism": mode}
     if heads_mode and peer is None:

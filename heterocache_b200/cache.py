@@ -202,6 +202,9 @@ class HeteroCache(_CacheBase):
         self._mapped: List[Optional[np.ndarray]] = [None] * n
         # opt-in diagnostics for parity tests: pooled scores and selections
         self.record_checks = bool(getattr(cache_config, "record_checks", False))
+        # a CacheGroup this cache's pages live in (shared pool per layer)
+        self._group: Optional["CacheGroup"] = None
+        self._gidx = 0
         # drift checks put off by decode_select(..., defer=True) until
         # flush_checks(), which runs them as one batch.  Off by default with
         # the pinned-host tier: there a layer's retrieval should start right
@@ -278,13 +281,25 @@ class HeteroCache(_CacheBase):
             mapped[r] = nb
         if ptr > total:
             raise RuntimeError(f"Layer {layer_idx}: Allocation logic error! Used more than allocated.")
-        self.key_pools[layer_idx] = torch.zeros(total, PAGE, 1, self.head_dim, device=device, dtype=dtype)
-        self.value_pools[layer_idx] = torch.zeros(total, PAGE, 1, self.head_dim, device=device, dtype=dtype)
-        self.block_tables[layer_idx] = torch.from_numpy(bt).to(device)
-        self.free_blocks[layer_idx] = torch.arange(ptr, total, dtype=torch.int32, device=device)
+        if self._group is not None:
+            # pages in the group's shared pool: this cache's ids start at its
+            # range's offset; page table and lengths are rows of shared tensors
+            kp, vp, off, bt_t, hl_t = self._group._layer_storage(self, layer_idx, total, rows, max_blocks,
+                                                                 device, dtype)
+            bt_t.copy_(torch.from_numpy(np.where(bt >= 0, bt + off, bt).astype(np.int32)))
+            hl_t.zero_()
+            self.key_pools[layer_idx], self.value_pools[layer_idx] = kp, vp
+            self.block_tables[layer_idx] = bt_t
+            self.free_blocks[layer_idx] = torch.arange(off + ptr, off + total, dtype=torch.int32, device=device)
+            self.heads_len[layer_idx] = hl_t
+        else:
+            self.key_pools[layer_idx] = torch.zeros(total, PAGE, 1, self.head_dim, device=device, dtype=dtype)
+            self.value_pools[layer_idx] = torch.zeros(total, PAGE, 1, self.head_dim, device=device, dtype=dtype)
+            self.block_tables[layer_idx] = torch.from_numpy(bt).to(device)
+            self.free_blocks[layer_idx] = torch.arange(ptr, total, dtype=torch.int32, device=device)
+            self.heads_len[layer_idx] = torch.zeros(rows, dtype=torch.int32, device=device)
         self.free_block_pointers[layer_idx] = 0
         self._free_ptr[layer_idx] = torch.zeros(1, dtype=torch.int32, device=device)
-        self.heads_len[layer_idx] = torch.zeros(rows, dtype=torch.int32, device=device)
         self.prefill_boundary_blocks[layer_idx] = pre_total
         self.layer_head_capacities[layer_idx] = caps
         self._hlen[layer_idx] = np.zeros(rows, dtype=np.int64)
@@ -502,7 +517,11 @@ class HeteroCache(_CacheBase):
             if bsz != 1 and self.data["leader_member_relations"][layer_idx]:
                 raise NotImplementedError("decode_select supports batch size 1 (as the reference, "
                                           "cache_utils.py:1093)")
-            self._qbuf[layer_idx] = torch.empty(S, H, D, dtype=query_states.dtype, device=query_states.device)
+            if self._group is not None:
+                self._qbuf[layer_idx] = self._group._query_buffer(self, layer_idx, S, H, D, query_states.dtype,
+                                                                  query_states.device)
+            else:
+                self._qbuf[layer_idx] = torch.empty(S, H, D, dtype=query_states.dtype, device=query_states.device)
         relations = self.data["leader_member_relations"][layer_idx]
         if self._jobs[layer_idx] is None and relations:
             remote = self.data.get("remote_member_alloc")
@@ -846,3 +865,147 @@ def flush_checks_together(caches) -> None:
             if c.record_checks:
                 c._log_check(l, jobs, None)
             c._retrieve_layer(l, jobs)
+
+
+class CacheGroup:
+    """Independent sequences -- one ``HeteroCache`` each, batch 1, as the
+    reference's drift check requires (heterocache/cache_utils.py:1093) --
+    whose pages share one pool per layer, so that one decode launch
+    (``attention_together``) attends over all of them instead of one launch
+    per sequence.  Each member's page ids are a range of its own in the
+    shared pool, and its page table and lengths are rows of shared tensors;
+    everything else (page appends, drift checks, retrievals, free lists) stays
+    per member and unchanged.  Adopt the caches before their prefill; they
+    must need the same pages per layer (the same model, roles and prompt
+    length)."""
+
+    def __init__(self, caches):
+        self.members = list(caches)
+        for i, c in enumerate(self.members):
+            if any(p is not None for p in c.key_pools):
+                raise RuntimeError("CacheGroup: adopt caches before their prefill")
+            c._group, c._gidx = self, i
+        self._layers: Dict[int, dict] = {}
+        self._qbufs: Dict[int, torch.Tensor] = {}
+        self._ws: Optional[Workspace] = None
+
+    def _query_buffer(self, cache, layer, S, H, D, dtype, device):
+        """Member's drift-check query buffer [S, H, D]: row ``cache._gidx`` of
+        the layer's [members, S, H, D] buffer, so that a step stages every
+        member's query in one copy."""
+        qb = self._qbufs.get(layer)
+        if qb is None:
+            qb = torch.empty(len(self.members), S, H, D, dtype=dtype, device=device)
+            self._qbufs[layer] = qb
+        if tuple(qb.shape[1:]) != (S, H, D) or qb.dtype != dtype:
+            raise ValueError("CacheGroup: the members' query buffers differ in shape")
+        return qb[cache._gidx]
+
+    def _workspace(self, device) -> Workspace:
+        if self._ws is None:
+            self._ws = Workspace(device)
+        return self._ws
+
+    def _layer_storage(self, cache, layer, total, rows, max_blocks, device, dtype):
+        st = self._layers.get(layer)
+        n = len(self.members)
+        if st is None:
+            D = cache.head_dim
+            st = dict(slot=total, rows=rows, mb=max_blocks, dtype=dtype, device=torch.device(device),
+                      kp=torch.zeros(n * total, PAGE, 1, D, device=device, dtype=dtype),
+                      vp=torch.zeros(n * total, PAGE, 1, D, device=device, dtype=dtype),
+                      bt=torch.full((n * rows, max_blocks), -1, dtype=torch.int32, device=device),
+                      hl=torch.zeros(n * rows, dtype=torch.int32, device=device))
+            self._layers[layer] = st
+        if (total > st["slot"] or rows != st["rows"] or max_blocks != st["mb"] or dtype != st["dtype"]):
+            raise ValueError("CacheGroup: the members need different pages for this layer")
+        i = cache._gidx
+        return st["kp"], st["vp"], i * st["slot"], st["bt"][i * rows:(i + 1) * rows], st["hl"][i * rows:(i + 1) * rows]
+
+
+def _batch_view(ts):
+    """[n, ...] view over n batch-1 tensors of one shape and strides that sit
+    at a constant distance in one storage (rows of one buffer), else None."""
+    t0 = ts[0]
+    if len(ts) == 1:
+        return t0
+    es = t0.element_size()
+    d = ts[1].data_ptr() - t0.data_ptr()
+    if d <= 0 or d % es:
+        return None
+    for i, t in enumerate(ts):
+        if (t.shape != t0.shape or t.stride() != t0.stride() or t.dtype != t0.dtype
+                or t.untyped_storage().data_ptr() != t0.untyped_storage().data_ptr()
+                or t.data_ptr() - t0.data_ptr() != i * d):
+            return None
+    return t0.as_strided((len(ts),) + tuple(t0.shape[1:]), (d // es,) + tuple(t0.stride()[1:]))
+
+
+def attention_together(group: CacheGroup, query_states, layer_idx, scale: float = 0.0, out=None, mirrors=None,
+                       mirror_batch_stride: int = 0):
+    """Every member's decode attention for one layer in one launch:
+    ``query_states`` [members, H, 1, D] (row i: member i's query) ->
+    [members, H, D], as each member's ``attention`` would give (the split of
+    the tokens over the launch differs, so the fp32 merge order does too).
+    Members with a deferred append (``update(..., {"defer_append": True})``)
+    all must have one: the step's tokens are merged from their k/v, then each
+    member appends on its own side stream.  ``mirrors`` as for
+    ``HeteroCache.attention``, row b of the batch being member b.  A
+    device-side error of the launch is reported in the first member's flag."""
+    members = group.members
+    for c in members:
+        if c._deferred and layer_idx in c._deferred:
+            c.flush_checks()
+        c._wait_retrieval(layer_idx)
+        c._wait_append(layer_idx)
+    st = group._layers[layer_idx]
+    c0 = members[0]
+    if query_states.shape[0] != len(members):
+        raise ValueError("attention_together: one query row per member")
+    ws = group._workspace(c0._dev)
+    total = sum(int(c._hlen[layer_idx].sum()) for c in members)
+    pends = [c._pending[layer_idx] for c in members]
+    if all(p is None for p in pends):
+        return ops.flash_decode(query_states, st["kp"], st["vp"], st["bt"], st["hl"], num_kv_heads=c0.num_kv_heads,
+                                scale=scale, out=out, workspace=ws, err=c0._err, total_tokens_hint=total,
+                                mirrors=mirrors, mirror_batch_stride=mirror_batch_stride)
+    if any(p is None for p in pends):
+        raise RuntimeError("attention_together: some members have the step's token pending and some not")
+    for c in members:
+        c._pending[layer_idx] = None
+    # the step's queries for the drift checks (this stream): one copy when
+    # they all go to the same slot of the group's buffer
+    stage = [(c, p[2], p[3]) for c, p in zip(members, pends) if p[2] is not None]
+    qg = group._qbufs.get(layer_idx)
+    if (qg is not None and len(stage) == len(members) and len({sl for _, _, sl in stage}) == 1
+            and all(c._qbuf[layer_idx].data_ptr() == qg[c._gidx].data_ptr() for c in members)):
+        qs = _batch_view([q for _, q, _ in stage])
+        if qs is None:
+            qs = torch.cat([q for _, q, _ in stage], 0)
+        qg[:, stage[0][2]].copy_(qs[:, :, 0, :])
+    else:
+        for c, q, slot in stage:
+            c._qbuf[layer_idx][slot].copy_(q[0, :, 0, :])
+    k_new = _batch_view([p[0] for p in pends])
+    v_new = _batch_view([p[1] for p in pends])
+    k_new = torch.cat([p[0] for p in pends], 0) if k_new is None else k_new
+    v_new = torch.cat([p[1] for p in pends], 0) if v_new is None else v_new
+    out = ops.flash_decode(query_states, st["kp"], st["vp"], st["bt"], st["hl"], num_kv_heads=c0.num_kv_heads,
+                           scale=scale, out=out, workspace=ws, err=c0._err, total_tokens_hint=total, k_new=k_new,
+                           v_new=v_new, mirrors=mirrors, mirror_batch_stride=mirror_batch_stride)
+    main = torch.cuda.current_stream(c0._dev)
+    for c, (k, v, q, slot, selected) in zip(members, pends):
+        side = c._side()
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            ops.decode_append(k, v, c.key_pools[layer_idx], c.value_pools[layer_idx], c.block_tables[layer_idx],
+                              c.heads_len[layer_idx], c.free_blocks[layer_idx], c._free_ptr[layer_idx], c._err)
+        if not torch.cuda.is_current_stream_capturing():
+            for t in (k, v):
+                t.record_stream(side)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        c._append_done[layer_idx] = ev
+        if q is not None and not selected:
+            c._q_staged[layer_idx] = True  # decode_select of this step comes next
+    return out

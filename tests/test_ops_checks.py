@@ -66,3 +66,19 @@ def test_flash_decode_rejects_query_heads_that_do_not_split_over_the_kv_heads():
         ops.flash_decode(torch.zeros(1, 30, 1, 128), torch.zeros(4, 256, 1, 128), torch.zeros(4, 256, 1, 128),
                          torch.zeros(8, 5, dtype=i32), torch.zeros(8, dtype=i32), num_kv_heads=8, workspace=None,
                          err=torch.zeros(1, dtype=i32))
+
+
+def test_batch_view_of_rows_of_one_buffer():
+    """attention_together's batching of the members' pending k/v and queries:
+    rows of one buffer give a strided view over all of them (no copy);
+    tensors of their own give None (the caller concatenates)."""
+    from heterocache_b200.cache import _batch_view
+    buf = torch.arange(4 * 3 * 8 * 2, dtype=torch.float32).reshape(4, 1, 3, 8, 2)
+    rows = [buf[i] for i in range(4)]
+    v = _batch_view(rows)
+    assert v is not None and v.shape == (4, 3, 8, 2) and torch.equal(v, buf[:, 0])
+    sub = [buf[i, :, 1:] for i in range(4)]  # strided rows: still one view
+    assert torch.equal(_batch_view(sub), buf[:, 0, 1:])
+    assert _batch_view([r.clone() for r in rows]) is None
+    assert _batch_view([rows[0], rows[2], rows[1]]) is None
+    assert _batch_view(rows[:1]) is rows[0]
