@@ -826,8 +826,11 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
 
     local = torch.zeros(n_local, hl, D, dtype=torch.bfloat16, device=dev)
     peer = None
+    words = 0
     if heads_mode and getattr(args, "gather", "peer") == "peer":
-        peer = PeerGather(n_local, hl, D, torch.bfloat16, rank, world, device=dev)
+        # mailboxes: row i's pivots' position lists at words i * words ..
+        words = views[0].remote_words(0)
+        peer = PeerGather(n_local, hl, D, torch.bfloat16, rank, world, device=dev, mail_words=n_local * words)
 
     # the sequences are independent: each runs its update, attention and
     # drift-check bookkeeping on a stream of its own, so that their chains of
@@ -852,6 +855,7 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     def local_step():
         """Everything but the NCCL calls: captured in the phase graphs."""
         cur = torch.cuda.current_stream(dev)
+        check = inner[0]._qcount[0] + 1 >= STEPS_PER_CHECK
         if peer is not None:
             peer.barrier()  # every rank has read the previous step's gathered output
         if group is not None:
@@ -887,15 +891,22 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         for c in inner:
             c.join_retrievals()
         if peer is not None:
-            peer.barrier()  # every rank's head rows have landed in every rank's peer.out
+            if check and words:  # the pivots' position lists into the other ranks' mailboxes
+                for i, view in enumerate(views):
+                    view.publish_remote(0, peer, i * words)
+            peer.barrier()  # every rank's head rows (and mail) have landed on every rank
+            if check and words:
+                for i, view in enumerate(views):
+                    view.retrieve_remote_mail(0, peer, i * words)
 
     gather_events = []
 
     def collectives(check, timed=False):
-        """Head-sharded mode, eager (NCCL stays out of the graphs): the output
-        all-gather of every sequence in one call, and at a check step the
-        position-list broadcasts and the retrievals of satellites whose pivot
-        sits on another GPU."""
+        """Head-sharded mode with ``--gather nccl``, eager (NCCL stays out of
+        the graphs): the output all-gather of every sequence in one call, and
+        at a check step the position-list broadcasts and the retrievals of
+        satellites whose pivot sits on another GPU (with the kernel-side
+        gather both happen inside the step's graph)."""
         if not heads_mode:
             return
         if peer is None:
@@ -906,7 +917,7 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
             if timed:
                 e1.record()
                 gather_events.append((e0, e1))
-        if check:
+        if check and peer is None:
             for view in views:
                 view.remote_checks(0)
 
@@ -977,7 +988,8 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
                              else "none (one rank holds every head)")
     elif heads_mode:
         res["collective"] = ("hc_flash_decode_peer output mirrors (P2P stores over NVLink to CUDA IPC mappings) "
-                             "+ hc_peer_barrier x2 per step" if world > 1 else
+                             "+ hc_peer_barrier x2 per step; at check steps the pivots' position lists stored "
+                             "into the other ranks' mailboxes by hc_peer_put" if world > 1 else
                              "hc_flash_decode_peer into the rank's own gathered output (one rank)")
     return res
 

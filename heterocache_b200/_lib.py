@@ -76,6 +76,7 @@ SIGNATURES = {
                                      c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p, c_int, c_void_p,
                                      c_int64, c_void_p, c_size_t, c_void_p, c_void_p]),
     "hc_peer_barrier": (c_int, [c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "hc_peer_put": (c_int, [c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p]),
     "hc_enable_peer_access": (c_int, [c_int]),
     "hc_ipc_export": (c_int, [c_void_p, c_void_p, c_void_p]),
     "hc_ipc_open": (c_int, [c_void_p, c_void_p]),

@@ -499,6 +499,18 @@ int hc_peer_barrier(int rank, int world, int32_t* const* peer_flags, int32_t* co
   return note_cuda(hc::peer_barrier_dispatch(rank, world, peer_flags, counter, err_flag, (cudaStream_t)stream));
 }
 
+int hc_peer_put(int n_segments, const int32_t* const* segments, const int64_t* segment_words, int n_dst,
+                int32_t* const* dsts, void* stream) {
+  if (n_segments <= 0 || n_segments > HC_MAX_PUT_SEGMENTS || n_dst < 0 || n_dst > HC_MAX_PEERS || !segments ||
+      !segment_words || (n_dst > 0 && !dsts))
+    return HC_ERR_INVALID;
+  for (int s = 0; s < n_segments; ++s)
+    if (segment_words[s] < 0 || (segment_words[s] > 0 && !segments[s])) return HC_ERR_INVALID;
+  for (int d = 0; d < n_dst; ++d)
+    if (!dsts[d] || (reinterpret_cast<uintptr_t>(dsts[d]) & 3u) != 0) return HC_ERR_INVALID;
+  return note_cuda(hc::peer_put_dispatch(n_segments, segments, segment_words, n_dst, dsts, (cudaStream_t)stream));
+}
+
 int hc_flash_decode_noalloc(int dtype, int bsz, int num_kv_heads, int groups, int head_dim, const void* q,
                             int64_t qsb, int64_t qsh, const void* k_pool, const void* v_pool, int n_pool_blocks,
                             const int32_t* block_table, int max_blocks, const int32_t* heads_len, float scale,

@@ -22,6 +22,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <utility>
 
 #include "hc_host.cuh"
@@ -817,6 +818,51 @@ int peer_barrier_dispatch(int rank, int world, int32_t* const* peer_flags, int32
   PeerFlags f;
   for (int i = 0; i < kMaxPeers; ++i) f.f[i] = i < world ? peer_flags[i] : nullptr;
   peer_barrier_kernel<<<1, 32, 0, st>>>(rank, world, f, counter, err, wait_limit_ns(kBarrierTimeoutNs));
+  return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
+}
+
+// Concatenation of up to kMaxPutSegs int32 segments stored into up to
+// kMaxPeers destinations (other ranks' buffers mapped through CUDA IPC):
+// word i of the concatenation goes to dst[d][i] for every d.  Each thread
+// fences its stores at system scope, so a peer barrier issued after this
+// kernel on the same stream publishes them.
+struct PutArgs {
+  const int32_t* src[kMaxPutSegs];
+  int64_t end[kMaxPutSegs];  // running word count through segment s
+  int32_t* dst[kMaxPeers];
+  int n_seg, n_dst;
+};
+
+__global__ void __launch_bounds__(256) peer_put_kernel(PutArgs a) {
+  const int64_t total = a.end[a.n_seg - 1];
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    int s = 0;
+    while (i >= a.end[s]) ++s;  // n_seg <= kMaxPutSegs
+    const int64_t j = i - (s ? a.end[s - 1] : 0);
+    const int32_t w = a.src[s][j];
+    for (int d = 0; d < a.n_dst; ++d) a.dst[d][i] = w;
+  }
+  __threadfence_system();
+}
+
+int peer_put_dispatch(int n_seg, const int32_t* const* srcs, const int64_t* seg_words, int n_dst,
+                      int32_t* const* dsts, cudaStream_t st) {
+  PutArgs a;
+  std::memset(&a, 0, sizeof(a));
+  int64_t run = 0;
+  for (int s = 0; s < n_seg; ++s) {
+    a.src[s] = srcs[s];
+    run += seg_words[s];
+    a.end[s] = run;
+  }
+  for (int d = 0; d < n_dst; ++d) a.dst[d] = dsts[d];
+  a.n_seg = n_seg;
+  a.n_dst = n_dst;
+  if (run == 0 || n_dst == 0) return HC_OK;
+  const int64_t blocks = (run + 255) / 256;
+  const int grid = (int)(blocks < 64 ? blocks : 64);
+  peer_put_kernel<<<grid, 256, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? HC_OK : HC_ERR_CUDA;
 }
 

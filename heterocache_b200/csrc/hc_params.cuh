@@ -167,6 +167,9 @@ size_t flash_decode_ws_bytes(int R, int G);
 // One step barrier across the GPUs of a head-sharded cache: the caller's
 // counter + 1 stored into slot `rank` of every rank's flags, then a wait
 // until every slot of this rank's flags holds at least that value.
+constexpr int kMaxPutSegs = 4;
+int peer_put_dispatch(int n_seg, const int32_t* const* srcs, const int64_t* seg_words, int n_dst,
+                      int32_t* const* dsts, cudaStream_t st);
 int peer_barrier_dispatch(int rank, int world, int32_t* const* peer_flags, int32_t* counter, int32_t* err,
                           cudaStream_t st);
 int flash_decode_dispatch(int dtype, FDParams& p, void* ws, size_t ws_bytes, cudaStream_t st);

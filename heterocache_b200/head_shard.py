@@ -21,11 +21,17 @@ Two steps cross ranks:
   pivot's trigger and position list (the list heterocache/cache_utils.py:
   1084-1101 builds from the pivot's last buffered step), and every rank
   holding one of its satellites retrieves that satellite's first
-  ``lengths[m]`` positions from its own full tier.
+  ``lengths[m]`` positions from its own full tier.  The list crosses by an
+  NCCL broadcast (``remote_checks``) or, with ``PeerGather``'s mailboxes,
+  by the pivot rank's stores into the other ranks' memory
+  (``publish_remote``, published by the step barrier, then
+  ``retrieve_remote_mail``), which keeps a check step inside the step's
+  graph too.
 
 Every rank issues the same collectives in the same order: one all-gather per
 ``attention`` call and, at check steps, one broadcast per star group of the
-layer (in relation order).
+layer (in relation order); with ``PeerGather`` the same holds for its
+barriers.
 """
 from __future__ import annotations
 
@@ -218,14 +224,58 @@ class HeadShardedCache:
             buf[1:1 + max_len].copy_(jobs.retrieve_positions[j, :max_len])
         return buf
 
-    def retrieve_remote(self, layer_idx, si) -> None:
+    def remote_words(self, layer_idx) -> int:
+        """int32 words of the layer's mailbox block (``publish_remote``): per
+        star group crossing ranks, its trigger and position list."""
+        return sum(1 + max(self._max_len(spec), 1) for spec in self.remote[layer_idx])
+
+    def publish_remote(self, layer_idx, peer: "PeerGather", base: int = 0) -> None:
+        """``remote_checks`` over peer memory, pivot side: for each star group
+        whose pivot this rank holds, its trigger and position list stored
+        straight into words ``base`` .. of every other rank's mailbox
+        (hc_peer_put, one launch per group; no collective call, so a check
+        step is captured in the step's graph).  Issue after the layer's drift
+        check and before the step's closing ``peer.barrier()``, which
+        publishes the words; the other ranks then run
+        ``retrieve_remote_mail`` with the same ``base``."""
+        off = base
+        c = self.cache
+        for spec in self.remote[layer_idx]:
+            max_len = self._max_len(spec)
+            if spec["src"] == self.rank:
+                jobs = c._jobs[layer_idx]
+                if jobs is None or spec["leader"] not in jobs.pivot_list:
+                    raise RuntimeError("pivot job missing on its rank")
+                j = jobs.pivot_list.index(spec["leader"])
+                dsts = [p + off * 4 for r, p in enumerate(peer.mail_ptrs) if r != self.rank]
+                segs = [jobs.trigger[j:j + 1]]
+                if max_len:
+                    segs.append(jobs.retrieve_positions[j, :max_len])
+                ops.peer_put(segs, dsts)
+            off += 1 + max(max_len, 1)
+
+    def retrieve_remote_mail(self, layer_idx, peer: "PeerGather", base: int = 0) -> None:
+        """``remote_checks`` over peer memory, satellite side: this rank's
+        satellites of remote pivots retrieved from the trigger and positions
+        ``publish_remote`` stored into this rank's mailbox (after the step's
+        closing ``peer.barrier()``)."""
+        off = base
+        for si, spec in enumerate(self.remote[layer_idx]):
+            n = 1 + max(self._max_len(spec), 1)
+            if spec["members"]:
+                self.retrieve_remote(layer_idx, si, buf=peer.mail[off:off + n])
+            off += n
+
+    def retrieve_remote(self, layer_idx, si, buf=None) -> None:
         """Retrieve this rank's satellites of star group ``si`` from the staged
-        trigger and positions."""
+        trigger and positions (``buf``: [1 + max_len] int32, by default the
+        broadcast buffer of ``stage_positions``)."""
         spec = self.remote[layer_idx][si]
         if not spec["members"]:
             return
         c = self.cache
-        buf = self._bufs[(layer_idx, si)]
+        if buf is None:
+            buf = self._bufs[(layer_idx, si)]
         key = ("members", layer_idx, si)
         if key not in self._bufs:  # device index arrays, made once
             base, L = c.base_compress_len, c.prefill_len
@@ -294,10 +344,16 @@ class PeerGather:
     them orders the stores: after the second, ``out`` holds every rank's
     heads on every rank.  All ranks construct it together (one object
     exchange over the process group) and call ``barrier`` equally often.
+
+    ``mail_words`` > 0 adds an int32 mailbox of that size per rank, mapped the
+    same way (``mail_ptrs``): the pivots' trigger and position lists reach
+    the ranks of their satellites there (``HeadShardedCache.publish_remote``,
+    hc_peer_put), published by the same step barrier, so that a check step
+    needs no collective call either.
     """
 
     def __init__(self, rows: int, h: int, D: int, dtype: torch.dtype, rank: int, world: int, group=None,
-                 device=None):
+                 device=None, mail_words: int = 0):
         if not 1 <= world <= 8:
             raise ValueError("PeerGather: 1 to 8 ranks")
         self.rank, self.world, self.h, self.D, self.rows = rank, world, h, D, rows
@@ -306,9 +362,11 @@ class PeerGather:
         self.flags = torch.zeros(world, dtype=torch.int32, device=dev)
         self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.mail = torch.zeros(max(int(mail_words), 1), dtype=torch.int32, device=dev)
         self._opened: List[int] = []  # this process's mappings of the other ranks' allocations
         if world == 1:
             self.out_ptrs, self.flag_ptrs = [self.out.data_ptr()], [self.flags.data_ptr()]
+            self.mail_ptrs = [self.mail.data_ptr()]
         else:
             import ctypes
             from ._lib import check, lib
@@ -319,7 +377,7 @@ class PeerGather:
                 check("hc_ipc_export", lib().hc_ipc_export(t.data_ptr(), h, ctypes.byref(off)))
                 return h.raw, off.value
 
-            mine = (export(self.out), export(self.flags))
+            mine = (export(self.out), export(self.flags), export(self.mail))
             allh: List = [None] * world
             dist.all_gather_object(allh, mine, group=group)
             opened: Dict[bytes, int] = {}  # one mapping per allocation (out and flags may share one)
@@ -333,14 +391,16 @@ class PeerGather:
                     opened[handle] = base.value
                 return opened[handle] + off
 
-            self.out_ptrs, self.flag_ptrs = [], []
-            for r, ((ho, oo), (hf, of)) in enumerate(allh):
+            self.out_ptrs, self.flag_ptrs, self.mail_ptrs = [], [], []
+            for r, ((ho, oo), (hf, of), (hm, om)) in enumerate(allh):
                 if r == rank:
                     self.out_ptrs.append(self.out.data_ptr())
                     self.flag_ptrs.append(self.flags.data_ptr())
+                    self.mail_ptrs.append(self.mail.data_ptr())
                 else:
                     self.out_ptrs.append(mapped(ho, oo))
                     self.flag_ptrs.append(mapped(hf, of))
+                    self.mail_ptrs.append(mapped(hm, om))
             self._opened = list(opened.values())
         self.mirror_batch_stride = world * h * D
         self._esz = self.out.element_size()

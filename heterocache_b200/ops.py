@@ -574,3 +574,26 @@ def peer_barrier(rank: int, world: int, flag_ptrs, counter: torch.Tensor, err: t
     arr = (ctypes.c_void_p * world)(*[int(p) for p in flag_ptrs])
     check("hc_peer_barrier", lib().hc_peer_barrier(rank, world, arr, _ptr(counter), _ptr(err), _stream(counter)))
     LAUNCHES[0] += 1
+
+
+def peer_put(segments, dst_ptrs) -> None:
+    """hc_peer_put: the concatenation of ``segments`` (up to 4 int32 CUDA
+    tensors, each contiguous) stored into every address of ``dst_ptrs`` (up
+    to 8 device addresses, e.g. other ranks' buffers mapped through CUDA IPC;
+    each must have room for the concatenation), fenced at system scope so
+    that a ``peer_barrier`` after it publishes the words.  Runs on the first
+    segment's current stream."""
+    import ctypes
+    _need(1 <= len(segments) <= 4, "peer_put takes 1 to 4 segments")
+    _need(len(dst_ptrs) <= 8, "peer_put takes at most 8 destinations")
+    _cuda(*segments)
+    for t in segments:
+        _i32(t, "peer_put segment")
+        _need(t.is_contiguous(), "peer_put segments must be contiguous")
+    n = len(segments)
+    srcs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in segments])
+    words = (ctypes.c_int64 * n)(*[t.numel() for t in segments])
+    dsts = (ctypes.c_void_p * max(len(dst_ptrs), 1))(*[int(p) for p in dst_ptrs])
+    check("hc_peer_put", lib().hc_peer_put(n, srcs, words, len(dst_ptrs), dsts, _stream(segments[0])))
+    if dst_ptrs and sum(t.numel() for t in segments):
+        LAUNCHES[0] += 1

@@ -296,6 +296,20 @@ int hc_flash_decode_peer(int dtype, int bsz, int num_kv_heads, int groups, int h
                          void* workspace, size_t workspace_bytes, int32_t* err_flag, void* stream);
 int hc_peer_barrier(int rank, int world, int32_t* const* peer_flags, int32_t* counter, int32_t* err_flag,
                     void* stream);
+/* hc_peer_put: the broadcast of a pivot's trigger and position list
+ * (replaces the torch.distributed.broadcast a head-sharded rank would issue;
+ * the reference runs one GPU and reads the list in place,
+ * heterocache/cache_utils.py:1084-1101).  Stores the concatenation of
+ * n_segments int32 segments (up to HC_MAX_PUT_SEGMENTS; segment s:
+ * segment_words[s] words at segments[s], device memory) into each of n_dst
+ * destinations (up to HC_MAX_PEERS device pointers, 4-byte aligned, e.g.
+ * other ranks' buffers mapped with hc_ipc_open), fenced at system scope: an
+ * hc_peer_barrier issued after it on the same stream publishes the words to
+ * the destinations' ranks.  Nothing is launched when there is no word or no
+ * destination. */
+#define HC_MAX_PUT_SEGMENTS 4
+int hc_peer_put(int n_segments, const int32_t* const* segments, const int64_t* segment_words, int n_dst,
+                int32_t* const* dsts, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Decode attention without a workspace.  No counterpart in the reference:

@@ -29,16 +29,21 @@ def main():
         full = HeteroCache(_config(layers, KV, H))
         shard = HeadShardedCache(_config(layers, KV, H), rank, world)
         # a second shard whose head outputs are gathered by the decode kernels
-        # over NVLink (PeerGather) instead of the NCCL all-gather
+        # over NVLink (PeerGather) instead of the NCCL all-gather, and whose
+        # pivots' position lists reach the other rank through its mailbox
+        # (publish_remote / retrieve_remote_mail) instead of NCCL broadcasts
         shard_p = HeadShardedCache(_config(layers, KV, H), rank, world)
-        peer = PeerGather(1, H // world, 128, torch.bfloat16, rank, world, device=dev)
         # both ranks prefill the full cache and only their own shards
         gens = _setup(dev, full.data, layers, KV, H, L, (full, [shard, shard_p]))
+        # mailbox words per layer are known once the budget is (after prefill)
+        base = [sum(shard_p.remote_words(x) for x in range(l)) for l in range(layers)]
+        mail = sum(shard_p.remote_words(x) for x in range(layers))
+        peer = PeerGather(1, H // world, 128, torch.bfloat16, rank, world, device=dev, mail_words=mail)
         print(f"rank {rank}: prefill done", flush=True)
         kl, hl = KV // world, H // world
         ks, hs = slice(rank * kl, (rank + 1) * kl), slice(rank * hl, (rank + 1) * hl)
         max_diff, same_rows, same_trig, n_trig = 0.0, True, True, 0
-        peer_exact, peer_diff = True, 0.0
+        peer_exact, peer_diff, mail_rows, mail_trig, n_mail = True, 0.0, True, True, 0
         for step in range(12):
             for layer in range(layers):
                 q, k, v = (t.to(dev) for t in gens[layer].step())
@@ -55,22 +60,31 @@ def main():
                 peer_diff = max(peer_diff, (o_full.float() - peer.out.float()).abs().max().item())
                 full.decode_select(q, layer)
                 shard.decode_select(q[:, hs].contiguous(), layer)
-                shard_p.decode_select(q[:, hs].contiguous(), layer)
+                if shard_p.select_local(q[:, hs].contiguous(), layer):  # the same on every rank
+                    shard_p.publish_remote(layer, peer, base[layer])
+                    peer.barrier()
+                    shard_p.retrieve_remote_mail(layer, peer, base[layer])
+                    n_mail += 1
                 torch.cuda.synchronize()
+                jp = shard_p.cache._jobs[layer]
                 jf, js = full._jobs[layer], shard.cache._jobs[layer]
                 if jf is not None and js is not None and js.n_jobs:
                     same_trig &= torch.equal(jf.trigger[:jf.n_jobs].cpu(), js.trigger[:js.n_jobs].cpu())
                     n_trig += int(js.trigger[:js.n_jobs].sum())
+                    mail_trig &= torch.equal(jp.trigger[:jp.n_jobs].cpu(), js.trigger[:js.n_jobs].cpu())
                 for h in range(kl):
                     a, b = _rows(full, layer, rank * kl + h), _rows(shard.cache, layer, h)
                     same_rows &= bool(torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]))
+                    c = _rows(shard_p.cache, layer, h)
+                    mail_rows &= bool(torch.equal(c[0], b[0]) and torch.equal(c[1], b[1]))
             print(f"rank {rank}: step {step} done", flush=True)
         full.check_errors()
         shard.check_errors()
         shard_p.check_errors()
         peer.check_errors()
         peer.close()
-        res.update(peer_exact=bool(peer_exact), peer_diff=peer_diff, max_diff=max_diff, same_rows=bool(same_rows), same_trig=bool(same_trig), n_trig=n_trig,
+        res.update(mail_rows=bool(mail_rows), mail_trig=bool(mail_trig), n_mail=n_mail,
+                   peer_exact=bool(peer_exact), peer_diff=peer_diff, max_diff=max_diff, same_rows=bool(same_rows), same_trig=bool(same_trig), n_trig=n_trig,
                    crossing=sum(len(s) for s in shard.remote))
     except Exception as e:  # reported through the result file
         res["error"] = repr(e)

@@ -145,6 +145,9 @@ def test_head_sharded_two_gpus_match_single_gpu(tmp_path):
         assert r["crossing"] > 0, r
         # the gather by the decode kernels over NVLink: the NCCL result bit for bit
         assert r["peer_exact"] and r["peer_diff"] <= 2e-2, r
+        # position lists through the mailboxes: the same pages and triggers as
+        # through NCCL broadcasts
+        assert r["mail_rows"] and r["mail_trig"] and r["n_mail"] > 0, r
     assert sum(r["n_trig"] for r in res) > 0
 
 
@@ -197,3 +200,24 @@ def test_peer_barrier_times_out_when_a_rank_never_arrives(cuda_device):
     assert int(counter.item()) == 1
     x = torch.ones(4, device=dev)
     assert float((x * 2).sum().item()) == 8.0
+
+
+def test_peer_put_stores_the_segments_into_every_destination(cuda_device):
+    """hc_peer_put on one GPU (the 2-GPU test covers another GPU's memory):
+    the concatenated segments land in every destination, words past them
+    are left alone, and nothing is launched without a destination."""
+    from heterocache_b200 import ops
+    dev = cuda_device
+    a = torch.tensor([7], dtype=torch.int32, device=dev)
+    b = torch.arange(3000, dtype=torch.int32, device=dev) * 3 - 1000
+    c = torch.arange(5, dtype=torch.int32, device=dev) + 40
+    d1 = torch.full((3010,), -9, dtype=torch.int32, device=dev)
+    d2 = torch.full((3020,), -9, dtype=torch.int32, device=dev)
+    ops.peer_put([a, b, c], [d1.data_ptr(), d2[4:].data_ptr()])
+    torch.cuda.synchronize()
+    want = torch.cat([a, b, c])
+    assert torch.equal(d1[:3006], want) and bool((d1[3006:] == -9).all())
+    assert torch.equal(d2[4:3010], want) and bool((d2[:4] == -9).all()) and bool((d2[3010:] == -9).all())
+    n0 = ops.LAUNCHES[0]
+    ops.peer_put([a], [])
+    assert ops.LAUNCHES[0] == n0

@@ -82,3 +82,11 @@ def test_batch_view_of_rows_of_one_buffer():
     assert _batch_view([r.clone() for r in rows]) is None
     assert _batch_view([rows[0], rows[2], rows[1]]) is None
     assert _batch_view(rows[:1]) is rows[0]
+
+
+def test_peer_put_rejects_too_many_segments_or_destinations():
+    seg = torch.zeros(4, dtype=i32)
+    with pytest.raises(ValueError, match="1 to 4 segments"):
+        ops.peer_put([seg] * 5, [0])
+    with pytest.raises(ValueError, match="at most 8 destinations"):
+        ops.peer_put([seg], [16] * 9)
