@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--per-sequence-launches", action="store_true",
                     help="config4: each sequence's own decode launch (default: the sequences' pages in one "
                          "CacheGroup pool per GPU, attended in one launch)")
+    ap.add_argument("--contiguous-heads", action="store_true",
+                    help="head-sharded mode: contiguous blocks of KV heads per GPU (default: capacity-balanced)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="head-sharded mode: head outputs gathered by the decode kernels over NVLink (peer) or "
                          "by an NCCL all-gather")
@@ -773,7 +775,9 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         cfg = HeteroCacheConfig(data, compression_ratio=0.5, stable_threshold=0.5, real_offload=False,
                                 max_gen_len=1024, decode_step=STEPS_PER_CHECK, pooling="avgpool", kernel_size=5,
                                 num_attn_heads=H, num_kv_heads=KV, num_layers=1)
-        views = [HeadShardedCache(cfg, rank, world) for _ in seqs]
+        # capacity-balanced head sets per rank (contiguous blocks with --contiguous-heads)
+        balance = not getattr(args, "contiguous_heads", False)
+        views = [HeadShardedCache(cfg, rank, world, balance=balance) for _ in seqs]
         inner = [v.cache for v in views]
         kl, hl = KV // world, H // world
     else:
@@ -786,8 +790,9 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     # the GPU's sequences' pages in one pool: one decode launch a step covers
     # them all (adopted before the prefill)
     group = None if getattr(args, "per_sequence_launches", False) else CacheGroup(inner)
-    ks, hs = slice(rank * kl, (rank + 1) * kl) if heads_mode else slice(None), \
-        slice(rank * hl, (rank + 1) * hl) if heads_mode else slice(None)
+    # this rank's KV heads and query heads (index tensors; all heads per sequence when sharded by sequence)
+    ks = views[0].head_index(0, dev) if heads_mode else torch.arange(KV, device=dev)
+    hs = views[0].head_index(0, dev, query=True) if heads_mode else torch.arange(H, device=dev)
     # prefill: every sequence's q/K/V from its own seed (identical on every
     # rank in the head-sharded mode, which keeps its own heads)
     q_last = []
@@ -795,7 +800,7 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
         g = torch.Generator(device=dev).manual_seed(5000 + s)
         q = torch.randn(1, H, L, D, generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
         k, v = prefill_kv_device(LLAMA_8B, L, q[:, :, -32:, :], seed=6000 + s, device=dev)
-        qq, kk, vv = q[:, hs].contiguous(), k[:, ks].contiguous(), v[:, ks].contiguous()
+        qq, kk, vv = q.index_select(1, hs), k.index_select(1, ks), v.index_select(1, ks)
         view.update(kk, vv, 0)
         view.init_coefficient(qq, kk, 0)
         view.prefill_select(qq, kk, vv, 0)
@@ -820,9 +825,9 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     stage = {}
 
     def load(t):
-        qb.copy_(qs[t][:, :, hs])
-        kb.copy_(kvs[0, t][:, :, ks])
-        vb.copy_(kvs[1, t][:, :, ks])
+        qb.copy_(qs[t].index_select(2, hs))
+        kb.copy_(kvs[0, t].index_select(2, ks))
+        vb.copy_(kvs[1, t].index_select(2, ks))
 
     local = torch.zeros(n_local, hl, D, dtype=torch.bfloat16, device=dev)
     peer = None
@@ -974,7 +979,9 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     gather = ("the decode combine kernels store their head rows into every GPU's gathered output over "
               "NVLink, two device-side barriers a step, inside the step's CUDA graph" if peer is not None
               else "NCCL all-gather of the head outputs per step")
-    mode = (f"KV-head-sharded x{world} (each GPU {KV // world} of the 8 KV heads of every sequence; {gather})"
+    heads_how = "contiguous blocks" if getattr(args, "contiguous_heads", False) else "capacity-balanced head sets"
+    mode = (f"KV-head-sharded x{world} (each GPU {KV // world} of the 8 KV heads of every sequence, "
+            f"{heads_how}; {gather})"
             if heads_mode
             else f"sequence-sharded x{world} ({n_seq // world} sequences per GPU, no data-path collective)")
     mode += ("; the GPU's sequences in one CacheGroup pool, one decode launch a step" if group is not None

@@ -57,11 +57,58 @@ def owner_of(head: int, num_kv_heads: int, world: int) -> int:
     return head // (num_kv_heads // world)
 
 
-def local_runtime_data(data: Dict, num_layers: int, num_kv_heads: int, world: int, rank: int):
+def head_weights(data: Dict, layer: int, compression_ratio: float, total_kv_heads: int) -> List[float]:
+    """Cached tokens of each KV head of the layer per prompt token: 1 for a
+    head kept whole (volatile, pivot), else its budget share
+    ``min(alloc * base / L, 1)`` with base the budget formula of
+    heterocache/cache_utils.py:15-16 (linear in L)."""
+    from .roles import full_head_count
+    F = full_head_count(data)
+    c = (compression_ratio * total_kv_heads - F) / (total_kv_heads - F)
+    cls = data["classification_matrix"][layer]
+    alloc = data["allocation_matrix"][layer]
+    return [1.0 if x in (2, 3) else max(min(a * c, 1.0), 0.0) for x, a in zip(cls, alloc)]
+
+
+def head_assignment(data: Dict, num_layers: int, num_kv_heads: int, world: int, balance: bool = False,
+                    compression_ratio: float = 0.5, total_kv_heads: Optional[int] = None) -> List[List[List[int]]]:
+    """Per layer, per rank: the rank's KV heads (ascending ids, KV/world each).
+
+    ``balance=False``: contiguous blocks (``head_blocks``).  ``balance=True``:
+    the heads spread so that the ranks hold about the same number of cached
+    tokens (largest head first onto the least-loaded rank with room; ties to
+    the lower rank): in the role order the heads kept whole (volatile, pivot)
+    sit together at the end, so contiguous blocks put most of a layer's
+    bytes, and the decode time, on the last ranks.  A rank's heads keep
+    their relative order, so the role order holds on every rank; the
+    gathered output lists the ranks' query heads rank by rank
+    (``HeadShardedCache.gathered_heads``)."""
+    if world < 1 or num_kv_heads % world:
+        raise ValueError(f"{num_kv_heads} KV heads do not split evenly over {world} ranks")
+    n = num_kv_heads // world
+    if not balance:
+        return [[list(b) for b in head_blocks(num_kv_heads, world)] for _ in range(num_layers)]
+    T = total_kv_heads or num_kv_heads * num_layers
+    out = []
+    for layer in range(num_layers):
+        w = head_weights(data, layer, compression_ratio, T)
+        load, ranks = [0.0] * world, [[] for _ in range(world)]
+        for h in sorted(range(num_kv_heads), key=lambda i: (-w[i], i)):
+            r = min((r for r in range(world) if len(ranks[r]) < n), key=lambda r: (load[r], r))
+            ranks[r].append(h)
+            load[r] += w[h]
+        out.append([sorted(x) for x in ranks])
+    return out
+
+
+def local_runtime_data(data: Dict, num_layers: int, num_kv_heads: int, world: int, rank: int,
+                       assignment: Optional[List[List[List[int]]]] = None):
     """Runtime role data of one rank's heads, plus its cross-rank retrieval specs.
 
-    Returns ``(local, remote)``.  ``local`` is a derived role document for the
-    rank's heads (local ids 0..n-1 in the same order): classification and
+    ``assignment`` (``head_assignment``; default contiguous blocks) gives
+    each layer's heads per rank.  Returns ``(local, remote)``.  ``local`` is
+    a derived role document for the rank's heads (local ids 0..n-1 in the
+    same order): classification and
     allocation rows sliced, relations kept for local pivots with their local
     satellites, ``remote_member_alloc[layer][local pivot]`` = allocations of
     that pivot's satellites held by other ranks (its position list must cover
@@ -71,16 +118,19 @@ def local_runtime_data(data: Dict, num_layers: int, num_kv_heads: int, world: in
     pivot's local id there, "alloc": allocations of all its satellites,
     "members": [(local head id, allocation)] of this rank's satellites}``.
     """
-    blocks = head_blocks(num_kv_heads, world)
-    mine = blocks[rank]
-    n = len(mine)
+    if assignment is None:
+        assignment = head_assignment(data, num_layers, num_kv_heads, world)
     local = {"meta": copy.deepcopy(data["meta"]), "classification_matrix": [], "allocation_matrix": [],
              "leader_member_relations": [], "remote_member_alloc": [], "need_to_update_counts": [],
              "need_to_select_counts": [], "need_to_compress_counts": [], "need_to_keep_counts": []}
     remote: List[List[Dict]] = []
     for layer in range(num_layers):
-        cls = list(data["classification_matrix"][layer][mine.start:mine.stop])
-        alloc = list(data["allocation_matrix"][layer][mine.start:mine.stop])
+        heads = assignment[layer]
+        owner = {h: r for r, hs in enumerate(heads) for h in hs}
+        lid = {h: i for hs in heads for i, h in enumerate(hs)}  # local id on the owner's rank
+        mine = heads[rank]
+        cls = [data["classification_matrix"][layer][h] for h in mine]
+        alloc = [data["allocation_matrix"][layer][h] for h in mine]
         local["classification_matrix"].append(cls)
         local["allocation_matrix"].append(alloc)
         local["need_to_compress_counts"].append(cls.count(1) + cls.count(4))
@@ -93,20 +143,20 @@ def local_runtime_data(data: Dict, num_layers: int, num_kv_heads: int, world: in
         full_alloc = data["allocation_matrix"][layer]
         for leader, members in data["leader_member_relations"][layer].items():
             lg = int(leader)
-            src = owner_of(lg, num_kv_heads, world)
+            src = owner[lg]
             if src == rank:
-                rel[str(lg - mine.start)] = [m - mine.start for m in members if owner_of(m, num_kv_heads, world) == rank]
-                off = [full_alloc[m] for m in members if owner_of(m, num_kv_heads, world) != rank]
+                rel[str(lid[lg])] = [lid[m] for m in members if owner[m] == rank]
+                off = [full_alloc[m] for m in members if owner[m] != rank]
                 if off:
-                    rem_alloc[str(lg - mine.start)] = off
+                    rem_alloc[str(lid[lg])] = off
             # a star group crossing ranks: every rank takes part in its broadcast
-            if any(owner_of(m, num_kv_heads, world) != src for m in members):
-                specs.append({"src": src, "leader": lg - blocks[src].start,
+            if any(owner[m] != src for m in members):
+                specs.append({"src": src, "leader": lid[lg],
                               "alloc": [full_alloc[m] for m in members],
-                              "members": [(m - mine.start, full_alloc[m]) for m in members
-                                          if owner_of(m, num_kv_heads, world) == rank and src != rank]})
+                              "members": [(lid[m], full_alloc[m]) for m in members
+                                          if owner[m] == rank and src != rank]})
         pivots = [int(x) for x in data["leader_member_relations"][layer]]
-        owners = {owner_of(p, num_kv_heads, world) for p in pivots}
+        owners = {owner[p] for p in pivots}
         if len(owners) > 1 and pivots != sorted(pivots):
             # the reference pairs relation entry i with the i-th pivot in sorted
             # order (cache_utils.py:1027 with utils.py:326); split over ranks that
@@ -122,16 +172,27 @@ class HeadShardedCache:
     """One rank's share of a head-sharded ``HeteroCache``.
 
     Inputs are the rank's slices: q [bsz, H/world, L, D], k/v
-    [bsz, KV/world, L, D].  ``attention`` returns every head's output
-    [bsz, H, D].  Method names and call order follow the cache object.
+    [bsz, KV/world, L, D] -- the heads ``q_heads(layer)`` / ``kv_heads(layer)``
+    (a contiguous block, or with ``balance=True`` the capacity-balanced
+    heads of ``head_assignment``).  ``attention`` returns every head's output
+    [bsz, H, D], rank by rank: row j is query head ``gathered_heads(layer)[j]``
+    (the identity for contiguous blocks; with ``balance`` the model's o_proj
+    input columns are permuted once to that order, as the load-time role
+    permutation permutes them).  Method names and call order follow the
+    cache object.
     """
 
-    def __init__(self, config: HeteroCacheConfig, rank: int, world: int, group=None):
+    def __init__(self, config: HeteroCacheConfig, rank: int, world: int, group=None, balance: bool = False):
         self.rank, self.world, self.group = rank, world, group
         KV, H = config.num_kv_heads, config.num_attn_heads
         if H % KV:
             raise ValueError("query heads must be a multiple of KV heads")
-        local, self.remote = local_runtime_data(config.data, config.num_layers, KV, world, rank)
+        T = getattr(config, "total_kv_heads", None) or KV * config.num_layers
+        self.assignment = head_assignment(config.data, config.num_layers, KV, world, balance,
+                                          config.compression_ratio, T)
+        self.groups = H // KV
+        local, self.remote = local_runtime_data(config.data, config.num_layers, KV, world, rank,
+                                                assignment=self.assignment)
         self.kv_local = KV // world
         self.h_local = H // world
         cfg = HeteroCacheConfig(local, compression_ratio=config.compression_ratio,
@@ -146,6 +207,33 @@ class HeadShardedCache:
         self.num_attn_heads = H
         self._gather: Dict = {}
         self._bufs: Dict = {}
+        self._index: Dict = {}
+
+    # -- which heads -----------------------------------------------------
+    def kv_heads(self, layer_idx) -> List[int]:
+        """This rank's KV heads of the layer (model ids, ascending)."""
+        return self.assignment[layer_idx][self.rank]
+
+    def q_heads(self, layer_idx) -> List[int]:
+        """This rank's query heads of the layer (each KV head's GQA group)."""
+        G = self.groups
+        return [h * G + g for h in self.kv_heads(layer_idx) for g in range(G)]
+
+    def gathered_heads(self, layer_idx) -> List[int]:
+        """Model query head of each row of the gathered output (rank by rank)."""
+        G = self.groups
+        return [h * G + g for hs in self.assignment[layer_idx] for h in hs for g in range(G)]
+
+    def head_index(self, layer_idx, device, query: bool = False) -> torch.Tensor:
+        """``kv_heads`` (or ``q_heads``) as an int64 index tensor on ``device``
+        (e.g. ``k.index_select(1, ...)`` to slice a layer's inputs)."""
+        key = (layer_idx, str(device), query)
+        t = self._index.get(key)
+        if t is None:
+            ids = self.q_heads(layer_idx) if query else self.kv_heads(layer_idx)
+            t = torch.tensor(ids, dtype=torch.int64, device=device)
+            self._index[key] = t
+        return t
 
     # -- prefill -------------------------------------------------------
     def update(self, key_states, value_states, layer_idx, cache_kwargs=None):

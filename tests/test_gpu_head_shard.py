@@ -46,9 +46,8 @@ def _setup(dev, data, layers, KV, H, L, caches):
         full.init_coefficient(qd, kd, layer)
         full.prefill_select(qd, kd, vd, layer)
         for sh in shards:
-            r, kl, hl = sh.rank, KV // sh.world, H // sh.world
-            qs, ksl, vsl = (qd[:, r * hl:(r + 1) * hl].contiguous(), kd[:, r * kl:(r + 1) * kl].contiguous(),
-                            vd[:, r * kl:(r + 1) * kl].contiguous())
+            ki, qi = sh.head_index(layer, dev), sh.head_index(layer, dev, query=True)
+            qs, ksl, vsl = qd.index_select(1, qi), kd.index_select(1, ki), vd.index_select(1, ki)
             sh.update(ksl, vsl, layer)
             sh.init_coefficient(qs, ksl, layer)
             sh.prefill_select(qs, ksl, vsl, layer)
@@ -67,33 +66,38 @@ def _config(layers=2, KV=8, H=32):
                              num_kv_heads=KV, num_layers=layers)
 
 
-def test_head_sharded_emulated_on_one_gpu(cuda_device):
+@pytest.mark.parametrize("balance", [False, True], ids=["contiguous", "balanced"])
+def test_head_sharded_emulated_on_one_gpu(cuda_device, balance):
     """Both ranks of a 2-way head split in one process on one GPU, with the two
     collectives done as copies: the sharding logic (budgets, local roles,
-    cross-rank position lists, remote retrievals) against the single cache."""
+    cross-rank position lists, remote retrievals) against the single cache,
+    with contiguous head blocks and with capacity-balanced head sets."""
     from heterocache_b200.cache import HeteroCache
     from heterocache_b200.head_shard import HeadShardedCache
     dev = cuda_device
     layers, KV, H, L, world = 2, 8, 32, 4096, 2
     full = HeteroCache(_config(layers, KV, H))
-    shards = [HeadShardedCache(_config(layers, KV, H), r, world) for r in range(world)]
+    shards = [HeadShardedCache(_config(layers, KV, H), r, world, balance=balance) for r in range(world)]
+    if balance:
+        assert any(sh.kv_heads(0) != list(range(sh.rank * KV // world, (sh.rank + 1) * KV // world))
+                   for sh in shards)
     assert sum(len(s) for s in shards[0].remote) > 0
     gens = _setup(dev, full.data, layers, KV, H, L, (full, shards))
-    kl, hl = KV // world, H // world
     n_trig = 0
     for step in range(12):
         for layer in range(layers):
             q, k, v = (t.to(dev) for t in gens[layer].step())
             full.update(k, v, layer)
+            qi = [sh.head_index(layer, dev, query=True) for sh in shards]
             for sh in shards:
-                r = sh.rank
-                sh.update(k[:, r * kl:(r + 1) * kl].contiguous(), v[:, r * kl:(r + 1) * kl].contiguous(), layer)
+                ki = sh.head_index(layer, dev)
+                sh.update(k.index_select(1, ki), v.index_select(1, ki), layer)
             o_full = full.attention(q, layer)
-            o = torch.cat([sh.cache.attention(q[:, sh.rank * hl:(sh.rank + 1) * hl].contiguous(), layer)
-                           for sh in shards], dim=1)
-            assert (o_full.float() - o.float()).abs().max().item() <= 2e-2, (step, layer)
+            o = torch.cat([sh.cache.attention(q.index_select(1, qi[sh.rank]), layer) for sh in shards], dim=1)
+            order = torch.tensor(shards[0].gathered_heads(layer), device=dev)
+            assert (o_full.index_select(1, order).float() - o.float()).abs().max().item() <= 2e-2, (step, layer)
             full.decode_select(q, layer)
-            checks = [sh.select_local(q[:, sh.rank * hl:(sh.rank + 1) * hl].contiguous(), layer) for sh in shards]
+            checks = [sh.select_local(q.index_select(1, qi[sh.rank]), layer) for sh in shards]
             assert len(set(checks)) == 1
             if checks[0]:
                 for si, spec in enumerate(shards[0].remote[layer]):
@@ -110,8 +114,8 @@ def test_head_sharded_emulated_on_one_gpu(cuda_device):
                 if jf is not None and js is not None and js.n_jobs:
                     assert torch.equal(jf.trigger[:jf.n_jobs].cpu(), js.trigger[:js.n_jobs].cpu()), (step, layer)
                     n_trig += int(js.trigger[:js.n_jobs].sum())
-                for h in range(kl):
-                    a, b = _rows(full, layer, sh.rank * kl + h), _rows(sh.cache, layer, h)
+                for h, g in enumerate(sh.kv_heads(layer)):
+                    a, b = _rows(full, layer, g), _rows(sh.cache, layer, h)
                     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1]), (step, layer, sh.rank, h)
     full.check_errors()
     for sh in shards:
@@ -119,7 +123,8 @@ def test_head_sharded_emulated_on_one_gpu(cuda_device):
     assert n_trig > 0
 
 
-def test_head_sharded_two_gpus_match_single_gpu(tmp_path):
+@pytest.mark.parametrize("balance", [False, True], ids=["contiguous", "balanced"])
+def test_head_sharded_two_gpus_match_single_gpu(tmp_path, balance):
     """The real thing: 2 processes, one GPU each, NCCL all-gather and
     broadcast (launched with torch.distributed.run; each rank writes its
     comparison result to a file)."""
@@ -129,7 +134,7 @@ def test_head_sharded_two_gpus_match_single_gpu(tmp_path):
     import subprocess
     import sys
     here = os.path.dirname(os.path.abspath(__file__))
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HC_SHARD_OUT=str(tmp_path))
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", HC_SHARD_OUT=str(tmp_path), HC_SHARD_BALANCE=str(int(balance)))
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(here, "head_shard_worker.py")]
