@@ -66,16 +66,21 @@ def _config(layers=2, KV=8, H=32):
                              num_kv_heads=KV, num_layers=layers)
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("balance", [False, True], ids=["contiguous", "balanced"])
-def test_head_sharded_emulated_on_one_gpu(cuda_device, balance):
-    """Both ranks of a 2-way head split in one process on one GPU, with the two
-    collectives done as copies: the sharding logic (budgets, local roles,
-    cross-rank position lists, remote retrievals) against the single cache,
-    with contiguous head blocks and with capacity-balanced head sets."""
+def test_head_sharded_emulated_on_one_gpu(cuda_device, balance, world):
+    """Every rank of a 2-, 4- or 8-way head split in one process on one GPU:
+    the sharding logic (budgets, local roles, cross-rank position lists,
+    remote retrievals; at 8 ranks a cache of one KV head, a pivot whose
+    satellites all sit elsewhere) against the single cache.  Contiguous head
+    blocks exchange the position lists as copies of the broadcast buffers;
+    capacity-balanced head sets through mailboxes (``publish_remote`` into
+    every other rank's buffer, ``retrieve_remote_mail``), as the kernel-side
+    gather does across GPUs."""
     from heterocache_b200.cache import HeteroCache
     from heterocache_b200.head_shard import HeadShardedCache
     dev = cuda_device
-    layers, KV, H, L, world = 2, 8, 32, 4096, 2
+    layers, KV, H, L = 2, 8, 32, 4096
     full = HeteroCache(_config(layers, KV, H))
     shards = [HeadShardedCache(_config(layers, KV, H), r, world, balance=balance) for r in range(world)]
     if balance:
@@ -83,6 +88,13 @@ def test_head_sharded_emulated_on_one_gpu(cuda_device, balance):
                    for sh in shards)
     assert sum(len(s) for s in shards[0].remote) > 0
     gens = _setup(dev, full.data, layers, KV, H, L, (full, shards))
+    # stand-ins for the ranks' PeerGather mailboxes, all on this GPU
+    import types
+    base = [sum(shards[0].remote_words(x) for x in range(l)) for l in range(layers)]
+    words = sum(shards[0].remote_words(x) for x in range(layers))
+    assert all(sum(sh.remote_words(x) for x in range(layers)) == words for sh in shards)
+    mails = [torch.full((max(words, 1),), -1, dtype=torch.int32, device=dev) for _ in shards]
+    boxes = [types.SimpleNamespace(mail=mails[r], mail_ptrs=[m.data_ptr() for m in mails]) for r in range(world)]
     n_trig = 0
     for step in range(12):
         for layer in range(layers):
@@ -99,7 +111,14 @@ def test_head_sharded_emulated_on_one_gpu(cuda_device, balance):
             full.decode_select(q, layer)
             checks = [sh.select_local(q.index_select(1, qi[sh.rank]), layer) for sh in shards]
             assert len(set(checks)) == 1
-            if checks[0]:
+            if checks[0] and balance:
+                # the mailbox path: each pivot rank stores its lists into the
+                # other ranks' mailboxes (one GPU, one stream: in order)
+                for sh in shards:
+                    sh.publish_remote(layer, boxes[sh.rank], base[layer])
+                for sh in shards:
+                    sh.retrieve_remote_mail(layer, boxes[sh.rank], base[layer])
+            elif checks[0]:
                 for si, spec in enumerate(shards[0].remote[layer]):
                     bufs = [sh.stage_positions(layer, si) for sh in shards]
                     for r in range(world):
