@@ -824,10 +824,15 @@ def measure_config4(args, rank, world, local_rank, heads_mode, n_seq, L, steps, 
     out = torch.zeros(n_local, H, D, dtype=torch.bfloat16, device=dev)
     stage = {}
 
+    # each rank's heads of every step's inputs, selected once (a rank's
+    # projections produce only its heads); a step then copies them in
+    qs = qs.index_select(3, hs)
+    kvs = kvs.index_select(4, ks)
+
     def load(t):
-        qb.copy_(qs[t].index_select(2, hs))
-        kb.copy_(kvs[0, t].index_select(2, ks))
-        vb.copy_(kvs[1, t].index_select(2, ks))
+        qb.copy_(qs[t])
+        kb.copy_(kvs[0, t])
+        vb.copy_(kvs[1, t])
 
     local = torch.zeros(n_local, hl, D, dtype=torch.bfloat16, device=dev)
     peer = None

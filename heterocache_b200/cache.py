@@ -200,6 +200,9 @@ class HeteroCache(_CacheBase):
         # host mirrors of deterministic bookkeeping
         self._hlen: List[Optional[np.ndarray]] = [None] * n
         self._mapped: List[Optional[np.ndarray]] = [None] * n
+        # per layer: decode appends that map no new page and stay inside the
+        # page table (0: unknown; _append_bookkeeping then checks in full)
+        self._slack: List[int] = [0] * n
         # opt-in diagnostics for parity tests: pooled scores and selections
         self.record_checks = bool(getattr(cache_config, "record_checks", False))
         # a CacheGroup this cache's pages live in (shared pool per layer)
@@ -304,6 +307,7 @@ class HeteroCache(_CacheBase):
         self.layer_head_capacities[layer_idx] = caps
         self._hlen[layer_idx] = np.zeros(rows, dtype=np.int64)
         self._mapped[layer_idx] = mapped
+        self._slack[layer_idx] = 0
 
     def _side(self) -> torch.cuda.Stream:
         if self._side_stream is None:
@@ -351,6 +355,7 @@ class HeteroCache(_CacheBase):
             self._init_layer_storage(layer_idx, key_states.device, key_states.dtype)
         seq_len = key_states.shape[-2]
         if seq_len > 1:
+            self._slack[layer_idx] = 0  # the prefill sets the lengths anew
             self.prefill_len = seq_len
             keep = self.data["need_to_keep_counts"][layer_idx]
             upd = self.data["need_to_update_counts"][layer_idx]
@@ -428,10 +433,24 @@ class HeteroCache(_CacheBase):
     def _append_bookkeeping(self, layer_idx: int) -> None:
         """Host side of a decode append: the free-list check of
         cache_utils.py:981-990 on the mirrored lengths (raises before any
-        launch), then the mirrors advance as the device state will."""
+        launch), then the mirrors advance as the device state will.
+
+        After a full check the layer's slack is the number of further appends
+        that can map no new page and hit no page-table end (every row grows by
+        one token per append): min over rows of min(mapped, table width) x
+        256 - length.  Those appends only advance the lengths, so they skip
+        the checks, which would find nothing (a few numpy calls per layer and
+        step on the host, which sets the pace of a captured decode step over
+        many small caches)."""
         hl = self._hlen[layer_idx]
+        s = self._slack[layer_idx]
+        if s > 0:
+            self._slack[layer_idx] = s - 1
+            hl += 1
+            return
+        width = self.block_tables[layer_idx].shape[1]
         logical = hl // PAGE
-        if np.any(logical >= self.block_tables[layer_idx].shape[1]):
+        if np.any(logical >= width):
             raise IndexError(f"Layer {layer_idx}: block table has no column for the next decode token")
         grow = logical >= self._mapped[layer_idx]
         need = int(np.count_nonzero(grow))
@@ -442,6 +461,8 @@ class HeteroCache(_CacheBase):
             self.free_block_pointers[layer_idx] += need
             self._mapped[layer_idx] += grow
         hl += 1
+        room = np.minimum(self._mapped[layer_idx], width) * PAGE - hl
+        self._slack[layer_idx] = max(int(room.min()), 0) if room.size else 0
 
     def init_coefficient(self, query_states, key_states, layer_idx):
         """Pivot reference sets (heterocache/cache_utils.py:1149-1190)."""
@@ -471,6 +492,7 @@ class HeteroCache(_CacheBase):
 
     def prefill_select(self, query_states, key_states, value_states, layer_idx):
         """Compressed heads (heterocache/cache_utils.py:782-882)."""
+        self._slack[layer_idx] = 0  # sets the compressed heads' lengths
         bsz = query_states.shape[0]
         nc = self.data["need_to_compress_counts"][layer_idx]
         if nc == 0:
@@ -585,7 +607,7 @@ class HeteroCache(_CacheBase):
 
     def _host_state(self):
         return {"hlen": [None if h is None else h.copy() for h in self._hlen],
-                "mapped": [None if m is None else m.copy() for m in self._mapped],
+                "mapped": [None if m is None else m.copy() for m in self._mapped], "slack": list(self._slack),
                 "free_ptr": list(self.free_block_pointers), "qcount": list(self._qcount),
                 "retrieve_done": list(self._retrieve_done), "seen": self._seen_tokens,
                 "pending": [None if x is None else list(x) for x in self._pending],
@@ -593,7 +615,7 @@ class HeteroCache(_CacheBase):
                 "q_staged": list(self._q_staged), "deferred": list(self._deferred)}
 
     def _restore_host_state(self, s) -> None:
-        self._hlen, self._mapped = s["hlen"], s["mapped"]
+        self._hlen, self._mapped, self._slack = s["hlen"], s["mapped"], s["slack"]
         self.free_block_pointers, self._qcount = s["free_ptr"], s["qcount"]
         self._retrieve_done, self._seen_tokens = s["retrieve_done"], s["seen"]
         self._pending, self._append_done, self._q_staged = s["pending"], s["append_done"], s["q_staged"]
