@@ -2,8 +2,9 @@
 multi-GPU configuration).
 
 A layer's KV heads, in the runtime order the role file's derivation produces
-(anchor -> satellite -> volatile -> pivot), are split into equal contiguous
-blocks, one per rank; a rank also holds the query heads of its KV heads
+(anchor -> satellite -> volatile -> pivot), are split into equal sets, one
+per rank: contiguous blocks, or sets balanced by cached tokens
+(``head_assignment``); a rank also holds the query heads of its KV heads
 (GQA groups stay whole).  Each rank runs the compressed-KV path for its heads
 with its own ``HeteroCache``; the budget formula still uses the model-wide
 head counts, so every head gets the capacity it would get on one GPU.
@@ -51,10 +52,6 @@ def head_blocks(num_kv_heads: int, world: int) -> List[range]:
         raise ValueError(f"{num_kv_heads} KV heads do not split evenly over {world} ranks")
     n = num_kv_heads // world
     return [range(r * n, (r + 1) * n) for r in range(world)]
-
-
-def owner_of(head: int, num_kv_heads: int, world: int) -> int:
-    return head // (num_kv_heads // world)
 
 
 def head_weights(data: Dict, layer: int, compression_ratio: float, total_kv_heads: int) -> List[float]:
