@@ -90,3 +90,35 @@ def test_peer_put_rejects_too_many_segments_or_destinations():
         ops.peer_put([seg] * 5, [0])
     with pytest.raises(ValueError, match="at most 8 destinations"):
         ops.peer_put([seg], [16] * 9)
+
+
+def test_cache_group_storage_gives_each_member_its_own_id_range():
+    """CacheGroup's host side (no kernel runs): one pool per layer sized for
+    every member, each member's page ids an offset range of its own, its
+    page table and lengths rows of shared tensors; members needing more
+    pages than the first one, or adopted after their prefill, are refused."""
+    import types
+    from heterocache_b200.cache import CacheGroup
+    members = [types.SimpleNamespace(key_pools=[None], head_dim=128) for _ in range(3)]
+    g = CacheGroup(members)
+    assert [m._gidx for m in members] == [0, 1, 2] and all(m._group is g for m in members)
+    out = [g._layer_storage(m, 0, 10, 8, 6, "cpu", torch.bfloat16) for m in members]
+    kp0, vp0 = out[0][0], out[0][1]
+    assert kp0.shape == (30, 256, 1, 128) and vp0.shape == kp0.shape
+    assert [o[2] for o in out] == [0, 10, 20]
+    for i, (kp, vp, off, bt, hl) in enumerate(out):
+        assert kp is kp0 and vp is vp0
+        assert bt.shape == (8, 6) and hl.shape == (8,)
+        bt.fill_(i)
+        hl.fill_(i + 1)
+    st = g._layers[0]
+    assert st["bt"][8:16].unique().tolist() == [1] and st["hl"][16:].unique().tolist() == [3]
+    with pytest.raises(ValueError, match="different pages"):
+        g._layer_storage(members[1], 0, 11, 8, 6, "cpu", torch.bfloat16)
+    with pytest.raises(ValueError, match="different pages"):
+        g._layer_storage(members[1], 0, 10, 8, 7, "cpu", torch.bfloat16)
+    q = [g._query_buffer(m, 0, 5, 32, 128, torch.bfloat16, "cpu") for m in members]
+    assert q[2].data_ptr() == g._qbufs[0][2].data_ptr() and q[0].shape == (5, 32, 128)
+    late = types.SimpleNamespace(key_pools=[torch.zeros(1)], head_dim=128)
+    with pytest.raises(RuntimeError, match="before their prefill"):
+        CacheGroup([late])
